@@ -1,0 +1,238 @@
+// C-ABI entry points (include/cyfa.h): host-side argument checks, TMA tensor
+// map construction and kernel launches.  No entry point allocates memory.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "../../include/cyfa.h"
+#include "cyfa_common.cuh"
+
+namespace cyfa {
+
+enum Status : int {
+  kOk = 0,
+  kBadShape = 1,
+  kNullPointer = 2,
+  kMisaligned = 3,
+  kBadDtype = 4,
+  kNoDriver = 5,
+  kTensorMap = 6,
+  kWorkspace = 7,
+};
+
+#define CYFA_REQUIRE(cond, code) \
+  do {                           \
+    if (!(cond)) return (code);  \
+  } while (0)
+
+static int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? kOk : -static_cast<int>(e);
+}
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point, so the
+// library does not link libcuda directly.
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// bf16 tensor map with a 128-byte swizzle and a box whose inner extent is 64
+// elements (one 128-byte row).  dims innermost first; strides in bytes for
+// dims 1..rank-1.  Out-of-bounds elements are filled with zeros.
+static int make_tmap_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
+                          const uint64_t* strides, const uint32_t* box) {
+  auto fn = encode_fn();
+  if (!fn) return kNoDriver;
+  if (!aligned(base, 16)) return kMisaligned;
+  for (int i = 0; i + 1 < rank; ++i)
+    if (strides[i] % 16) return kMisaligned;
+  cuuint64_t d[5], s[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+  }
+  for (int i = 0; i + 1 < rank; ++i) s[i] = strides[i];
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s,
+                        b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? kOk : kTensorMap;
+}
+
+// 2-D row-major [rows, cols] bf16 matrix, box {64, box_rows}.
+static int tmap_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols,
+                   uint32_t box_rows) {
+  const uint64_t dims[2] = {cols, rows};
+  const uint64_t strides[1] = {cols * 2};
+  const uint32_t box[2] = {64, box_rows};
+  return make_tmap_bf16(m, base, 2, dims, strides, box);
+}
+
+}  // namespace cyfa
+
+using namespace cyfa;
+
+extern "C" {
+
+int cyfa_version(void) { return 1; }
+
+const char* cyfa_strerror(int status) {
+  switch (status) {
+    case kOk: return "ok";
+    case kBadShape: return "unsupported or inconsistent shape";
+    case kNullPointer: return "required pointer is null";
+    case kMisaligned: return "pointer or stride is not 16-byte aligned";
+    case kBadDtype: return "unsupported dtype";
+    case kNoDriver: return "CUDA driver entry point cuTensorMapEncodeTiled unavailable";
+    case kTensorMap: return "cuTensorMapEncodeTiled rejected the tensor";
+    case kWorkspace: return "workspace too small";
+    default: break;
+  }
+  if (status < 0) return cudaGetErrorString(static_cast<cudaError_t>(-status));
+  return "unknown status";
+}
+
+int cyfa_device_error(int reset) {
+  int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(int)) != cudaSuccess) return -1;
+  if (reset) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_device_error, &zero, sizeof(int));
+  }
+  return v;
+}
+
+int cyfa_selftest_umma(const void* a, const void* b, float* c, int K, int N, int a_mn, int b_mn,
+                       void* stream) {
+  CYFA_REQUIRE(a && b && c, kNullPointer);
+  CYFA_REQUIRE(K >= 64 && K <= 256 && K % 64 == 0, kBadShape);
+  CYFA_REQUIRE(N == 64 || N == 128 || N == 256, kBadShape);
+  CUtensorMap ta, tb;
+  int st = a_mn ? tmap_2d(&ta, a, K, 128, K) : tmap_2d(&ta, a, 128, K, 128);
+  if (st) return st;
+  st = b_mn ? tmap_2d(&tb, b, K, N, K) : tmap_2d(&tb, b, N, K, N);
+  if (st) return st;
+  SelftestParams p{K, N, a_mn ? 1 : 0, b_mn ? 1 : 0, c};
+  const int smem = (128 + N) * K * 2 + 1024;
+  cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  umma_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  return launch_status();
+}
+
+int cyfa_decode_step(const void* q, const void* k, const void* v, const float* g,
+                     const float* delta, const float* beta, const float* table,
+                     const float* q_norm_weight, const float* k_norm_weight, const float* hk_in,
+                     const float* hv_in, const float* clock_in, float* hk_out, float* hv_out,
+                     float* clock_out, void* out, int B, int H, int K, int V, int dtype,
+                     float q_eps, float k_eps, float scale, void* stream) {
+  CYFA_REQUIRE(q && k && v && g && delta && beta && table && q_norm_weight && k_norm_weight &&
+                   hk_out && hv_out && clock_out && out,
+               kNullPointer);
+  CYFA_REQUIRE(B > 0 && H > 0 && (K == 128 || K == 256) && (V == 128 || V == 256), kBadShape);
+  CYFA_REQUIRE(dtype == 0 || dtype == 1, kBadDtype);
+  CYFA_REQUIRE(aligned(hk_out, 16) && aligned(hv_out, 16) && aligned(table, 16) &&
+                   (!hk_in || aligned(hk_in, 16)) && (!hv_in || aligned(hv_in, 16)),
+               kMisaligned);
+  DecodeParams p{q, k, v, g, delta, beta, table, q_norm_weight, k_norm_weight, hk_in, hv_in,
+                 clock_in, hk_out, hv_out, clock_out, out, B * H, H, q_eps, k_eps, scale};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid(B * H);
+#define CYFA_DECODE(T, KK, VV) decode_step_kernel<T, KK, VV><<<grid, 256, 0, s>>>(p)
+  if (dtype == 0) {
+    if (K == 256 && V == 256) CYFA_DECODE(__nv_bfloat16, 256, 256);
+    else if (K == 128 && V == 128) CYFA_DECODE(__nv_bfloat16, 128, 128);
+    else if (K == 256) CYFA_DECODE(__nv_bfloat16, 256, 128);
+    else CYFA_DECODE(__nv_bfloat16, 128, 256);
+  } else {
+    if (K == 256 && V == 256) CYFA_DECODE(float, 256, 256);
+    else if (K == 128 && V == 128) CYFA_DECODE(float, 128, 128);
+    else if (K == 256) CYFA_DECODE(float, 256, 128);
+    else CYFA_DECODE(float, 128, 256);
+  }
+#undef CYFA_DECODE
+  return launch_status();
+}
+
+int cyfa_gates_fwd(const float* g, const float* delta, const float* beta, const float* clock0,
+                   float* G, float* lam, float* beta_h, float* clock_out, int B, int T, int H,
+                   void* stream) {
+  CYFA_REQUIRE(g && delta && beta && G && lam && beta_h, kNullPointer);
+  CYFA_REQUIRE(B > 0 && T > 0 && H > 0, kBadShape);
+  const int TP = (T + 127) / 128 * 128;
+  GatesParams p{g, delta, beta, clock0, G, lam, beta_h, clock_out, B, T, H, TP};
+  gates_fwd_kernel<<<B * H, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return launch_status();
+}
+
+int cyfa_token_fwd(const void* q, const void* k, const float* q_norm_weight,
+                   const float* k_norm_weight, const float* lam, const float* beta_h, void* qn,
+                   void* kn, void* w, float* q_rs, float* k_rs, int B, int T, int H, int K,
+                   float q_eps, float k_eps, void* stream) {
+  CYFA_REQUIRE(q && k && q_norm_weight && k_norm_weight && lam && beta_h && qn && kn && w &&
+                   q_rs && k_rs,
+               kNullPointer);
+  CYFA_REQUIRE(B > 0 && T > 0 && H > 0 && (K == 128 || K == 256), kBadShape);
+  CYFA_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(qn, 16) && aligned(kn, 16) &&
+                   aligned(w, 16),
+               kMisaligned);
+  const int TP = (T + 127) / 128 * 128;
+  TokenFwdParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                   q_norm_weight, k_norm_weight, lam, beta_h,
+                   static_cast<__nv_bfloat16*>(qn), static_cast<__nv_bfloat16*>(kn),
+                   static_cast<__nv_bfloat16*>(w), q_rs, k_rs, B, T, H, TP, q_eps, k_eps};
+  const size_t rows = size_t(B) * H * TP;
+  const dim3 grid(unsigned((rows + 7) / 8));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 256) token_fwd_kernel<256><<<grid, 256, 0, s>>>(p);
+  else token_fwd_kernel<128><<<grid, 256, 0, s>>>(p);
+  return launch_status();
+}
+
+int cyfa_token_bwd(const void* q, const void* k, const float* q_norm_weight,
+                   const float* k_norm_weight, const float* q_rs, const float* k_rs,
+                   const float* dqn, const float* dkn, const float* lam, const float* beta_h,
+                   const float* dw, void* dq, void* dk, float* dqw_part, float* dkw_part,
+                   float* dlam, float* dbeta_h, int B, int T, int H, int K, void* stream) {
+  CYFA_REQUIRE(q && k && q_norm_weight && k_norm_weight && q_rs && k_rs && dqn && dkn && lam &&
+                   beta_h && dw && dq && dk && dqw_part && dkw_part && dlam && dbeta_h,
+               kNullPointer);
+  CYFA_REQUIRE(B > 0 && T > 0 && H > 0 && (K == 128 || K == 256), kBadShape);
+  const int TP = (T + 127) / 128 * 128;
+  TokenBwdParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                   q_norm_weight, k_norm_weight, q_rs, k_rs, dqn, dkn, lam, beta_h, dw,
+                   static_cast<__nv_bfloat16*>(dq), static_cast<__nv_bfloat16*>(dk), dqw_part,
+                   dkw_part, dlam, dbeta_h, B, T, H, TP};
+  const size_t rows = size_t(B) * H * TP;
+  const dim3 grid(unsigned((rows + 7) / 8));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 256) token_bwd_kernel<256><<<grid, 256, 0, s>>>(p);
+  else token_bwd_kernel<128><<<grid, 256, 0, s>>>(p);
+  return launch_status();
+}
+
+int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h, const float* dclock,
+                   float* dg, float* ddelta, float* dbeta, float* dclock0, int B, int T, int H,
+                   void* stream) {
+  CYFA_REQUIRE(dG && dlam && dbeta_h && dg && ddelta && dbeta, kNullPointer);
+  CYFA_REQUIRE(B > 0 && T > 0 && H > 0, kBadShape);
+  const int TP = (T + 127) / 128 * 128;
+  GatesBwdParams p{dG, dlam, dbeta_h, dclock, dg, ddelta, dbeta, dclock0, B, T, H, TP};
+  gates_bwd_kernel<<<B * H, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return launch_status();
+}
+
+}  // extern "C"

@@ -1,0 +1,8 @@
+// Single translation unit of the CyFA CUDA library (libcyfa.so): every kernel
+// file and the C-ABI are compiled together so that device globals (the error
+// word) and templates need no relocatable device code.
+#include "cyfa_common.cuh"
+#include "selftest.cu"
+#include "decode.cu"
+#include "prep.cu"
+#include "capi.cu"

@@ -1,0 +1,348 @@
+// Per-token preparation kernels of the chunked CyFA forward and their adjoints.
+//
+//  gates_fwd   : one CTA per (b,h).  Moves g/delta/beta from the public [B,T,H]
+//                layout to head-major [B,H,TP] (zero padded), and computes with
+//                fixed-order (deterministic) block scans
+//                  lam_t = clock0 + sum_{s<=t} delta_s              (ops/utils.py:229-302)
+//                  G_t   = log2(e) * sum_{s<=t, same 128-token tile} g_s   (ops/utils.py:495-520,
+//                          with the chunk widened from 64 to 128 tokens)
+//                  clock_T = clock0 + sum_t delta_t                  (ops/utils.py:305-348)
+//  token_fwd   : one warp per (b,t,h).  Per-head RMSNorm of q and k into head-major
+//                bf16 (ops/qk_norm.py:64-107) and the write vector
+//                w_t = beta_t U(-lam_t) b (ops/utils.py:543-587) as bf16.
+//  token_bwd   : adjoints of token_fwd: dq, dk (public layout), per-block partial
+//                sums of the norm-weight gradients, and dlam, dbeta of the write
+//                vector (ops/qk_norm.py:109-165, ops/utils.py:589-640).
+//  gates_bwd   : one CTA per (b,h): ddelta = reverse cumsum of dlam (+ d clock_T),
+//                dg = log2(e) * in-tile reverse cumsum of dG, layout back to [B,T,H].
+#include "cyfa_common.cuh"
+#include "phase.cuh"
+
+namespace cyfa {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct GatesParams {
+  const float* g;       // [B,T,H]
+  const float* delta;   // [B,T,H]
+  const float* beta;    // [B,T,H]
+  const float* clock0;  // [B,H] or null
+  float* G;             // [B,H,TP] log2 in-tile cumsum
+  float* lam;           // [B,H,TP]
+  float* beta_h;        // [B,H,TP]
+  float* clock_out;     // [B,H] or null
+  int B, T, H, TP;
+};
+
+// Inclusive scan over 128 threads in a fixed order; returns the prefix and
+// writes the block total to *total.
+__device__ __forceinline__ float scan128(float x, float* buf, float* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x = __fadd_rn(x, y);
+  }
+  if (lane == 31) buf[w] = x;
+  __syncthreads();
+  float carry = 0.f;
+  for (int i = 0; i < w; ++i) carry = __fadd_rn(carry, buf[i]);
+  const float t = __fadd_rn(__fadd_rn(__fadd_rn(buf[0], buf[1]), buf[2]), buf[3]);
+  __syncthreads();
+  *total = t;
+  return __fadd_rn(x, carry);
+}
+
+__global__ void __launch_bounds__(128) gates_fwd_kernel(GatesParams p) {
+  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
+  __shared__ float buf[4];
+  float clock = p.clock0 ? p.clock0[bh] : 0.f;
+  const size_t obase = size_t(bh) * p.TP;
+  for (int t0 = 0; t0 < p.TP; t0 += 128) {
+    const int t = t0 + threadIdx.x;
+    float gv = 0.f, dv = 0.f, bv = 0.f;
+    if (t < p.T) {
+      const size_t i = (size_t(b) * p.T + t) * p.H + h;
+      gv = p.g[i];
+      dv = p.delta[i];
+      bv = p.beta[i];
+    }
+    float tot;
+    const float gsum = scan128(gv, buf, &tot);
+    const float dsum = scan128(dv, buf, &tot);
+    p.G[obase + t] = gsum * kLog2e;
+    p.lam[obase + t] = __fadd_rn(clock, dsum);
+    p.beta_h[obase + t] = bv;
+    clock = __fadd_rn(clock, tot);
+  }
+  if (threadIdx.x == 0 && p.clock_out) p.clock_out[bh] = clock;
+}
+
+struct TokenFwdParams {
+  const __nv_bfloat16* q;  // [B,T,H,K]
+  const __nv_bfloat16* k;  // [B,T,H,K]
+  const float* qw;         // [K]
+  const float* kw;         // [K]
+  const float* lam;        // [B,H,TP]
+  const float* beta_h;     // [B,H,TP]
+  __nv_bfloat16* qn;       // [B,H,TP,K]
+  __nv_bfloat16* kn;       // [B,H,TP,K]
+  __nv_bfloat16* w;        // [B,H,TP,128]
+  float* q_rs;             // [B,H,TP]
+  float* k_rs;             // [B,H,TP]
+  int B, T, H, TP;
+  float q_eps, k_eps;
+};
+
+template <int K>
+__global__ void __launch_bounds__(256) token_fwd_kernel(TokenFwdParams p) {
+  constexpr int E = K / 32;  // elements per lane (8 for K=256, 4 for K=128)
+  const int lane = threadIdx.x & 31;
+  const size_t row = size_t(blockIdx.x) * 8 + (threadIdx.x >> 5);  // over B*H*TP
+  if (row >= size_t(p.B) * p.H * p.TP) return;
+  const int t = int(row % p.TP);
+  const size_t bh = row / p.TP;
+  const int b = int(bh / p.H), h = int(bh % p.H);
+  float qv[E], kv[E];
+  if (t < p.T) {
+    const size_t src = ((size_t(b) * p.T + t) * p.H + h) * K + lane * E;
+    if constexpr (E == 8) {
+      const uint4 a = *reinterpret_cast<const uint4*>(p.q + src);
+      const uint4 c = *reinterpret_cast<const uint4*>(p.k + src);
+      const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&a);
+      const __nv_bfloat16* cp = reinterpret_cast<const __nv_bfloat16*>(&c);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        qv[j] = __bfloat162float(ap[j]);
+        kv[j] = __bfloat162float(cp[j]);
+      }
+    } else {
+      const uint2 a = *reinterpret_cast<const uint2*>(p.q + src);
+      const uint2 c = *reinterpret_cast<const uint2*>(p.k + src);
+      const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&a);
+      const __nv_bfloat16* cp = reinterpret_cast<const __nv_bfloat16*>(&c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        qv[j] = __bfloat162float(ap[j]);
+        kv[j] = __bfloat162float(cp[j]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < E; ++j) qv[j] = kv[j] = 0.f;
+  }
+  float q2 = 0.f, k2 = 0.f;
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    q2 += qv[j] * qv[j];
+    k2 += kv[j] * kv[j];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    q2 += __shfl_xor_sync(0xffffffffu, q2, o);
+    k2 += __shfl_xor_sync(0xffffffffu, k2, o);
+  }
+  const float qr = rsqrtf(q2 / K + p.q_eps), kr = rsqrtf(k2 / K + p.k_eps);
+  uint32_t qo[E / 2], ko[E / 2];
+#pragma unroll
+  for (int j = 0; j < E; j += 2) {
+    const int d = lane * E + j;
+    qo[j / 2] = pack_bf16(qv[j] * qr * p.qw[d], qv[j + 1] * qr * p.qw[d + 1]);
+    ko[j / 2] = pack_bf16(kv[j] * kr * p.kw[d], kv[j + 1] * kr * p.kw[d + 1]);
+  }
+  const size_t dst = row * K + lane * E;
+  if constexpr (E == 8) {
+    *reinterpret_cast<uint4*>(p.qn + dst) = make_uint4(qo[0], qo[1], qo[2], qo[3]);
+    *reinterpret_cast<uint4*>(p.kn + dst) = make_uint4(ko[0], ko[1], ko[2], ko[3]);
+  } else {
+    *reinterpret_cast<uint2*>(p.qn + dst) = make_uint2(qo[0], qo[1]);
+    *reinterpret_cast<uint2*>(p.kn + dst) = make_uint2(ko[0], ko[1]);
+  }
+  if (lane == 0) {
+    p.q_rs[row] = t < p.T ? qr : 0.f;
+    p.k_rs[row] = t < p.T ? kr : 0.f;
+  }
+  // write vector: lane handles pairs lane and lane + 32
+  const float lam = p.lam[row], bt = p.beta_h[row];
+  uint32_t wo[2];
+#pragma unroll
+  for (int part = 0; part < 2; ++part) {
+    const int pair = lane + 32 * part;
+    float s, c;
+    sincosf(clock_phase(lam, pair), &s, &c);
+    const float a = bt * atom_scale(pair);
+    wo[part] = pack_bf16(a * c, -a * s);
+  }
+  uint32_t* wrow = reinterpret_cast<uint32_t*>(p.w + row * 128);
+  wrow[lane] = wo[0];
+  wrow[lane + 32] = wo[1];
+}
+
+template __global__ void token_fwd_kernel<256>(TokenFwdParams);
+template __global__ void token_fwd_kernel<128>(TokenFwdParams);
+
+struct TokenBwdParams {
+  const __nv_bfloat16* q;   // [B,T,H,K]
+  const __nv_bfloat16* k;
+  const float* qw;
+  const float* kw;
+  const float* q_rs;        // [B,H,TP]
+  const float* k_rs;
+  const float* dqn;         // [B,H,TP,K] fp32 gradient of the normalised q
+  const float* dkn;
+  const float* lam;         // [B,H,TP]
+  const float* beta_h;
+  const float* dw;          // [B,H,TP,128] gradient of the write vector (both passes)
+  __nv_bfloat16* dq;        // [B,T,H,K]
+  __nv_bfloat16* dk;
+  float* dqw_part;          // [gridDim.x, K]
+  float* dkw_part;
+  float* dlam;              // [B,H,TP] (phase part, added to by the readout part)
+  float* dbeta;             // [B,H,TP]
+  int B, T, H, TP;
+};
+
+// 8 warps per block, one (b,t,h) row each.  Norm-weight gradient partials are
+// reduced across the 8 rows of the block in a fixed order.
+template <int K>
+__global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
+  constexpr int E = K / 32;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  __shared__ float pq[8][K], pk[8][K];
+  const size_t row = size_t(blockIdx.x) * 8 + wid;
+  const bool live = row < size_t(p.B) * p.H * p.TP;
+  const int t = live ? int(row % p.TP) : 0;
+  const size_t bh = live ? row / p.TP : 0;
+  const int b = int(bh / p.H), h = int(bh % p.H);
+  const bool real = live && t < p.T;
+  float xq[E], xk[E], gq[E], gk[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) xq[j] = xk[j] = gq[j] = gk[j] = 0.f;
+  const size_t pub = ((size_t(b) * p.T + t) * p.H + h) * K + lane * E;
+  if (real) {
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      xq[j] = __bfloat162float(p.q[pub + j]);
+      xk[j] = __bfloat162float(p.k[pub + j]);
+      gq[j] = p.dqn[row * K + lane * E + j];
+      gk[j] = p.dkn[row * K + lane * E + j];
+    }
+  }
+  const float qr = real ? p.q_rs[row] : 0.f, kr = real ? p.k_rs[row] : 0.f;
+  float dotq = 0.f, dotk = 0.f;
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    const int d = lane * E + j;
+    dotq += gq[j] * p.qw[d] * xq[j];
+    dotk += gk[j] * p.kw[d] * xk[j];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    dotq += __shfl_xor_sync(0xffffffffu, dotq, o);
+    dotk += __shfl_xor_sync(0xffffffffu, dotk, o);
+  }
+  dotq *= qr * qr / K;
+  dotk *= kr * kr / K;
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    const int d = lane * E + j;
+    if (real) {
+      p.dq[pub + j] = __float2bfloat16_rn((gq[j] * p.qw[d] - xq[j] * dotq) * qr);
+      p.dk[pub + j] = __float2bfloat16_rn((gk[j] * p.kw[d] - xk[j] * dotk) * kr);
+    }
+    pq[wid][d] = xq[j] * qr * gq[j];
+    pk[wid][d] = xk[j] * kr * gk[j];
+  }
+  // write-vector adjoint (ops/utils.py:598-616)
+  if (live) {
+    const float lam = p.lam[row], bt = p.beta_h[row];
+    float dl = 0.f, db = 0.f;
+#pragma unroll
+    for (int part = 0; part < 2; ++part) {
+      const int pair = lane + 32 * part;
+      float s, c;
+      sincosf(clock_phase(lam, pair), &s, &c);
+      const float sc = atom_scale(pair);
+      const float de = p.dw[row * 128 + 2 * pair], dd = p.dw[row * 128 + 2 * pair + 1];
+      db += de * sc * c - dd * sc * s;
+      dl += (-de * bt * sc * s - dd * bt * sc * c) * (pair * kTwoPiOver127);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      dl += __shfl_xor_sync(0xffffffffu, dl, o);
+      db += __shfl_xor_sync(0xffffffffu, db, o);
+    }
+    if (lane == 0) {
+      p.dlam[row] = dl;
+      p.dbeta[row] = db;
+    }
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < K; d += 256) {
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sq += pq[i][d];
+      sk += pk[i][d];
+    }
+    p.dqw_part[size_t(blockIdx.x) * K + d] = sq;
+    p.dkw_part[size_t(blockIdx.x) * K + d] = sk;
+  }
+}
+
+template __global__ void token_bwd_kernel<256>(TokenBwdParams);
+template __global__ void token_bwd_kernel<128>(TokenBwdParams);
+
+struct GatesBwdParams {
+  const float* dG;       // [B,H,TP] gradient of the log2 in-tile cumsum
+  const float* dlam;     // [B,H,TP] total clock gradient
+  const float* dbeta_h;  // [B,H,TP]
+  const float* dclock;   // [B,H] gradient of the final clock, or null
+  float* dg;             // [B,T,H]
+  float* ddelta;         // [B,T,H]
+  float* dbeta;          // [B,T,H]
+  float* dclock0;        // [B,H] or null
+  int B, T, H, TP;
+};
+
+// Reverse inclusive scan over 128 threads (suffix sums), fixed order.
+__device__ __forceinline__ float rscan128(float x, float* buf, float* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = __shfl_down_sync(0xffffffffu, x, o);
+    if (lane + o < 32) x = __fadd_rn(x, y);
+  }
+  if (lane == 0) buf[w] = x;
+  __syncthreads();
+  float carry = 0.f;
+  for (int i = 3; i > w; --i) carry = __fadd_rn(carry, buf[i]);
+  const float t = __fadd_rn(__fadd_rn(__fadd_rn(buf[3], buf[2]), buf[1]), buf[0]);
+  __syncthreads();
+  *total = t;
+  return __fadd_rn(x, carry);
+}
+
+__global__ void __launch_bounds__(128) gates_bwd_kernel(GatesBwdParams p) {
+  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
+  __shared__ float buf[4];
+  float carry = p.dclock ? p.dclock[bh] : 0.f;
+  const size_t base = size_t(bh) * p.TP;
+  for (int t0 = p.TP - 128; t0 >= 0; t0 -= 128) {
+    const int t = t0 + threadIdx.x;
+    float tot;
+    const float gs = rscan128(p.dG[base + t], buf, &tot);
+    const float ls = rscan128(p.dlam[base + t], buf, &tot);
+    const float dd = __fadd_rn(carry, ls);
+    carry = __fadd_rn(carry, tot);
+    if (t < p.T) {
+      const size_t i = (size_t(b) * p.T + t) * p.H + h;
+      p.dg[i] = gs * kLog2e;
+      p.ddelta[i] = dd;
+      p.dbeta[i] = p.dbeta_h[base + t];
+    }
+  }
+  if (threadIdx.x == 0 && p.dclock0) p.dclock0[bh] = carry;
+}
+
+}  // namespace cyfa

@@ -1,0 +1,92 @@
+"""ctypes binding of libcyfa.so, the sm_100a CUDA library behind the ops.
+
+The library is built in-tree (``python __graft_entry__.py`` or ``make -C
+cyfa-jittor_b200/csrc``).  There is no CPU fallback: if the library or a CUDA
+device is missing, every op raises.
+"""
+
+import ctypes
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libcyfa.so")
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_f = ctypes.c_float
+
+# name -> argtypes (restype is int for all)
+_SIGNATURES = {
+    "cyfa_version": [],
+    "cyfa_device_error": [_i],
+    "cyfa_selftest_umma": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
+    "cyfa_decode_step": [_vp] * 16 + [_i] * 5 + [_f] * 3 + [_vp],
+    "cyfa_gates_fwd": [_vp] * 8 + [_i] * 3 + [_vp],
+    "cyfa_token_fwd": [_vp] * 11 + [_i] * 4 + [_f] * 2 + [_vp],
+    "cyfa_token_bwd": [_vp] * 17 + [_i] * 4 + [_vp],
+    "cyfa_gates_bwd": [_vp] * 8 + [_i] * 3 + [_vp],
+}
+
+
+class CyfaError(RuntimeError):
+    """A libcyfa entry point returned a non-zero status."""
+
+
+_lib = None
+
+
+def lib():
+    """Loads libcyfa.so once; raises if it is missing (no fallback path)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"CyFA CUDA library not built: {LIB_PATH} is missing. "
+                "Build it with `make -C cyfa-jittor_b200/csrc` (nvcc, sm_100a)."
+            )
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, args in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int
+        handle.cyfa_strerror.argtypes = [ctypes.c_int]
+        handle.cyfa_strerror.restype = ctypes.c_char_p
+        _lib = handle
+    return _lib
+
+
+def call(name, *args):
+    """Calls an entry point and raises CyfaError on a non-zero status."""
+    status = getattr(lib(), name)(*args)
+    if status != 0:
+        msg = lib().cyfa_strerror(status).decode()
+        raise CyfaError(f"{name} failed with status {status}: {msg}")
+
+
+def ptr(t):
+    """Device pointer of a tensor (None for None)."""
+    if t is None:
+        return None
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def stream():
+    """The current torch CUDA stream as a raw handle."""
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def require_cuda(*tensors):
+    """Raises unless every tensor lives on a CUDA device (no CPU fallback)."""
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError(
+                "CyFA ops run only on CUDA tensors (sm_100a); there is no CPU path. "
+                "The CPU restatement lives in oracle/ and is test infrastructure."
+            )
+
+
+def device_error(reset=True):
+    """Returns the device error word (1 = a bounded wait timed out)."""
+    return lib().cyfa_device_error(1 if reset else 0)

@@ -1,0 +1,112 @@
+/*
+ * CyFA B200 hot path -- C ABI.
+ *
+ * Framework-neutral entry points over raw device pointers and a CUDA stream
+ * (passed as void*).  The caller allocates every output and workspace; the
+ * library allocates nothing on these paths.  Every entry point checks its
+ * arguments on the host before launching and returns a status:
+ *   0  ok
+ *  >0  argument error (unsupported shape, null or misaligned pointer, ...);
+ *      nothing was launched
+ *  <0  CUDA launch error (negated cudaError_t)
+ * Device-side bounded waits that run out record a code that
+ * cyfa_device_error() returns.
+ *
+ * Layouts (row-major, contiguous):
+ *   public  q,k [B,T,H,K] bf16; v [B,T,H,V] bf16; g/delta/beta [B,T,H] f32
+ *   head-major (internal, T padded to TP = ceil(T/128)*128):
+ *           qn,kn [B,H,TP,K] bf16; w [B,H,TP,128] bf16; G, lam, beta_h [B,H,TP] f32
+ *   states  hk [B,H,K,128] f32; hv [B,H,128,V] f32; clock [B,H] f32
+ *   table   [H,127,128] f32 (readout R . Phi); table_bf [H,128,128] bf16, row 127 = 0
+ *
+ * The reference binds these operations as Jittor ops built from generated CUDA
+ * strings (cyclic_flow_attention/ops/*); each declaration names the reference
+ * interface it replaces.
+ */
+#ifndef CYFA_H_
+#define CYFA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library version: major*100 + minor. */
+int cyfa_version(void);
+
+/* Human-readable text of a status code. */
+const char* cyfa_strerror(int status);
+
+/* Reads (and, if reset != 0, clears) the device error word of the current
+ * device: 0 = no device-side failure; 1 = a bounded wait timed out.
+ * Synchronises the device. */
+int cyfa_device_error(int reset);
+
+/* ---------------------------------------------------------------- decode
+ * One constant-memory decode step (T = 1).
+ * Replaces: fused_recurrent_cyfa, cyclic_flow_attention/ops/fused_recurrent.py:10-200
+ * (kernel :55-188).
+ * q,k [B,1,H,K], v [B,1,H,V] in dtype `dtype` (0 = bf16, 1 = f32); g, delta, beta
+ * [B,1,H] f32; table [H,127,128] f32; norm weights [K] f32.  hk_in/hv_in/clock_in
+ * may be NULL (zero initial state).  Outputs may alias the inputs (in place).
+ * K, V in {128, 256}. */
+int cyfa_decode_step(const void* q, const void* k, const void* v, const float* g,
+                     const float* delta, const float* beta, const float* table,
+                     const float* q_norm_weight, const float* k_norm_weight,
+                     const float* hk_in, const float* hv_in, const float* clock_in,
+                     float* hk_out, float* hv_out, float* clock_out, void* out, int B, int H,
+                     int K, int V, int dtype, float q_eps, float k_eps, float scale,
+                     void* stream);
+
+/* ---------------------------------------------------------------- forward prep
+ * Gate layout + clock scan + in-tile log2 gate cumsum.
+ * Replaces: head_gates (ops/utils.py:434-492), ClockScan (:229-302),
+ * ClockTotal (:305-348), local_log2_cumsum (:495-520); tiles are 128 tokens.
+ * clock0 and clock_out may be NULL. */
+int cyfa_gates_fwd(const float* g, const float* delta, const float* beta, const float* clock0,
+                   float* G, float* lam, float* beta_h, float* clock_out, int B, int T, int H,
+                   void* stream);
+
+/* Per-head q/k RMSNorm into head-major bf16 plus the write vector.
+ * Replaces: VectorNorm / HeadRMSNorm (ops/qk_norm.py:64-107, 206-239), head_layout
+ * (ops/utils.py:351-387), PhaseWriteOnly (ops/utils.py:543-587).  K in {128, 256}. */
+int cyfa_token_fwd(const void* q, const void* k, const float* q_norm_weight,
+                   const float* k_norm_weight, const float* lam, const float* beta_h, void* qn,
+                   void* kn, void* w, float* q_rs, float* k_rs, int B, int T, int H, int K,
+                   float q_eps, float k_eps, void* stream);
+
+/* ---------------------------------------------------------------- backward prep
+ * Adjoint of cyfa_token_fwd.  dqn/dkn [B,H,TP,K] f32, dw [B,H,TP,128] f32 in;
+ * dq/dk public-layout bf16, norm-weight partial sums [ceil(B*H*TP/8), K] f32,
+ * dlam (write-vector part) and dbeta_h [B,H,TP] f32 out.
+ * Replaces: VectorNorm.grad (ops/qk_norm.py:109-165), PhaseWriteOnly.grad
+ * (ops/utils.py:589-640). */
+int cyfa_token_bwd(const void* q, const void* k, const float* q_norm_weight,
+                   const float* k_norm_weight, const float* q_rs, const float* k_rs,
+                   const float* dqn, const float* dkn, const float* lam, const float* beta_h,
+                   const float* dw, void* dq, void* dk, float* dqw_part, float* dkw_part,
+                   float* dlam, float* dbeta_h, int B, int T, int H, int K, void* stream);
+
+/* Adjoint of cyfa_gates_fwd: dG, dlam, dbeta_h [B,H,TP] (+ dclock [B,H] or NULL)
+ * -> dg, ddelta, dbeta [B,T,H] and dclock0 [B,H] (or NULL).
+ * Replaces: ClockScan.grad (ops/utils.py:297-298), ClockTotal.grad (:343-344),
+ * HeadGates.grad (:459-488) and the local cumsum adjoint. */
+int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h,
+                   const float* dclock, float* dg, float* ddelta, float* dbeta,
+                   float* dclock0, int B, int T, int H, void* stream);
+
+/* ---------------------------------------------------------------- self test
+ * C[128,N] = A * B through TMA + tcgen05 (test hook for the UMMA descriptor and
+ * swizzle encodings).  A is [128,K] (a_mn = 0) or [K,128] (a_mn = 1); B is [N,K]
+ * (b_mn = 0) or [K,N] (b_mn = 1); bf16, row-major.  K in {64,...,256} step 64,
+ * N in {64,128,256}.  No counterpart in the reference. */
+int cyfa_selftest_umma(const void* a, const void* b, float* c, int K, int N, int a_mn,
+                       int b_mn, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CYFA_H_ */

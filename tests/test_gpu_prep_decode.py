@@ -1,0 +1,231 @@
+"""GPU parity of the tcgen05 self-test GEMM, the decode step and the per-token
+prep kernels against the CPU oracle (bf16 paths: rel-L2 <= 1e-2; fp32-accumulated
+paths: <= 1e-4)."""
+
+import math
+
+import pytest
+import torch
+
+from gpu_util import bf16_cpu, rel_l2, seeded
+from oracle import cyfa_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 1e-2
+F32_TOL = 1e-4
+
+
+@pytest.fixture(scope="module")
+def L():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+    from cyclic_flow_attention import _lib
+
+    return _lib
+
+
+@pytest.mark.parametrize("a_mn", [0, 1])
+@pytest.mark.parametrize("b_mn", [0, 1])
+@pytest.mark.parametrize("K,N", [(64, 64), (128, 128), (256, 256), (192, 128)])
+def test_umma_selftest(L, a_mn, b_mn, K, N):
+    gen = seeded(K * 7 + N + a_mn * 3 + b_mn)
+    A = torch.randn(128, K, generator=gen).to(torch.bfloat16)
+    Bm = torch.randn(K, N, generator=gen).to(torch.bfloat16)
+    a_store = (A.t().contiguous() if a_mn else A).cuda()
+    b_store = (Bm if b_mn else Bm.t().contiguous()).cuda()
+    c = torch.zeros(128, N, device="cuda")
+    L.call("cyfa_selftest_umma", L.ptr(a_store), L.ptr(b_store), L.ptr(c), K, N, a_mn, b_mn,
+           L.stream())
+    torch.cuda.synchronize()
+    ref = A.float() @ Bm.float()
+    assert rel_l2(c, ref) < 1e-5
+    assert L.device_error() == 0
+
+
+def _decode_inputs(B, H, K, V, seed, with_state=True):
+    gen = seeded(seed)
+    q = torch.randn(B, 1, H, K, generator=gen)
+    k = torch.randn(B, 1, H, K, generator=gen)
+    v = torch.randn(B, 1, H, V, generator=gen)
+    g = torch.log(torch.rand(B, 1, H, generator=gen) * 0.1 + 0.9)
+    delta = torch.sigmoid(torch.randn(B, 1, H, generator=gen))
+    beta = torch.sigmoid(torch.randn(B, 1, H, generator=gen))
+    readout = torch.eye(127).expand(H, -1, -1) + 0.05 * torch.randn(H, 127, 127, generator=gen)
+    qw = 1 + 0.1 * torch.randn(K, generator=gen)
+    kw = 1 + 0.1 * torch.randn(K, generator=gen)
+    state = None
+    if with_state:
+        state = (0.1 * torch.randn(B, H, K, 128, generator=gen),
+                 0.1 * torch.randn(B, H, 128, V, generator=gen),
+                 torch.rand(B, H, generator=gen) * 3000)
+    return q, k, v, g, delta, beta, readout, qw, kw, state
+
+
+@pytest.mark.parametrize("K,V", [(256, 256), (128, 128), (256, 128)])
+@pytest.mark.parametrize("with_state", [True, False])
+def test_decode_step_matches_oracle(L, K, V, with_state):
+    B, H = 3, 2
+    q, k, v, g, delta, beta, readout, qw, kw, state = _decode_inputs(B, H, K, V, 11, with_state)
+    qb, kb, vb = bf16_cpu(q), bf16_cpu(k), bf16_cpu(v)
+    ref_o, ref_state = O.fused_recurrent_cyfa(qb, kb, vb, g, delta, beta, readout, qw, kw,
+                                              initial_state=state, output_final_state=True)
+    table = O.readout_table(readout).float().cuda()
+    dev = lambda x: x.contiguous().cuda()
+    out = torch.empty(B, 1, H, V, device="cuda", dtype=torch.bfloat16)
+    hk = torch.empty(B, H, K, 128, device="cuda")
+    hv = torch.empty(B, H, 128, V, device="cuda")
+    clk = torch.empty(B, H, device="cuda")
+    st = [dev(x) for x in state] if state is not None else [None, None, None]
+    args = [dev(q.to(torch.bfloat16)), dev(k.to(torch.bfloat16)), dev(v.to(torch.bfloat16)),
+            dev(g), dev(delta), dev(beta), table, dev(qw), dev(kw)] + st + [hk, hv, clk, out]
+    L.call("cyfa_decode_step", *[L.ptr(a) for a in args], B, H, K, V, 0, 1e-6, 1e-6,
+           K ** -0.5, L.stream())
+    torch.cuda.synchronize()
+    assert rel_l2(out, ref_o) < BF16_TOL
+    assert rel_l2(hk, ref_state[0]) < BF16_TOL
+    assert rel_l2(hv, ref_state[1]) < BF16_TOL
+    assert rel_l2(clk, ref_state[2]) < F32_TOL
+    assert L.device_error() == 0
+
+
+def test_decode_fp32_inputs(L):
+    B, H, K, V = 2, 2, 256, 256
+    q, k, v, g, delta, beta, readout, qw, kw, state = _decode_inputs(B, H, K, V, 12)
+    ref_o, ref_state = O.fused_recurrent_cyfa(q, k, v, g, delta, beta, readout, qw, kw,
+                                              initial_state=state, output_final_state=True)
+    table = O.readout_table(readout).float().cuda()
+    out = torch.empty(B, 1, H, V, device="cuda")
+    hk = torch.empty(B, H, K, 128, device="cuda")
+    hv = torch.empty(B, H, 128, V, device="cuda")
+    clk = torch.empty(B, H, device="cuda")
+    args = [x.contiguous().cuda() for x in (q, k, v, g, delta, beta)] + [table] + \
+        [qw.cuda(), kw.cuda()] + [x.cuda() for x in state] + [hk, hv, clk, out]
+    L.call("cyfa_decode_step", *[L.ptr(a) for a in args], B, H, K, V, 1, 1e-6, 1e-6,
+           K ** -0.5, L.stream())
+    torch.cuda.synchronize()
+    assert rel_l2(out, ref_o) < F32_TOL
+    assert rel_l2(hk, ref_state[0]) < F32_TOL
+    assert rel_l2(hv, ref_state[1]) < F32_TOL
+
+
+@pytest.mark.parametrize("T", [1, 100, 128, 300])
+def test_gates_fwd(L, T):
+    B, H = 2, 3
+    gen = seeded(T)
+    g = torch.log(torch.rand(B, T, H, generator=gen) * 0.1 + 0.9)
+    delta = torch.sigmoid(torch.randn(B, T, H, generator=gen))
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=gen))
+    clock0 = torch.rand(B, H, generator=gen) * 500
+    TP = (T + 127) // 128 * 128
+    G = torch.empty(B, H, TP, device="cuda")
+    lam = torch.empty_like(G)
+    bh = torch.empty_like(G)
+    clk = torch.empty(B, H, device="cuda")
+    L.call("cyfa_gates_fwd", *[L.ptr(x) for x in (g.cuda(), delta.cuda(), beta.cuda(),
+                                                   clock0.cuda(), G, lam, bh, clk)],
+           B, T, H, L.stream())
+    torch.cuda.synchronize()
+    ref_lam = O.clock_scan(delta.double().permute(0, 2, 1), clock0.double())
+    assert rel_l2(lam[..., :T], ref_lam) < F32_TOL
+    gp = torch.nn.functional.pad(g.double().permute(0, 2, 1), (0, TP - T))
+    ref_G = gp.reshape(B, H, TP // 128, 128).cumsum(-1).reshape(B, H, TP) / math.log(2)
+    assert rel_l2(G, ref_G) < F32_TOL
+    assert torch.equal(bh[..., :T].cpu(), beta.permute(0, 2, 1))
+    assert rel_l2(clk, delta.double().sum(1) + clock0.double()) < F32_TOL
+    # padded tail: the clock stops and beta is zero
+    if TP > T:
+        assert torch.all(bh[..., T:] == 0)
+        assert torch.all(lam[..., T:] == lam[..., T - 1:T])
+
+
+@pytest.mark.parametrize("K", [256, 128])
+def test_token_fwd_bwd(L, K):
+    B, T, H = 2, 130, 2
+    TP = 256
+    gen = seeded(K)
+    q = torch.randn(B, T, H, K, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, T, H, K, generator=gen).to(torch.bfloat16)
+    qw = 1 + 0.1 * torch.randn(K, generator=gen)
+    kw = 1 + 0.1 * torch.randn(K, generator=gen)
+    lam = torch.rand(B, H, TP, generator=gen) * 4000
+    beta = torch.rand(B, H, TP, generator=gen)
+    beta[..., T:] = 0
+    dev = lambda x: x.contiguous().cuda()
+    qn = torch.empty(B, H, TP, K, device="cuda", dtype=torch.bfloat16)
+    kn = torch.empty_like(qn)
+    w = torch.empty(B, H, TP, 128, device="cuda", dtype=torch.bfloat16)
+    qrs = torch.empty(B, H, TP, device="cuda")
+    krs = torch.empty_like(qrs)
+    L.call("cyfa_token_fwd", *[L.ptr(x) for x in (dev(q), dev(k), dev(qw), dev(kw), dev(lam),
+                                                   dev(beta), qn, kn, w, qrs, krs)],
+           B, T, H, K, 1e-6, 1e-6, L.stream())
+    torch.cuda.synchronize()
+    # forward parity
+    qf = q.float().requires_grad_()
+    kf = k.float().requires_grad_()
+    qwf = qw.clone().requires_grad_()
+    kwf = kw.clone().requires_grad_()
+    lamf = lam[..., :T].clone().double().requires_grad_()
+    betaf = beta[..., :T].clone().double().requires_grad_()
+    ref_q = O.head_rmsnorm(qf, qwf, 1e-6)
+    ref_k = O.head_rmsnorm(kf, kwf, 1e-6)
+    ref_w, _, _ = O.write_vector(lamf, betaf, 128)
+    assert rel_l2(qn[:, :, :T], ref_q) < BF16_TOL
+    assert rel_l2(kn[:, :, :T], ref_k) < BF16_TOL
+    assert rel_l2(w[:, :, :T], ref_w) < BF16_TOL
+    assert torch.all(qn[:, :, T:] == 0) and torch.all(w[:, :, T:] == 0)
+    # backward parity
+    dqn = torch.randn(B, H, TP, K, generator=gen)
+    dkn = torch.randn(B, H, TP, K, generator=gen)
+    dw = torch.randn(B, H, TP, 128, generator=gen)
+    (ref_q * dqn[:, :, :T]).sum().backward()
+    (ref_k * dkn[:, :, :T]).sum().backward()
+    (ref_w * dw[:, :, :T].double()).sum().backward()
+    nblk = (B * H * TP + 7) // 8
+    dq = torch.empty(B, T, H, K, device="cuda", dtype=torch.bfloat16)
+    dk = torch.empty_like(dq)
+    dqw = torch.empty(nblk, K, device="cuda")
+    dkw = torch.empty_like(dqw)
+    dlam = torch.empty(B, H, TP, device="cuda")
+    dbeta = torch.empty_like(dlam)
+    L.call("cyfa_token_bwd", *[L.ptr(x) for x in (dev(q), dev(k), dev(qw), dev(kw), qrs, krs,
+                                                   dev(dqn), dev(dkn), dev(lam), dev(beta),
+                                                   dev(dw), dq, dk, dqw, dkw, dlam, dbeta)],
+           B, T, H, K, L.stream())
+    torch.cuda.synchronize()
+    assert rel_l2(dq, qf.grad) < BF16_TOL
+    assert rel_l2(dk, kf.grad) < BF16_TOL
+    assert rel_l2(dqw.sum(0), qwf.grad) < 1e-3
+    assert rel_l2(dkw.sum(0), kwf.grad) < 1e-3
+    assert rel_l2(dlam[..., :T], lamf.grad) < 1e-3
+    assert rel_l2(dbeta[..., :T], betaf.grad) < 1e-3
+
+
+@pytest.mark.parametrize("T", [5, 128, 333])
+def test_gates_bwd(L, T):
+    B, H = 2, 2
+    TP = (T + 127) // 128 * 128
+    gen = seeded(T + 1)
+    dG = torch.randn(B, H, TP, generator=gen)
+    dlam = torch.randn(B, H, TP, generator=gen)
+    dbeta = torch.randn(B, H, TP, generator=gen)
+    dclock = torch.randn(B, H, generator=gen)
+    outs = [torch.empty(B, T, H, device="cuda") for _ in range(3)] + [torch.empty(B, H, device="cuda")]
+    L.call("cyfa_gates_bwd", *[L.ptr(x) for x in (dG.cuda(), dlam.cuda(), dbeta.cuda(),
+                                                   dclock.cuda(), *outs)], B, T, H, L.stream())
+    torch.cuda.synchronize()
+    # autograd through the forward definitions
+    g = torch.zeros(B, T, H, dtype=torch.float64, requires_grad=True)
+    d = torch.zeros(B, T, H, dtype=torch.float64, requires_grad=True)
+    c0 = torch.zeros(B, H, dtype=torch.float64, requires_grad=True)
+    gp = torch.nn.functional.pad(g.permute(0, 2, 1), (0, TP - T))
+    G = gp.reshape(B, H, TP // 128, 128).cumsum(-1).reshape(B, H, TP) / math.log(2)
+    dp = torch.nn.functional.pad(d.permute(0, 2, 1), (0, TP - T))
+    lam = dp.cumsum(-1) + c0.unsqueeze(-1)
+    clock = dp.sum(-1) + c0
+    ((G * dG).sum() + (lam * dlam).sum() + (clock * dclock).sum()).backward()
+    assert rel_l2(outs[0], g.grad) < 1e-5
+    assert rel_l2(outs[1], d.grad) < 1e-5
+    assert torch.equal(outs[2].cpu(), dbeta[..., :T].permute(0, 2, 1))
+    assert rel_l2(outs[3], c0.grad) < 1e-5
