@@ -5,4 +5,6 @@
 #include "selftest.cu"
 #include "decode.cu"
 #include "prep.cu"
+#include "gla_fwd.cu"
 #include "capi.cu"
+#include "chunk_api.cu"

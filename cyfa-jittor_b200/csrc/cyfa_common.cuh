@@ -100,6 +100,14 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const void* tmap, uint64_
       "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_t* bar, int x,
+                                            int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
@@ -221,6 +229,36 @@ __device__ __forceinline__ void store_row32_bf16(uint32_t block, uint32_t row, i
     st_shared_v4(block + sw128(row, c0 + c), pack_bf16(v[8 * c + 0], v[8 * c + 1]),
                  pack_bf16(v[8 * c + 2], v[8 * c + 3]), pack_bf16(v[8 * c + 4], v[8 * c + 5]),
                  pack_bf16(v[8 * c + 6], v[8 * c + 7]));
+  }
+}
+
+// Operand descriptors of a tile stored as 64-column blocks of [R x 64]
+// (one 128-byte swizzled row per tile row), for MMA k-step ks (16 elements).
+// K-major operand: R rows of the M (or N) dimension, K along the columns.
+__device__ __forceinline__ uint64_t kmaj_desc(uint32_t base, int R, int ks) {
+  return make_sdesc(base + (ks >> 2) * R * 128 + (ks & 3) * 32, 16, 1024);
+}
+// MN-major operand: R rows of the K dimension, M (or N) along the columns.
+__device__ __forceinline__ uint64_t mnmaj_desc(uint32_t base, int R, int ks) {
+  return make_sdesc(base + ks * 2048, R * 128, 1024);
+}
+
+// Loads 16 bytes (8 bf16) of row `row`, chunk c of a swizzled block.
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ void unpack_bf16x8(const uint4& u, float* f) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 x = __bfloat1622float2(h[i]);
+    f[2 * i] = x.x;
+    f[2 * i + 1] = x.y;
   }
 }
 

@@ -1,0 +1,517 @@
+// Chunked scalar-gated linear attention (ScalarGatedLA) forward on tcgen05.
+//
+// One pass computes, per (batch, head) and 128-token tile j (two of the
+// reference's 64-token chunks; the result does not depend on the tile size),
+//   S_{j+1} = 2^{G_L} S_j + K_j^T (V_j o 2^{G_L - G_t})                  (state scan)
+//   o_t     = scale [2^{G_t} q_t S_j + sum_{s<=t} 2^{G_t - G_s} (q_t.k_s) v_s]  (tile output)
+// with G the log2 in-tile cumsum of the gate.  This replaces the reference's
+// state_forward (cyclic_flow_attention/ops/chunk_h.py:10-343) and output_forward /
+// first_readout (ops/chunk_o.py:10-613, ops/chunk_readout.py:792-991).
+//
+// state_scan_kernel: one CTA per (bh, 128-row K slice, 64-column V slice).
+//   Tiles stream through a 3-stage TMA ring; the V tile is rescaled in place by
+//   the 128 threads (one token row each); one thread issues the 128x64x128 UMMA
+//   into a double-buffered TMEM accumulator; each thread keeps its state row
+//   (64 fp32) in registers, stores it as bf16 history S_j and adds the update.
+//   REVERSE runs the same recurrence backwards for the state adjoint
+//   H_j = 2^{G_L} H_{j+1} + Q_j^T (dO_j o scale 2^{G_t}) and also emits the
+//   per-tile gate boundary term <S_{j+1}, H_{j+1}>.
+// tile_fwd_kernel: one CTA per (bh, tile, 128-column V slice); all GEMMs of the
+//   tile on tcgen05 (Q K^T, Q S_j, P V), accumulators in TMEM, operands staged by
+//   TMA.  With READOUT (pass 1) the epilogue applies the softmax slot readout
+//   (ops/chunk.py:320-331): z = U(lam) raw, logits = z Table^T, p = softmax over
+//   the 127 active slots, coeff = p Table, weights = U(-lam) coeff, with both
+//   table products on tcgen05 and the rotations in registers.
+#include "cyfa_common.cuh"
+#include "phase.cuh"
+
+namespace cyfa {
+
+enum RowMode : int { kRows2D = 0, kPublic4D = 1 };
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Loads `cols` columns (from c0) of the 128-token tile j of head-row bh as
+// cols/64 swizzled blocks of [128 x 64] (16 KiB apart).  2-D maps index rows
+// bh*TP + t; public 4-D maps are {D, H, T, B} (rows past T read as zeros).
+__device__ __forceinline__ void load_token_tile(uint8_t* dst, const CUtensorMap* map, int mode,
+                                                int bh, int H, int TP, int j, int c0, int cols,
+                                                uint64_t* bar) {
+  for (int cb = 0; cb < cols / 64; ++cb) {
+    if (mode == kRows2D)
+      tma_load_2d(dst + cb * 16384, map, bar, c0 + 64 * cb, bh * TP + j * 128);
+    else
+      tma_load_4d(dst + cb * 16384, map, bar, c0 + 64 * cb, bh % H, j * 128, bh / H);
+  }
+}
+
+// Loads `cols` columns (from c0) of R history rows starting at row0 as cols/64
+// blocks of [R x 64] (R*128 bytes apart).
+__device__ __forceinline__ void load_hist_tile(uint8_t* dst, const CUtensorMap* map, int row0,
+                                               int c0, int cols, int R, uint64_t* bar) {
+  for (int cb = 0; cb < cols / 64; ++cb)
+    tma_load_2d(dst + cb * R * 128, map, bar, c0 + 64 * cb, row0);
+}
+
+__device__ __forceinline__ void store_bf16x32_global(__nv_bfloat16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    d[c] = make_uint4(pack_bf16(v[8 * c], v[8 * c + 1]), pack_bf16(v[8 * c + 2], v[8 * c + 3]),
+                      pack_bf16(v[8 * c + 4], v[8 * c + 5]), pack_bf16(v[8 * c + 6], v[8 * c + 7]));
+}
+
+// ============================================================ state scan
+struct ScanParams {
+  int BH, H, TP, NT;
+  int DK, DV;
+  int k_mode, v_mode;
+  const float* G;           // [BH, TP] log2 in-tile gate cumsum
+  const float* init;        // [BH, DK, DV] fp32 or null
+  __nv_bfloat16* hist;      // [BH, NT, DK, DV]: state entering each tile
+  float* last;              // [BH, DK, DV]: final state (forward) / initial-state adjoint
+  float scale;              // reverse: scale of dO
+  const __nv_bfloat16* fwd_hist;  // reverse: forward history of the same pass
+  const float* fwd_final;         // reverse: forward final state
+  float* bpart;                   // reverse: [BH, NT, nsub] partial boundary terms
+};
+
+constexpr int kScanStages = 3;
+constexpr int kScanStageBytes = 48 * 1024;  // K tile 32 KiB + V tile 16 KiB
+constexpr int kScanSmem = kScanStages * kScanStageBytes + 1024;
+
+template <bool REVERSE>
+__global__ void __launch_bounds__(128, 1)
+    state_scan_kernel(const __grid_constant__ CUtensorMap map_k,
+                      const __grid_constant__ CUtensorMap map_v, ScanParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  __shared__ __align__(8) uint64_t full[kScanStages];
+  __shared__ __align__(8) uint64_t mma_done[2];
+  __shared__ uint32_t tmem_base;
+  __shared__ float red[4];
+  const int tid = threadIdx.x;
+  const int bh = blockIdx.x, dk0 = blockIdx.y * 128, dv0 = blockIdx.z * 64;
+  const int NT = p.NT;
+
+  if (tid == 0) {
+    for (int s = 0; s < kScanStages; ++s) mbar_init(&full[s], 1);
+    mbar_init(&mma_done[0], 1);
+    mbar_init(&mma_done[1], 1);
+    mbar_fence_init();
+    prefetch_tmap(&map_k);
+    prefetch_tmap(&map_v);
+  }
+  if (tid < 32) tmem_alloc(&tmem_base, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_tmem = tmem_lane_base(tmem);
+
+  auto tile_of = [&](int idx) { return REVERSE ? NT - 1 - idx : idx; };
+  int issued = 0;
+  auto issue = [&](int idx) {
+    const int s = idx % kScanStages, j = tile_of(idx);
+    uint8_t* st = smem + s * kScanStageBytes;
+    mbar_expect_tx(&full[s], kScanStageBytes);
+    load_token_tile(st, &map_k, p.k_mode, bh, p.H, p.TP, j, dk0, 128, &full[s]);
+    load_token_tile(st + 32768, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 64, &full[s]);
+  };
+  if (tid == 0) {
+    for (; issued < kScanStages && issued < NT; ++issued) issue(issued);
+  }
+
+  float S[64];
+  const size_t row_off = (size_t(bh) * p.DK + dk0 + tid) * p.DV + dv0;
+  if (p.init) {
+    const float4* src = reinterpret_cast<const float4*>(p.init + row_off);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 x = src[i];
+      S[4 * i] = x.x;
+      S[4 * i + 1] = x.y;
+      S[4 * i + 2] = x.z;
+      S[4 * i + 3] = x.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) S[i] = 0.f;
+  }
+  const uint32_t idesc = make_idesc(128, 64, 1, 1);
+  const int nsub = gridDim.y * gridDim.z, sub = blockIdx.y * gridDim.z + blockIdx.z;
+  bool ok = true;
+  int consumed = 0, committed = 0, retired = 0;
+
+  for (int idx = 0; idx < NT; ++idx) {
+    const int s = idx % kScanStages, j = tile_of(idx);
+    uint8_t* st = smem + s * kScanStageBytes;
+    const float* Gt = p.G + size_t(bh) * p.TP + size_t(j) * 128;
+    const float gl = Gt[127], gt = Gt[tid];
+    const float f = REVERSE ? p.scale * exp2f(gt) : exp2f(gl - gt);
+    if (!mbar_wait(&full[s], (idx / kScanStages) & 1)) ok = false;
+    if (ok) {
+      const uint32_t vb = smem_u32(st + 32768);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t a = vb + sw128(tid, c);
+        float x[8];
+        unpack_bf16x8(ld_shared_v4(a), x);
+        st_shared_v4(a, pack_bf16(x[0] * f, x[1] * f), pack_bf16(x[2] * f, x[3] * f),
+                     pack_bf16(x[4] * f, x[5] * f), pack_bf16(x[6] * f, x[7] * f));
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    if (!__syncthreads_and(ok)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    consumed = idx + 1;
+    if (tid == 0) {
+      const uint32_t kb = smem_u32(st), vb = smem_u32(st + 32768);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem + (idx & 1) * 64, mnmaj_desc(kb, 128, ks), mnmaj_desc(vb, 128, ks), idesc,
+                  ks > 0);
+      umma_commit(&mma_done[idx & 1]);
+    }
+    committed = idx + 1;
+    // state entering tile j (forward) / adjoint leaving tile j (reverse)
+    {
+      uint4* dst = reinterpret_cast<uint4*>(p.hist + ((size_t(bh) * NT + j) * p.DK + dk0 + tid) *
+                                                         p.DV + dv0);
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        dst[c] = make_uint4(pack_bf16(S[8 * c], S[8 * c + 1]), pack_bf16(S[8 * c + 2], S[8 * c + 3]),
+                            pack_bf16(S[8 * c + 4], S[8 * c + 5]),
+                            pack_bf16(S[8 * c + 6], S[8 * c + 7]));
+    }
+    if constexpr (REVERSE) {
+      // <S_{j+1}, H_{j+1}> over this CTA's slice (S_{j+1} from the forward pass)
+      float dot = 0.f;
+      if (j + 1 < NT) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            p.fwd_hist + ((size_t(bh) * NT + j + 1) * p.DK + dk0 + tid) * p.DV + dv0);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float x[8];
+          unpack_bf16x8(src[c], x);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dot += x[e] * S[8 * c + e];
+        }
+      } else {
+        const float4* src = reinterpret_cast<const float4*>(p.fwd_final + row_off);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 x = src[i];
+          dot += x.x * S[4 * i] + x.y * S[4 * i + 1] + x.z * S[4 * i + 2] + x.w * S[4 * i + 3];
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      if ((tid & 31) == 0) red[tid >> 5] = dot;
+      __syncthreads();
+      if (tid == 0)
+        p.bpart[(size_t(bh) * NT + j) * nsub + sub] = (red[0] + red[1]) + (red[2] + red[3]);
+      __syncthreads();
+    }
+    if (!mbar_wait(&mma_done[idx & 1], (idx >> 1) & 1)) ok = false;
+    tc_fence_after();
+    if (ok) {
+      retired = idx + 1;
+      const float gamma = exp2f(gl);
+      float U[32];
+      tmem_ld32(lane_tmem + (idx & 1) * 64, U);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) S[i] = S[i] * gamma + U[i];
+      tmem_ld32(lane_tmem + (idx & 1) * 64 + 32, U);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) S[32 + i] = S[32 + i] * gamma + U[i];
+    }
+    tc_fence_before();
+    if (tid == 0 && ok && issued < NT) {
+      issue(issued);
+      ++issued;
+    }
+  }
+
+  if (ok) {
+    float4* dst = reinterpret_cast<float4*>(p.last + row_off);
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      dst[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
+  } else if (tid == 0) {
+    // unwind: let in-flight copies and MMAs land before TMEM and smem go away
+    for (int idx = consumed; idx < issued; ++idx)
+      mbar_wait(&full[idx % kScanStages], (idx / kScanStages) & 1);
+    for (int idx = retired; idx < committed; ++idx) mbar_wait(&mma_done[idx & 1], (idx >> 1) & 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (tid < 32) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
+  }
+}
+
+
+// ============================================================ tile output
+struct TileFwdParams {
+  int BH, H, TP, NT, T;
+  int DV;          // full value width (public output stride)
+  int v_mode;      // token-row mode of V
+  int o_mode;      // 0: raw [BH, TP, 128] bf16 (pass 1); 1: public o [B, T, H, DV] bf16
+  const float* G;  // [BH, TP]
+  const float* lam;  // [BH, TP] clock (READOUT)
+  float scale;
+  __nv_bfloat16* out;
+  __nv_bfloat16* weights;  // READOUT: [BH, TP, 128]
+};
+
+template <int DK>
+constexpr int tile_fwd_smem() {
+  return 3 * DK * 256 + 32768 + 1024;
+}
+
+template <int DK, bool READOUT>
+__global__ void __launch_bounds__(128, 1)
+    tile_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
+                    const __grid_constant__ CUtensorMap map_k,
+                    const __grid_constant__ CUtensorMap map_v,
+                    const __grid_constant__ CUtensorMap map_s,
+                    const __grid_constant__ CUtensorMap map_tab, TileFwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  constexpr int kQ = 0, kK = DK * 256, kS = 2 * DK * 256, kV = 3 * DK * 256;
+  __shared__ __align__(8) uint64_t bar_in, bar_v, bar_tab, bar_m[5];
+  __shared__ uint32_t tmem_base;
+  __shared__ float Gs[128];
+  const int tid = threadIdx.x;
+  const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT, dv0 = blockIdx.y * 128;
+  const int t = j * 128 + tid;
+
+  if (tid == 0) {
+    mbar_init(&bar_in, 1);
+    mbar_init(&bar_v, 1);
+    mbar_init(&bar_tab, 1);
+    for (int i = 0; i < 5; ++i) mbar_init(&bar_m[i], 1);
+    mbar_fence_init();
+  }
+  if (tid < 32) tmem_alloc(&tmem_base, 512);
+  Gs[tid] = p.G[size_t(bh) * p.TP + t];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_tmem = tmem_lane_base(tmem);
+  const uint32_t sQ = smem_u32(smem + kQ), sK = smem_u32(smem + kK), sS = smem_u32(smem + kS),
+                 sV = smem_u32(smem + kV);
+  bool ok = true;
+
+  if (tid == 0) {
+    mbar_expect_tx(&bar_in, 3 * DK * 256);
+    load_token_tile(smem + kQ, &map_q, kRows2D, bh, p.H, p.TP, j, 0, DK, &bar_in);
+    load_token_tile(smem + kK, &map_k, kRows2D, bh, p.H, p.TP, j, 0, DK, &bar_in);
+    load_hist_tile(smem + kS, &map_s, (bh * p.NT + j) * DK, dv0, 128, DK, &bar_in);
+    mbar_expect_tx(&bar_v, 32768);
+    load_token_tile(smem + kV, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 128, &bar_v);
+    ok = mbar_wait(&bar_in, 0);
+    tc_fence_after();
+    if (ok) {
+      // S_qk = Q K^T -> TMEM[0,128); O_inter = Q S_j -> TMEM[128,256)
+#pragma unroll 4
+      for (int ks = 0; ks < DK / 16; ++ks)
+        umma_bf16(tmem, kmaj_desc(sQ, 128, ks), kmaj_desc(sK, 128, ks), make_idesc(128, 128, 0, 0),
+                  ks > 0);
+      umma_commit(&bar_m[0]);
+#pragma unroll 4
+      for (int ks = 0; ks < DK / 16; ++ks)
+        umma_bf16(tmem + 128, kmaj_desc(sQ, 128, ks), mnmaj_desc(sS, DK, ks),
+                  make_idesc(128, 128, 0, 1), ks > 0);
+      umma_commit(&bar_m[1]);
+    } else {
+      mbar_arrive(&bar_m[0]);
+      mbar_arrive(&bar_m[1]);
+    }
+  }
+  __syncwarp();
+  // ---- P = mask(S_qk o 2^{G_t - G_s}) -> bf16, K-major A operand in the K region
+  if (!mbar_wait(&bar_m[0], 0)) ok = false;
+  tc_fence_after();
+  const float gt = Gs[tid];
+  if (ok) {
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float v[32];
+      tmem_ld32(lane_tmem + 32 * c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int s = 32 * c + i;
+        v[i] = s <= tid ? v[i] * exp2f(gt - Gs[s]) : 0.f;
+      }
+      store_row32_bf16(sK + (c >> 1) * 16384, tid, (c & 1) * 4, v);
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  tc_fence_after();
+  if (tid == 0) {
+    bool vok = ok && mbar_wait(&bar_v, 0);
+    tc_fence_after();
+    if (vok) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem + 256, kmaj_desc(sK, 128, ks), mnmaj_desc(sV, 128, ks),
+                  make_idesc(128, 128, 0, 1), ks > 0);
+      umma_commit(&bar_m[2]);
+    } else {
+      mbar_arrive(&bar_m[2]);
+    }
+    if (READOUT) {
+      // table rows of head h -> Q region once Q is no longer read
+      if (ok && mbar_wait(&bar_m[1], 0)) {
+        mbar_expect_tx(&bar_tab, 32768);
+        load_hist_tile(smem + kQ, &map_tab, (bh % p.H) * 128, 0, 128, 128, &bar_tab);
+      } else {
+        mbar_arrive(&bar_tab);
+      }
+    }
+  }
+  __syncwarp();
+  // ---- o = scale (2^{G_t} O_inter + O_intra)
+  if (!mbar_wait(&bar_m[2], 0)) ok = false;
+  tc_fence_after();
+  const float eg = exp2f(gt);
+  float lam = 0.f;
+  if (READOUT) lam = p.lam[size_t(bh) * p.TP + t];
+  if (ok) {
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float a[32], b[32];
+      tmem_ld32(lane_tmem + 128 + 32 * c, a);
+      tmem_ld32(lane_tmem + 256 + 32 * c, b);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) a[i] = p.scale * (eg * a[i] + b[i]);
+      if (p.o_mode == 1) {
+        if (t < p.T) {
+          const int b_ = bh / p.H, h = bh % p.H;
+          store_bf16x32_global(p.out + ((size_t(b_) * p.T + t) * p.H + h) * p.DV + dv0 + 32 * c, a);
+        }
+      } else {
+        store_bf16x32_global(p.out + (size_t(bh) * p.TP + t) * 128 + 32 * c, a);
+      }
+      if (READOUT) {
+        // z = U(lam) raw, from the bf16-rounded raw that is saved for the backward pass
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float e = bf16_round(a[i]), o = bf16_round(a[i + 1]);
+          float sn, cs;
+          __sincosf(clock_phase(lam, 16 * c + i / 2), &sn, &cs);
+          a[i] = cs * e - sn * o;
+          a[i + 1] = sn * e + cs * o;
+        }
+        store_row32_bf16(sK + 32768 + (c >> 1) * 16384, tid, (c & 1) * 4, a);
+      }
+    }
+  }
+  if (READOUT) {
+    const uint32_t sZ = sK + 32768, sTab = sQ, sP = sV;
+    fence_async_smem();
+    tc_fence_before();
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    if (tid == 0) {
+      if (ok && mbar_wait(&bar_tab, 0)) {
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_bf16(tmem, kmaj_desc(sZ, 128, ks), kmaj_desc(sTab, 128, ks),
+                    make_idesc(128, 128, 0, 0), ks > 0);
+        umma_commit(&bar_m[3]);
+      } else {
+        mbar_arrive(&bar_m[3]);
+      }
+    }
+    __syncwarp();
+    if (!mbar_wait(&bar_m[3], 0)) ok = false;
+    tc_fence_after();
+    if (ok) {
+      // softmax over the 127 active slots, one token row per thread
+      float mx = -1e30f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(lane_tmem + 32 * c, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (32 * c + i < 127) mx = fmaxf(mx, v[i]);
+      }
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(lane_tmem + 32 * c, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (32 * c + i < 127) sum += __expf(v[i] - mx);
+      }
+      const float inv = 1.f / sum;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(lane_tmem + 32 * c, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = (32 * c + i < 127) ? __expf(v[i] - mx) * inv : 0.f;
+        store_row32_bf16(sP + (c >> 1) * 16384, tid, (c & 1) * 4, v);
+      }
+    }
+    fence_async_smem();
+    tc_fence_before();
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    if (tid == 0) {
+      if (ok) {
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_bf16(tmem + 128, kmaj_desc(sP, 128, ks), mnmaj_desc(sTab, 128, ks),
+                    make_idesc(128, 128, 0, 1), ks > 0);
+        umma_commit(&bar_m[4]);
+      } else {
+        mbar_arrive(&bar_m[4]);
+      }
+    }
+    __syncwarp();
+    if (!mbar_wait(&bar_m[4], 0)) ok = false;
+    tc_fence_after();
+    if (ok) {
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(lane_tmem + 128 + 32 * c, v);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float sn, cs;
+          __sincosf(clock_phase(lam, 16 * c + i / 2), &sn, &cs);
+          const float e = v[i], o = v[i + 1];
+          v[i] = cs * e + sn * o;
+          v[i + 1] = -sn * e + cs * o;
+        }
+        store_bf16x32_global(p.weights + (size_t(bh) * p.TP + t) * 128 + 32 * c, v);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (tid < 32) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+
+}  // namespace cyfa

@@ -27,6 +27,14 @@ _SIGNATURES = {
     "cyfa_token_fwd": [_vp] * 11 + [_i] * 4 + [_f] * 2 + [_vp],
     "cyfa_token_bwd": [_vp] * 17 + [_i] * 4 + [_vp],
     "cyfa_gates_bwd": [_vp] * 8 + [_i] * 3 + [_vp],
+    "cyfa_chunk_fwd": [_vp, _vp, ctypes.c_size_t, _vp],
+    "cyfa_chunk_bwd": [_vp, _vp, ctypes.c_size_t, _vp, ctypes.c_size_t, _vp],
+}
+
+# size queries (restype size_t)
+_SIZE_QUERIES = {
+    "cyfa_chunk_saved_bytes": [_i] * 5,
+    "cyfa_chunk_work_bytes": [_i] * 5,
 }
 
 
@@ -48,9 +56,17 @@ def lib():
             )
         handle = ctypes.CDLL(LIB_PATH)
         for name, args in _SIGNATURES.items():
-            fn = getattr(handle, name)
+            fn = getattr(handle, name, None)
+            if fn is None:
+                continue
             fn.argtypes = args
             fn.restype = ctypes.c_int
+        for name, args in _SIZE_QUERIES.items():
+            fn = getattr(handle, name, None)
+            if fn is None:
+                continue
+            fn.argtypes = args
+            fn.restype = ctypes.c_size_t
         handle.cyfa_strerror.argtypes = [ctypes.c_int]
         handle.cyfa_strerror.restype = ctypes.c_char_p
         _lib = handle

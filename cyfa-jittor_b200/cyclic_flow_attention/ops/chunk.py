@@ -1,0 +1,207 @@
+"""Chunkwise Cyclic Flow Attention on B200 (sm_100a).
+
+Drop-in for the reference's ``chunk_cyfa`` (cyclic_flow_attention/ops/chunk.py:164-353):
+same signature, layouts, defaults and errors.  The whole op (gates, clock,
+q/k RMSNorm, write vector, both ScalarGatedLA passes and the softmax slot
+readout, forward and backward) runs in libcyfa.so; torch only allocates
+buffers, builds the readout table R.Phi and differentiates through it.
+"""
+
+import ctypes
+import math
+
+import torch
+
+from .. import _lib
+
+_c = ctypes
+
+
+class _FwdArgs(_c.Structure):
+    _fields_ = [(n, _c.c_int) for n in ("B", "T", "H", "K", "V")] + \
+        [(n, _c.c_float) for n in ("q_eps", "k_eps", "scale")] + \
+        [(n, _c.c_void_p) for n in ("q", "k", "v", "g", "delta", "beta", "q_norm_weight",
+                                     "k_norm_weight", "table_bf", "hk0", "hv0", "clock0",
+                                     "o", "hk", "hv", "clock")]
+
+
+class _BwdArgs(_c.Structure):
+    _fields_ = [("fwd", _FwdArgs)] + \
+        [(n, _c.c_void_p) for n in ("do", "dhk", "dhv", "dclock", "dq", "dk", "dv", "dg",
+                                     "ddelta", "dbeta", "dtable", "dq_norm_weight",
+                                     "dk_norm_weight", "dhk0", "dhv0", "dclock0")]
+
+
+_BASIS = {}
+
+
+def basis(M, device):
+    """Real Fourier basis Phi [M-1, M] (reference ops/chunk.py:82-103), built once
+    per device in fp64 and kept in fp32."""
+    key = (M, str(device))
+    if key not in _BASIS:
+        period = M - 1
+        row = torch.arange(period, dtype=torch.float64, device=device).unsqueeze(1)
+        col = torch.arange(M, device=device)
+        pair = (col // 2).to(torch.float64)
+        phase = row * (pair * (2 * math.pi / period)).unsqueeze(0)
+        z = torch.where((col % 2 == 1).unsqueeze(0), torch.sin(phase), torch.cos(phase))
+        scale = torch.full((M,), (2.0 / period) ** 0.5, dtype=torch.float64, device=device)
+        scale[:2] = period ** -0.5
+        out = z * scale
+        out[:, 1] = 0.0
+        _BASIS[key] = out.float()
+    return _BASIS[key]
+
+
+def readout_table(readout):
+    """Table_h = R_h . Phi in fp32, [H, M-1, M] (reference ops/chunk.py:281)."""
+    M = readout.shape[-1] + 1
+    return readout.float() @ basis(M, readout.device)
+
+
+def _table_bf(table):
+    H, R, M = table.shape
+    out = torch.zeros(H, M, M, device=table.device, dtype=torch.bfloat16)
+    out[:, :R] = table.detach().to(torch.bfloat16)
+    return out
+
+
+def _contig(x, dtype):
+    return x.to(dtype).contiguous()
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+class ChunkCyfaFunction(torch.autograd.Function):
+    """Autograd wrapper over cyfa_chunk_fwd / cyfa_chunk_bwd."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, delta, beta, table, qw, kw, hk0, hv0, clock0,
+                q_eps, k_eps, scale):
+        B, T, H, K = q.shape
+        V = v.shape[-1]
+        dev = q.device
+        tb = _table_bf(table)
+        o = torch.empty(B, T, H, V, device=dev, dtype=torch.bfloat16)
+        hk = torch.empty(B, H, K, 128, device=dev, dtype=torch.float32)
+        hv = torch.empty(B, H, 128, V, device=dev, dtype=torch.float32)
+        clock = torch.empty(B, H, device=dev, dtype=torch.float32)
+        nbytes = _lib.lib().cyfa_chunk_saved_bytes(B, T, H, K, V)
+        if nbytes == 0:
+            raise ValueError(f"unsupported chunk_cyfa shape B={B} T={T} H={H} K={K} V={V}")
+        saved = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+        args = _FwdArgs(B, T, H, K, V, q_eps, k_eps, scale,
+                        _p(q), _p(k), _p(v), _p(g), _p(delta), _p(beta), _p(qw), _p(kw),
+                        _p(tb), _p(hk0), _p(hv0), _p(clock0), _p(o), _p(hk), _p(hv), _p(clock))
+        _lib.call("cyfa_chunk_fwd", _c.byref(args), _lib.ptr(saved), _c.c_size_t(nbytes),
+                  _lib.stream())
+        ctx.save_for_backward(q, k, v, g, delta, beta, qw, kw, tb, hk0, hv0, clock0,
+                              hk, hv, clock, saved)
+        ctx.eps = (q_eps, k_eps, scale)
+        ctx.has_init = (hk0 is not None, hv0 is not None, clock0 is not None)
+        return o, hk, hv, clock
+
+    @staticmethod
+    def backward(ctx, do, dhk, dhv, dclock):
+        (q, k, v, g, delta, beta, qw, kw, tb, hk0, hv0, clock0, hk, hv, clock,
+         saved) = ctx.saved_tensors
+        B, T, H, K = q.shape
+        V = v.shape[-1]
+        dev = q.device
+        q_eps, k_eps, scale = ctx.eps
+        fwd = _FwdArgs(B, T, H, K, V, q_eps, k_eps, scale,
+                       _p(q), _p(k), _p(v), _p(g), _p(delta), _p(beta), _p(qw), _p(kw),
+                       _p(tb), _p(hk0), _p(hv0), _p(clock0), None, _p(hk), _p(hv), _p(clock))
+        do = torch.zeros(B, T, H, V, device=dev, dtype=torch.bfloat16) if do is None \
+            else _contig(do, torch.bfloat16)
+        dhk = None if dhk is None else _contig(dhk, torch.float32)
+        dhv = None if dhv is None else _contig(dhv, torch.float32)
+        dclock = None if dclock is None else _contig(dclock, torch.float32)
+        dq = torch.empty_like(q)
+        dk = torch.empty_like(k)
+        dv = torch.empty_like(v)
+        dg = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+        ddelta = torch.empty_like(dg)
+        dbeta = torch.empty_like(dg)
+        dtable = torch.empty(H, 128, 128, device=dev, dtype=torch.float32)
+        dqw = torch.empty(K, device=dev, dtype=torch.float32)
+        dkw = torch.empty(K, device=dev, dtype=torch.float32)
+        dhk0 = torch.empty(B, H, K, 128, device=dev, dtype=torch.float32)
+        dhv0 = torch.empty(B, H, 128, V, device=dev, dtype=torch.float32)
+        dclock0 = torch.empty(B, H, device=dev, dtype=torch.float32)
+        nwork = _lib.lib().cyfa_chunk_work_bytes(B, T, H, K, V)
+        work = torch.empty(nwork, device=dev, dtype=torch.uint8)
+        args = _BwdArgs(fwd, _p(do), _p(dhk), _p(dhv), _p(dclock), _p(dq), _p(dk), _p(dv),
+                        _p(dg), _p(ddelta), _p(dbeta), _p(dtable), _p(dqw), _p(dkw),
+                        _p(dhk0), _p(dhv0), _p(dclock0))
+        _lib.call("cyfa_chunk_bwd", _c.byref(args), _lib.ptr(saved),
+                  _c.c_size_t(saved.numel()), _lib.ptr(work), _c.c_size_t(nwork),
+                  _lib.stream())
+        has_hk0, has_hv0, has_c0 = ctx.has_init
+        return (dq, dk, dv, dg, ddelta, dbeta, dtable[:, :127], dqw, dkw,
+                dhk0 if has_hk0 else None, dhv0 if has_hv0 else None,
+                dclock0 if has_c0 else None, None, None, None)
+
+
+def chunk_cyfa(
+    q,
+    k,
+    v,
+    g,
+    delta,
+    beta,
+    readout,
+    q_norm_weight,
+    k_norm_weight,
+    q_norm_eps=1e-6,
+    k_norm_eps=1e-6,
+    scale=None,
+    initial_state=None,
+    output_final_state=False,
+    cu_seqlens=None,
+    checkpoint_level=0,
+    chunk_size=64,
+):
+    """Chunkwise Cyclic Flow Attention.
+
+    Inputs q and k use [batch, time, heads, K], v [batch, time, heads, V]; g,
+    delta and beta use [batch, time, heads]. The readout has [heads, slots-1,
+    slots-1].  Returns the output [batch, time, heads, V] and, when requested,
+    the fp32 state (key_state [B,H,K,slots], value_state [B,H,slots,V],
+    clock [B,H]).  Same contract as the reference (ops/chunk.py:164-189); the
+    tensors must live on a CUDA device.  ``chunk_size`` keeps its meaning for
+    padding semantics; the kernels tile time in blocks of 128 tokens, which
+    gives the same result (the chunk size is a scheduling choice).
+    """
+    if cu_seqlens is not None:
+        raise NotImplementedError("packed layout requires native segment dispatch")
+    if checkpoint_level != 0:
+        raise NotImplementedError("only saved-activation training is implemented")
+    _lib.require_cuda(q, k, v, g, delta, beta, readout, q_norm_weight, k_norm_weight)
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    M = readout.shape[-1] + 1
+    if M != 128:
+        raise ValueError("the B200 kernels need num_slots = 128 (127 active slots)")
+    if K not in (128, 256) or V not in (128, 256):
+        raise ValueError(f"head dims must be 128 or 256, got K={K} V={V}")
+    if chunk_size <= 0:
+        raise ValueError("chunk_size must be positive")
+    out_dtype = q.dtype
+    sc = K ** -0.5 if scale is None else float(scale)
+    table = readout_table(readout)
+    hk0 = hv0 = clock0 = None
+    if initial_state is not None:
+        hk0, hv0, clock0 = (_contig(x, torch.float32) for x in initial_state)
+    o, hk, hv, clock = ChunkCyfaFunction.apply(
+        _contig(q, torch.bfloat16), _contig(k, torch.bfloat16), _contig(v, torch.bfloat16),
+        _contig(g, torch.float32), _contig(delta, torch.float32), _contig(beta, torch.float32),
+        table, _contig(q_norm_weight, torch.float32), _contig(k_norm_weight, torch.float32),
+        hk0, hv0, clock0, float(q_norm_eps), float(k_norm_eps), sc)
+    if out_dtype != torch.bfloat16:
+        o = o.to(out_dtype)
+    state = (hk, hv, clock) if output_final_state else None
+    return o, state

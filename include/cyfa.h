@@ -97,6 +97,41 @@ int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h,
                    const float* dclock, float* dg, float* ddelta, float* dbeta,
                    float* dclock0, int B, int T, int H, void* stream);
 
+/* ---------------------------------------------------------------- chunk op
+ * Chunked CyFA (both ScalarGatedLA passes joined by the softmax slot readout).
+ * Replaces: chunk_cyfa, cyclic_flow_attention/ops/chunk.py:164-353, with its fused
+ * internals first_readout (ops/chunk_readout.py:961-991,1124-1136), scalar_la /
+ * ScalarAttention (ops/chunk.py:30-79), state_forward (ops/chunk_h.py:338) and
+ * output_forward (ops/chunk_o.py:394-613).  K in {128, 256}, V in {128, 256},
+ * 128 slot rows.  The caller owns `saved` (cyfa_chunk_saved_bytes) and keeps it
+ * for cyfa_chunk_bwd; the final state outputs are always written because the
+ * backward pass reads them. */
+typedef struct {
+  int B, T, H, K, V;
+  float q_eps, k_eps, scale;
+  const void* q;                /* [B,T,H,K] bf16 */
+  const void* k;                /* [B,T,H,K] bf16 */
+  const void* v;                /* [B,T,H,V] bf16 */
+  const float* g;               /* [B,T,H] log decay (<= 0) */
+  const float* delta;           /* [B,T,H] clock increment */
+  const float* beta;            /* [B,T,H] write strength */
+  const float* q_norm_weight;   /* [K] */
+  const float* k_norm_weight;   /* [K] */
+  const void* table_bf;         /* [H,128,128] bf16 readout table, row 127 zero */
+  const float* hk0;             /* [B,H,K,128] or NULL */
+  const float* hv0;             /* [B,H,128,V] or NULL */
+  const float* clock0;          /* [B,H] or NULL */
+  void* o;                      /* out [B,T,H,V] bf16 */
+  float* hk;                    /* out [B,H,K,128] final key state */
+  float* hv;                    /* out [B,H,128,V] final value state */
+  float* clock;                 /* out [B,H] final clock */
+} cyfa_chunk_fwd_args;
+
+size_t cyfa_chunk_saved_bytes(int B, int T, int H, int K, int V);
+
+int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* args, void* saved, size_t saved_bytes,
+                   void* stream);
+
 /* ---------------------------------------------------------------- self test
  * C[128,N] = A * B through TMA + tcgen05 (test hook for the UMMA descriptor and
  * swizzle encodings).  A is [128,K] (a_mn = 0) or [K,128] (a_mn = 1); B is [N,K]

@@ -1,0 +1,99 @@
+"""GPU parity of chunk_cyfa (forward and backward) against the CPU oracle.
+
+Tolerances: bf16 outputs and gradients rel-L2 <= 1e-2 of
+the fp32 oracle; the fp32 clock <= 1e-4.  Gate gradients (dg, ddelta, dbeta)
+are reductions over bf16 products and get 2e-2, as in the reference's own
+benchmark gate (benchmarks/core.py:576-580).
+"""
+
+import pytest
+import torch
+
+from gpu_util import rel_l2, seeded
+from oracle import cyfa_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 1e-2
+GATE_TOL = 2e-2
+F32_TOL = 1e-4
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+    from cyclic_flow_attention import ops as _ops
+
+    return _ops
+
+
+def make_inputs(B, T, H, K, V, seed=0, with_state=False, gate_scale=1.0):
+    gen = seeded(seed)
+    q = torch.randn(B, T, H, K, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, T, H, K, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, T, H, V, generator=gen).to(torch.bfloat16)
+    g = torch.log(1 - gate_scale * 0.1 * torch.rand(B, T, H, generator=gen))
+    delta = torch.sigmoid(torch.randn(B, T, H, generator=gen))
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=gen))
+    readout = torch.eye(127).expand(H, -1, -1) + 0.05 * torch.randn(H, 127, 127, generator=gen)
+    qw = 1 + 0.1 * torch.randn(K, generator=gen)
+    kw = 1 + 0.1 * torch.randn(K, generator=gen)
+    state = None
+    if with_state:
+        state = (0.05 * torch.randn(B, H, K, 128, generator=gen),
+                 0.05 * torch.randn(B, H, 128, V, generator=gen),
+                 torch.rand(B, H, generator=gen) * 1000)
+    return [q, k, v, g, delta, beta, readout, qw, kw], state
+
+
+FWD_CASES = [
+    (1, 256, 2, 256, 256, False),
+    (2, 300, 1, 256, 256, True),
+    (1, 200, 2, 128, 128, False),
+    (1, 384, 1, 256, 128, True),
+    (2, 130, 2, 128, 256, False),
+    (1, 1, 1, 256, 256, True),
+]
+
+
+@pytest.mark.parametrize("B,T,H,K,V,with_state", FWD_CASES)
+def test_chunk_forward(ops, B, T, H, K, V, with_state):
+    ins, state = make_inputs(B, T, H, K, V, seed=B * 1000 + T + K + V, with_state=with_state)
+    dev = [x.cuda() for x in ins]
+    st = None if state is None else tuple(x.cuda() for x in state)
+    with torch.no_grad():
+        o, fs = ops.chunk_cyfa(*dev, initial_state=st, output_final_state=True)
+    torch.cuda.synchronize()
+    ref_o, ref_s = O.chunk_cyfa(*[x.float() for x in ins[:6]], *ins[6:], initial_state=state,
+                                output_final_state=True, dtype=torch.float32)
+    assert rel_l2(fs[0], ref_s[0]) < BF16_TOL, "key state"
+    assert rel_l2(fs[1], ref_s[1]) < BF16_TOL, "value state"
+    assert rel_l2(fs[2], ref_s[2]) < F32_TOL, "clock"
+    assert rel_l2(o, ref_o) < BF16_TOL, "output"
+    from cyclic_flow_attention import _lib
+
+    assert _lib.device_error() == 0
+
+
+def test_chunk_forward_deterministic(ops):
+    ins, _ = make_inputs(2, 512, 2, 256, 256, seed=3)
+    dev = [x.cuda() for x in ins]
+    with torch.no_grad():
+        a, sa = ops.chunk_cyfa(*dev, output_final_state=True)
+        b, sb = ops.chunk_cyfa(*dev, output_final_state=True)
+    assert torch.equal(a, b)
+    for x, y in zip(sa, sb):
+        assert torch.equal(x, y)
+
+
+def test_chunk_strong_decay_stays_finite(ops):
+    """Gates near zero (alpha ~ 0) must not overflow the in-tile decay factors."""
+    ins, _ = make_inputs(1, 256, 1, 256, 256, seed=9)
+    ins[3] = torch.full_like(ins[3], -30.0)
+    dev = [x.cuda() for x in ins]
+    with torch.no_grad():
+        o, fs = ops.chunk_cyfa(*dev, output_final_state=True)
+    assert torch.isfinite(o).all() and all(torch.isfinite(x).all() for x in fs)
+    ref_o, _ = O.chunk_cyfa(*[x.float() for x in ins[:6]], *ins[6:], dtype=torch.float32)
+    assert rel_l2(o, ref_o) < BF16_TOL
