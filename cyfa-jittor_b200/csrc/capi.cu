@@ -217,7 +217,7 @@ int cyfa_token_bwd(const void* q, const void* k, const float* q_norm_weight,
                    static_cast<__nv_bfloat16*>(dq), static_cast<__nv_bfloat16*>(dk), dqw_part,
                    dkw_part, dlam, dbeta_h, B, T, H, TP};
   const size_t rows = size_t(B) * H * TP;
-  const dim3 grid(unsigned((rows + 7) / 8));
+  const dim3 grid(unsigned(token_bwd_blocks(rows)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (K == 256) token_bwd_kernel<256><<<grid, 256, 0, s>>>(p);
   else token_bwd_kernel<128><<<grid, 256, 0, s>>>(p);
@@ -230,7 +230,8 @@ int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h, con
   CYFA_REQUIRE(dG && dlam && dbeta_h && dg && ddelta && dbeta, kNullPointer);
   CYFA_REQUIRE(B > 0 && T > 0 && H > 0, kBadShape);
   const int TP = (T + 127) / 128 * 128;
-  GatesBwdParams p{dG, dlam, dbeta_h, dclock, dg, ddelta, dbeta, dclock0, B, T, H, TP};
+  GatesBwdParams p{dG, dlam, nullptr, nullptr, nullptr, 0, 0, dbeta_h, dclock, dg, ddelta,
+                   dbeta, dclock0, B, T, H, TP};
   gates_bwd_kernel<<<B * H, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return launch_status();
 }

@@ -56,6 +56,39 @@ static Saved carve_saved(const Dims& d, void* base, size_t* total) {
   return s;
 }
 
+// Scratch of the backward pass.
+struct Work {
+  __nv_bfloat16 *h1, *h2, *A, *Bp, *draw;
+  float *dweights, *dw, *dq1, *dk1, *dG, *dlam_r, *dlam_w, *dbeta_h, *bpart1, *bpart2, *dtab_part,
+      *dqw_part, *dkw_part;
+};
+
+static Work carve_work(const Dims& d, void* base, size_t* total) {
+  Carver c(base);
+  Work w;
+  const size_t n = size_t(d.BH) * d.TP, tiles = size_t(d.BH) * d.NT;
+  w.h1 = c.take<__nv_bfloat16>(tiles * d.K * 128);
+  w.h2 = c.take<__nv_bfloat16>(tiles * 128 * d.V);
+  w.A = c.take<__nv_bfloat16>(tiles * 128 * 128);
+  w.Bp = c.take<__nv_bfloat16>(tiles * 128 * 128);
+  w.draw = c.take<__nv_bfloat16>(n * 128);
+  w.dweights = c.take<float>(n * 128);
+  w.dw = c.take<float>(n * 128);
+  w.dq1 = c.take<float>(n * d.K);
+  w.dk1 = c.take<float>(n * d.K);
+  w.dG = c.take<float>(n);
+  w.dlam_r = c.take<float>(n);
+  w.dlam_w = c.take<float>(n);
+  w.dbeta_h = c.take<float>(n);
+  w.bpart1 = c.take<float>(tiles * (d.K / 128) * 2);
+  w.bpart2 = c.take<float>(tiles * (d.V / 64));
+  w.dtab_part = c.take<float>(tiles * 128 * 128);
+  w.dqw_part = c.take<float>(size_t(1184) * d.K);
+  w.dkw_part = c.take<float>(size_t(1184) * d.K);
+  if (total) *total = c.off + 256;
+  return w;
+}
+
 // [B,T,H,D] bf16 as the 4-D map {D, H, T, B} with a {64, 1, 128, 1} box.
 static int tmap_public(CUtensorMap* m, const void* base, int B, int T, int H, int D) {
   const uint64_t dims[4] = {uint64_t(D), uint64_t(H), uint64_t(T), uint64_t(B)};
@@ -158,6 +191,148 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
     if ((rc = launch_status())) return rc;
   }
   return kOk;
+}
+
+size_t cyfa_chunk_work_bytes(int B, int T, int H, int K, int V) {
+  if (!shape_ok(B, T, H, K, V)) return 0;
+  size_t total = 0;
+  carve_work(make_dims(B, T, H, K, V), nullptr, &total);
+  return total;
+}
+
+int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved_bytes,
+                   void* work, size_t work_bytes, void* stream) {
+  CYFA_REQUIRE(g && saved && work, kNullPointer);
+  const cyfa_chunk_fwd_args* a = &g->fwd;
+  CYFA_REQUIRE(shape_ok(a->B, a->T, a->H, a->K, a->V), kBadShape);
+  CYFA_REQUIRE(a->q && a->k && a->v && a->q_norm_weight && a->k_norm_weight && a->table_bf &&
+                   a->hk && a->hv && g->d_o && g->dq && g->dk && g->dv && g->dg && g->ddelta &&
+                   g->dbeta && g->dtable && g->dq_norm_weight && g->dk_norm_weight,
+               kNullPointer);
+  const Dims d = make_dims(a->B, a->T, a->H, a->K, a->V);
+  size_t need_s = 0, need_w = 0;
+  carve_saved(d, nullptr, &need_s);
+  carve_work(d, nullptr, &need_w);
+  CYFA_REQUIRE(saved_bytes >= need_s && work_bytes >= need_w, kWorkspace);
+  CYFA_REQUIRE(aligned(saved, 256) && aligned(work, 256), kMisaligned);
+  CYFA_REQUIRE(aligned(g->d_o, 16) && aligned(g->dv, 16) && aligned(a->v, 16) &&
+                   (!g->dhk || aligned(g->dhk, 16)) && (!g->dhv || aligned(g->dhv, 16)) &&
+                   (!g->dhk0 || aligned(g->dhk0, 16)) && (!g->dhv0 || aligned(g->dhv0, 16)),
+               kMisaligned);
+  const Saved s = carve_saved(d, const_cast<void*>(saved), nullptr);
+  const Work w = carve_work(d, work, nullptr);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc;
+  const uint64_t rows = uint64_t(d.BH) * d.TP, trows = uint64_t(d.BH) * d.NT * 128;
+  CUtensorMap m_qn, m_kn, m_w, m_weights, m_v, m_do, m_draw, m_s1, m_s2, m_h1, m_h2, m_A, m_Bp,
+      m_tab;
+  if ((rc = tmap_2d(&m_qn, s.qn, rows, d.K, 128))) return rc;
+  if ((rc = tmap_2d(&m_kn, s.kn, rows, d.K, 128))) return rc;
+  if ((rc = tmap_2d(&m_w, s.w, rows, 128, 128))) return rc;
+  if ((rc = tmap_2d(&m_weights, s.weights, rows, 128, 128))) return rc;
+  if ((rc = tmap_2d(&m_draw, w.draw, rows, 128, 128))) return rc;
+  if ((rc = tmap_public(&m_v, a->v, d.B, d.T, d.H, d.V))) return rc;
+  if ((rc = tmap_public(&m_do, g->d_o, d.B, d.T, d.H, d.V))) return rc;
+  if ((rc = tmap_2d(&m_s1, s.s1, uint64_t(d.BH) * d.NT * d.K, 128, d.K))) return rc;
+  if ((rc = tmap_2d(&m_h1, w.h1, uint64_t(d.BH) * d.NT * d.K, 128, d.K))) return rc;
+  if ((rc = tmap_2d(&m_s2, s.s2, uint64_t(d.BH) * d.NT * 128, d.V, 128))) return rc;
+  if ((rc = tmap_2d(&m_h2, w.h2, uint64_t(d.BH) * d.NT * 128, d.V, 128))) return rc;
+  if ((rc = tmap_2d(&m_A, w.A, trows, 128, 128))) return rc;
+  if ((rc = tmap_2d(&m_Bp, w.Bp, trows, 128, 128))) return rc;
+  if ((rc = tmap_2d(&m_tab, a->table_bf, uint64_t(d.H) * 128, 128, 128))) return rc;
+  const dim3 tiles(d.BH * d.NT);
+  set_smem(state_scan_kernel<true>, kScanSmem);
+  set_smem(dual_gemm_kernel, kDualSmem);
+  auto dual = [&](const CUtensorMap& x1, const CUtensorMap& y1, const CUtensorMap& x2,
+                  const CUtensorMap& y2, DualParams p) {
+    dual_gemm_kernel<<<tiles, 128, kDualSmem, st>>>(x1, y1, x2, y2, p);
+    return launch_status();
+  };
+  const int nsub1 = (d.K / 128) * 2, nsub2 = d.V / 64;
+
+  // ================= pass 2 (queries = weights, keys = w, values = v)
+  {
+    ScanParams p{d.BH, d.H, d.TP, d.NT, 128, d.V, kRows2D, kPublic4D, s.G, g->dhv, w.h2, g->dhv0,
+                 1.f, s.s2, a->hv, w.bpart2};
+    state_scan_kernel<true><<<dim3(d.BH, 1, d.V / 64), 128, kScanSmem, st>>>(m_weights, m_do, p);
+    if ((rc = launch_status())) return rc;
+    ScoresParams sp{d.BH, d.H, d.TP, d.NT, kPublic4D, kPublic4D, s.G, 1.f, w.A, w.Bp};
+    if (d.V == 256) {
+      set_smem(tile_scores_kernel<128, 256>, scores_smem<128, 256>());
+      tile_scores_kernel<128, 256><<<tiles, 128, scores_smem<128, 256>(), st>>>(m_weights, m_w,
+                                                                                 m_do, m_v, sp);
+    } else {
+      set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
+      tile_scores_kernel<128, 128><<<tiles, 128, scores_smem<128, 128>(), st>>>(m_weights, m_w,
+                                                                                 m_do, m_v, sp);
+    }
+    if ((rc = launch_status())) return rc;
+    // dweights = B' w + 2^{G_t} dO S^T ;  dG = weights . dweights
+    DualParams q2{d.BH, d.H, d.TP, d.NT, d.T, 0, kRows2D, kPublic4D, 1, 128, d.V, 128, d.V, s.G,
+                  1.f, 0, 0, w.dweights, s.weights, 1.f, 0, w.dG};
+    if ((rc = dual(m_Bp, m_w, m_do, m_s2, q2))) return rc;
+    // dw = B'^T weights + 2^{G_L-G_s} v H^T ;  dG -= w . dw
+    DualParams k2{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kPublic4D, 1, 128, d.V, 128, d.V, s.G,
+                  1.f, 1, 0, w.dw, s.w, -1.f, 1, w.dG};
+    if ((rc = dual(m_Bp, m_weights, m_v, m_h2, k2))) return rc;
+    // dv = A^T dO + 2^{G_L-G_s} w H  (public layout)
+    DualParams v2{d.BH, d.H, d.TP, d.NT, d.T, 1, kPublic4D, kRows2D, 0, d.V, 128, 128, d.V, s.G,
+                  1.f, 1, 2, g->dv, nullptr, 0.f, 0, nullptr};
+    if ((rc = dual(m_A, m_do, m_w, m_h2, v2))) return rc;
+  }
+  // ================= readout adjoint
+  {
+    ReadoutBwdParams rp{d.BH, d.H, d.TP, d.NT, s.raw, s.weights, w.dweights, s.lam, w.draw,
+                        w.dlam_r, w.dtab_part};
+    set_smem(readout_bwd_kernel, kReadoutBwdSmem);
+    readout_bwd_kernel<<<tiles, 128, kReadoutBwdSmem, st>>>(m_tab, rp);
+    if ((rc = launch_status())) return rc;
+    dtable_reduce_kernel<<<dim3(d.H, 128), 128, 0, st>>>(w.dtab_part, g->dtable, d.B, d.H, d.NT);
+    if ((rc = launch_status())) return rc;
+  }
+  // ================= pass 1 (queries = q^, keys = k^, values = w)
+  {
+    ScanParams p{d.BH, d.H, d.TP, d.NT, d.K, 128, kRows2D, kRows2D, s.G, g->dhk, w.h1, g->dhk0,
+                 a->scale, s.s1, a->hk, w.bpart1};
+    state_scan_kernel<true><<<dim3(d.BH, d.K / 128, 2), 128, kScanSmem, st>>>(m_qn, m_draw, p);
+    if ((rc = launch_status())) return rc;
+    ScoresParams sp{d.BH, d.H, d.TP, d.NT, kRows2D, kRows2D, s.G, a->scale, w.A, w.Bp};
+    if (d.K == 256) {
+      set_smem(tile_scores_kernel<256, 128>, scores_smem<256, 128>());
+      tile_scores_kernel<256, 128><<<tiles, 128, scores_smem<256, 128>(), st>>>(m_qn, m_kn,
+                                                                                 m_draw, m_w, sp);
+    } else {
+      set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
+      tile_scores_kernel<128, 128><<<tiles, 128, scores_smem<128, 128>(), st>>>(m_qn, m_kn,
+                                                                                 m_draw, m_w, sp);
+    }
+    if ((rc = launch_status())) return rc;
+    // dq^ = B' k^ + scale 2^{G_t} draw S^T ;  dG += q^ . dq^
+    DualParams q1{d.BH, d.H, d.TP, d.NT, d.T, 0, kRows2D, kRows2D, 1, d.K, 128, d.K, 128, s.G,
+                  a->scale, 0, 0, w.dq1, s.qn, 1.f, 1, w.dG};
+    if ((rc = dual(m_Bp, m_kn, m_draw, m_s1, q1))) return rc;
+    // dk^ = B'^T q^ + 2^{G_L-G_s} w H^T ;  dG -= k^ . dk^
+    DualParams k1{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kRows2D, 1, d.K, 128, d.K, 128, s.G,
+                  1.f, 1, 0, w.dk1, s.kn, -1.f, 1, w.dG};
+    if ((rc = dual(m_Bp, m_qn, m_w, m_h1, k1))) return rc;
+    // dw += A^T draw + 2^{G_L-G_s} k^ H
+    DualParams v1{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kRows2D, 0, 128, d.K, d.K, 128, s.G,
+                  1.f, 1, 1, w.dw, nullptr, 0.f, 0, nullptr};
+    if ((rc = dual(m_A, m_draw, m_kn, m_h1, v1))) return rc;
+  }
+  // ================= norms, write vector, gates, clock
+  rc = cyfa_token_bwd(a->q, a->k, a->q_norm_weight, a->k_norm_weight, s.q_rs, s.k_rs, w.dq1,
+                      w.dk1, s.lam, s.beta_h, w.dw, g->dq, g->dk, w.dqw_part, w.dkw_part,
+                      w.dlam_w, w.dbeta_h, d.B, d.T, d.H, d.K, stream);
+  if (rc) return rc;
+  const int nblk = token_bwd_blocks(rows);
+  column_sum_kernel<<<(d.K + 31) / 32, 256, 0, st>>>(w.dqw_part, g->dq_norm_weight, nblk, d.K);
+  column_sum_kernel<<<(d.K + 31) / 32, 256, 0, st>>>(w.dkw_part, g->dk_norm_weight, nblk, d.K);
+  if ((rc = launch_status())) return rc;
+  GatesBwdParams gp{w.dG, w.dlam_w, w.dlam_r, w.bpart1, w.bpart2, nsub1, nsub2, w.dbeta_h,
+                    g->dclock, g->dg, g->ddelta, g->dbeta, g->dclock0, d.B, d.T, d.H, d.TP};
+  gates_bwd_kernel<<<d.BH, 128, 0, st>>>(gp);
+  return launch_status();
 }
 
 }  // extern "C"

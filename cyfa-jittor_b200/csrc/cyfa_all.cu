@@ -6,5 +6,6 @@
 #include "decode.cu"
 #include "prep.cu"
 #include "gla_fwd.cu"
+#include "gla_bwd.cu"
 #include "capi.cu"
 #include "chunk_api.cu"

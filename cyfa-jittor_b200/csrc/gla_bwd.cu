@@ -1,0 +1,506 @@
+// Backward of the chunked CyFA op on tcgen05.
+//
+// For one ScalarGatedLA pass with tile states S_j (forward history) and state
+// adjoints H_{j+1} (reverse scan, state_scan_kernel<true>), and the masked tile
+// score matrices
+//   A_ts  = [s<=t] scale 2^{G_t-G_s} (q_t . k_s)
+//   B'_ts = [s<=t] scale 2^{G_t-G_s} (dO_t . v_s)
+// the adjoints are
+//   dq_t = sum_s B'_ts k_s + scale 2^{G_t} dO_t S_j^T
+//   dk_s = sum_t B'_ts q_t + 2^{G_L-G_s} v_s H_{j+1}^T
+//   dv_s = sum_t A_ts dO_t + 2^{G_L-G_s} k_s H_{j+1}
+//   dG_t = q_t . dq_t - k_t . dk_t + [t = L] <S_{j+1}, H_{j+1}>   (natural-log units)
+// (the reference's scalar_grad, cyclic_flow_attention/ops/chunk_bwd.py:1015-1041,
+// with its "force" and "boundary" gate terms at :203-235,247-272).
+//
+// tile_scores_kernel : A and B' of a tile (two 128x128 UMMAs + masked epilogue).
+// dual_gemm_kernel   : out = X1 Y1 + r_t (X2 Y2) for one tile, the shape shared by
+//                      dq, dk and dv of both passes; X1 is A or B' (or its
+//                      transpose), r_t the per-row decay factor, plus an optional
+//                      per-row dot product folded into dG.
+// readout_bwd_kernel : adjoint of the softmax slot readout (ops/chunk_readout.py:401-621):
+//                      dcoeff = U(lam) dw, dp = dcoeff Table^T, dl = p o (dp - <p,dp>),
+//                      dz = dl Table, draw = U(-lam) dz, dlam from the rotations,
+//                      and the tile's partial dTable = p^T dcoeff + dl^T z.
+#include "cyfa_common.cuh"
+#include "phase.cuh"
+
+namespace cyfa {
+
+// ============================================================ tile scores
+struct ScoresParams {
+  int BH, H, TP, NT;
+  int do_mode, v_mode;
+  const float* G;
+  float scale;
+  __nv_bfloat16* A;   // [BH*NT*128, 128]
+  __nv_bfloat16* Bp;  // [BH*NT*128, 128]
+};
+
+template <int DK, int DV>
+constexpr int scores_smem() {
+  return 2 * DK * 256 + 2 * DV * 256 + 1024;
+}
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(128, 1)
+    tile_scores_kernel(const __grid_constant__ CUtensorMap map_q,
+                       const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_do,
+                       const __grid_constant__ CUtensorMap map_v, ScoresParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  constexpr int kQ = 0, kK = DK * 256, kD = 2 * DK * 256, kV = 2 * DK * 256 + DV * 256;
+  __shared__ __align__(8) uint64_t bar_in, bar_mma;
+  __shared__ uint32_t tmem_base;
+  __shared__ float Gs[128];
+  const int tid = threadIdx.x;
+  const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT;
+  if (tid == 0) {
+    mbar_init(&bar_in, 1);
+    mbar_init(&bar_mma, 1);
+    mbar_fence_init();
+  }
+  if (tid < 32) tmem_alloc(&tmem_base, 256);
+  Gs[tid] = p.G[size_t(bh) * p.TP + j * 128 + tid];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base, lane_tmem = tmem_lane_base(tmem);
+  bool ok = true;
+  if (tid == 0) {
+    mbar_expect_tx(&bar_in, 2 * DK * 256 + 2 * DV * 256);
+    load_token_tile(smem + kQ, &map_q, kRows2D, bh, p.H, p.TP, j, 0, DK, &bar_in);
+    load_token_tile(smem + kK, &map_k, kRows2D, bh, p.H, p.TP, j, 0, DK, &bar_in);
+    load_token_tile(smem + kD, &map_do, p.do_mode, bh, p.H, p.TP, j, 0, DV, &bar_in);
+    load_token_tile(smem + kV, &map_v, p.v_mode, bh, p.H, p.TP, j, 0, DV, &bar_in);
+    if (mbar_wait(&bar_in, 0)) {
+      tc_fence_after();
+      const uint32_t sQ = smem_u32(smem + kQ), sK = smem_u32(smem + kK),
+                     sD = smem_u32(smem + kD), sV = smem_u32(smem + kV);
+#pragma unroll 4
+      for (int ks = 0; ks < DK / 16; ++ks)
+        umma_bf16(tmem, kmaj_desc(sQ, 128, ks), kmaj_desc(sK, 128, ks), make_idesc(128, 128, 0, 0),
+                  ks > 0);
+#pragma unroll 4
+      for (int ks = 0; ks < DV / 16; ++ks)
+        umma_bf16(tmem + 128, kmaj_desc(sD, 128, ks), kmaj_desc(sV, 128, ks),
+                  make_idesc(128, 128, 0, 0), ks > 0);
+      umma_commit(&bar_mma);
+    } else {
+      mbar_arrive(&bar_mma);
+    }
+  }
+  __syncwarp();
+  if (!mbar_wait(&bar_mma, 0)) ok = false;
+  tc_fence_after();
+  if (ok) {
+    const float gt = Gs[tid];
+    const size_t row = (size_t(bh) * p.NT + j) * 128 + tid;
+#pragma unroll 1
+    for (int m = 0; m < 2; ++m) {
+      __nv_bfloat16* dst = (m == 0 ? p.A : p.Bp) + row * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(lane_tmem + m * 128 + 32 * c, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int s = 32 * c + i;
+          v[i] = s <= tid ? p.scale * v[i] * exp2f(gt - Gs[s]) : 0.f;
+        }
+        store_bf16x32_global(dst + 32 * c, v);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (tid < 32) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ============================================================ dual GEMM
+struct DualParams {
+  int BH, H, TP, NT, T;
+  int x1_mn;          // 0: X1 as stored ([t][s], K-major); 1: its transpose (MN-major)
+  int y1_mode;        // token-row mode of Y1 [128 tok x N]
+  int x2_mode;        // token-row mode of X2 [128 tok x KD]
+  int y2_kmaj;        // 1: B2 = hist^T (N = hist rows); 0: B2 = hist (N = hist cols)
+  int N, KD;
+  int hrows, hcols;   // history tile [hrows x hcols]
+  const float* G;
+  float scale;
+  int fkind;          // row factor: 0 -> scale 2^{G_t}; 1 -> 2^{G_L - G_t}
+  int out_mode;       // 0: fp32 [BH,TP,N] store; 1: fp32 add; 2: bf16 public [B,T,H,N]
+  void* out;
+  const __nv_bfloat16* dot_src;  // optional [BH,TP,N] row-dot partner
+  float dot_sign;
+  int dot_acc;
+  float* dG;
+};
+
+constexpr int kDualSmem = 192 * 1024 + 1024;
+
+__global__ void __launch_bounds__(128, 1)
+    dual_gemm_kernel(const __grid_constant__ CUtensorMap map_x1,
+                     const __grid_constant__ CUtensorMap map_y1,
+                     const __grid_constant__ CUtensorMap map_x2,
+                     const __grid_constant__ CUtensorMap map_y2, DualParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  const int kX1 = 0, kY1 = 32768, kX2 = 32768 + p.N * 256, kY2 = kX2 + p.KD * 256;
+  __shared__ __align__(8) uint64_t bar_in, bar_mma;
+  __shared__ uint32_t tmem_base;
+  const int tid = threadIdx.x;
+  const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT;
+  const int t = j * 128 + tid;
+  if (tid == 0) {
+    mbar_init(&bar_in, 1);
+    mbar_init(&bar_mma, 1);
+    mbar_fence_init();
+  }
+  if (tid < 32) tmem_alloc(&tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base, lane_tmem = tmem_lane_base(tmem);
+  bool ok = true;
+  if (tid == 0) {
+    mbar_expect_tx(&bar_in, 32768 + p.N * 256 + p.KD * 256 + p.hrows * p.hcols * 2);
+    load_hist_tile(smem + kX1, &map_x1, (bh * p.NT + j) * 128, 0, 128, 128, &bar_in);
+    load_token_tile(smem + kY1, &map_y1, p.y1_mode, bh, p.H, p.TP, j, 0, p.N, &bar_in);
+    load_token_tile(smem + kX2, &map_x2, p.x2_mode, bh, p.H, p.TP, j, 0, p.KD, &bar_in);
+    load_hist_tile(smem + kY2, &map_y2, (bh * p.NT + j) * p.hrows, 0, p.hcols, p.hrows, &bar_in);
+    if (mbar_wait(&bar_in, 0)) {
+      tc_fence_after();
+      const uint32_t sX1 = smem_u32(smem + kX1), sY1 = smem_u32(smem + kY1),
+                     sX2 = smem_u32(smem + kX2), sY2 = smem_u32(smem + kY2);
+      const uint32_t id1 = make_idesc(128, p.N, p.x1_mn, 1);
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem, p.x1_mn ? mnmaj_desc(sX1, 128, ks) : kmaj_desc(sX1, 128, ks),
+                  mnmaj_desc(sY1, 128, ks), id1, ks > 0);
+      const uint32_t id2 = make_idesc(128, p.N, 0, p.y2_kmaj ? 0 : 1);
+      for (int ks = 0; ks < p.KD / 16; ++ks)
+        umma_bf16(tmem + 256, kmaj_desc(sX2, 128, ks),
+                  p.y2_kmaj ? kmaj_desc(sY2, p.hrows, ks) : mnmaj_desc(sY2, p.hrows, ks), id2,
+                  ks > 0);
+      umma_commit(&bar_mma);
+    } else {
+      mbar_arrive(&bar_mma);
+    }
+  }
+  __syncwarp();
+  if (!mbar_wait(&bar_mma, 0)) ok = false;
+  tc_fence_after();
+  if (ok) {
+    const float* Gt = p.G + size_t(bh) * p.TP + j * 128;
+    const float f = p.fkind == 0 ? p.scale * exp2f(Gt[tid]) : exp2f(Gt[127] - Gt[tid]);
+    float dot = 0.f;
+    const size_t row = size_t(bh) * p.TP + t;
+#pragma unroll 1
+    for (int c = 0; c < p.N / 32; ++c) {
+      float a[32], b[32];
+      tmem_ld32(lane_tmem + 32 * c, a);
+      tmem_ld32(lane_tmem + 256 + 32 * c, b);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) a[i] += f * b[i];
+      if (p.dot_src) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.dot_src + row * p.N + 32 * c);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float x[8];
+          unpack_bf16x8(src[q], x);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) dot += x[e] * a[8 * q + e];
+        }
+      }
+      if (p.out_mode == 2) {
+        if (t < p.T) {
+          const int b_ = bh / p.H, h = bh % p.H;
+          store_bf16x32_global(
+              static_cast<__nv_bfloat16*>(p.out) + ((size_t(b_) * p.T + t) * p.H + h) * p.N + 32 * c,
+              a);
+        }
+      } else {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + 32 * c);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 v = make_float4(a[4 * q], a[4 * q + 1], a[4 * q + 2], a[4 * q + 3]);
+          if (p.out_mode == 1) {
+            const float4 o = dst[q];
+            v.x += o.x;
+            v.y += o.y;
+            v.z += o.z;
+            v.w += o.w;
+          }
+          dst[q] = v;
+        }
+      }
+    }
+    if (p.dot_src) p.dG[row] = (p.dot_acc ? p.dG[row] : 0.f) + p.dot_sign * dot;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (tid < 32) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================ readout adjoint
+struct ReadoutBwdParams {
+  int BH, H, TP, NT;
+  const __nv_bfloat16* raw;      // [BH,TP,128]
+  const __nv_bfloat16* weights;  // [BH,TP,128]
+  const float* dweights;         // [BH,TP,128]
+  const float* lam;              // [BH,TP]
+  __nv_bfloat16* draw;           // [BH,TP,128]
+  float* dlam;                   // [BH,TP]
+  float* dtab_part;              // [BH*NT, 128, 128]
+};
+
+constexpr int kReadoutBwdSmem = 160 * 1024 + 1024;
+
+__global__ void __launch_bounds__(128, 1)
+    readout_bwd_kernel(const __grid_constant__ CUtensorMap map_tab, ReadoutBwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  __shared__ __align__(8) uint64_t bar_tab, bar_m1, bar_m2;
+  __shared__ uint32_t tmem_base;
+  const int tid = threadIdx.x;
+  const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT;
+  const int t = j * 128 + tid;
+  const size_t row = size_t(bh) * p.TP + t;
+  if (tid == 0) {
+    mbar_init(&bar_tab, 1);
+    mbar_init(&bar_m1, 1);
+    mbar_init(&bar_m2, 1);
+    mbar_fence_init();
+  }
+  if (tid < 32) tmem_alloc(&tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base, lane_tmem = tmem_lane_base(tmem);
+  const uint32_t sTab = smem_u32(smem), sZ = sTab + 32768, sDC = sTab + 65536,
+                 sP = sTab + 98304, sDL = sTab + 131072;
+  if (tid == 0) {
+    mbar_expect_tx(&bar_tab, 32768);
+    load_hist_tile(smem, &map_tab, (bh % p.H) * 128, 0, 128, 128, &bar_tab);
+  }
+  bool ok = true;
+  const float lam = p.lam[row];
+  // z = U(lam) raw and dcoeff = U(lam) dweights, bf16 operands
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    float z[32], dc[32];
+    const uint4* rsrc = reinterpret_cast<const uint4*>(p.raw + row * 128 + 32 * c);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) unpack_bf16x8(rsrc[q], z + 8 * q);
+    const float4* dsrc = reinterpret_cast<const float4*>(p.dweights + row * 128 + 32 * c);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 x = dsrc[q];
+      dc[4 * q] = x.x;
+      dc[4 * q + 1] = x.y;
+      dc[4 * q + 2] = x.z;
+      dc[4 * q + 3] = x.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      float sn, cs;
+      __sincosf(clock_phase(lam, 16 * c + i / 2), &sn, &cs);
+      const float e = z[i], o = z[i + 1];
+      z[i] = cs * e - sn * o;
+      z[i + 1] = sn * e + cs * o;
+      const float de = dc[i], dd = dc[i + 1];
+      dc[i] = cs * de - sn * dd;
+      dc[i + 1] = sn * de + cs * dd;
+    }
+    store_row32_bf16(sZ + (c >> 1) * 16384, tid, (c & 1) * 4, z);
+    store_row32_bf16(sDC + (c >> 1) * 16384, tid, (c & 1) * 4, dc);
+  }
+  fence_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid == 0) {
+    if (mbar_wait(&bar_tab, 0)) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem, kmaj_desc(sZ, 128, ks), kmaj_desc(sTab, 128, ks),
+                  make_idesc(128, 128, 0, 0), ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem + 128, kmaj_desc(sDC, 128, ks), kmaj_desc(sTab, 128, ks),
+                  make_idesc(128, 128, 0, 0), ks > 0);
+      umma_commit(&bar_m1);
+    } else {
+      mbar_arrive(&bar_m1);
+    }
+  }
+  __syncwarp();
+  if (!mbar_wait(&bar_m1, 0)) ok = false;
+  tc_fence_after();
+  if (ok) {
+    float mx = -1e30f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float v[32];
+      tmem_ld32(lane_tmem + 32 * c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (32 * c + i < 127) mx = fmaxf(mx, v[i]);
+    }
+    float sum = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float v[32];
+      tmem_ld32(lane_tmem + 32 * c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (32 * c + i < 127) sum += __expf(v[i] - mx);
+    }
+    const float inv = 1.f / sum;
+    float pdp = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float v[32], d[32];
+      tmem_ld32(lane_tmem + 32 * c, v);
+      tmem_ld32(lane_tmem + 128 + 32 * c, d);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        v[i] = (32 * c + i < 127) ? __expf(v[i] - mx) * inv : 0.f;
+        pdp += v[i] * d[i];
+      }
+      store_row32_bf16(sP + (c >> 1) * 16384, tid, (c & 1) * 4, v);
+    }
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float v[32], d[32];
+      tmem_ld32(lane_tmem + 32 * c, v);
+      tmem_ld32(lane_tmem + 128 + 32 * c, d);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float pr = (32 * c + i < 127) ? __expf(v[i] - mx) * inv : 0.f;
+        v[i] = pr * (d[i] - pdp);
+      }
+      store_row32_bf16(sDL + (c >> 1) * 16384, tid, (c & 1) * 4, v);
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  tc_fence_after();
+  if (tid == 0) {
+    if (ok) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem + 256, kmaj_desc(sDL, 128, ks), mnmaj_desc(sTab, 128, ks),
+                  make_idesc(128, 128, 0, 1), ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem + 384, mnmaj_desc(sP, 128, ks), mnmaj_desc(sDC, 128, ks),
+                  make_idesc(128, 128, 1, 1), ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem + 384, mnmaj_desc(sDL, 128, ks), mnmaj_desc(sZ, 128, ks),
+                  make_idesc(128, 128, 1, 1), 1);
+      umma_commit(&bar_m2);
+    } else {
+      mbar_arrive(&bar_m2);
+    }
+  }
+  __syncwarp();
+  if (!mbar_wait(&bar_m2, 0)) ok = false;
+  tc_fence_after();
+  if (ok) {
+    float dl = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float dz[32], z[32], w[32], dw[32];
+      tmem_ld32(lane_tmem + 256 + 32 * c, dz);
+      const uint4* rsrc = reinterpret_cast<const uint4*>(p.raw + row * 128 + 32 * c);
+      const uint4* wsrc = reinterpret_cast<const uint4*>(p.weights + row * 128 + 32 * c);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        unpack_bf16x8(rsrc[q], z + 8 * q);
+        unpack_bf16x8(wsrc[q], w + 8 * q);
+      }
+      const float4* dsrc = reinterpret_cast<const float4*>(p.dweights + row * 128 + 32 * c);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 x = dsrc[q];
+        dw[4 * q] = x.x;
+        dw[4 * q + 1] = x.y;
+        dw[4 * q + 2] = x.z;
+        dw[4 * q + 3] = x.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const int pair = 16 * c + i / 2;
+        float sn, cs;
+        __sincosf(clock_phase(lam, pair), &sn, &cs);
+        const float ze = bf16_round(cs * z[i] - sn * z[i + 1]);
+        const float zo = bf16_round(sn * z[i] + cs * z[i + 1]);
+        const float de = dz[i], dd = dz[i + 1];
+        dl += (pair * kTwoPiOver127) *
+              (-de * zo + dd * ze + dw[i] * w[i + 1] - dw[i + 1] * w[i]);
+        dz[i] = cs * de + sn * dd;
+        dz[i + 1] = -sn * de + cs * dd;
+      }
+      store_bf16x32_global(p.draw + row * 128 + 32 * c, dz);
+    }
+    p.dlam[row] = dl;
+    // this tile's partial table gradient: thread tid owns slot row r = tid
+    float* dst = p.dtab_part + size_t(blockIdx.x) * 16384 + tid * 128;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float v[32];
+      tmem_ld32(lane_tmem + 384 + 32 * c, v);
+      float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (tid < 32) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Fixed-order reduction of the per-tile table gradients:
+// dtab[h][r][m] = sum_{b, j} part[((b*H + h)*NT + j)][r][m].
+__global__ void __launch_bounds__(128) dtable_reduce_kernel(const float* part, float* dtab, int B,
+                                                            int H, int NT) {
+  const int h = blockIdx.x, r = blockIdx.y, m = threadIdx.x;
+  float s = 0.f;
+  for (int b = 0; b < B; ++b)
+    for (int j = 0; j < NT; ++j) s += part[((size_t(b) * H + h) * NT + j) * 16384 + r * 128 + m];
+  dtab[(size_t(h) * 128 + r) * 128 + m] = s;
+}
+
+// Fixed-order column sums of a [rows, cols] partial matrix: out[c] = sum_r part[r][c].
+__global__ void __launch_bounds__(256) column_sum_kernel(const float* part, float* out, int rows,
+                                                         int cols) {
+  __shared__ float acc[8][33];
+  const int c = blockIdx.x * 32 + (threadIdx.x & 31), lane_r = threadIdx.x >> 5;
+  float s = 0.f;
+  if (c < cols)
+    for (int r = lane_r; r < rows; r += 8) s += part[size_t(r) * cols + c];
+  acc[lane_r][threadIdx.x & 31] = s;
+  __syncthreads();
+  if (threadIdx.x < 32 && c < cols) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += acc[i][threadIdx.x];
+    out[c] = t;
+  }
+}
+
+}  // namespace cyfa

@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(128, 1)
     }
   }
 
-  if (ok) {
+  if (ok && p.last) {
     float4* dst = reinterpret_cast<float4*>(p.last + row_off);
 #pragma unroll
     for (int i = 0; i < 16; ++i)

@@ -14,7 +14,8 @@
 //                sums of the norm-weight gradients, and dlam, dbeta of the write
 //                vector (ops/qk_norm.py:109-165, ops/utils.py:589-640).
 //  gates_bwd   : one CTA per (b,h): ddelta = reverse cumsum of dlam (+ d clock_T),
-//                dg = log2(e) * in-tile reverse cumsum of dG, layout back to [B,T,H].
+//                dg = in-tile reverse cumsum of dG (dG taken w.r.t. the natural-log
+//                in-tile gate cumsum, tile-end terms added), layout back to [B,T,H].
 #include "cyfa_common.cuh"
 #include "phase.cuh"
 
@@ -202,70 +203,73 @@ struct TokenBwdParams {
   int B, T, H, TP;
 };
 
-// 8 warps per block, one (b,t,h) row each.  Norm-weight gradient partials are
-// reduced across the 8 rows of the block in a fixed order.
+// 8 warps per block; warp w of block b handles rows (b*8 + w) + i*gridDim.x*8.
+// Each block writes one row of norm-weight partial sums (its rows, fixed order),
+// so the partial matrices have gridDim.x rows.
 template <int K>
 __global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
   constexpr int E = K / 32;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   __shared__ float pq[8][K], pk[8][K];
-  const size_t row = size_t(blockIdx.x) * 8 + wid;
-  const bool live = row < size_t(p.B) * p.H * p.TP;
-  const int t = live ? int(row % p.TP) : 0;
-  const size_t bh = live ? row / p.TP : 0;
-  const int b = int(bh / p.H), h = int(bh % p.H);
-  const bool real = live && t < p.T;
-  float xq[E], xk[E], gq[E], gk[E];
+  float aq[E], ak[E];
 #pragma unroll
-  for (int j = 0; j < E; ++j) xq[j] = xk[j] = gq[j] = gk[j] = 0.f;
-  const size_t pub = ((size_t(b) * p.T + t) * p.H + h) * K + lane * E;
-  if (real) {
+  for (int j = 0; j < E; ++j) aq[j] = ak[j] = 0.f;
+  const size_t rows = size_t(p.B) * p.H * p.TP;
+  for (size_t row = size_t(blockIdx.x) * 8 + wid; row < rows; row += size_t(gridDim.x) * 8) {
+    const int t = int(row % p.TP);
+    const size_t bh = row / p.TP;
+    const int b = int(bh / p.H), h = int(bh % p.H);
+    const bool real = t < p.T;
+    float xq[E], xk[E], gq[E], gk[E];
+#pragma unroll
+    for (int j = 0; j < E; ++j) xq[j] = xk[j] = gq[j] = gk[j] = 0.f;
+    const size_t pub = ((size_t(b) * p.T + t) * p.H + h) * K + lane * E;
+    if (real) {
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        xq[j] = __bfloat162float(p.q[pub + j]);
+        xk[j] = __bfloat162float(p.k[pub + j]);
+        gq[j] = p.dqn[row * K + lane * E + j];
+        gk[j] = p.dkn[row * K + lane * E + j];
+      }
+    }
+    const float qr = real ? p.q_rs[row] : 0.f, kr = real ? p.k_rs[row] : 0.f;
+    float dotq = 0.f, dotk = 0.f;
 #pragma unroll
     for (int j = 0; j < E; ++j) {
-      xq[j] = __bfloat162float(p.q[pub + j]);
-      xk[j] = __bfloat162float(p.k[pub + j]);
-      gq[j] = p.dqn[row * K + lane * E + j];
-      gk[j] = p.dkn[row * K + lane * E + j];
+      const int d = lane * E + j;
+      dotq += gq[j] * p.qw[d] * xq[j];
+      dotk += gk[j] * p.kw[d] * xk[j];
     }
-  }
-  const float qr = real ? p.q_rs[row] : 0.f, kr = real ? p.k_rs[row] : 0.f;
-  float dotq = 0.f, dotk = 0.f;
 #pragma unroll
-  for (int j = 0; j < E; ++j) {
-    const int d = lane * E + j;
-    dotq += gq[j] * p.qw[d] * xq[j];
-    dotk += gk[j] * p.kw[d] * xk[j];
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    dotq += __shfl_xor_sync(0xffffffffu, dotq, o);
-    dotk += __shfl_xor_sync(0xffffffffu, dotk, o);
-  }
-  dotq *= qr * qr / K;
-  dotk *= kr * kr / K;
-#pragma unroll
-  for (int j = 0; j < E; ++j) {
-    const int d = lane * E + j;
-    if (real) {
-      p.dq[pub + j] = __float2bfloat16_rn((gq[j] * p.qw[d] - xq[j] * dotq) * qr);
-      p.dk[pub + j] = __float2bfloat16_rn((gk[j] * p.kw[d] - xk[j] * dotk) * kr);
+    for (int o = 16; o > 0; o >>= 1) {
+      dotq += __shfl_xor_sync(0xffffffffu, dotq, o);
+      dotk += __shfl_xor_sync(0xffffffffu, dotk, o);
     }
-    pq[wid][d] = xq[j] * qr * gq[j];
-    pk[wid][d] = xk[j] * kr * gk[j];
-  }
-  // write-vector adjoint (ops/utils.py:598-616)
-  if (live) {
+    dotq *= qr * qr / K;
+    dotk *= kr * kr / K;
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      const int d = lane * E + j;
+      if (real) {
+        p.dq[pub + j] = __float2bfloat16_rn((gq[j] * p.qw[d] - xq[j] * dotq) * qr);
+        p.dk[pub + j] = __float2bfloat16_rn((gk[j] * p.kw[d] - xk[j] * dotk) * kr);
+      }
+      aq[j] += xq[j] * qr * gq[j];
+      ak[j] += xk[j] * kr * gk[j];
+    }
+    // write-vector adjoint (ops/utils.py:598-616)
     const float lam = p.lam[row], bt = p.beta_h[row];
     float dl = 0.f, db = 0.f;
 #pragma unroll
     for (int part = 0; part < 2; ++part) {
       const int pair = lane + 32 * part;
-      float s, c;
-      sincosf(clock_phase(lam, pair), &s, &c);
+      float sn, cs;
+      sincosf(clock_phase(lam, pair), &sn, &cs);
       const float sc = atom_scale(pair);
       const float de = p.dw[row * 128 + 2 * pair], dd = p.dw[row * 128 + 2 * pair + 1];
-      db += de * sc * c - dd * sc * s;
-      dl += (-de * bt * sc * s - dd * bt * sc * c) * (pair * kTwoPiOver127);
+      db += de * sc * cs - dd * sc * sn;
+      dl += (-de * bt * sc * sn - dd * bt * sc * cs) * (pair * kTwoPiOver127);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -276,6 +280,11 @@ __global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
       p.dlam[row] = dl;
       p.dbeta[row] = db;
     }
+  }
+#pragma unroll
+  for (int j = 0; j < E; ++j) {
+    pq[wid][lane * E + j] = aq[j];
+    pk[wid][lane * E + j] = ak[j];
   }
   __syncthreads();
   for (int d = threadIdx.x; d < K; d += 256) {
@@ -290,12 +299,22 @@ __global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
   }
 }
 
+// Number of blocks (= partial rows) token_bwd_kernel uses for a shape.
+inline int token_bwd_blocks(size_t rows) {
+  const size_t want = (rows + 7) / 8;
+  return int(want < 1184 ? want : 1184);
+}
+
 template __global__ void token_bwd_kernel<256>(TokenBwdParams);
 template __global__ void token_bwd_kernel<128>(TokenBwdParams);
 
 struct GatesBwdParams {
-  const float* dG;       // [B,H,TP] gradient of the log2 in-tile cumsum
-  const float* dlam;     // [B,H,TP] total clock gradient
+  const float* dG;       // [B,H,TP] gradient of the in-tile gate cumsum (natural log)
+  const float* dlam;     // [B,H,TP] clock gradient
+  const float* dlam2;    // [B,H,TP] second clock gradient term, or null
+  const float* bpart1;   // [B*H, NT, nsub1] tile-end gate terms, or null
+  const float* bpart2;   // [B*H, NT, nsub2] or null
+  int nsub1, nsub2;
   const float* dbeta_h;  // [B,H,TP]
   const float* dclock;   // [B,H] gradient of the final clock, or null
   float* dg;             // [B,T,H]
@@ -331,13 +350,23 @@ __global__ void __launch_bounds__(128) gates_bwd_kernel(GatesBwdParams p) {
   for (int t0 = p.TP - 128; t0 >= 0; t0 -= 128) {
     const int t = t0 + threadIdx.x;
     float tot;
-    const float gs = rscan128(p.dG[base + t], buf, &tot);
-    const float ls = rscan128(p.dlam[base + t], buf, &tot);
+    float dGt = p.dG[base + t];
+    if (threadIdx.x == 127) {
+      const size_t tile = size_t(bh) * (p.TP / 128) + t0 / 128;
+      if (p.bpart1)
+        for (int i = 0; i < p.nsub1; ++i) dGt += p.bpart1[tile * p.nsub1 + i];
+      if (p.bpart2)
+        for (int i = 0; i < p.nsub2; ++i) dGt += p.bpart2[tile * p.nsub2 + i];
+    }
+    float dl = p.dlam[base + t];
+    if (p.dlam2) dl += p.dlam2[base + t];
+    const float gs = rscan128(dGt, buf, &tot);
+    const float ls = rscan128(dl, buf, &tot);
     const float dd = __fadd_rn(carry, ls);
     carry = __fadd_rn(carry, tot);
     if (t < p.T) {
       const size_t i = (size_t(b) * p.T + t) * p.H + h;
-      p.dg[i] = gs * kLog2e;
+      p.dg[i] = gs;
       p.ddelta[i] = dd;
       p.dbeta[i] = p.dbeta_h[base + t];
     }

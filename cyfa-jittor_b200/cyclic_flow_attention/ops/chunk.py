@@ -27,7 +27,7 @@ class _FwdArgs(_c.Structure):
 
 class _BwdArgs(_c.Structure):
     _fields_ = [("fwd", _FwdArgs)] + \
-        [(n, _c.c_void_p) for n in ("do", "dhk", "dhv", "dclock", "dq", "dk", "dv", "dg",
+        [(n, _c.c_void_p) for n in ("d_o", "dhk", "dhv", "dclock", "dq", "dk", "dv", "dg",
                                      "ddelta", "dbeta", "dtable", "dq_norm_weight",
                                      "dk_norm_weight", "dhk0", "dhv0", "dclock0")]
 

@@ -79,7 +79,8 @@ int cyfa_token_fwd(const void* q, const void* k, const float* q_norm_weight,
 
 /* ---------------------------------------------------------------- backward prep
  * Adjoint of cyfa_token_fwd.  dqn/dkn [B,H,TP,K] f32, dw [B,H,TP,128] f32 in;
- * dq/dk public-layout bf16, norm-weight partial sums [ceil(B*H*TP/8), K] f32,
+ * dq/dk public-layout bf16, norm-weight partial sums
+ * [min(ceil(B*H*TP/8), 1184), K] f32 (sum the rows for the weight gradient),
  * dlam (write-vector part) and dbeta_h [B,H,TP] f32 out.
  * Replaces: VectorNorm.grad (ops/qk_norm.py:109-165), PhaseWriteOnly.grad
  * (ops/utils.py:589-640). */
@@ -90,7 +91,8 @@ int cyfa_token_bwd(const void* q, const void* k, const float* q_norm_weight,
                    float* dlam, float* dbeta_h, int B, int T, int H, int K, void* stream);
 
 /* Adjoint of cyfa_gates_fwd: dG, dlam, dbeta_h [B,H,TP] (+ dclock [B,H] or NULL)
- * -> dg, ddelta, dbeta [B,T,H] and dclock0 [B,H] (or NULL).
+ * -> dg, ddelta, dbeta [B,T,H] and dclock0 [B,H] (or NULL).  dG is the gradient
+ * w.r.t. the natural-log in-tile gate cumsum (G / log2(e)).
  * Replaces: ClockScan.grad (ops/utils.py:297-298), ClockTotal.grad (:343-344),
  * HeadGates.grad (:459-488) and the local cumsum adjoint. */
 int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h,
@@ -131,6 +133,43 @@ size_t cyfa_chunk_saved_bytes(int B, int T, int H, int K, int V);
 
 int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* args, void* saved, size_t saved_bytes,
                    void* stream);
+
+/* Backward of cyfa_chunk_fwd.  `fwd` repeats the forward arguments (its o may be
+ * NULL; hk, hv and clock must hold the forward's final state).  d_o [B,T,H,V] bf16
+ * is required; dhk, dhv, dclock (gradients of the final state) may be NULL.
+ * Outputs: dq, dk [B,T,H,K] bf16, dv [B,T,H,V] bf16, dg, ddelta, dbeta [B,T,H] f32,
+ * dtable [H,128,128] f32 (gradient of the readout table R.Phi; row 127 unused),
+ * dq_norm_weight, dk_norm_weight [K] f32, and dhk0, dhv0, dclock0 (initial-state
+ * gradients, each may be NULL).  `work` is scratch (cyfa_chunk_work_bytes).
+ * Replaces: ScalarAttention.grad / scalar_grad (ops/chunk.py:51-71,
+ * ops/chunk_bwd.py:1015-1041), FirstReadoutCompact.grad / readout_grad_compact
+ * (ops/chunk_readout.py:976-987,401-621), state_backward (ops/chunk_h.py:342),
+ * PhaseWriteOnly.grad, ClockScan.grad, HeadGates.grad (ops/utils.py) and
+ * VectorNorm.grad (ops/qk_norm.py:109-165). */
+typedef struct {
+  cyfa_chunk_fwd_args fwd;
+  const void* d_o;              /* [B,T,H,V] bf16 */
+  const float* dhk;             /* [B,H,K,128] or NULL */
+  const float* dhv;             /* [B,H,128,V] or NULL */
+  const float* dclock;          /* [B,H] or NULL */
+  void* dq;                     /* out [B,T,H,K] bf16 */
+  void* dk;                     /* out [B,T,H,K] bf16 */
+  void* dv;                     /* out [B,T,H,V] bf16 */
+  float* dg;                    /* out [B,T,H] */
+  float* ddelta;                /* out [B,T,H] */
+  float* dbeta;                 /* out [B,T,H] */
+  float* dtable;                /* out [H,128,128] */
+  float* dq_norm_weight;        /* out [K] */
+  float* dk_norm_weight;        /* out [K] */
+  float* dhk0;                  /* out [B,H,K,128] or NULL */
+  float* dhv0;                  /* out [B,H,128,V] or NULL */
+  float* dclock0;               /* out [B,H] or NULL */
+} cyfa_chunk_bwd_args;
+
+size_t cyfa_chunk_work_bytes(int B, int T, int H, int K, int V);
+
+int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* args, const void* saved, size_t saved_bytes,
+                   void* work, size_t work_bytes, void* stream);
 
 /* ---------------------------------------------------------------- self test
  * C[128,N] = A * B through TMA + tcgen05 (test hook for the UMMA descriptor and

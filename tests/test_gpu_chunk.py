@@ -97,3 +97,68 @@ def test_chunk_strong_decay_stays_finite(ops):
     assert torch.isfinite(o).all() and all(torch.isfinite(x).all() for x in fs)
     ref_o, _ = O.chunk_cyfa(*[x.float() for x in ins[:6]], *ins[6:], dtype=torch.float32)
     assert rel_l2(o, ref_o) < BF16_TOL
+
+
+BWD_CASES = [
+    (1, 256, 2, 256, 256, False),
+    (2, 200, 1, 256, 256, True),
+    (1, 256, 2, 128, 128, True),
+    (1, 130, 1, 256, 128, False),
+    (1, 384, 1, 128, 256, True),
+]
+
+
+@pytest.mark.parametrize("B,T,H,K,V,with_state", BWD_CASES)
+def test_chunk_backward(ops, B, T, H, K, V, with_state):
+    ins, state = make_inputs(B, T, H, K, V, seed=B * 77 + T + K + 3 * V, with_state=with_state)
+    gen = seeded(T + 5)
+    do = torch.randn(B, T, H, V, generator=gen)
+    dst = None
+    if with_state:
+        dst = (torch.randn(B, H, K, 128, generator=gen), torch.randn(B, H, 128, V, generator=gen),
+               torch.randn(B, H, generator=gen))
+    # GPU
+    dev = [x.cuda().requires_grad_(True) for x in ins]
+    st = None if state is None else tuple(x.cuda().requires_grad_(True) for x in state)
+    o, fs = ops.chunk_cyfa(*dev, initial_state=st, output_final_state=True)
+    loss = (o.float() * do.cuda()).sum()
+    if dst is not None:
+        loss = loss + sum((a * b.cuda()).sum() for a, b in zip(fs, dst))
+    loss.backward()
+    torch.cuda.synchronize()
+    # oracle (fp32 autograd)
+    ref_in = [x.float().clone().requires_grad_(True) for x in ins]
+    ref_st = None if state is None else tuple(x.clone().requires_grad_(True) for x in state)
+    ro, rs = O.chunk_cyfa(*ref_in, initial_state=ref_st, output_final_state=True,
+                          dtype=torch.float32)
+    rl = (ro * do).sum()
+    if dst is not None:
+        rl = rl + sum((a * b).sum() for a, b in zip(rs, dst))
+    rl.backward()
+    names = ["q", "k", "v", "g", "delta", "beta", "readout", "q_norm_weight", "k_norm_weight"]
+    tols = [BF16_TOL, BF16_TOL, BF16_TOL, GATE_TOL, GATE_TOL, GATE_TOL, BF16_TOL, BF16_TOL,
+            BF16_TOL]
+    errs = {n: rel_l2(a.grad, b.grad) for n, a, b in zip(names, dev, ref_in)}
+    if st is not None:
+        for n, a, b in zip(["hk0", "hv0", "clock0"], st, ref_st):
+            errs[n] = rel_l2(a.grad, b.grad)
+        tols += [BF16_TOL, BF16_TOL, GATE_TOL]
+        names += ["hk0", "hv0", "clock0"]
+    bad = {n: e for n, t, (n2, e) in zip(names, tols, errs.items()) if e >= t}
+    assert not bad, f"gradient errors over tolerance: {bad} (all: {errs})"
+    from cyclic_flow_attention import _lib
+
+    assert _lib.device_error() == 0
+
+
+def test_chunk_backward_deterministic(ops):
+    ins, _ = make_inputs(2, 300, 2, 256, 256, seed=21)
+    do = torch.randn(2, 300, 2, 256, generator=seeded(1)).cuda()
+    grads = []
+    for _ in range(2):
+        dev = [x.cuda().requires_grad_(True) for x in ins]
+        o, _ = ops.chunk_cyfa(*dev)
+        (o.float() * do).sum().backward()
+        grads.append([x.grad.clone() for x in dev])
+    for a, b in zip(*grads):
+        assert torch.equal(a, b)

@@ -185,8 +185,8 @@ def test_token_fwd_bwd(L, K):
     nblk = (B * H * TP + 7) // 8
     dq = torch.empty(B, T, H, K, device="cuda", dtype=torch.bfloat16)
     dk = torch.empty_like(dq)
-    dqw = torch.empty(nblk, K, device="cuda")
-    dkw = torch.empty_like(dqw)
+    dqw = torch.zeros(nblk, K, device="cuda")
+    dkw = torch.zeros_like(dqw)
     dlam = torch.empty(B, H, TP, device="cuda")
     dbeta = torch.empty_like(dlam)
     L.call("cyfa_token_bwd", *[L.ptr(x) for x in (dev(q), dev(k), dev(qw), dev(kw), qrs, krs,
@@ -220,7 +220,8 @@ def test_gates_bwd(L, T):
     d = torch.zeros(B, T, H, dtype=torch.float64, requires_grad=True)
     c0 = torch.zeros(B, H, dtype=torch.float64, requires_grad=True)
     gp = torch.nn.functional.pad(g.permute(0, 2, 1), (0, TP - T))
-    G = gp.reshape(B, H, TP // 128, 128).cumsum(-1).reshape(B, H, TP) / math.log(2)
+    # dG is the gradient w.r.t. the natural-log in-tile cumsum
+    G = gp.reshape(B, H, TP // 128, 128).cumsum(-1).reshape(B, H, TP)
     dp = torch.nn.functional.pad(d.permute(0, 2, 1), (0, TP - T))
     lam = dp.cumsum(-1) + c0.unsqueeze(-1)
     clock = dp.sum(-1) + c0
