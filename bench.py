@@ -1,0 +1,385 @@
+#!/usr/bin/env python
+"""CyFA layer forward+backward benchmark on B200 (one JSON line on rank 0).
+
+Workload (the config the headline metric is quoted on):
+one CyclicFlowAttention layer, hidden 1024, 4 heads x head_dim 256, 128 slots,
+B=8, T=2048, bf16, forward + backward (loss = <y, dy>, dy ~ N(0,1)), random-init
+weights N(0, 0.02), synthetic x ~ N(0,1).  With --gpus N (torchrun) every rank
+runs its own B=8 batch (weak scaling, batch-sharded data parallel) and the
+weight gradients are averaged with one NCCL all-reduce per step.
+
+--impl reference times the reference algorithm's CPU restatement (the oracle;
+the reference itself has no CPU path and needs Jittor) on the host cores.
+"""
+
+import argparse
+import csv
+import datetime
+import io
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "cyfa-jittor_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "CyFA layer fwd+bwd tokens/s/GPU; decode tokens/s; % of TC/HBM roofline"
+UNIT = "tokens/s"
+CFG = dict(hidden=1024, heads=4, head_dim=256, slots=128, B=8, T=2048)
+L2_BYTES = 126 * 2 ** 20
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# Algorithmic work (FLOPs, full 128x128 tiles as the tensor cores issue them) per
+# 128-token tile of one (batch, head), by kernel, for K = V = 256, 128 slots.
+# A tile has C = 128 tokens; per pass: pass 1 is (Dk, Dv) = (K, 128), pass 2 (128, V).
+def _tile_flops(K=256, V=256, C=128, M=128):
+    p1 = (K, M)
+    p2 = (M, V)
+    out = {}
+    # forward output tiles: QK^T (2 C C Dk) + Q S (2 C Dk Dv) + P V (2 C C Dv)
+    def fwd(dk, dv):
+        return 2 * C * C * dk + 2 * C * dk * dv + 2 * C * C * dv
+    out["tile_fwd_readout"] = fwd(*p1) + 2 * (2 * C * M * M)
+    out["tile_fwd"] = fwd(*p2)
+    # state scans: K^T V per tile (2 C Dk Dv) per pass
+    out["state_scan_fwd"] = 2 * C * p1[0] * p1[1] + 2 * C * p2[0] * p2[1]
+    out["state_scan_bwd"] = out["state_scan_fwd"]
+    # scores: QK^T and dO V^T
+    out["tile_scores"] = sum(2 * C * C * dk + 2 * C * C * dv for dk, dv in (p1, p2))
+    # dual GEMMs: dq (N=Dk, KD=Dv), dk (N=Dk, KD=Dv), dv (N=Dv, KD=Dk): 2 C (C N + KD N)
+    out["dual_gemm"] = sum(2 * C * (C * dk + dv * dk) * 2 + 2 * C * (C * dv + dk * dv)
+                           for dk, dv in (p1, p2))
+    out["readout_bwd"] = 5 * 2 * C * M * M
+    return out
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    except (OSError, ValueError):
+        return PEAKS_FALLBACK, "fallback"
+
+
+def _traffic_from_profiles(kernel):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
+    try:
+        with open(path) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 2 and parts[0] == kernel:
+                    return float(parts[1])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4)
+                          if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].strip().replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def _rank_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+# ---------------------------------------------------------------- CPU baseline
+def cpu_layer_tokens_per_s(min_seconds=10.0, max_reps=20, T=None, warm=1):
+    """Times the oracle layer fwd+bwd (fp32, all host threads) on one sequence."""
+    import torch
+
+    from oracle import cyfa_oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    T = T or CFG["T"]
+    gen = torch.Generator().manual_seed(0)
+    H, hd, hid = CFG["heads"], CFG["head_dim"], CFG["hidden"]
+    shapes = {
+        "q_proj.weight": (H * hd, hid), "k_proj.weight": (H * hd, hid),
+        "v_proj.weight": (H * hd, hid), "a_proj.weight": (H, hid), "b_proj.weight": (H, hid),
+        "b_proj.bias": (H,), "d_proj.weight": (H, hid), "d_proj.bias": (H,),
+        "q_conv1d.weight": (H * hd, 1, 4), "k_conv1d.weight": (H * hd, 1, 4),
+        "v_conv1d.weight": (H * hd, 1, 4), "g_proj.0.weight": (hd, hid),
+        "g_proj.1.weight": (H * hd, hd), "g_proj.1.bias": (H * hd,),
+        "o_proj.weight": (hid, H * hd)}
+    params = {n: torch.randn(*s, generator=gen) * 0.02 for n, s in shapes.items()}
+    params["dt_bias"] = torch.full((H,), -4.0)
+    params["A_log"] = torch.log(torch.rand(H, generator=gen) * 16 + 1e-3)
+    params["readout"] = torch.eye(127).expand(H, -1, -1).clone()
+    for n in ("q_norm.weight", "k_norm.weight", "o_norm.weight"):
+        params[n] = torch.ones(hd)
+    for p in params.values():
+        p.requires_grad_(True)
+    x = torch.randn(1, T, hid, generator=gen, requires_grad=True)
+    dy = torch.randn(1, T, hid, generator=gen)
+
+    def step():
+        y = O.cyfa_layer(params, x, H, hd, hd)
+        (y * dy).sum().backward()
+
+    for _ in range(warm):
+        step()
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < max_reps and (reps == 0 or time.perf_counter() - t0 < min_seconds):
+        step()
+        reps += 1
+    dt = time.perf_counter() - t0
+    return reps * T / dt, threads, f"{reps} x (1 seq x {T} tokens) layer fwd+bwd, fp32 oracle"
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    # each step: one sequence of the workload (bounded sample), timed on host cores
+    tps_warm = cpu_layer_tokens_per_s(min_seconds=0.0, max_reps=max(1, args.warmup), warm=0)[0]
+    t0 = time.perf_counter()
+    tps, cores, _ = cpu_layer_tokens_per_s(min_seconds=0.0, max_reps=args.steps, warm=0)
+    dt = time.perf_counter() - t0
+    sample = f"{args.steps} steps x (1 seq x {CFG['T']} tokens) layer fwd+bwd, fp32 CPU oracle"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "cyfa_layer_fwd_bwd (BASELINE configs[2]) on host cores",
+                   **CFG, "parallelism": "cpu"},
+        "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference (Jittor) has no CPU path and cannot be installed here; "
+                "this is its algorithm restated in oracle/ (warm-up tokens/s %.1f)" % tps_warm,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def run_cyfa(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from cyclic_flow_attention import CyclicFlowAttention, _lib
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    B, T, hid = CFG["B"], CFG["T"], CFG["hidden"]
+    torch.manual_seed(0)
+    layer = CyclicFlowAttention(hid, CFG["heads"], CFG["head_dim"], num_slots=CFG["slots"])
+    with torch.no_grad():
+        for name, p in layer.named_parameters():
+            if p.dim() >= 2 and name != "readout":
+                p.normal_(0, 0.02)
+    layer = layer.keep_fp32().to(dev)
+    params = [p for p in layer.parameters()]
+    gen = torch.Generator().manual_seed(1000 + rank)
+    x_host = torch.randn(B, T, hid, generator=gen).to(torch.bfloat16).pin_memory()
+    dy_host = torch.randn(B, T, hid, generator=gen).to(torch.bfloat16).pin_memory()
+    x = x_host.to(dev)
+    dy = dy_host.to(dev)
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+
+    def allreduce_grads():
+        if world > 1:
+            flat = torch.cat([p.grad.float().reshape(-1) for p in params])
+            dist.all_reduce(flat, op=dist.ReduceOp.AVG)
+            off = 0
+            for p in params:
+                n = p.numel()
+                p.grad.copy_(flat[off:off + n].view_as(p.grad))
+                off += n
+
+    def step(xin, dyin):
+        for p in params:
+            p.grad = None
+        y, _ = layer(xin)
+        loss = (y.float() * dyin.float()).sum()
+        loss.backward()
+        allreduce_grads()
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(x, dy)
+    barrier()
+
+    # ---- device-resident timing (value): per-step events, L2 flushed between steps
+    sampler = ClockSampler(torch.cuda.current_device() if world == 1 else local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    launches0 = _lib.launch_count()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    barrier()
+    for a, b in evs:
+        flush.fill_(1)
+        a.record()
+        step(x, dy)
+        b.record()
+    barrier()
+    launches = _lib.launch_count() - launches0
+    clocks = sampler.stop()
+    total_ms = sum(a.elapsed_time(b) for a, b in evs)
+    t = torch.tensor([total_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = t.item() / args.steps
+    value = world * B * T / (ms_per_step / 1000.0)
+
+    # ---- end to end: pinned host inputs copied in, loss read back, every step
+    e_a, e_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e_a.record()
+    for _ in range(args.steps):
+        xi = x_host.to(dev, non_blocking=True)
+        di = dy_host.to(dev, non_blocking=True)
+        loss = step(xi, di)
+        loss.item()
+    e_b.record()
+    barrier()
+    te = torch.tensor([e_a.elapsed_time(e_b)], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = te.item() / args.steps
+    e2e = {"value": world * B * T / (e2e_ms / 1000.0), "unit": UNIT,
+           "h2d_bytes_per_step": x_host.numel() * 2 + dy_host.numel() * 2,
+           "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms}
+
+    # ---- per-kernel event timing of one step (separate pass) -> dominant kernel
+    barrier()
+    _lib.profile_enable(True)
+    flush.fill_(1)
+    step(x, dy)
+    torch.cuda.synchronize()
+    prof = _lib.profile_report()
+    _lib.profile_enable(False)
+    peaks, peak_kind = _peaks()
+    tiles = B * CFG["heads"] * math.ceil(T / 128)
+    flops = _tile_flops(CFG["head_dim"], CFG["head_dim"])
+    roofline = None
+    if prof:
+        dom = max(prof.items(), key=lambda kv: kv[1][0])
+        name, (ms, n) = dom
+        peak = peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"])
+        work = flops.get(name, 0) * tiles  # all launches of this kernel in one step
+        achieved = work / (ms / 1000.0) / 1e12 if ms > 0 else 0.0
+        traffic = _traffic_from_profiles(name)
+        roofline = {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": peak,
+                    "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                    "peak_kind": f"{peak_kind} bf16 sustained",
+                    "launches_per_step": n, "ms_per_step": ms,
+                    "kernel_ms": {k: round(v[0], 4) for k, v in sorted(prof.items())}}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tps, cores, sample = cpu_layer_tokens_per_s(min_seconds=args.cpu_seconds)
+        cpu = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "cyfa_layer_fwd_bwd (BASELINE configs[2])", **CFG,
+                       "global_batch": B * world, "seq_len": T,
+                       "parallelism": f"dp{world} (batch x head sharded, grad all-reduce)",
+                       "l2": "flushed between timed steps (2x126 MiB write outside the events)"},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("cyfa", "reference"), default="cyfa")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    rank, world, local_rank = _rank_env()
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    run_cyfa(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

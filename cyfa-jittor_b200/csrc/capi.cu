@@ -2,7 +2,9 @@
 // map construction and kernel launches.  No entry point allocates memory.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
+#include <vector>
 
 #include "../../include/cyfa.h"
 #include "cyfa_common.cuh"
@@ -29,6 +31,42 @@ static int launch_status() {
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? kOk : -static_cast<int>(e);
 }
+
+// Launch accounting and optional per-kernel timing.  Every kernel launch of the
+// library goes through CYFA_LAUNCH, which counts it and, while profiling is on,
+// brackets it with CUDA events on its own stream.
+static std::atomic<long long> g_launches{0};
+struct ProfRecord {
+  const char* name;
+  cudaEvent_t start, stop;
+};
+static std::mutex g_prof_mu;
+static std::vector<ProfRecord> g_prof;
+static bool g_prof_on = false;
+
+static cudaEvent_t prof_begin(cudaStream_t s) {
+  if (!g_prof_on) return nullptr;
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  cudaEventRecord(e, s);
+  return e;
+}
+static void prof_end(const char* name, cudaEvent_t start, cudaStream_t s) {
+  if (!start) return;
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  cudaEventRecord(e, s);
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  g_prof.push_back({name, start, e});
+}
+
+#define CYFA_LAUNCH(name, stream, ...)                 \
+  do {                                                 \
+    cudaEvent_t _cyfa_ev = prof_begin(stream);         \
+    __VA_ARGS__;                                       \
+    prof_end(name, _cyfa_ev, stream);                  \
+    g_launches.fetch_add(1, std::memory_order_relaxed); \
+  } while (0)
 
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
@@ -105,6 +143,41 @@ const char* cyfa_strerror(int status) {
   return "unknown status";
 }
 
+long long cyfa_launch_count(void) { return g_launches.load(); }
+
+int cyfa_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  for (auto& r : g_prof) {
+    cudaEventDestroy(r.start);
+    cudaEventDestroy(r.stop);
+  }
+  g_prof.clear();
+  g_prof_on = on != 0;
+  return 0;
+}
+
+int cyfa_profile_report(int max, const char** names, float* total_ms, int* counts) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  int n = 0;
+  for (auto& r : g_prof) {
+    if (cudaEventSynchronize(r.stop) != cudaSuccess) return -1;
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, r.start, r.stop);
+    int i = 0;
+    while (i < n && names[i] != r.name) ++i;
+    if (i == n) {
+      if (n == max) continue;
+      names[n] = r.name;
+      total_ms[n] = 0.f;
+      counts[n] = 0;
+      ++n;
+    }
+    total_ms[i] += ms;
+    counts[i] += 1;
+  }
+  return n;
+}
+
 int cyfa_device_error(int reset) {
   int v = 0;
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
@@ -129,7 +202,8 @@ int cyfa_selftest_umma(const void* a, const void* b, float* c, int K, int N, int
   SelftestParams p{K, N, a_mn ? 1 : 0, b_mn ? 1 : 0, c};
   const int smem = (128 + N) * K * 2 + 1024;
   cudaFuncSetAttribute(umma_selftest_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  umma_selftest_kernel<<<1, 128, smem, static_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  CYFA_LAUNCH("umma_selftest", cs, umma_selftest_kernel<<<1, 128, smem, cs>>>(ta, tb, p));
   return launch_status();
 }
 
@@ -151,7 +225,8 @@ int cyfa_decode_step(const void* q, const void* k, const void* v, const float* g
                  clock_in, hk_out, hv_out, clock_out, out, B * H, H, q_eps, k_eps, scale};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid(B * H);
-#define CYFA_DECODE(T, KK, VV) decode_step_kernel<T, KK, VV><<<grid, 256, 0, s>>>(p)
+#define CYFA_DECODE(T, KK, VV) \
+  CYFA_LAUNCH("decode_step", s, (decode_step_kernel<T, KK, VV><<<grid, 256, 0, s>>>(p)))
   if (dtype == 0) {
     if (K == 256 && V == 256) CYFA_DECODE(__nv_bfloat16, 256, 256);
     else if (K == 128 && V == 128) CYFA_DECODE(__nv_bfloat16, 128, 128);
@@ -174,7 +249,8 @@ int cyfa_gates_fwd(const float* g, const float* delta, const float* beta, const 
   CYFA_REQUIRE(B > 0 && T > 0 && H > 0, kBadShape);
   const int TP = (T + 127) / 128 * 128;
   GatesParams p{g, delta, beta, clock0, G, lam, beta_h, clock_out, B, T, H, TP};
-  gates_fwd_kernel<<<B * H, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CYFA_LAUNCH("gates_fwd", st, gates_fwd_kernel<<<B * H, 128, 0, st>>>(p));
   return launch_status();
 }
 
@@ -197,8 +273,8 @@ int cyfa_token_fwd(const void* q, const void* k, const float* q_norm_weight,
   const size_t rows = size_t(B) * H * TP;
   const dim3 grid(unsigned((rows + 7) / 8));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (K == 256) token_fwd_kernel<256><<<grid, 256, 0, s>>>(p);
-  else token_fwd_kernel<128><<<grid, 256, 0, s>>>(p);
+  if (K == 256) CYFA_LAUNCH("token_fwd", s, token_fwd_kernel<256><<<grid, 256, 0, s>>>(p));
+  else CYFA_LAUNCH("token_fwd", s, token_fwd_kernel<128><<<grid, 256, 0, s>>>(p));
   return launch_status();
 }
 
@@ -219,8 +295,8 @@ int cyfa_token_bwd(const void* q, const void* k, const float* q_norm_weight,
   const size_t rows = size_t(B) * H * TP;
   const dim3 grid(unsigned(token_bwd_blocks(rows)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (K == 256) token_bwd_kernel<256><<<grid, 256, 0, s>>>(p);
-  else token_bwd_kernel<128><<<grid, 256, 0, s>>>(p);
+  if (K == 256) CYFA_LAUNCH("token_bwd", s, token_bwd_kernel<256><<<grid, 256, 0, s>>>(p));
+  else CYFA_LAUNCH("token_bwd", s, token_bwd_kernel<128><<<grid, 256, 0, s>>>(p));
   return launch_status();
 }
 
@@ -232,7 +308,8 @@ int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h, con
   const int TP = (T + 127) / 128 * 128;
   GatesBwdParams p{dG, dlam, nullptr, nullptr, nullptr, 0, 0, dbeta_h, dclock, dg, ddelta,
                    dbeta, dclock0, B, T, H, TP};
-  gates_bwd_kernel<<<B * H, 128, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CYFA_LAUNCH("gates_bwd", st, gates_bwd_kernel<<<B * H, 128, 0, st>>>(p));
   return launch_status();
 }
 

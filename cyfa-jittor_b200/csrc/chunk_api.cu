@@ -162,18 +162,21 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
     ScanParams p{d.BH, d.H, d.TP, d.NT, d.K, 128, kRows2D, kRows2D, s.G, a->hk0, s.s1, a->hk,
                  0.f, nullptr, nullptr, nullptr};
     set_smem(state_scan_kernel<false>, kScanSmem);
-    state_scan_kernel<false><<<dim3(d.BH, d.K / 128, 2), 128, kScanSmem, st>>>(m_kn, m_w, p);
+    CYFA_LAUNCH("state_scan_fwd", st,
+                (state_scan_kernel<false><<<dim3(d.BH, d.K / 128, 2), 128, kScanSmem, st>>>(m_kn, m_w, p)));
     if ((rc = launch_status())) return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, 128, kRows2D, 0, s.G, s.lam, a->scale, s.raw,
                     s.weights};
     if (d.K == 256) {
       set_smem(tile_fwd_kernel<256, true>, tile_fwd_smem<256>());
-      tile_fwd_kernel<256, true><<<dim3(d.BH * d.NT, 1), 128, tile_fwd_smem<256>(), st>>>(
-          m_qn, m_kn, m_w, m_s1, m_tab, t);
+      CYFA_LAUNCH("tile_fwd_readout", st,
+                  (tile_fwd_kernel<256, true><<<dim3(d.BH * d.NT, 1), 128, tile_fwd_smem<256>(), st>>>(
+                      m_qn, m_kn, m_w, m_s1, m_tab, t)));
     } else {
       set_smem(tile_fwd_kernel<128, true>, tile_fwd_smem<128>());
-      tile_fwd_kernel<128, true><<<dim3(d.BH * d.NT, 1), 128, tile_fwd_smem<128>(), st>>>(
-          m_qn, m_kn, m_w, m_s1, m_tab, t);
+      CYFA_LAUNCH("tile_fwd_readout", st,
+                  (tile_fwd_kernel<128, true><<<dim3(d.BH * d.NT, 1), 128, tile_fwd_smem<128>(), st>>>(
+                      m_qn, m_kn, m_w, m_s1, m_tab, t)));
     }
     if ((rc = launch_status())) return rc;
   }
@@ -181,13 +184,15 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
   {
     ScanParams p{d.BH, d.H, d.TP, d.NT, 128, d.V, kRows2D, kPublic4D, s.G, a->hv0, s.s2, a->hv,
                  0.f, nullptr, nullptr, nullptr};
-    state_scan_kernel<false><<<dim3(d.BH, 1, d.V / 64), 128, kScanSmem, st>>>(m_w, m_v, p);
+    CYFA_LAUNCH("state_scan_fwd", st,
+                (state_scan_kernel<false><<<dim3(d.BH, 1, d.V / 64), 128, kScanSmem, st>>>(m_w, m_v, p)));
     if ((rc = launch_status())) return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, d.V, kPublic4D, 1, s.G, s.lam, 1.f,
                     static_cast<__nv_bfloat16*>(a->o), nullptr};
     set_smem(tile_fwd_kernel<128, false>, tile_fwd_smem<128>());
-    tile_fwd_kernel<128, false><<<dim3(d.BH * d.NT, d.V / 128), 128, tile_fwd_smem<128>(), st>>>(
-        m_weights, m_w, m_v, m_s2, m_tab, t);
+    CYFA_LAUNCH("tile_fwd", st,
+                (tile_fwd_kernel<128, false><<<dim3(d.BH * d.NT, d.V / 128), 128, tile_fwd_smem<128>(),
+                                               st>>>(m_weights, m_w, m_v, m_s2, m_tab, t)));
     if ((rc = launch_status())) return rc;
   }
   return kOk;
@@ -245,7 +250,7 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   set_smem(dual_gemm_kernel, kDualSmem);
   auto dual = [&](const CUtensorMap& x1, const CUtensorMap& y1, const CUtensorMap& x2,
                   const CUtensorMap& y2, DualParams p) {
-    dual_gemm_kernel<<<tiles, 128, kDualSmem, st>>>(x1, y1, x2, y2, p);
+    CYFA_LAUNCH("dual_gemm", st, (dual_gemm_kernel<<<tiles, 128, kDualSmem, st>>>(x1, y1, x2, y2, p)));
     return launch_status();
   };
   const int nsub1 = (d.K / 128) * 2, nsub2 = d.V / 64;
@@ -254,17 +259,21 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   {
     ScanParams p{d.BH, d.H, d.TP, d.NT, 128, d.V, kRows2D, kPublic4D, s.G, g->dhv, w.h2, g->dhv0,
                  1.f, s.s2, a->hv, w.bpart2};
-    state_scan_kernel<true><<<dim3(d.BH, 1, d.V / 64), 128, kScanSmem, st>>>(m_weights, m_do, p);
+    CYFA_LAUNCH("state_scan_bwd", st,
+                (state_scan_kernel<true><<<dim3(d.BH, 1, d.V / 64), 128, kScanSmem, st>>>(m_weights,
+                                                                                          m_do, p)));
     if ((rc = launch_status())) return rc;
     ScoresParams sp{d.BH, d.H, d.TP, d.NT, kPublic4D, kPublic4D, s.G, 1.f, w.A, w.Bp};
     if (d.V == 256) {
       set_smem(tile_scores_kernel<128, 256>, scores_smem<128, 256>());
-      tile_scores_kernel<128, 256><<<tiles, 128, scores_smem<128, 256>(), st>>>(m_weights, m_w,
-                                                                                 m_do, m_v, sp);
+      CYFA_LAUNCH("tile_scores", st,
+                  (tile_scores_kernel<128, 256><<<tiles, 128, scores_smem<128, 256>(), st>>>(
+                      m_weights, m_w, m_do, m_v, sp)));
     } else {
       set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
-      tile_scores_kernel<128, 128><<<tiles, 128, scores_smem<128, 128>(), st>>>(m_weights, m_w,
-                                                                                 m_do, m_v, sp);
+      CYFA_LAUNCH("tile_scores", st,
+                  (tile_scores_kernel<128, 128><<<tiles, 128, scores_smem<128, 128>(), st>>>(
+                      m_weights, m_w, m_do, m_v, sp)));
     }
     if ((rc = launch_status())) return rc;
     // dweights = B' w + 2^{G_t} dO S^T ;  dG = weights . dweights
@@ -285,26 +294,32 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     ReadoutBwdParams rp{d.BH, d.H, d.TP, d.NT, s.raw, s.weights, w.dweights, s.lam, w.draw,
                         w.dlam_r, w.dtab_part};
     set_smem(readout_bwd_kernel, kReadoutBwdSmem);
-    readout_bwd_kernel<<<tiles, 128, kReadoutBwdSmem, st>>>(m_tab, rp);
+    CYFA_LAUNCH("readout_bwd", st, (readout_bwd_kernel<<<tiles, 128, kReadoutBwdSmem, st>>>(m_tab, rp)));
     if ((rc = launch_status())) return rc;
-    dtable_reduce_kernel<<<dim3(d.H, 128), 128, 0, st>>>(w.dtab_part, g->dtable, d.B, d.H, d.NT);
+    CYFA_LAUNCH("dtable_reduce", st,
+                (dtable_reduce_kernel<<<dim3(d.H, 128), 128, 0, st>>>(w.dtab_part, g->dtable, d.B,
+                                                                      d.H, d.NT)));
     if ((rc = launch_status())) return rc;
   }
   // ================= pass 1 (queries = q^, keys = k^, values = w)
   {
     ScanParams p{d.BH, d.H, d.TP, d.NT, d.K, 128, kRows2D, kRows2D, s.G, g->dhk, w.h1, g->dhk0,
                  a->scale, s.s1, a->hk, w.bpart1};
-    state_scan_kernel<true><<<dim3(d.BH, d.K / 128, 2), 128, kScanSmem, st>>>(m_qn, m_draw, p);
+    CYFA_LAUNCH("state_scan_bwd", st,
+                (state_scan_kernel<true><<<dim3(d.BH, d.K / 128, 2), 128, kScanSmem, st>>>(m_qn, m_draw,
+                                                                                           p)));
     if ((rc = launch_status())) return rc;
     ScoresParams sp{d.BH, d.H, d.TP, d.NT, kRows2D, kRows2D, s.G, a->scale, w.A, w.Bp};
     if (d.K == 256) {
       set_smem(tile_scores_kernel<256, 128>, scores_smem<256, 128>());
-      tile_scores_kernel<256, 128><<<tiles, 128, scores_smem<256, 128>(), st>>>(m_qn, m_kn,
-                                                                                 m_draw, m_w, sp);
+      CYFA_LAUNCH("tile_scores", st,
+                  (tile_scores_kernel<256, 128><<<tiles, 128, scores_smem<256, 128>(), st>>>(
+                      m_qn, m_kn, m_draw, m_w, sp)));
     } else {
       set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
-      tile_scores_kernel<128, 128><<<tiles, 128, scores_smem<128, 128>(), st>>>(m_qn, m_kn,
-                                                                                 m_draw, m_w, sp);
+      CYFA_LAUNCH("tile_scores", st,
+                  (tile_scores_kernel<128, 128><<<tiles, 128, scores_smem<128, 128>(), st>>>(
+                      m_qn, m_kn, m_draw, m_w, sp)));
     }
     if ((rc = launch_status())) return rc;
     // dq^ = B' k^ + scale 2^{G_t} draw S^T ;  dG += q^ . dq^
@@ -326,12 +341,16 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                       w.dlam_w, w.dbeta_h, d.B, d.T, d.H, d.K, stream);
   if (rc) return rc;
   const int nblk = token_bwd_blocks(rows);
-  column_sum_kernel<<<(d.K + 31) / 32, 256, 0, st>>>(w.dqw_part, g->dq_norm_weight, nblk, d.K);
-  column_sum_kernel<<<(d.K + 31) / 32, 256, 0, st>>>(w.dkw_part, g->dk_norm_weight, nblk, d.K);
+  CYFA_LAUNCH("column_sum", st,
+              (column_sum_kernel<<<(d.K + 31) / 32, 256, 0, st>>>(w.dqw_part, g->dq_norm_weight, nblk,
+                                                                   d.K)));
+  CYFA_LAUNCH("column_sum", st,
+              (column_sum_kernel<<<(d.K + 31) / 32, 256, 0, st>>>(w.dkw_part, g->dk_norm_weight, nblk,
+                                                                   d.K)));
   if ((rc = launch_status())) return rc;
   GatesBwdParams gp{w.dG, w.dlam_w, w.dlam_r, w.bpart1, w.bpart2, nsub1, nsub2, w.dbeta_h,
                     g->dclock, g->dg, g->ddelta, g->dbeta, g->dclock0, d.B, d.T, d.H, d.TP};
-  gates_bwd_kernel<<<d.BH, 128, 0, st>>>(gp);
+  CYFA_LAUNCH("gates_bwd", st, (gates_bwd_kernel<<<d.BH, 128, 0, st>>>(gp)));
   return launch_status();
 }
 

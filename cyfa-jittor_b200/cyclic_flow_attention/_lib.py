@@ -67,6 +67,14 @@ def lib():
                 continue
             fn.argtypes = args
             fn.restype = ctypes.c_size_t
+        handle.cyfa_launch_count.argtypes = []
+        handle.cyfa_launch_count.restype = ctypes.c_longlong
+        handle.cyfa_profile_enable.argtypes = [ctypes.c_int]
+        handle.cyfa_profile_enable.restype = ctypes.c_int
+        handle.cyfa_profile_report.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
+                                               ctypes.POINTER(ctypes.c_float),
+                                               ctypes.POINTER(ctypes.c_int)]
+        handle.cyfa_profile_report.restype = ctypes.c_int
         handle.cyfa_strerror.argtypes = [ctypes.c_int]
         handle.cyfa_strerror.restype = ctypes.c_char_p
         _lib = handle
@@ -106,3 +114,24 @@ def require_cuda(*tensors):
 def device_error(reset=True):
     """Returns the device error word (1 = a bounded wait timed out)."""
     return lib().cyfa_device_error(1 if reset else 0)
+
+
+def launch_count():
+    """Kernels libcyfa has launched in this process."""
+    return lib().cyfa_launch_count()
+
+
+def profile_enable(on=True):
+    """Per-kernel CUDA-event timing on/off (clears earlier records)."""
+    lib().cyfa_profile_enable(1 if on else 0)
+
+
+def profile_report(max_names=64):
+    """{kernel name: (total ms, launches)} since profile_enable(True)."""
+    names = (ctypes.c_char_p * max_names)()
+    ms = (ctypes.c_float * max_names)()
+    counts = (ctypes.c_int * max_names)()
+    n = lib().cyfa_profile_report(max_names, names, ms, counts)
+    if n < 0:
+        raise CyfaError("cyfa_profile_report failed")
+    return {names[i].decode(): (ms[i], counts[i]) for i in range(n)}

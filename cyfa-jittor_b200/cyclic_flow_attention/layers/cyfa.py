@@ -1,0 +1,178 @@
+"""Cyclic Flow Attention layer (PyTorch host, B200 kernels underneath).
+
+Mirror of the reference layer (cyclic_flow_attention/layers/cyfa.py:236-357):
+identical parameter names, shapes and default initialisation, so checkpoints
+saved by the reference (PyTorch-compatible safetensors) load with
+``load_state_dict``.  The projections, short convolutions and the gated output
+norm are library ops (cuBLAS / cuDNN via torch); the attention core is
+``chunk_cyfa`` (training and prefill) or ``fused_recurrent_cyfa`` (T == 1
+decode), both in libcyfa.so.
+"""
+
+import math
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from ..ops import chunk_cyfa, fused_recurrent_cyfa
+
+
+class RMSNorm(nn.Module):
+    """RMSNorm with an optional sigmoid gate, computed in fp32 and cast back
+    (reference layers/cyfa.py:62-84)."""
+
+    def __init__(self, dim, eps):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.eps = eps
+
+    def forward(self, x, gate=None):
+        xf = x.float()
+        y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight.float()
+        if gate is not None:
+            y = y * torch.sigmoid(gate.float())
+        return y.to(x.dtype)
+
+
+class ShortConvolution(nn.Module):
+    """Causal depthwise convolution without activation, with a decode cache
+    (reference layers/cyfa.py:138-181).  weight [dim, 1, width]."""
+
+    def __init__(self, dim, width, bias=False):
+        super().__init__()
+        self.width = width
+        self.weight = nn.Parameter(torch.randn(dim, 1, width) * 0.02)
+        self.bias = nn.Parameter(torch.zeros(dim)) if bias else None
+
+    def forward(self, x, cache=None, lengths=None):
+        B, T, D = x.shape
+        history = x if cache is None else torch.cat([cache.to(x.dtype), x], dim=1)
+        offset = self.width - 1 if cache is None else 0
+        h = F.pad(history.transpose(1, 2), (offset, 0))
+        y = F.conv1d(h.float(), self.weight.float(), None if self.bias is None else self.bias.float(),
+                     groups=D)
+        y = y[..., y.shape[-1] - T:].transpose(1, 2)
+        if self.width == 1:
+            new_cache = history[:, :0]
+        elif lengths is None and history.shape[1] >= self.width - 1:
+            new_cache = history[:, -(self.width - 1):]
+        else:
+            ends = torch.full((B,), T, dtype=torch.long, device=x.device) if lengths is None \
+                else lengths.long()
+            positions = ends.unsqueeze(1) - offset + torch.arange(self.width - 1, device=x.device)
+            idx = positions.clamp_min(0)
+            new_cache = history[torch.arange(B, device=x.device).unsqueeze(1), idx]
+            new_cache = torch.where((positions >= 0).unsqueeze(-1), new_cache,
+                                    torch.zeros((), dtype=new_cache.dtype, device=x.device))
+        return y.to(x.dtype), new_cache
+
+
+class CyclicFlowAttention(nn.Module):
+    """CyFA attention with projections, short convolutions and a gated readout.
+
+    forward returns (hidden_states, cache).  The cache contains recurrent
+    states and the short-convolution histories when use_cache is enabled.
+    """
+
+    def __init__(
+        self,
+        hidden_size=1024,
+        num_heads=4,
+        head_dim=256,
+        expand_k=1.0,
+        expand_v=1.0,
+        num_slots=128,
+        use_short_conv=True,
+        conv_size=4,
+        conv_bias=False,
+        norm_eps=1e-6,
+        chunk_size=64,
+        **kwargs,
+    ):
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_k_dim = int(head_dim * expand_k)
+        self.head_v_dim = int(head_dim * expand_v)
+        self.key_dim = num_heads * self.head_k_dim
+        self.value_dim = num_heads * self.head_v_dim
+        self.num_slots, self.chunk_size = num_slots, chunk_size
+        self.q_proj = nn.Linear(hidden_size, self.key_dim, bias=False)
+        self.k_proj = nn.Linear(hidden_size, self.key_dim, bias=False)
+        self.v_proj = nn.Linear(hidden_size, self.value_dim, bias=False)
+        self.a_proj = nn.Linear(hidden_size, num_heads, bias=False)
+        self.b_proj = nn.Linear(hidden_size, num_heads, bias=True)
+        self.d_proj = nn.Linear(hidden_size, num_heads, bias=True)
+        # dt_bias / A_log / readout as the reference initialises them (:274-284)
+        dt = (torch.rand(num_heads) * (math.log(0.1) - math.log(0.001)) + math.log(0.001)).exp()
+        self.dt_bias = nn.Parameter(dt + torch.log(1.0 - torch.exp(-dt)))
+        self.A_log = nn.Parameter(torch.log(torch.rand(num_heads) * 16.0 + 1e-3))
+        self.readout = nn.Parameter(
+            torch.eye(num_slots - 1).expand(num_heads, -1, -1).clone())
+        self.q_norm = RMSNorm(self.head_k_dim, norm_eps)
+        self.k_norm = RMSNorm(self.head_k_dim, norm_eps)
+        self.use_short_conv = use_short_conv
+        if use_short_conv:
+            self.q_conv1d = ShortConvolution(self.key_dim, conv_size, conv_bias)
+            self.k_conv1d = ShortConvolution(self.key_dim, conv_size, conv_bias)
+            self.v_conv1d = ShortConvolution(self.value_dim, conv_size, conv_bias)
+        self.g_proj = nn.Sequential(
+            nn.Linear(hidden_size, self.head_v_dim, bias=False),
+            nn.Linear(self.head_v_dim, self.value_dim, bias=True),
+        )
+        self.o_norm = RMSNorm(self.head_v_dim, norm_eps)
+        self.o_proj = nn.Linear(self.value_dim, hidden_size, bias=False)
+
+    def keep_fp32(self):
+        """Casts to bf16 except the parameters the reference keeps in fp32
+        (norm weights, readout, A_log, dt_bias; models/cyfa/modeling_cyfa.py:110-116)."""
+        for name, p in self.named_parameters():
+            keep = name.endswith("norm.weight") or name in ("readout", "A_log", "dt_bias")
+            p.data = p.data.float() if keep else p.data.bfloat16()
+        return self
+
+    def forward(self, x, cache=None, use_cache=False, attention_mask=None):
+        B, T, _ = x.shape
+        H = self.num_heads
+        q, k, v = self.q_proj(x), self.k_proj(x), self.v_proj(x)
+        lengths = None
+        if attention_mask is not None:
+            # right padding is neutral for the recurrence and the convolution
+            mask = attention_mask.unsqueeze(-1)
+            q, k, v = (t * mask.to(t.dtype) for t in (q, k, v))
+            lengths = attention_mask.long().sum(1)
+        conv_cache = (None, None, None) if cache is None else cache.get("conv_state",
+                                                                       (None, None, None))
+        if self.use_short_conv:
+            q, cq = self.q_conv1d(q, conv_cache[0], lengths)
+            k, ck = self.k_conv1d(k, conv_cache[1], lengths)
+            v, cv = self.v_conv1d(v, conv_cache[2], lengths)
+        else:
+            cq = ck = cv = None
+        q = q.reshape(B, T, H, self.head_k_dim)
+        k = k.reshape(B, T, H, self.head_k_dim)
+        v = v.reshape(B, T, H, self.head_v_dim)
+        a = self.a_proj(x).float() + self.dt_bias.float()
+        g = -self.A_log.float().exp() * F.softplus(a)
+        delta = torch.sigmoid(self.d_proj(x.detach()).float())
+        beta = torch.sigmoid(self.b_proj(x).float())
+        if attention_mask is not None:
+            valid = attention_mask.unsqueeze(-1).bool()
+            zero = torch.zeros((), device=x.device)
+            g, delta, beta = (torch.where(valid, t, zero) for t in (g, delta, beta))
+        kwargs = dict(
+            q=q, k=k, v=v, g=g, delta=delta, beta=beta, readout=self.readout,
+            q_norm_weight=self.q_norm.weight.float(), k_norm_weight=self.k_norm.weight.float(),
+            q_norm_eps=self.q_norm.eps, k_norm_eps=self.k_norm.eps,
+            initial_state=None if cache is None else cache["recurrent_state"],
+            output_final_state=use_cache,
+        )
+        if not self.training and T == 1 and not torch.is_grad_enabled():
+            o, state = fused_recurrent_cyfa(**kwargs)
+        else:
+            o, state = chunk_cyfa(**kwargs, chunk_size=self.chunk_size)
+        gate = self.g_proj(x).reshape(B, T, H, self.head_v_dim)
+        o = self.o_norm(o * (self.num_slots - 1), gate).reshape(B, T, self.value_dim)
+        o = self.o_proj(o)
+        new_cache = {"recurrent_state": state, "conv_state": (cq, ck, cv)} if use_cache else None
+        return o, new_cache

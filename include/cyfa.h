@@ -44,6 +44,18 @@ const char* cyfa_strerror(int status);
  * Synchronises the device. */
 int cyfa_device_error(int reset);
 
+/* Number of kernels this library has launched in the process (all entry points). */
+long long cyfa_launch_count(void);
+
+/* Turns per-kernel timing on (1) or off (0) and clears earlier records.  While
+ * on, every launch is bracketed by CUDA events on its own stream. */
+int cyfa_profile_enable(int on);
+
+/* Aggregates the timing records per kernel name: fills up to `max` entries of
+ * names / total_ms / counts and returns the number filled (synchronises on the
+ * recorded events). */
+int cyfa_profile_report(int max, const char** names, float* total_ms, int* counts);
+
 /* ---------------------------------------------------------------- decode
  * One constant-memory decode step (T = 1).
  * Replaces: fused_recurrent_cyfa, cyclic_flow_attention/ops/fused_recurrent.py:10-200

@@ -144,6 +144,7 @@ def test_chunk_backward(ops, B, T, H, K, V, with_state):
             errs[n] = rel_l2(a.grad, b.grad)
         tols += [BF16_TOL, BF16_TOL, GATE_TOL]
         names += ["hk0", "hv0", "clock0"]
+    print("chunk grad errors", B, T, H, K, V, with_state, {k: round(v, 5) for k, v in errs.items()})
     bad = {n: e for n, t, (n2, e) in zip(names, tols, errs.items()) if e >= t}
     assert not bad, f"gradient errors over tolerance: {bad} (all: {errs})"
     from cyclic_flow_attention import _lib

@@ -1,0 +1,85 @@
+"""GPU checks of the CyclicFlowAttention layer: parity with the oracle layer
+(forward and backward), and the reference's own hot-path test
+(tests/test_inference.py:20-34 of the reference): decoding the next token from
+a prefill cache matches the full-sequence forward (rel-RMS < 0.02 there; the
+bf16 tolerance 1e-2 is used here)."""
+
+import pytest
+import torch
+
+from gpu_util import rel_l2
+from oracle import cyfa_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def Layer():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+    from cyclic_flow_attention import CyclicFlowAttention
+
+    return CyclicFlowAttention
+
+
+def _layer(Layer, hidden, H, hd, seed):
+    torch.manual_seed(seed)
+    m = Layer(hidden, H, hd)
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            if p.dim() >= 2 and name != "readout":
+                p.normal_(0, 0.02)
+        m.readout.add_(0.05 * torch.randn_like(m.readout))
+    return m.keep_fp32().cuda()
+
+
+@pytest.mark.parametrize("B,T,hidden,H,hd", [(2, 256, 512, 2, 256), (1, 200, 256, 2, 128)])
+def test_layer_forward_backward(Layer, B, T, hidden, H, hd):
+    m = _layer(Layer, hidden, H, hd, seed=T)
+    gen = torch.Generator().manual_seed(1)
+    x = torch.randn(B, T, hidden, generator=gen).to(torch.bfloat16)
+    dy = torch.randn(B, T, hidden, generator=gen)
+    xg = x.cuda().requires_grad_(True)
+    y, _ = m(xg)
+    (y.float() * dy.cuda()).sum().backward()
+    params = {n: p.detach().float().cpu().clone().requires_grad_(True)
+              for n, p in m.named_parameters()}
+    xr = x.float().requires_grad_(True)
+    yr = O.cyfa_layer(params, xr, H, hd, hd)
+    (yr * dy).sum().backward()
+    errs = {"y": rel_l2(y, yr), "x": rel_l2(xg.grad, xr.grad)}
+    errs.update({n: rel_l2(p.grad, params[n].grad) for n, p in m.named_parameters()})
+    print("layer errors", B, T, hidden, H, hd, {k: round(v, 5) for k, v in errs.items()})
+    # Tolerances by conditioning.  Output: 1e-2.  Gradients through two bf16 GEMM
+    # layers: 2e-2.  Gate/clock parameters are token sums of cancelling gate
+    # gradients; test_oracle_gate_param_conditioning shows that one bf16 rounding of
+    # the oracle's own inputs already moves them by 1-3 %, so the per-head scalars
+    # (A_log, dt_bias, d_proj.bias, b_proj.bias) get 1e-1 and the gate projection
+    # matrices (a_proj, d_proj) 5e-2.
+    loose = {"A_log": 1e-1, "dt_bias": 1e-1, "d_proj.bias": 1e-1, "b_proj.bias": 1e-1,
+             "d_proj.weight": 5e-2, "a_proj.weight": 5e-2}
+    for n, e in errs.items():
+        tol = 1e-2 if n == "y" else loose.get(n, 2e-2)
+        assert e < tol, (n, e)
+
+
+def test_layer_decode_matches_prefill(Layer):
+    B, T, hidden, H, hd = 2, 65, 512, 2, 256
+    m = _layer(Layer, hidden, H, hd, seed=4).eval()
+    x = torch.randn(B, T, hidden, generator=torch.Generator().manual_seed(2)).to(
+        torch.bfloat16).cuda()
+    with torch.no_grad():
+        full, _ = m(x)
+        _, cache = m(x[:, :64], use_cache=True)
+        y1, cache = m(x[:, 64:65], cache=cache, use_cache=True)
+    assert rel_l2(y1[:, 0], full[:, 64]) < 1e-2
+
+
+def test_layer_state_dict_roundtrip(Layer, tmp_path):
+    m = _layer(Layer, 256, 1, 256, seed=5)
+    path = tmp_path / "layer.pt"
+    torch.save(m.state_dict(), path)
+    m2 = _layer(Layer, 256, 1, 256, seed=6)
+    m2.load_state_dict(torch.load(path))
+    for (n, a), (_, b) in zip(m.state_dict().items(), m2.state_dict().items()):
+        assert torch.equal(a, b), n
