@@ -240,10 +240,11 @@ def run_cyfa(args, rank, world, local_rank):
                 off += n
 
     def step(xin, dyin):
+        # training step with the objective loss = <y, dy>: dL/dy = dy
         for p in params:
             p.grad = None
         y, _ = layer(xin)
-        loss = (y.float() * dyin.float()).sum()
+        loss = torch.dot(y.reshape(-1), dyin.reshape(-1))
         loss.backward()
         allreduce_grads()
         return loss

@@ -123,6 +123,61 @@ static int tmap_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t col
 
 using namespace cyfa;
 
+namespace cyfa {
+static int token_fwd_launch(const void* q, const void* k, const float* q_norm_weight,
+                            const float* k_norm_weight, const float* lam, const float* beta_h,
+                            void* qn, void* kn, void* w, float* q_rs, float* k_rs, int B, int T,
+                            int H, int K, float q_eps, float k_eps, long long q_stride,
+                            long long k_stride, void* stream) {
+  CYFA_REQUIRE(q && k && q_norm_weight && k_norm_weight && lam && beta_h && qn && kn && w &&
+                   q_rs && k_rs,
+               kNullPointer);
+  CYFA_REQUIRE(B > 0 && T > 0 && H > 0 && (K == 128 || K == 256), kBadShape);
+  CYFA_REQUIRE(aligned(q, 16) && aligned(k, 16) && q_stride % 8 == 0 && k_stride % 8 == 0 && aligned(qn, 16) && aligned(kn, 16) &&
+                   aligned(w, 16),
+               kMisaligned);
+  const int TP = (T + 127) / 128 * 128;
+  TokenFwdParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                   q_norm_weight, k_norm_weight, lam, beta_h,
+                   static_cast<__nv_bfloat16*>(qn), static_cast<__nv_bfloat16*>(kn),
+                   static_cast<__nv_bfloat16*>(w), q_rs, k_rs, B, T, H, TP, q_eps, k_eps,
+                   q_stride, k_stride};
+  const size_t rows = size_t(B) * H * TP;
+  const dim3 grid(unsigned((rows + 7) / 8));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 256) CYFA_LAUNCH("token_fwd", s, token_fwd_kernel<256><<<grid, 256, 0, s>>>(p));
+  else CYFA_LAUNCH("token_fwd", s, token_fwd_kernel<128><<<grid, 256, 0, s>>>(p));
+  return launch_status();
+}
+
+static int token_bwd_launch(const void* q, const void* k, const float* q_norm_weight,
+                            const float* k_norm_weight, const float* q_rs, const float* k_rs,
+                            const float* dqn, const float* dkn, const float* lam,
+                            const float* beta_h, const float* dw, const float* dw_b, void* dq,
+                            void* dk, float* dqw_part, float* dkw_part, float* dlam,
+                            float* dbeta_h, int B,
+                            int T, int H, int K, long long q_stride, long long k_stride,
+                            long long dq_stride, long long dk_stride, void* stream) {
+  CYFA_REQUIRE(q && k && q_norm_weight && k_norm_weight && q_rs && k_rs && dqn && dkn && lam &&
+                   beta_h && dw && dq && dk && dqw_part && dkw_part && dlam && dbeta_h,
+               kNullPointer);
+  CYFA_REQUIRE(B > 0 && T > 0 && H > 0 && (K == 128 || K == 256), kBadShape);
+  const int TP = (T + 127) / 128 * 128;
+  TokenBwdParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+                   q_norm_weight, k_norm_weight, q_rs, k_rs, dqn, dkn, lam, beta_h, dw, dw_b,
+                   static_cast<__nv_bfloat16*>(dq), static_cast<__nv_bfloat16*>(dk), dqw_part,
+                   dkw_part, dlam, dbeta_h, B, T, H, TP, q_stride, k_stride, dq_stride,
+                   dk_stride};
+  const size_t rows = size_t(B) * H * TP;
+  const dim3 grid(unsigned(token_bwd_blocks(rows)));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 256) CYFA_LAUNCH("token_bwd", s, token_bwd_kernel<256><<<grid, 256, 0, s>>>(p));
+  else CYFA_LAUNCH("token_bwd", s, token_bwd_kernel<128><<<grid, 256, 0, s>>>(p));
+  return launch_status();
+}
+
+}  // namespace cyfa
+
 extern "C" {
 
 int cyfa_version(void) { return 1; }
@@ -250,7 +305,7 @@ int cyfa_gates_fwd(const float* g, const float* delta, const float* beta, const 
   const int TP = (T + 127) / 128 * 128;
   GatesParams p{g, delta, beta, clock0, G, lam, beta_h, clock_out, B, T, H, TP};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  CYFA_LAUNCH("gates_fwd", st, gates_fwd_kernel<<<B * H, 128, 0, st>>>(p));
+  CYFA_LAUNCH("gates_fwd", st, gates_fwd_kernel<<<B * H, 1024, 0, st>>>(p));
   return launch_status();
 }
 
@@ -258,24 +313,8 @@ int cyfa_token_fwd(const void* q, const void* k, const float* q_norm_weight,
                    const float* k_norm_weight, const float* lam, const float* beta_h, void* qn,
                    void* kn, void* w, float* q_rs, float* k_rs, int B, int T, int H, int K,
                    float q_eps, float k_eps, void* stream) {
-  CYFA_REQUIRE(q && k && q_norm_weight && k_norm_weight && lam && beta_h && qn && kn && w &&
-                   q_rs && k_rs,
-               kNullPointer);
-  CYFA_REQUIRE(B > 0 && T > 0 && H > 0 && (K == 128 || K == 256), kBadShape);
-  CYFA_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(qn, 16) && aligned(kn, 16) &&
-                   aligned(w, 16),
-               kMisaligned);
-  const int TP = (T + 127) / 128 * 128;
-  TokenFwdParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-                   q_norm_weight, k_norm_weight, lam, beta_h,
-                   static_cast<__nv_bfloat16*>(qn), static_cast<__nv_bfloat16*>(kn),
-                   static_cast<__nv_bfloat16*>(w), q_rs, k_rs, B, T, H, TP, q_eps, k_eps};
-  const size_t rows = size_t(B) * H * TP;
-  const dim3 grid(unsigned((rows + 7) / 8));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (K == 256) CYFA_LAUNCH("token_fwd", s, token_fwd_kernel<256><<<grid, 256, 0, s>>>(p));
-  else CYFA_LAUNCH("token_fwd", s, token_fwd_kernel<128><<<grid, 256, 0, s>>>(p));
-  return launch_status();
+  return token_fwd_launch(q, k, q_norm_weight, k_norm_weight, lam, beta_h, qn, kn, w, q_rs, k_rs,
+                          B, T, H, K, q_eps, k_eps, (long long)H * K, (long long)H * K, stream);
 }
 
 int cyfa_token_bwd(const void* q, const void* k, const float* q_norm_weight,
@@ -283,21 +322,10 @@ int cyfa_token_bwd(const void* q, const void* k, const float* q_norm_weight,
                    const float* dqn, const float* dkn, const float* lam, const float* beta_h,
                    const float* dw, void* dq, void* dk, float* dqw_part, float* dkw_part,
                    float* dlam, float* dbeta_h, int B, int T, int H, int K, void* stream) {
-  CYFA_REQUIRE(q && k && q_norm_weight && k_norm_weight && q_rs && k_rs && dqn && dkn && lam &&
-                   beta_h && dw && dq && dk && dqw_part && dkw_part && dlam && dbeta_h,
-               kNullPointer);
-  CYFA_REQUIRE(B > 0 && T > 0 && H > 0 && (K == 128 || K == 256), kBadShape);
-  const int TP = (T + 127) / 128 * 128;
-  TokenBwdParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-                   q_norm_weight, k_norm_weight, q_rs, k_rs, dqn, dkn, lam, beta_h, dw,
-                   static_cast<__nv_bfloat16*>(dq), static_cast<__nv_bfloat16*>(dk), dqw_part,
-                   dkw_part, dlam, dbeta_h, B, T, H, TP};
-  const size_t rows = size_t(B) * H * TP;
-  const dim3 grid(unsigned(token_bwd_blocks(rows)));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (K == 256) CYFA_LAUNCH("token_bwd", s, token_bwd_kernel<256><<<grid, 256, 0, s>>>(p));
-  else CYFA_LAUNCH("token_bwd", s, token_bwd_kernel<128><<<grid, 256, 0, s>>>(p));
-  return launch_status();
+  const long long d = (long long)H * K;
+  return token_bwd_launch(q, k, q_norm_weight, k_norm_weight, q_rs, k_rs, dqn, dkn, lam, beta_h,
+                          dw, nullptr, dq, dk, dqw_part, dkw_part, dlam, dbeta_h, B, T, H, K, d, d, d, d,
+                          stream);
 }
 
 int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h, const float* dclock,
@@ -309,7 +337,7 @@ int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h, con
   GatesBwdParams p{dG, dlam, nullptr, nullptr, nullptr, 0, 0, dbeta_h, dclock, dg, ddelta,
                    dbeta, dclock0, B, T, H, TP};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  CYFA_LAUNCH("gates_bwd", st, gates_bwd_kernel<<<B * H, 128, 0, st>>>(p));
+  CYFA_LAUNCH("gates_bwd", st, gates_bwd_kernel<<<B * H, 1024, 0, st>>>(p));
   return launch_status();
 }
 

@@ -59,7 +59,7 @@ static Saved carve_saved(const Dims& d, void* base, size_t* total) {
 // Scratch of the backward pass.
 struct Work {
   __nv_bfloat16 *h1, *h2, *A, *Bp, *draw;
-  float *dweights, *dw, *dq1, *dk1, *dG, *dlam_r, *dlam_w, *dbeta_h, *bpart1, *bpart2, *dtab_part,
+  float *dweights, *dw, *dw_b, *dq1, *dk1, *dG, *dlam_r, *dlam_w, *dbeta_h, *bpart1, *bpart2, *dtab_part,
       *dqw_part, *dkw_part;
 };
 
@@ -74,6 +74,7 @@ static Work carve_work(const Dims& d, void* base, size_t* total) {
   w.draw = c.take<__nv_bfloat16>(n * 128);
   w.dweights = c.take<float>(n * 128);
   w.dw = c.take<float>(n * 128);
+  w.dw_b = c.take<float>(n * 128);
   w.dq1 = c.take<float>(n * d.K);
   w.dk1 = c.take<float>(n * d.K);
   w.dG = c.take<float>(n);
@@ -89,10 +90,13 @@ static Work carve_work(const Dims& d, void* base, size_t* total) {
   return w;
 }
 
-// [B,T,H,D] bf16 as the 4-D map {D, H, T, B} with a {64, 1, 128, 1} box.
-static int tmap_public(CUtensorMap* m, const void* base, int B, int T, int H, int D) {
+// [B,T,H,D] bf16 whose tokens are `stride` elements apart (stride >= H*D) as the
+// 4-D map {D, H, T, B} with a {64, 1, 128, 1} box.
+static int tmap_public(CUtensorMap* m, const void* base, int B, int T, int H, int D,
+                       long long stride) {
   const uint64_t dims[4] = {uint64_t(D), uint64_t(H), uint64_t(T), uint64_t(B)};
-  const uint64_t strides[3] = {uint64_t(D) * 2, uint64_t(H) * D * 2, uint64_t(T) * H * D * 2};
+  const uint64_t strides[3] = {uint64_t(D) * 2, uint64_t(stride) * 2,
+                               uint64_t(T) * uint64_t(stride) * 2};
   const uint32_t box[4] = {64, 1, 128, 1};
   return make_tmap_bf16(m, base, 4, dims, strides, box);
 }
@@ -101,6 +105,13 @@ static bool shape_ok(int B, int T, int H, int K, int V) {
   return B > 0 && T > 0 && H > 0 && (K == 128 || K == 256) && (V == 128 || V == 256) &&
          size_t(B) * H * ((T + 127) / 128 * 128) < (size_t(1) << 31);
 }
+
+// Token strides must be 0 (dense) or at least the row width and a multiple of 8
+// elements (16 bytes, the TMA stride rule).
+static bool strides_ok(long long s, long long dense) { return s == 0 || (s >= dense && s % 8 == 0); }
+
+// A token stride of 0 means the dense layout.
+static long long stride_or(long long s, long long dense) { return s > 0 ? s : dense; }
 
 template <typename Kern>
 static void set_smem(Kern k, int bytes) {
@@ -135,6 +146,9 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
                    aligned(a->hk, 16) && aligned(a->hv, 16) && aligned(a->table_bf, 16) &&
                    (!a->hk0 || aligned(a->hk0, 16)) && (!a->hv0 || aligned(a->hv0, 16)),
                kMisaligned);
+  CYFA_REQUIRE(strides_ok(a->q_stride, d.H * d.K) && strides_ok(a->k_stride, d.H * d.K) &&
+                   strides_ok(a->v_stride, d.H * d.V),
+               kBadShape);
   const Saved s = carve_saved(d, saved, nullptr);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc;
@@ -142,8 +156,10 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
   rc = cyfa_gates_fwd(a->g, a->delta, a->beta, a->clock0, s.G, s.lam, s.beta_h, a->clock, d.B,
                       d.T, d.H, stream);
   if (rc) return rc;
-  rc = cyfa_token_fwd(a->q, a->k, a->q_norm_weight, a->k_norm_weight, s.lam, s.beta_h, s.qn, s.kn,
-                      s.w, s.q_rs, s.k_rs, d.B, d.T, d.H, d.K, a->q_eps, a->k_eps, stream);
+  rc = token_fwd_launch(a->q, a->k, a->q_norm_weight, a->k_norm_weight, s.lam, s.beta_h, s.qn,
+                        s.kn, s.w, s.q_rs, s.k_rs, d.B, d.T, d.H, d.K, a->q_eps, a->k_eps,
+                        stride_or(a->q_stride, d.H * d.K), stride_or(a->k_stride, d.H * d.K),
+                        stream);
   if (rc) return rc;
 
   const uint64_t rows = uint64_t(d.BH) * d.TP;
@@ -152,7 +168,8 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
   if ((rc = tmap_2d(&m_kn, s.kn, rows, d.K, 128))) return rc;
   if ((rc = tmap_2d(&m_w, s.w, rows, 128, 128))) return rc;
   if ((rc = tmap_2d(&m_weights, s.weights, rows, 128, 128))) return rc;
-  if ((rc = tmap_public(&m_v, a->v, d.B, d.T, d.H, d.V))) return rc;
+  if ((rc = tmap_public(&m_v, a->v, d.B, d.T, d.H, d.V, stride_or(a->v_stride, d.H * d.V))))
+    return rc;
   if ((rc = tmap_2d(&m_s1, s.s1, uint64_t(d.BH) * d.NT * d.K, 128, d.K))) return rc;
   if ((rc = tmap_2d(&m_s2, s.s2, uint64_t(d.BH) * d.NT * 128, d.V, 128))) return rc;
   if ((rc = tmap_2d(&m_tab, a->table_bf, uint64_t(d.H) * 128, 128, 128))) return rc;
@@ -224,6 +241,10 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                    (!g->dhk || aligned(g->dhk, 16)) && (!g->dhv || aligned(g->dhv, 16)) &&
                    (!g->dhk0 || aligned(g->dhk0, 16)) && (!g->dhv0 || aligned(g->dhv0, 16)),
                kMisaligned);
+  CYFA_REQUIRE(strides_ok(a->q_stride, d.H * d.K) && strides_ok(a->k_stride, d.H * d.K) &&
+                   strides_ok(a->v_stride, d.H * d.V) && strides_ok(g->dq_stride, d.H * d.K) &&
+                   strides_ok(g->dk_stride, d.H * d.K) && strides_ok(g->dv_stride, d.H * d.V),
+               kBadShape);
   const Saved s = carve_saved(d, const_cast<void*>(saved), nullptr);
   const Work w = carve_work(d, work, nullptr);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -236,8 +257,9 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   if ((rc = tmap_2d(&m_w, s.w, rows, 128, 128))) return rc;
   if ((rc = tmap_2d(&m_weights, s.weights, rows, 128, 128))) return rc;
   if ((rc = tmap_2d(&m_draw, w.draw, rows, 128, 128))) return rc;
-  if ((rc = tmap_public(&m_v, a->v, d.B, d.T, d.H, d.V))) return rc;
-  if ((rc = tmap_public(&m_do, g->d_o, d.B, d.T, d.H, d.V))) return rc;
+  if ((rc = tmap_public(&m_v, a->v, d.B, d.T, d.H, d.V, stride_or(a->v_stride, d.H * d.V))))
+    return rc;
+  if ((rc = tmap_public(&m_do, g->d_o, d.B, d.T, d.H, d.V, (long long)d.H * d.V))) return rc;
   if ((rc = tmap_2d(&m_s1, s.s1, uint64_t(d.BH) * d.NT * d.K, 128, d.K))) return rc;
   if ((rc = tmap_2d(&m_h1, w.h1, uint64_t(d.BH) * d.NT * d.K, 128, d.K))) return rc;
   if ((rc = tmap_2d(&m_s2, s.s2, uint64_t(d.BH) * d.NT * 128, d.V, 128))) return rc;
@@ -250,7 +272,7 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   set_smem(dual_gemm_kernel, kDualSmem);
   auto dual = [&](const CUtensorMap& x1, const CUtensorMap& y1, const CUtensorMap& x2,
                   const CUtensorMap& y2, DualParams p) {
-    CYFA_LAUNCH("dual_gemm", st, (dual_gemm_kernel<<<tiles, 128, kDualSmem, st>>>(x1, y1, x2, y2, p)));
+    CYFA_LAUNCH("dual_gemm", st, (dual_gemm_kernel<<<tiles, 256, kDualSmem, st>>>(x1, y1, x2, y2, p)));
     return launch_status();
   };
   const int nsub1 = (d.K / 128) * 2, nsub2 = d.V / 64;
@@ -267,12 +289,12 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     if (d.V == 256) {
       set_smem(tile_scores_kernel<128, 256>, scores_smem<128, 256>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<128, 256><<<tiles, 128, scores_smem<128, 256>(), st>>>(
+                  (tile_scores_kernel<128, 256><<<tiles, 256, scores_smem<128, 256>(), st>>>(
                       m_weights, m_w, m_do, m_v, sp)));
     } else {
       set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<128, 128><<<tiles, 128, scores_smem<128, 128>(), st>>>(
+                  (tile_scores_kernel<128, 128><<<tiles, 256, scores_smem<128, 128>(), st>>>(
                       m_weights, m_w, m_do, m_v, sp)));
     }
     if ((rc = launch_status())) return rc;
@@ -286,7 +308,7 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     if ((rc = dual(m_Bp, m_weights, m_v, m_h2, k2))) return rc;
     // dv = A^T dO + 2^{G_L-G_s} w H  (public layout)
     DualParams v2{d.BH, d.H, d.TP, d.NT, d.T, 1, kPublic4D, kRows2D, 0, d.V, 128, 128, d.V, s.G,
-                  1.f, 1, 2, g->dv, nullptr, 0.f, 0, nullptr};
+                  1.f, 1, 2, g->dv, nullptr, 0.f, 0, nullptr, stride_or(g->dv_stride, d.H * d.V)};
     if ((rc = dual(m_A, m_do, m_w, m_h2, v2))) return rc;
   }
   // ================= readout adjoint
@@ -313,12 +335,12 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     if (d.K == 256) {
       set_smem(tile_scores_kernel<256, 128>, scores_smem<256, 128>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<256, 128><<<tiles, 128, scores_smem<256, 128>(), st>>>(
+                  (tile_scores_kernel<256, 128><<<tiles, 256, scores_smem<256, 128>(), st>>>(
                       m_qn, m_kn, m_draw, m_w, sp)));
     } else {
       set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<128, 128><<<tiles, 128, scores_smem<128, 128>(), st>>>(
+                  (tile_scores_kernel<128, 128><<<tiles, 256, scores_smem<128, 128>(), st>>>(
                       m_qn, m_kn, m_draw, m_w, sp)));
     }
     if ((rc = launch_status())) return rc;
@@ -330,27 +352,30 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     DualParams k1{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kRows2D, 1, d.K, 128, d.K, 128, s.G,
                   1.f, 1, 0, w.dk1, s.kn, -1.f, 1, w.dG};
     if ((rc = dual(m_Bp, m_qn, m_w, m_h1, k1))) return rc;
-    // dw += A^T draw + 2^{G_L-G_s} k^ H
+    // dw_b = A^T draw + 2^{G_L-G_s} k^ H  (the write-vector gradient is dw + dw_b)
     DualParams v1{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kRows2D, 0, 128, d.K, d.K, 128, s.G,
-                  1.f, 1, 1, w.dw, nullptr, 0.f, 0, nullptr};
+                  1.f, 1, 0, w.dw_b, nullptr, 0.f, 0, nullptr};
     if ((rc = dual(m_A, m_draw, m_kn, m_h1, v1))) return rc;
   }
   // ================= norms, write vector, gates, clock
-  rc = cyfa_token_bwd(a->q, a->k, a->q_norm_weight, a->k_norm_weight, s.q_rs, s.k_rs, w.dq1,
-                      w.dk1, s.lam, s.beta_h, w.dw, g->dq, g->dk, w.dqw_part, w.dkw_part,
-                      w.dlam_w, w.dbeta_h, d.B, d.T, d.H, d.K, stream);
+  rc = token_bwd_launch(a->q, a->k, a->q_norm_weight, a->k_norm_weight, s.q_rs, s.k_rs, w.dq1,
+                        w.dk1, s.lam, s.beta_h, w.dw, w.dw_b, g->dq, g->dk, w.dqw_part, w.dkw_part,
+                        w.dlam_w, w.dbeta_h, d.B, d.T, d.H, d.K,
+                        stride_or(a->q_stride, d.H * d.K), stride_or(a->k_stride, d.H * d.K),
+                        stride_or(g->dq_stride, d.H * d.K), stride_or(g->dk_stride, d.H * d.K),
+                        stream);
   if (rc) return rc;
   const int nblk = token_bwd_blocks(rows);
   CYFA_LAUNCH("column_sum", st,
-              (column_sum_kernel<<<(d.K + 31) / 32, 256, 0, st>>>(w.dqw_part, g->dq_norm_weight, nblk,
+              (column_sum_kernel<<<(d.K + 31) / 32, 1024, 0, st>>>(w.dqw_part, g->dq_norm_weight, nblk,
                                                                    d.K)));
   CYFA_LAUNCH("column_sum", st,
-              (column_sum_kernel<<<(d.K + 31) / 32, 256, 0, st>>>(w.dkw_part, g->dk_norm_weight, nblk,
+              (column_sum_kernel<<<(d.K + 31) / 32, 1024, 0, st>>>(w.dkw_part, g->dk_norm_weight, nblk,
                                                                    d.K)));
   if ((rc = launch_status())) return rc;
   GatesBwdParams gp{w.dG, w.dlam_w, w.dlam_r, w.bpart1, w.bpart2, nsub1, nsub2, w.dbeta_h,
                     g->dclock, g->dg, g->ddelta, g->dbeta, g->dclock0, d.B, d.T, d.H, d.TP};
-  CYFA_LAUNCH("gates_bwd", st, (gates_bwd_kernel<<<d.BH, 128, 0, st>>>(gp)));
+  CYFA_LAUNCH("gates_bwd", st, (gates_bwd_kernel<<<d.BH, 1024, 0, st>>>(gp)));
   return launch_status();
 }
 

@@ -7,5 +7,7 @@
 #include "prep.cu"
 #include "gla_fwd.cu"
 #include "gla_bwd.cu"
+#include "layer.cu"
 #include "capi.cu"
 #include "chunk_api.cu"
+#include "layer_api.cu"

@@ -43,7 +43,7 @@ constexpr int scores_smem() {
 }
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(256, 1)
     tile_scores_kernel(const __grid_constant__ CUtensorMap map_q,
                        const __grid_constant__ CUtensorMap map_k,
                        const __grid_constant__ CUtensorMap map_do,
@@ -54,19 +54,22 @@ __global__ void __launch_bounds__(128, 1)
   __shared__ __align__(8) uint64_t bar_in, bar_mma;
   __shared__ uint32_t tmem_base;
   __shared__ float Gs[128];
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT;
   if (tid == 0) {
     mbar_init(&bar_in, 1);
     mbar_init(&bar_mma, 1);
     mbar_fence_init();
   }
-  if (tid < 32) tmem_alloc(&tmem_base, 256);
-  Gs[tid] = p.G[size_t(bh) * p.TP + j * 128 + tid];
+  if (warp == 0) tmem_alloc(&tmem_base, 256);
+  if (tid < 128) Gs[tid] = p.G[size_t(bh) * p.TP + j * 128 + tid];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = tmem_base, lane_tmem = tmem_lane_base(tmem);
+  const uint32_t tmem = tmem_base;
+  // warp w: TMEM lane quadrant (w & 3), matrix (w >> 2): 0 = A (q.k), 1 = B' (dO.v)
+  const int quad = warp & 3, m = warp >> 2, r = quad * 32 + lane;
+  const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
   bool ok = true;
   if (tid == 0) {
     mbar_expect_tx(&bar_in, 2 * DK * 256 + 2 * DV * 256);
@@ -95,27 +98,24 @@ __global__ void __launch_bounds__(128, 1)
   if (!mbar_wait(&bar_mma, 0)) ok = false;
   tc_fence_after();
   if (ok) {
-    const float gt = Gs[tid];
-    const size_t row = (size_t(bh) * p.NT + j) * 128 + tid;
+    const float gt = Gs[r];
+    const size_t row = (size_t(bh) * p.NT + j) * 128 + r;
+    __nv_bfloat16* dst = (m == 0 ? p.A : p.Bp) + row * 128;
 #pragma unroll 1
-    for (int m = 0; m < 2; ++m) {
-      __nv_bfloat16* dst = (m == 0 ? p.A : p.Bp) + row * 128;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(lane_tmem + m * 128 + 32 * c, v);
+    for (int c = 0; c < 4; ++c) {
+      float v[32];
+      tmem_ld32(lane_tmem + m * 128 + 32 * c, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int s = 32 * c + i;
-          v[i] = s <= tid ? p.scale * v[i] * exp2f(gt - Gs[s]) : 0.f;
-        }
-        store_bf16x32_global(dst + 32 * c, v);
+      for (int i = 0; i < 32; ++i) {
+        const int s = 32 * c + i;
+        v[i] = s <= r ? p.scale * v[i] * exp2f(gt - Gs[s]) : 0.f;
       }
+      store_bf16x32_global(dst + 32 * c, v);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (tid < 32) {
+  if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 256);
   }
@@ -139,11 +139,15 @@ struct DualParams {
   float dot_sign;
   int dot_acc;
   float* dG;
+  long long out_stride;  // out_mode 2: elements between consecutive tokens
 };
 
 constexpr int kDualSmem = 192 * 1024 + 1024;
 
-__global__ void __launch_bounds__(128, 1)
+// 8 warps: warp w reads TMEM lane quadrant (w & 3) (rows 32(w&3) .. +31) and
+// column half (w >> 2).  The epilogue's global loads (gate factors, row-dot
+// partner) are issued before waiting for the MMAs so that they overlap them.
+__global__ void __launch_bounds__(256, 1)
     dual_gemm_kernel(const __grid_constant__ CUtensorMap map_x1,
                      const __grid_constant__ CUtensorMap map_y1,
                      const __grid_constant__ CUtensorMap map_x2,
@@ -153,19 +157,22 @@ __global__ void __launch_bounds__(128, 1)
   const int kX1 = 0, kY1 = 32768, kX2 = 32768 + p.N * 256, kY2 = kX2 + p.KD * 256;
   __shared__ __align__(8) uint64_t bar_in, bar_mma;
   __shared__ uint32_t tmem_base;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
   const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT;
-  const int t = j * 128 + tid;
+  const int r = quad * 32 + lane;  // tile row = TMEM lane
+  const int t = j * 128 + r;
   if (tid == 0) {
     mbar_init(&bar_in, 1);
     mbar_init(&bar_mma, 1);
     mbar_fence_init();
   }
-  if (tid < 32) tmem_alloc(&tmem_base, 512);
+  if (warp == 0) tmem_alloc(&tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = tmem_base, lane_tmem = tmem_lane_base(tmem);
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
   bool ok = true;
   if (tid == 0) {
     mbar_expect_tx(&bar_in, 32768 + p.N * 256 + p.KD * 256 + p.hrows * p.hcols * 2);
@@ -191,27 +198,37 @@ __global__ void __launch_bounds__(128, 1)
       mbar_arrive(&bar_mma);
     }
   }
+  // ---- epilogue prefetch (independent of the MMAs)
+  const float* Gt = p.G + size_t(bh) * p.TP + j * 128;
+  const float f = p.fkind == 0 ? p.scale * exp2f(Gt[r]) : exp2f(Gt[127] - Gt[r]);
+  const size_t row = size_t(bh) * p.TP + t;
+  const int ncol = p.N / 2, c_beg = half * ncol;  // 64 or 128 columns
+  uint4 dpre[16];
+  if (p.dot_src) {
+    const uint4* src = reinterpret_cast<const uint4*>(p.dot_src + row * p.N + c_beg);
+#pragma unroll
+    for (int q = 0; q < 16; ++q)
+      if (q < ncol / 8) dpre[q] = src[q];
+  }
   __syncwarp();
   if (!mbar_wait(&bar_mma, 0)) ok = false;
   tc_fence_after();
   if (ok) {
-    const float* Gt = p.G + size_t(bh) * p.TP + j * 128;
-    const float f = p.fkind == 0 ? p.scale * exp2f(Gt[tid]) : exp2f(Gt[127] - Gt[tid]);
     float dot = 0.f;
-    const size_t row = size_t(bh) * p.TP + t;
-#pragma unroll 1
-    for (int c = 0; c < p.N / 32; ++c) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (c >= ncol / 32) break;
+      const int col = c_beg + 32 * c;
       float a[32], b[32];
-      tmem_ld32(lane_tmem + 32 * c, a);
-      tmem_ld32(lane_tmem + 256 + 32 * c, b);
+      tmem_ld32(lane_tmem + col, a);
+      tmem_ld32(lane_tmem + 256 + col, b);
 #pragma unroll
       for (int i = 0; i < 32; ++i) a[i] += f * b[i];
       if (p.dot_src) {
-        const uint4* src = reinterpret_cast<const uint4*>(p.dot_src + row * p.N + 32 * c);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           float x[8];
-          unpack_bf16x8(src[q], x);
+          unpack_bf16x8(dpre[4 * c + q], x);
 #pragma unroll
           for (int e = 0; e < 8; ++e) dot += x[e] * a[8 * q + e];
         }
@@ -219,31 +236,34 @@ __global__ void __launch_bounds__(128, 1)
       if (p.out_mode == 2) {
         if (t < p.T) {
           const int b_ = bh / p.H, h = bh % p.H;
-          store_bf16x32_global(
-              static_cast<__nv_bfloat16*>(p.out) + ((size_t(b_) * p.T + t) * p.H + h) * p.N + 32 * c,
-              a);
+          store_bf16x32_global(static_cast<__nv_bfloat16*>(p.out) +
+                                   (size_t(b_) * p.T + t) * p.out_stride + size_t(h) * p.N + col,
+                               a);
         }
       } else {
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + 32 * c);
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + col);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 v = make_float4(a[4 * q], a[4 * q + 1], a[4 * q + 2], a[4 * q + 3]);
-          if (p.out_mode == 1) {
-            const float4 o = dst[q];
-            v.x += o.x;
-            v.y += o.y;
-            v.z += o.z;
-            v.w += o.w;
-          }
-          dst[q] = v;
-        }
+        for (int q = 0; q < 8; ++q)
+          __stcs(dst + q, make_float4(a[4 * q], a[4 * q + 1], a[4 * q + 2], a[4 * q + 3]));
       }
     }
-    if (p.dot_src) p.dG[row] = (p.dot_acc ? p.dG[row] : 0.f) + p.dot_sign * dot;
+    if (p.dot_src) {
+      // combine the two column halves of the row dot in a fixed order
+      __shared__ float dot_half[2][128];
+      dot_half[half][r] = dot;
+      __syncwarp();
+      asm volatile("bar.sync 1, 256;");
+      if (half == 0) {
+        const float total = dot_half[0][r] + dot_half[1][r];
+        p.dG[row] = (p.dot_acc ? p.dG[row] : 0.f) + p.dot_sign * total;
+      }
+    }
+  } else if (p.dot_src) {
+    asm volatile("bar.sync 1, 256;");
   }
   tc_fence_before();
   __syncthreads();
-  if (tid < 32) {
+  if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -486,19 +506,30 @@ __global__ void __launch_bounds__(128) dtable_reduce_kernel(const float* part, f
 }
 
 // Fixed-order column sums of a [rows, cols] partial matrix: out[c] = sum_r part[r][c].
-__global__ void __launch_bounds__(256) column_sum_kernel(const float* part, float* out, int rows,
-                                                         int cols) {
-  __shared__ float acc[8][33];
+// 1024 threads: 32 columns x 32 row lanes, each lane with 4 independent accumulators.
+__global__ void __launch_bounds__(1024) column_sum_kernel(const float* part, float* out, int rows,
+                                                          int cols) {
+  __shared__ float acc[32][33];
   const int c = blockIdx.x * 32 + (threadIdx.x & 31), lane_r = threadIdx.x >> 5;
   float s = 0.f;
-  if (c < cols)
-    for (int r = lane_r; r < rows; r += 8) s += part[size_t(r) * cols + c];
+  if (c < cols) {
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    int r = lane_r;
+    for (; r + 96 < rows; r += 128) {
+      s0 += part[size_t(r) * cols + c];
+      s1 += part[size_t(r + 32) * cols + c];
+      s2 += part[size_t(r + 64) * cols + c];
+      s3 += part[size_t(r + 96) * cols + c];
+    }
+    for (; r < rows; r += 32) s0 += part[size_t(r) * cols + c];
+    s = (s0 + s1) + (s2 + s3);
+  }
   acc[lane_r][threadIdx.x & 31] = s;
   __syncthreads();
   if (threadIdx.x < 32 && c < cols) {
     float t = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) t += acc[i][threadIdx.x];
+    for (int i = 0; i < 32; ++i) t += acc[i][threadIdx.x];
     out[c] = t;
   }
 }

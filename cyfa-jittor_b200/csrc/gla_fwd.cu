@@ -142,17 +142,18 @@ __global__ void __launch_bounds__(128, 1)
   }
   const uint32_t idesc = make_idesc(128, 64, 1, 1);
   const int nsub = gridDim.y * gridDim.z, sub = blockIdx.y * gridDim.z + blockIdx.z;
-  bool ok = true;
   int consumed = 0, committed = 0, retired = 0;
 
-  for (int idx = 0; idx < NT; ++idx) {
+  // Waits for tile idx's operands, rescales its V rows and issues its UMMA into
+  // TMEM buffer idx & 1.  Returns false (on every thread) if a wait timed out.
+  auto prepare = [&](int idx) -> bool {
     const int s = idx % kScanStages, j = tile_of(idx);
     uint8_t* st = smem + s * kScanStageBytes;
     const float* Gt = p.G + size_t(bh) * p.TP + size_t(j) * 128;
-    const float gl = Gt[127], gt = Gt[tid];
-    const float f = REVERSE ? p.scale * exp2f(gt) : exp2f(gl - gt);
-    if (!mbar_wait(&full[s], (idx / kScanStages) & 1)) ok = false;
-    if (ok) {
+    const float gt = Gt[tid];
+    const float f = REVERSE ? p.scale * exp2f(gt) : exp2f(Gt[127] - gt);
+    bool good = mbar_wait(&full[s], (idx / kScanStages) & 1);
+    if (good) {
       const uint32_t vb = smem_u32(st + 32768);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
@@ -165,12 +166,10 @@ __global__ void __launch_bounds__(128, 1)
     }
     fence_async_smem();
     tc_fence_before();
-    if (!__syncthreads_and(ok)) {
-      ok = false;
-      break;
-    }
+    good = __syncthreads_and(good);
     tc_fence_after();
     consumed = idx + 1;
+    if (!good) return false;
     if (tid == 0) {
       const uint32_t kb = smem_u32(st), vb = smem_u32(st + 32768);
 #pragma unroll
@@ -180,6 +179,28 @@ __global__ void __launch_bounds__(128, 1)
       umma_commit(&mma_done[idx & 1]);
     }
     committed = idx + 1;
+    return true;
+  };
+
+  bool ok = NT > 0 ? prepare(0) : true;
+  for (int idx = 0; idx < NT && ok; ++idx) {
+    const int j = tile_of(idx);
+    const float gl = p.G[size_t(bh) * p.TP + size_t(j) * 128 + 127];
+    // REVERSE: fetch S_{j+1} (this CTA's row slice) early; it is consumed below
+    uint4 nxt[8];
+    if constexpr (REVERSE) {
+      if (j + 1 < NT) {
+        const uint4* src = reinterpret_cast<const uint4*>(
+            p.fwd_hist + ((size_t(bh) * NT + j + 1) * p.DK + dk0 + tid) * p.DV + dv0);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) nxt[c] = src[c];
+      }
+    }
+    // overlap: the next tile's update is independent of the running state
+    if (idx + 1 < NT && !prepare(idx + 1)) {
+      ok = false;
+      break;
+    }
     // state entering tile j (forward) / adjoint leaving tile j (reverse)
     {
       uint4* dst = reinterpret_cast<uint4*>(p.hist + ((size_t(bh) * NT + j) * p.DK + dk0 + tid) *
@@ -194,12 +215,10 @@ __global__ void __launch_bounds__(128, 1)
       // <S_{j+1}, H_{j+1}> over this CTA's slice (S_{j+1} from the forward pass)
       float dot = 0.f;
       if (j + 1 < NT) {
-        const uint4* src = reinterpret_cast<const uint4*>(
-            p.fwd_hist + ((size_t(bh) * NT + j + 1) * p.DK + dk0 + tid) * p.DV + dv0);
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           float x[8];
-          unpack_bf16x8(src[c], x);
+          unpack_bf16x8(nxt[c], x);
 #pragma unroll
           for (int e = 0; e < 8; ++e) dot += x[e] * S[8 * c + e];
         }
@@ -219,10 +238,9 @@ __global__ void __launch_bounds__(128, 1)
         p.bpart[(size_t(bh) * NT + j) * nsub + sub] = (red[0] + red[1]) + (red[2] + red[3]);
       __syncthreads();
     }
-    if (!mbar_wait(&mma_done[idx & 1], (idx >> 1) & 1)) ok = false;
+    const bool got = mbar_wait(&mma_done[idx & 1], (idx >> 1) & 1);
     tc_fence_after();
-    if (ok) {
-      retired = idx + 1;
+    if (got) {
       const float gamma = exp2f(gl);
       float U[32];
       tmem_ld32(lane_tmem + (idx & 1) * 64, U);
@@ -233,18 +251,22 @@ __global__ void __launch_bounds__(128, 1)
       for (int i = 0; i < 32; ++i) S[32 + i] = S[32 + i] * gamma + U[i];
     }
     tc_fence_before();
+    ok = __syncthreads_and(got);  // every thread leaves the loop at the same iteration
+    if (ok) retired = idx + 1;
+    // tile idx's stage is free once its MMA has completed
     if (tid == 0 && ok && issued < NT) {
       issue(issued);
       ++issued;
     }
   }
+  ok = __syncthreads_and(ok);
 
   if (ok && p.last) {
     float4* dst = reinterpret_cast<float4*>(p.last + row_off);
 #pragma unroll
     for (int i = 0; i < 16; ++i)
       dst[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
-  } else if (tid == 0) {
+  } else if (!ok && tid == 0) {
     // unwind: let in-flight copies and MMAs land before TMEM and smem go away
     for (int idx = consumed; idx < issued; ++idx)
       mbar_wait(&full[idx % kScanStages], (idx / kScanStages) & 1);
@@ -257,7 +279,6 @@ __global__ void __launch_bounds__(128, 1)
     tmem_dealloc(tmem, 128);
   }
 }
-
 
 // ============================================================ tile output
 struct TileFwdParams {

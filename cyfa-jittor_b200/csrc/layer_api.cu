@@ -1,0 +1,197 @@
+// C-ABI of the layer glue kernels (short convolution, gate activations, gated
+// output norm).  Work buffers for the deterministic weight-gradient partials are
+// caller-owned; their sizes come from the *_work_bytes queries.
+#include "../../include/cyfa.h"
+#include "cyfa_common.cuh"
+
+namespace cyfa {
+
+static int conv_bwd_rows(int B) { return B * kConvSplit; }
+
+static int gate_bwd_blocks(long long n) {
+  const long long want = (n + 255) / 256;
+  return int(want < 592 ? want : 592);
+}
+
+static int norm_bwd_blocks(int rows) {
+  const int want = (rows + 7) / 8;
+  return want < 296 ? want : 296;
+}
+
+}  // namespace cyfa
+
+using namespace cyfa;
+
+extern "C" {
+
+size_t cyfa_short_conv_work_bytes(int B, int T, int C, int W) {
+  if (B <= 0 || T <= 0 || C <= 0 || W < 1 || W > 4) return 0;
+  return size_t(conv_bwd_rows(B)) * C * (W + 1) * sizeof(float);
+}
+
+int cyfa_short_conv_fwd(const void* x, long long x_stride, const void* cache, const float* w,
+                        const float* bias, void* y, int B, int T, int C, int W, void* stream) {
+  CYFA_REQUIRE(x && w && y, kNullPointer);
+  CYFA_REQUIRE(B > 0 && T > 0 && C > 0 && C % 8 == 0 && W >= 1 && W <= 4 && x_stride >= C &&
+                   x_stride % 8 == 0,
+               kBadShape);
+  CYFA_REQUIRE(aligned(x, 16) && aligned(y, 16) && (!cache || aligned(cache, 16)), kMisaligned);
+  ConvParams p{static_cast<const __nv_bfloat16*>(x), x_stride,
+               static_cast<const __nv_bfloat16*>(cache), w, bias, static_cast<__nv_bfloat16*>(y),
+               nullptr, nullptr, 0, nullptr, B, T, C};
+  const dim3 grid((C + 255) / 256, (T + kConvChunk - 1) / kConvChunk, B);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (W) {
+    case 1: CYFA_LAUNCH("short_conv_fwd", s, short_conv_fwd_kernel<1><<<grid, 256, 0, s>>>(p)); break;
+    case 2: CYFA_LAUNCH("short_conv_fwd", s, short_conv_fwd_kernel<2><<<grid, 256, 0, s>>>(p)); break;
+    case 3: CYFA_LAUNCH("short_conv_fwd", s, short_conv_fwd_kernel<3><<<grid, 256, 0, s>>>(p)); break;
+    default: CYFA_LAUNCH("short_conv_fwd", s, short_conv_fwd_kernel<4><<<grid, 256, 0, s>>>(p)); break;
+  }
+  return launch_status();
+}
+
+int cyfa_short_conv_bwd(const void* x, long long x_stride, const float* w, const void* dy,
+                        void* dx, long long dx_stride, float* dw, float* dbias, int B, int T,
+                        int C, int W, void* work, size_t work_bytes, void* stream) {
+  CYFA_REQUIRE(x && w && dy && dx && dw && work, kNullPointer);
+  CYFA_REQUIRE(B > 0 && T > 0 && C > 0 && C % 8 == 0 && W >= 1 && W <= 4 && x_stride >= C &&
+                   x_stride % 8 == 0 && dx_stride >= C && dx_stride % 8 == 0,
+               kBadShape);
+  CYFA_REQUIRE(work_bytes >= cyfa_short_conv_work_bytes(B, T, C, W), kWorkspace);
+  CYFA_REQUIRE(aligned(x, 16) && aligned(dy, 16) && aligned(dx, 16), kMisaligned);
+  float* part = static_cast<float*>(work);
+  ConvParams p{static_cast<const __nv_bfloat16*>(x), x_stride, nullptr, w, nullptr, nullptr,
+               static_cast<const __nv_bfloat16*>(dy), static_cast<__nv_bfloat16*>(dx), dx_stride,
+               part, B, T, C};
+  const dim3 grid((C + 255) / 256, conv_bwd_rows(B));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (W) {
+    case 1:
+      set_smem(short_conv_bwd_kernel<1>, conv_bwd_smem<1>());
+      CYFA_LAUNCH("short_conv_bwd", s,
+                  (short_conv_bwd_kernel<1><<<grid, 256, conv_bwd_smem<1>(), s>>>(p)));
+      break;
+    case 2:
+      set_smem(short_conv_bwd_kernel<2>, conv_bwd_smem<2>());
+      CYFA_LAUNCH("short_conv_bwd", s,
+                  (short_conv_bwd_kernel<2><<<grid, 256, conv_bwd_smem<2>(), s>>>(p)));
+      break;
+    case 3:
+      set_smem(short_conv_bwd_kernel<3>, conv_bwd_smem<3>());
+      CYFA_LAUNCH("short_conv_bwd", s,
+                  (short_conv_bwd_kernel<3><<<grid, 256, conv_bwd_smem<3>(), s>>>(p)));
+      break;
+    default:
+      set_smem(short_conv_bwd_kernel<4>, conv_bwd_smem<4>());
+      CYFA_LAUNCH("short_conv_bwd", s,
+                  (short_conv_bwd_kernel<4><<<grid, 256, conv_bwd_smem<4>(), s>>>(p)));
+      break;
+  }
+  int rc = launch_status();
+  if (rc) return rc;
+  // reduce the partial rows: columns are [c][0..W-1] = dw, [c][W] = dbias
+  const int rows = conv_bwd_rows(B), cols = C * (W + 1);
+  CYFA_LAUNCH("conv_param_sum", s,
+              (conv_param_sum_kernel<<<(cols + 255) / 256, 256, 0, s>>>(part, rows, C, W, dw,
+                                                                        dbias)));
+  return launch_status();
+}
+
+int cyfa_gate_act_fwd(const void* a, long long a_stride, const void* b, long long b_stride,
+                      const void* d, long long d_stride, const float* A_log,
+                      const float* dt_bias, float* g, float* delta, float* beta, int rows, int H,
+                      void* stream) {
+  CYFA_REQUIRE(a && b && d && A_log && dt_bias && g && delta && beta, kNullPointer);
+  CYFA_REQUIRE(rows > 0 && H > 0 && 256 % H == 0 && a_stride >= H && b_stride >= H &&
+                   d_stride >= H,
+               kBadShape);
+  GateActParams p{static_cast<const __nv_bfloat16*>(a), a_stride,
+                  static_cast<const __nv_bfloat16*>(b), b_stride,
+                  static_cast<const __nv_bfloat16*>(d), d_stride, A_log, dt_bias, g, delta, beta,
+                  nullptr, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, 0, nullptr, rows, H};
+  const long long n = (long long)rows * H;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CYFA_LAUNCH("gate_act_fwd", s,
+              (gate_act_fwd_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(p)));
+  return launch_status();
+}
+
+size_t cyfa_gate_act_work_bytes(int rows, int H) {
+  if (rows <= 0 || H <= 0) return 0;
+  return size_t(gate_bwd_blocks((long long)rows * H)) * 2 * H * sizeof(float);
+}
+
+int cyfa_gate_act_bwd(const void* a, long long a_stride, const void* b, long long b_stride,
+                      const void* d, long long d_stride, const float* A_log,
+                      const float* dt_bias, const float* dg, const float* ddelta,
+                      const float* dbeta, void* da, long long da_stride, void* db,
+                      long long db_stride, void* dd, long long dd_stride, float* dA_log,
+                      float* ddt_bias, int rows, int H, void* work, size_t work_bytes,
+                      void* stream) {
+  CYFA_REQUIRE(a && b && d && A_log && dt_bias && dg && ddelta && dbeta && da && db && dd &&
+                   dA_log && ddt_bias && work,
+               kNullPointer);
+  CYFA_REQUIRE(rows > 0 && H > 0 && 256 % H == 0, kBadShape);
+  CYFA_REQUIRE(work_bytes >= cyfa_gate_act_work_bytes(rows, H), kWorkspace);
+  float* part = static_cast<float*>(work);
+  GateActParams p{static_cast<const __nv_bfloat16*>(a), a_stride,
+                  static_cast<const __nv_bfloat16*>(b), b_stride,
+                  static_cast<const __nv_bfloat16*>(d), d_stride, A_log, dt_bias, nullptr,
+                  nullptr, nullptr, dg, ddelta, dbeta, static_cast<__nv_bfloat16*>(da), da_stride,
+                  static_cast<__nv_bfloat16*>(db), db_stride, static_cast<__nv_bfloat16*>(dd),
+                  dd_stride, part, rows, H};
+  const int nblk = gate_bwd_blocks((long long)rows * H);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CYFA_LAUNCH("gate_act_bwd", s, (gate_act_bwd_kernel<<<nblk, 256, 0, s>>>(p)));
+  int rc = launch_status();
+  if (rc) return rc;
+  CYFA_LAUNCH("column_sum", s,
+              (strided_column_sum_kernel<<<1, 256, 0, s>>>(part, dA_log, nblk, H, 2 * H)));
+  CYFA_LAUNCH("column_sum", s,
+              (strided_column_sum_kernel<<<1, 256, 0, s>>>(part + H, ddt_bias, nblk, H, 2 * H)));
+  return launch_status();
+}
+
+int cyfa_gated_norm_fwd(const void* x, const void* gate, const float* w, float eps, float scale,
+                        void* y, float* rstd, int rows, int D, void* stream) {
+  CYFA_REQUIRE(x && gate && w && y && rstd, kNullPointer);
+  CYFA_REQUIRE(rows > 0 && (D == 256 || D == 128), kBadShape);
+  CYFA_REQUIRE(aligned(x, 16) && aligned(gate, 16) && aligned(y, 16), kMisaligned);
+  GatedNormParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gate),
+                    w, eps, scale, static_cast<__nv_bfloat16*>(y), rstd, nullptr, nullptr, nullptr,
+                    nullptr, rows};
+  const unsigned grid = unsigned((rows + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (D == 256) CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<8><<<grid, 256, 0, s>>>(p)));
+  else CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<4><<<grid, 256, 0, s>>>(p)));
+  return launch_status();
+}
+
+size_t cyfa_gated_norm_work_bytes(int rows, int D) {
+  if (rows <= 0 || D <= 0) return 0;
+  return size_t(norm_bwd_blocks(rows)) * D * sizeof(float);
+}
+
+int cyfa_gated_norm_bwd(const void* x, const void* gate, const float* w, float scale,
+                        const float* rstd, const void* dy, void* dx, void* dgate, float* dw,
+                        int rows, int D, void* work, size_t work_bytes, void* stream) {
+  CYFA_REQUIRE(x && gate && w && rstd && dy && dx && dgate && dw && work, kNullPointer);
+  CYFA_REQUIRE(rows > 0 && (D == 256 || D == 128), kBadShape);
+  CYFA_REQUIRE(work_bytes >= cyfa_gated_norm_work_bytes(rows, D), kWorkspace);
+  float* part = static_cast<float*>(work);
+  GatedNormParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gate),
+                    w, 0.f, scale, nullptr, const_cast<float*>(rstd),
+                    static_cast<const __nv_bfloat16*>(dy), static_cast<__nv_bfloat16*>(dx),
+                    static_cast<__nv_bfloat16*>(dgate), part, rows};
+  const int nblk = norm_bwd_blocks(rows);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (D == 256) CYFA_LAUNCH("gated_norm_bwd", s, (gated_norm_bwd_kernel<8><<<nblk, 256, 0, s>>>(p)));
+  else CYFA_LAUNCH("gated_norm_bwd", s, (gated_norm_bwd_kernel<4><<<nblk, 256, 0, s>>>(p)));
+  int rc = launch_status();
+  if (rc) return rc;
+  CYFA_LAUNCH("column_sum", s,
+              (column_sum_kernel<<<(D + 31) / 32, 1024, 0, s>>>(part, dw, nblk, D)));
+  return launch_status();
+}
+
+}  // extern "C"

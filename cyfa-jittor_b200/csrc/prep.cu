@@ -23,6 +23,43 @@ namespace cyfa {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Vector loads/stores of E = 4 or 8 consecutive elements (16/32-byte aligned rows).
+template <int E>
+__device__ __forceinline__ void load_bf16_vec(const __nv_bfloat16* p, float* f) {
+  if constexpr (E == 8) {
+    unpack_bf16x8(*reinterpret_cast<const uint4*>(p), f);
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    f[0] = a.x;
+    f[1] = a.y;
+    f[2] = b.x;
+    f[3] = b.y;
+  }
+}
+template <int E>
+__device__ __forceinline__ void load_f32_vec(const float* p, float* f) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < E / 4; ++i) {
+    const float4 x = q[i];
+    f[4 * i] = x.x;
+    f[4 * i + 1] = x.y;
+    f[4 * i + 2] = x.z;
+    f[4 * i + 3] = x.w;
+  }
+}
+template <int E>
+__device__ __forceinline__ void store_bf16_vec(__nv_bfloat16* p, const float* f) {
+  if constexpr (E == 8) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]),
+                                              pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
+  } else {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16(f[0], f[1]), pack_bf16(f[2], f[3]));
+  }
+}
+
 struct GatesParams {
   const float* g;       // [B,T,H]
   const float* delta;   // [B,T,H]
@@ -35,31 +72,46 @@ struct GatesParams {
   int B, T, H, TP;
 };
 
-// Inclusive scan over 128 threads in a fixed order; returns the prefix and
-// writes the block total to *total.
-__device__ __forceinline__ float scan128(float x, float* buf, float* total) {
+// Block-wide scans of the gate kernels: 1024 threads = 32 warps cover 1024 tokens,
+// i.e. 8 tiles of 128 tokens (4 warps each).  All sums run in a fixed order.
+struct ScanPair {
+  float tile;   // scan within the 128-token tile
+  float block;  // scan within the 1024-token block
+};
+
+// Inclusive (REVERSE: suffix) scans of x; also returns the block total.
+template <bool REVERSE>
+__device__ __forceinline__ ScanPair scan1024(float x, float* wsum, float* total) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const float y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x = __fadd_rn(x, y);
+    const float y = REVERSE ? __shfl_down_sync(0xffffffffu, x, o) : __shfl_up_sync(0xffffffffu, x, o);
+    if (REVERSE ? (lane + o < 32) : (lane >= o)) x = __fadd_rn(x, y);
   }
-  if (lane == 31) buf[w] = x;
+  if (lane == (REVERSE ? 0 : 31)) wsum[w] = x;
   __syncthreads();
-  float carry = 0.f;
-  for (int i = 0; i < w; ++i) carry = __fadd_rn(carry, buf[i]);
-  const float t = __fadd_rn(__fadd_rn(__fadd_rn(buf[0], buf[1]), buf[2]), buf[3]);
+  float tile_carry = 0.f, block_carry = 0.f;
+  const int t0 = w & ~3;  // first warp of this 128-token tile
+  if (!REVERSE) {
+    for (int i = 0; i < w; ++i) block_carry = __fadd_rn(block_carry, wsum[i]);
+    for (int i = t0; i < w; ++i) tile_carry = __fadd_rn(tile_carry, wsum[i]);
+  } else {
+    for (int i = 31; i > w; --i) block_carry = __fadd_rn(block_carry, wsum[i]);
+    for (int i = t0 + 3; i > w; --i) tile_carry = __fadd_rn(tile_carry, wsum[i]);
+  }
+  float tot = 0.f;
+  for (int i = 0; i < 32; ++i) tot = __fadd_rn(tot, wsum[REVERSE ? 31 - i : i]);
   __syncthreads();
-  *total = t;
-  return __fadd_rn(x, carry);
+  *total = tot;
+  return {__fadd_rn(x, tile_carry), __fadd_rn(x, block_carry)};
 }
 
-__global__ void __launch_bounds__(128) gates_fwd_kernel(GatesParams p) {
+__global__ void __launch_bounds__(1024) gates_fwd_kernel(GatesParams p) {
   const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
-  __shared__ float buf[4];
+  __shared__ float wsum[32];
   float clock = p.clock0 ? p.clock0[bh] : 0.f;
   const size_t obase = size_t(bh) * p.TP;
-  for (int t0 = 0; t0 < p.TP; t0 += 128) {
+  for (int t0 = 0; t0 < p.TP; t0 += 1024) {
     const int t = t0 + threadIdx.x;
     float gv = 0.f, dv = 0.f, bv = 0.f;
     if (t < p.T) {
@@ -69,11 +121,13 @@ __global__ void __launch_bounds__(128) gates_fwd_kernel(GatesParams p) {
       bv = p.beta[i];
     }
     float tot;
-    const float gsum = scan128(gv, buf, &tot);
-    const float dsum = scan128(dv, buf, &tot);
-    p.G[obase + t] = gsum * kLog2e;
-    p.lam[obase + t] = __fadd_rn(clock, dsum);
-    p.beta_h[obase + t] = bv;
+    const ScanPair gs = scan1024<false>(gv, wsum, &tot);
+    const ScanPair ds = scan1024<false>(dv, wsum, &tot);
+    if (t < p.TP) {
+      p.G[obase + t] = gs.tile * kLog2e;
+      p.lam[obase + t] = __fadd_rn(clock, ds.block);
+      p.beta_h[obase + t] = bv;
+    }
     clock = __fadd_rn(clock, tot);
   }
   if (threadIdx.x == 0 && p.clock_out) p.clock_out[bh] = clock;
@@ -93,6 +147,7 @@ struct TokenFwdParams {
   float* k_rs;             // [B,H,TP]
   int B, T, H, TP;
   float q_eps, k_eps;
+  long long q_stride, k_stride;  // elements between consecutive tokens of q / k
 };
 
 template <int K>
@@ -106,10 +161,11 @@ __global__ void __launch_bounds__(256) token_fwd_kernel(TokenFwdParams p) {
   const int b = int(bh / p.H), h = int(bh % p.H);
   float qv[E], kv[E];
   if (t < p.T) {
-    const size_t src = ((size_t(b) * p.T + t) * p.H + h) * K + lane * E;
+    const size_t tok = size_t(b) * p.T + t, col = size_t(h) * K + lane * E;
+    const size_t srcq = tok * p.q_stride + col, srck = tok * p.k_stride + col;
     if constexpr (E == 8) {
-      const uint4 a = *reinterpret_cast<const uint4*>(p.q + src);
-      const uint4 c = *reinterpret_cast<const uint4*>(p.k + src);
+      const uint4 a = *reinterpret_cast<const uint4*>(p.q + srcq);
+      const uint4 c = *reinterpret_cast<const uint4*>(p.k + srck);
       const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&a);
       const __nv_bfloat16* cp = reinterpret_cast<const __nv_bfloat16*>(&c);
 #pragma unroll
@@ -118,8 +174,8 @@ __global__ void __launch_bounds__(256) token_fwd_kernel(TokenFwdParams p) {
         kv[j] = __bfloat162float(cp[j]);
       }
     } else {
-      const uint2 a = *reinterpret_cast<const uint2*>(p.q + src);
-      const uint2 c = *reinterpret_cast<const uint2*>(p.k + src);
+      const uint2 a = *reinterpret_cast<const uint2*>(p.q + srcq);
+      const uint2 c = *reinterpret_cast<const uint2*>(p.k + srck);
       const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&a);
       const __nv_bfloat16* cp = reinterpret_cast<const __nv_bfloat16*>(&c);
 #pragma unroll
@@ -193,7 +249,8 @@ struct TokenBwdParams {
   const float* dkn;
   const float* lam;         // [B,H,TP]
   const float* beta_h;
-  const float* dw;          // [B,H,TP,128] gradient of the write vector (both passes)
+  const float* dw;          // [B,H,TP,128] gradient of the write vector
+  const float* dw_b;        // second term of the write-vector gradient, or null
   __nv_bfloat16* dq;        // [B,T,H,K]
   __nv_bfloat16* dk;
   float* dqw_part;          // [gridDim.x, K]
@@ -201,6 +258,7 @@ struct TokenBwdParams {
   float* dlam;              // [B,H,TP] (phase part, added to by the readout part)
   float* dbeta;             // [B,H,TP]
   int B, T, H, TP;
+  long long q_stride, k_stride, dq_stride, dk_stride;  // token strides (elements)
 };
 
 // 8 warps per block; warp w of block b handles rows (b*8 + w) + i*gridDim.x*8.
@@ -223,15 +281,12 @@ __global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
     float xq[E], xk[E], gq[E], gk[E];
 #pragma unroll
     for (int j = 0; j < E; ++j) xq[j] = xk[j] = gq[j] = gk[j] = 0.f;
-    const size_t pub = ((size_t(b) * p.T + t) * p.H + h) * K + lane * E;
+    const size_t tok = size_t(b) * p.T + t, col = size_t(h) * K + lane * E;
     if (real) {
-#pragma unroll
-      for (int j = 0; j < E; ++j) {
-        xq[j] = __bfloat162float(p.q[pub + j]);
-        xk[j] = __bfloat162float(p.k[pub + j]);
-        gq[j] = p.dqn[row * K + lane * E + j];
-        gk[j] = p.dkn[row * K + lane * E + j];
-      }
+      load_bf16_vec<E>(p.q + tok * p.q_stride + col, xq);
+      load_bf16_vec<E>(p.k + tok * p.k_stride + col, xk);
+      load_f32_vec<E>(p.dqn + row * K + lane * E, gq);
+      load_f32_vec<E>(p.dkn + row * K + lane * E, gk);
     }
     const float qr = real ? p.q_rs[row] : 0.f, kr = real ? p.k_rs[row] : 0.f;
     float dotq = 0.f, dotk = 0.f;
@@ -248,15 +303,18 @@ __global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
     }
     dotq *= qr * qr / K;
     dotk *= kr * kr / K;
+    float oq[E], ok[E];
 #pragma unroll
     for (int j = 0; j < E; ++j) {
       const int d = lane * E + j;
-      if (real) {
-        p.dq[pub + j] = __float2bfloat16_rn((gq[j] * p.qw[d] - xq[j] * dotq) * qr);
-        p.dk[pub + j] = __float2bfloat16_rn((gk[j] * p.kw[d] - xk[j] * dotk) * kr);
-      }
+      oq[j] = (gq[j] * p.qw[d] - xq[j] * dotq) * qr;
+      ok[j] = (gk[j] * p.kw[d] - xk[j] * dotk) * kr;
       aq[j] += xq[j] * qr * gq[j];
       ak[j] += xk[j] * kr * gk[j];
+    }
+    if (real) {
+      store_bf16_vec<E>(p.dq + tok * p.dq_stride + col, oq);
+      store_bf16_vec<E>(p.dk + tok * p.dk_stride + col, ok);
     }
     // write-vector adjoint (ops/utils.py:598-616)
     const float lam = p.lam[row], bt = p.beta_h[row];
@@ -267,7 +325,13 @@ __global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
       float sn, cs;
       sincosf(clock_phase(lam, pair), &sn, &cs);
       const float sc = atom_scale(pair);
-      const float de = p.dw[row * 128 + 2 * pair], dd = p.dw[row * 128 + 2 * pair + 1];
+      float2 dwp = reinterpret_cast<const float2*>(p.dw + row * 128)[pair];
+      if (p.dw_b) {
+        const float2 e2 = reinterpret_cast<const float2*>(p.dw_b + row * 128)[pair];
+        dwp.x += e2.x;
+        dwp.y += e2.y;
+      }
+      const float de = dwp.x, dd = dwp.y;
       db += de * sc * cs - dd * sc * sn;
       dl += (-de * bt * sc * sn - dd * bt * sc * cs) * (pair * kTwoPiOver127);
     }
@@ -302,7 +366,7 @@ __global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
 // Number of blocks (= partial rows) token_bwd_kernel uses for a shape.
 inline int token_bwd_blocks(size_t rows) {
   const size_t want = (rows + 7) / 8;
-  return int(want < 1184 ? want : 1184);
+  return int(want < 296 ? want : 296);
 }
 
 template __global__ void token_bwd_kernel<256>(TokenBwdParams);
@@ -324,49 +388,33 @@ struct GatesBwdParams {
   int B, T, H, TP;
 };
 
-// Reverse inclusive scan over 128 threads (suffix sums), fixed order.
-__device__ __forceinline__ float rscan128(float x, float* buf, float* total) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float y = __shfl_down_sync(0xffffffffu, x, o);
-    if (lane + o < 32) x = __fadd_rn(x, y);
-  }
-  if (lane == 0) buf[w] = x;
-  __syncthreads();
-  float carry = 0.f;
-  for (int i = 3; i > w; --i) carry = __fadd_rn(carry, buf[i]);
-  const float t = __fadd_rn(__fadd_rn(__fadd_rn(buf[3], buf[2]), buf[1]), buf[0]);
-  __syncthreads();
-  *total = t;
-  return __fadd_rn(x, carry);
-}
-
-__global__ void __launch_bounds__(128) gates_bwd_kernel(GatesBwdParams p) {
+__global__ void __launch_bounds__(1024) gates_bwd_kernel(GatesBwdParams p) {
   const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
-  __shared__ float buf[4];
+  __shared__ float wsum[32];
   float carry = p.dclock ? p.dclock[bh] : 0.f;
   const size_t base = size_t(bh) * p.TP;
-  for (int t0 = p.TP - 128; t0 >= 0; t0 -= 128) {
-    const int t = t0 + threadIdx.x;
-    float tot;
-    float dGt = p.dG[base + t];
-    if (threadIdx.x == 127) {
-      const size_t tile = size_t(bh) * (p.TP / 128) + t0 / 128;
+  const int nblk = (p.TP + 1023) / 1024;
+  for (int k = nblk - 1; k >= 0; --k) {
+    const int t = k * 1024 + threadIdx.x;
+    const bool in = t < p.TP;
+    float dGt = in ? p.dG[base + t] : 0.f;
+    if (in && (t & 127) == 127) {
+      const size_t tile = size_t(bh) * (p.TP / 128) + t / 128;
       if (p.bpart1)
         for (int i = 0; i < p.nsub1; ++i) dGt += p.bpart1[tile * p.nsub1 + i];
       if (p.bpart2)
         for (int i = 0; i < p.nsub2; ++i) dGt += p.bpart2[tile * p.nsub2 + i];
     }
-    float dl = p.dlam[base + t];
-    if (p.dlam2) dl += p.dlam2[base + t];
-    const float gs = rscan128(dGt, buf, &tot);
-    const float ls = rscan128(dl, buf, &tot);
-    const float dd = __fadd_rn(carry, ls);
+    float dl = in ? p.dlam[base + t] : 0.f;
+    if (in && p.dlam2) dl += p.dlam2[base + t];
+    float tot;
+    const ScanPair gs = scan1024<true>(dGt, wsum, &tot);
+    const ScanPair ls = scan1024<true>(dl, wsum, &tot);
+    const float dd = __fadd_rn(carry, ls.block);
     carry = __fadd_rn(carry, tot);
     if (t < p.T) {
       const size_t i = (size_t(b) * p.T + t) * p.H + h;
-      p.dg[i] = gs;
+      p.dg[i] = gs.tile;
       p.ddelta[i] = dd;
       p.dbeta[i] = p.dbeta_h[base + t];
     }

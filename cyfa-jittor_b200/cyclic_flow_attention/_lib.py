@@ -28,6 +28,15 @@ _SIGNATURES = {
     "cyfa_token_bwd": [_vp] * 17 + [_i] * 4 + [_vp],
     "cyfa_gates_bwd": [_vp] * 8 + [_i] * 3 + [_vp],
     "cyfa_chunk_fwd": [_vp, _vp, ctypes.c_size_t, _vp],
+    "cyfa_short_conv_fwd": [_vp, ctypes.c_longlong, _vp, _vp, _vp, _vp] + [_i] * 4 + [_vp],
+    "cyfa_short_conv_bwd": [_vp, ctypes.c_longlong, _vp, _vp, _vp, ctypes.c_longlong, _vp, _vp]
+    + [_i] * 4 + [_vp, ctypes.c_size_t, _vp],
+    "cyfa_gate_act_fwd": [_vp, ctypes.c_longlong] * 3 + [_vp] * 5 + [_i, _i, _vp],
+    "cyfa_gate_act_bwd": [_vp, ctypes.c_longlong] * 3 + [_vp] * 5
+    + [_vp, ctypes.c_longlong] * 3 + [_vp, _vp, _i, _i, _vp, ctypes.c_size_t, _vp],
+    "cyfa_gated_norm_fwd": [_vp, _vp, _vp, _f, _f, _vp, _vp, _i, _i, _vp],
+    "cyfa_gated_norm_bwd": [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp,
+                            ctypes.c_size_t, _vp],
     "cyfa_chunk_bwd": [_vp, _vp, ctypes.c_size_t, _vp, ctypes.c_size_t, _vp],
 }
 
@@ -35,6 +44,9 @@ _SIGNATURES = {
 _SIZE_QUERIES = {
     "cyfa_chunk_saved_bytes": [_i] * 5,
     "cyfa_chunk_work_bytes": [_i] * 5,
+    "cyfa_short_conv_work_bytes": [_i] * 4,
+    "cyfa_gate_act_work_bytes": [_i] * 2,
+    "cyfa_gated_norm_work_bytes": [_i] * 2,
 }
 
 

@@ -16,6 +16,13 @@ import torch.nn.functional as F
 from torch import nn
 
 from ..ops import chunk_cyfa, fused_recurrent_cyfa
+from ..ops.chunk import readout_table
+from ..ops.layer_ops import (
+    ChunkCyfaPackedFunction,
+    GateActFunction,
+    GatedNormFunction,
+    ShortConvFunction,
+)
 
 
 class RMSNorm(nn.Module):
@@ -131,7 +138,60 @@ class CyclicFlowAttention(nn.Module):
             p.data = p.data.float() if keep else p.data.bfloat16()
         return self
 
+    def _fused_ok(self, x, cache, attention_mask):
+        return (
+            cache is None
+            and attention_mask is None
+            and x.is_cuda
+            and x.dtype == torch.bfloat16
+            and self.q_proj.weight.dtype == torch.bfloat16
+            and self.use_short_conv
+            and self.q_conv1d.width <= 4
+            and self.q_conv1d.bias is None
+            and self.num_slots == 128
+            and self.head_k_dim in (128, 256)
+            and self.head_v_dim in (128, 256)
+            and (self.training or x.shape[1] > 1 or torch.is_grad_enabled())
+        )
+
+    def _forward_fused(self, x, use_cache):
+        """One packed q|k|v GEMM, one short-conv kernel over all 3 projections,
+        one auxiliary GEMM for the output gate and the a/b gates, and the CyFA op
+        on the packed buffer; the same math as the reference execute()."""
+        B, T, _ = x.shape
+        H, K, V = self.num_heads, self.head_k_dim, self.head_v_dim
+        w_qkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight])
+        qkv = F.linear(x, w_qkv)
+        g0 = self.g_proj[0]
+        w_aux = torch.cat([g0.weight, self.a_proj.weight, self.b_proj.weight])
+        b_aux = torch.cat([torch.zeros(V + H, device=x.device, dtype=self.b_proj.bias.dtype),
+                           self.b_proj.bias])
+        aux = F.linear(x, w_aux, b_aux)
+        dlin = F.linear(x.detach(), self.d_proj.weight, self.d_proj.bias)
+        conv_w = torch.cat([self.q_conv1d.weight, self.k_conv1d.weight, self.v_conv1d.weight])
+        qkv = ShortConvFunction.apply(qkv, conv_w, None)
+        g, delta, beta = GateActFunction.apply(aux, dlin, self.A_log, self.dt_bias, V, V + H, H)
+        table = readout_table(self.readout)
+        o, hk, hv, clock = ChunkCyfaPackedFunction.apply(
+            qkv, H, K, V, g, delta, beta, table, self.q_norm.weight.float(),
+            self.k_norm.weight.float(), float(self.q_norm.eps), float(self.k_norm.eps), K ** -0.5)
+        gate = self.g_proj[1](aux[..., :V])
+        y = GatedNormFunction.apply(o, gate, self.o_norm.weight, self.o_norm.eps,
+                                    float(self.num_slots - 1))
+        y = self.o_proj(y)
+        new_cache = None
+        if use_cache:
+            W = self.q_conv1d.width
+            # conv histories: the last W-1 projected (pre-conv) rows of q, k and v
+            pre = F.linear(x[:, -(W - 1):], w_qkv) if W > 1 else x[:, :0]
+            cq, ck, cv = (pre[..., :H * K], pre[..., H * K:2 * H * K], pre[..., 2 * H * K:]) \
+                if W > 1 else (pre, pre, pre)
+            new_cache = {"recurrent_state": (hk, hv, clock), "conv_state": (cq, ck, cv)}
+        return y, new_cache
+
     def forward(self, x, cache=None, use_cache=False, attention_mask=None):
+        if self._fused_ok(x, cache, attention_mask):
+            return self._forward_fused(x, use_cache)
         B, T, _ = x.shape
         H = self.num_heads
         q, k, v = self.q_proj(x), self.k_proj(x), self.v_proj(x)

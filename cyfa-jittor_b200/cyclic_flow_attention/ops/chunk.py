@@ -22,14 +22,16 @@ class _FwdArgs(_c.Structure):
         [(n, _c.c_float) for n in ("q_eps", "k_eps", "scale")] + \
         [(n, _c.c_void_p) for n in ("q", "k", "v", "g", "delta", "beta", "q_norm_weight",
                                      "k_norm_weight", "table_bf", "hk0", "hv0", "clock0",
-                                     "o", "hk", "hv", "clock")]
+                                     "o", "hk", "hv", "clock")] + \
+        [(n, _c.c_longlong) for n in ("q_stride", "k_stride", "v_stride")]
 
 
 class _BwdArgs(_c.Structure):
     _fields_ = [("fwd", _FwdArgs)] + \
         [(n, _c.c_void_p) for n in ("d_o", "dhk", "dhv", "dclock", "dq", "dk", "dv", "dg",
                                      "ddelta", "dbeta", "dtable", "dq_norm_weight",
-                                     "dk_norm_weight", "dhk0", "dhv0", "dclock0")]
+                                     "dk_norm_weight", "dhk0", "dhv0", "dclock0")] + \
+        [(n, _c.c_longlong) for n in ("dq_stride", "dk_stride", "dv_stride")]
 
 
 _BASIS = {}

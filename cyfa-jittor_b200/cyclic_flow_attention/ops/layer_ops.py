@@ -1,0 +1,206 @@
+"""Autograd wrappers of the layer glue kernels and of the chunk op on a packed
+q|k|v projection, used by the layer's fused training/prefill path.
+
+All compute runs in libcyfa.so; these wrappers allocate outputs and work
+buffers and pass raw pointers.
+"""
+
+import ctypes
+
+import torch
+
+from .. import _lib
+from .chunk import _BwdArgs, _FwdArgs, _p, _table_bf
+
+_c = ctypes
+
+
+def _work(nbytes, dev):
+    return torch.empty(max(int(nbytes), 1), device=dev, dtype=torch.uint8)
+
+
+class ShortConvFunction(torch.autograd.Function):
+    """Causal depthwise conv (no activation) of x [B,T,C] bf16 with weight [C,1,W]."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):
+        B, T, C = x.shape
+        W = weight.shape[-1]
+        w = weight.detach().float().reshape(C, W).contiguous()
+        b = None if bias is None else bias.detach().float().contiguous()
+        y = torch.empty(B, T, C, device=x.device, dtype=torch.bfloat16)
+        _lib.call("cyfa_short_conv_fwd", _p(x), _c.c_longlong(x.stride(1)), None, _p(w), _p(b),
+                  _p(y), B, T, C, W, _lib.stream())
+        ctx.save_for_backward(x, w)
+        ctx.meta = (W, weight.dtype, bias is not None, None if bias is None else bias.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        W, wdt, has_bias, bdt = ctx.meta
+        B, T, C = x.shape
+        dy = dy.to(torch.bfloat16).contiguous()
+        dx = torch.empty(B, T, C, device=x.device, dtype=torch.bfloat16)
+        dw = torch.empty(C, W, device=x.device, dtype=torch.float32)
+        db = torch.empty(C, device=x.device, dtype=torch.float32) if has_bias else None
+        nbytes = _lib.lib().cyfa_short_conv_work_bytes(B, T, C, W)
+        work = _work(nbytes, x.device)
+        _lib.call("cyfa_short_conv_bwd", _p(x), _c.c_longlong(x.stride(1)), _p(w), _p(dy), _p(dx),
+                  _c.c_longlong(C), _p(dw), _p(db), B, T, C, W, _p(work), _c.c_size_t(nbytes),
+                  _lib.stream())
+        return dx, dw.reshape(C, 1, W).to(wdt), None if db is None else db.to(bdt)
+
+
+class GateActFunction(torch.autograd.Function):
+    """(g, delta, beta) from the packed auxiliary projection `aux` (a at column
+    a_col, b at b_col, H columns each) and the d projection `dlin` [B,T,H]."""
+
+    @staticmethod
+    def forward(ctx, aux, dlin, A_log, dt_bias, a_col, b_col, H):
+        B, T, _ = aux.shape
+        rows = B * T
+        dev = aux.device
+        A = A_log.detach().float().contiguous()
+        dt = dt_bias.detach().float().contiguous()
+        g = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+        delta = torch.empty_like(g)
+        beta = torch.empty_like(g)
+        st = _c.c_longlong(aux.stride(1))
+        _lib.call("cyfa_gate_act_fwd", _c.c_void_p(aux.data_ptr() + 2 * a_col), st,
+                  _c.c_void_p(aux.data_ptr() + 2 * b_col), st, _p(dlin),
+                  _c.c_longlong(dlin.stride(1)), _p(A), _p(dt), _p(g), _p(delta), _p(beta), rows,
+                  H, _lib.stream())
+        ctx.save_for_backward(aux, dlin, A, dt)
+        ctx.meta = (a_col, b_col, H, A_log.dtype, dt_bias.dtype)
+        return g, delta, beta
+
+    @staticmethod
+    def backward(ctx, dg, ddelta, dbeta):
+        aux, dlin, A, dt = ctx.saved_tensors
+        a_col, b_col, H, adt, ddt = ctx.meta
+        B, T, width = aux.shape
+        rows = B * T
+        dev = aux.device
+        zeros = lambda: torch.zeros(B, T, H, device=dev, dtype=torch.float32)
+        dg = zeros() if dg is None else dg.float().contiguous()
+        ddelta = zeros() if ddelta is None else ddelta.float().contiguous()
+        dbeta = zeros() if dbeta is None else dbeta.float().contiguous()
+        daux = torch.zeros(B, T, width, device=dev, dtype=torch.bfloat16)
+        dd = torch.empty(B, T, H, device=dev, dtype=torch.bfloat16)
+        dA = torch.empty(H, device=dev, dtype=torch.float32)
+        ddtb = torch.empty(H, device=dev, dtype=torch.float32)
+        nbytes = _lib.lib().cyfa_gate_act_work_bytes(rows, H)
+        work = _work(nbytes, dev)
+        st = _c.c_longlong(aux.stride(1))
+        _lib.call("cyfa_gate_act_bwd", _c.c_void_p(aux.data_ptr() + 2 * a_col), st,
+                  _c.c_void_p(aux.data_ptr() + 2 * b_col), st, _p(dlin),
+                  _c.c_longlong(dlin.stride(1)), _p(A), _p(dt), _p(dg), _p(ddelta), _p(dbeta),
+                  _c.c_void_p(daux.data_ptr() + 2 * a_col), _c.c_longlong(width),
+                  _c.c_void_p(daux.data_ptr() + 2 * b_col), _c.c_longlong(width), _p(dd),
+                  _c.c_longlong(H), _p(dA), _p(ddtb), rows, H, _p(work), _c.c_size_t(nbytes),
+                  _lib.stream())
+        return daux, dd, dA.to(adt), ddtb.to(ddt), None, None, None
+
+
+class GatedNormFunction(torch.autograd.Function):
+    """y = RMSNorm(scale * x) * w * sigmoid(gate) over the last dim D of
+    x [B,T,H,D] and gate [B,T,H*D]; returns [B,T,H*D] bf16."""
+
+    @staticmethod
+    def forward(ctx, x, gate, weight, eps, scale):
+        B, T, H, D = x.shape
+        rows = B * T * H
+        x = x.to(torch.bfloat16).contiguous()
+        gate = gate.to(torch.bfloat16).contiguous()
+        w = weight.detach().float().contiguous()
+        y = torch.empty(B, T, H * D, device=x.device, dtype=torch.bfloat16)
+        rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
+        _lib.call("cyfa_gated_norm_fwd", _p(x), _p(gate), _p(w), float(eps), float(scale), _p(y),
+                  _p(rstd), rows, D, _lib.stream())
+        ctx.save_for_backward(x, gate, w, rstd)
+        ctx.meta = (scale, weight.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, gate, w, rstd = ctx.saved_tensors
+        scale, wdt = ctx.meta
+        B, T, H, D = x.shape
+        rows = B * T * H
+        dy = dy.to(torch.bfloat16).contiguous()
+        dx = torch.empty_like(x)
+        dgate = torch.empty_like(gate)
+        dw = torch.empty(D, device=x.device, dtype=torch.float32)
+        nbytes = _lib.lib().cyfa_gated_norm_work_bytes(rows, D)
+        work = _work(nbytes, x.device)
+        _lib.call("cyfa_gated_norm_bwd", _p(x), _p(gate), _p(w), float(scale), _p(rstd), _p(dy),
+                  _p(dx), _p(dgate), _p(dw), rows, D, _p(work), _c.c_size_t(nbytes),
+                  _lib.stream())
+        return dx, dgate, dw.to(wdt), None, None
+
+
+class ChunkCyfaPackedFunction(torch.autograd.Function):
+    """chunk_cyfa on q|k|v packed in one [B,T,H*K + H*K + H*V] bf16 tensor (the
+    projection + short-conv output); the gradient comes back in the same
+    packed layout."""
+
+    @staticmethod
+    def forward(ctx, qkv, H, K, V, g, delta, beta, table, qw, kw, q_eps, k_eps, scale):
+        B, T, width = qkv.shape
+        dev = qkv.device
+        row = qkv.stride(1)
+        base = qkv.data_ptr()
+        tb = _table_bf(table)
+        o = torch.empty(B, T, H, V, device=dev, dtype=torch.bfloat16)
+        hk = torch.empty(B, H, K, 128, device=dev, dtype=torch.float32)
+        hv = torch.empty(B, H, 128, V, device=dev, dtype=torch.float32)
+        clock = torch.empty(B, H, device=dev, dtype=torch.float32)
+        nbytes = _lib.lib().cyfa_chunk_saved_bytes(B, T, H, K, V)
+        if nbytes == 0:
+            raise ValueError(f"unsupported chunk_cyfa shape B={B} T={T} H={H} K={K} V={V}")
+        saved = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+        qp, kp, vp = base, base + 2 * H * K, base + 4 * H * K
+        args = _FwdArgs(B, T, H, K, V, q_eps, k_eps, scale, qp, kp, vp, _p(g), _p(delta),
+                        _p(beta), _p(qw), _p(kw), _p(tb), None, None, None, _p(o), _p(hk),
+                        _p(hv), _p(clock), row, row, row)
+        _lib.call("cyfa_chunk_fwd", _c.byref(args), _lib.ptr(saved), _c.c_size_t(nbytes),
+                  _lib.stream())
+        ctx.save_for_backward(qkv, g, delta, beta, qw, kw, tb, hk, hv, clock, saved)
+        ctx.meta = (H, K, V, q_eps, k_eps, scale)
+        return o, hk, hv, clock
+
+    @staticmethod
+    def backward(ctx, do, dhk, dhv, dclock):
+        qkv, g, delta, beta, qw, kw, tb, hk, hv, clock, saved = ctx.saved_tensors
+        H, K, V, q_eps, k_eps, scale = ctx.meta
+        B, T, width = qkv.shape
+        dev = qkv.device
+        row = qkv.stride(1)
+        base = qkv.data_ptr()
+        qp, kp, vp = base, base + 2 * H * K, base + 4 * H * K
+        fwd = _FwdArgs(B, T, H, K, V, q_eps, k_eps, scale, qp, kp, vp, _p(g), _p(delta),
+                       _p(beta), _p(qw), _p(kw), _p(tb), None, None, None, None, _p(hk), _p(hv),
+                       _p(clock), row, row, row)
+        do = torch.zeros(B, T, H, V, device=dev, dtype=torch.bfloat16) if do is None \
+            else do.to(torch.bfloat16).contiguous()
+        dhk = None if dhk is None else dhk.float().contiguous()
+        dhv = None if dhv is None else dhv.float().contiguous()
+        dclock = None if dclock is None else dclock.float().contiguous()
+        dqkv = torch.empty(B, T, width, device=dev, dtype=torch.bfloat16)
+        db_ = dqkv.data_ptr()
+        dg = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+        ddelta = torch.empty_like(dg)
+        dbeta = torch.empty_like(dg)
+        dtable = torch.empty(H, 128, 128, device=dev, dtype=torch.float32)
+        dqw = torch.empty(K, device=dev, dtype=torch.float32)
+        dkw = torch.empty(K, device=dev, dtype=torch.float32)
+        nwork = _lib.lib().cyfa_chunk_work_bytes(B, T, H, K, V)
+        work = _work(nwork, dev)
+        args = _BwdArgs(fwd, _p(do), _p(dhk), _p(dhv), _p(dclock), db_, db_ + 2 * H * K,
+                        db_ + 4 * H * K, _p(dg), _p(ddelta), _p(dbeta), _p(dtable), _p(dqw),
+                        _p(dkw), None, None, None, width, width, width)
+        _lib.call("cyfa_chunk_bwd", _c.byref(args), _lib.ptr(saved), _c.c_size_t(saved.numel()),
+                  _lib.ptr(work), _c.c_size_t(nwork), _lib.stream())
+        return (dqkv, None, None, None, dg, ddelta, dbeta, dtable[:, :127], dqw, dkw, None,
+                None, None)

@@ -92,7 +92,7 @@ int cyfa_token_fwd(const void* q, const void* k, const float* q_norm_weight,
 /* ---------------------------------------------------------------- backward prep
  * Adjoint of cyfa_token_fwd.  dqn/dkn [B,H,TP,K] f32, dw [B,H,TP,128] f32 in;
  * dq/dk public-layout bf16, norm-weight partial sums
- * [min(ceil(B*H*TP/8), 1184), K] f32 (sum the rows for the weight gradient),
+ * [min(ceil(B*H*TP/8), 296), K] f32 (sum the rows for the weight gradient),
  * dlam (write-vector part) and dbeta_h [B,H,TP] f32 out.
  * Replaces: VectorNorm.grad (ops/qk_norm.py:109-165), PhaseWriteOnly.grad
  * (ops/utils.py:589-640). */
@@ -119,7 +119,9 @@ int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h,
  * output_forward (ops/chunk_o.py:394-613).  K in {128, 256}, V in {128, 256},
  * 128 slot rows.  The caller owns `saved` (cyfa_chunk_saved_bytes) and keeps it
  * for cyfa_chunk_bwd; the final state outputs are always written because the
- * backward pass reads them. */
+ * backward pass reads them.  q, k and v may be column slices of wider rows (a
+ * packed projection output): their token strides are given in elements (multiples
+ * of 8, >= the row width; 0 = dense). */
 typedef struct {
   int B, T, H, K, V;
   float q_eps, k_eps, scale;
@@ -139,6 +141,9 @@ typedef struct {
   float* hk;                    /* out [B,H,K,128] final key state */
   float* hv;                    /* out [B,H,128,V] final value state */
   float* clock;                 /* out [B,H] final clock */
+  long long q_stride;           /* elements between consecutive tokens of q (0 = H*K) */
+  long long k_stride;           /* ... of k (0 = H*K) */
+  long long v_stride;           /* ... of v (0 = H*V) */
 } cyfa_chunk_fwd_args;
 
 size_t cyfa_chunk_saved_bytes(int B, int T, int H, int K, int V);
@@ -176,12 +181,62 @@ typedef struct {
   float* dhk0;                  /* out [B,H,K,128] or NULL */
   float* dhv0;                  /* out [B,H,128,V] or NULL */
   float* dclock0;               /* out [B,H] or NULL */
+  long long dq_stride;          /* token stride of dq (0 = H*K) */
+  long long dk_stride;          /* token stride of dk (0 = H*K) */
+  long long dv_stride;          /* token stride of dv (0 = H*V) */
 } cyfa_chunk_bwd_args;
 
 size_t cyfa_chunk_work_bytes(int B, int T, int H, int K, int V);
 
 int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* args, const void* saved, size_t saved_bytes,
                    void* work, size_t work_bytes, void* stream);
+
+/* ---------------------------------------------------------------- layer glue
+ * Causal depthwise short convolution without activation.
+ * Replaces: ShortConvolution (cyclic_flow_attention/layers/cyfa.py:138-233).
+ * x [B,T,C] bf16 with token stride x_stride (elements); cache [B,W-1,C] bf16 (the
+ * history before t = 0) or NULL for zeros; w [C,W] f32; bias [C] f32 or NULL;
+ * y [B,T,C] bf16 dense.  C % 8 == 0, 1 <= W <= 4. */
+int cyfa_short_conv_fwd(const void* x, long long x_stride, const void* cache, const float* w,
+                        const float* bias, void* y, int B, int T, int C, int W, void* stream);
+
+size_t cyfa_short_conv_work_bytes(int B, int T, int C, int W);
+
+/* Adjoint of cyfa_short_conv_fwd without cache: dy [B,T,C] bf16 dense -> dx (token
+ * stride dx_stride), dw [C,W] f32 and dbias [C] f32 (or NULL). */
+int cyfa_short_conv_bwd(const void* x, long long x_stride, const float* w, const void* dy,
+                        void* dx, long long dx_stride, float* dw, float* dbias, int B, int T,
+                        int C, int W, void* work, size_t work_bytes, void* stream);
+
+/* Gate activations of the layer: g = -exp(A_log) softplus(a + dt_bias),
+ * delta = sigmoid(d), beta = sigmoid(b), all [rows, H] f32 out; a, b, d are bf16
+ * projection outputs with token strides.  Replaces layers/cyfa.py:323-326. */
+int cyfa_gate_act_fwd(const void* a, long long a_stride, const void* b, long long b_stride,
+                      const void* d, long long d_stride, const float* A_log,
+                      const float* dt_bias, float* g, float* delta, float* beta, int rows, int H,
+                      void* stream);
+
+size_t cyfa_gate_act_work_bytes(int rows, int H);
+
+int cyfa_gate_act_bwd(const void* a, long long a_stride, const void* b, long long b_stride,
+                      const void* d, long long d_stride, const float* A_log,
+                      const float* dt_bias, const float* dg, const float* ddelta,
+                      const float* dbeta, void* da, long long da_stride, void* db,
+                      long long db_stride, void* dd, long long dd_stride, float* dA_log,
+                      float* ddt_bias, int rows, int H, void* work, size_t work_bytes,
+                      void* stream);
+
+/* Gated output norm: y = RMSNorm(scale * x) * w * sigmoid(gate) over rows of D
+ * (x, gate, y [rows, D] bf16; rstd [rows] f32 saved for the backward).
+ * Replaces: o_norm(o * (num_slots - 1), gate) (layers/cyfa.py:350, RMSNorm :62-135). */
+int cyfa_gated_norm_fwd(const void* x, const void* gate, const float* w, float eps, float scale,
+                        void* y, float* rstd, int rows, int D, void* stream);
+
+size_t cyfa_gated_norm_work_bytes(int rows, int D);
+
+int cyfa_gated_norm_bwd(const void* x, const void* gate, const float* w, float scale,
+                        const float* rstd, const void* dy, void* dx, void* dgate, float* dw,
+                        int rows, int D, void* work, size_t work_bytes, void* stream);
 
 /* ---------------------------------------------------------------- self test
  * C[128,N] = A * B through TMA + tcgen05 (test hook for the UMMA descriptor and

@@ -1,0 +1,93 @@
+"""GPU parity of the layer glue kernels (short conv, gate activations, gated
+output norm) against plain fp32 torch references with autograd."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from gpu_util import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def LO():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+    from cyclic_flow_attention.ops import layer_ops
+
+    return layer_ops
+
+
+def _conv_ref(x, w, b=None):
+    B, T, C = x.shape
+    W = w.shape[-1]
+    y = F.conv1d(F.pad(x.transpose(1, 2), (W - 1, 0)), w, b, groups=C)
+    return y.transpose(1, 2)
+
+
+@pytest.mark.parametrize("B,T,C,W", [(2, 300, 256, 4), (1, 128, 3072, 4), (2, 17, 64, 3)])
+def test_short_conv(LO, B, T, C, W):
+    gen = torch.Generator().manual_seed(T + C)
+    x = torch.randn(B, T, C, generator=gen).to(torch.bfloat16).cuda().requires_grad_(True)
+    w = (0.3 * torch.randn(C, 1, W, generator=gen)).cuda().requires_grad_(True)
+    dy = torch.randn(B, T, C, generator=gen).cuda()
+    y = LO.ShortConvFunction.apply(x, w, None)
+    (y.float() * dy).sum().backward()
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.detach().clone().requires_grad_(True)
+    yr = _conv_ref(xr, wr)
+    (yr * dy).sum().backward()
+    assert rel_l2(y, yr) < 1e-2
+    assert rel_l2(x.grad, xr.grad) < 1e-2
+    assert rel_l2(w.grad, wr.grad) < 1e-2  # dy enters in bf16
+
+
+def test_gate_act(LO):
+    B, T, H, width = 2, 100, 4, 264
+    gen = torch.Generator().manual_seed(7)
+    aux = torch.randn(B, T, width, generator=gen).to(torch.bfloat16).cuda().requires_grad_(True)
+    dlin = torch.randn(B, T, H, generator=gen).to(torch.bfloat16).cuda().requires_grad_(True)
+    A_log = torch.log(torch.rand(H, generator=gen) * 16 + 1e-3).cuda().requires_grad_(True)
+    dt = (torch.randn(H, generator=gen) - 4).cuda().requires_grad_(True)
+    a_col, b_col = 256, 260
+    g, d, b = LO.GateActFunction.apply(aux, dlin, A_log, dt, a_col, b_col, H)
+    ups = [torch.randn(B, T, H, generator=gen).cuda() for _ in range(3)]
+    sum((x * u).sum() for x, u in zip((g, d, b), ups)).backward()
+    auxr = aux.detach().float().requires_grad_(True)
+    dlr = dlin.detach().float().requires_grad_(True)
+    Ar = A_log.detach().clone().requires_grad_(True)
+    dtr = dt.detach().clone().requires_grad_(True)
+    gr = -Ar.exp() * F.softplus(auxr[..., a_col:a_col + H] + dtr)
+    drr = torch.sigmoid(dlr)
+    brr = torch.sigmoid(auxr[..., b_col:b_col + H])
+    sum((x * u).sum() for x, u in zip((gr, drr, brr), ups)).backward()
+    for a_, b_ in zip((g, d, b), (gr, drr, brr)):
+        assert rel_l2(a_, b_) < 1e-5
+    assert rel_l2(aux.grad, auxr.grad) < 1e-2
+    assert rel_l2(dlin.grad, dlr.grad) < 1e-2
+    assert rel_l2(A_log.grad, Ar.grad) < 1e-4
+    assert rel_l2(dt.grad, dtr.grad) < 1e-4
+
+
+@pytest.mark.parametrize("D", [256, 128])
+def test_gated_norm(LO, D):
+    B, T, H = 2, 70, 3
+    gen = torch.Generator().manual_seed(D)
+    x = (0.01 * torch.randn(B, T, H, D, generator=gen)).to(torch.bfloat16).cuda().requires_grad_(True)
+    gate = torch.randn(B, T, H * D, generator=gen).to(torch.bfloat16).cuda().requires_grad_(True)
+    w = (1 + 0.1 * torch.randn(D, generator=gen)).cuda().requires_grad_(True)
+    dy = torch.randn(B, T, H * D, generator=gen).cuda()
+    y = LO.GatedNormFunction.apply(x, gate, w, 1e-6, 127.0)
+    (y.float() * dy).sum().backward()
+    xr = x.detach().float().requires_grad_(True)
+    gr = gate.detach().float().requires_grad_(True)
+    wr = w.detach().clone().requires_grad_(True)
+    u = xr * 127.0
+    yr = u * torch.rsqrt(u.pow(2).mean(-1, keepdim=True) + 1e-6) * wr
+    yr = (yr * torch.sigmoid(gr.reshape(B, T, H, D))).reshape(B, T, H * D)
+    (yr * dy).sum().backward()
+    assert rel_l2(y, yr) < 1e-2
+    assert rel_l2(x.grad, xr.grad) < 1e-2
+    assert rel_l2(gate.grad, gr.grad) < 1e-2
+    assert rel_l2(w.grad, wr.grad) < 1e-2  # dy enters in bf16
