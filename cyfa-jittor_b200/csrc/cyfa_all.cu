@@ -11,3 +11,4 @@
 #include "capi.cu"
 #include "chunk_api.cu"
 #include "layer_api.cu"
+#include "noalloc.cu"

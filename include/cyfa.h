@@ -238,6 +238,20 @@ int cyfa_gated_norm_bwd(const void* x, const void* gate, const float* w, float s
                         const float* rstd, const void* dy, void* dx, void* dgate, float* dw,
                         int rows, int D, void* work, size_t work_bytes, void* stream);
 
+/* Allocation-free variant of cyfa_gated_norm_bwd, for callers that cannot hand the
+ * library a workspace: bindings whose signature carries only the op's tensors, or
+ * processes whose device memory belongs entirely to a framework allocator.  No
+ * counterpart in the reference.  The weight-gradient partials live in a fixed
+ * device array inside the library (296 KiB, held on every GPU that loads the
+ * library until exit) instead of a caller buffer; D in {128, 256}, any rows.
+ * The first call on each device looks up that array's device address
+ * (cudaGetSymbolAddress); make the first call before any stream capture.  All
+ * calls share the array: each call overwrites what it reads, but calls whose
+ * kernels overlap on the GPU race.  Calls no allocator. */
+int cyfa_gated_norm_bwd_static(const void* x, const void* gate, const float* w, float scale,
+                               const float* rstd, const void* dy, void* dx, void* dgate,
+                               float* dw, int rows, int D, void* stream);
+
 /* ---------------------------------------------------------------- self test
  * C[128,N] = A * B through TMA + tcgen05 (test hook for the UMMA descriptor and
  * swizzle encodings).  A is [128,K] (a_mn = 0) or [K,128] (a_mn = 1); B is [N,K]
