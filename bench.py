@@ -76,7 +76,7 @@ def _traffic_from_profiles(kernel):
         with open(path) as f:
             for line in f:
                 parts = line.split()
-                if len(parts) >= 2 and parts[0] == kernel:
+                if len(parts) >= 2 and not line.startswith("#") and parts[0] == kernel:
                     return float(parts[1])
     except OSError:
         pass
@@ -204,12 +204,82 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- decode leg
+DECODE = dict(layers=24, batch=256, heads=8, head_dim=256, slots=128)
+
+
+def measure_decode(args, rank, world, dev, peaks, barrier):
+    """One decode token step of the attention cores of BASELINE configs[3]
+    (24 layers, batch 256 sharded over the ranks, 8 x 256 heads, fp32 states):
+    24 calls of cyfa_decode_step (in place).  Reports tokens/s of the cores and
+    the decode kernel's achieved HBM bandwidth."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from cyclic_flow_attention import _lib
+    from cyclic_flow_attention.ops.chunk import readout_table
+
+    Ly, H, K = DECODE["layers"], DECODE["heads"], DECODE["head_dim"]
+    B = DECODE["batch"] // world
+    gen = torch.Generator(device=dev).manual_seed(7 + rank)
+    states = [(0.01 * torch.randn(B, H, K, 128, device=dev, generator=gen),
+               0.01 * torch.randn(B, H, 128, K, device=dev, generator=gen),
+               torch.zeros(B, H, device=dev)) for _ in range(Ly)]
+    tables = [readout_table(torch.eye(127, device=dev).expand(H, -1, -1).contiguous())
+              .contiguous() for _ in range(Ly)]
+    q = torch.randn(B, 1, H, K, device=dev, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, 1, H, K, device=dev, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, 1, H, K, device=dev, generator=gen).to(torch.bfloat16)
+    g = torch.full((B, 1, H), -0.05, device=dev)
+    delta = torch.full((B, 1, H), 0.5, device=dev)
+    beta = torch.full((B, 1, H), 0.5, device=dev)
+    w = torch.ones(K, device=dev)
+    out = torch.empty(B, 1, H, K, device=dev, dtype=torch.bfloat16)
+    P = _lib.ptr
+    stream = _lib.stream()
+
+    def token_step():
+        for (hk, hv, ck), tab in zip(states, tables):
+            _lib.call("cyfa_decode_step", P(q), P(k), P(v), P(g), P(delta), P(beta), P(tab),
+                      P(w), P(w), P(hk), P(hv), P(ck), P(hk), P(hv), P(ck), P(out),
+                      B, H, K, K, 0, 1e-6, 1e-6, K ** -0.5, stream)
+
+    for _ in range(3):
+        token_step()
+    barrier()
+    n = max(3, min(args.steps, 10))
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(n):
+        token_step()
+    b.record()
+    barrier()
+    t = torch.tensor([a.elapsed_time(b) / n], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    per_bh = 2 * (K * 128 + 128 * K) * 4 + (2 * K + 2 * K) * 2 + 12
+    nbytes = Ly * B * H * per_bh
+    gbs = nbytes / (ms / 1000.0) / 1e9
+    peak = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+    del states
+    torch.cuda.empty_cache()
+    return {"workload": "decode token step of the attention cores, BASELINE configs[3] "
+                        "(24 layers, batch 256 over the ranks, 8x256 heads, fp32 states)",
+            "tokens_per_s": world * B / (ms / 1000.0), "ms_per_token_step": ms,
+            "bytes_per_step": nbytes * world, "achieved_gbs_per_gpu": gbs,
+            "hbm_peak_gbs": peak, "frac": gbs / peak}
+
+
 # ---------------------------------------------------------------- GPU arm
 def run_cyfa(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
 
     from cyclic_flow_attention import CyclicFlowAttention, _lib
+    from cyclic_flow_attention.distributed import allreduce_gradients
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -228,16 +298,11 @@ def run_cyfa(args, rank, world, local_rank):
     x = x_host.to(dev)
     dy = dy_host.to(dev)
     flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+    peaks, peak_kind = _peaks()
 
     def allreduce_grads():
         if world > 1:
-            flat = torch.cat([p.grad.float().reshape(-1) for p in params])
-            dist.all_reduce(flat, op=dist.ReduceOp.AVG)
-            off = 0
-            for p in params:
-                n = p.numel()
-                p.grad.copy_(flat[off:off + n].view_as(p.grad))
-                off += n
+            allreduce_gradients(params)
 
     def step(xin, dyin):
         # training step with the objective loss = <y, dy>: dL/dy = dy
@@ -281,14 +346,36 @@ def run_cyfa(args, rank, world, local_rank):
     ms_per_step = t.item() / args.steps
     value = world * B * T / (ms_per_step / 1000.0)
 
-    # ---- end to end: pinned host inputs copied in, loss read back, every step
+    # ---- end to end: every step copies its inputs from pinned host memory and
+    # reads its loss back.  The next step's copy runs on a side stream while the
+    # current step computes (double-buffered device inputs), as a data loader would.
+    copy_stream = torch.cuda.Stream(device=dev)
+    bufs = [(torch.empty_like(x), torch.empty_like(dy)) for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+    main = torch.cuda.current_stream(dev)
+
+    def start_copy(i):
+        b = i % 2
+        copy_stream.wait_event(done[b])
+        with torch.cuda.stream(copy_stream):
+            bufs[b][0].copy_(x_host, non_blocking=True)
+            bufs[b][1].copy_(dy_host, non_blocking=True)
+            copied[b].record(copy_stream)
+
+    for b in range(2):
+        done[b].record(main)
     e_a, e_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     e_a.record()
-    for _ in range(args.steps):
-        xi = x_host.to(dev, non_blocking=True)
-        di = dy_host.to(dev, non_blocking=True)
-        loss = step(xi, di)
+    start_copy(0)
+    for i in range(args.steps):
+        b = i % 2
+        main.wait_event(copied[b])
+        if i + 1 < args.steps:
+            start_copy(i + 1)
+        loss = step(bufs[b][0], bufs[b][1])
+        done[b].record(main)
         loss.item()
     e_b.record()
     barrier()
@@ -298,7 +385,8 @@ def run_cyfa(args, rank, world, local_rank):
     e2e_ms = te.item() / args.steps
     e2e = {"value": world * B * T / (e2e_ms / 1000.0), "unit": UNIT,
            "h2d_bytes_per_step": x_host.numel() * 2 + dy_host.numel() * 2,
-           "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms}
+           "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms,
+           "note": "H2D of step i+1 overlaps step i on a copy stream; loss read back each step"}
 
     # ---- per-kernel event timing of one step (separate pass) -> dominant kernel
     barrier()
@@ -308,7 +396,6 @@ def run_cyfa(args, rank, world, local_rank):
     torch.cuda.synchronize()
     prof = _lib.profile_report()
     _lib.profile_enable(False)
-    peaks, peak_kind = _peaks()
     tiles = B * CFG["heads"] * math.ceil(T / 128)
     flops = _tile_flops(CFG["head_dim"], CFG["head_dim"])
     roofline = None
@@ -324,6 +411,8 @@ def run_cyfa(args, rank, world, local_rank):
                     "peak_kind": f"{peak_kind} bf16 sustained",
                     "launches_per_step": n, "ms_per_step": ms,
                     "kernel_ms": {k: round(v[0], 4) for k, v in sorted(prof.items())}}
+
+    decode = None if args.no_decode else measure_decode(args, rank, world, dev, peaks, barrier)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -345,6 +434,7 @@ def run_cyfa(args, rank, world, local_rank):
             "e2e": e2e,
             "gpu_launches": launches,
             "clocks": clocks,
+            "decode": decode,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -360,6 +450,7 @@ def main():
     ap.add_argument("--impl", choices=("cyfa", "reference"), default="cyfa")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode-kernel leg")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

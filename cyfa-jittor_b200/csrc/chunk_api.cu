@@ -81,8 +81,8 @@ static Work carve_work(const Dims& d, void* base, size_t* total) {
   w.dlam_r = c.take<float>(n);
   w.dlam_w = c.take<float>(n);
   w.dbeta_h = c.take<float>(n);
-  w.bpart1 = c.take<float>(tiles * (d.K / 128) * 2);
-  w.bpart2 = c.take<float>(tiles * (d.V / 64));
+  w.bpart1 = c.take<float>(tiles * (d.K / 128) * 2 * 4);
+  w.bpart2 = c.take<float>(tiles * (d.V / 64) * 4);
   w.dtab_part = c.take<float>(tiles * 128 * 128);
   w.dqw_part = c.take<float>(size_t(1184) * d.K);
   w.dkw_part = c.take<float>(size_t(1184) * d.K);
@@ -275,7 +275,8 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     CYFA_LAUNCH("dual_gemm", st, (dual_gemm_kernel<<<tiles, 256, kDualSmem, st>>>(x1, y1, x2, y2, p)));
     return launch_status();
   };
-  const int nsub1 = (d.K / 128) * 2, nsub2 = d.V / 64;
+  // boundary partials per tile: one per (CTA slice, warp)
+  const int nsub1 = (d.K / 128) * 2 * 4, nsub2 = (d.V / 64) * 4;
 
   // ================= pass 2 (queries = weights, keys = w, values = v)
   {

@@ -75,7 +75,7 @@ struct ScanParams {
   float scale;              // reverse: scale of dO
   const __nv_bfloat16* fwd_hist;  // reverse: forward history of the same pass
   const float* fwd_final;         // reverse: forward final state
-  float* bpart;                   // reverse: [BH, NT, nsub] partial boundary terms
+  float* bpart;                   // reverse: [BH, NT, nsub, 4] partial boundary terms
 };
 
 constexpr int kScanStages = 3;
@@ -91,7 +91,6 @@ __global__ void __launch_bounds__(128, 1)
   __shared__ __align__(8) uint64_t full[kScanStages];
   __shared__ __align__(8) uint64_t mma_done[2];
   __shared__ uint32_t tmem_base;
-  __shared__ float red[4];
   const int tid = threadIdx.x;
   const int bh = blockIdx.x, dk0 = blockIdx.y * 128, dv0 = blockIdx.z * 64;
   const int NT = p.NT;
@@ -146,12 +145,16 @@ __global__ void __launch_bounds__(128, 1)
 
   // Waits for tile idx's operands, rescales its V rows and issues its UMMA into
   // TMEM buffer idx & 1.  Returns false (on every thread) if a wait timed out.
-  auto prepare = [&](int idx) -> bool {
-    const int s = idx % kScanStages, j = tile_of(idx);
+  // gate values of a tile: (G_t of this thread's token row, G_last)
+  auto load_g = [&](int idx, float& gt, float& gl) {
+    const float* Gt = p.G + size_t(bh) * p.TP + size_t(tile_of(idx)) * 128;
+    gt = Gt[tid];
+    gl = Gt[127];
+  };
+  auto prepare = [&](int idx, float gt, float gl) -> bool {
+    const int s = idx % kScanStages;
     uint8_t* st = smem + s * kScanStageBytes;
-    const float* Gt = p.G + size_t(bh) * p.TP + size_t(j) * 128;
-    const float gt = Gt[tid];
-    const float f = REVERSE ? p.scale * exp2f(gt) : exp2f(Gt[127] - gt);
+    const float f = REVERSE ? p.scale * exp2f(gt) : exp2f(gl - gt);
     bool good = mbar_wait(&full[s], (idx / kScanStages) & 1);
     if (good) {
       const uint32_t vb = smem_u32(st + 32768);
@@ -182,10 +185,16 @@ __global__ void __launch_bounds__(128, 1)
     return true;
   };
 
-  bool ok = NT > 0 ? prepare(0) : true;
+  float g_cur_t = 0.f, g_cur_l = 0.f, g_nxt_t = 0.f, g_nxt_l = 0.f;
+  if (NT > 0) load_g(0, g_cur_t, g_cur_l);
+  if (NT > 1) load_g(1, g_nxt_t, g_nxt_l);
+  bool ok = NT > 0 ? prepare(0, g_cur_t, g_cur_l) : true;
   for (int idx = 0; idx < NT && ok; ++idx) {
     const int j = tile_of(idx);
-    const float gl = p.G[size_t(bh) * p.TP + size_t(j) * 128 + 127];
+    const float gl = g_cur_l;
+    // gate values two tiles ahead, loaded while this tile's work runs
+    float g_far_t = 0.f, g_far_l = 0.f;
+    if (idx + 2 < NT) load_g(idx + 2, g_far_t, g_far_l);
     // REVERSE: fetch S_{j+1} (this CTA's row slice) early; it is consumed below
     uint4 nxt[8];
     if constexpr (REVERSE) {
@@ -197,10 +206,13 @@ __global__ void __launch_bounds__(128, 1)
       }
     }
     // overlap: the next tile's update is independent of the running state
-    if (idx + 1 < NT && !prepare(idx + 1)) {
+    if (idx + 1 < NT && !prepare(idx + 1, g_nxt_t, g_nxt_l)) {
       ok = false;
       break;
     }
+    g_cur_l = g_nxt_l;
+    g_nxt_t = g_far_t;
+    g_nxt_l = g_far_l;
     // state entering tile j (forward) / adjoint leaving tile j (reverse)
     {
       uint4* dst = reinterpret_cast<uint4*>(p.hist + ((size_t(bh) * NT + j) * p.DK + dk0 + tid) *
@@ -232,11 +244,8 @@ __global__ void __launch_bounds__(128, 1)
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      if ((tid & 31) == 0) red[tid >> 5] = dot;
-      __syncthreads();
-      if (tid == 0)
-        p.bpart[(size_t(bh) * NT + j) * nsub + sub] = (red[0] + red[1]) + (red[2] + red[3]);
-      __syncthreads();
+      // one partial per warp: bpart[bh][j][sub][warp]
+      if ((tid & 31) == 0) p.bpart[((size_t(bh) * NT + j) * nsub + sub) * 4 + (tid >> 5)] = dot;
     }
     const bool got = mbar_wait(&mma_done[idx & 1], (idx >> 1) & 1);
     tc_fence_after();

@@ -234,6 +234,8 @@ struct GateActParams {
   long long d_stride;
   const float* A_log;      // [H]
   const float* dt_bias;    // [H]
+  const float* b_bias;     // [H] added to b, or null
+  const float* d_bias;     // [H] added to d, or null
   float* g;                // [rows, H]
   float* delta;
   float* beta;
@@ -247,7 +249,7 @@ struct GateActParams {
   long long db_stride;
   __nv_bfloat16* dd;
   long long dd_stride;
-  float* part;             // [gridDim.x, 2H]: dA_log | ddt_bias
+  float* part;             // [gridDim.x, 4H]: dA_log | ddt_bias | db_bias | dd_bias
   int rows, H;
 };
 
@@ -263,15 +265,15 @@ __global__ void __launch_bounds__(256) gate_act_fwd_kernel(GateActParams p) {
   const int h = int(i % p.H);
   const float a = __bfloat162float(p.a[r * p.a_stride + h]) + p.dt_bias[h];
   p.g[i] = -expf(p.A_log[h]) * softplus_f(a);
-  p.delta[i] = sigmoid_f(__bfloat162float(p.d[r * p.d_stride + h]));
-  p.beta[i] = sigmoid_f(__bfloat162float(p.b[r * p.b_stride + h]));
+  p.delta[i] = sigmoid_f(__bfloat162float(p.d[r * p.d_stride + h]) + (p.d_bias ? p.d_bias[h] : 0.f));
+  p.beta[i] = sigmoid_f(__bfloat162float(p.b[r * p.b_stride + h]) + (p.b_bias ? p.b_bias[h] : 0.f));
 }
 
 // One thread per (row, head); grid-strided; per-block fixed-order partial sums.
 __global__ void __launch_bounds__(256) gate_act_bwd_kernel(GateActParams p) {
-  __shared__ float red[256][2];
+  __shared__ float red[256][4];
   const int h = threadIdx.x % p.H;  // H divides 256 (checked on the host)
-  float sA = 0.f, sdt = 0.f;
+  float sA = 0.f, sdt = 0.f, sb = 0.f, sd = 0.f;
   const size_t n = size_t(p.rows) * p.H;
   for (size_t i = size_t(blockIdx.x) * 256 + threadIdx.x; i < n; i += size_t(gridDim.x) * 256) {
     const size_t r = i / p.H;
@@ -283,22 +285,29 @@ __global__ void __launch_bounds__(256) gate_act_bwd_kernel(GateActParams p) {
     sA += dgv * gv;
     sdt += da;
     p.da[r * p.da_stride + h] = __float2bfloat16_rn(da);
-    const float de = sigmoid_f(__bfloat162float(p.d[r * p.d_stride + h]));
-    p.dd[r * p.dd_stride + h] = __float2bfloat16_rn(p.ddelta[i] * de * (1.f - de));
-    const float be = sigmoid_f(__bfloat162float(p.b[r * p.b_stride + h]));
-    p.db[r * p.db_stride + h] = __float2bfloat16_rn(p.dbeta[i] * be * (1.f - be));
+    const float de = sigmoid_f(__bfloat162float(p.d[r * p.d_stride + h]) +
+                               (p.d_bias ? p.d_bias[h] : 0.f));
+    const float ddv = p.ddelta[i] * de * (1.f - de);
+    p.dd[r * p.dd_stride + h] = __float2bfloat16_rn(ddv);
+    const float be = sigmoid_f(__bfloat162float(p.b[r * p.b_stride + h]) +
+                               (p.b_bias ? p.b_bias[h] : 0.f));
+    const float dbv = p.dbeta[i] * be * (1.f - be);
+    p.db[r * p.db_stride + h] = __float2bfloat16_rn(dbv);
+    sb += dbv;
+    sd += ddv;
   }
   red[threadIdx.x][0] = sA;
   red[threadIdx.x][1] = sdt;
+  red[threadIdx.x][2] = sb;
+  red[threadIdx.x][3] = sd;
   __syncthreads();
   if (threadIdx.x < p.H) {
-    float x = 0.f, y = 0.f;
-    for (int t = threadIdx.x; t < 256; t += p.H) {
-      x += red[t][0];
-      y += red[t][1];
-    }
-    p.part[size_t(blockIdx.x) * 2 * p.H + threadIdx.x] = x;
-    p.part[size_t(blockIdx.x) * 2 * p.H + p.H + threadIdx.x] = y;
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int t = threadIdx.x; t < 256; t += p.H)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) x[k] += red[t][k];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) p.part[size_t(blockIdx.x) * 4 * p.H + k * p.H + threadIdx.x] = x[k];
   }
 }
 
@@ -427,14 +436,23 @@ __global__ void __launch_bounds__(256) conv_param_sum_kernel(const float* part, 
     dbias[c] = s;
 }
 
-// out[c] = sum_r part[r * row_stride + c] for c < cols, fixed order.
-__global__ void __launch_bounds__(256) strided_column_sum_kernel(const float* part, float* out,
-                                                                 int rows, int cols,
-                                                                 int row_stride) {
-  for (int c = threadIdx.x; c < cols; c += 256) {
+// out[c] = sum_r part[r * row_stride + c] for c < cols (small cols), fixed order:
+// 1024 threads split the rows, then a fixed-order tree over the threads.
+__global__ void __launch_bounds__(1024) strided_column_sum_kernel(const float* part, float* out,
+                                                                  int rows, int cols,
+                                                                  int row_stride) {
+  __shared__ float red[1024];
+  for (int c = 0; c < cols; ++c) {
     float s = 0.f;
-    for (int r = 0; r < rows; ++r) s += part[size_t(r) * row_stride + c];
-    out[c] = s;
+    for (int r = threadIdx.x; r < rows; r += 1024) s += part[size_t(r) * row_stride + c];
+    red[threadIdx.x] = s;
+    __syncthreads();
+    for (int w = 512; w > 0; w >>= 1) {
+      if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) out[c] = red[0];
+    __syncthreads();
   }
 }
 

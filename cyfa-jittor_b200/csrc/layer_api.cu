@@ -99,16 +99,17 @@ int cyfa_short_conv_bwd(const void* x, long long x_stride, const float* w, const
 
 int cyfa_gate_act_fwd(const void* a, long long a_stride, const void* b, long long b_stride,
                       const void* d, long long d_stride, const float* A_log,
-                      const float* dt_bias, float* g, float* delta, float* beta, int rows, int H,
-                      void* stream) {
+                      const float* dt_bias, const float* b_bias, const float* d_bias, float* g,
+                      float* delta, float* beta, int rows, int H, void* stream) {
   CYFA_REQUIRE(a && b && d && A_log && dt_bias && g && delta && beta, kNullPointer);
   CYFA_REQUIRE(rows > 0 && H > 0 && 256 % H == 0 && a_stride >= H && b_stride >= H &&
                    d_stride >= H,
                kBadShape);
   GateActParams p{static_cast<const __nv_bfloat16*>(a), a_stride,
                   static_cast<const __nv_bfloat16*>(b), b_stride,
-                  static_cast<const __nv_bfloat16*>(d), d_stride, A_log, dt_bias, g, delta, beta,
-                  nullptr, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, 0, nullptr, rows, H};
+                  static_cast<const __nv_bfloat16*>(d), d_stride, A_log, dt_bias, b_bias, d_bias, g,
+                  delta, beta, nullptr, nullptr, nullptr, nullptr, 0, nullptr, 0, nullptr, 0,
+                  nullptr, rows, H};
   const long long n = (long long)rows * H;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CYFA_LAUNCH("gate_act_fwd", s,
@@ -118,15 +119,16 @@ int cyfa_gate_act_fwd(const void* a, long long a_stride, const void* b, long lon
 
 size_t cyfa_gate_act_work_bytes(int rows, int H) {
   if (rows <= 0 || H <= 0) return 0;
-  return size_t(gate_bwd_blocks((long long)rows * H)) * 2 * H * sizeof(float);
+  return size_t(gate_bwd_blocks((long long)rows * H)) * 4 * H * sizeof(float);
 }
 
 int cyfa_gate_act_bwd(const void* a, long long a_stride, const void* b, long long b_stride,
                       const void* d, long long d_stride, const float* A_log,
-                      const float* dt_bias, const float* dg, const float* ddelta,
-                      const float* dbeta, void* da, long long da_stride, void* db,
-                      long long db_stride, void* dd, long long dd_stride, float* dA_log,
-                      float* ddt_bias, int rows, int H, void* work, size_t work_bytes,
+                      const float* dt_bias, const float* b_bias, const float* d_bias,
+                      const float* dg, const float* ddelta, const float* dbeta, void* da,
+                      long long da_stride, void* db, long long db_stride, void* dd,
+                      long long dd_stride, float* dA_log, float* ddt_bias, float* db_bias,
+                      float* dd_bias, int rows, int H, void* work, size_t work_bytes,
                       void* stream) {
   CYFA_REQUIRE(a && b && d && A_log && dt_bias && dg && ddelta && dbeta && da && db && dd &&
                    dA_log && ddt_bias && work,
@@ -136,8 +138,9 @@ int cyfa_gate_act_bwd(const void* a, long long a_stride, const void* b, long lon
   float* part = static_cast<float*>(work);
   GateActParams p{static_cast<const __nv_bfloat16*>(a), a_stride,
                   static_cast<const __nv_bfloat16*>(b), b_stride,
-                  static_cast<const __nv_bfloat16*>(d), d_stride, A_log, dt_bias, nullptr,
-                  nullptr, nullptr, dg, ddelta, dbeta, static_cast<__nv_bfloat16*>(da), da_stride,
+                  static_cast<const __nv_bfloat16*>(d), d_stride, A_log, dt_bias, b_bias, d_bias,
+                  nullptr, nullptr, nullptr, dg, ddelta, dbeta, static_cast<__nv_bfloat16*>(da),
+                  da_stride,
                   static_cast<__nv_bfloat16*>(db), db_stride, static_cast<__nv_bfloat16*>(dd),
                   dd_stride, part, rows, H};
   const int nblk = gate_bwd_blocks((long long)rows * H);
@@ -145,10 +148,19 @@ int cyfa_gate_act_bwd(const void* a, long long a_stride, const void* b, long lon
   CYFA_LAUNCH("gate_act_bwd", s, (gate_act_bwd_kernel<<<nblk, 256, 0, s>>>(p)));
   int rc = launch_status();
   if (rc) return rc;
+  // partial columns: dA_log | ddt_bias | db_bias | dd_bias, each H wide
   CYFA_LAUNCH("column_sum", s,
-              (strided_column_sum_kernel<<<1, 256, 0, s>>>(part, dA_log, nblk, H, 2 * H)));
+              (strided_column_sum_kernel<<<1, 1024, 0, s>>>(part, dA_log, nblk, H, 4 * H)));
   CYFA_LAUNCH("column_sum", s,
-              (strided_column_sum_kernel<<<1, 256, 0, s>>>(part + H, ddt_bias, nblk, H, 2 * H)));
+              (strided_column_sum_kernel<<<1, 1024, 0, s>>>(part + H, ddt_bias, nblk, H, 4 * H)));
+  if (db_bias)
+    CYFA_LAUNCH("column_sum", s,
+                (strided_column_sum_kernel<<<1, 1024, 0, s>>>(part + 2 * H, db_bias, nblk, H,
+                                                              4 * H)));
+  if (dd_bias)
+    CYFA_LAUNCH("column_sum", s,
+                (strided_column_sum_kernel<<<1, 1024, 0, s>>>(part + 3 * H, dd_bias, nblk, H,
+                                                              4 * H)));
   return launch_status();
 }
 

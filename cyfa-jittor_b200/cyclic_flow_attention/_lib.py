@@ -31,9 +31,9 @@ _SIGNATURES = {
     "cyfa_short_conv_fwd": [_vp, ctypes.c_longlong, _vp, _vp, _vp, _vp] + [_i] * 4 + [_vp],
     "cyfa_short_conv_bwd": [_vp, ctypes.c_longlong, _vp, _vp, _vp, ctypes.c_longlong, _vp, _vp]
     + [_i] * 4 + [_vp, ctypes.c_size_t, _vp],
-    "cyfa_gate_act_fwd": [_vp, ctypes.c_longlong] * 3 + [_vp] * 5 + [_i, _i, _vp],
-    "cyfa_gate_act_bwd": [_vp, ctypes.c_longlong] * 3 + [_vp] * 5
-    + [_vp, ctypes.c_longlong] * 3 + [_vp, _vp, _i, _i, _vp, ctypes.c_size_t, _vp],
+    "cyfa_gate_act_fwd": [_vp, ctypes.c_longlong] * 3 + [_vp] * 7 + [_i, _i, _vp],
+    "cyfa_gate_act_bwd": [_vp, ctypes.c_longlong] * 3 + [_vp] * 7
+    + [_vp, ctypes.c_longlong] * 3 + [_vp] * 4 + [_i, _i, _vp, ctypes.c_size_t, _vp],
     "cyfa_gated_norm_fwd": [_vp, _vp, _vp, _f, _f, _vp, _vp, _i, _i, _vp],
     "cyfa_gated_norm_bwd": [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp,
                             ctypes.c_size_t, _vp],

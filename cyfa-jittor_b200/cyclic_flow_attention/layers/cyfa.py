@@ -164,20 +164,19 @@ class CyclicFlowAttention(nn.Module):
         qkv = F.linear(x, w_qkv)
         g0 = self.g_proj[0]
         w_aux = torch.cat([g0.weight, self.a_proj.weight, self.b_proj.weight])
-        b_aux = torch.cat([torch.zeros(V + H, device=x.device, dtype=self.b_proj.bias.dtype),
-                           self.b_proj.bias])
-        aux = F.linear(x, w_aux, b_aux)
-        dlin = F.linear(x.detach(), self.d_proj.weight, self.d_proj.bias)
+        aux = F.linear(x, w_aux)
+        dlin = F.linear(x.detach(), self.d_proj.weight)
         conv_w = torch.cat([self.q_conv1d.weight, self.k_conv1d.weight, self.v_conv1d.weight])
         qkv = ShortConvFunction.apply(qkv, conv_w, None)
-        g, delta, beta = GateActFunction.apply(aux, dlin, self.A_log, self.dt_bias, V, V + H, H)
+        g, delta, beta = GateActFunction.apply(aux, dlin, self.A_log, self.dt_bias,
+                                               self.b_proj.bias, self.d_proj.bias, V, V + H, H)
         table = readout_table(self.readout)
         o, hk, hv, clock = ChunkCyfaPackedFunction.apply(
             qkv, H, K, V, g, delta, beta, table, self.q_norm.weight.float(),
             self.k_norm.weight.float(), float(self.q_norm.eps), float(self.k_norm.eps), K ** -0.5)
-        gate = self.g_proj[1](aux[..., :V])
-        y = GatedNormFunction.apply(o, gate, self.o_norm.weight, self.o_norm.eps,
-                                    float(self.num_slots - 1))
+        g1 = self.g_proj[1]
+        y = GatedNormFunction.apply(o, aux[..., :V], g1.weight, g1.bias, self.o_norm.weight,
+                                    self.o_norm.eps, float(self.num_slots - 1))
         y = self.o_proj(y)
         new_cache = None
         if use_cache:

@@ -54,31 +54,35 @@ class ShortConvFunction(torch.autograd.Function):
 
 class GateActFunction(torch.autograd.Function):
     """(g, delta, beta) from the packed auxiliary projection `aux` (a at column
-    a_col, b at b_col, H columns each) and the d projection `dlin` [B,T,H]."""
+    a_col, b at b_col, H columns each; no bias) and the d projection `dlin`
+    [B,T,H] (no bias); the b and d biases are applied here so their gradients
+    come from the kernel's fixed-order partial sums."""
 
     @staticmethod
-    def forward(ctx, aux, dlin, A_log, dt_bias, a_col, b_col, H):
+    def forward(ctx, aux, dlin, A_log, dt_bias, b_bias, d_bias, a_col, b_col, H):
         B, T, _ = aux.shape
         rows = B * T
         dev = aux.device
         A = A_log.detach().float().contiguous()
         dt = dt_bias.detach().float().contiguous()
+        bb = b_bias.detach().float().contiguous()
+        db = d_bias.detach().float().contiguous()
         g = torch.empty(B, T, H, device=dev, dtype=torch.float32)
         delta = torch.empty_like(g)
         beta = torch.empty_like(g)
         st = _c.c_longlong(aux.stride(1))
         _lib.call("cyfa_gate_act_fwd", _c.c_void_p(aux.data_ptr() + 2 * a_col), st,
                   _c.c_void_p(aux.data_ptr() + 2 * b_col), st, _p(dlin),
-                  _c.c_longlong(dlin.stride(1)), _p(A), _p(dt), _p(g), _p(delta), _p(beta), rows,
-                  H, _lib.stream())
-        ctx.save_for_backward(aux, dlin, A, dt)
-        ctx.meta = (a_col, b_col, H, A_log.dtype, dt_bias.dtype)
+                  _c.c_longlong(dlin.stride(1)), _p(A), _p(dt), _p(bb), _p(db), _p(g),
+                  _p(delta), _p(beta), rows, H, _lib.stream())
+        ctx.save_for_backward(aux, dlin, A, dt, bb, db)
+        ctx.meta = (a_col, b_col, H, A_log.dtype, dt_bias.dtype, b_bias.dtype, d_bias.dtype)
         return g, delta, beta
 
     @staticmethod
     def backward(ctx, dg, ddelta, dbeta):
-        aux, dlin, A, dt = ctx.saved_tensors
-        a_col, b_col, H, adt, ddt = ctx.meta
+        aux, dlin, A, dt, bb, db_ = ctx.saved_tensors
+        a_col, b_col, H, adt, ddt, bdt, dbt = ctx.meta
         B, T, width = aux.shape
         rows = B * T
         dev = aux.device
@@ -90,42 +94,46 @@ class GateActFunction(torch.autograd.Function):
         dd = torch.empty(B, T, H, device=dev, dtype=torch.bfloat16)
         dA = torch.empty(H, device=dev, dtype=torch.float32)
         ddtb = torch.empty(H, device=dev, dtype=torch.float32)
+        dbb = torch.empty(H, device=dev, dtype=torch.float32)
+        ddb = torch.empty(H, device=dev, dtype=torch.float32)
         nbytes = _lib.lib().cyfa_gate_act_work_bytes(rows, H)
         work = _work(nbytes, dev)
         st = _c.c_longlong(aux.stride(1))
         _lib.call("cyfa_gate_act_bwd", _c.c_void_p(aux.data_ptr() + 2 * a_col), st,
                   _c.c_void_p(aux.data_ptr() + 2 * b_col), st, _p(dlin),
-                  _c.c_longlong(dlin.stride(1)), _p(A), _p(dt), _p(dg), _p(ddelta), _p(dbeta),
-                  _c.c_void_p(daux.data_ptr() + 2 * a_col), _c.c_longlong(width),
-                  _c.c_void_p(daux.data_ptr() + 2 * b_col), _c.c_longlong(width), _p(dd),
-                  _c.c_longlong(H), _p(dA), _p(ddtb), rows, H, _p(work), _c.c_size_t(nbytes),
-                  _lib.stream())
-        return daux, dd, dA.to(adt), ddtb.to(ddt), None, None, None
+                  _c.c_longlong(dlin.stride(1)), _p(A), _p(dt), _p(bb), _p(db_), _p(dg),
+                  _p(ddelta), _p(dbeta), _c.c_void_p(daux.data_ptr() + 2 * a_col),
+                  _c.c_longlong(width), _c.c_void_p(daux.data_ptr() + 2 * b_col),
+                  _c.c_longlong(width), _p(dd), _c.c_longlong(H), _p(dA), _p(ddtb), _p(dbb),
+                  _p(ddb), rows, H, _p(work), _c.c_size_t(nbytes), _lib.stream())
+        return (daux, dd, dA.to(adt), ddtb.to(ddt), dbb.to(bdt), ddb.to(dbt), None, None, None)
 
 
 class GatedNormFunction(torch.autograd.Function):
     """y = RMSNorm(scale * x) * w * sigmoid(gate) over the last dim D of
-    x [B,T,H,D] and gate [B,T,H*D]; returns [B,T,H*D] bf16."""
+    x [B,T,H,D], with gate = gate_in @ W^T + b (the output gate's second linear,
+    [B,T,H*D]); returns [B,T,H*D] bf16.  The linear runs on cuBLAS; the bias
+    gradient is a cuBLAS GEMV over the gate gradient."""
 
     @staticmethod
-    def forward(ctx, x, gate, weight, eps, scale):
+    def forward(ctx, x, gate_in, gate_w, gate_b, weight, eps, scale):
         B, T, H, D = x.shape
         rows = B * T * H
         x = x.to(torch.bfloat16).contiguous()
-        gate = gate.to(torch.bfloat16).contiguous()
+        gate = torch.nn.functional.linear(gate_in, gate_w, gate_b).contiguous()
         w = weight.detach().float().contiguous()
         y = torch.empty(B, T, H * D, device=x.device, dtype=torch.bfloat16)
         rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
         _lib.call("cyfa_gated_norm_fwd", _p(x), _p(gate), _p(w), float(eps), float(scale), _p(y),
                   _p(rstd), rows, D, _lib.stream())
-        ctx.save_for_backward(x, gate, w, rstd)
-        ctx.meta = (scale, weight.dtype)
+        ctx.save_for_backward(x, gate, gate_in, gate_w, w, rstd)
+        ctx.meta = (scale, weight.dtype, gate_b is not None)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        x, gate, w, rstd = ctx.saved_tensors
-        scale, wdt = ctx.meta
+        x, gate, gate_in, gate_w, w, rstd = ctx.saved_tensors
+        scale, wdt, has_b = ctx.meta
         B, T, H, D = x.shape
         rows = B * T * H
         dy = dy.to(torch.bfloat16).contiguous()
@@ -137,7 +145,15 @@ class GatedNormFunction(torch.autograd.Function):
         _lib.call("cyfa_gated_norm_bwd", _p(x), _p(gate), _p(w), float(scale), _p(rstd), _p(dy),
                   _p(dx), _p(dgate), _p(dw), rows, D, _p(work), _c.c_size_t(nbytes),
                   _lib.stream())
-        return dx, dgate, dw.to(wdt), None, None
+        dg2 = dgate.reshape(-1, H * D)
+        gin2 = gate_in.reshape(-1, gate_in.shape[-1])
+        d_gate_in = (dg2 @ gate_w).reshape(gate_in.shape)
+        d_gate_w = dg2.t() @ gin2
+        d_gate_b = None
+        if has_b:
+            ones = torch.ones(dg2.shape[0], device=x.device, dtype=dg2.dtype)
+            d_gate_b = torch.mv(dg2.t(), ones)
+        return dx, d_gate_in, d_gate_w, d_gate_b, dw.to(wdt), None, None
 
 
 class ChunkCyfaPackedFunction(torch.autograd.Function):

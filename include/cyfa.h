@@ -209,21 +209,26 @@ int cyfa_short_conv_bwd(const void* x, long long x_stride, const float* w, const
                         int C, int W, void* work, size_t work_bytes, void* stream);
 
 /* Gate activations of the layer: g = -exp(A_log) softplus(a + dt_bias),
- * delta = sigmoid(d), beta = sigmoid(b), all [rows, H] f32 out; a, b, d are bf16
- * projection outputs with token strides.  Replaces layers/cyfa.py:323-326. */
+ * delta = sigmoid(d + d_bias), beta = sigmoid(b + b_bias), all [rows, H] f32 out;
+ * a, b, d are bf16 projection outputs with token strides; the biases [H] f32 may
+ * be NULL.  Replaces layers/cyfa.py:323-326. */
 int cyfa_gate_act_fwd(const void* a, long long a_stride, const void* b, long long b_stride,
                       const void* d, long long d_stride, const float* A_log,
-                      const float* dt_bias, float* g, float* delta, float* beta, int rows, int H,
-                      void* stream);
+                      const float* dt_bias, const float* b_bias, const float* d_bias, float* g,
+                      float* delta, float* beta, int rows, int H, void* stream);
 
 size_t cyfa_gate_act_work_bytes(int rows, int H);
 
+/* Adjoint of cyfa_gate_act_fwd: da, db, dd bf16 (token strides), and the
+ * parameter gradients dA_log, ddt_bias, db_bias, dd_bias [H] (the last two may be
+ * NULL). */
 int cyfa_gate_act_bwd(const void* a, long long a_stride, const void* b, long long b_stride,
                       const void* d, long long d_stride, const float* A_log,
-                      const float* dt_bias, const float* dg, const float* ddelta,
-                      const float* dbeta, void* da, long long da_stride, void* db,
-                      long long db_stride, void* dd, long long dd_stride, float* dA_log,
-                      float* ddt_bias, int rows, int H, void* work, size_t work_bytes,
+                      const float* dt_bias, const float* b_bias, const float* d_bias,
+                      const float* dg, const float* ddelta, const float* dbeta, void* da,
+                      long long da_stride, void* db, long long db_stride, void* dd,
+                      long long dd_stride, float* dA_log, float* ddt_bias, float* db_bias,
+                      float* dd_bias, int rows, int H, void* work, size_t work_bytes,
                       void* stream);
 
 /* Gated output norm: y = RMSNorm(scale * x) * w * sigmoid(gate) over rows of D
