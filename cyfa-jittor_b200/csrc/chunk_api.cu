@@ -110,6 +110,14 @@ static bool shape_ok(int B, int T, int H, int K, int V) {
 // elements (16 bytes, the TMA stride rule).
 static bool strides_ok(long long s, long long dense) { return s == 0 || (s >= dense && s % 8 == 0); }
 
+// CTAs per head of the persistent readout adjoint: about one CTA per SM in
+// total, at least one tile each.
+static int readout_ctas_per_head(const Dims& d) {
+  const int want = (148 + d.H - 1) / d.H;
+  const int tiles = d.B * d.NT;
+  return want < tiles ? want : tiles;
+}
+
 // A token stride of 0 means the dense layout.
 static long long stride_or(long long s, long long dense) { return s > 0 ? s : dense; }
 
@@ -314,14 +322,16 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   }
   // ================= readout adjoint
   {
-    ReadoutBwdParams rp{d.BH, d.H, d.TP, d.NT, s.raw, s.weights, w.dweights, s.lam, w.draw,
+    const int per_head = readout_ctas_per_head(d);
+    ReadoutBwdParams rp{d.BH, d.H, d.TP, d.NT, d.B, per_head, s.raw, w.dweights, s.lam, w.draw,
                         w.dlam_r, w.dtab_part};
     set_smem(readout_bwd_kernel, kReadoutBwdSmem);
-    CYFA_LAUNCH("readout_bwd", st, (readout_bwd_kernel<<<tiles, 128, kReadoutBwdSmem, st>>>(m_tab, rp)));
+    CYFA_LAUNCH("readout_bwd", st,
+                (readout_bwd_kernel<<<d.H * per_head, 256, kReadoutBwdSmem, st>>>(m_tab, rp)));
     if ((rc = launch_status())) return rc;
     CYFA_LAUNCH("dtable_reduce", st,
-                (dtable_reduce_kernel<<<dim3(d.H, 128), 128, 0, st>>>(w.dtab_part, g->dtable, d.B,
-                                                                      d.H, d.NT)));
+                (dtable_reduce_kernel<<<dim3(d.H, 128), 128, 0, st>>>(w.dtab_part, g->dtable,
+                                                                      per_head)));
     if ((rc = launch_status())) return rc;
   }
   // ================= pass 1 (queries = q^, keys = k^, values = w)

@@ -271,238 +271,254 @@ __global__ void __launch_bounds__(256, 1)
 
 // ============================================================ readout adjoint
 struct ReadoutBwdParams {
-  int BH, H, TP, NT;
+  int BH, H, TP, NT, B;
+  int per_head;                  // CTAs per head; gridDim.x = H * per_head
   const __nv_bfloat16* raw;      // [BH,TP,128]
-  const __nv_bfloat16* weights;  // [BH,TP,128]
   const float* dweights;         // [BH,TP,128]
   const float* lam;              // [BH,TP]
   __nv_bfloat16* draw;           // [BH,TP,128]
   float* dlam;                   // [BH,TP]
-  float* dtab_part;              // [BH*NT, 128, 128]
+  float* dtab_part;              // [H * per_head, 128, 128]
 };
 
 constexpr int kReadoutBwdSmem = 160 * 1024 + 1024;
 
-__global__ void __launch_bounds__(128, 1)
+// Persistent over the tiles of one head: CTA (h, split) handles tiles
+// split, split + per_head, ... of head h and accumulates the table gradient in
+// TMEM across them (one partial per CTA).  8 warps: warp w owns TMEM lane
+// quadrant (w & 3) (token rows) and column half (w >> 2).  Per tile:
+//   z = U(lam) raw, dc = U(lam) dw                  (registers -> bf16 smem)
+//   logits = z Tab^T, dp = dc Tab^T                  (UMMA)
+//   p = softmax(logits), dl = p o (dp - <p,dp>)     (registers; row halves joined in smem)
+//   dz = dl Tab, coeff = p Tab, dTab += p^T dc + dl^T z   (UMMA)
+//   draw = U(-lam) dz,  dlam = sum_p w_p [z x dz + dc x coeff]   (epilogue)
+// The rotation terms use the on-chip z, dc and coeff, so no input is read twice.
+__global__ void __launch_bounds__(256, 1)
     readout_bwd_kernel(const __grid_constant__ CUtensorMap map_tab, ReadoutBwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   __shared__ __align__(8) uint64_t bar_tab, bar_m1, bar_m2;
   __shared__ uint32_t tmem_base;
-  const int tid = threadIdx.x;
-  const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT;
-  const int t = j * 128 + tid;
-  const size_t row = size_t(bh) * p.TP + t;
+  __shared__ float xch[2][128];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
+  const int r = quad * 32 + lane;
+  const int h = blockIdx.x / p.per_head, split = blockIdx.x % p.per_head;
+  const int ntiles = p.B * p.NT;
   if (tid == 0) {
     mbar_init(&bar_tab, 1);
     mbar_init(&bar_m1, 1);
     mbar_init(&bar_m2, 1);
     mbar_fence_init();
   }
-  if (tid < 32) tmem_alloc(&tmem_base, 512);
+  if (warp == 0) tmem_alloc(&tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = tmem_base, lane_tmem = tmem_lane_base(tmem);
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
   const uint32_t sTab = smem_u32(smem), sZ = sTab + 32768, sDC = sTab + 65536,
                  sP = sTab + 98304, sDL = sTab + 131072;
   if (tid == 0) {
     mbar_expect_tx(&bar_tab, 32768);
-    load_hist_tile(smem, &map_tab, (bh % p.H) * 128, 0, 128, 128, &bar_tab);
+    load_hist_tile(smem, &map_tab, h * 128, 0, 128, 128, &bar_tab);
   }
   bool ok = true;
-  const float lam = p.lam[row];
-  // z = U(lam) raw and dcoeff = U(lam) dweights, bf16 operands
-#pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    float z[32], dc[32];
-    const uint4* rsrc = reinterpret_cast<const uint4*>(p.raw + row * 128 + 32 * c);
+  int it = 0;
+  for (int tile = split; tile < ntiles; tile += p.per_head, ++it) {
+    const int b = tile / p.NT, j = tile % p.NT, bh = b * p.H + h;
+    const size_t row = size_t(bh) * p.TP + j * 128 + r;
+    const float lam = p.lam[row];
+    // ---- z = U(lam) raw and dc = U(lam) dw for this thread's 64 columns
+    {
+      float z[64], dc[64];
+      const uint4* rsrc = reinterpret_cast<const uint4*>(p.raw + row * 128 + half * 64);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) unpack_bf16x8(rsrc[q], z + 8 * q);
-    const float4* dsrc = reinterpret_cast<const float4*>(p.dweights + row * 128 + 32 * c);
+      for (int q = 0; q < 8; ++q) unpack_bf16x8(rsrc[q], z + 8 * q);
+      const float4* dsrc = reinterpret_cast<const float4*>(p.dweights + row * 128 + half * 64);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const float4 x = dsrc[q];
-      dc[4 * q] = x.x;
-      dc[4 * q + 1] = x.y;
-      dc[4 * q + 2] = x.z;
-      dc[4 * q + 3] = x.w;
+      for (int q = 0; q < 16; ++q) {
+        const float4 x = dsrc[q];
+        dc[4 * q] = x.x;
+        dc[4 * q + 1] = x.y;
+        dc[4 * q + 2] = x.z;
+        dc[4 * q + 3] = x.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 64; i += 2) {
+        float sn, cs;
+        __sincosf(clock_phase(lam, 32 * half + i / 2), &sn, &cs);
+        const float e = z[i], o = z[i + 1];
+        z[i] = cs * e - sn * o;
+        z[i + 1] = sn * e + cs * o;
+        const float de = dc[i], dd = dc[i + 1];
+        dc[i] = cs * de - sn * dd;
+        dc[i + 1] = sn * de + cs * dd;
+      }
+      store_row64_bf16(sZ + half * 16384, r, z);
+      store_row64_bf16(sDC + half * 16384, r, dc);
     }
+    fence_async_smem();
+    tc_fence_before();
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    if (!ok) break;
+    if (tid == 0) {
+      if (it > 0 || mbar_wait(&bar_tab, 0)) {
+        tc_fence_after();
 #pragma unroll
-    for (int i = 0; i < 32; i += 2) {
-      float sn, cs;
-      __sincosf(clock_phase(lam, 16 * c + i / 2), &sn, &cs);
-      const float e = z[i], o = z[i + 1];
-      z[i] = cs * e - sn * o;
-      z[i + 1] = sn * e + cs * o;
-      const float de = dc[i], dd = dc[i + 1];
-      dc[i] = cs * de - sn * dd;
-      dc[i + 1] = sn * de + cs * dd;
+        for (int ks = 0; ks < 8; ++ks)
+          umma_bf16(tmem, kmaj_desc(sZ, 128, ks), kmaj_desc(sTab, 128, ks),
+                    make_idesc(128, 128, 0, 0), ks > 0);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_bf16(tmem + 128, kmaj_desc(sDC, 128, ks), kmaj_desc(sTab, 128, ks),
+                    make_idesc(128, 128, 0, 0), ks > 0);
+        umma_commit(&bar_m1);
+      } else {
+        mbar_arrive(&bar_m1);
+      }
     }
-    store_row32_bf16(sZ + (c >> 1) * 16384, tid, (c & 1) * 4, z);
-    store_row32_bf16(sDC + (c >> 1) * 16384, tid, (c & 1) * 4, dc);
-  }
-  fence_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (tid == 0) {
-    if (mbar_wait(&bar_tab, 0)) {
-      tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks)
-        umma_bf16(tmem, kmaj_desc(sZ, 128, ks), kmaj_desc(sTab, 128, ks),
-                  make_idesc(128, 128, 0, 0), ks > 0);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks)
-        umma_bf16(tmem + 128, kmaj_desc(sDC, 128, ks), kmaj_desc(sTab, 128, ks),
-                  make_idesc(128, 128, 0, 0), ks > 0);
-      umma_commit(&bar_m1);
-    } else {
-      mbar_arrive(&bar_m1);
-    }
-  }
-  __syncwarp();
-  if (!mbar_wait(&bar_m1, 0)) ok = false;
-  tc_fence_after();
-  if (ok) {
+    __syncwarp();
+    if (!mbar_wait(&bar_m1, it & 1)) ok = false;
+    tc_fence_after();
+    // ---- softmax over the 127 active slots, row split over two column halves
+    float l[64], d[64];
+    tmem_ld32(lane_tmem + half * 64, *reinterpret_cast<float(*)[32]>(l));
+    tmem_ld32(lane_tmem + half * 64 + 32, *reinterpret_cast<float(*)[32]>(l + 32));
+    tmem_ld32(lane_tmem + 128 + half * 64, *reinterpret_cast<float(*)[32]>(d));
+    tmem_ld32(lane_tmem + 128 + half * 64 + 32, *reinterpret_cast<float(*)[32]>(d + 32));
     float mx = -1e30f;
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tmem_ld32(lane_tmem + 32 * c, v);
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (32 * c + i < 127) mx = fmaxf(mx, v[i]);
-    }
+    for (int i = 0; i < 64; ++i)
+      if (half * 64 + i < 127) mx = fmaxf(mx, l[i]);
+    xch[half][r] = mx;
+    __syncthreads();
+    mx = fmaxf(xch[0][r], xch[1][r]);
     float sum = 0.f;
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tmem_ld32(lane_tmem + 32 * c, v);
 #pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (32 * c + i < 127) sum += __expf(v[i] - mx);
+    for (int i = 0; i < 64; ++i) {
+      l[i] = (half * 64 + i < 127) ? __expf(l[i] - mx) : 0.f;
+      sum += l[i];
     }
-    const float inv = 1.f / sum;
+    __syncthreads();
+    xch[half][r] = sum;
+    __syncthreads();
+    const float inv = 1.f / (xch[0][r] + xch[1][r]);
     float pdp = 0.f;
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float v[32], d[32];
-      tmem_ld32(lane_tmem + 32 * c, v);
-      tmem_ld32(lane_tmem + 128 + 32 * c, d);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        v[i] = (32 * c + i < 127) ? __expf(v[i] - mx) * inv : 0.f;
-        pdp += v[i] * d[i];
-      }
-      store_row32_bf16(sP + (c >> 1) * 16384, tid, (c & 1) * 4, v);
+    for (int i = 0; i < 64; ++i) {
+      l[i] *= inv;
+      pdp += l[i] * d[i];
     }
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float v[32], d[32];
-      tmem_ld32(lane_tmem + 32 * c, v);
-      tmem_ld32(lane_tmem + 128 + 32 * c, d);
+    __syncthreads();
+    xch[half][r] = pdp;
+    __syncthreads();
+    pdp = xch[0][r] + xch[1][r];
+    store_row64_bf16(sP + half * 16384, r, l);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float pr = (32 * c + i < 127) ? __expf(v[i] - mx) * inv : 0.f;
-        v[i] = pr * (d[i] - pdp);
-      }
-      store_row32_bf16(sDL + (c >> 1) * 16384, tid, (c & 1) * 4, v);
-    }
-  }
-  fence_async_smem();
-  tc_fence_before();
-  ok = __syncthreads_and(ok);
-  tc_fence_after();
-  if (tid == 0) {
-    if (ok) {
+    for (int i = 0; i < 64; ++i) d[i] = l[i] * (d[i] - pdp);
+    store_row64_bf16(sDL + half * 16384, r, d);
+    fence_async_smem();
+    tc_fence_before();
+    ok = __syncthreads_and(ok);
+    tc_fence_after();
+    if (!ok) break;
+    if (tid == 0) {
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks)
         umma_bf16(tmem + 256, kmaj_desc(sDL, 128, ks), mnmaj_desc(sTab, 128, ks),
                   make_idesc(128, 128, 0, 1), ks > 0);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem, kmaj_desc(sP, 128, ks), mnmaj_desc(sTab, 128, ks),
+                  make_idesc(128, 128, 0, 1), ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
         umma_bf16(tmem + 384, mnmaj_desc(sP, 128, ks), mnmaj_desc(sDC, 128, ks),
-                  make_idesc(128, 128, 1, 1), ks > 0);
+                  make_idesc(128, 128, 1, 1), (it > 0 || ks > 0) ? 1u : 0u);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks)
         umma_bf16(tmem + 384, mnmaj_desc(sDL, 128, ks), mnmaj_desc(sZ, 128, ks),
                   make_idesc(128, 128, 1, 1), 1);
       umma_commit(&bar_m2);
-    } else {
-      mbar_arrive(&bar_m2);
     }
+    __syncwarp();
+    if (!mbar_wait(&bar_m2, it & 1)) ok = false;
+    tc_fence_after();
+    // ---- draw = U(-lam) dz, dlam from the rotations (z, dc from smem, coeff from TMEM)
+    {
+      float dz[64], cf[64];
+      tmem_ld32(lane_tmem + 256 + half * 64, *reinterpret_cast<float(*)[32]>(dz));
+      tmem_ld32(lane_tmem + 256 + half * 64 + 32, *reinterpret_cast<float(*)[32]>(dz + 32));
+      tmem_ld32(lane_tmem + half * 64, *reinterpret_cast<float(*)[32]>(cf));
+      tmem_ld32(lane_tmem + half * 64 + 32, *reinterpret_cast<float(*)[32]>(cf + 32));
+      float dl = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        float z[8], dc[8];
+        unpack_bf16x8(ld_shared_v4(sZ + half * 16384 + sw128(r, c8)), z);
+        unpack_bf16x8(ld_shared_v4(sDC + half * 16384 + sw128(r, c8)), dc);
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const int i = 8 * c8 + e;
+          const int pair = 32 * half + i / 2;
+          float sn, cs;
+          __sincosf(clock_phase(lam, pair), &sn, &cs);
+          const float de = dz[i], dd = dz[i + 1];
+          dl += (pair * kTwoPiOver127) *
+                (-de * z[e + 1] + dd * z[e] + dc[e] * cf[i + 1] - dc[e + 1] * cf[i]);
+          dz[i] = cs * de + sn * dd;
+          dz[i + 1] = -sn * de + cs * dd;
+        }
+      }
+      __nv_bfloat16* dst = p.draw + row * 128 + half * 64;
+      store_bf16x32_global(dst, dz);
+      store_bf16x32_global(dst + 32, dz + 32);
+      __syncthreads();
+      xch[half][r] = dl;
+      __syncthreads();
+      if (half == 0) p.dlam[row] = xch[0][r] + xch[1][r];
+    }
+    tc_fence_before();
+    ok = __syncthreads_and(ok);  // smem tiles and TMEM are reused by the next tile
+    tc_fence_after();
+    if (!ok) break;
   }
-  __syncwarp();
-  if (!mbar_wait(&bar_m2, 0)) ok = false;
-  tc_fence_after();
-  if (ok) {
-    float dl = 0.f;
+  // this CTA's partial table gradient: thread (quad, half) owns slot row r, 64 columns
+  if (ok && it > 0) {
+    float* dst = p.dtab_part + size_t(blockIdx.x) * 16384 + r * 128 + half * 64;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float dz[32], z[32], w[32], dw[32];
-      tmem_ld32(lane_tmem + 256 + 32 * c, dz);
-      const uint4* rsrc = reinterpret_cast<const uint4*>(p.raw + row * 128 + 32 * c);
-      const uint4* wsrc = reinterpret_cast<const uint4*>(p.weights + row * 128 + 32 * c);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        unpack_bf16x8(rsrc[q], z + 8 * q);
-        unpack_bf16x8(wsrc[q], w + 8 * q);
-      }
-      const float4* dsrc = reinterpret_cast<const float4*>(p.dweights + row * 128 + 32 * c);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 x = dsrc[q];
-        dw[4 * q] = x.x;
-        dw[4 * q + 1] = x.y;
-        dw[4 * q + 2] = x.z;
-        dw[4 * q + 3] = x.w;
-      }
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        const int pair = 16 * c + i / 2;
-        float sn, cs;
-        __sincosf(clock_phase(lam, pair), &sn, &cs);
-        const float ze = bf16_round(cs * z[i] - sn * z[i + 1]);
-        const float zo = bf16_round(sn * z[i] + cs * z[i + 1]);
-        const float de = dz[i], dd = dz[i + 1];
-        dl += (pair * kTwoPiOver127) *
-              (-de * zo + dd * ze + dw[i] * w[i + 1] - dw[i + 1] * w[i]);
-        dz[i] = cs * de + sn * dd;
-        dz[i + 1] = -sn * de + cs * dd;
-      }
-      store_bf16x32_global(p.draw + row * 128 + 32 * c, dz);
-    }
-    p.dlam[row] = dl;
-    // this tile's partial table gradient: thread tid owns slot row r = tid
-    float* dst = p.dtab_part + size_t(blockIdx.x) * 16384 + tid * 128;
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
       float v[32];
-      tmem_ld32(lane_tmem + 384 + 32 * c, v);
+      tmem_ld32(lane_tmem + 384 + half * 64 + 32 * c, v);
       float4* d4 = reinterpret_cast<float4*>(dst + 32 * c);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      for (int q = 0; q < 8; ++q)
+        d4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (tid < 32) {
+  if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
 }
 
-// Fixed-order reduction of the per-tile table gradients:
-// dtab[h][r][m] = sum_{b, j} part[((b*H + h)*NT + j)][r][m].
-__global__ void __launch_bounds__(128) dtable_reduce_kernel(const float* part, float* dtab, int B,
-                                                            int H, int NT) {
+// Fixed-order reduction of the per-CTA table gradients:
+// dtab[h][r][m] = sum_{s < per_head} part[h * per_head + s][r][m].
+__global__ void __launch_bounds__(128) dtable_reduce_kernel(const float* part, float* dtab,
+                                                            int per_head) {
   const int h = blockIdx.x, r = blockIdx.y, m = threadIdx.x;
-  float s = 0.f;
-  for (int b = 0; b < B; ++b)
-    for (int j = 0; j < NT; ++j) s += part[((size_t(b) * H + h) * NT + j) * 16384 + r * 128 + m];
-  dtab[(size_t(h) * 128 + r) * 128 + m] = s;
+  float s0 = 0.f, s1 = 0.f;
+  int k = 0;
+  for (; k + 1 < per_head; k += 2) {
+    s0 += part[(size_t(h) * per_head + k) * 16384 + r * 128 + m];
+    s1 += part[(size_t(h) * per_head + k + 1) * 16384 + r * 128 + m];
+  }
+  if (k < per_head) s0 += part[(size_t(h) * per_head + k) * 16384 + r * 128 + m];
+  dtab[(size_t(h) * 128 + r) * 128 + m] = s0 + s1;
 }
 
 // Fixed-order column sums of a [rows, cols] partial matrix: out[c] = sum_r part[r][c].
