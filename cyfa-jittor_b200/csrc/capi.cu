@@ -152,12 +152,13 @@ static int token_fwd_launch(const void* q, const void* k, const float* q_norm_we
 
 static int token_bwd_launch(const void* q, const void* k, const float* q_norm_weight,
                             const float* k_norm_weight, const float* q_rs, const float* k_rs,
-                            const float* dqn, const float* dkn, const float* lam,
-                            const float* beta_h, const float* dw, const float* dw_b, void* dq,
+                            const void* dqn, const void* dkn, const float* lam,
+                            const float* beta_h, const void* dw, const void* dw_b, void* dq,
                             void* dk, float* dqw_part, float* dkw_part, float* dlam,
                             float* dbeta_h, int B,
                             int T, int H, int K, long long q_stride, long long k_stride,
-                            long long dq_stride, long long dk_stride, void* stream) {
+                            long long dq_stride, long long dk_stride, bool grads_bf16,
+                            void* stream) {
   CYFA_REQUIRE(q && k && q_norm_weight && k_norm_weight && q_rs && k_rs && dqn && dkn && lam &&
                    beta_h && dw && dq && dk && dqw_part && dkw_part && dlam && dbeta_h,
                kNullPointer);
@@ -171,8 +172,15 @@ static int token_bwd_launch(const void* q, const void* k, const float* q_norm_we
   const size_t rows = size_t(B) * H * TP;
   const dim3 grid(unsigned(token_bwd_blocks(rows)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (K == 256) CYFA_LAUNCH("token_bwd", s, token_bwd_kernel<256><<<grid, 256, 0, s>>>(p));
-  else CYFA_LAUNCH("token_bwd", s, token_bwd_kernel<128><<<grid, 256, 0, s>>>(p));
+  if (grads_bf16) {
+    if (K == 256)
+      CYFA_LAUNCH("token_bwd", s, (token_bwd_kernel<256, __nv_bfloat16><<<grid, 256, 0, s>>>(p)));
+    else
+      CYFA_LAUNCH("token_bwd", s, (token_bwd_kernel<128, __nv_bfloat16><<<grid, 256, 0, s>>>(p)));
+  } else {
+    if (K == 256) CYFA_LAUNCH("token_bwd", s, (token_bwd_kernel<256, float><<<grid, 256, 0, s>>>(p)));
+    else CYFA_LAUNCH("token_bwd", s, (token_bwd_kernel<128, float><<<grid, 256, 0, s>>>(p)));
+  }
   return launch_status();
 }
 
@@ -325,7 +333,7 @@ int cyfa_token_bwd(const void* q, const void* k, const float* q_norm_weight,
   const long long d = (long long)H * K;
   return token_bwd_launch(q, k, q_norm_weight, k_norm_weight, q_rs, k_rs, dqn, dkn, lam, beta_h,
                           dw, nullptr, dq, dk, dqw_part, dkw_part, dlam, dbeta_h, B, T, H, K, d, d, d, d,
-                          stream);
+                          false, stream);
 }
 
 int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h, const float* dclock,

@@ -58,8 +58,8 @@ static Saved carve_saved(const Dims& d, void* base, size_t* total) {
 
 // Scratch of the backward pass.
 struct Work {
-  __nv_bfloat16 *h1, *h2, *A, *Bp, *draw;
-  float *dweights, *dw, *dw_b, *dq1, *dk1, *dG, *dlam_r, *dlam_w, *dbeta_h, *bpart1, *bpart2, *dtab_part,
+  __nv_bfloat16 *h1, *h2, *A, *Bp, *draw, *dweights, *dw, *dw_b, *dq1, *dk1;
+  float *dG, *dlam_r, *dlam_w, *dbeta_h, *bpart1, *bpart2, *dtab_part,
       *dqw_part, *dkw_part;
 };
 
@@ -72,11 +72,11 @@ static Work carve_work(const Dims& d, void* base, size_t* total) {
   w.A = c.take<__nv_bfloat16>(tiles * 128 * 128);
   w.Bp = c.take<__nv_bfloat16>(tiles * 128 * 128);
   w.draw = c.take<__nv_bfloat16>(n * 128);
-  w.dweights = c.take<float>(n * 128);
-  w.dw = c.take<float>(n * 128);
-  w.dw_b = c.take<float>(n * 128);
-  w.dq1 = c.take<float>(n * d.K);
-  w.dk1 = c.take<float>(n * d.K);
+  w.dweights = c.take<__nv_bfloat16>(n * 128);
+  w.dw = c.take<__nv_bfloat16>(n * 128);
+  w.dw_b = c.take<__nv_bfloat16>(n * 128);
+  w.dq1 = c.take<__nv_bfloat16>(n * d.K);
+  w.dk1 = c.take<__nv_bfloat16>(n * d.K);
   w.dG = c.take<float>(n);
   w.dlam_r = c.take<float>(n);
   w.dlam_w = c.take<float>(n);
@@ -195,12 +195,12 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
     if (d.K == 256) {
       set_smem(tile_fwd_kernel<256, true>, tile_fwd_smem<256>());
       CYFA_LAUNCH("tile_fwd_readout", st,
-                  (tile_fwd_kernel<256, true><<<dim3(d.BH * d.NT, 1), 128, tile_fwd_smem<256>(), st>>>(
+                  (tile_fwd_kernel<256, true><<<dim3(d.BH * d.NT, 1), 256, tile_fwd_smem<256>(), st>>>(
                       m_qn, m_kn, m_w, m_s1, m_tab, t)));
     } else {
       set_smem(tile_fwd_kernel<128, true>, tile_fwd_smem<128>());
       CYFA_LAUNCH("tile_fwd_readout", st,
-                  (tile_fwd_kernel<128, true><<<dim3(d.BH * d.NT, 1), 128, tile_fwd_smem<128>(), st>>>(
+                  (tile_fwd_kernel<128, true><<<dim3(d.BH * d.NT, 1), 256, tile_fwd_smem<128>(), st>>>(
                       m_qn, m_kn, m_w, m_s1, m_tab, t)));
     }
     if ((rc = launch_status())) return rc;
@@ -216,7 +216,7 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
                     static_cast<__nv_bfloat16*>(a->o), nullptr};
     set_smem(tile_fwd_kernel<128, false>, tile_fwd_smem<128>());
     CYFA_LAUNCH("tile_fwd", st,
-                (tile_fwd_kernel<128, false><<<dim3(d.BH * d.NT, d.V / 128), 128, tile_fwd_smem<128>(),
+                (tile_fwd_kernel<128, false><<<dim3(d.BH * d.NT, d.V / 128), 256, tile_fwd_smem<128>(),
                                                st>>>(m_weights, m_w, m_v, m_s2, m_tab, t)));
     if ((rc = launch_status())) return rc;
   }
@@ -309,11 +309,11 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     if ((rc = launch_status())) return rc;
     // dweights = B' w + 2^{G_t} dO S^T ;  dG = weights . dweights
     DualParams q2{d.BH, d.H, d.TP, d.NT, d.T, 0, kRows2D, kPublic4D, 1, 128, d.V, 128, d.V, s.G,
-                  1.f, 0, 0, w.dweights, s.weights, 1.f, 0, w.dG};
+                  1.f, 0, 3, w.dweights, s.weights, 1.f, 0, w.dG};
     if ((rc = dual(m_Bp, m_w, m_do, m_s2, q2))) return rc;
     // dw = B'^T weights + 2^{G_L-G_s} v H^T ;  dG -= w . dw
     DualParams k2{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kPublic4D, 1, 128, d.V, 128, d.V, s.G,
-                  1.f, 1, 0, w.dw, s.w, -1.f, 1, w.dG};
+                  1.f, 1, 3, w.dw, s.w, -1.f, 1, w.dG};
     if ((rc = dual(m_Bp, m_weights, m_v, m_h2, k2))) return rc;
     // dv = A^T dO + 2^{G_L-G_s} w H  (public layout)
     DualParams v2{d.BH, d.H, d.TP, d.NT, d.T, 1, kPublic4D, kRows2D, 0, d.V, 128, 128, d.V, s.G,
@@ -357,15 +357,15 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     if ((rc = launch_status())) return rc;
     // dq^ = B' k^ + scale 2^{G_t} draw S^T ;  dG += q^ . dq^
     DualParams q1{d.BH, d.H, d.TP, d.NT, d.T, 0, kRows2D, kRows2D, 1, d.K, 128, d.K, 128, s.G,
-                  a->scale, 0, 0, w.dq1, s.qn, 1.f, 1, w.dG};
+                  a->scale, 0, 3, w.dq1, s.qn, 1.f, 1, w.dG};
     if ((rc = dual(m_Bp, m_kn, m_draw, m_s1, q1))) return rc;
     // dk^ = B'^T q^ + 2^{G_L-G_s} w H^T ;  dG -= k^ . dk^
     DualParams k1{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kRows2D, 1, d.K, 128, d.K, 128, s.G,
-                  1.f, 1, 0, w.dk1, s.kn, -1.f, 1, w.dG};
+                  1.f, 1, 3, w.dk1, s.kn, -1.f, 1, w.dG};
     if ((rc = dual(m_Bp, m_qn, m_w, m_h1, k1))) return rc;
     // dw_b = A^T draw + 2^{G_L-G_s} k^ H  (the write-vector gradient is dw + dw_b)
     DualParams v1{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kRows2D, 0, 128, d.K, d.K, 128, s.G,
-                  1.f, 1, 0, w.dw_b, nullptr, 0.f, 0, nullptr};
+                  1.f, 1, 3, w.dw_b, nullptr, 0.f, 0, nullptr};
     if ((rc = dual(m_A, m_draw, m_kn, m_h1, v1))) return rc;
   }
   // ================= norms, write vector, gates, clock
@@ -374,15 +374,12 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                         w.dlam_w, w.dbeta_h, d.B, d.T, d.H, d.K,
                         stride_or(a->q_stride, d.H * d.K), stride_or(a->k_stride, d.H * d.K),
                         stride_or(g->dq_stride, d.H * d.K), stride_or(g->dk_stride, d.H * d.K),
-                        stream);
+                        true, stream);
   if (rc) return rc;
   const int nblk = token_bwd_blocks(rows);
   CYFA_LAUNCH("column_sum", st,
-              (column_sum_kernel<<<(d.K + 31) / 32, 1024, 0, st>>>(w.dqw_part, g->dq_norm_weight, nblk,
-                                                                   d.K)));
-  CYFA_LAUNCH("column_sum", st,
-              (column_sum_kernel<<<(d.K + 31) / 32, 1024, 0, st>>>(w.dkw_part, g->dk_norm_weight, nblk,
-                                                                   d.K)));
+              (column_sum_kernel<<<dim3((d.K + 31) / 32, 2), 1024, 0, st>>>(
+                  w.dqw_part, g->dq_norm_weight, nblk, d.K, w.dkw_part, g->dk_norm_weight)));
   if ((rc = launch_status())) return rc;
   GatesBwdParams gp{w.dG, w.dlam_w, w.dlam_r, w.bpart1, w.bpart2, nsub1, nsub2, w.dbeta_h,
                     g->dclock, g->dg, g->ddelta, g->dbeta, g->dclock0, d.B, d.T, d.H, d.TP};

@@ -133,7 +133,7 @@ struct DualParams {
   const float* G;
   float scale;
   int fkind;          // row factor: 0 -> scale 2^{G_t}; 1 -> 2^{G_L - G_t}
-  int out_mode;       // 0: fp32 [BH,TP,N] store; 1: fp32 add; 2: bf16 public [B,T,H,N]
+  int out_mode;       // 0: fp32 [BH,TP,N]; 2: bf16 public [B,T,H,N]; 3: bf16 [BH,TP,N]
   void* out;
   const __nv_bfloat16* dot_src;  // optional [BH,TP,N] row-dot partner
   float dot_sign;
@@ -240,6 +240,8 @@ __global__ void __launch_bounds__(256, 1)
                                    (size_t(b_) * p.T + t) * p.out_stride + size_t(h) * p.N + col,
                                a);
         }
+      } else if (p.out_mode == 3) {
+        store_bf16x32_global(static_cast<__nv_bfloat16*>(p.out) + row * p.N + col, a);
       } else {
         float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + col);
 #pragma unroll
@@ -274,7 +276,7 @@ struct ReadoutBwdParams {
   int BH, H, TP, NT, B;
   int per_head;                  // CTAs per head; gridDim.x = H * per_head
   const __nv_bfloat16* raw;      // [BH,TP,128]
-  const float* dweights;         // [BH,TP,128]
+  const __nv_bfloat16* dweights;  // [BH,TP,128]
   const float* lam;              // [BH,TP]
   __nv_bfloat16* draw;           // [BH,TP,128]
   float* dlam;                   // [BH,TP]
@@ -335,15 +337,9 @@ __global__ void __launch_bounds__(256, 1)
       const uint4* rsrc = reinterpret_cast<const uint4*>(p.raw + row * 128 + half * 64);
 #pragma unroll
       for (int q = 0; q < 8; ++q) unpack_bf16x8(rsrc[q], z + 8 * q);
-      const float4* dsrc = reinterpret_cast<const float4*>(p.dweights + row * 128 + half * 64);
+      const uint4* dsrc = reinterpret_cast<const uint4*>(p.dweights + row * 128 + half * 64);
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const float4 x = dsrc[q];
-        dc[4 * q] = x.x;
-        dc[4 * q + 1] = x.y;
-        dc[4 * q + 2] = x.z;
-        dc[4 * q + 3] = x.w;
-      }
+      for (int q = 0; q < 8; ++q) unpack_bf16x8(dsrc[q], dc + 8 * q);
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
         float sn, cs;
@@ -524,8 +520,13 @@ __global__ void __launch_bounds__(128) dtable_reduce_kernel(const float* part, f
 // Fixed-order column sums of a [rows, cols] partial matrix: out[c] = sum_r part[r][c].
 // 1024 threads: 32 columns x 32 row lanes, each lane with 4 independent accumulators.
 __global__ void __launch_bounds__(1024) column_sum_kernel(const float* part, float* out, int rows,
-                                                          int cols) {
+                                                          int cols, const float* part2 = nullptr,
+                                                          float* out2 = nullptr) {
   __shared__ float acc[32][33];
+  if (blockIdx.y == 1) {  // second (part, out) pair
+    part = part2;
+    out = out2;
+  }
   const int c = blockIdx.x * 32 + (threadIdx.x & 31), lane_r = threadIdx.x >> 5;
   float s = 0.f;
   if (c < cols) {

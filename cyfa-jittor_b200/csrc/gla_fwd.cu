@@ -307,8 +307,11 @@ constexpr int tile_fwd_smem() {
   return 3 * DK * 256 + 32768 + 1024;
 }
 
+// 8 warps: warp w owns TMEM lane quadrant (w & 3) (token rows 32(w&3)..+31) and
+// column half (w >> 2) of every 128-column accumulator; row-wide softmax
+// statistics are joined through shared memory.
 template <int DK, bool READOUT>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(256, 1)
     tile_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
                     const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v,
@@ -320,9 +323,12 @@ __global__ void __launch_bounds__(128, 1)
   __shared__ __align__(8) uint64_t bar_in, bar_v, bar_tab, bar_m[5];
   __shared__ uint32_t tmem_base;
   __shared__ float Gs[128];
-  const int tid = threadIdx.x;
+  __shared__ float xch[2][128];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
+  const int r = quad * 32 + lane;
   const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT, dv0 = blockIdx.y * 128;
-  const int t = j * 128 + tid;
+  const int t = j * 128 + r;
 
   if (tid == 0) {
     mbar_init(&bar_in, 1);
@@ -331,13 +337,13 @@ __global__ void __launch_bounds__(128, 1)
     for (int i = 0; i < 5; ++i) mbar_init(&bar_m[i], 1);
     mbar_fence_init();
   }
-  if (tid < 32) tmem_alloc(&tmem_base, 512);
-  Gs[tid] = p.G[size_t(bh) * p.TP + t];
+  if (warp == 0) tmem_alloc(&tmem_base, 512);
+  if (tid < 128) Gs[tid] = p.G[size_t(bh) * p.TP + j * 128 + tid];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
-  const uint32_t lane_tmem = tmem_lane_base(tmem);
+  const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
   const uint32_t sQ = smem_u32(smem + kQ), sK = smem_u32(smem + kK), sS = smem_u32(smem + kS),
                  sV = smem_u32(smem + kV);
   bool ok = true;
@@ -349,9 +355,8 @@ __global__ void __launch_bounds__(128, 1)
     load_hist_tile(smem + kS, &map_s, (bh * p.NT + j) * DK, dv0, 128, DK, &bar_in);
     mbar_expect_tx(&bar_v, 32768);
     load_token_tile(smem + kV, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 128, &bar_v);
-    ok = mbar_wait(&bar_in, 0);
-    tc_fence_after();
-    if (ok) {
+    if (mbar_wait(&bar_in, 0)) {
+      tc_fence_after();
       // S_qk = Q K^T -> TMEM[0,128); O_inter = Q S_j -> TMEM[128,256)
 #pragma unroll 4
       for (int ks = 0; ks < DK / 16; ++ks)
@@ -368,22 +373,25 @@ __global__ void __launch_bounds__(128, 1)
       mbar_arrive(&bar_m[1]);
     }
   }
+  const float gt = Gs[r];
+  float lam = 0.f;
+  if (READOUT) lam = p.lam[size_t(bh) * p.TP + t];
   __syncwarp();
   // ---- P = mask(S_qk o 2^{G_t - G_s}) -> bf16, K-major A operand in the K region
   if (!mbar_wait(&bar_m[0], 0)) ok = false;
   tc_fence_after();
-  const float gt = Gs[tid];
   if (ok) {
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
+      const int col0 = half * 64 + 32 * c;
       float v[32];
-      tmem_ld32(lane_tmem + 32 * c, v);
+      tmem_ld32(lane_tmem + col0, v);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const int s = 32 * c + i;
-        v[i] = s <= tid ? v[i] * exp2f(gt - Gs[s]) : 0.f;
+        const int s_ = col0 + i;
+        v[i] = s_ <= r ? v[i] * exp2f(gt - Gs[s_]) : 0.f;
       }
-      store_row32_bf16(sK + (c >> 1) * 16384, tid, (c & 1) * 4, v);
+      store_row32_bf16(sK + half * 16384, r, c * 4, v);
     }
   }
   fence_async_smem();
@@ -417,23 +425,22 @@ __global__ void __launch_bounds__(128, 1)
   if (!mbar_wait(&bar_m[2], 0)) ok = false;
   tc_fence_after();
   const float eg = exp2f(gt);
-  float lam = 0.f;
-  if (READOUT) lam = p.lam[size_t(bh) * p.TP + t];
   if (ok) {
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
+      const int col0 = half * 64 + 32 * c;
       float a[32], b[32];
-      tmem_ld32(lane_tmem + 128 + 32 * c, a);
-      tmem_ld32(lane_tmem + 256 + 32 * c, b);
+      tmem_ld32(lane_tmem + 128 + col0, a);
+      tmem_ld32(lane_tmem + 256 + col0, b);
 #pragma unroll
       for (int i = 0; i < 32; ++i) a[i] = p.scale * (eg * a[i] + b[i]);
       if (p.o_mode == 1) {
         if (t < p.T) {
           const int b_ = bh / p.H, h = bh % p.H;
-          store_bf16x32_global(p.out + ((size_t(b_) * p.T + t) * p.H + h) * p.DV + dv0 + 32 * c, a);
+          store_bf16x32_global(p.out + ((size_t(b_) * p.T + t) * p.H + h) * p.DV + dv0 + col0, a);
         }
       } else {
-        store_bf16x32_global(p.out + (size_t(bh) * p.TP + t) * 128 + 32 * c, a);
+        store_bf16x32_global(p.out + (size_t(bh) * p.TP + t) * 128 + col0, a);
       }
       if (READOUT) {
         // z = U(lam) raw, from the bf16-rounded raw that is saved for the backward pass
@@ -441,11 +448,11 @@ __global__ void __launch_bounds__(128, 1)
         for (int i = 0; i < 32; i += 2) {
           const float e = bf16_round(a[i]), o = bf16_round(a[i + 1]);
           float sn, cs;
-          __sincosf(clock_phase(lam, 16 * c + i / 2), &sn, &cs);
+          __sincosf(clock_phase(lam, col0 / 2 + i / 2), &sn, &cs);
           a[i] = cs * e - sn * o;
           a[i + 1] = sn * e + cs * o;
         }
-        store_row32_bf16(sK + 32768 + (c >> 1) * 16384, tid, (c & 1) * 4, a);
+        store_row32_bf16(sK + 32768 + half * 16384, r, c * 4, a);
       }
     }
   }
@@ -470,36 +477,30 @@ __global__ void __launch_bounds__(128, 1)
     __syncwarp();
     if (!mbar_wait(&bar_m[3], 0)) ok = false;
     tc_fence_after();
-    if (ok) {
-      // softmax over the 127 active slots, one token row per thread
-      float mx = -1e30f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(lane_tmem + 32 * c, v);
+    // softmax over the 127 active slots; each thread holds half of its token's row
+    float l[64];
+    tmem_ld32(lane_tmem + half * 64, *reinterpret_cast<float(*)[32]>(l));
+    tmem_ld32(lane_tmem + half * 64 + 32, *reinterpret_cast<float(*)[32]>(l + 32));
+    float mx = -1e30f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (32 * c + i < 127) mx = fmaxf(mx, v[i]);
-      }
-      float sum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(lane_tmem + 32 * c, v);
+    for (int i = 0; i < 64; ++i)
+      if (half * 64 + i < 127) mx = fmaxf(mx, l[i]);
+    xch[half][r] = mx;
+    __syncthreads();
+    mx = fmaxf(xch[0][r], xch[1][r]);
+    float sum = 0.f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (32 * c + i < 127) sum += __expf(v[i] - mx);
-      }
-      const float inv = 1.f / sum;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(lane_tmem + 32 * c, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = (32 * c + i < 127) ? __expf(v[i] - mx) * inv : 0.f;
-        store_row32_bf16(sP + (c >> 1) * 16384, tid, (c & 1) * 4, v);
-      }
+    for (int i = 0; i < 64; ++i) {
+      l[i] = (half * 64 + i < 127) ? __expf(l[i] - mx) : 0.f;
+      sum += l[i];
     }
+    __syncthreads();
+    xch[half][r] = sum;
+    __syncthreads();
+    const float inv = 1.f / (xch[0][r] + xch[1][r]);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) l[i] *= inv;
+    if (ok) store_row64_bf16(sP + half * 16384, r, l);
     fence_async_smem();
     tc_fence_before();
     ok = __syncthreads_and(ok);
@@ -520,28 +521,28 @@ __global__ void __launch_bounds__(128, 1)
     tc_fence_after();
     if (ok) {
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
+        const int col0 = half * 64 + 32 * c;
         float v[32];
-        tmem_ld32(lane_tmem + 128 + 32 * c, v);
+        tmem_ld32(lane_tmem + 128 + col0, v);
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           float sn, cs;
-          __sincosf(clock_phase(lam, 16 * c + i / 2), &sn, &cs);
+          __sincosf(clock_phase(lam, col0 / 2 + i / 2), &sn, &cs);
           const float e = v[i], o = v[i + 1];
           v[i] = cs * e + sn * o;
           v[i + 1] = -sn * e + cs * o;
         }
-        store_bf16x32_global(p.weights + (size_t(bh) * p.TP + t) * 128 + 32 * c, v);
+        store_bf16x32_global(p.weights + (size_t(bh) * p.TP + t) * 128 + col0, v);
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (tid < 32) {
+  if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
 }
-
 
 }  // namespace cyfa

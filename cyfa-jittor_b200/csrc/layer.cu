@@ -456,4 +456,25 @@ __global__ void __launch_bounds__(1024) strided_column_sum_kernel(const float* p
   }
 }
 
+// The four gate-parameter gradients from the [rows, 4H] partials of
+// gate_act_bwd_kernel (dA_log | ddt_bias | db_bias | dd_bias), fixed order.
+__global__ void __launch_bounds__(1024) gate_param_sum_kernel(const float* part, int rows, int H,
+                                                              float* dA, float* ddt, float* dbb,
+                                                              float* ddb) {
+  __shared__ float red[1024];
+  float* outs[4] = {dA, ddt, dbb, ddb};
+  for (int c = 0; c < 4 * H; ++c) {
+    float s = 0.f;
+    for (int r = threadIdx.x; r < rows; r += 1024) s += part[size_t(r) * 4 * H + c];
+    red[threadIdx.x] = s;
+    __syncthreads();
+    for (int w = 512; w > 0; w >>= 1) {
+      if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
+      __syncthreads();
+    }
+    if (threadIdx.x == 0 && outs[c / H]) outs[c / H][c % H] = red[0];
+    __syncthreads();
+  }
+}
+
 }  // namespace cyfa

@@ -10,7 +10,7 @@ static int conv_bwd_rows(int B) { return B * kConvSplit; }
 
 static int gate_bwd_blocks(long long n) {
   const long long want = (n + 255) / 256;
-  return int(want < 592 ? want : 592);
+  return int(want < 296 ? want : 296);
 }
 
 static int norm_bwd_blocks(int rows) {
@@ -150,17 +150,8 @@ int cyfa_gate_act_bwd(const void* a, long long a_stride, const void* b, long lon
   if (rc) return rc;
   // partial columns: dA_log | ddt_bias | db_bias | dd_bias, each H wide
   CYFA_LAUNCH("column_sum", s,
-              (strided_column_sum_kernel<<<1, 1024, 0, s>>>(part, dA_log, nblk, H, 4 * H)));
-  CYFA_LAUNCH("column_sum", s,
-              (strided_column_sum_kernel<<<1, 1024, 0, s>>>(part + H, ddt_bias, nblk, H, 4 * H)));
-  if (db_bias)
-    CYFA_LAUNCH("column_sum", s,
-                (strided_column_sum_kernel<<<1, 1024, 0, s>>>(part + 2 * H, db_bias, nblk, H,
-                                                              4 * H)));
-  if (dd_bias)
-    CYFA_LAUNCH("column_sum", s,
-                (strided_column_sum_kernel<<<1, 1024, 0, s>>>(part + 3 * H, dd_bias, nblk, H,
-                                                              4 * H)));
+              (gate_param_sum_kernel<<<1, 1024, 0, s>>>(part, nblk, H, dA_log, ddt_bias, db_bias,
+                                                        dd_bias)));
   return launch_status();
 }
 

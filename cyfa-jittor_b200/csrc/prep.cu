@@ -245,12 +245,12 @@ struct TokenBwdParams {
   const float* kw;
   const float* q_rs;        // [B,H,TP]
   const float* k_rs;
-  const float* dqn;         // [B,H,TP,K] fp32 gradient of the normalised q
-  const float* dkn;
+  const void* dqn;          // [B,H,TP,K] gradient of the normalised q (fp32 or bf16)
+  const void* dkn;
   const float* lam;         // [B,H,TP]
   const float* beta_h;
-  const float* dw;          // [B,H,TP,128] gradient of the write vector
-  const float* dw_b;        // second term of the write-vector gradient, or null
+  const void* dw;           // [B,H,TP,128] gradient of the write vector (fp32 or bf16)
+  const void* dw_b;         // second term of the write-vector gradient, or null
   __nv_bfloat16* dq;        // [B,T,H,K]
   __nv_bfloat16* dk;
   float* dqw_part;          // [gridDim.x, K]
@@ -264,7 +264,24 @@ struct TokenBwdParams {
 // 8 warps per block; warp w of block b handles rows (b*8 + w) + i*gridDim.x*8.
 // Each block writes one row of norm-weight partial sums (its rows, fixed order),
 // so the partial matrices have gridDim.x rows.
-template <int K>
+template <int E, typename GT>
+__device__ __forceinline__ void load_grad_vec(const void* base, size_t off, float* f) {
+  if constexpr (sizeof(GT) == 4)
+    load_f32_vec<E>(static_cast<const float*>(base) + off, f);
+  else
+    load_bf16_vec<E>(static_cast<const __nv_bfloat16*>(base) + off, f);
+}
+template <typename GT>
+__device__ __forceinline__ float2 load_grad_pair(const void* base, size_t off) {
+  if constexpr (sizeof(GT) == 4)
+    return *reinterpret_cast<const float2*>(static_cast<const float*>(base) + off);
+  else
+    return __bfloat1622float2(
+        *reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(base) + off));
+}
+
+// GT: element type of the incoming gradients (dqn, dkn, dw, dw_b).
+template <int K, typename GT>
 __global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
   constexpr int E = K / 32;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -285,8 +302,8 @@ __global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
     if (real) {
       load_bf16_vec<E>(p.q + tok * p.q_stride + col, xq);
       load_bf16_vec<E>(p.k + tok * p.k_stride + col, xk);
-      load_f32_vec<E>(p.dqn + row * K + lane * E, gq);
-      load_f32_vec<E>(p.dkn + row * K + lane * E, gk);
+      load_grad_vec<E, GT>(p.dqn, row * K + lane * E, gq);
+      load_grad_vec<E, GT>(p.dkn, row * K + lane * E, gk);
     }
     const float qr = real ? p.q_rs[row] : 0.f, kr = real ? p.k_rs[row] : 0.f;
     float dotq = 0.f, dotk = 0.f;
@@ -325,9 +342,9 @@ __global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
       float sn, cs;
       sincosf(clock_phase(lam, pair), &sn, &cs);
       const float sc = atom_scale(pair);
-      float2 dwp = reinterpret_cast<const float2*>(p.dw + row * 128)[pair];
+      float2 dwp = load_grad_pair<GT>(p.dw, row * 128 + 2 * pair);
       if (p.dw_b) {
-        const float2 e2 = reinterpret_cast<const float2*>(p.dw_b + row * 128)[pair];
+        const float2 e2 = load_grad_pair<GT>(p.dw_b, row * 128 + 2 * pair);
         dwp.x += e2.x;
         dwp.y += e2.y;
       }
@@ -369,8 +386,6 @@ inline int token_bwd_blocks(size_t rows) {
   return int(want < 296 ? want : 296);
 }
 
-template __global__ void token_bwd_kernel<256>(TokenBwdParams);
-template __global__ void token_bwd_kernel<128>(TokenBwdParams);
 
 struct GatesBwdParams {
   const float* dG;       // [B,H,TP] gradient of the in-tile gate cumsum (natural log)
