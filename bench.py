@@ -15,6 +15,7 @@ the reference itself has no CPU path and needs Jittor) on the host cores.
 import argparse
 import csv
 import datetime
+import gc
 import io
 import json
 import math
@@ -279,7 +280,8 @@ def run_cyfa(args, rank, world, local_rank):
     import torch.distributed as dist
 
     from cyclic_flow_attention import CyclicFlowAttention, _lib
-    from cyclic_flow_attention.distributed import allreduce_gradients
+    from cyclic_flow_attention.distributed import GradientBuckets
+    from cyclic_flow_attention.graphs import GraphedStep
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -300,9 +302,12 @@ def run_cyfa(args, rank, world, local_rank):
     flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
     peaks, peak_kind = _peaks()
 
+    # gradient averaging over ranks, bucketed and overlapped with the backward
+    buckets = GradientBuckets(params) if world > 1 else None
+
     def allreduce_grads():
-        if world > 1:
-            allreduce_gradients(params)
+        if buckets is not None:
+            buckets.finish()
 
     def step(xin, dyin):
         # training step with the objective loss = <y, dy>: dL/dy = dy
@@ -319,25 +324,27 @@ def run_cyfa(args, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        step(x, dy)
+    # the whole step (forward, backward, gradient all-reduce) as one CUDA graph,
+    # captured after W eager warm-up steps; inputs live at fixed device addresses
+    graphed = GraphedStep(step, [x, dy], params, warmup=args.warmup)
+    for _ in range(3):
+        graphed.replay()
     barrier()
 
     # ---- device-resident timing (value): per-step events, L2 flushed between steps
     sampler = ClockSampler(torch.cuda.current_device() if world == 1 else local_rank)
     sampler.start()
     time.sleep(0.3)
-    launches0 = _lib.launch_count()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     barrier()
     for a, b in evs:
         flush.fill_(1)
         a.record()
-        step(x, dy)
+        graphed.replay()
         b.record()
     barrier()
-    launches = _lib.launch_count() - launches0
+    launches = graphed.library_launches * args.steps
     clocks = sampler.stop()
     total_ms = sum(a.elapsed_time(b) for a, b in evs)
     t = torch.tensor([total_ms], device=dev)
@@ -347,8 +354,9 @@ def run_cyfa(args, rank, world, local_rank):
     value = world * B * T / (ms_per_step / 1000.0)
 
     # ---- end to end: every step copies its inputs from pinned host memory and
-    # reads its loss back.  The next step's copy runs on a side stream while the
-    # current step computes (double-buffered device inputs), as a data loader would.
+    # reads its loss back.  The next step's host-to-device copy runs on a side
+    # stream into a staging buffer while the current step computes, as a data
+    # loader would; the step then moves it into the graph's input buffers.
     copy_stream = torch.cuda.Stream(device=dev)
     bufs = [(torch.empty_like(x), torch.empty_like(dy)) for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
@@ -374,7 +382,7 @@ def run_cyfa(args, rank, world, local_rank):
         main.wait_event(copied[b])
         if i + 1 < args.steps:
             start_copy(i + 1)
-        loss = step(bufs[b][0], bufs[b][1])
+        loss = graphed(bufs[b][0], bufs[b][1])
         done[b].record(main)
         loss.item()
     e_b.record()
@@ -428,7 +436,8 @@ def run_cyfa(args, rank, world, local_rank):
             "config": {"workload": "cyfa_layer_fwd_bwd (BASELINE configs[2])", **CFG,
                        "global_batch": B * world, "seq_len": T,
                        "parallelism": f"dp{world} (batch x head sharded, grad all-reduce)",
-                       "l2": "flushed between timed steps (2x126 MiB write outside the events)"},
+                       "l2": "flushed between timed steps (2x126 MiB write outside the events)",
+                       "launch": "whole step (fwd, bwd, grad all-reduce) replayed as one CUDA graph"},
             "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
@@ -437,6 +446,10 @@ def run_cyfa(args, rank, world, local_rank):
             "decode": decode,
         }
         print(json.dumps(line), flush=True)
+    # a graph that holds NCCL calls must be gone before the process group is
+    graphed = None
+    gc.collect()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

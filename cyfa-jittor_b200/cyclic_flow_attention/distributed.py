@@ -1,11 +1,15 @@
 """Data-parallel plumbing for multi-GPU CyFA training (one process per GPU).
 
 The CyFA op shards over (batch x head) with no exchange inside it, so a step
-on N GPUs is: each rank runs its own batch shard, then the weight gradients are
-averaged with one flat all-reduce (the reference averages one flat fp32 bucket
-with Jittor MPI, training/optim.py:52-63).  NCCL over NVLink on B200; the same
-code runs on gloo for CPU tests.
+on N GPUs is: each rank runs its own batch shard, and the weight gradients are
+averaged across ranks (the reference averages one flat fp32 bucket with Jittor
+MPI, training/optim.py:52-63).  `allreduce_gradients` is that single flat
+bucket after the backward; `GradientBuckets` splits it into buckets that are
+all-reduced while the backward is still running.  NCCL over NVLink on B200; the
+same code runs on gloo for CPU tests.
 """
+
+import contextlib
 
 import torch
 import torch.distributed as dist
@@ -52,6 +56,126 @@ def allreduce_gradients(params, group=None, op="avg"):
         else:
             p.grad.copy_(g)
         off += n
+
+
+class GradientBuckets:
+    """Bucketed gradient averaging overlapped with the backward pass.
+
+    Parameters are grouped, in reverse registration order (the order in which
+    backward produces their gradients), into fp32 buckets of about
+    `bucket_bytes`.  A post-accumulate-grad hook copies each gradient into its
+    bucket slot as soon as autograd has it; a completed bucket is all-reduced
+    asynchronously while the rest of the backward runs.  Buckets are launched
+    strictly in index order, so every rank issues the same collectives in the
+    same order even if its gradients arrive in another order.  `finish()`
+    launches what is left (parameters without a gradient contribute zeros),
+    waits, and writes the averages back into `.grad`.
+
+    The reference averages one flat fp32 bucket after the backward
+    (training/optim.py:52-63); the arithmetic is the same, the transfer overlaps.
+    """
+
+    def __init__(self, params, group=None, bucket_bytes=8 << 20):
+        self.params = [p for p in params if p.requires_grad]
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.avg_op = dist.get_backend(group) == "nccl"
+        order = list(reversed(self.params))
+        self.buckets = []
+        cur, size = [], 0
+        for p in order:
+            cur.append(p)
+            size += p.numel() * 4
+            if size >= bucket_bytes:
+                self.buckets.append(cur)
+                cur, size = [], 0
+        if cur:
+            self.buckets.append(cur)
+        self.flat = []
+        self.slot = {}
+        for i, bucket in enumerate(self.buckets):
+            n = sum(p.numel() for p in bucket)
+            flat = torch.zeros(n, dtype=torch.float32, device=bucket[0].device)
+            off = 0
+            for p in bucket:
+                self.slot[p] = (i, flat[off:off + p.numel()])
+                off += p.numel()
+            self.flat.append(flat)
+        self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.params]
+        self.sync = True
+        self._reset()
+
+    def _reset(self):
+        self.pending = [len(b) for b in self.buckets]
+        self.filled = [set() for _ in self.buckets]
+        self.works = [None] * len(self.buckets)
+        self.next = 0
+
+    @contextlib.contextmanager
+    def no_sync(self):
+        """Backward passes inside accumulate locally only (gradient accumulation
+        over micro-batches); the last backward, outside, averages the sums."""
+        self.sync = False
+        try:
+            yield
+        finally:
+            self.sync = True
+
+    def _on_grad(self, p):
+        if self.world == 1 or not self.sync:
+            return
+        i, view = self.slot[p]
+        if p in self.filled[i]:
+            return
+        view.copy_(p.grad.reshape(-1))
+        self.filled[i].add(p)
+        self.pending[i] -= 1
+        self._launch_ready()
+
+    def _launch(self, i):
+        op = dist.ReduceOp.AVG if self.avg_op else dist.ReduceOp.SUM
+        self.works[i] = dist.all_reduce(self.flat[i], op=op, group=self.group, async_op=True)
+        self.next = i + 1
+
+    def _launch_ready(self):
+        while self.next < len(self.buckets) and self.pending[self.next] == 0:
+            self._launch(self.next)
+
+    def finish(self):
+        """Completes the averaging of this step's gradients (call after backward)."""
+        if self.world == 1:
+            self._reset()
+            return
+        for i in range(self.next, len(self.buckets)):
+            for p in self.buckets[i]:
+                view = self.slot[p][1]
+                if p in self.filled[i]:
+                    continue
+                if p.grad is None:
+                    view.zero_()
+                else:
+                    view.copy_(p.grad.reshape(-1))
+            self._launch(i)
+        dsts, srcs = [], []
+        for i, bucket in enumerate(self.buckets):
+            self.works[i].wait()
+            if not self.avg_op:
+                self.flat[i].div_(self.world)
+            for p in bucket:
+                view = self.slot[p][1].view_as(p)
+                if p.grad is None:
+                    p.grad = view.to(p.dtype).clone()
+                else:
+                    dsts.append(p.grad)
+                    srcs.append(view)
+        if dsts:
+            torch._foreach_copy_(dsts, srcs)
+        self._reset()
+
+    def remove(self):
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []
 
 
 def broadcast_parameters(params, src=0, group=None):

@@ -94,3 +94,82 @@ def test_shard_batch_rejects_uneven():
 
     with pytest.raises(ValueError):
         shard_batch(torch.zeros(5, 2), 0, 2)
+
+
+def _bucket_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "cyfa-jittor_b200"))
+    from cyclic_flow_attention.distributed import (
+        GradientBuckets,
+        allreduce_gradients,
+        broadcast_parameters,
+    )
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        torch.manual_seed(rank)
+
+        def make():
+            torch.manual_seed(7)
+            m = torch.nn.Sequential(torch.nn.Linear(5, 7), torch.nn.Tanh(),
+                                    torch.nn.Linear(7, 3), torch.nn.Linear(3, 2))
+            m.unused = torch.nn.Parameter(torch.ones(4))  # never receives a gradient
+            return m
+
+        ref, net = make(), make()
+        broadcast_parameters(ref.parameters())
+        broadcast_parameters(net.parameters())
+        # tiny buckets: several collectives, launched while backward runs
+        buckets = GradientBuckets(net.parameters(), bucket_bytes=64)
+        xs = [torch.randn(6, 5) for _ in range(3)]
+        out = {"n_buckets": len(buckets.buckets)}
+        for step in range(2):  # the same buckets are reused every step
+            for m in (ref, net):
+                for p in m.parameters():
+                    p.grad = None
+            # micro-batch accumulation: the first two backward passes stay local
+            with buckets.no_sync():
+                for x in xs[:2]:
+                    net(x * (step + 1)).pow(2).sum().backward()
+            net(xs[2] * (step + 1)).pow(2).sum().backward()
+            buckets.finish()
+            for x in xs:
+                ref(x * (step + 1)).pow(2).sum().backward()
+            allreduce_gradients(ref.parameters())
+            out[f"ref{step}"] = [(p.grad if p.grad is not None else torch.zeros_like(p)).tolist()
+                                 for p in ref.parameters()]
+            out[f"net{step}"] = [p.grad.tolist() for p in net.parameters()]
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_buckets_match_flat_allreduce():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_bucket_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, out = q.get(timeout=120)
+        res[r] = out
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[0]["n_buckets"] > 2
+    for r in range(world):
+        for step in range(2):
+            for a, b in zip(res[r][f"ref{step}"], res[r][f"net{step}"]):
+                assert torch.allclose(torch.tensor(a), torch.tensor(b), rtol=1e-6, atol=1e-6)
+    for step in range(2):
+        for a, b in zip(res[0][f"net{step}"], res[1][f"net{step}"]):
+            assert torch.equal(torch.tensor(a), torch.tensor(b))
