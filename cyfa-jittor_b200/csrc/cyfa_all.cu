@@ -12,3 +12,4 @@
 #include "chunk_api.cu"
 #include "layer_api.cu"
 #include "noalloc.cu"
+#include "gradbuf.cu"

@@ -39,6 +39,8 @@ _SIGNATURES = {
                             ctypes.c_size_t, _vp],
     "cyfa_gated_norm_bwd_static": [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp],
     "cyfa_chunk_bwd": [_vp, _vp, ctypes.c_size_t, _vp, ctypes.c_size_t, _vp],
+    "cyfa_bucket_gather": [_vp, _i, _vp, _vp],
+    "cyfa_bucket_scatter": [_vp, _i, _vp, _f, _vp],
 }
 
 # size queries (restype size_t)
@@ -49,6 +51,13 @@ _SIZE_QUERIES = {
     "cyfa_gate_act_work_bytes": [_i] * 2,
     "cyfa_gated_norm_work_bytes": [_i] * 2,
 }
+
+
+class BucketPiece(ctypes.Structure):
+    """cyfa_bucket_piece: one gradient tensor inside a flat fp32 bucket."""
+
+    _fields_ = [("ptr", ctypes.c_void_p), ("n", ctypes.c_longlong),
+                ("offset", ctypes.c_longlong), ("dtype", ctypes.c_int)]
 
 
 class CyfaError(RuntimeError):

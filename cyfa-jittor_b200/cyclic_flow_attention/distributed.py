@@ -14,6 +14,8 @@ import contextlib
 import torch
 import torch.distributed as dist
 
+from . import _lib
+
 
 def shard_batch(x, rank, world):
     """Rank's contiguous slice of the batch dimension (weak or strong scaling)."""
@@ -61,11 +63,13 @@ def allreduce_gradients(params, group=None, op="avg"):
 class GradientBuckets:
     """Bucketed gradient averaging overlapped with the backward pass.
 
-    Parameters are grouped, in reverse registration order (the order in which
-    backward produces their gradients), into fp32 buckets of about
-    `bucket_bytes`.  A post-accumulate-grad hook copies each gradient into its
+    Parameters are grouped into fp32 buckets of about `bucket_bytes`: first in
+    reverse registration order, then, from the second synced step on, in the
+    order in which the first backward produced their gradients.  A post-accumulate-grad hook copies each gradient into its
     bucket slot as soon as autograd has it; a completed bucket is all-reduced
-    asynchronously while the rest of the backward runs.  Buckets are launched
+    asynchronously while the rest of the backward runs (on CUDA one library
+    kernel gathers a bucket's bf16/f32 gradients into it and one scatters the
+    averages back).  Buckets are launched
     strictly in index order, so every rank issues the same collectives in the
     same order even if its gradients arrive in another order.  `finish()`
     launches what is left (parameters without a gradient contribute zeros),
@@ -78,32 +82,54 @@ class GradientBuckets:
     def __init__(self, params, group=None, bucket_bytes=8 << 20):
         self.params = [p for p in params if p.requires_grad]
         self.group = group
+        self.bucket_bytes = bucket_bytes
         self.world = dist.get_world_size(group)
         self.avg_op = dist.get_backend(group) == "nccl"
-        order = list(reversed(self.params))
+        self._arrivals = []  # parameter indices in the order of the first backward
+        self._param_index = {id(p): k for k, p in enumerate(self.params)}
+        self._rebuilt = False
+        self._build(list(reversed(self.params)))
+        self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.params]
+        self.sync = True
+        self._reset()
+
+    def _build(self, order):
         self.buckets = []
         cur, size = [], 0
         for p in order:
             cur.append(p)
             size += p.numel() * 4
-            if size >= bucket_bytes:
+            if size >= self.bucket_bytes:
                 self.buckets.append(cur)
                 cur, size = [], 0
         if cur:
             self.buckets.append(cur)
         self.flat = []
-        self.slot = {}
+        self.slot = {}  # param -> (bucket, element offset, flat view)
         for i, bucket in enumerate(self.buckets):
-            n = sum(p.numel() for p in bucket)
-            flat = torch.zeros(n, dtype=torch.float32, device=bucket[0].device)
-            off = 0
+            offs, off = [], 0
             for p in bucket:
-                self.slot[p] = (i, flat[off:off + p.numel()])
-                off += p.numel()
+                offs.append(off)
+                off += (p.numel() + 63) // 64 * 64  # 256-byte aligned slots
+            flat = torch.zeros(off, dtype=torch.float32, device=bucket[0].device)
+            for p, o in zip(bucket, offs):
+                self.slot[p] = (i, o, flat[o:o + p.numel()])
             self.flat.append(flat)
-        self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.params]
-        self.sync = True
-        self._reset()
+
+    def _rebuild_by_arrival(self):
+        """After the first synced step: regroup the buckets in the order in which
+        that backward produced the gradients (rank 0's order, broadcast, so all
+        ranks agree), so that early buckets fill early.  Not during stream capture."""
+        self._rebuilt = True
+        if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
+            return
+        seen = list(dict.fromkeys(self._arrivals))
+        seen_set = set(seen)
+        rest = [k for k in reversed(range(len(self.params))) if k not in seen_set]
+        order = torch.tensor(seen + rest, dtype=torch.int64, device=self.flat[0].device)
+        dist.broadcast(order, src=dist.get_global_rank(self.group, 0) if self.group else 0,
+                       group=self.group)
+        self._build([self.params[k] for k in order.tolist()])
 
     def _reset(self):
         self.pending = [len(b) for b in self.buckets]
@@ -124,15 +150,66 @@ class GradientBuckets:
     def _on_grad(self, p):
         if self.world == 1 or not self.sync:
             return
-        i, view = self.slot[p]
+        i = self.slot[p][0]
         if p in self.filled[i]:
             return
-        view.copy_(p.grad.reshape(-1))
+        if not self._rebuilt:
+            self._arrivals.append(self._param_index[id(p)])
         self.filled[i].add(p)
         self.pending[i] -= 1
         self._launch_ready()
 
+    def _pieces(self, i):
+        """Bucket i's gradients as library pieces, or None if one of them does
+        not fit the kernel (not CUDA, other dtype, non-contiguous, unaligned)."""
+        pieces = []
+        for p in self.buckets[i]:
+            g = p.grad
+            if g is None:
+                continue
+            if (not g.is_cuda or g.dtype not in (torch.float32, torch.bfloat16)
+                    or not g.is_contiguous() or g.data_ptr() % 16):
+                return None
+            pieces.append((g.data_ptr(), g.numel(), self.slot[p][1],
+                           0 if g.dtype == torch.float32 else 1))
+        arr = (_lib.BucketPiece * max(len(pieces), 1))()
+        for k, pc in enumerate(pieces):
+            arr[k] = _lib.BucketPiece(*pc)
+        return arr, len(pieces)
+
+    def _gather(self, i):
+        """Copies bucket i's gradients into its flat fp32 buffer; slots of
+        parameters without a gradient are zero."""
+        flat = self.flat[i]
+        missing = [p for p in self.buckets[i] if p.grad is None]
+        for p in missing:
+            self.slot[p][2].zero_()
+        packed = self._pieces(i) if flat.is_cuda else None
+        if packed is not None:
+            arr, n = packed
+            _lib.call("cyfa_bucket_gather", arr, n, _lib.ptr(flat), _lib.stream())
+            return
+        for p in self.buckets[i]:
+            if p.grad is not None:
+                self.slot[p][2].copy_(p.grad.reshape(-1))
+
+    def _scatter(self, i, scale):
+        """Writes scale * bucket i back into the gradients (allocating missing ones)."""
+        flat = self.flat[i]
+        for p in self.buckets[i]:
+            if p.grad is None:
+                p.grad = torch.empty_like(p)
+        packed = self._pieces(i) if flat.is_cuda else None
+        if packed is not None:
+            arr, n = packed
+            _lib.call("cyfa_bucket_scatter", arr, n, _lib.ptr(flat), float(scale), _lib.stream())
+            return
+        for p in self.buckets[i]:
+            view = self.slot[p][2].view_as(p)
+            p.grad.copy_(view * scale if scale != 1.0 else view)
+
     def _launch(self, i):
+        self._gather(i)
         op = dist.ReduceOp.AVG if self.avg_op else dist.ReduceOp.SUM
         self.works[i] = dist.all_reduce(self.flat[i], op=op, group=self.group, async_op=True)
         self.next = i + 1
@@ -147,29 +224,13 @@ class GradientBuckets:
             self._reset()
             return
         for i in range(self.next, len(self.buckets)):
-            for p in self.buckets[i]:
-                view = self.slot[p][1]
-                if p in self.filled[i]:
-                    continue
-                if p.grad is None:
-                    view.zero_()
-                else:
-                    view.copy_(p.grad.reshape(-1))
             self._launch(i)
-        dsts, srcs = [], []
-        for i, bucket in enumerate(self.buckets):
+        scale = 1.0 if self.avg_op else 1.0 / self.world
+        for i in range(len(self.buckets)):
             self.works[i].wait()
-            if not self.avg_op:
-                self.flat[i].div_(self.world)
-            for p in bucket:
-                view = self.slot[p][1].view_as(p)
-                if p.grad is None:
-                    p.grad = view.to(p.dtype).clone()
-                else:
-                    dsts.append(p.grad)
-                    srcs.append(view)
-        if dsts:
-            torch._foreach_copy_(dsts, srcs)
+            self._scatter(i, scale)
+        if not self._rebuilt:
+            self._rebuild_by_arrival()
         self._reset()
 
     def remove(self):

@@ -265,6 +265,26 @@ int cyfa_gated_norm_bwd_static(const void* x, const void* gate, const float* w, 
 int cyfa_selftest_umma(const void* a, const void* b, float* c, int K, int N, int a_mn,
                        int b_mn, void* stream);
 
+/* ---------------------------------------------------------------- gradient buckets
+ * Data-parallel plumbing: the weight gradients of a bucket are gathered into one
+ * flat fp32 buffer for the all-reduce and the averaged values are written back.
+ * The reference flattens its fp32 gradient bucket with Jittor ops before the MPI
+ * all-reduce (training/optim.py:52-63); these replace those copies with one
+ * launch per bucket each way. */
+typedef struct {
+  void* ptr;          /* the tensor's contiguous data, 16-byte aligned */
+  long long n;        /* elements */
+  long long offset;   /* first element in the flat bucket, a multiple of 8 */
+  int dtype;          /* 0 = f32, 1 = bf16 */
+} cyfa_bucket_piece;
+
+/* flat[offset + i] = float(ptr[i]) for every piece (one launch per 64 pieces). */
+int cyfa_bucket_gather(const cyfa_bucket_piece* pieces, int count, float* flat, void* stream);
+
+/* ptr[i] = dtype(scale * flat[offset + i]) for every piece (one launch per 64 pieces). */
+int cyfa_bucket_scatter(const cyfa_bucket_piece* pieces, int count, const float* flat,
+                        float scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
