@@ -310,12 +310,14 @@ def run_cyfa(args, rank, world, local_rank):
             buckets.finish()
 
     def step(xin, dyin):
-        # training step with the objective loss = <y, dy>: dL/dy = dy
+        # training step with the objective loss = <y, dy>: the backward is seeded
+        # with dL/dy = dy, and the loss value is formed for the host to read
         for p in params:
             p.grad = None
         y, _ = layer(xin)
-        loss = torch.dot(y.reshape(-1), dyin.reshape(-1))
-        loss.backward()
+        y.backward(dyin)
+        with torch.no_grad():
+            loss = torch.dot(y.reshape(-1), dyin.reshape(-1))
         allreduce_grads()
         return loss
 

@@ -519,9 +519,12 @@ __global__ void __launch_bounds__(128) dtable_reduce_kernel(const float* part, f
 
 // Fixed-order column sums of a [rows, cols] partial matrix: out[c] = sum_r part[r][c].
 // 1024 threads: 32 columns x 32 row lanes, each lane with 4 independent accumulators.
+// Columns c >= split go to out_hi[c - split] instead of out[c].
 __global__ void __launch_bounds__(1024) column_sum_kernel(const float* part, float* out, int rows,
                                                           int cols, const float* part2 = nullptr,
-                                                          float* out2 = nullptr) {
+                                                          float* out2 = nullptr,
+                                                          int split = 0x7fffffff,
+                                                          float* out_hi = nullptr) {
   __shared__ float acc[32][33];
   if (blockIdx.y == 1) {  // second (part, out) pair
     part = part2;
@@ -547,7 +550,8 @@ __global__ void __launch_bounds__(1024) column_sum_kernel(const float* part, flo
     float t = 0.f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) t += acc[i][threadIdx.x];
-    out[c] = t;
+    if (c < split) out[c] = t;
+    else out_hi[c - split] = t;
   }
 }
 

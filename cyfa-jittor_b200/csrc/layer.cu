@@ -322,8 +322,11 @@ struct GatedNormParams {
   const __nv_bfloat16* dy;    // backward
   __nv_bfloat16* dx;
   __nv_bfloat16* dgate;
-  float* part;                // [gridDim.x, D] partial weight gradient
+  float* part;                // [gridDim.x, part_cols] partials: weight [D] | gate bias [H*D]
   int rows;
+  const __nv_bfloat16* gbias = nullptr;  // optional gate bias [H*D]; rows are (token, head)
+  int H = 1;                             // heads per token (rows % H = head)
+  int part_cols = 0;                     // 0: D (no bias partials); else D + H*D
 };
 
 // One warp per row (grid-strided), D = 32 * E.
@@ -343,6 +346,12 @@ __global__ void __launch_bounds__(256) gated_norm_fwd_kernel(GatedNormParams p) 
       x[e] = __bfloat162float(p.x[size_t(row) * D + lane * E + e]);
       g[e] = __bfloat162float(p.gate[size_t(row) * D + lane * E + e]);
     }
+  }
+  if (p.gbias) {
+    float b[E];
+    load_bf16_vec<E>(p.gbias + size_t(row % p.H) * D + lane * E, b);
+#pragma unroll
+    for (int e = 0; e < E; ++e) g[e] += b[e];
   }
   float ss = 0.f;
 #pragma unroll
@@ -365,19 +374,27 @@ __global__ void __launch_bounds__(256) gated_norm_fwd_kernel(GatedNormParams p) 
   }
 }
 
+// With a gate bias the grid is a multiple of H, so every warp's rows belong to
+// one head ((blockIdx.x * 8 + warp) % H) and its bias-gradient partial stays in
+// registers; the block's per-head sums are formed in a fixed warp order.
 template <int E>
 __global__ void __launch_bounds__(256) gated_norm_bwd_kernel(GatedNormParams p) {
   constexpr int D = 32 * E;
   __shared__ float red[8][D];
+  __shared__ float red_b[8][D];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  float acc[E];
+  const bool has_b = p.gbias != nullptr;
+  float acc[E], acc_b[E], bias[E];
 #pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] = 0.f;
+  for (int e = 0; e < E; ++e) acc[e] = acc_b[e] = bias[e] = 0.f;
+  if (has_b) load_bf16_vec<E>(p.gbias + size_t((blockIdx.x * 8 + wid) % p.H) * D + lane * E, bias);
   for (int row = blockIdx.x * 8 + wid; row < p.rows; row += gridDim.x * 8) {
     float x[E], g[E], dy[E];
     load_bf16_vec<E>(p.x + size_t(row) * D + lane * E, x);
     load_bf16_vec<E>(p.gate + size_t(row) * D + lane * E, g);
     load_bf16_vec<E>(p.dy + size_t(row) * D + lane * E, dy);
+#pragma unroll
+    for (int e = 0; e < E; ++e) g[e] += bias[e];
 #pragma unroll
     for (int e = 0; e < E; ++e) x[e] *= p.scale;
     const float rs = p.rstd[row];
@@ -401,15 +418,32 @@ __global__ void __launch_bounds__(256) gated_norm_bwd_kernel(GatedNormParams p) 
     for (int e = 0; e < E; ++e) dxv[e] = p.scale * rs * (dn[e] - n[e] * dot);
     store_bf16_vec<E>(p.dx + size_t(row) * D + lane * E, dxv);
     store_bf16_vec<E>(p.dgate + size_t(row) * D + lane * E, dgv);
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc_b[e] += dgv[e];
   }
 #pragma unroll
-  for (int e = 0; e < E; ++e) red[wid][lane * E + e] = acc[e];
+  for (int e = 0; e < E; ++e) {
+    red[wid][lane * E + e] = acc[e];
+    red_b[wid][lane * E + e] = acc_b[e];
+  }
   __syncthreads();
+  const int pc = p.part_cols > 0 ? p.part_cols : D;
+  float* part = p.part + size_t(blockIdx.x) * pc;
   for (int c = threadIdx.x; c < D; c += 256) {
     float s = 0.f;
 #pragma unroll
     for (int k = 0; k < 8; ++k) s += red[k][c];
-    p.part[size_t(blockIdx.x) * D + c] = s;
+    part[c] = s;
+  }
+  if (has_b) {
+    for (int c = threadIdx.x; c < p.H * D; c += 256) {
+      const int h = c / D, d = c % D;
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if ((blockIdx.x * 8 + k) % p.H == h) s += red_b[k][d];
+      part[D + c] = s;
+    }
   }
 }
 
@@ -461,19 +495,15 @@ __global__ void __launch_bounds__(1024) strided_column_sum_kernel(const float* p
 __global__ void __launch_bounds__(1024) gate_param_sum_kernel(const float* part, int rows, int H,
                                                               float* dA, float* ddt, float* dbb,
                                                               float* ddb) {
-  __shared__ float red[1024];
+  // one warp per column; lanes stride the rows, then a fixed shuffle tree
   float* outs[4] = {dA, ddt, dbb, ddb};
-  for (int c = 0; c < 4 * H; ++c) {
+  const int lane = threadIdx.x & 31;
+  for (int c = threadIdx.x >> 5; c < 4 * H; c += 32) {
     float s = 0.f;
-    for (int r = threadIdx.x; r < rows; r += 1024) s += part[size_t(r) * 4 * H + c];
-    red[threadIdx.x] = s;
-    __syncthreads();
-    for (int w = 512; w > 0; w >>= 1) {
-      if (threadIdx.x < w) red[threadIdx.x] += red[threadIdx.x + w];
-      __syncthreads();
-    }
-    if (threadIdx.x == 0 && outs[c / H]) outs[c / H][c % H] = red[0];
-    __syncthreads();
+    for (int r = lane; r < rows; r += 32) s += part[size_t(r) * 4 * H + c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0 && outs[c / H]) outs[c / H][c % H] = s;
   }
 }
 

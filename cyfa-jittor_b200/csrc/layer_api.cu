@@ -197,4 +197,61 @@ int cyfa_gated_norm_bwd(const void* x, const void* gate, const float* w, float s
   return launch_status();
 }
 
+int cyfa_gated_norm_bias_fwd(const void* x, const void* gate, const void* gate_bias, int H,
+                             const float* w, float eps, float scale, void* y, float* rstd,
+                             int rows, int D, void* stream) {
+  CYFA_REQUIRE(x && gate && gate_bias && w && y && rstd, kNullPointer);
+  CYFA_REQUIRE(rows > 0 && H > 0 && rows % H == 0 && (D == 256 || D == 128), kBadShape);
+  CYFA_REQUIRE(aligned(x, 16) && aligned(gate, 16) && aligned(y, 16) && aligned(gate_bias, 16),
+               kMisaligned);
+  GatedNormParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gate),
+                    w, eps, scale, static_cast<__nv_bfloat16*>(y), rstd, nullptr, nullptr, nullptr,
+                    nullptr, rows, static_cast<const __nv_bfloat16*>(gate_bias), H, 0};
+  const unsigned grid = unsigned((rows + 7) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (D == 256) CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<8><<<grid, 256, 0, s>>>(p)));
+  else CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<4><<<grid, 256, 0, s>>>(p)));
+  return launch_status();
+}
+
+// Block count of the biased backward: a multiple of H (each warp stays on one head).
+static int norm_bias_bwd_blocks(int rows, int H) {
+  int n = norm_bwd_blocks(rows);
+  n -= n % H;
+  return n < H ? H : n;
+}
+
+size_t cyfa_gated_norm_bias_work_bytes(int rows, int D, int H) {
+  if (rows <= 0 || D <= 0 || H <= 0) return 0;
+  return size_t(norm_bias_bwd_blocks(rows, H)) * size_t(D + H * D) * sizeof(float);
+}
+
+int cyfa_gated_norm_bias_bwd(const void* x, const void* gate, const void* gate_bias, int H,
+                             const float* w, float scale, const float* rstd, const void* dy,
+                             void* dx, void* dgate, float* dw, float* dgate_bias, int rows, int D,
+                             void* work, size_t work_bytes, void* stream) {
+  CYFA_REQUIRE(x && gate && gate_bias && w && rstd && dy && dx && dgate && dw && dgate_bias && work,
+               kNullPointer);
+  CYFA_REQUIRE(rows > 0 && H > 0 && rows % H == 0 && (D == 256 || D == 128), kBadShape);
+  CYFA_REQUIRE(aligned(gate_bias, 16), kMisaligned);
+  CYFA_REQUIRE(work_bytes >= cyfa_gated_norm_bias_work_bytes(rows, D, H), kWorkspace);
+  float* part = static_cast<float*>(work);
+  const int cols = D + H * D;
+  GatedNormParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gate),
+                    w, 0.f, scale, nullptr, const_cast<float*>(rstd),
+                    static_cast<const __nv_bfloat16*>(dy), static_cast<__nv_bfloat16*>(dx),
+                    static_cast<__nv_bfloat16*>(dgate), part, rows,
+                    static_cast<const __nv_bfloat16*>(gate_bias), H, cols};
+  const int nblk = norm_bias_bwd_blocks(rows, H);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (D == 256) CYFA_LAUNCH("gated_norm_bwd", s, (gated_norm_bwd_kernel<8><<<nblk, 256, 0, s>>>(p)));
+  else CYFA_LAUNCH("gated_norm_bwd", s, (gated_norm_bwd_kernel<4><<<nblk, 256, 0, s>>>(p)));
+  int rc = launch_status();
+  if (rc) return rc;
+  CYFA_LAUNCH("column_sum", s,
+              (column_sum_kernel<<<(cols + 31) / 32, 1024, 0, s>>>(part, dw, nblk, cols, nullptr,
+                                                                  nullptr, D, dgate_bias)));
+  return launch_status();
+}
+
 }  // extern "C"

@@ -38,6 +38,9 @@ _SIGNATURES = {
     "cyfa_gated_norm_bwd": [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp,
                             ctypes.c_size_t, _vp],
     "cyfa_gated_norm_bwd_static": [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp],
+    "cyfa_gated_norm_bias_fwd": [_vp, _vp, _vp, _i, _vp, _f, _f, _vp, _vp, _i, _i, _vp],
+    "cyfa_gated_norm_bias_bwd": [_vp, _vp, _vp, _i, _vp, _f, _vp, _vp, _vp, _vp, _vp, _vp,
+                                 _i, _i, _vp, ctypes.c_size_t, _vp],
     "cyfa_chunk_bwd": [_vp, _vp, ctypes.c_size_t, _vp, ctypes.c_size_t, _vp],
     "cyfa_bucket_gather": [_vp, _i, _vp, _vp],
     "cyfa_bucket_scatter": [_vp, _i, _vp, _f, _vp],
@@ -50,6 +53,7 @@ _SIZE_QUERIES = {
     "cyfa_short_conv_work_bytes": [_i] * 4,
     "cyfa_gate_act_work_bytes": [_i] * 2,
     "cyfa_gated_norm_work_bytes": [_i] * 2,
+    "cyfa_gated_norm_bias_work_bytes": [_i] * 3,
 }
 
 

@@ -112,47 +112,59 @@ class GateActFunction(torch.autograd.Function):
 class GatedNormFunction(torch.autograd.Function):
     """y = RMSNorm(scale * x) * w * sigmoid(gate) over the last dim D of
     x [B,T,H,D], with gate = gate_in @ W^T + b (the output gate's second linear,
-    [B,T,H*D]); returns [B,T,H*D] bf16.  The linear runs on cuBLAS; the bias
-    gradient is a cuBLAS GEMV over the gate gradient."""
+    [B,T,H*D]); returns [B,T,H*D] bf16.  The linear runs on cuBLAS without its
+    bias; the kernels add b and return its gradient (fixed-order sums)."""
 
     @staticmethod
     def forward(ctx, x, gate_in, gate_w, gate_b, weight, eps, scale):
         B, T, H, D = x.shape
         rows = B * T * H
         x = x.to(torch.bfloat16).contiguous()
-        gate = torch.nn.functional.linear(gate_in, gate_w, gate_b).contiguous()
+        gate = torch.nn.functional.linear(gate_in, gate_w).contiguous()
         w = weight.detach().float().contiguous()
         y = torch.empty(B, T, H * D, device=x.device, dtype=torch.bfloat16)
         rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
-        _lib.call("cyfa_gated_norm_fwd", _p(x), _p(gate), _p(w), float(eps), float(scale), _p(y),
-                  _p(rstd), rows, D, _lib.stream())
-        ctx.save_for_backward(x, gate, gate_in, gate_w, w, rstd)
-        ctx.meta = (scale, weight.dtype, gate_b is not None)
+        b = None
+        if gate_b is not None:
+            b = gate_b.detach().to(torch.bfloat16).contiguous()
+            _lib.call("cyfa_gated_norm_bias_fwd", _p(x), _p(gate), _p(b), H, _p(w), float(eps),
+                      float(scale), _p(y), _p(rstd), rows, D, _lib.stream())
+        else:
+            _lib.call("cyfa_gated_norm_fwd", _p(x), _p(gate), _p(w), float(eps), float(scale),
+                      _p(y), _p(rstd), rows, D, _lib.stream())
+        ctx.save_for_backward(x, gate, gate_in, gate_w, w, rstd, b)
+        ctx.meta = (scale, weight.dtype, None if gate_b is None else gate_b.dtype)
         return y
 
     @staticmethod
     def backward(ctx, dy):
-        x, gate, gate_in, gate_w, w, rstd = ctx.saved_tensors
-        scale, wdt, has_b = ctx.meta
+        x, gate, gate_in, gate_w, w, rstd, b = ctx.saved_tensors
+        scale, wdt, bdt = ctx.meta
         B, T, H, D = x.shape
         rows = B * T * H
         dy = dy.to(torch.bfloat16).contiguous()
         dx = torch.empty_like(x)
         dgate = torch.empty_like(gate)
         dw = torch.empty(D, device=x.device, dtype=torch.float32)
-        nbytes = _lib.lib().cyfa_gated_norm_work_bytes(rows, D)
-        work = _work(nbytes, x.device)
-        _lib.call("cyfa_gated_norm_bwd", _p(x), _p(gate), _p(w), float(scale), _p(rstd), _p(dy),
-                  _p(dx), _p(dgate), _p(dw), rows, D, _p(work), _c.c_size_t(nbytes),
-                  _lib.stream())
+        d_gate_b = None
+        if b is not None:
+            db = torch.empty(H * D, device=x.device, dtype=torch.float32)
+            nbytes = _lib.lib().cyfa_gated_norm_bias_work_bytes(rows, D, H)
+            work = _work(nbytes, x.device)
+            _lib.call("cyfa_gated_norm_bias_bwd", _p(x), _p(gate), _p(b), H, _p(w), float(scale),
+                      _p(rstd), _p(dy), _p(dx), _p(dgate), _p(dw), _p(db), rows, D, _p(work),
+                      _c.c_size_t(nbytes), _lib.stream())
+            d_gate_b = db.to(bdt)
+        else:
+            nbytes = _lib.lib().cyfa_gated_norm_work_bytes(rows, D)
+            work = _work(nbytes, x.device)
+            _lib.call("cyfa_gated_norm_bwd", _p(x), _p(gate), _p(w), float(scale), _p(rstd),
+                      _p(dy), _p(dx), _p(dgate), _p(dw), rows, D, _p(work), _c.c_size_t(nbytes),
+                      _lib.stream())
         dg2 = dgate.reshape(-1, H * D)
         gin2 = gate_in.reshape(-1, gate_in.shape[-1])
         d_gate_in = (dg2 @ gate_w).reshape(gate_in.shape)
         d_gate_w = dg2.t() @ gin2
-        d_gate_b = None
-        if has_b:
-            ones = torch.ones(dg2.shape[0], device=x.device, dtype=dg2.dtype)
-            d_gate_b = torch.mv(dg2.t(), ones)
         return dx, d_gate_in, d_gate_w, d_gate_b, dw.to(wdt), None, None
 
 

@@ -243,6 +243,20 @@ int cyfa_gated_norm_bwd(const void* x, const void* gate, const float* w, float s
                         const float* rstd, const void* dy, void* dx, void* dgate, float* dw,
                         int rows, int D, void* work, size_t work_bytes, void* stream);
 
+/* Gated norm with the output gate's bias folded in: sigmoid(gate + b[head])
+ * where rows are (token, head) pairs, head = row % H, b [H*D] bf16 (the bias of
+ * the gate's second linear, reference layers/cyfa.py:292-295,349-350).  The
+ * backward also returns dgate_bias [H*D] f32 (fixed-order sums).  Work buffer:
+ * cyfa_gated_norm_bias_work_bytes(rows, D, H). */
+int cyfa_gated_norm_bias_fwd(const void* x, const void* gate, const void* gate_bias, int H,
+                             const float* w, float eps, float scale, void* y, float* rstd,
+                             int rows, int D, void* stream);
+size_t cyfa_gated_norm_bias_work_bytes(int rows, int D, int H);
+int cyfa_gated_norm_bias_bwd(const void* x, const void* gate, const void* gate_bias, int H,
+                             const float* w, float scale, const float* rstd, const void* dy,
+                             void* dx, void* dgate, float* dw, float* dgate_bias, int rows, int D,
+                             void* work, size_t work_bytes, void* stream);
+
 /* Allocation-free variant of cyfa_gated_norm_bwd, for callers that cannot hand the
  * library a workspace: bindings whose signature carries only the op's tensors, or
  * processes whose device memory belongs entirely to a framework allocator.  No

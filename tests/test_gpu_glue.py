@@ -77,8 +77,8 @@ def test_gate_act(LO):
 
 
 @pytest.mark.parametrize("D", [256, 128])
-def test_gated_norm(LO, D):
-    B, T, H = 2, 70, 3
+@pytest.mark.parametrize("B,T,H", [(2, 70, 3), (4, 700, 4)])
+def test_gated_norm(LO, D, B, T, H):
     gen = torch.Generator().manual_seed(D)
     x = (0.01 * torch.randn(B, T, H, D, generator=gen)).to(torch.bfloat16).cuda().requires_grad_(True)
     gin = torch.randn(B, T, D, generator=gen).to(torch.bfloat16).cuda().requires_grad_(True)
