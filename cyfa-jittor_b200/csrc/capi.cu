@@ -133,8 +133,9 @@ static int token_fwd_launch(const void* q, const void* k, const float* q_norm_we
                    q_rs && k_rs,
                kNullPointer);
   CYFA_REQUIRE(B > 0 && T > 0 && H > 0 && (K == 128 || K == 256), kBadShape);
-  CYFA_REQUIRE(aligned(q, 16) && aligned(k, 16) && q_stride % 8 == 0 && k_stride % 8 == 0 && aligned(qn, 16) && aligned(kn, 16) &&
-                   aligned(w, 16),
+  CYFA_REQUIRE(aligned(q, 16) && aligned(k, 16) && q_stride % 8 == 0 && k_stride % 8 == 0 &&
+                   aligned(qn, 16) && aligned(kn, 16) && aligned(w, 16) &&
+                   aligned(q_norm_weight, 16) && aligned(k_norm_weight, 16),
                kMisaligned);
   const int TP = (T + 127) / 128 * 128;
   TokenFwdParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
@@ -143,7 +144,7 @@ static int token_fwd_launch(const void* q, const void* k, const float* q_norm_we
                    static_cast<__nv_bfloat16*>(w), q_rs, k_rs, B, T, H, TP, q_eps, k_eps,
                    q_stride, k_stride};
   const size_t rows = size_t(B) * H * TP;
-  const dim3 grid(unsigned((rows + 7) / 8));
+  const dim3 grid(unsigned(token_fwd_blocks(rows)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (K == 256) CYFA_LAUNCH("token_fwd", s, token_fwd_kernel<256><<<grid, 256, 0, s>>>(p));
   else CYFA_LAUNCH("token_fwd", s, token_fwd_kernel<128><<<grid, 256, 0, s>>>(p));
@@ -163,6 +164,11 @@ static int token_bwd_launch(const void* q, const void* k, const float* q_norm_we
                    beta_h && dw && dq && dk && dqw_part && dkw_part && dlam && dbeta_h,
                kNullPointer);
   CYFA_REQUIRE(B > 0 && T > 0 && H > 0 && (K == 128 || K == 256), kBadShape);
+  CYFA_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(dq, 16) && aligned(dk, 16) &&
+                   aligned(dqn, 16) && aligned(dkn, 16) && aligned(q_norm_weight, 16) &&
+                   aligned(k_norm_weight, 16) && q_stride % 8 == 0 && k_stride % 8 == 0 &&
+                   dq_stride % 8 == 0 && dk_stride % 8 == 0,
+               kMisaligned);
   const int TP = (T + 127) / 128 * 128;
   TokenBwdParams p{static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
                    q_norm_weight, k_norm_weight, q_rs, k_rs, dqn, dkn, lam, beta_h, dw, dw_b,

@@ -294,7 +294,8 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   set_smem(dual_gemm_kernel, kDualSmem);
   auto dual = [&](const CUtensorMap& x1, const CUtensorMap& y1, const CUtensorMap& x2,
                   const CUtensorMap& y2, DualParams p) {
-    CYFA_LAUNCH("dual_gemm", st, (dual_gemm_kernel<<<tiles, 256, kDualSmem, st>>>(x1, y1, x2, y2, p)));
+    const unsigned ntile = unsigned(d.BH * d.NT), grid = ntile < 148 ? ntile : 148;  // persistent
+    CYFA_LAUNCH("dual_gemm", st, (dual_gemm_kernel<<<grid, 256, kDualSmem, st>>>(x1, y1, x2, y2, p)));
     return launch_status();
   };
   // boundary partials per tile: one per (CTA slice, warp)

@@ -144,9 +144,26 @@ struct DualParams {
 
 constexpr int kDualSmem = 192 * 1024 + 1024;
 
+// Persistent: CTA c handles tiles c, c + gridDim.x, ...  Per tile the elected
+// thread waits for the operand tiles, issues both GEMMs into TMEM, and as soon
+// as their commit says shared memory has been read it issues the loads of the
+// CTA's next tile, which then stream in while the 8 warps drain TMEM (epilogue).
 // 8 warps: warp w reads TMEM lane quadrant (w & 3) (rows 32(w&3) .. +31) and
 // column half (w >> 2).  The epilogue's global loads (gate factors, row-dot
 // partner) are issued before waiting for the MMAs so that they overlap them.
+__device__ __forceinline__ void dual_issue_loads(uint8_t* smem, const CUtensorMap* x1,
+                                                 const CUtensorMap* y1, const CUtensorMap* x2,
+                                                 const CUtensorMap* y2, const DualParams& p,
+                                                 int tile, uint64_t* bar) {
+  const int kY1 = 32768, kX2 = 32768 + p.N * 256, kY2 = kX2 + p.KD * 256;
+  const int bh = tile / p.NT, j = tile % p.NT;
+  mbar_expect_tx(bar, 32768 + p.N * 256 + p.KD * 256 + p.hrows * p.hcols * 2);
+  load_hist_tile(smem, x1, tile * 128, 0, 128, 128, bar);
+  load_token_tile(smem + kY1, y1, p.y1_mode, bh, p.H, p.TP, j, 0, p.N, bar);
+  load_token_tile(smem + kX2, x2, p.x2_mode, bh, p.H, p.TP, j, 0, p.KD, bar);
+  load_hist_tile(smem + kY2, y2, tile * p.hrows, 0, p.hcols, p.hrows, bar);
+}
+
 __global__ void __launch_bounds__(256, 1)
     dual_gemm_kernel(const __grid_constant__ CUtensorMap map_x1,
                      const __grid_constant__ CUtensorMap map_y1,
@@ -154,14 +171,14 @@ __global__ void __launch_bounds__(256, 1)
                      const __grid_constant__ CUtensorMap map_y2, DualParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  const int kX1 = 0, kY1 = 32768, kX2 = 32768 + p.N * 256, kY2 = kX2 + p.KD * 256;
+  const int kY1 = 32768, kX2 = 32768 + p.N * 256, kY2 = kX2 + p.KD * 256;
   __shared__ __align__(8) uint64_t bar_in, bar_mma;
   __shared__ uint32_t tmem_base;
+  __shared__ float dot_half[2][128];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2;
-  const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT;
   const int r = quad * 32 + lane;  // tile row = TMEM lane
-  const int t = j * 128 + r;
+  const int ntiles = p.BH * p.NT;
   if (tid == 0) {
     mbar_init(&bar_in, 1);
     mbar_init(&bar_mma, 1);
@@ -173,95 +190,124 @@ __global__ void __launch_bounds__(256, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base;
   const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
-  bool ok = true;
-  if (tid == 0) {
-    mbar_expect_tx(&bar_in, 32768 + p.N * 256 + p.KD * 256 + p.hrows * p.hcols * 2);
-    load_hist_tile(smem + kX1, &map_x1, (bh * p.NT + j) * 128, 0, 128, 128, &bar_in);
-    load_token_tile(smem + kY1, &map_y1, p.y1_mode, bh, p.H, p.TP, j, 0, p.N, &bar_in);
-    load_token_tile(smem + kX2, &map_x2, p.x2_mode, bh, p.H, p.TP, j, 0, p.KD, &bar_in);
-    load_hist_tile(smem + kY2, &map_y2, (bh * p.NT + j) * p.hrows, 0, p.hcols, p.hrows, &bar_in);
-    if (mbar_wait(&bar_in, 0)) {
-      tc_fence_after();
-      const uint32_t sX1 = smem_u32(smem + kX1), sY1 = smem_u32(smem + kY1),
-                     sX2 = smem_u32(smem + kX2), sY2 = smem_u32(smem + kY2);
-      const uint32_t id1 = make_idesc(128, p.N, p.x1_mn, 1);
-      for (int ks = 0; ks < 8; ++ks)
-        umma_bf16(tmem, p.x1_mn ? mnmaj_desc(sX1, 128, ks) : kmaj_desc(sX1, 128, ks),
-                  mnmaj_desc(sY1, 128, ks), id1, ks > 0);
-      const uint32_t id2 = make_idesc(128, p.N, 0, p.y2_kmaj ? 0 : 1);
-      for (int ks = 0; ks < p.KD / 16; ++ks)
-        umma_bf16(tmem + 256, kmaj_desc(sX2, 128, ks),
-                  p.y2_kmaj ? kmaj_desc(sY2, p.hrows, ks) : mnmaj_desc(sY2, p.hrows, ks), id2,
-                  ks > 0);
-      umma_commit(&bar_mma);
-    } else {
-      mbar_arrive(&bar_mma);
-    }
-  }
-  // ---- epilogue prefetch (independent of the MMAs)
-  const float* Gt = p.G + size_t(bh) * p.TP + j * 128;
-  const float f = p.fkind == 0 ? p.scale * exp2f(Gt[r]) : exp2f(Gt[127] - Gt[r]);
-  const size_t row = size_t(bh) * p.TP + t;
+  const uint32_t sX1 = smem_u32(smem), sY1 = smem_u32(smem + kY1), sX2 = smem_u32(smem + kX2),
+                 sY2 = smem_u32(smem + kY2);
+  const uint32_t id1 = make_idesc(128, p.N, p.x1_mn, 1);
+  const uint32_t id2 = make_idesc(128, p.N, 0, p.y2_kmaj ? 0 : 1);
   const int ncol = p.N / 2, c_beg = half * ncol;  // 64 or 128 columns
-  uint4 dpre[16];
-  if (p.dot_src) {
-    const uint4* src = reinterpret_cast<const uint4*>(p.dot_src + row * p.N + c_beg);
-#pragma unroll
-    for (int q = 0; q < 16; ++q)
-      if (q < ncol / 8) dpre[q] = src[q];
+  bool ok = true;
+  // elected-thread state: an operand load in flight (and its barrier parity), MMAs
+  // committed but not yet seen complete -- both are waited for before exit
+  bool in_pending = false, mma_pending = false;
+  uint32_t in_ph = 0;
+  if (tid == 0 && blockIdx.x < ntiles) {
+    dual_issue_loads(smem, &map_x1, &map_y1, &map_x2, &map_y2, p, blockIdx.x, &bar_in);
+    in_pending = true;
+    in_ph = 0;
   }
-  __syncwarp();
-  if (!mbar_wait(&bar_mma, 0)) ok = false;
-  tc_fence_after();
-  if (ok) {
-    float dot = 0.f;
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      if (c >= ncol / 32) break;
-      const int col = c_beg + 32 * c;
-      float a[32], b[32];
-      tmem_ld32(lane_tmem + col, a);
-      tmem_ld32(lane_tmem + 256 + col, b);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) a[i] += f * b[i];
-      if (p.dot_src) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float x[8];
-          unpack_bf16x8(dpre[4 * c + q], x);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) dot += x[e] * a[8 * q + e];
+  uint32_t phase = 0;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, phase ^= 1) {
+    const int bh = tile / p.NT, j = tile % p.NT;
+    const int t = j * 128 + r;
+    if (tid == 0) {
+      bool got = ok && mbar_wait(&bar_in, phase);
+      if (got) in_pending = false;
+      tc_fence_after();
+      if (got) {
+        for (int ks = 0; ks < 8; ++ks)
+          umma_bf16(tmem, p.x1_mn ? mnmaj_desc(sX1, 128, ks) : kmaj_desc(sX1, 128, ks),
+                    mnmaj_desc(sY1, 128, ks), id1, ks > 0);
+        for (int ks = 0; ks < p.KD / 16; ++ks)
+          umma_bf16(tmem + 256, kmaj_desc(sX2, 128, ks),
+                    p.y2_kmaj ? kmaj_desc(sY2, p.hrows, ks) : mnmaj_desc(sY2, p.hrows, ks), id2,
+                    ks > 0);
+        umma_commit(&bar_mma);
+        mma_pending = true;
+        // shared memory is free once the MMAs are done: prefetch the next tile
+        const int next = tile + gridDim.x;
+        if (next < ntiles) {
+          if (mbar_wait(&bar_mma, phase)) {
+            mma_pending = false;
+            dual_issue_loads(smem, &map_x1, &map_y1, &map_x2, &map_y2, p, next, &bar_in);
+            in_pending = true;
+            in_ph = phase ^ 1;
+          } else {
+            got = false;
+          }
         }
-      }
-      if (p.out_mode == 2) {
-        if (t < p.T) {
-          const int b_ = bh / p.H, h = bh % p.H;
-          store_bf16x32_global(static_cast<__nv_bfloat16*>(p.out) +
-                                   (size_t(b_) * p.T + t) * p.out_stride + size_t(h) * p.N + col,
-                               a);
-        }
-      } else if (p.out_mode == 3) {
-        store_bf16x32_global(static_cast<__nv_bfloat16*>(p.out) + row * p.N + col, a);
       } else {
-        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + col);
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          __stcs(dst + q, make_float4(a[4 * q], a[4 * q + 1], a[4 * q + 2], a[4 * q + 3]));
+        mbar_arrive(&bar_mma);  // releases the epilogue's wait; its result is discarded
       }
+      if (!got) ok = false;
     }
+    // ---- epilogue prefetch (independent of the MMAs)
+    const float* Gt = p.G + size_t(bh) * p.TP + j * 128;
+    const float f = p.fkind == 0 ? p.scale * exp2f(Gt[r]) : exp2f(Gt[127] - Gt[r]);
+    const size_t row = size_t(bh) * p.TP + t;
+    uint4 dpre[16];
     if (p.dot_src) {
-      // combine the two column halves of the row dot in a fixed order
-      __shared__ float dot_half[2][128];
-      dot_half[half][r] = dot;
-      __syncwarp();
-      asm volatile("bar.sync 1, 256;");
-      if (half == 0) {
-        const float total = dot_half[0][r] + dot_half[1][r];
-        p.dG[row] = (p.dot_acc ? p.dG[row] : 0.f) + p.dot_sign * total;
-      }
+      const uint4* src = reinterpret_cast<const uint4*>(p.dot_src + row * p.N + c_beg);
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        if (q < ncol / 8) dpre[q] = src[q];
     }
-  } else if (p.dot_src) {
-    asm volatile("bar.sync 1, 256;");
+    __syncwarp();
+    bool mm = mbar_wait(&bar_mma, phase);
+    if (tid == 0 && mm) mma_pending = false;
+    tc_fence_after();
+    mm = __syncthreads_and(mm && ok) != 0;
+    if (mm) {
+      float dot = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c >= ncol / 32) break;
+        const int col = c_beg + 32 * c;
+        float a[32], b[32];
+        tmem_ld32(lane_tmem + col, a);
+        tmem_ld32(lane_tmem + 256 + col, b);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) a[i] += f * b[i];
+        if (p.dot_src) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float x[8];
+            unpack_bf16x8(dpre[4 * c + q], x);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dot += x[e] * a[8 * q + e];
+          }
+        }
+        if (p.out_mode == 2) {
+          if (t < p.T) {
+            const int b_ = bh / p.H, h = bh % p.H;
+            store_bf16x32_global(static_cast<__nv_bfloat16*>(p.out) +
+                                     (size_t(b_) * p.T + t) * p.out_stride + size_t(h) * p.N + col,
+                                 a);
+          }
+        } else if (p.out_mode == 3) {
+          store_bf16x32_global(static_cast<__nv_bfloat16*>(p.out) + row * p.N + col, a);
+        } else {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + col);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcs(dst + q, make_float4(a[4 * q], a[4 * q + 1], a[4 * q + 2], a[4 * q + 3]));
+        }
+      }
+      if (p.dot_src) dot_half[half][r] = dot;
+    }
+    // TMEM drained and the row-dot halves visible before the next tile's MMAs
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (mm && p.dot_src && half == 0) {
+      const float total = dot_half[0][r] + dot_half[1][r];
+      p.dG[row] = (p.dot_acc ? p.dG[row] : 0.f) + p.dot_sign * total;
+    }
+    if (!mm) break;
+  }
+  // error paths: let committed MMAs and an unconsumed prefetch finish (bounded)
+  if (tid == 0) {
+    if (mma_pending) mbar_wait(&bar_mma, phase);
+    if (in_pending) mbar_wait(&bar_in, in_ph);
   }
   tc_fence_before();
   __syncthreads();

@@ -35,193 +35,178 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* f) {
                                             pack_bf16(f[4], f[5]), pack_bf16(f[6], f[7]));
 }
 
-// Tiled short convolution.  A CTA of 256 threads owns 256 channels; a chunk of
-// tokens (plus the W-1 halo rows) is staged in shared memory with asynchronous
-// 16-byte copies, and thread (cg, run) computes channels 8cg..8cg+7 of the run's
-// tokens.  Weights are staged once per CTA.  The backward CTA walks a token range
-// with double-buffered staging.
-constexpr int kConvChunk = 64;       // forward tokens per CTA
-constexpr int kConvBwdChunk = 32;    // backward tokens per staged chunk
-constexpr int kConvSplit = 8;        // backward token ranges per (channel block, batch)
+// Streaming short convolution: no shared-memory staging.  A warp walks a run of
+// kConvRun consecutive tokens for a block of channels, keeping the W-1 previous
+// input rows (packed bf16) in registers; each step issues the loads of
+// kConvUnroll rows before any arithmetic, so every warp has several 256- or
+// 512-byte row segments in flight.
+constexpr int kConvRun = 32;     // tokens per warp
+constexpr int kConvUnroll = 4;   // rows loaded ahead per step
+constexpr int kConvWarps = 8;    // warps per CTA (consecutive token runs)
 
-// Issues async copies of rows row0 .. row0 + nrows - 1 (token index) of src,
-// channels c_base .. +255, into tile (row-major [nrows][256] bf16).
-template <int W>
-__device__ __forceinline__ void conv_stage_rows(uint8_t* tile, const __nv_bfloat16* src,
-                                                long long stride, int b, int T, int C,
-                                                int c_base, int row0, int nrows,
-                                                const __nv_bfloat16* cache) {
-  const uint32_t base = smem_u32(tile);
-  for (int idx = threadIdx.x; idx < nrows * 32; idx += blockDim.x) {
-    const int r = idx >> 5, cg = idx & 31;
-    const int t = row0 + r, c = c_base + cg * 8;
-    const __nv_bfloat16* g = src;
-    bool valid = false;
-    if (c < C) {
-      if (t >= 0 && t < T) {
-        g = src + (size_t(b) * T + t) * stride + c;
-        valid = true;
-      } else if (t < 0 && cache) {
-        g = cache + (size_t(b) * (W - 1) + (W - 1) + t) * C + c;
-        valid = true;
-      }
-    }
-    cp_async16(base + r * 512 + cg * 16, g, valid);
-  }
-}
+__device__ __forceinline__ float bf_lo(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+
+// Forward: lane owns channels c0 .. c0+3 (c0 = 128 * blockIdx.x + 4 * lane), and
+// each step loads kConvUnrollF rows ahead.  y[t] = bias + sum_i w_i x[t - (W-1) + i];
+// rows before t = 0 come from the cache (or are zero).
+// grid (ceil(C/128), ceil(T / (kConvWarps*kConvRun)), B).
+constexpr int kConvUnrollF = 8;
 
 template <int W>
 __global__ void __launch_bounds__(256) short_conv_fwd_kernel(ConvParams p) {
-  __shared__ __align__(16) __nv_bfloat16 xs[kConvChunk + W - 1][256];
-  __shared__ float ws[256][W + 1];
-  const int c_base = blockIdx.x * 256, b = blockIdx.z;
-  const int t0 = blockIdx.y * kConvChunk;
-  conv_stage_rows<W>(reinterpret_cast<uint8_t*>(xs), p.x, p.x_stride, b, p.T, p.C, c_base,
-                     t0 - (W - 1), kConvChunk + W - 1, p.cache);
-  cp_async_commit();
-  for (int i = threadIdx.x; i < 256 * W; i += 256) {
-    const int c = c_base + i / W;
-    ws[i / W][i % W] = c < p.C ? p.w[size_t(c) * W + i % W] : 0.f;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * 128 + lane * 4, b = blockIdx.z;
+  const int t0 = (blockIdx.y * kConvWarps + wid) * kConvRun;
+  if (c0 >= p.C || t0 >= p.T) return;
+  float wr[W][4], bias[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+#pragma unroll
+    for (int i = 0; i < W; ++i) wr[i][e] = p.w[size_t(c0 + e) * W + i];
+    bias[e] = p.bias ? p.bias[c0 + e] : 0.f;
   }
-  {
-    const int c = c_base + threadIdx.x;
-    ws[threadIdx.x][W] = (p.bias && c < p.C) ? p.bias[c] : 0.f;
+  const __nv_bfloat16* xb = p.x + size_t(b) * p.T * p.x_stride + c0;
+  uint2 win[W > 1 ? W - 1 : 1];  // x rows t-(W-1) .. t-1
+#pragma unroll
+  for (int i = 0; i < W - 1; ++i) {
+    const int t = t0 - (W - 1) + i;
+    win[i] = make_uint2(0, 0);
+    if (t >= 0)
+      win[i] = *reinterpret_cast<const uint2*>(xb + size_t(t) * p.x_stride);
+    else if (p.cache)
+      win[i] = *reinterpret_cast<const uint2*>(p.cache + (size_t(b) * (W - 1) + (W - 1) + t) * p.C + c0);
   }
-  cp_async_wait<0>();
-  __syncthreads();
-  const int cg = threadIdx.x & 31, run = threadIdx.x >> 5;
-  const int c0 = c_base + cg * 8;
-  if (c0 >= p.C) return;
-  float wr[W][8], bias[8];
+  __nv_bfloat16* yb = p.y + size_t(b) * p.T * p.C + c0;
+  const int tend = min(p.T, t0 + kConvRun);
+  for (int t1 = t0; t1 < tend; t1 += kConvUnrollF) {
+    uint2 cur[kConvUnrollF];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
+    for (int u = 0; u < kConvUnrollF; ++u)
+      cur[u] = t1 + u < tend ? *reinterpret_cast<const uint2*>(xb + size_t(t1 + u) * p.x_stride)
+                             : make_uint2(0, 0);
 #pragma unroll
-    for (int i = 0; i < W; ++i) wr[i][e] = ws[cg * 8 + e][i];
-    bias[e] = ws[cg * 8 + e][W];
-  }
+    for (int u = 0; u < kConvUnrollF; ++u) {
+      if (t1 + u >= tend) break;
+      float y[4] = {bias[0], bias[1], bias[2], bias[3]};
 #pragma unroll
-  for (int tt = 0; tt < 8; ++tt) {
-    const int r = run * 8 + tt;  // output token t0 + r uses staged rows r .. r + W - 1
-    const int t = t0 + r;
-    float y[8];
+      for (int i = 0; i < W; ++i) {
+        const uint2 r = i < W - 1 ? win[i < W - 1 ? i : 0] : cur[u];
+        y[0] += wr[i][0] * bf_lo(r.x);
+        y[1] += wr[i][1] * bf_hi(r.x);
+        y[2] += wr[i][2] * bf_lo(r.y);
+        y[3] += wr[i][3] * bf_hi(r.y);
+      }
+      *reinterpret_cast<uint2*>(yb + size_t(t1 + u) * p.C) =
+          make_uint2(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]));
 #pragma unroll
-    for (int e = 0; e < 8; ++e) y[e] = bias[e];
-#pragma unroll
-    for (int i = 0; i < W; ++i) {
-      float x[8];
-      unpack_bf16x8(*reinterpret_cast<const uint4*>(&xs[r + i][cg * 8]), x);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) y[e] += wr[i][e] * x[e];
+      for (int i = 0; i + 1 < W - 1; ++i) win[i] = win[i + 1];
+      if (W > 1) win[W > 1 ? W - 2 : 0] = cur[u];
     }
-    if (t < p.T) store8(p.y + (size_t(b) * p.T + t) * p.C + c0, y);
   }
 }
 
-template <int W>
-constexpr int conv_bwd_stage_bytes() {
-  return 2 * (kConvBwdChunk + W - 1) * 512;  // x rows + dy rows
-}
-template <int W>
-constexpr int conv_bwd_smem() {
-  return 2 * conv_bwd_stage_bytes<W>() > 8 * 256 * (W + 1) * 4 ? 2 * conv_bwd_stage_bytes<W>()
-                                                               : 8 * 256 * (W + 1) * 4;
-}
-
-// dx[tau] = sum_i w_i dy[tau + (W-1) - i];  dw_i = sum_t dy[t] x[t + i - (W-1)];  db = sum_t dy[t]
-// grid (C/256, B * kConvSplit): each CTA walks one token range in chunks.
+// Backward without cache, lane owns channels c0 .. c0+3 (c0 = 128 * blockIdx.x + 4 * lane):
+//   dx[t] = sum_i w_i dy[t + (W-1) - i],  dw_i = sum_t dy[t] x[t + i - (W-1)],
+//   dbias = sum_t dy[t].
+// A warp keeps x rows t-(W-1) .. t-1 and dy rows t .. t+W-2 in registers.  The 8
+// warps of a CTA (consecutive token runs of one batch row) add their dw/dbias
+// sums in a fixed order into one partial row per CTA row index blockIdx.y.
+// grid (ceil(C/128), B * ceil(T / (kConvWarps*kConvRun))).
 template <int W>
 __global__ void __launch_bounds__(256) short_conv_bwd_kernel(ConvParams p) {
-  extern __shared__ __align__(16) uint8_t conv_smem[];
-  __shared__ float ws[256][W];
-  constexpr int R = kConvBwdChunk + W - 1;  // staged rows per tile
-  const int c_base = blockIdx.x * 256;
-  const int b = blockIdx.y / kConvSplit, split = blockIdx.y % kConvSplit;
-  const int nchunks = (p.T + kConvBwdChunk - 1) / kConvBwdChunk;
-  const int per = (nchunks + kConvSplit - 1) / kConvSplit;
-  const int k0 = split * per, k1 = min(nchunks, k0 + per);
-  auto stage = [&](int kc, int buf) {
-    uint8_t* base = conv_smem + buf * conv_bwd_stage_bytes<W>();
-    const int t0 = kc * kConvBwdChunk;
-    conv_stage_rows<W>(base, p.x, p.x_stride, b, p.T, p.C, c_base, t0 - (W - 1), R, nullptr);
-    conv_stage_rows<W>(base + R * 512, p.dy, p.C, b, p.T, p.C, c_base, t0, R, nullptr);
-    cp_async_commit();
-  };
-  if (k0 < k1) stage(k0, 0);
-  for (int i = threadIdx.x; i < 256 * W; i += 256) {
-    const int c = c_base + i / W;
-    ws[i / W][i % W] = c < p.C ? p.w[size_t(c) * W + i % W] : 0.f;
-  }
-  __syncthreads();
-  const int cg = threadIdx.x & 31, run = threadIdx.x >> 5;
-  const int c0 = c_base + cg * 8;
-  float wr[W][8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e)
-#pragma unroll
-    for (int i = 0; i < W; ++i) wr[i][e] = ws[cg * 8 + e][i];
-  float acc[W + 1][8];
+  __shared__ float red[kConvWarps][128 * (W + 1)];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int ng = (p.T + kConvWarps * kConvRun - 1) / (kConvWarps * kConvRun);
+  const int b = blockIdx.y / ng, grp = blockIdx.y % ng;
+  const int c0 = blockIdx.x * 128 + lane * 4;
+  const int t0 = (grp * kConvWarps + wid) * kConvRun;
+  float acc[W + 1][4];
 #pragma unroll
   for (int i = 0; i <= W; ++i)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
-  for (int kc = k0; kc < k1; ++kc) {
-    const int buf = (kc - k0) & 1;
-    if (kc + 1 < k1) {
-      stage(kc + 1, buf ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
+    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
+  if (c0 < p.C && t0 < p.T) {
+    float wr[W][4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+      for (int i = 0; i < W; ++i) wr[i][e] = p.w[size_t(c0 + e) * W + i];
+    const __nv_bfloat16* xb = p.x + size_t(b) * p.T * p.x_stride + c0;
+    const __nv_bfloat16* db = p.dy + size_t(b) * p.T * p.C + c0;
+    __nv_bfloat16* dxb = p.dx + size_t(b) * p.T * p.dx_stride + c0;
+    uint2 X[W > 1 ? W - 1 : 1], D[W > 1 ? W - 1 : 1];
+#pragma unroll
+    for (int i = 0; i < W - 1; ++i) {
+      const int tx = t0 - (W - 1) + i, td = t0 + i;
+      X[i] = tx >= 0 ? *reinterpret_cast<const uint2*>(xb + size_t(tx) * p.x_stride) : make_uint2(0, 0);
+      D[i] = td < p.T ? *reinterpret_cast<const uint2*>(db + size_t(td) * p.C) : make_uint2(0, 0);
     }
-    __syncthreads();
-    const uint8_t* base = conv_smem + buf * conv_bwd_stage_bytes<W>();
-    auto xrow = [&](int r) { return reinterpret_cast<const uint4*>(base + r * 512 + cg * 16); };
-    auto drow = [&](int r) {
-      return reinterpret_cast<const uint4*>(base + R * 512 + r * 512 + cg * 16);
-    };
-    const int t0 = kc * kConvBwdChunk;
-    if (c0 < p.C) {
+    const int tend = min(p.T, t0 + kConvRun);
+    for (int t1 = t0; t1 < tend; t1 += kConvUnroll) {
+      uint2 xs[kConvUnroll], ds[kConvUnroll];
 #pragma unroll
-      for (int tt = 0; tt < kConvBwdChunk / 8; ++tt) {
-        const int r = run * (kConvBwdChunk / 8) + tt;
-        const int t = t0 + r;
-        float dy0[8], dx[8];
-        unpack_bf16x8(*drow(r), dy0);
+      for (int u = 0; u < kConvUnroll; ++u) {
+        const int t = t1 + u, td = t + W - 1;
+        xs[u] = t < tend ? *reinterpret_cast<const uint2*>(xb + size_t(t) * p.x_stride) : make_uint2(0, 0);
+        ds[u] = (t < tend && td < p.T) ? *reinterpret_cast<const uint2*>(db + size_t(td) * p.C)
+                                       : make_uint2(0, 0);
+      }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) dx[e] = 0.f;
+      for (int u = 0; u < kConvUnroll; ++u) {
+        if (t1 + u >= tend) break;
+        // dy rows t .. t+W-1 = D[0..W-2], ds[u];  x rows t-(W-1) .. t = X[0..W-2], xs[u]
+        const uint2 d0r = W > 1 ? D[0] : ds[u];
+        const float d0[4] = {bf_lo(d0r.x), bf_hi(d0r.x), bf_lo(d0r.y), bf_hi(d0r.y)};
+        float dx[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int i = 0; i < W; ++i) {
-          float d[8], x[8];
-          unpack_bf16x8(*drow(r + W - 1 - i), d);
-          unpack_bf16x8(*xrow(r + i), x);
+          const int j = W - 1 - i;  // dy row t + j
+          const uint2 dr = j < W - 1 ? D[j < W - 1 ? j : 0] : ds[u];
+          const uint2 xr = i < W - 1 ? X[i < W - 1 ? i : 0] : xs[u];
+          const float dv[4] = {bf_lo(dr.x), bf_hi(dr.x), bf_lo(dr.y), bf_hi(dr.y)};
+          const float xv[4] = {bf_lo(xr.x), bf_hi(xr.x), bf_lo(xr.y), bf_hi(xr.y)};
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            dx[e] += wr[i][e] * d[e];
-            acc[i][e] += dy0[e] * x[e];
+          for (int e = 0; e < 4; ++e) {
+            dx[e] += wr[i][e] * dv[e];
+            acc[i][e] += d0[e] * xv[e];
           }
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[W][e] += dy0[e];
-        if (t < p.T) store8(p.dx + (size_t(b) * p.T + t) * p.dx_stride + c0, dx);
+        for (int e = 0; e < 4; ++e) acc[W][e] += d0[e];
+        *reinterpret_cast<uint2*>(dxb + size_t(t1 + u) * p.dx_stride) =
+            make_uint2(pack_bf16(dx[0], dx[1]), pack_bf16(dx[2], dx[3]));
+#pragma unroll
+        for (int i = 0; i + 1 < W - 1; ++i) {
+          X[i] = X[i + 1];
+          D[i] = D[i + 1];
+        }
+        if (W > 1) {
+          X[W > 1 ? W - 2 : 0] = xs[u];
+          D[W > 1 ? W - 2 : 0] = ds[u];
+        }
       }
     }
-    __syncthreads();
   }
-  // reduce the 8 runs through shared memory in a fixed order
-  float* red = reinterpret_cast<float*>(conv_smem);  // 8 * 256 * (W+1) floats
 #pragma unroll
   for (int i = 0; i <= W; ++i)
 #pragma unroll
-    for (int e = 0; e < 8; ++e) red[(run * 256 + cg * 8 + e) * (W + 1) + i] = acc[i][e];
+    for (int e = 0; e < 4; ++e) red[wid][(lane * 4 + e) * (W + 1) + i] = acc[i][e];
   __syncthreads();
-  const size_t prow = blockIdx.y;
-  for (int idx = threadIdx.x; idx < 256 * (W + 1); idx += 256) {
-    const int c = c_base + idx / (W + 1);
+  for (int idx = threadIdx.x; idx < 128 * (W + 1); idx += 256) {
+    const int c = blockIdx.x * 128 + idx / (W + 1);
     if (c >= p.C) continue;
     float sum = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) sum += red[k * 256 * (W + 1) + idx];
-    p.part[prow * (size_t(p.C) * (W + 1)) + size_t(c) * (W + 1) + idx % (W + 1)] = sum;
+    for (int k = 0; k < kConvWarps; ++k) sum += red[k][idx];
+    p.part[size_t(blockIdx.y) * (size_t(p.C) * (W + 1)) + size_t(c) * (W + 1) + idx % (W + 1)] =
+        sum;
   }
+}
+
+// Partial rows of the backward for a shape.
+inline int conv_bwd_rows(int B, int T) {
+  return B * ((T + kConvWarps * kConvRun - 1) / (kConvWarps * kConvRun));
 }
 
 // ============================================================ gate activations
@@ -329,62 +314,74 @@ struct GatedNormParams {
   int part_cols = 0;                     // 0: D (no bias partials); else D + H*D
 };
 
-// One warp per row (grid-strided), D = 32 * E.
+// One warp per row, grid-strided, two rows per iteration (loads of both rows
+// issued first).  The weight (and, with a gate bias, the bias of the warp's head:
+// the grid is then a multiple of H, so (blockIdx.x * 8 + warp) % H is the head of
+// every row the warp visits) stays in registers.  D = 32 * E.
 template <int E>
-__global__ void __launch_bounds__(256) gated_norm_fwd_kernel(GatedNormParams p) {
+__global__ void __launch_bounds__(256, 3) gated_norm_fwd_kernel(GatedNormParams p) {
   constexpr int D = 32 * E;
-  const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= p.rows) return;
-  float x[E], g[E];
-  if constexpr (E == 8) {
-    load8(p.x + size_t(row) * D + lane * 8, x);
-    load8(p.gate + size_t(row) * D + lane * 8, g);
-  } else {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const size_t stride = size_t(gridDim.x) * 8;
+  float w[E], bias[E];
+  load_f32_vec<E>(p.w + lane * E, w);
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      x[e] = __bfloat162float(p.x[size_t(row) * D + lane * E + e]);
-      g[e] = __bfloat162float(p.gate[size_t(row) * D + lane * E + e]);
+  for (int e = 0; e < E; ++e) bias[e] = 0.f;
+  if (p.gbias) load_bf16_vec<E>(p.gbias + size_t((blockIdx.x * 8 + wid) % p.H) * D + lane * E, bias);
+  for (size_t row0 = size_t(blockIdx.x) * 8 + wid; row0 < size_t(p.rows); row0 += 2 * stride) {
+    float x[2][E], g[2][E];
+    bool live[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const size_t row = row0 + u * stride;
+      live[u] = row < size_t(p.rows);
+      if (live[u]) {
+        load_bf16_vec<E>(p.x + row * D + lane * E, x[u]);
+        load_bf16_vec<E>(p.gate + row * D + lane * E, g[u]);
+      }
     }
-  }
-  if (p.gbias) {
-    float b[E];
-    load_bf16_vec<E>(p.gbias + size_t(row % p.H) * D + lane * E, b);
 #pragma unroll
-    for (int e = 0; e < E; ++e) g[e] += b[e];
-  }
-  float ss = 0.f;
+    for (int u = 0; u < 2; ++u) {
+      if (!live[u]) continue;
+      const size_t row = row0 + u * stride;
+      float ss = 0.f;
 #pragma unroll
-  for (int e = 0; e < E; ++e) {
-    x[e] *= p.scale;
-    ss += x[e] * x[e];
-  }
+      for (int e = 0; e < E; ++e) {
+        x[u][e] *= p.scale;
+        ss += x[u][e] * x[u][e];
+      }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float rs = rsqrtf(ss / D + p.eps);
-  if (lane == 0) p.rstd[row] = rs;
-  float y[E];
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rs = rsqrtf(ss / D + p.eps);
+      if (lane == 0) p.rstd[row] = rs;
+      float y[E];
 #pragma unroll
-  for (int e = 0; e < E; ++e) y[e] = x[e] * rs * p.w[lane * E + e] * sigmoid_f(g[e]);
-  if constexpr (E == 8) {
-    store8(p.y + size_t(row) * D + lane * 8, y);
-  } else {
-#pragma unroll
-    for (int e = 0; e < E; ++e) p.y[size_t(row) * D + lane * E + e] = __float2bfloat16_rn(y[e]);
+      for (int e = 0; e < E; ++e) y[e] = x[u][e] * rs * w[e] * sigmoid_f(g[u][e] + bias[e]);
+      store_bf16_vec<E>(p.y + row * D + lane * E, y);
+    }
   }
 }
 
-// With a gate bias the grid is a multiple of H, so every warp's rows belong to
-// one head ((blockIdx.x * 8 + warp) % H) and its bias-gradient partial stays in
-// registers; the block's per-head sums are formed in a fixed warp order.
+// Grid of the gated-norm forward: two rows per warp per pass, three blocks per SM,
+// a multiple of H (see above).
+inline int norm_fwd_blocks(int rows, int H) {
+  int n = (rows + 15) / 16;
+  if (n > 444) n = 444;
+  n -= n % H;
+  return n < H ? H : n;
+}
+
+// Same warp/head rule as the forward.  Register-lean: n, dn and dgate overwrite
+// x, dy and the gate in place.
 template <int E>
-__global__ void __launch_bounds__(256) gated_norm_bwd_kernel(GatedNormParams p) {
+__global__ void __launch_bounds__(256, 3) gated_norm_bwd_kernel(GatedNormParams p) {
   constexpr int D = 32 * E;
   __shared__ float red[8][D];
   __shared__ float red_b[8][D];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const bool has_b = p.gbias != nullptr;
-  float acc[E], acc_b[E], bias[E];
+  float w[E], acc[E], acc_b[E], bias[E];
+  load_f32_vec<E>(p.w + lane * E, w);
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = acc_b[e] = bias[e] = 0.f;
   if (has_b) load_bf16_vec<E>(p.gbias + size_t((blockIdx.x * 8 + wid) % p.H) * D + lane * E, bias);
@@ -393,33 +390,27 @@ __global__ void __launch_bounds__(256) gated_norm_bwd_kernel(GatedNormParams p) 
     load_bf16_vec<E>(p.x + size_t(row) * D + lane * E, x);
     load_bf16_vec<E>(p.gate + size_t(row) * D + lane * E, g);
     load_bf16_vec<E>(p.dy + size_t(row) * D + lane * E, dy);
-#pragma unroll
-    for (int e = 0; e < E; ++e) g[e] += bias[e];
-#pragma unroll
-    for (int e = 0; e < E; ++e) x[e] *= p.scale;
     const float rs = p.rstd[row];
-    float dn[E], n[E], dgv[E], dot = 0.f;
+    float dot = 0.f;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      const float sg = sigmoid_f(g[e]), wv = p.w[lane * E + e];
-      n[e] = x[e] * rs;
-      const float z = n[e] * wv;
-      dgv[e] = dy[e] * z * sg * (1.f - sg);
+      const float sg = sigmoid_f(g[e] + bias[e]);
+      const float n = x[e] * p.scale * rs;
       const float dz = dy[e] * sg;
-      acc[e] += dz * n[e];
-      dn[e] = dz * wv;
-      dot += dn[e] * n[e];
+      g[e] = dy[e] * n * w[e] * sg * (1.f - sg);  // dgate
+      acc[e] += dz * n;
+      acc_b[e] += g[e];
+      dy[e] = dz * w[e];  // dn
+      x[e] = n;
+      dot += dy[e] * n;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
     dot /= D;
-    float dxv[E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) dxv[e] = p.scale * rs * (dn[e] - n[e] * dot);
-    store_bf16_vec<E>(p.dx + size_t(row) * D + lane * E, dxv);
-    store_bf16_vec<E>(p.dgate + size_t(row) * D + lane * E, dgv);
-#pragma unroll
-    for (int e = 0; e < E; ++e) acc_b[e] += dgv[e];
+    for (int e = 0; e < E; ++e) dy[e] = p.scale * rs * (dy[e] - x[e] * dot);  // dx
+    store_bf16_vec<E>(p.dx + size_t(row) * D + lane * E, dy);
+    store_bf16_vec<E>(p.dgate + size_t(row) * D + lane * E, g);
   }
 #pragma unroll
   for (int e = 0; e < E; ++e) {

@@ -6,7 +6,6 @@
 
 namespace cyfa {
 
-static int conv_bwd_rows(int B) { return B * kConvSplit; }
 
 static int gate_bwd_blocks(long long n) {
   const long long want = (n + 255) / 256;
@@ -26,7 +25,7 @@ extern "C" {
 
 size_t cyfa_short_conv_work_bytes(int B, int T, int C, int W) {
   if (B <= 0 || T <= 0 || C <= 0 || W < 1 || W > 4) return 0;
-  return size_t(conv_bwd_rows(B)) * C * (W + 1) * sizeof(float);
+  return size_t(conv_bwd_rows(B, T)) * C * (W + 1) * sizeof(float);
 }
 
 int cyfa_short_conv_fwd(const void* x, long long x_stride, const void* cache, const float* w,
@@ -39,7 +38,7 @@ int cyfa_short_conv_fwd(const void* x, long long x_stride, const void* cache, co
   ConvParams p{static_cast<const __nv_bfloat16*>(x), x_stride,
                static_cast<const __nv_bfloat16*>(cache), w, bias, static_cast<__nv_bfloat16*>(y),
                nullptr, nullptr, 0, nullptr, B, T, C};
-  const dim3 grid((C + 255) / 256, (T + kConvChunk - 1) / kConvChunk, B);
+  const dim3 grid((C + 127) / 128, (T + kConvWarps * kConvRun - 1) / (kConvWarps * kConvRun), B);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (W) {
     case 1: CYFA_LAUNCH("short_conv_fwd", s, short_conv_fwd_kernel<1><<<grid, 256, 0, s>>>(p)); break;
@@ -63,34 +62,18 @@ int cyfa_short_conv_bwd(const void* x, long long x_stride, const float* w, const
   ConvParams p{static_cast<const __nv_bfloat16*>(x), x_stride, nullptr, w, nullptr, nullptr,
                static_cast<const __nv_bfloat16*>(dy), static_cast<__nv_bfloat16*>(dx), dx_stride,
                part, B, T, C};
-  const dim3 grid((C + 255) / 256, conv_bwd_rows(B));
+  const dim3 grid((C + 127) / 128, conv_bwd_rows(B, T));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (W) {
-    case 1:
-      set_smem(short_conv_bwd_kernel<1>, conv_bwd_smem<1>());
-      CYFA_LAUNCH("short_conv_bwd", s,
-                  (short_conv_bwd_kernel<1><<<grid, 256, conv_bwd_smem<1>(), s>>>(p)));
-      break;
-    case 2:
-      set_smem(short_conv_bwd_kernel<2>, conv_bwd_smem<2>());
-      CYFA_LAUNCH("short_conv_bwd", s,
-                  (short_conv_bwd_kernel<2><<<grid, 256, conv_bwd_smem<2>(), s>>>(p)));
-      break;
-    case 3:
-      set_smem(short_conv_bwd_kernel<3>, conv_bwd_smem<3>());
-      CYFA_LAUNCH("short_conv_bwd", s,
-                  (short_conv_bwd_kernel<3><<<grid, 256, conv_bwd_smem<3>(), s>>>(p)));
-      break;
-    default:
-      set_smem(short_conv_bwd_kernel<4>, conv_bwd_smem<4>());
-      CYFA_LAUNCH("short_conv_bwd", s,
-                  (short_conv_bwd_kernel<4><<<grid, 256, conv_bwd_smem<4>(), s>>>(p)));
-      break;
+    case 1: CYFA_LAUNCH("short_conv_bwd", s, (short_conv_bwd_kernel<1><<<grid, 256, 0, s>>>(p))); break;
+    case 2: CYFA_LAUNCH("short_conv_bwd", s, (short_conv_bwd_kernel<2><<<grid, 256, 0, s>>>(p))); break;
+    case 3: CYFA_LAUNCH("short_conv_bwd", s, (short_conv_bwd_kernel<3><<<grid, 256, 0, s>>>(p))); break;
+    default: CYFA_LAUNCH("short_conv_bwd", s, (short_conv_bwd_kernel<4><<<grid, 256, 0, s>>>(p))); break;
   }
   int rc = launch_status();
   if (rc) return rc;
   // reduce the partial rows: columns are [c][0..W-1] = dw, [c][W] = dbias
-  const int rows = conv_bwd_rows(B), cols = C * (W + 1);
+  const int rows = conv_bwd_rows(B, T), cols = C * (W + 1);
   CYFA_LAUNCH("conv_param_sum", s,
               (conv_param_sum_kernel<<<(cols + 255) / 256, 256, 0, s>>>(part, rows, C, W, dw,
                                                                         dbias)));
@@ -157,13 +140,14 @@ int cyfa_gate_act_bwd(const void* a, long long a_stride, const void* b, long lon
 
 int cyfa_gated_norm_fwd(const void* x, const void* gate, const float* w, float eps, float scale,
                         void* y, float* rstd, int rows, int D, void* stream) {
+  CYFA_REQUIRE(aligned(w, 16), kMisaligned);
   CYFA_REQUIRE(x && gate && w && y && rstd, kNullPointer);
   CYFA_REQUIRE(rows > 0 && (D == 256 || D == 128), kBadShape);
   CYFA_REQUIRE(aligned(x, 16) && aligned(gate, 16) && aligned(y, 16), kMisaligned);
   GatedNormParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gate),
                     w, eps, scale, static_cast<__nv_bfloat16*>(y), rstd, nullptr, nullptr, nullptr,
                     nullptr, rows};
-  const unsigned grid = unsigned((rows + 7) / 8);
+  const unsigned grid = unsigned(norm_fwd_blocks(rows, 1));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (D == 256) CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<8><<<grid, 256, 0, s>>>(p)));
   else CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<4><<<grid, 256, 0, s>>>(p)));
@@ -178,6 +162,7 @@ size_t cyfa_gated_norm_work_bytes(int rows, int D) {
 int cyfa_gated_norm_bwd(const void* x, const void* gate, const float* w, float scale,
                         const float* rstd, const void* dy, void* dx, void* dgate, float* dw,
                         int rows, int D, void* work, size_t work_bytes, void* stream) {
+  CYFA_REQUIRE(aligned(w, 16), kMisaligned);
   CYFA_REQUIRE(x && gate && w && rstd && dy && dx && dgate && dw && work, kNullPointer);
   CYFA_REQUIRE(rows > 0 && (D == 256 || D == 128), kBadShape);
   CYFA_REQUIRE(work_bytes >= cyfa_gated_norm_work_bytes(rows, D), kWorkspace);
@@ -200,6 +185,7 @@ int cyfa_gated_norm_bwd(const void* x, const void* gate, const float* w, float s
 int cyfa_gated_norm_bias_fwd(const void* x, const void* gate, const void* gate_bias, int H,
                              const float* w, float eps, float scale, void* y, float* rstd,
                              int rows, int D, void* stream) {
+  CYFA_REQUIRE(aligned(w, 16), kMisaligned);
   CYFA_REQUIRE(x && gate && gate_bias && w && y && rstd, kNullPointer);
   CYFA_REQUIRE(rows > 0 && H > 0 && rows % H == 0 && (D == 256 || D == 128), kBadShape);
   CYFA_REQUIRE(aligned(x, 16) && aligned(gate, 16) && aligned(y, 16) && aligned(gate_bias, 16),
@@ -207,16 +193,18 @@ int cyfa_gated_norm_bias_fwd(const void* x, const void* gate, const void* gate_b
   GatedNormParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gate),
                     w, eps, scale, static_cast<__nv_bfloat16*>(y), rstd, nullptr, nullptr, nullptr,
                     nullptr, rows, static_cast<const __nv_bfloat16*>(gate_bias), H, 0};
-  const unsigned grid = unsigned((rows + 7) / 8);
+  const unsigned grid = unsigned(norm_fwd_blocks(rows, H));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (D == 256) CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<8><<<grid, 256, 0, s>>>(p)));
   else CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<4><<<grid, 256, 0, s>>>(p)));
   return launch_status();
 }
 
-// Block count of the biased backward: a multiple of H (each warp stays on one head).
+// Block count of the biased backward: three per SM, a multiple of H (each warp
+// stays on one head).
 static int norm_bias_bwd_blocks(int rows, int H) {
-  int n = norm_bwd_blocks(rows);
+  int n = (rows + 7) / 8;
+  if (n > 444) n = 444;
   n -= n % H;
   return n < H ? H : n;
 }
@@ -230,6 +218,7 @@ int cyfa_gated_norm_bias_bwd(const void* x, const void* gate, const void* gate_b
                              const float* w, float scale, const float* rstd, const void* dy,
                              void* dx, void* dgate, float* dw, float* dgate_bias, int rows, int D,
                              void* work, size_t work_bytes, void* stream) {
+  CYFA_REQUIRE(aligned(w, 16), kMisaligned);
   CYFA_REQUIRE(x && gate && gate_bias && w && rstd && dy && dx && dgate && dw && dgate_bias && work,
                kNullPointer);
   CYFA_REQUIRE(rows > 0 && H > 0 && rows % H == 0 && (D == 256 || D == 128), kBadShape);

@@ -53,6 +53,7 @@ extern "C" {
 int cyfa_gated_norm_bwd_static(const void* x, const void* gate, const float* w, float scale,
                                const float* rstd, const void* dy, void* dx, void* dgate,
                                float* dw, int rows, int D, void* stream) {
+  CYFA_REQUIRE(aligned(w, 16), kMisaligned);
   CYFA_REQUIRE(x && gate && w && rstd && dy && dx && dgate && dw, kNullPointer);
   CYFA_REQUIRE(rows > 0 && (D == 256 || D == 128), kBadShape);
   const int nblk = norm_bwd_blocks(rows);

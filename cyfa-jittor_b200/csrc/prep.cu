@@ -150,89 +150,92 @@ struct TokenFwdParams {
   long long q_stride, k_stride;  // elements between consecutive tokens of q / k
 };
 
+// One warp per (b, h, t) row, grid-strided, two rows per iteration (all loads of
+// both rows issued before any math); the norm weights stay in registers.
 template <int K>
 __global__ void __launch_bounds__(256) token_fwd_kernel(TokenFwdParams p) {
   constexpr int E = K / 32;  // elements per lane (8 for K=256, 4 for K=128)
   const int lane = threadIdx.x & 31;
-  const size_t row = size_t(blockIdx.x) * 8 + (threadIdx.x >> 5);  // over B*H*TP
-  if (row >= size_t(p.B) * p.H * p.TP) return;
-  const int t = int(row % p.TP);
-  const size_t bh = row / p.TP;
-  const int b = int(bh / p.H), h = int(bh % p.H);
-  float qv[E], kv[E];
-  if (t < p.T) {
-    const size_t tok = size_t(b) * p.T + t, col = size_t(h) * K + lane * E;
-    const size_t srcq = tok * p.q_stride + col, srck = tok * p.k_stride + col;
-    if constexpr (E == 8) {
-      const uint4 a = *reinterpret_cast<const uint4*>(p.q + srcq);
-      const uint4 c = *reinterpret_cast<const uint4*>(p.k + srck);
-      const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&a);
-      const __nv_bfloat16* cp = reinterpret_cast<const __nv_bfloat16*>(&c);
+  const size_t rows = size_t(p.B) * p.H * p.TP;
+  const size_t stride = size_t(gridDim.x) * 8;
+  float qw[E], kw[E];
+  load_f32_vec<E>(p.qw + lane * E, qw);
+  load_f32_vec<E>(p.kw + lane * E, kw);
+  for (size_t row0 = size_t(blockIdx.x) * 8 + (threadIdx.x >> 5); row0 < rows; row0 += 2 * stride) {
+    float qv[2][E], kv[2][E], lam[2], bt[2];
+    size_t rowv[2];
+    bool live[2], real[2];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        qv[j] = __bfloat162float(ap[j]);
-        kv[j] = __bfloat162float(cp[j]);
+    for (int u = 0; u < 2; ++u) {
+      const size_t row = row0 + u * stride;
+      rowv[u] = row;
+      live[u] = row < rows;
+      const int t = live[u] ? int(row % p.TP) : 0;
+      real[u] = live[u] && t < p.T;
+#pragma unroll
+      for (int j = 0; j < E; ++j) qv[u][j] = kv[u][j] = 0.f;
+      lam[u] = bt[u] = 0.f;
+      if (real[u]) {
+        const size_t bh = row / p.TP;
+        const int b = int(bh / p.H), h = int(bh % p.H);
+        const size_t tok = size_t(b) * p.T + t, col = size_t(h) * K + lane * E;
+        load_bf16_vec<E>(p.q + tok * p.q_stride + col, qv[u]);
+        load_bf16_vec<E>(p.k + tok * p.k_stride + col, kv[u]);
       }
-    } else {
-      const uint2 a = *reinterpret_cast<const uint2*>(p.q + srcq);
-      const uint2 c = *reinterpret_cast<const uint2*>(p.k + srck);
-      const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(&a);
-      const __nv_bfloat16* cp = reinterpret_cast<const __nv_bfloat16*>(&c);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        qv[j] = __bfloat162float(ap[j]);
-        kv[j] = __bfloat162float(cp[j]);
+      if (live[u]) {
+        lam[u] = p.lam[row];
+        bt[u] = p.beta_h[row];
       }
     }
-  } else {
 #pragma unroll
-    for (int j = 0; j < E; ++j) qv[j] = kv[j] = 0.f;
-  }
-  float q2 = 0.f, k2 = 0.f;
+    for (int u = 0; u < 2; ++u) {
+      if (!live[u]) continue;
+      const size_t row = rowv[u];
+      float q2 = 0.f, k2 = 0.f;
 #pragma unroll
-  for (int j = 0; j < E; ++j) {
-    q2 += qv[j] * qv[j];
-    k2 += kv[j] * kv[j];
-  }
+      for (int j = 0; j < E; ++j) {
+        q2 += qv[u][j] * qv[u][j];
+        k2 += kv[u][j] * kv[u][j];
+      }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    q2 += __shfl_xor_sync(0xffffffffu, q2, o);
-    k2 += __shfl_xor_sync(0xffffffffu, k2, o);
-  }
-  const float qr = rsqrtf(q2 / K + p.q_eps), kr = rsqrtf(k2 / K + p.k_eps);
-  uint32_t qo[E / 2], ko[E / 2];
+      for (int o = 16; o > 0; o >>= 1) {
+        q2 += __shfl_xor_sync(0xffffffffu, q2, o);
+        k2 += __shfl_xor_sync(0xffffffffu, k2, o);
+      }
+      const float qr = rsqrtf(q2 / K + p.q_eps), kr = rsqrtf(k2 / K + p.k_eps);
+      float qo[E], ko[E];
 #pragma unroll
-  for (int j = 0; j < E; j += 2) {
-    const int d = lane * E + j;
-    qo[j / 2] = pack_bf16(qv[j] * qr * p.qw[d], qv[j + 1] * qr * p.qw[d + 1]);
-    ko[j / 2] = pack_bf16(kv[j] * kr * p.kw[d], kv[j + 1] * kr * p.kw[d + 1]);
-  }
-  const size_t dst = row * K + lane * E;
-  if constexpr (E == 8) {
-    *reinterpret_cast<uint4*>(p.qn + dst) = make_uint4(qo[0], qo[1], qo[2], qo[3]);
-    *reinterpret_cast<uint4*>(p.kn + dst) = make_uint4(ko[0], ko[1], ko[2], ko[3]);
-  } else {
-    *reinterpret_cast<uint2*>(p.qn + dst) = make_uint2(qo[0], qo[1]);
-    *reinterpret_cast<uint2*>(p.kn + dst) = make_uint2(ko[0], ko[1]);
-  }
-  if (lane == 0) {
-    p.q_rs[row] = t < p.T ? qr : 0.f;
-    p.k_rs[row] = t < p.T ? kr : 0.f;
-  }
-  // write vector: lane handles pairs lane and lane + 32
-  const float lam = p.lam[row], bt = p.beta_h[row];
-  uint32_t wo[2];
+      for (int j = 0; j < E; ++j) {
+        qo[j] = qv[u][j] * qr * qw[j];
+        ko[j] = kv[u][j] * kr * kw[j];
+      }
+      store_bf16_vec<E>(p.qn + row * K + lane * E, qo);
+      store_bf16_vec<E>(p.kn + row * K + lane * E, ko);
+      if (lane == 0) {
+        p.q_rs[row] = real[u] ? qr : 0.f;
+        p.k_rs[row] = real[u] ? kr : 0.f;
+      }
+      // write vector: lane handles pairs lane and lane + 32 (|phase| <= pi)
+      uint32_t wo[2];
 #pragma unroll
-  for (int part = 0; part < 2; ++part) {
-    const int pair = lane + 32 * part;
-    float s, c;
-    sincosf(clock_phase(lam, pair), &s, &c);
-    const float a = bt * atom_scale(pair);
-    wo[part] = pack_bf16(a * c, -a * s);
+      for (int part = 0; part < 2; ++part) {
+        const int pair = lane + 32 * part;
+        float sn, cs;
+        __sincosf(clock_phase(lam[u], pair), &sn, &cs);
+        const float a = bt[u] * atom_scale(pair);
+        wo[part] = pack_bf16(a * cs, -a * sn);
+      }
+      uint32_t* wrow = reinterpret_cast<uint32_t*>(p.w + row * 128);
+      wrow[lane] = wo[0];
+      wrow[lane + 32] = wo[1];
+    }
   }
-  uint32_t* wrow = reinterpret_cast<uint32_t*>(p.w + row * 128);
-  wrow[lane] = wo[0];
-  wrow[lane + 32] = wo[1];
+}
+
+// Blocks of token_fwd_kernel: enough for two rows per warp per pass, at most 8 per SM.
+inline int token_fwd_blocks(size_t rows) {
+  const size_t want = (rows + 15) / 16;
+  return int(want < 1184 ? want : 1184);
 }
 
 template __global__ void token_fwd_kernel<256>(TokenFwdParams);
@@ -281,109 +284,113 @@ __device__ __forceinline__ float2 load_grad_pair(const void* base, size_t off) {
 }
 
 // GT: element type of the incoming gradients (dqn, dkn, dw, dw_b).
+// 8 warps per block as 4 row slots x 2 roles: role 0 does the q side of a row,
+// role 1 the k side and the write-vector adjoint, so a warp holds one vector set
+// (few registers, three blocks per SM).  Slot s of block b handles rows
+// b*4 + s + i*gridDim.x*4; each block writes one row of q and k norm-weight
+// partials (its rows, fixed order), so the partial matrices have gridDim.x rows.
 template <int K, typename GT>
-__global__ void __launch_bounds__(256) token_bwd_kernel(TokenBwdParams p) {
+__global__ void __launch_bounds__(256, 3) token_bwd_kernel(TokenBwdParams p) {
   constexpr int E = K / 32;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  __shared__ float pq[8][K], pk[8][K];
-  float aq[E], ak[E];
+  const int role = wid & 1, slot = wid >> 1;
+  __shared__ float part_s[2][4][K];
+  const __nv_bfloat16* xsrc = role ? p.k : p.q;
+  const void* gsrc = role ? p.dkn : p.dqn;
+  const float* rsv = role ? p.k_rs : p.q_rs;
+  __nv_bfloat16* dst = role ? p.dk : p.dq;
+  const long long xs = role ? p.k_stride : p.q_stride, ds = role ? p.dk_stride : p.dq_stride;
+  float wv[E], acc[E];
+  load_f32_vec<E>((role ? p.kw : p.qw) + lane * E, wv);
 #pragma unroll
-  for (int j = 0; j < E; ++j) aq[j] = ak[j] = 0.f;
+  for (int j = 0; j < E; ++j) acc[j] = 0.f;
   const size_t rows = size_t(p.B) * p.H * p.TP;
-  for (size_t row = size_t(blockIdx.x) * 8 + wid; row < rows; row += size_t(gridDim.x) * 8) {
+  for (size_t row = size_t(blockIdx.x) * 4 + slot; row < rows; row += size_t(gridDim.x) * 4) {
     const int t = int(row % p.TP);
     const size_t bh = row / p.TP;
     const int b = int(bh / p.H), h = int(bh % p.H);
     const bool real = t < p.T;
-    float xq[E], xk[E], gq[E], gk[E];
+    float x[E], g[E];
 #pragma unroll
-    for (int j = 0; j < E; ++j) xq[j] = xk[j] = gq[j] = gk[j] = 0.f;
+    for (int j = 0; j < E; ++j) x[j] = g[j] = 0.f;
     const size_t tok = size_t(b) * p.T + t, col = size_t(h) * K + lane * E;
+    float lam = 0.f, bt = 0.f;
+    float2 dwp[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     if (real) {
-      load_bf16_vec<E>(p.q + tok * p.q_stride + col, xq);
-      load_bf16_vec<E>(p.k + tok * p.k_stride + col, xk);
-      load_grad_vec<E, GT>(p.dqn, row * K + lane * E, gq);
-      load_grad_vec<E, GT>(p.dkn, row * K + lane * E, gk);
+      load_bf16_vec<E>(xsrc + tok * xs + col, x);
+      load_grad_vec<E, GT>(gsrc, row * K + lane * E, g);
     }
-    const float qr = real ? p.q_rs[row] : 0.f, kr = real ? p.k_rs[row] : 0.f;
-    float dotq = 0.f, dotk = 0.f;
+    if (role == 1) {
+      lam = p.lam[row];
+      bt = p.beta_h[row];
 #pragma unroll
-    for (int j = 0; j < E; ++j) {
-      const int d = lane * E + j;
-      dotq += gq[j] * p.qw[d] * xq[j];
-      dotk += gk[j] * p.kw[d] * xk[j];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      dotq += __shfl_xor_sync(0xffffffffu, dotq, o);
-      dotk += __shfl_xor_sync(0xffffffffu, dotk, o);
-    }
-    dotq *= qr * qr / K;
-    dotk *= kr * kr / K;
-    float oq[E], ok[E];
-#pragma unroll
-    for (int j = 0; j < E; ++j) {
-      const int d = lane * E + j;
-      oq[j] = (gq[j] * p.qw[d] - xq[j] * dotq) * qr;
-      ok[j] = (gk[j] * p.kw[d] - xk[j] * dotk) * kr;
-      aq[j] += xq[j] * qr * gq[j];
-      ak[j] += xk[j] * kr * gk[j];
-    }
-    if (real) {
-      store_bf16_vec<E>(p.dq + tok * p.dq_stride + col, oq);
-      store_bf16_vec<E>(p.dk + tok * p.dk_stride + col, ok);
-    }
-    // write-vector adjoint (ops/utils.py:598-616)
-    const float lam = p.lam[row], bt = p.beta_h[row];
-    float dl = 0.f, db = 0.f;
-#pragma unroll
-    for (int part = 0; part < 2; ++part) {
-      const int pair = lane + 32 * part;
-      float sn, cs;
-      sincosf(clock_phase(lam, pair), &sn, &cs);
-      const float sc = atom_scale(pair);
-      float2 dwp = load_grad_pair<GT>(p.dw, row * 128 + 2 * pair);
-      if (p.dw_b) {
-        const float2 e2 = load_grad_pair<GT>(p.dw_b, row * 128 + 2 * pair);
-        dwp.x += e2.x;
-        dwp.y += e2.y;
+      for (int part = 0; part < 2; ++part) {
+        const int pair = lane + 32 * part;
+        dwp[part] = load_grad_pair<GT>(p.dw, row * 128 + 2 * pair);
+        if (p.dw_b) {
+          const float2 e2 = load_grad_pair<GT>(p.dw_b, row * 128 + 2 * pair);
+          dwp[part].x += e2.x;
+          dwp[part].y += e2.y;
+        }
       }
-      const float de = dwp.x, dd = dwp.y;
-      db += de * sc * cs - dd * sc * sn;
-      dl += (-de * bt * sc * sn - dd * bt * sc * cs) * (pair * kTwoPiOver127);
     }
+    const float r = real ? rsv[row] : 0.f;
+    float dot = 0.f;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      dl += __shfl_xor_sync(0xffffffffu, dl, o);
-      db += __shfl_xor_sync(0xffffffffu, db, o);
+    for (int j = 0; j < E; ++j) dot += g[j] * wv[j] * x[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    dot *= r * r / K;
+    float o_[E];
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      o_[j] = (g[j] * wv[j] - x[j] * dot) * r;
+      acc[j] += x[j] * r * g[j];
     }
-    if (lane == 0) {
-      p.dlam[row] = dl;
-      p.dbeta[row] = db;
+    if (real) store_bf16_vec<E>(dst + tok * ds + col, o_);
+    if (role == 1) {
+      // write-vector adjoint (ops/utils.py:598-616)
+      float dl = 0.f, db = 0.f;
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        const int pair = lane + 32 * part;
+        float sn, cs;
+        __sincosf(clock_phase(lam, pair), &sn, &cs);
+        const float sc = atom_scale(pair);
+        const float de = dwp[part].x, dd = dwp[part].y;
+        db += de * sc * cs - dd * sc * sn;
+        dl += (-de * bt * sc * sn - dd * bt * sc * cs) * (pair * kTwoPiOver127);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        dl += __shfl_xor_sync(0xffffffffu, dl, o);
+        db += __shfl_xor_sync(0xffffffffu, db, o);
+      }
+      if (lane == 0) {
+        p.dlam[row] = dl;
+        p.dbeta[row] = db;
+      }
     }
   }
 #pragma unroll
-  for (int j = 0; j < E; ++j) {
-    pq[wid][lane * E + j] = aq[j];
-    pk[wid][lane * E + j] = ak[j];
-  }
+  for (int j = 0; j < E; ++j) part_s[role][slot][lane * E + j] = acc[j];
   __syncthreads();
   for (int d = threadIdx.x; d < K; d += 256) {
     float sq = 0.f, sk = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      sq += pq[i][d];
-      sk += pk[i][d];
+    for (int i = 0; i < 4; ++i) {
+      sq += part_s[0][i][d];
+      sk += part_s[1][i][d];
     }
     p.dqw_part[size_t(blockIdx.x) * K + d] = sq;
     p.dkw_part[size_t(blockIdx.x) * K + d] = sk;
   }
 }
 
-// Number of blocks (= partial rows) token_bwd_kernel uses for a shape.
+// Number of blocks (= partial rows) token_bwd_kernel uses for a shape: three per SM.
 inline int token_bwd_blocks(size_t rows) {
-  const size_t want = (rows + 7) / 8;
-  return int(want < 296 ? want : 296);
+  const size_t want = (rows + 3) / 4;
+  return int(want < 444 ? want : 444);
 }
 
 
