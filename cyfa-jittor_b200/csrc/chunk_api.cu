@@ -202,7 +202,7 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
                  0.f, nullptr, nullptr, nullptr};
     set_smem(state_scan_kernel<false>, kScanSmem);
     CYFA_LAUNCH("state_scan_fwd", st,
-                (state_scan_kernel<false><<<dim3(d.BH, d.K / 128, 2), 128, kScanSmem, st>>>(m_kn, m_w, p)));
+                (state_scan_kernel<false><<<dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st>>>(m_kn, m_w, p)));
     if ((rc = launch_status())) return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, 128, kRows2D, 0, s.G, s.lam, a->scale, s.raw,
                     s.weights};
@@ -224,7 +224,7 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
     ScanParams p{d.BH, d.H, d.TP, d.NT, 128, d.V, kRows2D, kPublic4D, s.G, a->hv0, s.s2, a->hv,
                  0.f, nullptr, nullptr, nullptr};
     CYFA_LAUNCH("state_scan_fwd", st,
-                (state_scan_kernel<false><<<dim3(d.BH, 1, d.V / 64), 128, kScanSmem, st>>>(m_w, m_v, p)));
+                (state_scan_kernel<false><<<dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st>>>(m_w, m_v, p)));
     if ((rc = launch_status())) return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, d.V, kPublic4D, 1, s.G, s.lam, 1.f,
                     static_cast<__nv_bfloat16*>(a->o), nullptr};
@@ -306,7 +306,7 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     ScanParams p{d.BH, d.H, d.TP, d.NT, 128, d.V, kRows2D, kPublic4D, s.G, g->dhv, w.h2, g->dhv0,
                  1.f, s.s2, a->hv, w.bpart2};
     CYFA_LAUNCH("state_scan_bwd", st,
-                (state_scan_kernel<true><<<dim3(d.BH, 1, d.V / 64), 128, kScanSmem, st>>>(m_weights,
+                (state_scan_kernel<true><<<dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st>>>(m_weights,
                                                                                           m_do, p)));
     if ((rc = launch_status())) return rc;
     ScoresParams sp{d.BH, d.H, d.TP, d.NT, kPublic4D, kPublic4D, s.G, 1.f, w.A, w.Bp};
@@ -354,7 +354,7 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     ScanParams p{d.BH, d.H, d.TP, d.NT, d.K, 128, kRows2D, kRows2D, s.G, g->dhk, w.h1, g->dhk0,
                  a->scale, s.s1, a->hk, w.bpart1};
     CYFA_LAUNCH("state_scan_bwd", st,
-                (state_scan_kernel<true><<<dim3(d.BH, d.K / 128, 2), 128, kScanSmem, st>>>(m_qn, m_draw,
+                (state_scan_kernel<true><<<dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st>>>(m_qn, m_draw,
                                                                                            p)));
     if ((rc = launch_status())) return rc;
     ScoresParams sp{d.BH, d.H, d.TP, d.NT, kRows2D, kRows2D, s.G, a->scale, w.A, w.Bp};

@@ -78,214 +78,270 @@ struct ScanParams {
   float* bpart;                   // reverse: [BH, NT, nsub, 4] partial boundary terms
 };
 
-constexpr int kScanStages = 3;
+constexpr int kScanStages = 4;
 constexpr int kScanStageBytes = 48 * 1024;  // K tile 32 KiB + V tile 16 KiB
 constexpr int kScanSmem = kScanStages * kScanStageBytes + 1024;
+constexpr int kScanBufs = 4;                // TMEM update buffers of 64 columns
+
+// OR of v over the `n` threads of named barrier `id` (every one of them gets it).
+__device__ __forceinline__ bool named_bar_or(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n"
+      " selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"(v ? 1u : 0u), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
+// Chunk-state scan, warp-specialised.  One CTA owns rows dk0..dk0+127 and
+// columns dv0..dv0+63 of the state of one (b, h); 320 threads in five roles that
+// hand tiles to each other through mbarriers only:
+//   warp 8, lane 0 (producer): TMA loads of each tile's K/V operands into a ring
+//     of kScanStages stages; a stage is refilled once the UMMA of its previous
+//     tile is done;
+//   warps 4-7 (scalers): scale the tile's V rows by its gate factor in shared
+//     memory, then signal `scaled`;
+//   warp 9, lane 0 (MMA issuer): U = K^T (V o f) into one of kScanBufs TMEM
+//     buffers once the consumers have released it;
+//   warps 0-3 (consumers): thread r keeps state row r in registers, stores the
+//     state entering each tile (bf16 history) and applies S = 2^{G_last} S + U.
+// The updates U do not depend on the state, so producer, scalers and issuer run
+// up to kScanBufs tiles ahead of the serial recurrence.
+// REVERSE walks the tiles backwards with f = scale 2^{G_t} (adjoint scan) and
+// also forms the boundary partials <S_{j+1}, H_{j+1}>.
+constexpr int kScanThreads = 320;
 
 template <bool REVERSE>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(kScanThreads, 1)
     state_scan_kernel(const __grid_constant__ CUtensorMap map_k,
                       const __grid_constant__ CUtensorMap map_v, ScanParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   __shared__ __align__(8) uint64_t full[kScanStages];
-  __shared__ __align__(8) uint64_t mma_done[2];
+  __shared__ __align__(8) uint64_t scaled[kScanStages];
+  __shared__ __align__(8) uint64_t mma_done[kScanBufs];
+  __shared__ __align__(8) uint64_t tmem_free[kScanBufs];
   __shared__ uint32_t tmem_base;
-  const int tid = threadIdx.x;
+  __shared__ int s_abort;
+  volatile int* abort_flag = &s_abort;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.x, dk0 = blockIdx.y * 128, dv0 = blockIdx.z * 64;
   const int NT = p.NT;
+  static_assert(kScanStages <= kScanBufs, "stage reuse relies on mma_done parity");
 
   if (tid == 0) {
-    for (int s = 0; s < kScanStages; ++s) mbar_init(&full[s], 1);
-    mbar_init(&mma_done[0], 1);
-    mbar_init(&mma_done[1], 1);
+    for (int s = 0; s < kScanStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&scaled[s], 4);
+    }
+    for (int b = 0; b < kScanBufs; ++b) {
+      mbar_init(&mma_done[b], 1);
+      mbar_init(&tmem_free[b], 4);
+    }
+    s_abort = 0;
     mbar_fence_init();
     prefetch_tmap(&map_k);
     prefetch_tmap(&map_v);
   }
-  if (tid < 32) tmem_alloc(&tmem_base, 128);
+  if (warp == 0) tmem_alloc(&tmem_base, 64 * kScanBufs);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
-  const uint32_t lane_tmem = tmem_lane_base(tmem);
-
   auto tile_of = [&](int idx) { return REVERSE ? NT - 1 - idx : idx; };
-  int issued = 0;
-  auto issue = [&](int idx) {
-    const int s = idx % kScanStages, j = tile_of(idx);
-    uint8_t* st = smem + s * kScanStageBytes;
-    mbar_expect_tx(&full[s], kScanStageBytes);
-    load_token_tile(st, &map_k, p.k_mode, bh, p.H, p.TP, j, dk0, 128, &full[s]);
-    load_token_tile(st + 32768, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 64, &full[s]);
-  };
-  if (tid == 0) {
-    for (; issued < kScanStages && issued < NT; ++issued) issue(issued);
-  }
+  const float* Gbh = p.G + size_t(bh) * p.TP;
 
-  float S[64];
-  const size_t row_off = (size_t(bh) * p.DK + dk0 + tid) * p.DV + dv0;
-  if (p.init) {
-    const float4* src = reinterpret_cast<const float4*>(p.init + row_off);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float4 x = src[i];
-      S[4 * i] = x.x;
-      S[4 * i + 1] = x.y;
-      S[4 * i + 2] = x.z;
-      S[4 * i + 3] = x.w;
+  if (warp == 8) {
+    // ------------------------------------------------ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int idx = 0; idx < NT; ++idx) {
+        if (*abort_flag) break;
+        const int s = idx % kScanStages, j = tile_of(idx);
+        if (idx >= kScanStages) {
+          const int prev = idx - kScanStages;  // previous tile of this stage
+          if (!mbar_wait(&mma_done[prev % kScanBufs], (prev / kScanBufs) & 1)) {
+            *abort_flag = 1;
+            break;
+          }
+        }
+        uint8_t* st = smem + s * kScanStageBytes;
+        mbar_expect_tx(&full[s], kScanStageBytes);
+        load_token_tile(st, &map_k, p.k_mode, bh, p.H, p.TP, j, dk0, 128, &full[s]);
+        load_token_tile(st + 32768, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 64, &full[s]);
+        issued = idx + 1;
+      }
+      // every issued copy lands before shared memory goes away
+      for (int idx = issued > kScanStages ? issued - kScanStages : 0; idx < issued; ++idx)
+        mbar_wait(&full[idx % kScanStages], (idx / kScanStages) & 1);
     }
-  } else {
+  } else if (warp == 9) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(128, 64, 1, 1);
+      int last_commit = -1;
+      for (int idx = 0; idx < NT; ++idx) {
+        if (*abort_flag) break;
+        const int s = idx % kScanStages, b = idx % kScanBufs;
+        bool ok = mbar_wait(&scaled[s], (idx / kScanStages) & 1);
+        if (ok && idx >= kScanBufs) ok = mbar_wait(&tmem_free[b], ((idx / kScanBufs) - 1) & 1);
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kb = smem_u32(smem + s * kScanStageBytes), vb = kb + 32768;
 #pragma unroll
-    for (int i = 0; i < 64; ++i) S[i] = 0.f;
-  }
-  const uint32_t idesc = make_idesc(128, 64, 1, 1);
-  const int nsub = gridDim.y * gridDim.z, sub = blockIdx.y * gridDim.z + blockIdx.z;
-  int consumed = 0, committed = 0, retired = 0;
-
-  // Waits for tile idx's operands, rescales its V rows and issues its UMMA into
-  // TMEM buffer idx & 1.  Returns false (on every thread) if a wait timed out.
-  // gate values of a tile: (G_t of this thread's token row, G_last)
-  auto load_g = [&](int idx, float& gt, float& gl) {
-    const float* Gt = p.G + size_t(bh) * p.TP + size_t(tile_of(idx)) * 128;
-    gt = Gt[tid];
-    gl = Gt[127];
-  };
-  auto prepare = [&](int idx, float gt, float gl) -> bool {
-    const int s = idx % kScanStages;
-    uint8_t* st = smem + s * kScanStageBytes;
-    const float f = REVERSE ? p.scale * exp2f(gt) : exp2f(gl - gt);
-    bool good = mbar_wait(&full[s], (idx / kScanStages) & 1);
-    if (good) {
-      const uint32_t vb = smem_u32(st + 32768);
+        for (int ks = 0; ks < 8; ++ks)
+          umma_bf16(tmem + b * 64, mnmaj_desc(kb, 128, ks), mnmaj_desc(vb, 128, ks), idesc,
+                    ks > 0);
+        umma_commit(&mma_done[b]);
+        last_commit = idx;
+      }
+      if (last_commit >= 0)
+        mbar_wait(&mma_done[last_commit % kScanBufs], (last_commit / kScanBufs) & 1);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------ scalers
+    const int srow = tid - 128;
+    float gt_n = 0.f, gl_n = 0.f;
+    if (NT > 0) {
+      gt_n = Gbh[size_t(tile_of(0)) * 128 + srow];
+      gl_n = Gbh[size_t(tile_of(0)) * 128 + 127];
+    }
+    for (int idx = 0; idx < NT; ++idx) {
+      const int s = idx % kScanStages;
+      const float gt = gt_n, gl = gl_n;
+      if (idx + 1 < NT) {
+        gt_n = Gbh[size_t(tile_of(idx + 1)) * 128 + srow];
+        gl_n = Gbh[size_t(tile_of(idx + 1)) * 128 + 127];
+      }
+      const float f = REVERSE ? p.scale * exp2f(gt) : exp2f(gl - gt);
+      const bool got =
+          __all_sync(0xffffffffu, *abort_flag == 0 && mbar_wait(&full[s], (idx / kScanStages) & 1));
+      if (!got) {
+        *abort_flag = 1;
+        break;
+      }
+      const uint32_t vb = smem_u32(smem + s * kScanStageBytes + 32768);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
-        const uint32_t a = vb + sw128(tid, c);
+        const uint32_t a = vb + sw128(srow, c);
         float x[8];
         unpack_bf16x8(ld_shared_v4(a), x);
         st_shared_v4(a, pack_bf16(x[0] * f, x[1] * f), pack_bf16(x[2] * f, x[3] * f),
                      pack_bf16(x[4] * f, x[5] * f), pack_bf16(x[6] * f, x[7] * f));
       }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&scaled[s]);
     }
-    fence_async_smem();
-    tc_fence_before();
-    good = __syncthreads_and(good);
-    tc_fence_after();
-    consumed = idx + 1;
-    if (!good) return false;
-    if (tid == 0) {
-      const uint32_t kb = smem_u32(st), vb = smem_u32(st + 32768);
+  } else {
+    // ------------------------------------------------ consumers: the recurrence
+    float S[64];
+    const size_t row_off = (size_t(bh) * p.DK + dk0 + tid) * p.DV + dv0;
+    if (p.init) {
+      const float4* src = reinterpret_cast<const float4*>(p.init + row_off);
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks)
-        umma_bf16(tmem + (idx & 1) * 64, mnmaj_desc(kb, 128, ks), mnmaj_desc(vb, 128, ks), idesc,
-                  ks > 0);
-      umma_commit(&mma_done[idx & 1]);
-    }
-    committed = idx + 1;
-    return true;
-  };
-
-  float g_cur_t = 0.f, g_cur_l = 0.f, g_nxt_t = 0.f, g_nxt_l = 0.f;
-  if (NT > 0) load_g(0, g_cur_t, g_cur_l);
-  if (NT > 1) load_g(1, g_nxt_t, g_nxt_l);
-  bool ok = NT > 0 ? prepare(0, g_cur_t, g_cur_l) : true;
-  for (int idx = 0; idx < NT && ok; ++idx) {
-    const int j = tile_of(idx);
-    const float gl = g_cur_l;
-    // gate values two tiles ahead, loaded while this tile's work runs
-    float g_far_t = 0.f, g_far_l = 0.f;
-    if (idx + 2 < NT) load_g(idx + 2, g_far_t, g_far_l);
-    // REVERSE: fetch S_{j+1} (this CTA's row slice) early; it is consumed below
-    uint4 nxt[8];
-    if constexpr (REVERSE) {
-      if (j + 1 < NT) {
-        const uint4* src = reinterpret_cast<const uint4*>(
-            p.fwd_hist + ((size_t(bh) * NT + j + 1) * p.DK + dk0 + tid) * p.DV + dv0);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) nxt[c] = src[c];
+      for (int i = 0; i < 16; ++i) {
+        const float4 x = src[i];
+        S[4 * i] = x.x;
+        S[4 * i + 1] = x.y;
+        S[4 * i + 2] = x.z;
+        S[4 * i + 3] = x.w;
       }
-    }
-    // overlap: the next tile's update is independent of the running state
-    if (idx + 1 < NT && !prepare(idx + 1, g_nxt_t, g_nxt_l)) {
-      ok = false;
-      break;
-    }
-    g_cur_l = g_nxt_l;
-    g_nxt_t = g_far_t;
-    g_nxt_l = g_far_l;
-    // state entering tile j (forward) / adjoint leaving tile j (reverse)
-    {
-      uint4* dst = reinterpret_cast<uint4*>(p.hist + ((size_t(bh) * NT + j) * p.DK + dk0 + tid) *
-                                                         p.DV + dv0);
+    } else {
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        dst[c] = make_uint4(pack_bf16(S[8 * c], S[8 * c + 1]), pack_bf16(S[8 * c + 2], S[8 * c + 3]),
-                            pack_bf16(S[8 * c + 4], S[8 * c + 5]),
-                            pack_bf16(S[8 * c + 6], S[8 * c + 7]));
+      for (int i = 0; i < 64; ++i) S[i] = 0.f;
     }
-    if constexpr (REVERSE) {
-      // <S_{j+1}, H_{j+1}> over this CTA's slice (S_{j+1} from the forward pass)
-      float dot = 0.f;
-      if (j + 1 < NT) {
+    const uint32_t lane_tmem = tmem + ((warp * 32) << 16);
+    const int nsub = gridDim.y * gridDim.z, sub = blockIdx.y * gridDim.z + blockIdx.z;
+    bool ok = true;
+    // loads one iteration ahead: the gate total of the next tile and (REVERSE)
+    // the forward state rows that the next boundary term pairs with
+    float gl_next = NT > 0 ? Gbh[size_t(tile_of(0)) * 128 + 127] : 0.f;
+    uint4 fwd_next[8];
+    for (int idx = 0; idx < NT; ++idx) {
+      const int j = tile_of(idx), b = idx % kScanBufs;
+      const float gl = gl_next;
+      if (idx + 1 < NT) gl_next = Gbh[size_t(tile_of(idx + 1)) * 128 + 127];
+      // state entering tile j (forward) / adjoint leaving tile j (reverse)
+      {
+        uint4* dst = reinterpret_cast<uint4*>(p.hist + ((size_t(bh) * NT + j) * p.DK + dk0 + tid) *
+                                                           p.DV + dv0);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float x[8];
-          unpack_bf16x8(nxt[c], x);
+        for (int c = 0; c < 8; ++c)
+          dst[c] = make_uint4(pack_bf16(S[8 * c], S[8 * c + 1]), pack_bf16(S[8 * c + 2], S[8 * c + 3]),
+                              pack_bf16(S[8 * c + 4], S[8 * c + 5]),
+                              pack_bf16(S[8 * c + 6], S[8 * c + 7]));
+      }
+      if constexpr (REVERSE) {
+        // <S_{j+1}, H_{j+1}> over this CTA's slice (S_{j+1} from the forward pass)
+        float dot = 0.f;
+        if (j + 1 < NT) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) dot += x[e] * S[8 * c + e];
+          for (int c = 0; c < 8; ++c) {
+            float x[8];
+            unpack_bf16x8(fwd_next[c], x);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dot += x[e] * S[8 * c + e];
+          }
+        } else {
+          const float4* src = reinterpret_cast<const float4*>(p.fwd_final + row_off);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float4 x = src[i];
+            dot += x.x * S[4 * i] + x.y * S[4 * i + 1] + x.z * S[4 * i + 2] + x.w * S[4 * i + 3];
+          }
         }
-      } else {
-        const float4* src = reinterpret_cast<const float4*>(p.fwd_final + row_off);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float4 x = src[i];
-          dot += x.x * S[4 * i] + x.y * S[4 * i + 1] + x.z * S[4 * i + 2] + x.w * S[4 * i + 3];
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        // one partial per warp: bpart[bh][j][sub][warp]
+        if (lane == 0) p.bpart[((size_t(bh) * NT + j) * nsub + sub) * 4 + warp] = dot;
+        // S_{j'+1} of the next tile j' = j - 1 is the forward state entering tile j
+        if (idx + 1 < NT) {
+          const uint4* src = reinterpret_cast<const uint4*>(
+              p.fwd_hist + ((size_t(bh) * NT + j) * p.DK + dk0 + tid) * p.DV + dv0);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) fwd_next[c] = src[c];
         }
       }
+      const bool got = __all_sync(0xffffffffu, mbar_wait(&mma_done[b], (idx / kScanBufs) & 1));
+      tc_fence_after();
+      if (got) {
+        const float gamma = exp2f(gl);
+        float U[32];
+        tmem_ld32(lane_tmem + b * 64, U);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      // one partial per warp: bpart[bh][j][sub][warp]
-      if ((tid & 31) == 0) p.bpart[((size_t(bh) * NT + j) * nsub + sub) * 4 + (tid >> 5)] = dot;
+        for (int i = 0; i < 32; ++i) S[i] = S[i] * gamma + U[i];
+        tmem_ld32(lane_tmem + b * 64 + 32, U);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) S[32 + i] = S[32 + i] * gamma + U[i];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_free[b]);
+      if (!got || __any_sync(0xffffffffu, *abort_flag != 0)) {
+        ok = false;
+        *abort_flag = 1;
+        break;
+      }
     }
-    const bool got = mbar_wait(&mma_done[idx & 1], (idx >> 1) & 1);
-    tc_fence_after();
-    if (got) {
-      const float gamma = exp2f(gl);
-      float U[32];
-      tmem_ld32(lane_tmem + (idx & 1) * 64, U);
+    // the final state (forward) / initial-state adjoint (reverse)
+    if (ok && p.last) {
+      float4* dst = reinterpret_cast<float4*>(p.last + row_off);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) S[i] = S[i] * gamma + U[i];
-      tmem_ld32(lane_tmem + (idx & 1) * 64 + 32, U);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) S[32 + i] = S[32 + i] * gamma + U[i];
+      for (int i = 0; i < 16; ++i)
+        dst[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
     }
-    tc_fence_before();
-    ok = __syncthreads_and(got);  // every thread leaves the loop at the same iteration
-    if (ok) retired = idx + 1;
-    // tile idx's stage is free once its MMA has completed
-    if (tid == 0 && ok && issued < NT) {
-      issue(issued);
-      ++issued;
-    }
-  }
-  ok = __syncthreads_and(ok);
-
-  if (ok && p.last) {
-    float4* dst = reinterpret_cast<float4*>(p.last + row_off);
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      dst[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
-  } else if (!ok && tid == 0) {
-    // unwind: let in-flight copies and MMAs land before TMEM and smem go away
-    for (int idx = consumed; idx < issued; ++idx)
-      mbar_wait(&full[idx % kScanStages], (idx / kScanStages) & 1);
-    for (int idx = retired; idx < committed; ++idx) mbar_wait(&mma_done[idx & 1], (idx >> 1) & 1);
   }
   tc_fence_before();
   __syncthreads();
-  if (tid < 32) {
+  if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 128);
+    tmem_dealloc(tmem, 64 * kScanBufs);
   }
 }
 
