@@ -290,6 +290,7 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   if ((rc = tmap_2d(&m_Bp, w.Bp, trows, 128, 128))) return rc;
   if ((rc = tmap_2d(&m_tab, a->table_bf, uint64_t(d.H) * 128, 128, 128))) return rc;
   const dim3 tiles(d.BH * d.NT);
+  const dim3 persist(d.BH * d.NT < 148 ? d.BH * d.NT : 148);  // one CTA per SM
   set_smem(state_scan_kernel<true>, kScanSmem);
   set_smem(dual_gemm_kernel, kDualSmem);
   auto dual = [&](const CUtensorMap& x1, const CUtensorMap& y1, const CUtensorMap& x2,
@@ -313,12 +314,12 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     if (d.V == 256) {
       set_smem(tile_scores_kernel<128, 256>, scores_smem<128, 256>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<128, 256><<<tiles, 256, scores_smem<128, 256>(), st>>>(
+                  (tile_scores_kernel<128, 256><<<persist, 256, scores_smem<128, 256>(), st>>>(
                       m_weights, m_w, m_do, m_v, sp)));
     } else {
       set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<128, 128><<<tiles, 256, scores_smem<128, 128>(), st>>>(
+                  (tile_scores_kernel<128, 128><<<persist, 256, scores_smem<128, 128>(), st>>>(
                       m_weights, m_w, m_do, m_v, sp)));
     }
     if ((rc = launch_status())) return rc;
@@ -361,12 +362,12 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     if (d.K == 256) {
       set_smem(tile_scores_kernel<256, 128>, scores_smem<256, 128>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<256, 128><<<tiles, 256, scores_smem<256, 128>(), st>>>(
+                  (tile_scores_kernel<256, 128><<<persist, 256, scores_smem<256, 128>(), st>>>(
                       m_qn, m_kn, m_draw, m_w, sp)));
     } else {
       set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<128, 128><<<tiles, 256, scores_smem<128, 128>(), st>>>(
+                  (tile_scores_kernel<128, 128><<<persist, 256, scores_smem<128, 128>(), st>>>(
                       m_qn, m_kn, m_draw, m_w, sp)));
     }
     if ((rc = launch_status())) return rc;

@@ -42,6 +42,23 @@ constexpr int scores_smem() {
   return 2 * DK * 256 + 2 * DV * 256 + 1024;
 }
 
+// Persistent: CTA c handles tiles c, c + gridDim.x, ...; the next tile's
+// operands are loaded as soon as the current tile's MMAs have read shared
+// memory, so they stream in during the masked epilogue.
+template <int DK, int DV>
+__device__ __forceinline__ void scores_issue_loads(uint8_t* smem, const CUtensorMap* mq,
+                                                   const CUtensorMap* mk, const CUtensorMap* mdo,
+                                                   const CUtensorMap* mv, const ScoresParams& p,
+                                                   int tile, uint64_t* bar) {
+  constexpr int kK = DK * 256, kD = 2 * DK * 256, kV = 2 * DK * 256 + DV * 256;
+  const int bh = tile / p.NT, j = tile % p.NT;
+  mbar_expect_tx(bar, 2 * DK * 256 + 2 * DV * 256);
+  load_token_tile(smem, mq, kRows2D, bh, p.H, p.TP, j, 0, DK, bar);
+  load_token_tile(smem + kK, mk, kRows2D, bh, p.H, p.TP, j, 0, DK, bar);
+  load_token_tile(smem + kD, mdo, p.do_mode, bh, p.H, p.TP, j, 0, DV, bar);
+  load_token_tile(smem + kV, mv, p.v_mode, bh, p.H, p.TP, j, 0, DV, bar);
+}
+
 template <int DK, int DV>
 __global__ void __launch_bounds__(256, 1)
     tile_scores_kernel(const __grid_constant__ CUtensorMap map_q,
@@ -55,14 +72,13 @@ __global__ void __launch_bounds__(256, 1)
   __shared__ uint32_t tmem_base;
   __shared__ float Gs[128];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT;
+  const int ntiles = p.BH * p.NT;
   if (tid == 0) {
     mbar_init(&bar_in, 1);
     mbar_init(&bar_mma, 1);
     mbar_fence_init();
   }
   if (warp == 0) tmem_alloc(&tmem_base, 256);
-  if (tid < 128) Gs[tid] = p.G[size_t(bh) * p.TP + j * 128 + tid];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -70,48 +86,80 @@ __global__ void __launch_bounds__(256, 1)
   // warp w: TMEM lane quadrant (w & 3), matrix (w >> 2): 0 = A (q.k), 1 = B' (dO.v)
   const int quad = warp & 3, m = warp >> 2, r = quad * 32 + lane;
   const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
+  const uint32_t sQ = smem_u32(smem + kQ), sK = smem_u32(smem + kK), sD = smem_u32(smem + kD),
+                 sV = smem_u32(smem + kV);
   bool ok = true;
-  if (tid == 0) {
-    mbar_expect_tx(&bar_in, 2 * DK * 256 + 2 * DV * 256);
-    load_token_tile(smem + kQ, &map_q, kRows2D, bh, p.H, p.TP, j, 0, DK, &bar_in);
-    load_token_tile(smem + kK, &map_k, kRows2D, bh, p.H, p.TP, j, 0, DK, &bar_in);
-    load_token_tile(smem + kD, &map_do, p.do_mode, bh, p.H, p.TP, j, 0, DV, &bar_in);
-    load_token_tile(smem + kV, &map_v, p.v_mode, bh, p.H, p.TP, j, 0, DV, &bar_in);
-    if (mbar_wait(&bar_in, 0)) {
-      tc_fence_after();
-      const uint32_t sQ = smem_u32(smem + kQ), sK = smem_u32(smem + kK),
-                     sD = smem_u32(smem + kD), sV = smem_u32(smem + kV);
-#pragma unroll 4
-      for (int ks = 0; ks < DK / 16; ++ks)
-        umma_bf16(tmem, kmaj_desc(sQ, 128, ks), kmaj_desc(sK, 128, ks), make_idesc(128, 128, 0, 0),
-                  ks > 0);
-#pragma unroll 4
-      for (int ks = 0; ks < DV / 16; ++ks)
-        umma_bf16(tmem + 128, kmaj_desc(sD, 128, ks), kmaj_desc(sV, 128, ks),
-                  make_idesc(128, 128, 0, 0), ks > 0);
-      umma_commit(&bar_mma);
-    } else {
-      mbar_arrive(&bar_mma);
-    }
+  bool in_pending = false, mma_pending = false;  // elected-thread state, drained before exit
+  uint32_t in_ph = 0;
+  if (tid == 0 && blockIdx.x < ntiles) {
+    scores_issue_loads<DK, DV>(smem, &map_q, &map_k, &map_do, &map_v, p, blockIdx.x, &bar_in);
+    in_pending = true;
   }
-  __syncwarp();
-  if (!mbar_wait(&bar_mma, 0)) ok = false;
-  tc_fence_after();
-  if (ok) {
-    const float gt = Gs[r];
-    const size_t row = (size_t(bh) * p.NT + j) * 128 + r;
-    __nv_bfloat16* dst = (m == 0 ? p.A : p.Bp) + row * 128;
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float v[32];
-      tmem_ld32(lane_tmem + m * 128 + 32 * c, v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int s = 32 * c + i;
-        v[i] = s <= r ? p.scale * v[i] * exp2f(gt - Gs[s]) : 0.f;
+  uint32_t phase = 0;
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, phase ^= 1) {
+    const int bh = tile / p.NT, j = tile % p.NT;
+    if (tid < 128) Gs[tid] = p.G[size_t(bh) * p.TP + j * 128 + tid];
+    if (tid == 0) {
+      bool got = ok && mbar_wait(&bar_in, phase);
+      if (got) in_pending = false;
+      tc_fence_after();
+      if (got) {
+#pragma unroll 4
+        for (int ks = 0; ks < DK / 16; ++ks)
+          umma_bf16(tmem, kmaj_desc(sQ, 128, ks), kmaj_desc(sK, 128, ks),
+                    make_idesc(128, 128, 0, 0), ks > 0);
+#pragma unroll 4
+        for (int ks = 0; ks < DV / 16; ++ks)
+          umma_bf16(tmem + 128, kmaj_desc(sD, 128, ks), kmaj_desc(sV, 128, ks),
+                    make_idesc(128, 128, 0, 0), ks > 0);
+        umma_commit(&bar_mma);
+        mma_pending = true;
+        const int next = tile + gridDim.x;
+        if (next < ntiles) {
+          if (mbar_wait(&bar_mma, phase)) {
+            mma_pending = false;
+            scores_issue_loads<DK, DV>(smem, &map_q, &map_k, &map_do, &map_v, p, next, &bar_in);
+            in_pending = true;
+            in_ph = phase ^ 1;
+          } else {
+            got = false;
+          }
+        }
+      } else {
+        mbar_arrive(&bar_mma);  // releases the epilogue's wait; its result is discarded
       }
-      store_bf16x32_global(dst + 32 * c, v);
+      if (!got) ok = false;
     }
+    __syncwarp();
+    bool mm = mbar_wait(&bar_mma, phase);
+    if (tid == 0 && mm) mma_pending = false;
+    tc_fence_after();
+    mm = __syncthreads_and(mm && ok) != 0;  // also publishes Gs
+    if (mm) {
+      const float gt = Gs[r];
+      const size_t row = (size_t(bh) * p.NT + j) * 128 + r;
+      __nv_bfloat16* dst = (m == 0 ? p.A : p.Bp) + row * 128;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(lane_tmem + m * 128 + 32 * c, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int s_ = 32 * c + i;
+          v[i] = s_ <= r ? p.scale * v[i] * exp2f(gt - Gs[s_]) : 0.f;
+        }
+        store_bf16x32_global(dst + 32 * c, v);
+      }
+    }
+    // TMEM drained and Gs free before the next tile
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (!mm) break;
+  }
+  if (tid == 0) {
+    if (mma_pending) mbar_wait(&bar_mma, phase);
+    if (in_pending) mbar_wait(&bar_in, in_ph);
   }
   tc_fence_before();
   __syncthreads();
