@@ -266,6 +266,39 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
   return v;
 }
 
+// 2^x on the special-function unit (relative error about 2^-22; results below
+// 2^-126 flush to zero).  Used for decay factors 2^{G_t - G_s} <= 1.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Warp-cooperative store of a 32-row x 32-column bf16 block.  Lane l holds the
+// 32 values of row l (fp32); they are packed into the warp's 2 KiB staging
+// buffer `scratch` (16-byte chunks XOR-swizzled, conflict-free both ways) and
+// written back so that each store instruction covers 8 rows x 64 contiguous
+// bytes instead of 32 rows x 16 bytes.  Row r goes to dst + r * stride
+// (elements) when bit r of `valid` is set.
+__device__ __forceinline__ void warp_store_block_bf16(uint32_t scratch, const float* v,
+                                                      __nv_bfloat16* dst, size_t stride,
+                                                      uint32_t valid) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+    st_shared_v4(scratch + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4),
+                 pack_bf16(v[8 * c], v[8 * c + 1]), pack_bf16(v[8 * c + 2], v[8 * c + 3]),
+                 pack_bf16(v[8 * c + 4], v[8 * c + 5]), pack_bf16(v[8 * c + 6], v[8 * c + 7]));
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + (lane >> 2), c = lane & 3;
+    const uint4 val = ld_shared_v4(scratch + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+    if ((valid >> r) & 1u) *reinterpret_cast<uint4*>(dst + r * stride + c * 8) = val;
+  }
+  __syncwarp();
+}
+
 __device__ __forceinline__ void unpack_bf16x8(const uint4& u, float* f) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll

@@ -39,7 +39,7 @@ struct ScoresParams {
 
 template <int DK, int DV>
 constexpr int scores_smem() {
-  return 2 * DK * 256 + 2 * DV * 256 + 1024;
+  return 2 * DK * 256 + 2 * DV * 256 + 1024 + 8 * 2048;  // operands + per-warp staging
 }
 
 // Persistent: CTA c handles tiles c, c + gridDim.x, ...; the next tile's
@@ -83,8 +83,10 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
-  // warp w: TMEM lane quadrant (w & 3), matrix (w >> 2): 0 = A (q.k), 1 = B' (dO.v)
-  const int quad = warp & 3, m = warp >> 2, r = quad * 32 + lane;
+  // warp w: TMEM lane quadrant (w & 3) = token rows, column half (w >> 2); it
+  // writes both A (q.k) and B' (dO.v) there, sharing each decay factor
+  const int quad = warp & 3, half = warp >> 2, r = quad * 32 + lane;
+  const uint32_t scratch = smem_u32(smem + 2 * DK * 256 + 2 * DV * 256) + warp * 2048;
   const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
   const uint32_t sQ = smem_u32(smem + kQ), sK = smem_u32(smem + kK), sD = smem_u32(smem + kD),
                  sV = smem_u32(smem + kV);
@@ -137,18 +139,26 @@ __global__ void __launch_bounds__(256, 1)
     mm = __syncthreads_and(mm && ok) != 0;  // also publishes Gs
     if (mm) {
       const float gt = Gs[r];
-      const size_t row = (size_t(bh) * p.NT + j) * 128 + r;
-      __nv_bfloat16* dst = (m == 0 ? p.A : p.Bp) + row * 128;
+      const size_t row0 = (size_t(bh) * p.NT + j) * 128 + quad * 32;  // warp's first row
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tmem_ld32(lane_tmem + m * 128 + 32 * c, v);
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {
+        float a[32], b[32];
+        if (c <= quad) {  // chunks above the diagonal block are all masked
+          tmem_ld32(lane_tmem + 32 * c, a);
+          tmem_ld32(lane_tmem + 128 + 32 * c, b);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int s_ = 32 * c + i;
-          v[i] = s_ <= r ? p.scale * v[i] * exp2f(gt - Gs[s_]) : 0.f;
+          for (int i = 0; i < 32; ++i) {
+            const int s_ = 32 * c + i;
+            const float f = s_ <= r ? p.scale * fast_exp2(gt - Gs[s_]) : 0.f;
+            a[i] *= f;
+            b[i] *= f;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) a[i] = b[i] = 0.f;
         }
-        store_bf16x32_global(dst + 32 * c, v);
+        warp_store_block_bf16(scratch, a, p.A + row0 * 128 + 32 * c, 128, 0xffffffffu);
+        warp_store_block_bf16(scratch, b, p.Bp + row0 * 128 + 32 * c, 128, 0xffffffffu);
       }
     }
     // TMEM drained and Gs free before the next tile
@@ -190,7 +200,7 @@ struct DualParams {
   long long out_stride;  // out_mode 2: elements between consecutive tokens
 };
 
-constexpr int kDualSmem = 192 * 1024 + 1024;
+constexpr int kDualSmem = 192 * 1024 + 1024 + 8 * 2048;  // operands + per-warp staging
 
 // Persistent: CTA c handles tiles c, c + gridDim.x, ...  Per tile the elected
 // thread waits for the operand tiles, issues both GEMMs into TMEM, and as soon
@@ -243,6 +253,7 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t id1 = make_idesc(128, p.N, p.x1_mn, 1);
   const uint32_t id2 = make_idesc(128, p.N, 0, p.y2_kmaj ? 0 : 1);
   const int ncol = p.N / 2, c_beg = half * ncol;  // 64 or 128 columns
+  const uint32_t scratch = smem_u32(smem) + 192 * 1024 + warp * 2048;
   bool ok = true;
   // elected-thread state: an operand load in flight (and its barrier parity), MMAs
   // committed but not yet seen complete -- both are waited for before exit
@@ -325,14 +336,18 @@ __global__ void __launch_bounds__(256, 1)
           }
         }
         if (p.out_mode == 2) {
-          if (t < p.T) {
-            const int b_ = bh / p.H, h = bh % p.H;
-            store_bf16x32_global(static_cast<__nv_bfloat16*>(p.out) +
-                                     (size_t(b_) * p.T + t) * p.out_stride + size_t(h) * p.N + col,
-                                 a);
-          }
+          const int b_ = bh / p.H, h = bh % p.H, t0 = j * 128 + quad * 32;
+          const int nvalid = p.T - t0;
+          const uint32_t valid = nvalid >= 32 ? 0xffffffffu : (nvalid <= 0 ? 0u : (1u << nvalid) - 1u);
+          warp_store_block_bf16(scratch, a,
+                                static_cast<__nv_bfloat16*>(p.out) +
+                                    (size_t(b_) * p.T + t0) * p.out_stride + size_t(h) * p.N + col,
+                                p.out_stride, valid);
         } else if (p.out_mode == 3) {
-          store_bf16x32_global(static_cast<__nv_bfloat16*>(p.out) + row * p.N + col, a);
+          warp_store_block_bf16(scratch, a,
+                                static_cast<__nv_bfloat16*>(p.out) +
+                                    (size_t(bh) * p.TP + j * 128 + quad * 32) * p.N + col,
+                                p.N, 0xffffffffu);
         } else {
           float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + col);
 #pragma unroll
