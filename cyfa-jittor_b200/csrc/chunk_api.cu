@@ -97,11 +97,11 @@ static Work carve_work(const Dims& d, void* base, size_t* total) {
 // [B,T,H,D] bf16 whose tokens are `stride` elements apart (stride >= H*D) as the
 // 4-D map {D, H, T, B} with a {64, 1, 128, 1} box.
 static int tmap_public(CUtensorMap* m, const void* base, int B, int T, int H, int D,
-                       long long stride) {
+                       long long stride, uint32_t box_rows = 128) {
   const uint64_t dims[4] = {uint64_t(D), uint64_t(H), uint64_t(T), uint64_t(B)};
   const uint64_t strides[3] = {uint64_t(D) * 2, uint64_t(stride) * 2,
                                uint64_t(T) * uint64_t(stride) * 2};
-  const uint32_t box[4] = {64, 1, 128, 1};
+  const uint32_t box[4] = {64, 1, box_rows, 1};
   return make_tmap_bf16(m, base, 4, dims, strides, box);
 }
 
@@ -289,6 +289,19 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   if ((rc = tmap_2d(&m_A, w.A, trows, 128, 128))) return rc;
   if ((rc = tmap_2d(&m_Bp, w.Bp, trows, 128, 128))) return rc;
   if ((rc = tmap_2d(&m_tab, a->table_bf, uint64_t(d.H) * 128, 128, 128))) return rc;
+  // 64-row boxes: operands the dual GEMM reads MN-major in 64-row k-blocks
+  CUtensorMap m_qn64, m_kn64, m_w64, m_weights64, m_do64, m_draw64, m_h1_64, m_h2_64, m_A64,
+      m_Bp64;
+  if ((rc = tmap_2d(&m_qn64, s.qn, rows, d.K, 64))) return rc;
+  if ((rc = tmap_2d(&m_kn64, s.kn, rows, d.K, 64))) return rc;
+  if ((rc = tmap_2d(&m_w64, s.w, rows, 128, 64))) return rc;
+  if ((rc = tmap_2d(&m_weights64, s.weights, rows, 128, 64))) return rc;
+  if ((rc = tmap_2d(&m_draw64, w.draw, rows, 128, 64))) return rc;
+  if ((rc = tmap_public(&m_do64, g->d_o, d.B, d.T, d.H, d.V, (long long)d.H * d.V, 64))) return rc;
+  if ((rc = tmap_2d(&m_h1_64, w.h1, uint64_t(d.BH) * d.NT * d.K, 128, 64))) return rc;
+  if ((rc = tmap_2d(&m_h2_64, w.h2, uint64_t(d.BH) * d.NT * 128, d.V, 64))) return rc;
+  if ((rc = tmap_2d(&m_A64, w.A, trows, 128, 64))) return rc;
+  if ((rc = tmap_2d(&m_Bp64, w.Bp, trows, 128, 64))) return rc;
   const dim3 tiles(d.BH * d.NT);
   const dim3 persist(d.BH * d.NT < 148 ? d.BH * d.NT : 148);  // one CTA per SM
   set_smem(state_scan_kernel<true>, kScanSmem);
@@ -296,7 +309,8 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   auto dual = [&](const CUtensorMap& x1, const CUtensorMap& y1, const CUtensorMap& x2,
                   const CUtensorMap& y2, DualParams p) {
     const unsigned ntile = unsigned(d.BH * d.NT), grid = ntile < 148 ? ntile : 148;  // persistent
-    CYFA_LAUNCH("dual_gemm", st, (dual_gemm_kernel<<<grid, 256, kDualSmem, st>>>(x1, y1, x2, y2, p)));
+    CYFA_LAUNCH("dual_gemm", st,
+                (dual_gemm_kernel<<<grid, kDualThreads, kDualSmem, st>>>(x1, y1, x2, y2, p)));
     return launch_status();
   };
   // boundary partials per tile: one per (CTA slice, warp)
@@ -326,15 +340,15 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     // dweights = B' w + 2^{G_t} dO S^T ;  dG = weights . dweights
     DualParams q2{d.BH, d.H, d.TP, d.NT, d.T, 0, kRows2D, kPublic4D, 1, 128, d.V, 128, d.V, s.G,
                   1.f, 0, 3, w.dweights, s.weights, 1.f, 0, w.dG};
-    if ((rc = dual(m_Bp, m_w, m_do, m_s2, q2))) return rc;
+    if ((rc = dual(m_Bp, m_w64, m_do, m_s2, q2))) return rc;
     // dw = B'^T weights + 2^{G_L-G_s} v H^T ;  dG -= w . dw
     DualParams k2{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kPublic4D, 1, 128, d.V, 128, d.V, s.G,
                   1.f, 1, 3, w.dw, s.w, -1.f, 1, w.dG};
-    if ((rc = dual(m_Bp, m_weights, m_v, m_h2, k2))) return rc;
+    if ((rc = dual(m_Bp64, m_weights64, m_v, m_h2, k2))) return rc;
     // dv = A^T dO + 2^{G_L-G_s} w H  (public layout)
     DualParams v2{d.BH, d.H, d.TP, d.NT, d.T, 1, kPublic4D, kRows2D, 0, d.V, 128, 128, d.V, s.G,
                   1.f, 1, 2, g->dv, nullptr, 0.f, 0, nullptr, stride_or(g->dv_stride, d.H * d.V)};
-    if ((rc = dual(m_A, m_do, m_w, m_h2, v2))) return rc;
+    if ((rc = dual(m_A64, m_do64, m_w, m_h2_64, v2))) return rc;
   }
   // ================= readout adjoint
   {
@@ -374,15 +388,15 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     // dq^ = B' k^ + scale 2^{G_t} draw S^T ;  dG += q^ . dq^
     DualParams q1{d.BH, d.H, d.TP, d.NT, d.T, 0, kRows2D, kRows2D, 1, d.K, 128, d.K, 128, s.G,
                   a->scale, 0, 3, w.dq1, s.qn, 1.f, 1, w.dG};
-    if ((rc = dual(m_Bp, m_kn, m_draw, m_s1, q1))) return rc;
+    if ((rc = dual(m_Bp, m_kn64, m_draw, m_s1, q1))) return rc;
     // dk^ = B'^T q^ + 2^{G_L-G_s} w H^T ;  dG -= k^ . dk^
     DualParams k1{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kRows2D, 1, d.K, 128, d.K, 128, s.G,
                   1.f, 1, 3, w.dk1, s.kn, -1.f, 1, w.dG};
-    if ((rc = dual(m_Bp, m_qn, m_w, m_h1, k1))) return rc;
+    if ((rc = dual(m_Bp64, m_qn64, m_w, m_h1, k1))) return rc;
     // dw_b = A^T draw + 2^{G_L-G_s} k^ H  (the write-vector gradient is dw + dw_b)
     DualParams v1{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kRows2D, 0, 128, d.K, d.K, 128, s.G,
                   1.f, 1, 3, w.dw_b, nullptr, 0.f, 0, nullptr};
-    if ((rc = dual(m_A, m_draw, m_kn, m_h1, v1))) return rc;
+    if ((rc = dual(m_A64, m_draw64, m_kn, m_h1_64, v1))) return rc;
   }
   // ================= norms, write vector, gates, clock
   rc = token_bwd_launch(a->q, a->k, a->q_norm_weight, a->k_norm_weight, s.q_rs, s.k_rs, w.dq1,

@@ -200,46 +200,56 @@ struct DualParams {
   long long out_stride;  // out_mode 2: elements between consecutive tokens
 };
 
-constexpr int kDualSmem = 192 * 1024 + 1024 + 8 * 2048;  // operands + per-warp staging
+constexpr int kDualRing = 192 * 1024;                 // operand ring
+constexpr int kDualSmem = kDualRing + 8 * 2048 + 1024;  // + per-warp staging + alignment
+constexpr int kDualThreads = 320;
+constexpr int kDualMaxStages = 6;
 
-// Persistent: CTA c handles tiles c, c + gridDim.x, ...  Per tile the elected
-// thread waits for the operand tiles, issues both GEMMs into TMEM, and as soon
-// as their commit says shared memory has been read it issues the loads of the
-// CTA's next tile, which then stream in while the 8 warps drain TMEM (epilogue).
-// 8 warps: warp w reads TMEM lane quadrant (w & 3) (rows 32(w&3) .. +31) and
-// column half (w >> 2).  The epilogue's global loads (gate factors, row-dot
-// partner) are issued before waiting for the MMAs so that they overlap them.
-__device__ __forceinline__ void dual_issue_loads(uint8_t* smem, const CUtensorMap* x1,
-                                                 const CUtensorMap* y1, const CUtensorMap* x2,
-                                                 const CUtensorMap* y2, const DualParams& p,
-                                                 int tile, uint64_t* bar) {
-  const int kY1 = 32768, kX2 = 32768 + p.N * 256, kY2 = kX2 + p.KD * 256;
-  const int bh = tile / p.NT, j = tile % p.NT;
-  mbar_expect_tx(bar, 32768 + p.N * 256 + p.KD * 256 + p.hrows * p.hcols * 2);
-  load_hist_tile(smem, x1, tile * 128, 0, 128, 128, bar);
-  load_token_tile(smem + kY1, y1, p.y1_mode, bh, p.H, p.TP, j, 0, p.N, bar);
-  load_token_tile(smem + kX2, x2, p.x2_mode, bh, p.H, p.TP, j, 0, p.KD, bar);
-  load_hist_tile(smem + kY2, y2, tile * p.hrows, 0, p.hcols, p.hrows, bar);
-}
-
-__global__ void __launch_bounds__(256, 1)
+// Persistent, warp-specialised, streaming over the contraction dimension.
+// Every tile's two GEMMs are cut into 64-wide k-blocks (2 for X1 Y1, KD/64 for
+// X2 Y2); a k-block stage holds one 128x64 block of the left operand and the
+// matching 64xN block of the right operand (16 KiB + N*128 B), and a ring of
+// stages keeps the loads streaming across tile boundaries:
+//   warp 8, lane 0 (producer): TMA loads into the ring;
+//   warp 9, lane 0 (MMA issuer): the k-block UMMAs into the tile's TMEM buffer
+//     (acc1 = X1 Y1 | acc2 = X2 Y2, 2N columns; two buffers when N = 128), a
+//     commit per stage frees it, a commit per tile hands the buffer over;
+//   warps 0-7 (epilogue): warp w reads TMEM lane quadrant (w & 3) and column
+//     half (w >> 2), forms out = acc1 + r_t acc2 (+ the row dot folded into dG).
+// Operand boxes: X1 stored [t][s]; K-major X1 uses the 64-column panel of all
+// 128 rows, MN-major X1 (its transpose) 64 rows x 128 columns.  Y1 (token rows)
+// is read MN-major in 64-row blocks; Y2 (state history) K-major as a 64-column
+// panel of its N rows, or MN-major in 64-row blocks.  Maps given to the kernel
+// have the matching box heights (128, or 64 for the MN-major 64-row blocks).
+__global__ void __launch_bounds__(kDualThreads, 1)
     dual_gemm_kernel(const __grid_constant__ CUtensorMap map_x1,
                      const __grid_constant__ CUtensorMap map_y1,
                      const __grid_constant__ CUtensorMap map_x2,
                      const __grid_constant__ CUtensorMap map_y2, DualParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  const int kY1 = 32768, kX2 = 32768 + p.N * 256, kY2 = kX2 + p.KD * 256;
-  __shared__ __align__(8) uint64_t bar_in, bar_mma;
+  __shared__ __align__(8) uint64_t full[kDualMaxStages], empty[kDualMaxStages];
+  __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
-  __shared__ float dot_half[2][128];
+  __shared__ float dot_half[2][2][128];
+  __shared__ int s_abort;
+  volatile int* abort_flag = &s_abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quad = warp & 3, half = warp >> 2;
-  const int r = quad * 32 + lane;  // tile row = TMEM lane
   const int ntiles = p.BH * p.NT;
+  const int N = p.N, nkb = 2 + p.KD / 64;
+  const int stage_bytes = 16384 + N * 128;
+  const int nst = (kDualRing / stage_bytes) < kDualMaxStages ? kDualRing / stage_bytes : kDualMaxStages;
+  const int nbuf = 2 * N <= 256 ? 2 : 1;
   if (tid == 0) {
-    mbar_init(&bar_in, 1);
-    mbar_init(&bar_mma, 1);
+    for (int i = 0; i < nst; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);
+    }
+    s_abort = 0;
     mbar_fence_init();
   }
   if (warp == 0) tmem_alloc(&tmem_base, 512);
@@ -247,130 +257,183 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
-  const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
-  const uint32_t sX1 = smem_u32(smem), sY1 = smem_u32(smem + kY1), sX2 = smem_u32(smem + kX2),
-                 sY2 = smem_u32(smem + kY2);
-  const uint32_t id1 = make_idesc(128, p.N, p.x1_mn, 1);
-  const uint32_t id2 = make_idesc(128, p.N, 0, p.y2_kmaj ? 0 : 1);
-  const int ncol = p.N / 2, c_beg = half * ncol;  // 64 or 128 columns
-  const uint32_t scratch = smem_u32(smem) + 192 * 1024 + warp * 2048;
-  bool ok = true;
-  // elected-thread state: an operand load in flight (and its barrier parity), MMAs
-  // committed but not yet seen complete -- both are waited for before exit
-  bool in_pending = false, mma_pending = false;
-  uint32_t in_ph = 0;
-  if (tid == 0 && blockIdx.x < ntiles) {
-    dual_issue_loads(smem, &map_x1, &map_y1, &map_x2, &map_y2, p, blockIdx.x, &bar_in);
-    in_pending = true;
-    in_ph = 0;
-  }
-  uint32_t phase = 0;
-  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, phase ^= 1) {
-    const int bh = tile / p.NT, j = tile % p.NT;
-    const int t = j * 128 + r;
-    if (tid == 0) {
-      bool got = ok && mbar_wait(&bar_in, phase);
-      if (got) in_pending = false;
-      tc_fence_after();
-      if (got) {
-        for (int ks = 0; ks < 8; ++ks)
-          umma_bf16(tmem, p.x1_mn ? mnmaj_desc(sX1, 128, ks) : kmaj_desc(sX1, 128, ks),
-                    mnmaj_desc(sY1, 128, ks), id1, ks > 0);
-        for (int ks = 0; ks < p.KD / 16; ++ks)
-          umma_bf16(tmem + 256, kmaj_desc(sX2, 128, ks),
-                    p.y2_kmaj ? kmaj_desc(sY2, p.hrows, ks) : mnmaj_desc(sY2, p.hrows, ks), id2,
-                    ks > 0);
-        umma_commit(&bar_mma);
-        mma_pending = true;
-        // shared memory is free once the MMAs are done: prefetch the next tile
-        const int next = tile + gridDim.x;
-        if (next < ntiles) {
-          if (mbar_wait(&bar_mma, phase)) {
-            mma_pending = false;
-            dual_issue_loads(smem, &map_x1, &map_y1, &map_x2, &map_y2, p, next, &bar_in);
-            in_pending = true;
-            in_ph = phase ^ 1;
+
+  if (warp == 8) {
+    // ------------------------------------------------ producer
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < ntiles && !*abort_flag; tile += gridDim.x) {
+        const int bh = tile / p.NT, j = tile % p.NT;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % nst;
+          if (it >= nst && !mbar_wait(&empty[s], ((it / nst) - 1) & 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          uint8_t* xb = smem + s * stage_bytes;
+          uint8_t* yb = xb + 16384;
+          mbar_expect_tx(&full[s], stage_bytes);
+          if (kb < 2) {
+            if (p.x1_mn) {
+              tma_load_2d(xb, &map_x1, &full[s], 0, tile * 128 + 64 * kb);
+              tma_load_2d(xb + 8192, &map_x1, &full[s], 64, tile * 128 + 64 * kb);
+            } else {
+              tma_load_2d(xb, &map_x1, &full[s], 64 * kb, tile * 128);
+            }
+            for (int c = 0; c < N / 64; ++c) {
+              if (p.y1_mode == kRows2D)
+                tma_load_2d(yb + c * 8192, &map_y1, &full[s], 64 * c, bh * p.TP + j * 128 + 64 * kb);
+              else
+                tma_load_4d(yb + c * 8192, &map_y1, &full[s], 64 * c, bh % p.H, j * 128 + 64 * kb,
+                            bh / p.H);
+            }
           } else {
-            got = false;
+            const int k2 = kb - 2;
+            load_token_tile(xb, &map_x2, p.x2_mode, bh, p.H, p.TP, j, 64 * k2, 64, &full[s]);
+            if (p.y2_kmaj) {
+              tma_load_2d(yb, &map_y2, &full[s], 64 * k2, tile * p.hrows);
+            } else {
+              for (int c = 0; c < N / 64; ++c)
+                tma_load_2d(yb + c * 8192, &map_y2, &full[s], 64 * c, tile * p.hrows + 64 * k2);
+            }
           }
         }
-      } else {
-        mbar_arrive(&bar_mma);  // releases the epilogue's wait; its result is discarded
       }
-      if (!got) ok = false;
+      // every issued copy lands before shared memory goes away
+      for (int i = it > nst ? it - nst : 0; i < it; ++i) mbar_wait(&full[i % nst], (i / nst) & 1);
     }
-    // ---- epilogue prefetch (independent of the MMAs)
-    const float* Gt = p.G + size_t(bh) * p.TP + j * 128;
-    const float f = p.fkind == 0 ? p.scale * exp2f(Gt[r]) : exp2f(Gt[127] - Gt[r]);
-    const size_t row = size_t(bh) * p.TP + t;
-    uint4 dpre[16];
-    if (p.dot_src) {
-      const uint4* src = reinterpret_cast<const uint4*>(p.dot_src + row * p.N + c_beg);
+  } else if (warp == 9) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t id1 = make_idesc(128, N, p.x1_mn, 1);
+      const uint32_t id2 = make_idesc(128, N, 0, p.y2_kmaj ? 0 : 1);
+      int it = 0, tl = 0;
+      uint64_t* last_bar = nullptr;
+      uint32_t last_par = 0;
+      for (int tile = blockIdx.x; tile < ntiles && !*abort_flag; tile += gridDim.x, ++tl) {
+        const int b = tl % nbuf;
+        if (tl >= nbuf && !mbar_wait(&acc_empty[b], ((tl / nbuf) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc1 = tmem + b * 2 * N, acc2 = acc1 + N;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % nst;
+          if (!mbar_wait(&full[s], (it / nst) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t xb = smem_u32(smem + s * stage_bytes), yb = xb + 16384;
+          if (kb < 2) {
 #pragma unroll
-      for (int q = 0; q < 16; ++q)
-        if (q < ncol / 8) dpre[q] = src[q];
+            for (int ks = 0; ks < 4; ++ks)
+              umma_bf16(acc1, p.x1_mn ? mnmaj_desc(xb, 64, ks) : kmaj_desc(xb, 128, ks),
+                        mnmaj_desc(yb, 64, ks), id1, kb > 0 || ks > 0);
+          } else {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              umma_bf16(acc2, kmaj_desc(xb, 128, ks),
+                        p.y2_kmaj ? kmaj_desc(yb, N, ks) : mnmaj_desc(yb, 64, ks), id2,
+                        kb > 2 || ks > 0);
+          }
+          umma_commit(&empty[s]);
+          last_bar = &empty[s];
+          last_par = (it / nst) & 1;
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        umma_commit(&acc_full[b]);
+        last_bar = &acc_full[b];
+        last_par = (tl / nbuf) & 1;
+      }
+      if (last_bar) mbar_wait(last_bar, last_par);  // all issued MMAs are done
     }
-    __syncwarp();
-    bool mm = mbar_wait(&bar_mma, phase);
-    if (tid == 0 && mm) mma_pending = false;
-    tc_fence_after();
-    mm = __syncthreads_and(mm && ok) != 0;
-    if (mm) {
+  } else {
+    // ------------------------------------------------ epilogue
+    const int quad = warp & 3, half = warp >> 2;
+    const int r = quad * 32 + lane;  // tile row = TMEM lane
+    const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
+    const int ncol = N / 2, c_beg = half * ncol;  // 64 or 128 columns
+    const uint32_t scratch = smem_u32(smem) + kDualRing + warp * 2048;
+    int tl = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
+      const int bh = tile / p.NT, j = tile % p.NT, b = tl % nbuf;
+      const int t = j * 128 + r;
+      const float* Gt = p.G + size_t(bh) * p.TP + j * 128;
+      const float f = p.fkind == 0 ? p.scale * exp2f(Gt[r]) : exp2f(Gt[127] - Gt[r]);
+      const size_t row = size_t(bh) * p.TP + t;
+      uint4 dpre[16];
+      if (p.dot_src) {
+        const uint4* src = reinterpret_cast<const uint4*>(p.dot_src + row * N + c_beg);
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          if (q < ncol / 8) dpre[q] = src[q];
+      }
+      const bool got =
+          __all_sync(0xffffffffu, *abort_flag == 0 && mbar_wait(&acc_full[b], (tl / nbuf) & 1));
+      tc_fence_after();
       float dot = 0.f;
+      if (got) {
+        const uint32_t acc1 = lane_tmem + b * 2 * N, acc2 = acc1 + N;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (c >= ncol / 32) break;
-        const int col = c_beg + 32 * c;
-        float a[32], b[32];
-        tmem_ld32(lane_tmem + col, a);
-        tmem_ld32(lane_tmem + 256 + col, b);
+        for (int c = 0; c < 4; ++c) {
+          if (c >= ncol / 32) break;
+          const int col = c_beg + 32 * c;
+          float a[32], bb[32];
+          tmem_ld32x2(acc1 + col, a, acc2 + col, bb);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) a[i] += f * b[i];
-        if (p.dot_src) {
+          for (int i = 0; i < 32; ++i) a[i] += f * bb[i];
+          if (p.dot_src) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float x[8];
-            unpack_bf16x8(dpre[4 * c + q], x);
+            for (int q = 0; q < 4; ++q) {
+              float x[8];
+              unpack_bf16x8(dpre[4 * c + q], x);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) dot += x[e] * a[8 * q + e];
+              for (int e = 0; e < 8; ++e) dot += x[e] * a[8 * q + e];
+            }
+          }
+          if (p.out_mode == 2) {
+            const int b_ = bh / p.H, h = bh % p.H, t0 = j * 128 + quad * 32;
+            const int nvalid = p.T - t0;
+            const uint32_t valid =
+                nvalid >= 32 ? 0xffffffffu : (nvalid <= 0 ? 0u : (1u << nvalid) - 1u);
+            warp_store_block_bf16(scratch, a,
+                                  static_cast<__nv_bfloat16*>(p.out) +
+                                      (size_t(b_) * p.T + t0) * p.out_stride + size_t(h) * N + col,
+                                  p.out_stride, valid);
+          } else if (p.out_mode == 3) {
+            warp_store_block_bf16(scratch, a,
+                                  static_cast<__nv_bfloat16*>(p.out) +
+                                      (size_t(bh) * p.TP + j * 128 + quad * 32) * N + col,
+                                  N, 0xffffffffu);
+          } else {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * N + col);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              __stcs(dst + q, make_float4(a[4 * q], a[4 * q + 1], a[4 * q + 2], a[4 * q + 3]));
           }
         }
-        if (p.out_mode == 2) {
-          const int b_ = bh / p.H, h = bh % p.H, t0 = j * 128 + quad * 32;
-          const int nvalid = p.T - t0;
-          const uint32_t valid = nvalid >= 32 ? 0xffffffffu : (nvalid <= 0 ? 0u : (1u << nvalid) - 1u);
-          warp_store_block_bf16(scratch, a,
-                                static_cast<__nv_bfloat16*>(p.out) +
-                                    (size_t(b_) * p.T + t0) * p.out_stride + size_t(h) * p.N + col,
-                                p.out_stride, valid);
-        } else if (p.out_mode == 3) {
-          warp_store_block_bf16(scratch, a,
-                                static_cast<__nv_bfloat16*>(p.out) +
-                                    (size_t(bh) * p.TP + j * 128 + quad * 32) * p.N + col,
-                                p.N, 0xffffffffu);
-        } else {
-          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * p.N + col);
-#pragma unroll
-          for (int q = 0; q < 8; ++q)
-            __stcs(dst + q, make_float4(a[4 * q], a[4 * q + 1], a[4 * q + 2], a[4 * q + 3]));
-        }
       }
-      if (p.dot_src) dot_half[half][r] = dot;
+      // hand the TMEM buffer back to the MMA issuer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (p.dot_src) dot_half[tl & 1][half][r] = dot;
+      // join the two column halves of the row dot (and agree on stopping)
+      if (named_bar_or(1, 256, !got)) {
+        *abort_flag = 1;
+        break;
+      }
+      if (p.dot_src && half == 0) {
+        const float total = dot_half[tl & 1][0][r] + dot_half[tl & 1][1][r];
+        p.dG[row] = (p.dot_acc ? p.dG[row] : 0.f) + p.dot_sign * total;
+      }
     }
-    // TMEM drained and the row-dot halves visible before the next tile's MMAs
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (mm && p.dot_src && half == 0) {
-      const float total = dot_half[0][r] + dot_half[1][r];
-      p.dG[row] = (p.dot_acc ? p.dG[row] : 0.f) + p.dot_sign * total;
-    }
-    if (!mm) break;
-  }
-  // error paths: let committed MMAs and an unconsumed prefetch finish (bounded)
-  if (tid == 0) {
-    if (mma_pending) mbar_wait(&bar_mma, phase);
-    if (in_pending) mbar_wait(&bar_in, in_ph);
   }
   tc_fence_before();
   __syncthreads();

@@ -163,3 +163,39 @@ def test_chunk_backward_deterministic(ops):
         grads.append([x.grad.clone() for x in dev])
     for a, b in zip(*grads):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("K,V", [(256, 256), (256, 128), (128, 256)])
+def test_chunk_batched_matches_per_sequence(ops, K, V):
+    """(b, h) pairs are independent, so a batch of 8 sequences (512 tiles at
+    T = 2048, H = 4: several tiles per persistent CTA, ring and TMEM buffers
+    wrapping around) must give exactly the per-token outputs and gradients of
+    the same sequences run one at a time (64 tiles, one per CTA).  Parameter
+    gradients are sums over the batch, reduced in another order: 1e-5."""
+    B, T, H = 8, 2048, 4
+    ins, state = make_inputs(B, T, H, K, V, seed=K + V, with_state=True)
+    do = torch.randn(B, T, H, V, generator=seeded(9)).to(torch.bfloat16).cuda()
+
+    def run(sl):
+        dev = [x[sl].cuda().requires_grad_(True) if i < 6 else x.cuda().requires_grad_(True)
+               for i, x in enumerate(ins)]
+        st = tuple(x[sl].cuda().requires_grad_(True) for x in state)
+        o, fs = ops.chunk_cyfa(*dev, initial_state=st, output_final_state=True)
+        (o.float() * do[sl].float()).sum().backward()
+        return o.detach(), [x.grad for x in dev] + [x.grad for x in st]
+
+    o_all, g_all = run(slice(0, B))
+    per = [run(slice(b, b + 1)) for b in range(B)]
+    torch.cuda.synchronize()
+    assert torch.equal(o_all, torch.cat([p[0] for p in per]))
+    # per-token tensors: q k v g delta beta and the initial-state grads (batch dim 0)
+    for i in list(range(6)) + [9, 10, 11]:
+        want = torch.cat([p[1][i] for p in per])
+        assert torch.equal(g_all[i], want), i
+    # batch-reduced parameters: readout, q/k norm weights
+    for i in (6, 7, 8):
+        want = sum(p[1][i] for p in per)
+        assert rel_l2(g_all[i], want) <= 1e-5, i
+    from cyclic_flow_attention import _lib
+
+    assert _lib.device_error() == 0
