@@ -355,9 +355,13 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     const int per_head = readout_ctas_per_head(d);
     ReadoutBwdParams rp{d.BH, d.H, d.TP, d.NT, d.B, per_head, s.raw, w.dweights, s.lam, w.draw,
                         w.dlam_r, w.dtab_part};
+    CUtensorMap m_raw, m_dwt;
+    if ((rc = tmap_2d(&m_raw, s.raw, rows, 128, 128))) return rc;
+    if ((rc = tmap_2d(&m_dwt, w.dweights, rows, 128, 128))) return rc;
     set_smem(readout_bwd_kernel, kReadoutBwdSmem);
     CYFA_LAUNCH("readout_bwd", st,
-                (readout_bwd_kernel<<<d.H * per_head, 256, kReadoutBwdSmem, st>>>(m_tab, rp)));
+                (readout_bwd_kernel<<<d.H * per_head, 256, kReadoutBwdSmem, st>>>(m_tab, m_raw,
+                                                                                  m_dwt, rp)));
     if ((rc = launch_status())) return rc;
     CYFA_LAUNCH("dtable_reduce", st,
                 (dtable_reduce_kernel<<<dim3(d.H, 128), 128, 0, st>>>(w.dtab_part, g->dtable,

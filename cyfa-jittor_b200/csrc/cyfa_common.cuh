@@ -108,6 +108,29 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
       "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
 }
+// Coalesced warp load of a 32-row x 32-column bf16 block (the inverse of
+// warp_store_block_bf16, in two steps so that the global loads can be issued
+// early): warp_fetch_block_bf16 reads 8 rows x 64 contiguous bytes per
+// instruction into `raw` (lane l holds row 8k + l/4, 16-byte chunk l%4, k = 0..3);
+// warp_transpose_block_bf16 passes them through the warp's 2 KiB staging buffer
+// and returns row `lane` (32 values as 4 x 8 bf16).
+__device__ __forceinline__ void warp_fetch_block_bf16(const __nv_bfloat16* src, size_t stride,
+                                                      uint4 (&raw)[4]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    raw[k] = *reinterpret_cast<const uint4*>(src + (8 * k + (lane >> 2)) * stride + (lane & 3) * 8);
+}
+// Plain bulk copy of `bytes` contiguous bytes (16-byte aligned, a multiple of
+// 16) from global to shared memory; completion on an mbarrier.  No multicast.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
@@ -290,6 +313,21 @@ __device__ __forceinline__ void tmem_ld32x2(uint32_t ta, float (&a)[32], uint32_
     a[i] = __uint_as_float(ra[i]);
     b[i] = __uint_as_float(rb[i]);
   }
+}
+
+__device__ __forceinline__ void warp_transpose_block_bf16(uint32_t scratch, const uint4 (&raw)[4],
+                                                          uint4 (&row)[4]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = 8 * k + (lane >> 2), c = lane & 3;
+    st_shared_v4(scratch + r * 64 + ((c ^ ((r >> 1) & 3)) << 4), raw[k].x, raw[k].y, raw[k].z,
+                 raw[k].w);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int c = 0; c < 4; ++c) row[c] = ld_shared_v4(scratch + lane * 64 + ((c ^ ((lane >> 1) & 3)) << 4));
+  __syncwarp();
 }
 
 // 2^x on the special-function unit (relative error about 2^-22; results below

@@ -367,12 +367,13 @@ __global__ void __launch_bounds__(kDualThreads, 1)
       const float* Gt = p.G + size_t(bh) * p.TP + j * 128;
       const float f = p.fkind == 0 ? p.scale * exp2f(Gt[r]) : exp2f(Gt[127] - Gt[r]);
       const size_t row = size_t(bh) * p.TP + t;
-      uint4 dpre[16];
+      // the row-dot partner, fetched coalesced before the MMAs are waited for
+      uint4 dpre[4][4];
       if (p.dot_src) {
-        const uint4* src = reinterpret_cast<const uint4*>(p.dot_src + row * N + c_beg);
+        const __nv_bfloat16* src = p.dot_src + (size_t(bh) * p.TP + j * 128 + quad * 32) * N + c_beg;
 #pragma unroll
-        for (int q = 0; q < 16; ++q)
-          if (q < ncol / 8) dpre[q] = src[q];
+        for (int c = 0; c < 4; ++c)
+          if (c < ncol / 32) warp_fetch_block_bf16(src + 32 * c, N, dpre[c]);
       }
       const bool got =
           __all_sync(0xffffffffu, *abort_flag == 0 && mbar_wait(&acc_full[b], (tl / nbuf) & 1));
@@ -389,10 +390,12 @@ __global__ void __launch_bounds__(kDualThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) a[i] += f * bb[i];
           if (p.dot_src) {
+            uint4 drow[4];
+            warp_transpose_block_bf16(scratch, dpre[c], drow);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               float x[8];
-              unpack_bf16x8(dpre[4 * c + q], x);
+              unpack_bf16x8(drow[q], x);
 #pragma unroll
               for (int e = 0; e < 8; ++e) dot += x[e] * a[8 * q + e];
             }
@@ -455,7 +458,8 @@ struct ReadoutBwdParams {
   float* dtab_part;              // [H * per_head, 128, 128]
 };
 
-constexpr int kReadoutBwdSmem = 160 * 1024 + 1024;
+// table | z | dc | p | dl (32 KiB each) | raw | dw staging (32 KiB each)
+constexpr int kReadoutBwdSmem = 224 * 1024 + 1024;
 
 // Persistent over the tiles of one head: CTA (h, split) handles tiles
 // split, split + per_head, ... of head h and accumulates the table gradient in
@@ -467,11 +471,25 @@ constexpr int kReadoutBwdSmem = 160 * 1024 + 1024;
 //   dz = dl Tab, coeff = p Tab, dTab += p^T dc + dl^T z   (UMMA)
 //   draw = U(-lam) dz,  dlam = sum_p w_p [z x dz + dc x coeff]   (epilogue)
 // The rotation terms use the on-chip z, dc and coeff, so no input is read twice.
+// The raw and dweights tiles of the next tile are fetched by TMA into a staging
+// area while the current tile computes.
+__device__ __forceinline__ void readout_bwd_issue(uint8_t* smem, const CUtensorMap* mraw,
+                                                  const CUtensorMap* mdw, const ReadoutBwdParams& p,
+                                                  int h, int tile, uint64_t* bar) {
+  const int b = tile / p.NT, j = tile % p.NT, bh = b * p.H + h;
+  const int row0 = bh * p.TP + j * 128;
+  mbar_expect_tx(bar, 65536);
+  load_hist_tile(smem + 163840, mraw, row0, 0, 128, 128, bar);
+  load_hist_tile(smem + 196608, mdw, row0, 0, 128, 128, bar);
+}
+
 __global__ void __launch_bounds__(256, 1)
-    readout_bwd_kernel(const __grid_constant__ CUtensorMap map_tab, ReadoutBwdParams p) {
+    readout_bwd_kernel(const __grid_constant__ CUtensorMap map_tab,
+                       const __grid_constant__ CUtensorMap map_raw,
+                       const __grid_constant__ CUtensorMap map_dw, ReadoutBwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  __shared__ __align__(8) uint64_t bar_tab, bar_m1, bar_m2;
+  __shared__ __align__(8) uint64_t bar_tab, bar_m1, bar_m2, bar_ld;
   __shared__ uint32_t tmem_base;
   __shared__ float xch[2][128];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -483,6 +501,7 @@ __global__ void __launch_bounds__(256, 1)
     mbar_init(&bar_tab, 1);
     mbar_init(&bar_m1, 1);
     mbar_init(&bar_m2, 1);
+    mbar_init(&bar_ld, 1);
     mbar_fence_init();
   }
   if (warp == 0) tmem_alloc(&tmem_base, 512);
@@ -493,25 +512,37 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
   const uint32_t sTab = smem_u32(smem), sZ = sTab + 32768, sDC = sTab + 65536,
                  sP = sTab + 98304, sDL = sTab + 131072;
+  const uint32_t sRaw = sTab + 163840, sDw = sTab + 196608;
+  bool ld_pending = false;  // elected thread: a staging load in flight
   if (tid == 0) {
     mbar_expect_tx(&bar_tab, 32768);
     load_hist_tile(smem, &map_tab, h * 128, 0, 128, 128, &bar_tab);
+    if (split < ntiles) {
+      readout_bwd_issue(smem, &map_raw, &map_dw, p, h, split, &bar_ld);
+      ld_pending = true;
+    }
   }
   bool ok = true;
   int it = 0;
+  auto lam_of = [&](int tl) {
+    const int bh_ = (tl / p.NT) * p.H + h;
+    return p.lam[size_t(bh_) * p.TP + (tl % p.NT) * 128 + r];
+  };
+  float lam_next = split < ntiles ? lam_of(split) : 0.f;
   for (int tile = split; tile < ntiles; tile += p.per_head, ++it) {
     const int b = tile / p.NT, j = tile % p.NT, bh = b * p.H + h;
     const size_t row = size_t(bh) * p.TP + j * 128 + r;
-    const float lam = p.lam[row];
+    const float lam = lam_next;
+    if (tile + p.per_head < ntiles) lam_next = lam_of(tile + p.per_head);
+    if (!mbar_wait(&bar_ld, it & 1)) ok = false;
+    if (tid == 0) ld_pending = false;
     // ---- z = U(lam) raw and dc = U(lam) dw for this thread's 64 columns
     {
       float z[64], dc[64];
-      const uint4* rsrc = reinterpret_cast<const uint4*>(p.raw + row * 128 + half * 64);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) unpack_bf16x8(rsrc[q], z + 8 * q);
-      const uint4* dsrc = reinterpret_cast<const uint4*>(p.dweights + row * 128 + half * 64);
+      for (int q = 0; q < 8; ++q) unpack_bf16x8(ld_shared_v4(sRaw + half * 16384 + sw128(r, q)), z + 8 * q);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) unpack_bf16x8(dsrc[q], dc + 8 * q);
+      for (int q = 0; q < 8; ++q) unpack_bf16x8(ld_shared_v4(sDw + half * 16384 + sw128(r, q)), dc + 8 * q);
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
         float sn, cs;
@@ -531,6 +562,11 @@ __global__ void __launch_bounds__(256, 1)
     ok = __syncthreads_and(ok);
     tc_fence_after();
     if (!ok) break;
+    // the staging area is free: fetch the next tile's inputs
+    if (tid == 0 && tile + p.per_head < ntiles) {
+      readout_bwd_issue(smem, &map_raw, &map_dw, p, h, tile + p.per_head, &bar_ld);
+      ld_pending = true;
+    }
     if (tid == 0) {
       if (it > 0 || mbar_wait(&bar_tab, 0)) {
         tc_fence_after();
@@ -653,6 +689,7 @@ __global__ void __launch_bounds__(256, 1)
     tc_fence_after();
     if (!ok) break;
   }
+  if (tid == 0 && ld_pending) mbar_wait(&bar_ld, it & 1);  // error path: let it land
   // this CTA's partial table gradient: thread (quad, half) owns slot row r, 64 columns
   if (ok && it > 0) {
     float* dst = p.dtab_part + size_t(blockIdx.x) * 16384 + r * 128 + half * 64;
