@@ -330,6 +330,46 @@ __device__ __forceinline__ void warp_transpose_block_bf16(uint32_t scratch, cons
   __syncwarp();
 }
 
+// The same for 32-row x 64-column bf16 blocks (128 bytes per row), staging
+// buffer 4 KiB: lane l holds row l as 8 x 16-byte chunks; each global access
+// instruction covers 4 rows x 128 contiguous bytes (lane l: row 4k + l/8, chunk l%8).
+__device__ __forceinline__ void warp_store_rows128(uint32_t scratch, const uint4 (&row)[8],
+                                                   __nv_bfloat16* dst, size_t stride) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    st_shared_v4(scratch + lane * 128 + ((c ^ (lane & 7)) << 4), row[c].x, row[c].y, row[c].z,
+                 row[c].w);
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int r = 4 * k + (lane >> 3), c = lane & 7;
+    *reinterpret_cast<uint4*>(dst + r * stride + c * 8) =
+        ld_shared_v4(scratch + r * 128 + ((c ^ (r & 7)) << 4));
+  }
+  __syncwarp();
+}
+__device__ __forceinline__ void warp_fetch_rows128(const __nv_bfloat16* src, size_t stride,
+                                                   uint4 (&raw)[8]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    raw[k] = *reinterpret_cast<const uint4*>(src + (4 * k + (lane >> 3)) * stride + (lane & 7) * 8);
+}
+__device__ __forceinline__ void warp_transpose_rows128(uint32_t scratch, const uint4 (&raw)[8],
+                                                       uint4 (&row)[8]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int r = 4 * k + (lane >> 3), c = lane & 7;
+    st_shared_v4(scratch + r * 128 + ((c ^ (r & 7)) << 4), raw[k].x, raw[k].y, raw[k].z, raw[k].w);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int c = 0; c < 8; ++c) row[c] = ld_shared_v4(scratch + lane * 128 + ((c ^ (lane & 7)) << 4));
+  __syncwarp();
+}
+
 // 2^x on the special-function unit (relative error about 2^-22; results below
 // 2^-126 flush to zero).  Used for decay factors 2^{G_t - G_s} <= 1.
 __device__ __forceinline__ float fast_exp2(float x) {

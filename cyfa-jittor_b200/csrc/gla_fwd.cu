@@ -80,7 +80,8 @@ struct ScanParams {
 
 constexpr int kScanStages = 4;
 constexpr int kScanStageBytes = 48 * 1024;  // K tile 32 KiB + V tile 16 KiB
-constexpr int kScanSmem = kScanStages * kScanStageBytes + 1024;
+// ring + 4 KiB staging per consumer warp (coalesced history traffic) + alignment
+constexpr int kScanSmem = kScanStages * kScanStageBytes + 4 * 4096 + 1024;
 constexpr int kScanBufs = 4;                // TMEM update buffers of 64 columns
 
 // OR of v over the `n` threads of named barrier `id` (every one of them gets it).
@@ -257,6 +258,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       for (int i = 0; i < 64; ++i) S[i] = 0.f;
     }
     const uint32_t lane_tmem = tmem + ((warp * 32) << 16);
+    const uint32_t scratch = smem_u32(smem) + kScanStages * kScanStageBytes + warp * 4096;
     const int nsub = gridDim.y * gridDim.z, sub = blockIdx.y * gridDim.z + blockIdx.z;
     bool ok = true;
     // loads one iteration ahead: the gate total of the next tile and (REVERSE)
@@ -269,13 +271,15 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       if (idx + 1 < NT) gl_next = Gbh[size_t(tile_of(idx + 1)) * 128 + 127];
       // state entering tile j (forward) / adjoint leaving tile j (reverse)
       {
-        uint4* dst = reinterpret_cast<uint4*>(p.hist + ((size_t(bh) * NT + j) * p.DK + dk0 + tid) *
-                                                           p.DV + dv0);
+        uint4 packed[8];
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          dst[c] = make_uint4(pack_bf16(S[8 * c], S[8 * c + 1]), pack_bf16(S[8 * c + 2], S[8 * c + 3]),
-                              pack_bf16(S[8 * c + 4], S[8 * c + 5]),
-                              pack_bf16(S[8 * c + 6], S[8 * c + 7]));
+          packed[c] = make_uint4(pack_bf16(S[8 * c], S[8 * c + 1]), pack_bf16(S[8 * c + 2], S[8 * c + 3]),
+                                 pack_bf16(S[8 * c + 4], S[8 * c + 5]),
+                                 pack_bf16(S[8 * c + 6], S[8 * c + 7]));
+        warp_store_rows128(scratch, packed,
+                           p.hist + ((size_t(bh) * NT + j) * p.DK + dk0 + warp * 32) * p.DV + dv0,
+                           p.DV);
       }
       if constexpr (REVERSE) {
         // <S_{j+1}, H_{j+1}> over this CTA's slice (S_{j+1} from the forward pass)
