@@ -364,7 +364,9 @@ struct TileFwdParams {
 
 template <int DK>
 constexpr int tile_fwd_smem() {
-  return 3 * DK * 256 + 32768 + 1024;
+  // Q | K | S | V, plus (DK = 128) a 16 KiB staging area for the output stores;
+  // with DK = 256 the staging uses the S region, free once the MMAs are done
+  return 3 * DK * 256 + 32768 + 1024 + (DK == 256 ? 0 : 16384);
 }
 
 // 8 warps: warp w owns TMEM lane quadrant (w & 3) (token rows 32(w&3)..+31) and
@@ -485,22 +487,29 @@ __global__ void __launch_bounds__(256, 1)
   if (!mbar_wait(&bar_m[2], 0)) ok = false;
   tc_fence_after();
   const float eg = exp2f(gt);
-  if (ok) {
+  // per-warp staging for coalesced output stores (8 rows x 64 bytes per
+  // instruction): the S region, free once the MMAs above are done, when DK = 256
+  // (with DK = 128 the READOUT z tile lives there, so a separate area is used)
+  const uint32_t scratch = (DK == 256 ? sS : sV + 32768) + warp * 2048;
+  const int t0 = j * 128 + quad * 32;  // first token row of this warp
+  if (__all_sync(0xffffffffu, ok)) {
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
       const int col0 = half * 64 + 32 * c;
       float a[32], b[32];
-      tmem_ld32(lane_tmem + 128 + col0, a);
-      tmem_ld32(lane_tmem + 256 + col0, b);
+      tmem_ld32x2(lane_tmem + 128 + col0, a, lane_tmem + 256 + col0, b);
 #pragma unroll
       for (int i = 0; i < 32; ++i) a[i] = p.scale * (eg * a[i] + b[i]);
       if (p.o_mode == 1) {
-        if (t < p.T) {
-          const int b_ = bh / p.H, h = bh % p.H;
-          store_bf16x32_global(p.out + ((size_t(b_) * p.T + t) * p.H + h) * p.DV + dv0 + col0, a);
-        }
+        const int b_ = bh / p.H, h = bh % p.H;
+        const int nvalid = p.T - t0;
+        const uint32_t valid = nvalid >= 32 ? 0xffffffffu : (nvalid <= 0 ? 0u : (1u << nvalid) - 1u);
+        warp_store_block_bf16(scratch, a,
+                              p.out + ((size_t(b_) * p.T + t0) * p.H + h) * p.DV + dv0 + col0,
+                              size_t(p.H) * p.DV, valid);
       } else {
-        store_bf16x32_global(p.out + (size_t(bh) * p.TP + t) * 128 + col0, a);
+        warp_store_block_bf16(scratch, a, p.out + (size_t(bh) * p.TP + t0) * 128 + col0, 128,
+                              0xffffffffu);
       }
       if (READOUT) {
         // z = U(lam) raw, from the bf16-rounded raw that is saved for the backward pass
@@ -579,7 +588,7 @@ __global__ void __launch_bounds__(256, 1)
     __syncwarp();
     if (!mbar_wait(&bar_m[4], 0)) ok = false;
     tc_fence_after();
-    if (ok) {
+    if (__all_sync(0xffffffffu, ok)) {
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         const int col0 = half * 64 + 32 * c;
@@ -593,7 +602,8 @@ __global__ void __launch_bounds__(256, 1)
           v[i] = cs * e + sn * o;
           v[i + 1] = -sn * e + cs * o;
         }
-        store_bf16x32_global(p.weights + (size_t(bh) * p.TP + t) * 128 + col0, v);
+        warp_store_block_bf16(scratch, v, p.weights + (size_t(bh) * p.TP + t0) * 128 + col0, 128,
+                              0xffffffffu);
       }
     }
   }
