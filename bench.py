@@ -60,6 +60,28 @@ def _tile_flops(K=256, V=256, C=128, M=128):
     return out
 
 
+def _tile_bytes(K=256, V=256, C=128, M=128):
+    """Algorithmic HBM bytes per 128-token tile of one (batch, head), summed over
+    all launches of each kernel in one layer step (bf16 operands, each tensor
+    read or written once per launch as the kernel's interface requires)."""
+    b = 2
+    out = {}
+
+    def dual(N, KD, dot):
+        # X1 (scores) + Y1 (token rows) + X2 (token rows) + Y2 (state history) + out (+ dot partner)
+        return b * (C * C + C * N + C * KD + KD * N + C * N + (C * N if dot else 0))
+
+    out["dual_gemm"] = (dual(M, V, True) + dual(M, V, True) + dual(V, M, False)
+                        + dual(K, M, True) + dual(K, M, True) + dual(M, K, False))
+    out["tile_scores"] = sum(b * (2 * C * dk + 2 * C * dv + 2 * C * C) for dk, dv in ((K, M), (M, V)))
+    out["state_scan_fwd"] = sum(b * (C * dk + C * dv + dk * dv) for dk, dv in ((K, M), (M, V)))
+    out["state_scan_bwd"] = sum(b * (C * dk + C * dv + 2 * dk * dv) for dk, dv in ((K, M), (M, V)))
+    out["tile_fwd_readout"] = b * (2 * C * K + K * M + C * M + 2 * C * M) + 8 * C
+    out["tile_fwd"] = b * (2 * C * M + M * V + 2 * C * V)
+    out["readout_bwd"] = b * 3 * C * M + 8 * C
+    return out
+
+
 def _peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -408,19 +430,32 @@ def run_cyfa(args, rank, world, local_rank):
     _lib.profile_enable(False)
     tiles = B * CFG["heads"] * math.ceil(T / 128)
     flops = _tile_flops(CFG["head_dim"], CFG["head_dim"])
+    tbytes = _tile_bytes(CFG["head_dim"], CFG["head_dim"])
     roofline = None
     if prof:
         dom = max(prof.items(), key=lambda kv: kv[1][0])
         name, (ms, n) = dom
-        peak = peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"])
-        work = flops.get(name, 0) * tiles  # all launches of this kernel in one step
-        achieved = work / (ms / 1000.0) / 1e12 if ms > 0 else 0.0
         traffic = _traffic_from_profiles(name)
-        roofline = {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": peak,
-                    "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                    "peak_kind": f"{peak_kind} bf16 sustained",
-                    "launches_per_step": n, "ms_per_step": ms,
-                    "kernel_ms": {k: round(v[0], 4) for k, v in sorted(prof.items())}}
+        # the tile kernels move ~64-100 B per FLOP-pair: below the ridge
+        # (peak FLOP/s / peak B/s), so they are bounded by HBM bandwidth
+        if name in tbytes:
+            peak = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+            work = tbytes[name] * tiles  # all launches of this kernel in one step
+            achieved = work / (ms / 1000.0) / 1e9 if ms > 0 else 0.0
+            roofline = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": peak,
+                        "unit": "GB/s", "frac": achieved / peak,
+                        "traffic": traffic, "algorithmic_bytes_per_launch": work / n,
+                        "tflops": flops.get(name, 0) * tiles / (ms / 1000.0) / 1e12,
+                        "peak_kind": f"{peak_kind} HBM copy"}
+        else:
+            peak = peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"])
+            work = flops.get(name, 0) * tiles
+            achieved = work / (ms / 1000.0) / 1e12 if ms > 0 else 0.0
+            roofline = {"bound": "tensor", "kernel": name, "achieved": achieved, "peak": peak,
+                        "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                        "peak_kind": f"{peak_kind} bf16 sustained"}
+        roofline.update({"launches_per_step": n, "ms_per_step": ms,
+                         "kernel_ms": {k: round(v[0], 4) for k, v in sorted(prof.items())}})
 
     decode = None if args.no_decode else measure_decode(args, rank, world, dev, peaks, barrier)
 
