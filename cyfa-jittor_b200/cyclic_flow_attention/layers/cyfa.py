@@ -19,9 +19,9 @@ from ..ops import chunk_cyfa, fused_recurrent_cyfa
 from ..ops.chunk import readout_table
 from ..ops.layer_ops import (
     ChunkCyfaPackedFunction,
-    GateActFunction,
     GatedNormFunction,
-    ShortConvFunction,
+    LayerFrontFunction,
+    PackedGradSlot,
 )
 
 
@@ -155,32 +155,31 @@ class CyclicFlowAttention(nn.Module):
         )
 
     def _forward_fused(self, x, use_cache):
-        """One packed q|k|v GEMM, one short-conv kernel over all 3 projections,
-        one auxiliary GEMM for the output gate and the a/b gates, and the CyFA op
-        on the packed buffer; the same math as the reference execute()."""
+        """One packed q|k|v|g0|a|b|d projection with the short convolution and the
+        gate activations on its columns (LayerFrontFunction), the CyFA op on the
+        convolved q|k|v, the gated output norm with the gate's second linear, and
+        o_proj; the same math as the reference execute()."""
         B, T, _ = x.shape
         H, K, V = self.num_heads, self.head_k_dim, self.head_v_dim
-        w_qkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight])
-        qkv = F.linear(x, w_qkv)
         g0 = self.g_proj[0]
-        w_aux = torch.cat([g0.weight, self.a_proj.weight, self.b_proj.weight])
-        aux = F.linear(x, w_aux)
-        dlin = F.linear(x.detach(), self.d_proj.weight)
-        conv_w = torch.cat([self.q_conv1d.weight, self.k_conv1d.weight, self.v_conv1d.weight])
-        qkv = ShortConvFunction.apply(qkv, conv_w, None)
-        g, delta, beta = GateActFunction.apply(aux, dlin, self.A_log, self.dt_bias,
-                                               self.b_proj.bias, self.d_proj.bias, V, V + H, H)
+        slot = PackedGradSlot()
+        qkv, gate_in, g, delta, beta = LayerFrontFunction.apply(
+            x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, g0.weight,
+            self.a_proj.weight, self.b_proj.weight, self.d_proj.weight, self.q_conv1d.weight,
+            self.k_conv1d.weight, self.v_conv1d.weight, self.A_log, self.dt_bias,
+            self.b_proj.bias, self.d_proj.bias, H, slot)
         table = readout_table(self.readout)
         o, hk, hv, clock = ChunkCyfaPackedFunction.apply(
             qkv, H, K, V, g, delta, beta, table, self.q_norm.weight.float(),
             self.k_norm.weight.float(), float(self.q_norm.eps), float(self.k_norm.eps), K ** -0.5)
         g1 = self.g_proj[1]
-        y = GatedNormFunction.apply(o, aux[..., :V], g1.weight, g1.bias, self.o_norm.weight,
-                                    self.o_norm.eps, float(self.num_slots - 1))
+        y = GatedNormFunction.apply(o, gate_in, g1.weight, g1.bias, self.o_norm.weight,
+                                    self.o_norm.eps, float(self.num_slots - 1), slot)
         y = self.o_proj(y)
         new_cache = None
         if use_cache:
             W = self.q_conv1d.width
+            w_qkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight])
             # conv histories: the last W-1 projected (pre-conv) rows of q, k and v
             pre = F.linear(x[:, -(W - 1):], w_qkv) if W > 1 else x[:, :0]
             cq, ck, cv = (pre[..., :H * K], pre[..., H * K:2 * H * K], pre[..., 2 * H * K:]) \

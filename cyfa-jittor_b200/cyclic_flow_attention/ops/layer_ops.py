@@ -116,7 +116,7 @@ class GatedNormFunction(torch.autograd.Function):
     bias; the kernels add b and return its gradient (fixed-order sums)."""
 
     @staticmethod
-    def forward(ctx, x, gate_in, gate_w, gate_b, weight, eps, scale):
+    def forward(ctx, x, gate_in, gate_w, gate_b, weight, eps, scale, slot=None):
         B, T, H, D = x.shape
         rows = B * T * H
         x = x.to(torch.bfloat16).contiguous()
@@ -134,6 +134,7 @@ class GatedNormFunction(torch.autograd.Function):
                       _p(y), _p(rstd), rows, D, _lib.stream())
         ctx.save_for_backward(x, gate, gate_in, gate_w, w, rstd, b)
         ctx.meta = (scale, weight.dtype, None if gate_b is None else gate_b.dtype)
+        ctx.slot = slot
         return y
 
     @staticmethod
@@ -163,9 +164,161 @@ class GatedNormFunction(torch.autograd.Function):
                       _lib.stream())
         dg2 = dgate.reshape(-1, H * D)
         gin2 = gate_in.reshape(-1, gate_in.shape[-1])
-        d_gate_in = (dg2 @ gate_w).reshape(gate_in.shape)
         d_gate_w = dg2.t() @ gin2
-        return dx, d_gate_in, d_gate_w, d_gate_b, dw.to(wdt), None, None
+        slot = ctx.slot
+        if slot is not None:
+            # the producer of gate_in collects its gradient in a packed buffer:
+            # write this part there directly and pass no separate gradient
+            view = slot.claim(gate_in.device)
+            torch.matmul(dg2, gate_w, out=view.reshape(-1, view.shape[-1]))
+            d_gate_in = None
+        else:
+            d_gate_in = (dg2 @ gate_w).reshape(gate_in.shape)
+        return dx, d_gate_in, d_gate_w, d_gate_b, dw.to(wdt), None, None, None
+
+
+class PackedGradSlot:
+    """Hand-over of a packed gradient buffer between two autograd Functions.
+
+    LayerFrontFunction returns the output-gate input as a column view of its
+    packed projection; its consumer (GatedNormFunction, whose backward runs
+    first) writes that gradient straight into the matching columns of a packed
+    gradient buffer of the projection's layout instead of returning a separate
+    tensor, and LayerFrontFunction's backward picks the buffer up.  This saves a
+    strided copy of the gradient per step.  Without a consumer backward the buffer
+    is allocated (and those columns zeroed) by LayerFrontFunction itself."""
+
+    def __init__(self):
+        self.shape = None  # (B, T, NB), column range of the gate input
+        self.cols = None
+        self.buf = None
+
+    def claim(self, device):
+        if self.buf is None:
+            self.buf = torch.empty(self.shape, device=device, dtype=torch.bfloat16)
+        c0, c1 = self.cols
+        return self.buf[..., c0:c1]
+
+    def take(self):
+        buf, self.buf = self.buf, None
+        return buf
+
+
+class LayerFrontFunction(torch.autograd.Function):
+    """The layer's input side as one op: a single projection of x onto
+    [W_q; W_k; W_v; W_g0; W_a; W_b; W_d] (one GEMM, one read of x), the short
+    convolution of the q|k|v columns, and the gate activations of the a, b, d
+    columns.  Returns the convolved q|k|v [B,T,3C], the output-gate input
+    (a column view of the projection) and g, delta, beta [B,T,H].
+
+    Backward: every consumer's gradient lands in one packed buffer of the
+    projection's layout (the conv and gate kernels write their columns with
+    strides), so dx is one GEMM over the packed gradient and the weight gradients
+    one more; d is projected from x.detach() in the reference
+    (layers/cyfa.py:323-326), so its columns enter the weight gradient but not dx.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w_q, w_k, w_v, w_g0, w_a, w_b, w_d, cw_q, cw_k, cw_v, A_log, dt_bias,
+                b_bias, d_bias, H, slot=None):
+        B, T, hid = x.shape
+        rows = B * T
+        dev = x.device
+        n_qkv = w_q.shape[0] + w_k.shape[0] + w_v.shape[0]
+        c_g, n_g = n_qkv, w_g0.shape[0]
+        c_a = c_g + n_g
+        c_b, c_d = c_a + H, c_a + 2 * H
+        n_used = c_d + H
+        NB = (n_used + 7) // 8 * 8  # 16-byte rows
+        parts = [w_q, w_k, w_v, w_g0, w_a, w_b, w_d]
+        if NB > n_used:
+            parts.append(torch.zeros(NB - n_used, hid, device=dev, dtype=w_q.dtype))
+        W_big = torch.cat(parts)
+        big = torch.nn.functional.linear(x, W_big)  # [B, T, NB]
+        Wc = cw_q.shape[-1]
+        cw = torch.cat([cw_q, cw_k, cw_v]).detach().float().reshape(n_qkv, Wc).contiguous()
+        qkv = torch.empty(B, T, n_qkv, device=dev, dtype=torch.bfloat16)
+        _lib.call("cyfa_short_conv_fwd", _p(big), _c.c_longlong(NB), None, _p(cw), None, _p(qkv),
+                  B, T, n_qkv, Wc, _lib.stream())
+        A = A_log.detach().float().contiguous()
+        dt = dt_bias.detach().float().contiguous()
+        bb = b_bias.detach().float().contiguous()
+        db = d_bias.detach().float().contiguous()
+        g = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+        delta = torch.empty_like(g)
+        beta = torch.empty_like(g)
+        base, st = big.data_ptr(), _c.c_longlong(NB)
+        _lib.call("cyfa_gate_act_fwd", _c.c_void_p(base + 2 * c_a), st, _c.c_void_p(base + 2 * c_b),
+                  st, _c.c_void_p(base + 2 * c_d), st, _p(A), _p(dt), _p(bb), _p(db), _p(g),
+                  _p(delta), _p(beta), rows, H, _lib.stream())
+        gate_in = big[..., c_g:c_g + n_g]
+        if slot is not None:
+            slot.shape, slot.cols, slot.buf = (B, T, NB), (c_g, c_g + n_g), None
+        ctx.slot = slot
+        ctx.save_for_backward(x, W_big, big, cw, A, dt, bb, db)
+        ctx.meta = (H, NB, n_qkv, c_g, n_g, c_a, c_b, c_d, n_used, Wc,
+                    [w.shape[0] for w in parts[:7]], cw_q.dtype,
+                    (A_log.dtype, dt_bias.dtype, b_bias.dtype, d_bias.dtype))
+        return qkv, gate_in, g, delta, beta
+
+    @staticmethod
+    def backward(ctx, dqkv, dgate_in, dg, ddelta, dbeta):
+        x, W_big, big, cw, A, dt, bb, db_ = ctx.saved_tensors
+        (H, NB, n_qkv, c_g, n_g, c_a, c_b, c_d, n_used, Wc, sizes, cdt, gdts) = ctx.meta
+        B, T, hid = x.shape
+        rows = B * T
+        dev = x.device
+        # the packed gradient: possibly already holding the gate-input columns
+        dbig = ctx.slot.take() if ctx.slot is not None else None
+        gate_done = dbig is not None
+        if dbig is None:
+            dbig = torch.empty(B, T, NB, device=dev, dtype=torch.bfloat16)
+        base, dbase, st = big.data_ptr(), dbig.data_ptr(), _c.c_longlong(NB)
+        # short conv adjoint -> columns [0, n_qkv) of the packed gradient
+        dcw = torch.empty(n_qkv, Wc, device=dev, dtype=torch.float32)
+        if dqkv is None:
+            dbig[..., :n_qkv].zero_()
+            dcw.zero_()
+        else:
+            dqkv = dqkv.to(torch.bfloat16).contiguous()
+            nbytes = _lib.lib().cyfa_short_conv_work_bytes(B, T, n_qkv, Wc)
+            work = _work(nbytes, dev)
+            _lib.call("cyfa_short_conv_bwd", _p(big), st, _p(cw), _p(dqkv), _p(dbig), st, _p(dcw),
+                      None, B, T, n_qkv, Wc, _p(work), _c.c_size_t(nbytes), _lib.stream())
+        # gate activation adjoints -> the a, b, d columns
+        zeros = lambda: torch.zeros(B, T, H, device=dev, dtype=torch.float32)
+        dg = zeros() if dg is None else dg.float().contiguous()
+        ddelta = zeros() if ddelta is None else ddelta.float().contiguous()
+        dbeta = zeros() if dbeta is None else dbeta.float().contiguous()
+        dA = torch.empty(H, device=dev, dtype=torch.float32)
+        ddtb = torch.empty(H, device=dev, dtype=torch.float32)
+        dbb = torch.empty(H, device=dev, dtype=torch.float32)
+        ddb = torch.empty(H, device=dev, dtype=torch.float32)
+        nbytes = _lib.lib().cyfa_gate_act_work_bytes(rows, H)
+        work = _work(nbytes, dev)
+        _lib.call("cyfa_gate_act_bwd", _c.c_void_p(base + 2 * c_a), st, _c.c_void_p(base + 2 * c_b),
+                  st, _c.c_void_p(base + 2 * c_d), st, _p(A), _p(dt), _p(bb), _p(db_), _p(dg),
+                  _p(ddelta), _p(dbeta), _c.c_void_p(dbase + 2 * c_a), st,
+                  _c.c_void_p(dbase + 2 * c_b), st, _c.c_void_p(dbase + 2 * c_d), st, _p(dA),
+                  _p(ddtb), _p(dbb), _p(ddb), rows, H, _p(work), _c.c_size_t(nbytes),
+                  _lib.stream())
+        # output-gate input gradient -> its columns (unless its consumer wrote them)
+        if dgate_in is not None:
+            if gate_done:
+                dbig[..., c_g:c_g + n_g].add_(dgate_in)
+            else:
+                dbig[..., c_g:c_g + n_g].copy_(dgate_in)
+        elif not gate_done:
+            dbig[..., c_g:c_g + n_g].zero_()
+        d2 = dbig.view(rows, NB)
+        x2 = x.reshape(rows, hid)
+        # dx from every column except d (projected from x.detach()) and the padding
+        dx = torch.matmul(d2[:, :c_d], W_big[:c_d]).view(B, T, hid)
+        dW = torch.matmul(d2[:, :n_used].t(), x2)
+        grads_w = list(torch.split(dW, sizes))
+        dcw_parts = torch.split(dcw.to(cdt).reshape(n_qkv, 1, Wc), sizes[:3])
+        return (dx, *grads_w, *dcw_parts, dA.to(gdts[0]), ddtb.to(gdts[1]), dbb.to(gdts[2]),
+                ddb.to(gdts[3]), None, None)
 
 
 class ChunkCyfaPackedFunction(torch.autograd.Function):
