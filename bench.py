@@ -319,13 +319,21 @@ def run_cyfa(args, rank, world, local_rank):
     gen = torch.Generator().manual_seed(1000 + rank)
     x_host = torch.randn(B, T, hid, generator=gen).to(torch.bfloat16).pin_memory()
     dy_host = torch.randn(B, T, hid, generator=gen).to(torch.bfloat16).pin_memory()
-    x = x_host.to(dev)
+    # the layer's input requires grad, as for any layer inside a network: the
+    # backward includes dx (the reference's FLOP count is fwd + dgrad + wgrad)
+    x = x_host.to(dev).requires_grad_(True)
     dy = dy_host.to(dev)
     flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
     peaks, peak_kind = _peaks()
 
     # gradient averaging over ranks, bucketed and overlapped with the backward
-    buckets = GradientBuckets(params) if world > 1 else None
+    buckets = None
+    if world > 1:
+        # one fp32 bucket for the whole layer, completed by the input-side weight
+        # gradients, which the fused backward hands over before its dx GEMM: the
+        # all-reduce overlaps that GEMM instead of the persistent core kernels
+        buckets = GradientBuckets(params, groups=[sum(layer.grad_groups(), [])])
+        layer.grad_ready = buckets.early
 
     def allreduce_grads():
         if buckets is not None:
@@ -336,6 +344,7 @@ def run_cyfa(args, rank, world, local_rank):
         # with dL/dy = dy, and the loss value is formed for the host to read
         for p in params:
             p.grad = None
+        xin.grad = None
         y, _ = layer(xin)
         y.backward(dyin)
         with torch.no_grad():
@@ -382,7 +391,7 @@ def run_cyfa(args, rank, world, local_rank):
     # stream into a staging buffer while the current step computes, as a data
     # loader would; the step then moves it into the graph's input buffers.
     copy_stream = torch.cuda.Stream(device=dev)
-    bufs = [(torch.empty_like(x), torch.empty_like(dy)) for _ in range(2)]
+    bufs = [(torch.empty_like(x, requires_grad=False), torch.empty_like(dy)) for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
     done = [torch.cuda.Event() for _ in range(2)]
     main = torch.cuda.current_stream(dev)
@@ -505,6 +514,8 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank, world, local_rank = _rank_env()
+    # keep stdout to the one JSON line (NCCL's version banner otherwise precedes it)
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     if world > 1:
         import torch
         import torch.distributed as dist

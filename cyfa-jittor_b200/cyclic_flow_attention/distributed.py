@@ -79,7 +79,7 @@ class GradientBuckets:
     (training/optim.py:52-63); the arithmetic is the same, the transfer overlaps.
     """
 
-    def __init__(self, params, group=None, bucket_bytes=8 << 20):
+    def __init__(self, params, group=None, bucket_bytes=8 << 20, groups=None):
         self.params = [p for p in params if p.requires_grad]
         self.group = group
         self.bucket_bytes = bucket_bytes
@@ -87,23 +87,36 @@ class GradientBuckets:
         self.avg_op = dist.get_backend(group) == "nccl"
         self._arrivals = []  # parameter indices in the order of the first backward
         self._param_index = {id(p): k for k, p in enumerate(self.params)}
-        self._rebuilt = False
-        self._build(list(reversed(self.params)))
+        if groups is not None:
+            # explicit buckets, in the order the backward fills them (a model
+            # knows which gradients arrive together); leftovers go last
+            self._rebuilt = True
+            listed = {id(p) for g in groups for p in g}
+            buckets = [[p for p in g if p.requires_grad] for g in groups]
+            rest = [p for p in reversed(self.params) if id(p) not in listed]
+            self._build_groups([b for b in buckets if b] + ([rest] if rest else []))
+        else:
+            self._rebuilt = False
+            self._build(list(reversed(self.params)))
         self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in self.params]
         self.sync = True
         self._reset()
 
     def _build(self, order):
-        self.buckets = []
+        buckets = []
         cur, size = [], 0
         for p in order:
             cur.append(p)
             size += p.numel() * 4
             if size >= self.bucket_bytes:
-                self.buckets.append(cur)
+                buckets.append(cur)
                 cur, size = [], 0
         if cur:
-            self.buckets.append(cur)
+            buckets.append(cur)
+        self._build_groups(buckets)
+
+    def _build_groups(self, buckets):
+        self.buckets = buckets
         self.flat = []
         self.slot = {}  # param -> (bucket, element offset, flat view)
         for i, bucket in enumerate(self.buckets):
@@ -159,12 +172,38 @@ class GradientBuckets:
         self.pending[i] -= 1
         self._launch_ready()
 
-    def _pieces(self, i):
+    def early(self, params, grads):
+        """Gradients handed over by the op that computes them, before autograd
+        accumulates them (e.g. weight gradients formed ahead of the input
+        gradient).  If they complete a bucket (its other parameters' gradients
+        have already arrived) and every earlier bucket has been launched, the
+        bucket is gathered (these from `grads`, the others from `.grad`) and
+        all-reduced now, overlapping the rest of the op; the parameters' hooks
+        then do nothing.  Otherwise nothing happens and the hooks work as usual."""
+        if self.world == 1 or not self.sync or not params:
+            return
+        first = self.slot.get(params[0])
+        if first is None:
+            return
+        i = first[0]
+        given = dict(zip(params, grads))
+        if any(self.slot.get(p, (None,))[0] != i for p in params):
+            return
+        if any(p not in given and p not in self.filled[i] for p in self.buckets[i]):
+            return
+        self._launch_ready()
+        if self.next != i:
+            return
+        self.filled[i] = set(self.buckets[i])
+        self.pending[i] = 0
+        self._launch(i, given)
+
+    def _pieces(self, i, given=None):
         """Bucket i's gradients as library pieces, or None if one of them does
         not fit the kernel (not CUDA, other dtype, non-contiguous, unaligned)."""
         pieces = []
         for p in self.buckets[i]:
-            g = p.grad
+            g = given.get(p, p.grad) if given is not None else p.grad
             if g is None:
                 continue
             if (not g.is_cuda or g.dtype not in (torch.float32, torch.bfloat16)
@@ -177,21 +216,22 @@ class GradientBuckets:
             arr[k] = _lib.BucketPiece(*pc)
         return arr, len(pieces)
 
-    def _gather(self, i):
-        """Copies bucket i's gradients into its flat fp32 buffer; slots of
-        parameters without a gradient are zero."""
+    def _gather(self, i, given=None):
+        """Copies bucket i's gradients (or the `given` ones) into its flat fp32
+        buffer; slots of parameters without a gradient are zero."""
         flat = self.flat[i]
-        missing = [p for p in self.buckets[i] if p.grad is None]
-        for p in missing:
-            self.slot[p][2].zero_()
-        packed = self._pieces(i) if flat.is_cuda else None
+        grad = (lambda p: given.get(p, p.grad)) if given is not None else (lambda p: p.grad)
+        for p in self.buckets[i]:
+            if grad(p) is None:
+                self.slot[p][2].zero_()
+        packed = self._pieces(i, given) if flat.is_cuda else None
         if packed is not None:
             arr, n = packed
             _lib.call("cyfa_bucket_gather", arr, n, _lib.ptr(flat), _lib.stream())
             return
         for p in self.buckets[i]:
-            if p.grad is not None:
-                self.slot[p][2].copy_(p.grad.reshape(-1))
+            if grad(p) is not None:
+                self.slot[p][2].copy_(grad(p).reshape(-1))
 
     def _scatter(self, i, scale):
         """Writes scale * bucket i back into the gradients (allocating missing ones)."""
@@ -208,8 +248,8 @@ class GradientBuckets:
             view = self.slot[p][2].view_as(p)
             p.grad.copy_(view * scale if scale != 1.0 else view)
 
-    def _launch(self, i):
-        self._gather(i)
+    def _launch(self, i, given=None):
+        self._gather(i, given)
         op = dist.ReduceOp.AVG if self.avg_op else dist.ReduceOp.SUM
         self.works[i] = dist.all_reduce(self.flat[i], op=op, group=self.group, async_op=True)
         self.next = i + 1

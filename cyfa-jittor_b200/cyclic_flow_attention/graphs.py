@@ -76,7 +76,8 @@ class GraphedStep:
     def __call__(self, *inputs):
         if len(inputs) != len(self.static_inputs):
             raise ValueError(f"expected {len(self.static_inputs)} inputs, got {len(inputs)}")
-        for dst, src in zip(self.static_inputs, inputs):
-            if src is not dst:
-                dst.copy_(src, non_blocking=True)
+        with torch.no_grad():  # static inputs may be leaves that require grad
+            for dst, src in zip(self.static_inputs, inputs):
+                if src is not dst:
+                    dst.copy_(src, non_blocking=True)
         return self.replay()

@@ -130,6 +130,25 @@ class CyclicFlowAttention(nn.Module):
         self.o_norm = RMSNorm(self.head_v_dim, norm_eps)
         self.o_proj = nn.Linear(self.value_dim, hidden_size, bias=False)
 
+    # Optional callable(params, grads): receives the input-side weight gradients
+    # as soon as the fused backward has formed them (before the input gradient),
+    # e.g. GradientBuckets.early to start their all-reduce early.
+    grad_ready = None
+
+    def grad_groups(self):
+        """Parameters grouped in the order the fused backward produces their
+        gradients (output side first, input side last); the last group is the
+        one the fused backward hands to `grad_ready`."""
+        front = [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight,
+                 self.g_proj[0].weight, self.a_proj.weight, self.b_proj.weight,
+                 self.d_proj.weight, self.q_conv1d.weight, self.k_conv1d.weight,
+                 self.v_conv1d.weight, self.A_log, self.dt_bias, self.b_proj.bias,
+                 self.d_proj.bias]
+        g1 = self.g_proj[1]
+        back = [p for p in (g1.weight, g1.bias, self.o_norm.weight) if p is not None]
+        core = [self.readout, self.q_norm.weight, self.k_norm.weight]
+        return [[self.o_proj.weight], back, core, front]
+
     def keep_fp32(self):
         """Casts to bf16 except the parameters the reference keeps in fp32
         (norm weights, readout, A_log, dt_bias; models/cyfa/modeling_cyfa.py:110-116)."""
@@ -167,7 +186,7 @@ class CyclicFlowAttention(nn.Module):
             x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, g0.weight,
             self.a_proj.weight, self.b_proj.weight, self.d_proj.weight, self.q_conv1d.weight,
             self.k_conv1d.weight, self.v_conv1d.weight, self.A_log, self.dt_bias,
-            self.b_proj.bias, self.d_proj.bias, H, slot)
+            self.b_proj.bias, self.d_proj.bias, H, slot, self.grad_ready)
         table = readout_table(self.readout)
         o, hk, hv, clock = ChunkCyfaPackedFunction.apply(
             qkv, H, K, V, g, delta, beta, table, self.q_norm.weight.float(),

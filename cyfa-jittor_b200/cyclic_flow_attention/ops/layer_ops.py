@@ -220,7 +220,7 @@ class LayerFrontFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, w_q, w_k, w_v, w_g0, w_a, w_b, w_d, cw_q, cw_k, cw_v, A_log, dt_bias,
-                b_bias, d_bias, H, slot=None):
+                b_bias, d_bias, H, slot=None, grad_ready=None):
         B, T, hid = x.shape
         rows = B * T
         dev = x.device
@@ -255,6 +255,11 @@ class LayerFrontFunction(torch.autograd.Function):
         if slot is not None:
             slot.shape, slot.cols, slot.buf = (B, T, NB), (c_g, c_g + n_g), None
         ctx.slot = slot
+        # optional hand-over of the weight gradients as soon as they exist (before
+        # dx), e.g. to start their data-parallel all-reduce early
+        ctx.grad_ready = grad_ready
+        ctx.params = (w_q, w_k, w_v, w_g0, w_a, w_b, w_d, cw_q, cw_k, cw_v, A_log, dt_bias,
+                      b_bias, d_bias) if grad_ready is not None else None
         ctx.save_for_backward(x, W_big, big, cw, A, dt, bb, db)
         ctx.meta = (H, NB, n_qkv, c_g, n_g, c_a, c_b, c_d, n_used, Wc,
                     [w.shape[0] for w in parts[:7]], cw_q.dtype,
@@ -312,13 +317,17 @@ class LayerFrontFunction(torch.autograd.Function):
             dbig[..., c_g:c_g + n_g].zero_()
         d2 = dbig.view(rows, NB)
         x2 = x.reshape(rows, hid)
-        # dx from every column except d (projected from x.detach()) and the padding
-        dx = torch.matmul(d2[:, :c_d], W_big[:c_d]).view(B, T, hid)
+        # weight gradients first, so that their hand-over overlaps the dx GEMM
         dW = torch.matmul(d2[:, :n_used].t(), x2)
-        grads_w = list(torch.split(dW, sizes))
-        dcw_parts = torch.split(dcw.to(cdt).reshape(n_qkv, 1, Wc), sizes[:3])
-        return (dx, *grads_w, *dcw_parts, dA.to(gdts[0]), ddtb.to(gdts[1]), dbb.to(gdts[2]),
-                ddb.to(gdts[3]), None, None)
+        grads = (*torch.split(dW, sizes), *torch.split(dcw.to(cdt).reshape(n_qkv, 1, Wc), sizes[:3]),
+                 dA.to(gdts[0]), ddtb.to(gdts[1]), dbb.to(gdts[2]), ddb.to(gdts[3]))
+        if ctx.grad_ready is not None:
+            ctx.grad_ready(ctx.params, grads)
+        # dx from every column except d (projected from x.detach()) and the padding
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.matmul(d2[:, :c_d], W_big[:c_d]).view(B, T, hid)
+        return (dx, *grads, None, None, None)
 
 
 class ChunkCyfaPackedFunction(torch.autograd.Function):

@@ -173,3 +173,84 @@ def test_gradient_buckets_match_flat_allreduce():
     for step in range(2):
         for a, b in zip(res[0][f"net{step}"], res[1][f"net{step}"]):
             assert torch.equal(torch.tensor(a), torch.tensor(b))
+
+
+class _EarlyLinear(torch.autograd.Function):
+    """y = x w^T + b whose backward hands (w, b)'s gradients over before dx."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, ready):
+        ctx.save_for_backward(x, w)
+        ctx.ready, ctx.params = ready, (w, b)
+        return x @ w.t() + b
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dw, db = dy.t() @ x, dy.sum(0)
+        ctx.ready(ctx.params, (dw, db))
+        return dy @ w, dw, db, None
+
+
+def _early_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "cyfa-jittor_b200"))
+    from cyclic_flow_attention.distributed import GradientBuckets, allreduce_gradients
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        def make():
+            torch.manual_seed(3)
+            return torch.nn.Linear(5, 6), torch.nn.Linear(6, 2)
+
+        l1, l2 = make()
+        r1, r2 = make()
+        params = list(l1.parameters()) + list(l2.parameters())
+        # explicit groups in backward order: l2 first, then l1 (handed over early)
+        buckets = GradientBuckets(params, groups=[list(l2.parameters()), list(l1.parameters())])
+        torch.manual_seed(10 + rank)
+        x = torch.randn(4, 5)
+        out = {"n": len(buckets.buckets)}
+        for step in range(2):
+            for p in params + list(r1.parameters()) + list(r2.parameters()):
+                p.grad = None
+            y = l2(_EarlyLinear.apply(x * (step + 1), l1.weight, l1.bias, buckets.early))
+            y.pow(2).sum().backward()
+            out[f"early_used{step}"] = buckets.next  # bucket 1 launched before finish()
+            buckets.finish()
+            r2(r1(x * (step + 1))).pow(2).sum().backward()
+            allreduce_gradients(list(r1.parameters()) + list(r2.parameters()))
+            out[f"net{step}"] = [p.grad.tolist() for p in params]
+            out[f"ref{step}"] = [p.grad.tolist() for p in list(r1.parameters()) + list(r2.parameters())]
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_buckets_groups_and_early_handover():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_early_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, out = q.get(timeout=120)
+        res[r] = out
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert res[r]["n"] == 2
+        for step in range(2):
+            assert res[r][f"early_used{step}"] == 2  # both buckets launched during backward
+            for a, b in zip(res[r][f"net{step}"], res[r][f"ref{step}"]):
+                assert torch.allclose(torch.tensor(a), torch.tensor(b), rtol=1e-6, atol=1e-6)
