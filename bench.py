@@ -25,6 +25,11 @@ import subprocess
 import sys
 import time
 
+# Keep stdout to the one JSON line: an image-wide NCCL_DEBUG=VERSION makes NCCL
+# print its version banner there.  Must be set before torch (and NCCL) load.
+if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+    os.environ["NCCL_DEBUG"] = "WARN"
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 for _p in (ROOT, os.path.join(ROOT, "cyfa-jittor_b200")):
     if _p not in sys.path:
@@ -514,8 +519,6 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     rank, world, local_rank = _rank_env()
-    # keep stdout to the one JSON line (NCCL's version banner otherwise precedes it)
-    os.environ.setdefault("NCCL_DEBUG", "WARN")
     if world > 1:
         import torch
         import torch.distributed as dist
