@@ -4,12 +4,29 @@
 
 #include <atomic>
 #include <mutex>
+#include <set>
+#include <tuple>
 #include <vector>
 
 #include "../../include/cyfa.h"
 #include "cyfa_common.cuh"
 
 namespace cyfa {
+
+// Raises a kernel's dynamic shared memory limit once per (kernel, device); the
+// attribute call is host-side only, so launches inside stream capture stay cheap.
+template <typename Kern>
+static void set_smem(Kern k, int bytes) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, int>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(reinterpret_cast<const void*>(k), dev, bytes);
+  std::lock_guard<std::mutex> lk(mu);
+  if (done.count(key)) return;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess)
+    done.insert(key);
+}
 
 enum Status : int {
   kOk = 0,
@@ -165,7 +182,8 @@ static int token_bwd_launch(const void* q, const void* k, const float* q_norm_we
                kNullPointer);
   CYFA_REQUIRE(B > 0 && T > 0 && H > 0 && (K == 128 || K == 256), kBadShape);
   CYFA_REQUIRE(aligned(q, 16) && aligned(k, 16) && aligned(dq, 16) && aligned(dk, 16) &&
-                   aligned(dqn, 16) && aligned(dkn, 16) && aligned(q_norm_weight, 16) &&
+                   aligned(dqn, 16) && aligned(dkn, 16) && aligned(dw, 16) &&
+                   (!dw_b || aligned(dw_b, 16)) && aligned(q_norm_weight, 16) &&
                    aligned(k_norm_weight, 16) && q_stride % 8 == 0 && k_stride % 8 == 0 &&
                    dq_stride % 8 == 0 && dk_stride % 8 == 0,
                kMisaligned);

@@ -125,20 +125,7 @@ static int readout_ctas_per_head(const Dims& d) {
 // A token stride of 0 means the dense layout.
 static long long stride_or(long long s, long long dense) { return s > 0 ? s : dense; }
 
-// Raises a kernel's dynamic shared memory limit once per (kernel, device); the
-// attribute call is host-side only, so launches inside stream capture stay cheap.
-template <typename Kern>
-static void set_smem(Kern k, int bytes) {
-  static std::mutex mu;
-  static std::set<std::tuple<const void*, int, int>> done;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const auto key = std::make_tuple(reinterpret_cast<const void*>(k), dev, bytes);
-  std::lock_guard<std::mutex> lk(mu);
-  if (done.count(key)) return;
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess)
-    done.insert(key);
-}
+
 
 }  // namespace cyfa
 
