@@ -166,7 +166,8 @@ def cpu_layer_tokens_per_s(min_seconds=10.0, max_reps=20, T=None, warm=1):
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    T = T or CFG["T"]
+    # long sequences: time 4096 tokens (the chunked cost is linear in T)
+    T = T or min(CFG["T"], 4096)
     gen = torch.Generator().manual_seed(0)
     H, hd, hid = CFG["heads"], CFG["head_dim"], CFG["hidden"]
     shapes = {
@@ -200,7 +201,8 @@ def cpu_layer_tokens_per_s(min_seconds=10.0, max_reps=20, T=None, warm=1):
         step()
         reps += 1
     dt = time.perf_counter() - t0
-    return reps * T / dt, threads, f"{reps} x (1 seq x {T} tokens) layer fwd+bwd, fp32 oracle"
+    note = "" if T == CFG["T"] else f" (tokens/s extrapolated to T={CFG['T']}: linear cost)"
+    return reps * T / dt, threads, f"{reps} x (1 seq x {T} tokens) layer fwd+bwd, fp32 oracle{note}"
 
 
 def run_reference(args, rank, world):
@@ -234,6 +236,87 @@ def run_reference(args, rank, world):
 
 # ---------------------------------------------------------------- decode leg
 DECODE = dict(layers=24, batch=256, heads=8, head_dim=256, slots=128)
+# BASELINE configs[1] (c2): the public chunk_cyfa op alone, per GPU
+OPCFG = dict(B=8, T=4096, H=4, K=256, V=256)
+# per token-head FLOPs of the op (full 128x128 tiles), K = V = 256, 128 slots:
+# forward 2 x 180,224 + readout 65,536; backward 393,216 + 376,832 + readout 196,608
+OP_FLOPS_FWD, OP_FLOPS_BWD = 425_984, 966_656
+# BASELINE configs[4] (c5): long-context layer, per GPU one 32768-token sequence
+C5 = dict(hidden=2048, heads=8, head_dim=256, slots=128, B=1, T=32768)
+
+
+def measure_op(args, rank, world, dev, peaks, barrier):
+    """chunk_cyfa (q/k RMSNorm, both ScalarGatedLA passes and the
+    readout) forward and forward+backward on seeded synthetic inputs with the
+    reference benchmark's distributions (benchmarks/run.py:135-151), B = 8 per GPU,
+    H = 4, T = 4096, K = V = 256.  CUDA events per step, L2 flushed between steps."""
+    import torch
+    import torch.distributed as dist
+
+    from cyclic_flow_attention import ops
+    from cyclic_flow_attention.graphs import GraphedStep
+
+    B, T, H, K, V = (OPCFG[k] for k in ("B", "T", "H", "K", "V"))
+    gen = torch.Generator(device=dev).manual_seed(11 + rank)
+    bf = torch.bfloat16
+    q = torch.randn(B, T, H, K, device=dev, generator=gen).to(bf).requires_grad_(True)
+    k = torch.randn(B, T, H, K, device=dev, generator=gen).to(bf).requires_grad_(True)
+    v = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf).requires_grad_(True)
+    g = (-0.1 * torch.rand(B, T, H, device=dev, generator=gen)).requires_grad_(True)
+    delta = torch.sigmoid(torch.randn(B, T, H, device=dev, generator=gen)).requires_grad_(True)
+    beta = torch.sigmoid(torch.randn(B, T, H, device=dev, generator=gen)).requires_grad_(True)
+    readout = (torch.eye(127, device=dev).expand(H, -1, -1)
+               + 0.05 * torch.randn(H, 127, 127, device=dev, generator=gen)).requires_grad_(True)
+    qw = (1 + 0.1 * torch.randn(K, device=dev, generator=gen)).requires_grad_(True)
+    kw = (1 + 0.1 * torch.randn(K, device=dev, generator=gen)).requires_grad_(True)
+    do = torch.randn(B, T, H, V, device=dev, generator=gen).to(bf)
+    leaves = [q, k, v, g, delta, beta, readout, qw, kw]
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+
+    def fwd():
+        with torch.no_grad():
+            o, _ = ops.chunk_cyfa(q, k, v, g, delta, beta, readout, qw, kw)
+        return o
+
+    def fwd_bwd():
+        for t in leaves:
+            t.grad = None
+        o, _ = ops.chunk_cyfa(q, k, v, g, delta, beta, readout, qw, kw)
+        o.backward(do)
+        return o.detach()
+
+    def timed(step_graph):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(max(3, min(args.steps, 10)))]
+        barrier()
+        for a, b in evs:
+            flush.fill_(1)
+            a.record()
+            step_graph.replay()
+            b.record()
+        barrier()
+        t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs) / len(evs)], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    gf = GraphedStep(fwd, [], [], warmup=3)
+    ms_f = timed(gf)
+    gfb = GraphedStep(fwd_bwd, [], leaves, warmup=3)
+    ms_fb = timed(gfb)
+    tok = B * T
+    th = tok * H
+    peak = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    out = {"workload": "chunk_cyfa op, BASELINE configs[1] (B=8 per GPU, H=4, T=4096, K=V=256, "
+                       "bf16, seeded synthetic inputs)",
+           "fwd": {"tokens_per_s": world * tok / (ms_f / 1000.0), "ms": ms_f,
+                   "tflops": th * OP_FLOPS_FWD / (ms_f / 1000.0) / 1e12},
+           "fwd_bwd": {"tokens_per_s": world * tok / (ms_fb / 1000.0), "ms": ms_fb,
+                       "tflops": th * (OP_FLOPS_FWD + OP_FLOPS_BWD) / (ms_fb / 1000.0) / 1e12},
+           "tensor_peak_tflops": peak,
+           "l2": "flushed between timed steps"}
+    del gf, gfb
+    return out
 
 
 def measure_decode(args, rank, world, dev, peaks, barrier):
@@ -472,6 +555,7 @@ def run_cyfa(args, rank, world, local_rank):
                          "kernel_ms": {k: round(v[0], 4) for k, v in sorted(prof.items())}})
 
     decode = None if args.no_decode else measure_decode(args, rank, world, dev, peaks, barrier)
+    op = None if args.no_op else measure_op(args, rank, world, dev, peaks, barrier)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -484,7 +568,9 @@ def run_cyfa(args, rank, world, local_rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": "cyfa_layer_fwd_bwd (BASELINE configs[2])", **CFG,
+            "config": {"workload": ("cyfa_layer_fwd_bwd (BASELINE configs[2])" if args.workload == "c3"
+                                    else "cyfa_layer_fwd_bwd long context (BASELINE configs[4])"),
+                       **CFG,
                        "global_batch": B * world, "seq_len": T,
                        "parallelism": f"dp{world} (batch x head sharded, grad all-reduce)",
                        "l2": "flushed between timed steps (2x126 MiB write outside the events)",
@@ -495,6 +581,7 @@ def run_cyfa(args, rank, world, local_rank):
             "gpu_launches": launches,
             "clocks": clocks,
             "decode": decode,
+            "op": op,
         }
         print(json.dumps(line), flush=True)
     # a graph that holds NCCL calls must be gone before the process group is
@@ -515,9 +602,16 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-kernel leg")
+    ap.add_argument("--no-op", action="store_true", help="skip the chunk_cyfa op leg (configs[1])")
+    ap.add_argument("--workload", choices=("c3", "c5"), default="c3",
+                    help="layer config: c3 (BASELINE configs[2], default) or c5 (long context, "
+                         "configs[4], one 32768-token sequence per GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.workload == "c5":
+        CFG.clear()
+        CFG.update(C5)
     rank, world, local_rank = _rank_env()
     if world > 1:
         import torch
