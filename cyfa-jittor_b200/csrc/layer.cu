@@ -55,6 +55,7 @@ constexpr int kConvUnrollF = 8;
 
 template <int W>
 __global__ void __launch_bounds__(256) short_conv_fwd_kernel(ConvParams p) {
+  constexpr int WM = W > 1 ? W - 1 : 1;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int c0 = blockIdx.x * 128 + lane * 4, b = blockIdx.z;
   const int t0 = (blockIdx.y * kConvWarps + wid) * kConvRun;
@@ -67,41 +68,53 @@ __global__ void __launch_bounds__(256) short_conv_fwd_kernel(ConvParams p) {
     bias[e] = p.bias ? p.bias[c0 + e] : 0.f;
   }
   const __nv_bfloat16* xb = p.x + size_t(b) * p.T * p.x_stride + c0;
-  uint2 win[W > 1 ? W - 1 : 1];  // x rows t-(W-1) .. t-1
+  float win[WM][4];  // x rows t-(W-1) .. t-1, fp32
 #pragma unroll
   for (int i = 0; i < W - 1; ++i) {
     const int t = t0 - (W - 1) + i;
-    win[i] = make_uint2(0, 0);
+    uint2 r = make_uint2(0, 0);
     if (t >= 0)
-      win[i] = *reinterpret_cast<const uint2*>(xb + size_t(t) * p.x_stride);
+      r = *reinterpret_cast<const uint2*>(xb + size_t(t) * p.x_stride);
     else if (p.cache)
-      win[i] = *reinterpret_cast<const uint2*>(p.cache + (size_t(b) * (W - 1) + (W - 1) + t) * p.C + c0);
+      r = *reinterpret_cast<const uint2*>(p.cache + (size_t(b) * (W - 1) + (W - 1) + t) * p.C + c0);
+    win[i][0] = bf_lo(r.x), win[i][1] = bf_hi(r.x), win[i][2] = bf_lo(r.y), win[i][3] = bf_hi(r.y);
   }
   __nv_bfloat16* yb = p.y + size_t(b) * p.T * p.C + c0;
   const int tend = min(p.T, t0 + kConvRun);
   for (int t1 = t0; t1 < tend; t1 += kConvUnrollF) {
     uint2 cur[kConvUnrollF];
+    const __nv_bfloat16* xr = xb + size_t(t1) * p.x_stride;
+    if (t1 + kConvUnrollF <= tend) {
 #pragma unroll
-    for (int u = 0; u < kConvUnrollF; ++u)
-      cur[u] = t1 + u < tend ? *reinterpret_cast<const uint2*>(xb + size_t(t1 + u) * p.x_stride)
-                             : make_uint2(0, 0);
+      for (int u = 0; u < kConvUnrollF; ++u)
+        cur[u] = *reinterpret_cast<const uint2*>(xr + size_t(u) * p.x_stride);
+    } else {
+#pragma unroll
+      for (int u = 0; u < kConvUnrollF; ++u)
+        cur[u] = t1 + u < tend ? *reinterpret_cast<const uint2*>(xr + size_t(u) * p.x_stride)
+                               : make_uint2(0, 0);
+    }
 #pragma unroll
     for (int u = 0; u < kConvUnrollF; ++u) {
       if (t1 + u >= tend) break;
+      const float xn[4] = {bf_lo(cur[u].x), bf_hi(cur[u].x), bf_lo(cur[u].y), bf_hi(cur[u].y)};
       float y[4] = {bias[0], bias[1], bias[2], bias[3]};
 #pragma unroll
       for (int i = 0; i < W; ++i) {
-        const uint2 r = i < W - 1 ? win[i < W - 1 ? i : 0] : cur[u];
-        y[0] += wr[i][0] * bf_lo(r.x);
-        y[1] += wr[i][1] * bf_hi(r.x);
-        y[2] += wr[i][2] * bf_lo(r.y);
-        y[3] += wr[i][3] * bf_hi(r.y);
+        const float* r = i < W - 1 ? win[i < W - 1 ? i : 0] : xn;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y[e] += wr[i][e] * r[e];
       }
       *reinterpret_cast<uint2*>(yb + size_t(t1 + u) * p.C) =
           make_uint2(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]));
 #pragma unroll
-      for (int i = 0; i + 1 < W - 1; ++i) win[i] = win[i + 1];
-      if (W > 1) win[W > 1 ? W - 2 : 0] = cur[u];
+      for (int i = 0; i + 1 < W - 1; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) win[i][e] = win[i + 1][e];
+      if (W > 1) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) win[W > 1 ? W - 2 : 0][e] = xn[e];
+      }
     }
   }
 }
@@ -109,13 +122,20 @@ __global__ void __launch_bounds__(256) short_conv_fwd_kernel(ConvParams p) {
 // Backward without cache, lane owns channels c0 .. c0+3 (c0 = 128 * blockIdx.x + 4 * lane):
 //   dx[t] = sum_i w_i dy[t + (W-1) - i],  dw_i = sum_t dy[t] x[t + i - (W-1)],
 //   dbias = sum_t dy[t].
-// A warp keeps x rows t-(W-1) .. t-1 and dy rows t .. t+W-2 in registers.  The 8
-// warps of a CTA (consecutive token runs of one batch row) add their dw/dbias
-// sums in a fixed order into one partial row per CTA row index blockIdx.y.
+// A warp keeps x rows t-(W-1) .. t-1 and dy rows t .. t+W-2 in registers, unpacked
+// once to fp32 as they arrive; each step loads kConvUnroll rows of both ahead
+// (bounds checks only on the last step of a batch row).  The 8 warps of a CTA
+// (consecutive token runs of one batch row) add their dw/dbias sums in a fixed
+// order into one partial row per CTA row index blockIdx.y.
 // grid (ceil(C/128), B * ceil(T / (kConvWarps*kConvRun))).
+__device__ __forceinline__ void unpack4(uint2 r, float* f) {
+  f[0] = bf_lo(r.x), f[1] = bf_hi(r.x), f[2] = bf_lo(r.y), f[3] = bf_hi(r.y);
+}
+
 template <int W>
-__global__ void __launch_bounds__(256) short_conv_bwd_kernel(ConvParams p) {
+__global__ void __launch_bounds__(256, 2) short_conv_bwd_kernel(ConvParams p) {
   __shared__ float red[kConvWarps][128 * (W + 1)];
+  constexpr int WM = W > 1 ? W - 1 : 1;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int ng = (p.T + kConvWarps * kConvRun - 1) / (kConvWarps * kConvRun);
   const int b = blockIdx.y / ng, grp = blockIdx.y % ng;
@@ -135,37 +155,50 @@ __global__ void __launch_bounds__(256) short_conv_bwd_kernel(ConvParams p) {
     const __nv_bfloat16* xb = p.x + size_t(b) * p.T * p.x_stride + c0;
     const __nv_bfloat16* db = p.dy + size_t(b) * p.T * p.C + c0;
     __nv_bfloat16* dxb = p.dx + size_t(b) * p.T * p.dx_stride + c0;
-    uint2 X[W > 1 ? W - 1 : 1], D[W > 1 ? W - 1 : 1];
+    float X[WM][4], D[WM][4];
 #pragma unroll
     for (int i = 0; i < W - 1; ++i) {
       const int tx = t0 - (W - 1) + i, td = t0 + i;
-      X[i] = tx >= 0 ? *reinterpret_cast<const uint2*>(xb + size_t(tx) * p.x_stride) : make_uint2(0, 0);
-      D[i] = td < p.T ? *reinterpret_cast<const uint2*>(db + size_t(td) * p.C) : make_uint2(0, 0);
+      unpack4(tx >= 0 ? *reinterpret_cast<const uint2*>(xb + size_t(tx) * p.x_stride)
+                      : make_uint2(0, 0), X[i]);
+      unpack4(td < p.T ? *reinterpret_cast<const uint2*>(db + size_t(td) * p.C) : make_uint2(0, 0),
+              D[i]);
     }
     const int tend = min(p.T, t0 + kConvRun);
     for (int t1 = t0; t1 < tend; t1 += kConvUnroll) {
       uint2 xs[kConvUnroll], ds[kConvUnroll];
+      const __nv_bfloat16* xr = xb + size_t(t1) * p.x_stride;
+      const __nv_bfloat16* dr = db + size_t(t1 + W - 1) * p.C;
+      if (t1 + kConvUnroll <= tend && t1 + kConvUnroll + W - 1 <= p.T) {
 #pragma unroll
-      for (int u = 0; u < kConvUnroll; ++u) {
-        const int t = t1 + u, td = t + W - 1;
-        xs[u] = t < tend ? *reinterpret_cast<const uint2*>(xb + size_t(t) * p.x_stride) : make_uint2(0, 0);
-        ds[u] = (t < tend && td < p.T) ? *reinterpret_cast<const uint2*>(db + size_t(td) * p.C)
-                                       : make_uint2(0, 0);
+        for (int u = 0; u < kConvUnroll; ++u) {
+          xs[u] = *reinterpret_cast<const uint2*>(xr + size_t(u) * p.x_stride);
+          ds[u] = *reinterpret_cast<const uint2*>(dr + size_t(u) * p.C);
+        }
+      } else {
+#pragma unroll
+        for (int u = 0; u < kConvUnroll; ++u) {
+          const int t = t1 + u, td = t + W - 1;
+          xs[u] = t < tend ? *reinterpret_cast<const uint2*>(xr + size_t(u) * p.x_stride)
+                           : make_uint2(0, 0);
+          ds[u] = (t < tend && td < p.T) ? *reinterpret_cast<const uint2*>(dr + size_t(u) * p.C)
+                                         : make_uint2(0, 0);
+        }
       }
 #pragma unroll
       for (int u = 0; u < kConvUnroll; ++u) {
         if (t1 + u >= tend) break;
-        // dy rows t .. t+W-1 = D[0..W-2], ds[u];  x rows t-(W-1) .. t = X[0..W-2], xs[u]
-        const uint2 d0r = W > 1 ? D[0] : ds[u];
-        const float d0[4] = {bf_lo(d0r.x), bf_hi(d0r.x), bf_lo(d0r.y), bf_hi(d0r.y)};
+        float xn[4], dn[4];
+        unpack4(xs[u], xn);
+        unpack4(ds[u], dn);
+        // dy rows t .. t+W-1 = D[0..W-2], dn;  x rows t-(W-1) .. t = X[0..W-2], xn
         float dx[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int i = 0; i < W; ++i) {
           const int j = W - 1 - i;  // dy row t + j
-          const uint2 dr = j < W - 1 ? D[j < W - 1 ? j : 0] : ds[u];
-          const uint2 xr = i < W - 1 ? X[i < W - 1 ? i : 0] : xs[u];
-          const float dv[4] = {bf_lo(dr.x), bf_hi(dr.x), bf_lo(dr.y), bf_hi(dr.y)};
-          const float xv[4] = {bf_lo(xr.x), bf_hi(xr.x), bf_lo(xr.y), bf_hi(xr.y)};
+          const float* dv = j < W - 1 ? D[j < W - 1 ? j : 0] : dn;
+          const float* xv = i < W - 1 ? X[i < W - 1 ? i : 0] : xn;
+          const float* d0 = W > 1 ? D[0] : dn;
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             dx[e] += wr[i][e] * dv[e];
@@ -173,17 +206,22 @@ __global__ void __launch_bounds__(256) short_conv_bwd_kernel(ConvParams p) {
           }
         }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[W][e] += d0[e];
+        for (int e = 0; e < 4; ++e) acc[W][e] += (W > 1 ? D[0] : dn)[e];
         *reinterpret_cast<uint2*>(dxb + size_t(t1 + u) * p.dx_stride) =
             make_uint2(pack_bf16(dx[0], dx[1]), pack_bf16(dx[2], dx[3]));
 #pragma unroll
-        for (int i = 0; i + 1 < W - 1; ++i) {
-          X[i] = X[i + 1];
-          D[i] = D[i + 1];
-        }
+        for (int i = 0; i + 1 < W - 1; ++i)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            X[i][e] = X[i + 1][e];
+            D[i][e] = D[i + 1][e];
+          }
         if (W > 1) {
-          X[W > 1 ? W - 2 : 0] = xs[u];
-          D[W > 1 ? W - 2 : 0] = ds[u];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            X[W > 1 ? W - 2 : 0][e] = xn[e];
+            D[W > 1 ? W - 2 : 0][e] = dn[e];
+          }
         }
       }
     }

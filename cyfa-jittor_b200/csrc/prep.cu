@@ -283,102 +283,153 @@ __device__ __forceinline__ float2 load_grad_pair(const void* base, size_t off) {
         *reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(base) + off));
 }
 
+// E consecutive elements of type T kept packed (as loaded) until they are used,
+// so that rows loaded ahead cost E*sizeof(T)/4 registers instead of E.
+template <int E, typename T>
+struct RawVec {
+  static constexpr int N = E * int(sizeof(T)) / 4;
+  uint32_t w[N];
+  __device__ __forceinline__ void load(const T* p) {
+    if constexpr (N % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < N / 4; ++i) {
+        const uint4 v = reinterpret_cast<const uint4*>(p)[i];
+        w[4 * i] = v.x, w[4 * i + 1] = v.y, w[4 * i + 2] = v.z, w[4 * i + 3] = v.w;
+      }
+    } else {
+      const uint2 v = *reinterpret_cast<const uint2*>(p);
+      w[0] = v.x, w[1] = v.y;
+    }
+  }
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int i = 0; i < N; ++i) w[i] = 0u;
+  }
+  __device__ __forceinline__ void unpack(float* f) const {
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      if constexpr (sizeof(T) == 4) {
+        f[i] = __uint_as_float(w[i]);
+      } else {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+    }
+  }
+};
+
 // GT: element type of the incoming gradients (dqn, dkn, dw, dw_b).
-// 8 warps per block as 4 row slots x 2 roles: role 0 does the q side of a row,
-// role 1 the k side and the write-vector adjoint, so a warp holds one vector set
-// (few registers, three blocks per SM).  Slot s of block b handles rows
-// b*4 + s + i*gridDim.x*4; each block writes one row of q and k norm-weight
-// partials (its rows, fixed order), so the partial matrices have gridDim.x rows.
+// One warp per row (q side, k side and the write-vector adjoint together, so all
+// warps carry the same work), every load of the row issued before any
+// arithmetic.  Warp w of block b handles rows b*8 + w + i*gridDim.x*8; each block
+// writes one row of q and k norm-weight partials (its rows, fixed order), so the
+// partial matrices have gridDim.x rows.
 template <int K, typename GT>
 __global__ void __launch_bounds__(256, 3) token_bwd_kernel(TokenBwdParams p) {
   constexpr int E = K / 32;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  const int role = wid & 1, slot = wid >> 1;
-  __shared__ float part_s[2][4][K];
-  const __nv_bfloat16* xsrc = role ? p.k : p.q;
-  const void* gsrc = role ? p.dkn : p.dqn;
-  const float* rsv = role ? p.k_rs : p.q_rs;
-  __nv_bfloat16* dst = role ? p.dk : p.dq;
-  const long long xs = role ? p.k_stride : p.q_stride, ds = role ? p.dk_stride : p.dq_stride;
-  float wv[E], acc[E];
-  load_f32_vec<E>((role ? p.kw : p.qw) + lane * E, wv);
+  __shared__ float wts[2][K];
+  __shared__ float part_s[2][8][K];
+  for (int i = threadIdx.x; i < K; i += 256) {
+    wts[0][i] = p.qw[i];
+    wts[1][i] = p.kw[i];
+  }
+  __syncthreads();
+  float acc_q[E], acc_k[E];
 #pragma unroll
-  for (int j = 0; j < E; ++j) acc[j] = 0.f;
+  for (int j = 0; j < E; ++j) acc_q[j] = acc_k[j] = 0.f;
   const size_t rows = size_t(p.B) * p.H * p.TP;
-  for (size_t row = size_t(blockIdx.x) * 4 + slot; row < rows; row += size_t(gridDim.x) * 4) {
+  for (size_t row = size_t(blockIdx.x) * 8 + wid; row < rows; row += size_t(gridDim.x) * 8) {
     const int t = int(row % p.TP);
     const size_t bh = row / p.TP;
     const int b = int(bh / p.H), h = int(bh % p.H);
     const bool real = t < p.T;
-    float x[E], g[E];
-#pragma unroll
-    for (int j = 0; j < E; ++j) x[j] = g[j] = 0.f;
     const size_t tok = size_t(b) * p.T + t, col = size_t(h) * K + lane * E;
-    float lam = 0.f, bt = 0.f;
-    float2 dwp[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    RawVec<E, __nv_bfloat16> xq, xk;
+    RawVec<E, GT> gq, gk;
+    xq.zero(), xk.zero(), gq.zero(), gk.zero();
+    float rq = 0.f, rk = 0.f;
     if (real) {
-      load_bf16_vec<E>(xsrc + tok * xs + col, x);
-      load_grad_vec<E, GT>(gsrc, row * K + lane * E, g);
+      xq.load(p.q + tok * p.q_stride + col);
+      xk.load(p.k + tok * p.k_stride + col);
+      gq.load(static_cast<const GT*>(p.dqn) + row * K + lane * E);
+      gk.load(static_cast<const GT*>(p.dkn) + row * K + lane * E);
+      rq = p.q_rs[row];
+      rk = p.k_rs[row];
     }
-    if (role == 1) {
-      lam = p.lam[row];
-      bt = p.beta_h[row];
+    const float lam = p.lam[row], bt = p.beta_h[row];
+    float2 dwp[2];
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        const int pair = lane + 32 * part;
-        dwp[part] = load_grad_pair<GT>(p.dw, row * 128 + 2 * pair);
-        if (p.dw_b) {
-          const float2 e2 = load_grad_pair<GT>(p.dw_b, row * 128 + 2 * pair);
-          dwp[part].x += e2.x;
-          dwp[part].y += e2.y;
-        }
+    for (int part = 0; part < 2; ++part) {
+      const int pair = lane + 32 * part;
+      dwp[part] = load_grad_pair<GT>(p.dw, row * 128 + 2 * pair);
+      if (p.dw_b) {
+        const float2 e2 = load_grad_pair<GT>(p.dw_b, row * 128 + 2 * pair);
+        dwp[part].x += e2.x;
+        dwp[part].y += e2.y;
       }
     }
-    const float r = real ? rsv[row] : 0.f;
-    float dot = 0.f;
+    // RMSNorm adjoints (ops/qk_norm.py:109-165), q then k
 #pragma unroll
-    for (int j = 0; j < E; ++j) dot += g[j] * wv[j] * x[j];
+    for (int side = 0; side < 2; ++side) {
+      float xv[E], gv[E], wv[E];
+      (side ? xk : xq).unpack(xv);
+      (side ? gk : gq).unpack(gv);
+      const float r = side ? rk : rq;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    dot *= r * r / K;
-    float o_[E];
+      for (int j = 0; j < E; j += 4) {
+        const float4 w4 = *reinterpret_cast<const float4*>(&wts[side][lane * E + j]);
+        wv[j] = w4.x, wv[j + 1] = w4.y, wv[j + 2] = w4.z, wv[j + 3] = w4.w;
+      }
+      float dot = 0.f;
 #pragma unroll
-    for (int j = 0; j < E; ++j) {
-      o_[j] = (g[j] * wv[j] - x[j] * dot) * r;
-      acc[j] += x[j] * r * g[j];
+      for (int j = 0; j < E; ++j) dot += gv[j] * wv[j] * xv[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      dot *= r * r / K;
+      float o_[E];
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        o_[j] = (gv[j] * wv[j] - xv[j] * dot) * r;
+        (side ? acc_k : acc_q)[j] += xv[j] * r * gv[j];
+      }
+      if (real) {
+        if (side) store_bf16_vec<E>(p.dk + tok * p.dk_stride + col, o_);
+        else store_bf16_vec<E>(p.dq + tok * p.dq_stride + col, o_);
+      }
     }
-    if (real) store_bf16_vec<E>(dst + tok * ds + col, o_);
-    if (role == 1) {
-      // write-vector adjoint (ops/utils.py:598-616)
-      float dl = 0.f, db = 0.f;
+    // write-vector adjoint (ops/utils.py:598-616)
+    float dl = 0.f, db = 0.f;
 #pragma unroll
-      for (int part = 0; part < 2; ++part) {
-        const int pair = lane + 32 * part;
-        float sn, cs;
-        __sincosf(clock_phase(lam, pair), &sn, &cs);
-        const float sc = atom_scale(pair);
-        const float de = dwp[part].x, dd = dwp[part].y;
-        db += de * sc * cs - dd * sc * sn;
-        dl += (-de * bt * sc * sn - dd * bt * sc * cs) * (pair * kTwoPiOver127);
-      }
+    for (int part = 0; part < 2; ++part) {
+      const int pair = lane + 32 * part;
+      float sn, cs;
+      __sincosf(clock_phase(lam, pair), &sn, &cs);
+      const float sc = atom_scale(pair);
+      const float de = dwp[part].x, dd = dwp[part].y;
+      db += de * sc * cs - dd * sc * sn;
+      dl += (-de * bt * sc * sn - dd * bt * sc * cs) * (pair * kTwoPiOver127);
+    }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        dl += __shfl_xor_sync(0xffffffffu, dl, o);
-        db += __shfl_xor_sync(0xffffffffu, db, o);
-      }
-      if (lane == 0) {
-        p.dlam[row] = dl;
-        p.dbeta[row] = db;
-      }
+    for (int o = 16; o > 0; o >>= 1) {
+      dl += __shfl_xor_sync(0xffffffffu, dl, o);
+      db += __shfl_xor_sync(0xffffffffu, db, o);
+    }
+    if (lane == 0) {
+      p.dlam[row] = dl;
+      p.dbeta[row] = db;
     }
   }
 #pragma unroll
-  for (int j = 0; j < E; ++j) part_s[role][slot][lane * E + j] = acc[j];
+  for (int j = 0; j < E; ++j) {
+    part_s[0][wid][lane * E + j] = acc_q[j];
+    part_s[1][wid][lane * E + j] = acc_k[j];
+  }
   __syncthreads();
   for (int d = threadIdx.x; d < K; d += 256) {
     float sq = 0.f, sk = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 8; ++i) {
       sq += part_s[0][i][d];
       sk += part_s[1][i][d];
     }
@@ -389,7 +440,7 @@ __global__ void __launch_bounds__(256, 3) token_bwd_kernel(TokenBwdParams p) {
 
 // Number of blocks (= partial rows) token_bwd_kernel uses for a shape: three per SM.
 inline int token_bwd_blocks(size_t rows) {
-  const size_t want = (rows + 3) / 4;
+  const size_t want = (rows + 7) / 8;
   return int(want < 444 ? want : 444);
 }
 

@@ -92,7 +92,7 @@ int cyfa_token_fwd(const void* q, const void* k, const float* q_norm_weight,
 /* ---------------------------------------------------------------- backward prep
  * Adjoint of cyfa_token_fwd.  dqn/dkn [B,H,TP,K] f32, dw [B,H,TP,128] f32 in;
  * dq/dk public-layout bf16, norm-weight partial sums
- * [min(ceil(B*H*TP/4), 444), K] f32 (sum the rows for the weight gradient),
+ * [min(ceil(B*H*TP/8), 444), K] f32 (sum the rows for the weight gradient),
  * dlam (write-vector part) and dbeta_h [B,H,TP] f32 out.
  * Replaces: VectorNorm.grad (ops/qk_norm.py:109-165), PhaseWriteOnly.grad
  * (ops/utils.py:589-640). */

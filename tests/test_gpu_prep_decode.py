@@ -182,7 +182,7 @@ def test_token_fwd_bwd(L, K):
     (ref_q * dqn[:, :, :T]).sum().backward()
     (ref_k * dkn[:, :, :T]).sum().backward()
     (ref_w * dw[:, :, :T].double()).sum().backward()
-    nblk = min((B * H * TP + 3) // 4, 444)  # partial rows, as the header states
+    nblk = min((B * H * TP + 7) // 8, 444)  # partial rows, as the header states
     dq = torch.empty(B, T, H, K, device="cuda", dtype=torch.bfloat16)
     dk = torch.empty_like(dq)
     dqw = torch.zeros(nblk, K, device="cuda")
