@@ -38,6 +38,7 @@ static Dims make_dims(int B, int T, int H, int K, int V) {
 struct Saved {
   float *G, *lam, *beta_h, *q_rs, *k_rs;
   __nv_bfloat16 *qn, *kn, *w, *raw, *weights, *s1, *s2;
+  __nv_bfloat16 *s1_fin, *s2_fin;  // bf16 copies of the final states (reverse boundary terms)
 };
 
 static Saved carve_saved(const Dims& d, void* base, size_t* total) {
@@ -56,6 +57,8 @@ static Saved carve_saved(const Dims& d, void* base, size_t* total) {
   s.weights = c.take<__nv_bfloat16>(n * 128);
   s.s1 = c.take<__nv_bfloat16>(size_t(d.BH) * d.NT * d.K * 128);
   s.s2 = c.take<__nv_bfloat16>(size_t(d.BH) * d.NT * 128 * d.V);
+  s.s1_fin = c.take<__nv_bfloat16>(size_t(d.BH) * d.K * 128);
+  s.s2_fin = c.take<__nv_bfloat16>(size_t(d.BH) * 128 * d.V);
   if (total) *total = c.off + 256;
   return s;
 }
@@ -186,10 +189,11 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
   // ---- pass 1: key memory (k^, w) -> raw, then the readout -> weights
   {
     ScanParams p{d.BH, d.H, d.TP, d.NT, d.K, 128, kRows2D, kRows2D, s.G, a->hk0, s.s1, a->hk,
-                 0.f, nullptr, nullptr, nullptr};
+                 0.f, s.s1_fin, nullptr};
     set_smem(state_scan_kernel<false>, kScanSmem);
     CYFA_LAUNCH("state_scan_fwd", st,
-                (state_scan_kernel<false><<<dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st>>>(m_kn, m_w, p)));
+                (state_scan_kernel<false><<<dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st>>>(
+                    m_kn, m_w, m_kn, m_kn, p)));
     if ((rc = launch_status())) return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, 128, kRows2D, 0, s.G, s.lam, a->scale, s.raw,
                     s.weights};
@@ -209,9 +213,10 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
   // ---- pass 2: value memory (weights as queries, w as keys, v) -> o
   {
     ScanParams p{d.BH, d.H, d.TP, d.NT, 128, d.V, kRows2D, kPublic4D, s.G, a->hv0, s.s2, a->hv,
-                 0.f, nullptr, nullptr, nullptr};
+                 0.f, s.s2_fin, nullptr};
     CYFA_LAUNCH("state_scan_fwd", st,
-                (state_scan_kernel<false><<<dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st>>>(m_w, m_v, p)));
+                (state_scan_kernel<false><<<dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st>>>(
+                    m_w, m_v, m_w, m_w, p)));
     if ((rc = launch_status())) return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, d.V, kPublic4D, 1, s.G, s.lam, 1.f,
                     static_cast<__nv_bfloat16*>(a->o), nullptr};
@@ -306,10 +311,12 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   // ================= pass 2 (queries = weights, keys = w, values = v)
   {
     ScanParams p{d.BH, d.H, d.TP, d.NT, 128, d.V, kRows2D, kPublic4D, s.G, g->dhv, w.h2, g->dhv0,
-                 1.f, s.s2, a->hv, w.bpart2};
+                 1.f, nullptr, w.bpart2};
+    CUtensorMap m_ff2;
+    if ((rc = tmap_2d(&m_ff2, s.s2_fin, uint64_t(d.BH) * 128, d.V, 128))) return rc;
     CYFA_LAUNCH("state_scan_bwd", st,
-                (state_scan_kernel<true><<<dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st>>>(m_weights,
-                                                                                          m_do, p)));
+                (state_scan_kernel<true><<<dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st>>>(
+                    m_weights, m_do, m_s2, m_ff2, p)));
     if ((rc = launch_status())) return rc;
     ScoresParams sp{d.BH, d.H, d.TP, d.NT, kPublic4D, kPublic4D, s.G, 1.f, w.A, w.Bp};
     if (d.V == 256) {
@@ -358,10 +365,13 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   // ================= pass 1 (queries = q^, keys = k^, values = w)
   {
     ScanParams p{d.BH, d.H, d.TP, d.NT, d.K, 128, kRows2D, kRows2D, s.G, g->dhk, w.h1, g->dhk0,
-                 a->scale, s.s1, a->hk, w.bpart1};
+                 a->scale, nullptr, w.bpart1};
+    CUtensorMap m_f1, m_ff1;
+    if ((rc = tmap_2d(&m_f1, s.s1, uint64_t(d.BH) * d.NT * d.K, 128, 128))) return rc;
+    if ((rc = tmap_2d(&m_ff1, s.s1_fin, uint64_t(d.BH) * d.K, 128, 128))) return rc;
     CYFA_LAUNCH("state_scan_bwd", st,
-                (state_scan_kernel<true><<<dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st>>>(m_qn, m_draw,
-                                                                                           p)));
+                (state_scan_kernel<true><<<dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st>>>(
+                    m_qn, m_draw, m_f1, m_ff1, p)));
     if ((rc = launch_status())) return rc;
     ScoresParams sp{d.BH, d.H, d.TP, d.NT, kRows2D, kRows2D, s.G, a->scale, w.A, w.Bp};
     if (d.K == 256) {

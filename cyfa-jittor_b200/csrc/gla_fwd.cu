@@ -73,15 +73,24 @@ struct ScanParams {
   __nv_bfloat16* hist;      // [BH, NT, DK, DV]: state entering each tile
   float* last;              // [BH, DK, DV]: final state (forward) / initial-state adjoint
   float scale;              // reverse: scale of dO
-  const __nv_bfloat16* fwd_hist;  // reverse: forward history of the same pass
-  const float* fwd_final;         // reverse: forward final state
-  float* bpart;                   // reverse: [BH, NT, nsub, 4] partial boundary terms
+  __nv_bfloat16* last_bf;   // forward: bf16 copy of the final state [BH, DK, DV], or null
+  float* bpart;             // reverse: [BH, NT, nsub, 4] partial boundary terms
 };
 
-constexpr int kScanStages = 4;
-constexpr int kScanStageBytes = 48 * 1024;  // K tile 32 KiB + V tile 16 KiB
+// Ring of the scan: forward stages hold the K tile (32 KiB) and the V tile
+// (16 KiB); reverse stages also hold the forward state S_{j+1} slice (16 KiB)
+// that the boundary term of tile j pairs with.
+template <bool REVERSE>
+struct ScanRing {
+  static constexpr int stages = REVERSE ? 3 : 4;
+  static constexpr int stage_bytes = (REVERSE ? 64 : 48) * 1024;
+};
+constexpr int kScanRingBytes = 192 * 1024;
+static_assert(ScanRing<false>::stages * ScanRing<false>::stage_bytes <= kScanRingBytes &&
+                  ScanRing<true>::stages * ScanRing<true>::stage_bytes <= kScanRingBytes,
+              "scan ring");
 // ring + 4 KiB staging per consumer warp (coalesced history traffic) + alignment
-constexpr int kScanSmem = kScanStages * kScanStageBytes + 4 * 4096 + 1024;
+constexpr int kScanSmem = kScanRingBytes + 4 * 4096 + 1024;
 constexpr int kScanBufs = 4;                // TMEM update buffers of 64 columns
 
 // OR of v over the `n` threads of named barrier `id` (every one of them gets it).
@@ -99,9 +108,10 @@ __device__ __forceinline__ bool named_bar_or(int id, int n, bool v) {
 // Chunk-state scan, warp-specialised.  One CTA owns rows dk0..dk0+127 and
 // columns dv0..dv0+63 of the state of one (b, h); 320 threads in five roles that
 // hand tiles to each other through mbarriers only:
-//   warp 8, lane 0 (producer): TMA loads of each tile's K/V operands into a ring
-//     of kScanStages stages; a stage is refilled once the UMMA of its previous
-//     tile is done;
+//   warp 8, lane 0 (producer): TMA loads of each tile's K/V operands (and, in
+//     REVERSE, the forward state slice S_{j+1}) into a ring of stages; a stage is
+//     refilled once the UMMA (and, in REVERSE, the consumers) of its previous
+//     tile are done with it;
 //   warps 4-7 (scalers): scale the tile's V rows by its gate factor in shared
 //     memory, then signal `scaled`;
 //   warp 9, lane 0 (MMA issuer): U = K^T (V o f) into one of kScanBufs TMEM
@@ -111,17 +121,24 @@ __device__ __forceinline__ bool named_bar_or(int id, int n, bool v) {
 // The updates U do not depend on the state, so producer, scalers and issuer run
 // up to kScanBufs tiles ahead of the serial recurrence.
 // REVERSE walks the tiles backwards with f = scale 2^{G_t} (adjoint scan) and
-// also forms the boundary partials <S_{j+1}, H_{j+1}>.
+// also forms the boundary partials <S_{j+1}, H_{j+1}> from the forward history
+// (map_f, rows of S_{j+1} for j + 1 < NT) or the forward final state (map_ff),
+// both bf16 and brought in by the producer with the tile's operands.
 constexpr int kScanThreads = 320;
 
 template <bool REVERSE>
 __global__ void __launch_bounds__(kScanThreads, 1)
     state_scan_kernel(const __grid_constant__ CUtensorMap map_k,
-                      const __grid_constant__ CUtensorMap map_v, ScanParams p) {
+                      const __grid_constant__ CUtensorMap map_v,
+                      const __grid_constant__ CUtensorMap map_f,
+                      const __grid_constant__ CUtensorMap map_ff, ScanParams p) {
+  constexpr int kScanStages = ScanRing<REVERSE>::stages;
+  constexpr int kScanStageBytes = ScanRing<REVERSE>::stage_bytes;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   __shared__ __align__(8) uint64_t full[kScanStages];
   __shared__ __align__(8) uint64_t scaled[kScanStages];
+  __shared__ __align__(8) uint64_t f_free[kScanStages];
   __shared__ __align__(8) uint64_t mma_done[kScanBufs];
   __shared__ __align__(8) uint64_t tmem_free[kScanBufs];
   __shared__ uint32_t tmem_base;
@@ -136,6 +153,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     for (int s = 0; s < kScanStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&scaled[s], 4);
+      mbar_init(&f_free[s], 4);
     }
     for (int b = 0; b < kScanBufs; ++b) {
       mbar_init(&mma_done[b], 1);
@@ -145,6 +163,10 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     mbar_fence_init();
     prefetch_tmap(&map_k);
     prefetch_tmap(&map_v);
+    if (REVERSE) {
+      prefetch_tmap(&map_f);
+      prefetch_tmap(&map_ff);
+    }
   }
   if (warp == 0) tmem_alloc(&tmem_base, 64 * kScanBufs);
   tc_fence_before();
@@ -163,7 +185,9 @@ __global__ void __launch_bounds__(kScanThreads, 1)
         const int s = idx % kScanStages, j = tile_of(idx);
         if (idx >= kScanStages) {
           const int prev = idx - kScanStages;  // previous tile of this stage
-          if (!mbar_wait(&mma_done[prev % kScanBufs], (prev / kScanBufs) & 1)) {
+          bool ok = mbar_wait(&mma_done[prev % kScanBufs], (prev / kScanBufs) & 1);
+          if (REVERSE && ok) ok = mbar_wait(&f_free[s], (prev / kScanStages) & 1);
+          if (!ok) {
             *abort_flag = 1;
             break;
           }
@@ -172,6 +196,12 @@ __global__ void __launch_bounds__(kScanThreads, 1)
         mbar_expect_tx(&full[s], kScanStageBytes);
         load_token_tile(st, &map_k, p.k_mode, bh, p.H, p.TP, j, dk0, 128, &full[s]);
         load_token_tile(st + 32768, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 64, &full[s]);
+        if (REVERSE) {
+          if (j + 1 < NT)
+            tma_load_2d(st + 49152, &map_f, &full[s], dv0, (bh * NT + j + 1) * p.DK + dk0);
+          else
+            tma_load_2d(st + 49152, &map_ff, &full[s], dv0, bh * p.DK + dk0);
+        }
         issued = idx + 1;
       }
       // every issued copy lands before shared memory goes away
@@ -261,10 +291,8 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     const uint32_t scratch = smem_u32(smem) + kScanStages * kScanStageBytes + warp * 4096;
     const int nsub = gridDim.y * gridDim.z, sub = blockIdx.y * gridDim.z + blockIdx.z;
     bool ok = true;
-    // loads one iteration ahead: the gate total of the next tile and (REVERSE)
-    // the forward state rows that the next boundary term pairs with
+    // the gate total of the next tile is loaded one iteration ahead
     float gl_next = NT > 0 ? Gbh[size_t(tile_of(0)) * 128 + 127] : 0.f;
-    uint4 fwd_next[8];
     for (int idx = 0; idx < NT; ++idx) {
       const int j = tile_of(idx), b = idx % kScanBufs;
       const float gl = gl_next;
@@ -281,38 +309,29 @@ __global__ void __launch_bounds__(kScanThreads, 1)
                            p.hist + ((size_t(bh) * NT + j) * p.DK + dk0 + warp * 32) * p.DV + dv0,
                            p.DV);
       }
+      bool got = __all_sync(0xffffffffu, mbar_wait(&mma_done[b], (idx / kScanBufs) & 1));
       if constexpr (REVERSE) {
-        // <S_{j+1}, H_{j+1}> over this CTA's slice (S_{j+1} from the forward pass)
+        // <S_{j+1}, H_{j+1}> over this CTA's slice; S holds H_{j+1} until the update
+        const int s = idx % kScanStages;
+        got = got && __all_sync(0xffffffffu, mbar_wait(&full[s], (idx / kScanStages) & 1));
         float dot = 0.f;
-        if (j + 1 < NT) {
+        if (got) {
+          const uint32_t fb = smem_u32(smem + s * kScanStageBytes + 49152);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             float x[8];
-            unpack_bf16x8(fwd_next[c], x);
+            unpack_bf16x8(ld_shared_v4(fb + sw128(tid, c)), x);
 #pragma unroll
             for (int e = 0; e < 8; ++e) dot += x[e] * S[8 * c + e];
-          }
-        } else {
-          const float4* src = reinterpret_cast<const float4*>(p.fwd_final + row_off);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float4 x = src[i];
-            dot += x.x * S[4 * i] + x.y * S[4 * i + 1] + x.z * S[4 * i + 2] + x.w * S[4 * i + 3];
           }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
         // one partial per warp: bpart[bh][j][sub][warp]
-        if (lane == 0) p.bpart[((size_t(bh) * NT + j) * nsub + sub) * 4 + warp] = dot;
-        // S_{j'+1} of the next tile j' = j - 1 is the forward state entering tile j
-        if (idx + 1 < NT) {
-          const uint4* src = reinterpret_cast<const uint4*>(
-              p.fwd_hist + ((size_t(bh) * NT + j) * p.DK + dk0 + tid) * p.DV + dv0);
-#pragma unroll
-          for (int c = 0; c < 8; ++c) fwd_next[c] = src[c];
-        }
+        if (lane == 0 && got) p.bpart[((size_t(bh) * NT + j) * nsub + sub) * 4 + warp] = dot;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&f_free[s]);
       }
-      const bool got = __all_sync(0xffffffffu, mbar_wait(&mma_done[b], (idx / kScanBufs) & 1));
       tc_fence_after();
       if (got) {
         const float gamma = exp2f(gl);
@@ -339,6 +358,16 @@ __global__ void __launch_bounds__(kScanThreads, 1)
 #pragma unroll
       for (int i = 0; i < 16; ++i)
         dst[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
+    }
+    if (!REVERSE && ok && p.last_bf) {
+      uint4 packed[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        packed[c] = make_uint4(pack_bf16(S[8 * c], S[8 * c + 1]), pack_bf16(S[8 * c + 2], S[8 * c + 3]),
+                               pack_bf16(S[8 * c + 4], S[8 * c + 5]),
+                               pack_bf16(S[8 * c + 6], S[8 * c + 7]));
+      warp_store_rows128(scratch, packed,
+                         p.last_bf + (size_t(bh) * p.DK + dk0 + warp * 32) * p.DV + dv0, p.DV);
     }
   }
   tc_fence_before();
