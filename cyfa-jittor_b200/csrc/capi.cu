@@ -85,6 +85,29 @@ static void prof_end(const char* name, cudaEvent_t start, cudaStream_t s) {
     g_launches.fetch_add(1, std::memory_order_relaxed); \
   } while (0)
 
+// Kernel launch with programmatic stream serialisation: the kernel may start
+// while the previous kernel on the stream finishes (each kernel of this library
+// waits in pdl_wait() before touching global memory), so launch latency and the
+// prologue (barrier setup, TMEM allocation) overlap the previous kernel's tail.
+// cyfa_set_pdl(0) turns it off (plain stream order).
+static std::atomic<int> g_pdl{1};
+
+template <typename... KArgs, typename... Args>
+static void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t stream, Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = g_pdl.load(std::memory_order_relaxed);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point, so the
@@ -163,8 +186,8 @@ static int token_fwd_launch(const void* q, const void* k, const float* q_norm_we
   const size_t rows = size_t(B) * H * TP;
   const dim3 grid(unsigned(token_fwd_blocks(rows)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (K == 256) CYFA_LAUNCH("token_fwd", s, token_fwd_kernel<256><<<grid, 256, 0, s>>>(p));
-  else CYFA_LAUNCH("token_fwd", s, token_fwd_kernel<128><<<grid, 256, 0, s>>>(p));
+  if (K == 256) CYFA_LAUNCH("token_fwd", s, launch_k(token_fwd_kernel<256>, grid, 256, 0, s, p));
+  else CYFA_LAUNCH("token_fwd", s, launch_k(token_fwd_kernel<128>, grid, 256, 0, s, p));
   return launch_status();
 }
 
@@ -198,12 +221,12 @@ static int token_bwd_launch(const void* q, const void* k, const float* q_norm_we
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (grads_bf16) {
     if (K == 256)
-      CYFA_LAUNCH("token_bwd", s, (token_bwd_kernel<256, __nv_bfloat16><<<grid, 256, 0, s>>>(p)));
+      CYFA_LAUNCH("token_bwd", s, (launch_k(token_bwd_kernel<256, __nv_bfloat16>, grid, 256, 0, s, p)));
     else
-      CYFA_LAUNCH("token_bwd", s, (token_bwd_kernel<128, __nv_bfloat16><<<grid, 256, 0, s>>>(p)));
+      CYFA_LAUNCH("token_bwd", s, (launch_k(token_bwd_kernel<128, __nv_bfloat16>, grid, 256, 0, s, p)));
   } else {
-    if (K == 256) CYFA_LAUNCH("token_bwd", s, (token_bwd_kernel<256, float><<<grid, 256, 0, s>>>(p)));
-    else CYFA_LAUNCH("token_bwd", s, (token_bwd_kernel<128, float><<<grid, 256, 0, s>>>(p)));
+    if (K == 256) CYFA_LAUNCH("token_bwd", s, (launch_k(token_bwd_kernel<256, float>, grid, 256, 0, s, p)));
+    else CYFA_LAUNCH("token_bwd", s, (launch_k(token_bwd_kernel<128, float>, grid, 256, 0, s, p)));
   }
   return launch_status();
 }
@@ -231,6 +254,8 @@ const char* cyfa_strerror(int status) {
 }
 
 long long cyfa_launch_count(void) { return g_launches.load(); }
+
+int cyfa_set_pdl(int on) { return g_pdl.exchange(on != 0 ? 1 : 0); }
 
 int cyfa_profile_enable(int on) {
   std::lock_guard<std::mutex> lk(g_prof_mu);
@@ -313,7 +338,7 @@ int cyfa_decode_step(const void* q, const void* k, const void* v, const float* g
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const dim3 grid(B * H);
 #define CYFA_DECODE(T, KK, VV) \
-  CYFA_LAUNCH("decode_step", s, (decode_step_kernel<T, KK, VV><<<grid, 256, 0, s>>>(p)))
+  CYFA_LAUNCH("decode_step", s, (launch_k(decode_step_kernel<T, KK, VV>, grid, 256, 0, s, p)))
   if (dtype == 0) {
     if (K == 256 && V == 256) CYFA_DECODE(__nv_bfloat16, 256, 256);
     else if (K == 128 && V == 128) CYFA_DECODE(__nv_bfloat16, 128, 128);
@@ -337,7 +362,7 @@ int cyfa_gates_fwd(const float* g, const float* delta, const float* beta, const 
   const int TP = (T + 127) / 128 * 128;
   GatesParams p{g, delta, beta, clock0, G, lam, beta_h, clock_out, B, T, H, TP};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  CYFA_LAUNCH("gates_fwd", st, gates_fwd_kernel<<<B * H, 1024, 0, st>>>(p));
+  CYFA_LAUNCH("gates_fwd", st, launch_k(gates_fwd_kernel, B * H, 1024, 0, st, p));
   return launch_status();
 }
 
@@ -369,7 +394,7 @@ int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h, con
   GatesBwdParams p{dG, dlam, nullptr, nullptr, nullptr, 0, 0, dbeta_h, dclock, dg, ddelta,
                    dbeta, dclock0, B, T, H, TP};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  CYFA_LAUNCH("gates_bwd", st, gates_bwd_kernel<<<B * H, 1024, 0, st>>>(p));
+  CYFA_LAUNCH("gates_bwd", st, launch_k(gates_bwd_kernel, B * H, 1024, 0, st, p));
   return launch_status();
 }
 

@@ -192,7 +192,7 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
                  0.f, s.s1_fin, nullptr};
     set_smem(state_scan_kernel<false>, kScanSmem);
     CYFA_LAUNCH("state_scan_fwd", st,
-                (state_scan_kernel<false><<<dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st>>>(
+                (launch_k(state_scan_kernel<false>, dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st, 
                     m_kn, m_w, m_kn, m_kn, p)));
     if ((rc = launch_status())) return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, 128, kRows2D, 0, s.G, s.lam, a->scale, s.raw,
@@ -200,12 +200,12 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
     if (d.K == 256) {
       set_smem(tile_fwd_kernel<256, true>, tile_fwd_smem<256>());
       CYFA_LAUNCH("tile_fwd_readout", st,
-                  (tile_fwd_kernel<256, true><<<dim3(d.BH * d.NT, 1), 256, tile_fwd_smem<256>(), st>>>(
+                  (launch_k(tile_fwd_kernel<256, true>, dim3(d.BH * d.NT, 1), 256, tile_fwd_smem<256>(), st, 
                       m_qn, m_kn, m_w, m_s1, m_tab, t)));
     } else {
       set_smem(tile_fwd_kernel<128, true>, tile_fwd_smem<128>());
       CYFA_LAUNCH("tile_fwd_readout", st,
-                  (tile_fwd_kernel<128, true><<<dim3(d.BH * d.NT, 1), 256, tile_fwd_smem<128>(), st>>>(
+                  (launch_k(tile_fwd_kernel<128, true>, dim3(d.BH * d.NT, 1), 256, tile_fwd_smem<128>(), st, 
                       m_qn, m_kn, m_w, m_s1, m_tab, t)));
     }
     if ((rc = launch_status())) return rc;
@@ -215,15 +215,14 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
     ScanParams p{d.BH, d.H, d.TP, d.NT, 128, d.V, kRows2D, kPublic4D, s.G, a->hv0, s.s2, a->hv,
                  0.f, s.s2_fin, nullptr};
     CYFA_LAUNCH("state_scan_fwd", st,
-                (state_scan_kernel<false><<<dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st>>>(
+                (launch_k(state_scan_kernel<false>, dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st, 
                     m_w, m_v, m_w, m_w, p)));
     if ((rc = launch_status())) return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, d.V, kPublic4D, 1, s.G, s.lam, 1.f,
                     static_cast<__nv_bfloat16*>(a->o), nullptr};
     set_smem(tile_fwd_kernel<128, false>, tile_fwd_smem<128>());
     CYFA_LAUNCH("tile_fwd", st,
-                (tile_fwd_kernel<128, false><<<dim3(d.BH * d.NT, d.V / 128), 256, tile_fwd_smem<128>(),
-                                               st>>>(m_weights, m_w, m_v, m_s2, m_tab, t)));
+                (launch_k(tile_fwd_kernel<128, false>, dim3(d.BH * d.NT, d.V / 128), 256, tile_fwd_smem<128>(), st, m_weights, m_w, m_v, m_s2, m_tab, t)));
     if ((rc = launch_status())) return rc;
   }
   return kOk;
@@ -302,7 +301,7 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                   const CUtensorMap& y2, DualParams p) {
     const unsigned ntile = unsigned(d.BH * d.NT), grid = ntile < 148 ? ntile : 148;  // persistent
     CYFA_LAUNCH("dual_gemm", st,
-                (dual_gemm_kernel<<<grid, kDualThreads, kDualSmem, st>>>(x1, y1, x2, y2, p)));
+                (launch_k(dual_gemm_kernel, grid, kDualThreads, kDualSmem, st, x1, y1, x2, y2, p)));
     return launch_status();
   };
   // boundary partials per tile: one per (CTA slice, warp)
@@ -315,19 +314,19 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     CUtensorMap m_ff2;
     if ((rc = tmap_2d(&m_ff2, s.s2_fin, uint64_t(d.BH) * 128, d.V, 128))) return rc;
     CYFA_LAUNCH("state_scan_bwd", st,
-                (state_scan_kernel<true><<<dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st>>>(
+                (launch_k(state_scan_kernel<true>, dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st, 
                     m_weights, m_do, m_s2, m_ff2, p)));
     if ((rc = launch_status())) return rc;
     ScoresParams sp{d.BH, d.H, d.TP, d.NT, kPublic4D, kPublic4D, s.G, 1.f, w.A, w.Bp};
     if (d.V == 256) {
       set_smem(tile_scores_kernel<128, 256>, scores_smem<128, 256>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<128, 256><<<persist, 256, scores_smem<128, 256>(), st>>>(
+                  (launch_k(tile_scores_kernel<128, 256>, persist, 256, scores_smem<128, 256>(), st, 
                       m_weights, m_w, m_do, m_v, sp)));
     } else {
       set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<128, 128><<<persist, 256, scores_smem<128, 128>(), st>>>(
+                  (launch_k(tile_scores_kernel<128, 128>, persist, 256, scores_smem<128, 128>(), st, 
                       m_weights, m_w, m_do, m_v, sp)));
     }
     if ((rc = launch_status())) return rc;
@@ -354,11 +353,11 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     if ((rc = tmap_2d(&m_dwt, w.dweights, rows, 128, 128))) return rc;
     set_smem(readout_bwd_kernel, kReadoutBwdSmem);
     CYFA_LAUNCH("readout_bwd", st,
-                (readout_bwd_kernel<<<d.H * per_head, 256, kReadoutBwdSmem, st>>>(m_tab, m_raw,
+                (launch_k(readout_bwd_kernel, d.H * per_head, 256, kReadoutBwdSmem, st, m_tab, m_raw,
                                                                                   m_dwt, rp)));
     if ((rc = launch_status())) return rc;
     CYFA_LAUNCH("dtable_reduce", st,
-                (dtable_reduce_kernel<<<dim3(d.H, 128), 128, 0, st>>>(w.dtab_part, g->dtable,
+                (launch_k(dtable_reduce_kernel, dim3(d.H, 128), 128, 0, st, w.dtab_part, g->dtable,
                                                                       per_head)));
     if ((rc = launch_status())) return rc;
   }
@@ -370,19 +369,19 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     if ((rc = tmap_2d(&m_f1, s.s1, uint64_t(d.BH) * d.NT * d.K, 128, 128))) return rc;
     if ((rc = tmap_2d(&m_ff1, s.s1_fin, uint64_t(d.BH) * d.K, 128, 128))) return rc;
     CYFA_LAUNCH("state_scan_bwd", st,
-                (state_scan_kernel<true><<<dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st>>>(
+                (launch_k(state_scan_kernel<true>, dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st, 
                     m_qn, m_draw, m_f1, m_ff1, p)));
     if ((rc = launch_status())) return rc;
     ScoresParams sp{d.BH, d.H, d.TP, d.NT, kRows2D, kRows2D, s.G, a->scale, w.A, w.Bp};
     if (d.K == 256) {
       set_smem(tile_scores_kernel<256, 128>, scores_smem<256, 128>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<256, 128><<<persist, 256, scores_smem<256, 128>(), st>>>(
+                  (launch_k(tile_scores_kernel<256, 128>, persist, 256, scores_smem<256, 128>(), st, 
                       m_qn, m_kn, m_draw, m_w, sp)));
     } else {
       set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
       CYFA_LAUNCH("tile_scores", st,
-                  (tile_scores_kernel<128, 128><<<persist, 256, scores_smem<128, 128>(), st>>>(
+                  (launch_k(tile_scores_kernel<128, 128>, persist, 256, scores_smem<128, 128>(), st, 
                       m_qn, m_kn, m_draw, m_w, sp)));
     }
     if ((rc = launch_status())) return rc;
@@ -409,12 +408,13 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   if (rc) return rc;
   const int nblk = token_bwd_blocks(rows);
   CYFA_LAUNCH("column_sum", st,
-              (column_sum_kernel<<<dim3((d.K + 31) / 32, 2), 1024, 0, st>>>(
-                  w.dqw_part, g->dq_norm_weight, nblk, d.K, w.dkw_part, g->dk_norm_weight)));
+              (launch_k(column_sum_kernel, dim3((d.K + 31) / 32, 2), 1024, 0, st, w.dqw_part,
+                        g->dq_norm_weight, nblk, d.K, w.dkw_part, g->dk_norm_weight, 0x7fffffff,
+                        nullptr)));
   if ((rc = launch_status())) return rc;
   GatesBwdParams gp{w.dG, w.dlam_w, w.dlam_r, w.bpart1, w.bpart2, nsub1, nsub2, w.dbeta_h,
                     g->dclock, g->dg, g->ddelta, g->dbeta, g->dclock0, d.B, d.T, d.H, d.TP};
-  CYFA_LAUNCH("gates_bwd", st, (gates_bwd_kernel<<<d.BH, 1024, 0, st>>>(gp)));
+  CYFA_LAUNCH("gates_bwd", st, (launch_k(gates_bwd_kernel, d.BH, 1024, 0, st, gp)));
   return launch_status();
 }
 

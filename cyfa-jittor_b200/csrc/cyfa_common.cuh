@@ -37,6 +37,17 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Programmatic dependent launch.  Every kernel of this library calls pdl_wait()
+// before its first global-memory access (it returns once the grids this launch
+// depends on have completed and their writes are visible; without a
+// programmatic dependency it returns at once) and pdl_trigger() once it holds
+// its on-chip resources (after any TMEM allocation), which lets the next
+// kernel in the stream launch and run its own prologue early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -91,6 +91,8 @@ __device__ __forceinline__ float block_max_256(float x, float* red) {
 
 template <typename Tin, int K, int V>
 __global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int M = 128;
   const int bh = blockIdx.x;
   const int h = bh % p.H;

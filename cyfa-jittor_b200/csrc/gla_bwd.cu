@@ -82,6 +82,8 @@ __global__ void __launch_bounds__(256, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = tmem_base;
   // warp w: TMEM lane quadrant (w & 3) = token rows, column half (w >> 2); it
   // writes both A (q.k) and B' (dO.v) there, sharing each decay factor
@@ -256,6 +258,8 @@ __global__ void __launch_bounds__(kDualThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = tmem_base;
 
   if (warp == 8) {
@@ -508,6 +512,8 @@ __global__ void __launch_bounds__(256, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = tmem_base;
   const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
   const uint32_t sTab = smem_u32(smem), sZ = sTab + 32768, sDC = sTab + 65536,
@@ -715,6 +721,8 @@ __global__ void __launch_bounds__(256, 1)
 // dtab[h][r][m] = sum_{s < per_head} part[h * per_head + s][r][m].
 __global__ void __launch_bounds__(128) dtable_reduce_kernel(const float* part, float* dtab,
                                                             int per_head) {
+  pdl_wait();
+  pdl_trigger();
   const int h = blockIdx.x, r = blockIdx.y, m = threadIdx.x;
   float s0 = 0.f, s1 = 0.f;
   int k = 0;
@@ -735,6 +743,8 @@ __global__ void __launch_bounds__(1024) column_sum_kernel(const float* part, flo
                                                           int split = 0x7fffffff,
                                                           float* out_hi = nullptr) {
   __shared__ float acc[32][33];
+  pdl_wait();
+  pdl_trigger();
   if (blockIdx.y == 1) {  // second (part, out) pair
     part = part2;
     out = out2;

@@ -172,6 +172,8 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();
+  pdl_trigger();
   const uint32_t tmem = tmem_base;
   auto tile_of = [&](int idx) { return REVERSE ? NT - 1 - idx : idx; };
   const float* Gbh = p.G + size_t(bh) * p.TP;
@@ -429,10 +431,12 @@ __global__ void __launch_bounds__(256, 1)
     mbar_fence_init();
   }
   if (warp == 0) tmem_alloc(&tmem_base, 512);
+  pdl_wait();
   if (tid < 128) Gs[tid] = p.G[size_t(bh) * p.TP + j * 128 + tid];
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_trigger();
   const uint32_t tmem = tmem_base;
   const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
   const uint32_t sQ = smem_u32(smem + kQ), sK = smem_u32(smem + kK), sS = smem_u32(smem + kS),

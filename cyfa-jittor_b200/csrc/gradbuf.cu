@@ -33,6 +33,8 @@ __device__ __forceinline__ int bucket_piece(const BucketArgs& a, int b) {
 
 template <bool GATHER>
 __global__ void __launch_bounds__(256) bucket_copy_kernel(const __grid_constant__ BucketArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int i = bucket_piece(a, blockIdx.x);
   const long long e0 = (long long)(blockIdx.x - a.blk_prefix[i]) * kBucketChunk + threadIdx.x * 8;
   const long long n = a.n[i];
@@ -120,9 +122,9 @@ static int bucket_launch(const cyfa_bucket_piece* pieces, int count, float* flat
     a.blk_prefix[a.count] = static_cast<int>(blocks);
     if (blocks == 0) continue;
     if (gather) {
-      CYFA_LAUNCH("bucket_gather", st, (bucket_copy_kernel<true><<<unsigned(blocks), 256, 0, st>>>(a)));
+      CYFA_LAUNCH("bucket_gather", st, (launch_k(bucket_copy_kernel<true>, unsigned(blocks), 256, 0, st, a)));
     } else {
-      CYFA_LAUNCH("bucket_scatter", st, (bucket_copy_kernel<false><<<unsigned(blocks), 256, 0, st>>>(a)));
+      CYFA_LAUNCH("bucket_scatter", st, (launch_k(bucket_copy_kernel<false>, unsigned(blocks), 256, 0, st, a)));
     }
     const int s = launch_status();
     if (s != kOk) return s;

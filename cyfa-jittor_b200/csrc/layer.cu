@@ -55,6 +55,8 @@ constexpr int kConvUnrollF = 8;
 
 template <int W>
 __global__ void __launch_bounds__(256) short_conv_fwd_kernel(ConvParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int WM = W > 1 ? W - 1 : 1;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int c0 = blockIdx.x * 128 + lane * 4, b = blockIdx.z;
@@ -134,6 +136,8 @@ __device__ __forceinline__ void unpack4(uint2 r, float* f) {
 
 template <int W>
 __global__ void __launch_bounds__(256, 2) short_conv_bwd_kernel(ConvParams p) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[kConvWarps][128 * (W + 1)];
   constexpr int WM = W > 1 ? W - 1 : 1;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -282,6 +286,8 @@ __device__ __forceinline__ float softplus_f(float x) {
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
 
 __global__ void __launch_bounds__(256) gate_act_fwd_kernel(GateActParams p) {
+  pdl_wait();
+  pdl_trigger();
   const size_t i = size_t(blockIdx.x) * 256 + threadIdx.x;
   if (i >= size_t(p.rows) * p.H) return;
   const size_t r = i / p.H;
@@ -294,6 +300,8 @@ __global__ void __launch_bounds__(256) gate_act_fwd_kernel(GateActParams p) {
 
 // One thread per (row, head); grid-strided; per-block fixed-order partial sums.
 __global__ void __launch_bounds__(256) gate_act_bwd_kernel(GateActParams p) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[256][4];
   const int h = threadIdx.x % p.H;  // H divides 256 (checked on the host)
   float sA = 0.f, sdt = 0.f, sb = 0.f, sd = 0.f;
@@ -358,6 +366,8 @@ struct GatedNormParams {
 // every row the warp visits) stays in registers.  D = 32 * E.
 template <int E>
 __global__ void __launch_bounds__(256, 3) gated_norm_fwd_kernel(GatedNormParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int D = 32 * E;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const size_t stride = size_t(gridDim.x) * 8;
@@ -413,6 +423,8 @@ inline int norm_fwd_blocks(int rows, int H) {
 // x, dy and the gate in place.
 template <int E>
 __global__ void __launch_bounds__(256, 3) gated_norm_bwd_kernel(GatedNormParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int D = 32 * E;
   __shared__ float red[8][D];
   __shared__ float red_b[8][D];
@@ -479,6 +491,8 @@ __global__ void __launch_bounds__(256, 3) gated_norm_bwd_kernel(GatedNormParams 
 // Fixed-order sums of the short-conv partial rows into dw [C, W] and dbias [C].
 __global__ void __launch_bounds__(256) conv_param_sum_kernel(const float* part, int rows, int C,
                                                              int W, float* dw, float* dbias) {
+  pdl_wait();
+  pdl_trigger();
   const int cols = C * (W + 1);
   const int idx = blockIdx.x * 256 + threadIdx.x;
   if (idx >= cols) return;
@@ -504,6 +518,8 @@ __global__ void __launch_bounds__(256) conv_param_sum_kernel(const float* part, 
 __global__ void __launch_bounds__(1024) strided_column_sum_kernel(const float* part, float* out,
                                                                   int rows, int cols,
                                                                   int row_stride) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[1024];
   for (int c = 0; c < cols; ++c) {
     float s = 0.f;
@@ -524,6 +540,8 @@ __global__ void __launch_bounds__(1024) strided_column_sum_kernel(const float* p
 __global__ void __launch_bounds__(1024) gate_param_sum_kernel(const float* part, int rows, int H,
                                                               float* dA, float* ddt, float* dbb,
                                                               float* ddb) {
+  pdl_wait();
+  pdl_trigger();
   // one warp per column; lanes stride the rows, then a fixed shuffle tree
   float* outs[4] = {dA, ddt, dbb, ddb};
   const int lane = threadIdx.x & 31;

@@ -41,10 +41,10 @@ int cyfa_short_conv_fwd(const void* x, long long x_stride, const void* cache, co
   const dim3 grid((C + 127) / 128, (T + kConvWarps * kConvRun - 1) / (kConvWarps * kConvRun), B);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (W) {
-    case 1: CYFA_LAUNCH("short_conv_fwd", s, short_conv_fwd_kernel<1><<<grid, 256, 0, s>>>(p)); break;
-    case 2: CYFA_LAUNCH("short_conv_fwd", s, short_conv_fwd_kernel<2><<<grid, 256, 0, s>>>(p)); break;
-    case 3: CYFA_LAUNCH("short_conv_fwd", s, short_conv_fwd_kernel<3><<<grid, 256, 0, s>>>(p)); break;
-    default: CYFA_LAUNCH("short_conv_fwd", s, short_conv_fwd_kernel<4><<<grid, 256, 0, s>>>(p)); break;
+    case 1: CYFA_LAUNCH("short_conv_fwd", s, launch_k(short_conv_fwd_kernel<1>, grid, 256, 0, s, p)); break;
+    case 2: CYFA_LAUNCH("short_conv_fwd", s, launch_k(short_conv_fwd_kernel<2>, grid, 256, 0, s, p)); break;
+    case 3: CYFA_LAUNCH("short_conv_fwd", s, launch_k(short_conv_fwd_kernel<3>, grid, 256, 0, s, p)); break;
+    default: CYFA_LAUNCH("short_conv_fwd", s, launch_k(short_conv_fwd_kernel<4>, grid, 256, 0, s, p)); break;
   }
   return launch_status();
 }
@@ -65,17 +65,17 @@ int cyfa_short_conv_bwd(const void* x, long long x_stride, const float* w, const
   const dim3 grid((C + 127) / 128, conv_bwd_rows(B, T));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (W) {
-    case 1: CYFA_LAUNCH("short_conv_bwd", s, (short_conv_bwd_kernel<1><<<grid, 256, 0, s>>>(p))); break;
-    case 2: CYFA_LAUNCH("short_conv_bwd", s, (short_conv_bwd_kernel<2><<<grid, 256, 0, s>>>(p))); break;
-    case 3: CYFA_LAUNCH("short_conv_bwd", s, (short_conv_bwd_kernel<3><<<grid, 256, 0, s>>>(p))); break;
-    default: CYFA_LAUNCH("short_conv_bwd", s, (short_conv_bwd_kernel<4><<<grid, 256, 0, s>>>(p))); break;
+    case 1: CYFA_LAUNCH("short_conv_bwd", s, (launch_k(short_conv_bwd_kernel<1>, grid, 256, 0, s, p))); break;
+    case 2: CYFA_LAUNCH("short_conv_bwd", s, (launch_k(short_conv_bwd_kernel<2>, grid, 256, 0, s, p))); break;
+    case 3: CYFA_LAUNCH("short_conv_bwd", s, (launch_k(short_conv_bwd_kernel<3>, grid, 256, 0, s, p))); break;
+    default: CYFA_LAUNCH("short_conv_bwd", s, (launch_k(short_conv_bwd_kernel<4>, grid, 256, 0, s, p))); break;
   }
   int rc = launch_status();
   if (rc) return rc;
   // reduce the partial rows: columns are [c][0..W-1] = dw, [c][W] = dbias
   const int rows = conv_bwd_rows(B, T), cols = C * (W + 1);
   CYFA_LAUNCH("conv_param_sum", s,
-              (conv_param_sum_kernel<<<(cols + 255) / 256, 256, 0, s>>>(part, rows, C, W, dw,
+              (launch_k(conv_param_sum_kernel, (cols + 255) / 256, 256, 0, s, part, rows, C, W, dw,
                                                                         dbias)));
   return launch_status();
 }
@@ -96,7 +96,7 @@ int cyfa_gate_act_fwd(const void* a, long long a_stride, const void* b, long lon
   const long long n = (long long)rows * H;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CYFA_LAUNCH("gate_act_fwd", s,
-              (gate_act_fwd_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(p)));
+              (launch_k(gate_act_fwd_kernel, unsigned((n + 255) / 256), 256, 0, s, p)));
   return launch_status();
 }
 
@@ -128,12 +128,12 @@ int cyfa_gate_act_bwd(const void* a, long long a_stride, const void* b, long lon
                   dd_stride, part, rows, H};
   const int nblk = gate_bwd_blocks((long long)rows * H);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  CYFA_LAUNCH("gate_act_bwd", s, (gate_act_bwd_kernel<<<nblk, 256, 0, s>>>(p)));
+  CYFA_LAUNCH("gate_act_bwd", s, (launch_k(gate_act_bwd_kernel, nblk, 256, 0, s, p)));
   int rc = launch_status();
   if (rc) return rc;
   // partial columns: dA_log | ddt_bias | db_bias | dd_bias, each H wide
   CYFA_LAUNCH("column_sum", s,
-              (gate_param_sum_kernel<<<1, 1024, 0, s>>>(part, nblk, H, dA_log, ddt_bias, db_bias,
+              (launch_k(gate_param_sum_kernel, 1, 1024, 0, s, part, nblk, H, dA_log, ddt_bias, db_bias,
                                                         dd_bias)));
   return launch_status();
 }
@@ -149,8 +149,8 @@ int cyfa_gated_norm_fwd(const void* x, const void* gate, const float* w, float e
                     nullptr, rows};
   const unsigned grid = unsigned(norm_fwd_blocks(rows, 1));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (D == 256) CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<8><<<grid, 256, 0, s>>>(p)));
-  else CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<4><<<grid, 256, 0, s>>>(p)));
+  if (D == 256) CYFA_LAUNCH("gated_norm_fwd", s, (launch_k(gated_norm_fwd_kernel<8>, grid, 256, 0, s, p)));
+  else CYFA_LAUNCH("gated_norm_fwd", s, (launch_k(gated_norm_fwd_kernel<4>, grid, 256, 0, s, p)));
   return launch_status();
 }
 
@@ -173,12 +173,13 @@ int cyfa_gated_norm_bwd(const void* x, const void* gate, const float* w, float s
                     static_cast<__nv_bfloat16*>(dgate), part, rows};
   const int nblk = norm_bwd_blocks(rows);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (D == 256) CYFA_LAUNCH("gated_norm_bwd", s, (gated_norm_bwd_kernel<8><<<nblk, 256, 0, s>>>(p)));
-  else CYFA_LAUNCH("gated_norm_bwd", s, (gated_norm_bwd_kernel<4><<<nblk, 256, 0, s>>>(p)));
+  if (D == 256) CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_kernel<8>, nblk, 256, 0, s, p)));
+  else CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_kernel<4>, nblk, 256, 0, s, p)));
   int rc = launch_status();
   if (rc) return rc;
   CYFA_LAUNCH("column_sum", s,
-              (column_sum_kernel<<<(D + 31) / 32, 1024, 0, s>>>(part, dw, nblk, D)));
+              (launch_k(column_sum_kernel, (D + 31) / 32, 1024, 0, s, part, dw, nblk, D, nullptr,
+                        nullptr, 0x7fffffff, nullptr)));
   return launch_status();
 }
 
@@ -195,8 +196,8 @@ int cyfa_gated_norm_bias_fwd(const void* x, const void* gate, const void* gate_b
                     nullptr, rows, static_cast<const __nv_bfloat16*>(gate_bias), H, 0};
   const unsigned grid = unsigned(norm_fwd_blocks(rows, H));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (D == 256) CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<8><<<grid, 256, 0, s>>>(p)));
-  else CYFA_LAUNCH("gated_norm_fwd", s, (gated_norm_fwd_kernel<4><<<grid, 256, 0, s>>>(p)));
+  if (D == 256) CYFA_LAUNCH("gated_norm_fwd", s, (launch_k(gated_norm_fwd_kernel<8>, grid, 256, 0, s, p)));
+  else CYFA_LAUNCH("gated_norm_fwd", s, (launch_k(gated_norm_fwd_kernel<4>, grid, 256, 0, s, p)));
   return launch_status();
 }
 
@@ -233,13 +234,13 @@ int cyfa_gated_norm_bias_bwd(const void* x, const void* gate, const void* gate_b
                     static_cast<const __nv_bfloat16*>(gate_bias), H, cols};
   const int nblk = norm_bias_bwd_blocks(rows, H);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (D == 256) CYFA_LAUNCH("gated_norm_bwd", s, (gated_norm_bwd_kernel<8><<<nblk, 256, 0, s>>>(p)));
-  else CYFA_LAUNCH("gated_norm_bwd", s, (gated_norm_bwd_kernel<4><<<nblk, 256, 0, s>>>(p)));
+  if (D == 256) CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_kernel<8>, nblk, 256, 0, s, p)));
+  else CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_kernel<4>, nblk, 256, 0, s, p)));
   int rc = launch_status();
   if (rc) return rc;
   CYFA_LAUNCH("column_sum", s,
-              (column_sum_kernel<<<(cols + 31) / 32, 1024, 0, s>>>(part, dw, nblk, cols, nullptr,
-                                                                  nullptr, D, dgate_bias)));
+              (launch_k(column_sum_kernel, (cols + 31) / 32, 1024, 0, s, part, dw, nblk, cols,
+                        nullptr, nullptr, D, dgate_bias)));
   return launch_status();
 }
 

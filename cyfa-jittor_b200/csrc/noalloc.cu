@@ -69,13 +69,14 @@ int cyfa_gated_norm_bwd_static(const void* x, const void* gate, const float* w, 
                     static_cast<__nv_bfloat16*>(dgate), part, rows};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (D == 256)
-    CYFA_LAUNCH("gated_norm_bwd", s, (gated_norm_bwd_kernel<8><<<nblk, 256, 0, s>>>(p)));
+    CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_kernel<8>, nblk, 256, 0, s, p)));
   else
-    CYFA_LAUNCH("gated_norm_bwd", s, (gated_norm_bwd_kernel<4><<<nblk, 256, 0, s>>>(p)));
+    CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_kernel<4>, nblk, 256, 0, s, p)));
   int rc = launch_status();
   if (rc) return rc;
   CYFA_LAUNCH("column_sum", s,
-              (column_sum_kernel<<<(D + 31) / 32, 1024, 0, s>>>(part, dw, nblk, D)));
+              (launch_k(column_sum_kernel, (D + 31) / 32, 1024, 0, s, part, dw, nblk, D, nullptr,
+                        nullptr, 0x7fffffff, nullptr)));
   return launch_status();
 }
 

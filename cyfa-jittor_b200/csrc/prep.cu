@@ -107,6 +107,8 @@ __device__ __forceinline__ ScanPair scan1024(float x, float* wsum, float* total)
 }
 
 __global__ void __launch_bounds__(1024) gates_fwd_kernel(GatesParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
   __shared__ float wsum[32];
   float clock = p.clock0 ? p.clock0[bh] : 0.f;
@@ -154,6 +156,8 @@ struct TokenFwdParams {
 // both rows issued before any math); the norm weights stay in registers.
 template <int K>
 __global__ void __launch_bounds__(256) token_fwd_kernel(TokenFwdParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int E = K / 32;  // elements per lane (8 for K=256, 4 for K=128)
   const int lane = threadIdx.x & 31;
   const size_t rows = size_t(p.B) * p.H * p.TP;
@@ -326,6 +330,8 @@ struct RawVec {
 // partial matrices have gridDim.x rows.
 template <int K, typename GT>
 __global__ void __launch_bounds__(256, 3) token_bwd_kernel(TokenBwdParams p) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int E = K / 32;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   __shared__ float wts[2][K];
@@ -462,6 +468,8 @@ struct GatesBwdParams {
 };
 
 __global__ void __launch_bounds__(1024) gates_bwd_kernel(GatesBwdParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
   __shared__ float wsum[32];
   float carry = p.dclock ? p.dclock[bh] : 0.f;

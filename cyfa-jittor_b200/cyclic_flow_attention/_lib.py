@@ -97,6 +97,8 @@ def lib():
         handle.cyfa_launch_count.restype = ctypes.c_longlong
         handle.cyfa_profile_enable.argtypes = [ctypes.c_int]
         handle.cyfa_profile_enable.restype = ctypes.c_int
+        handle.cyfa_set_pdl.argtypes = [ctypes.c_int]
+        handle.cyfa_set_pdl.restype = ctypes.c_int
         handle.cyfa_profile_report.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
                                                ctypes.POINTER(ctypes.c_float),
                                                ctypes.POINTER(ctypes.c_int)]
@@ -145,6 +147,12 @@ def device_error(reset=True):
 def launch_count():
     """Kernels libcyfa has launched in this process."""
     return lib().cyfa_launch_count()
+
+
+def set_pdl(on=True):
+    """Programmatic dependent launch of the library's kernels on/off; returns
+    the previous setting."""
+    return bool(lib().cyfa_set_pdl(1 if on else 0))
 
 
 def profile_enable(on=True):

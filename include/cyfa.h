@@ -47,6 +47,12 @@ int cyfa_device_error(int reset);
 /* Number of kernels this library has launched in the process (all entry points). */
 long long cyfa_launch_count(void);
 
+/* Programmatic dependent launch of the library's kernels: on (1, the default)
+ * each kernel may begin while the previous kernel on its stream finishes (it
+ * waits on the device before touching memory); off (0) gives plain stream
+ * order.  Returns the previous setting. */
+int cyfa_set_pdl(int on);
+
 /* Turns per-kernel timing on (1) or off (0) and clears earlier records.  While
  * on, every launch is bracketed by CUDA events on its own stream. */
 int cyfa_profile_enable(int on);

@@ -59,3 +59,40 @@ def test_graphed_step_matches_eager(B, T, hidden, H, hd):
             err = rel_l2(g, p.grad)
             assert err <= 1e-5, (name, err)
     del graphed
+
+
+def test_pdl_launch_matches_stream_order():
+    """Programmatic dependent launch (kernels may start while their predecessor
+    drains) gives bitwise the same step as plain stream order, eager and graphed."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+    from cyclic_flow_attention import _lib
+    from cyclic_flow_attention.graphs import GraphedStep
+
+    B, T, hidden, H, hd = 2, 384, 512, 2, 256
+    m, params, step = _setup(B, T, hidden, H, hd)
+    gen = torch.Generator().manual_seed(9)
+    x = torch.randn(B, T, hidden, generator=gen).to(torch.bfloat16).cuda()
+    dy = torch.randn(B, T, hidden, generator=gen).to(torch.bfloat16).cuda()
+    results = {}
+    prev = _lib.set_pdl(True)
+    try:
+        for on in (False, True):
+            _lib.set_pdl(on)
+            # detached: a live autograd graph would keep the eager AccumulateGrad
+            # nodes (bound to this stream) for the capture below
+            loss = step(x, dy).detach().clone()
+            grads = [p.grad.clone() for p in params]
+            static = [x.clone(), dy.clone()]
+            graphed = GraphedStep(step, static, params, warmup=2)
+            loss_g = graphed(x, dy).clone()
+            grads_g = [p.grad.clone() for p in params]
+            del graphed
+            torch.cuda.synchronize()
+            results[on] = (loss, grads, loss_g, grads_g)
+    finally:
+        _lib.set_pdl(prev)
+    off, on_ = results[False], results[True]
+    assert torch.equal(off[0], on_[0]) and torch.equal(off[2], on_[2])
+    for a, b, c, d in zip(off[1], on_[1], off[3], on_[3]):
+        assert torch.equal(a, b) and torch.equal(c, d)
