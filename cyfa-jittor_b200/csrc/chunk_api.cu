@@ -228,6 +228,27 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
   return kOk;
 }
 
+int cyfa_readout_table(const float* readout, const float* basis, void* table_bf, int H,
+                       void* stream) {
+  CYFA_REQUIRE(readout && basis && table_bf, kNullPointer);
+  CYFA_REQUIRE(H > 0, kBadShape);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CYFA_LAUNCH("readout_table", st,
+              launch_k(readout_table_kernel, dim3(H, 128), 128, 0, st, readout, basis,
+                       static_cast<__nv_bfloat16*>(table_bf)));
+  return launch_status();
+}
+
+int cyfa_readout_table_grad(const float* dtable, const float* basis_t, float* dreadout, int H,
+                            void* stream) {
+  CYFA_REQUIRE(dtable && basis_t && dreadout, kNullPointer);
+  CYFA_REQUIRE(H > 0, kBadShape);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CYFA_LAUNCH("readout_grad", st,
+              launch_k(readout_grad_kernel, dim3(H, 127), 128, 0, st, dtable, basis_t, dreadout));
+  return launch_status();
+}
+
 size_t cyfa_chunk_work_bytes(int B, int T, int H, int K, int V) {
   if (!shape_ok(B, T, H, K, V)) return 0;
   size_t total = 0;

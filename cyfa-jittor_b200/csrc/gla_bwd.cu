@@ -717,6 +717,42 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
+// Readout table of the chunked op in the kernels' bf16 layout, last row zero:
+//   tab[h][r][m] = sum_{k < 127} R[h][r][k] Phi[k][m]  (r < 127),  tab[h][127][:] = 0,
+// the product Table_h = R_h Phi of the reference (ops/chunk.py:281) rounded once
+// to bf16.  One CTA per (h, r), thread m; fixed-order fp32 sums.
+__global__ void __launch_bounds__(128) readout_table_kernel(const float* R, const float* phi,
+                                                            __nv_bfloat16* tab) {
+  pdl_wait();
+  pdl_trigger();
+  const int h = blockIdx.x, r = blockIdx.y, m = threadIdx.x;
+  __shared__ float row[128];
+  if (r < 127 && m < 127) row[m] = R[(size_t(h) * 127 + r) * 127 + m];
+  __syncthreads();
+  float acc = 0.f;
+  if (r < 127)
+    for (int k = 0; k < 127; ++k) acc = fmaf(row[k], phi[k * 128 + m], acc);
+  tab[(size_t(h) * 128 + r) * 128 + m] = __float2bfloat16_rn(acc);
+}
+
+// Readout gradient from the table gradient (the adjoint of the product above):
+//   dR[h][r][k] = sum_{m < 128} dtab[h][r][m] Phi[k][m],  r, k < 127,
+// with phiT = Phi^T [128][127].  One CTA per (h, r), thread k; fixed-order sums.
+__global__ void __launch_bounds__(128) readout_grad_kernel(const float* dtab, const float* phiT,
+                                                           float* dR) {
+  pdl_wait();
+  pdl_trigger();
+  const int h = blockIdx.x, r = blockIdx.y, k = threadIdx.x;
+  __shared__ float row[128];
+  row[k] = dtab[(size_t(h) * 128 + r) * 128 + k];
+  __syncthreads();
+  if (k < 127) {
+    float acc = 0.f;
+    for (int m = 0; m < 128; ++m) acc = fmaf(row[m], phiT[m * 127 + k], acc);
+    dR[(size_t(h) * 127 + r) * 127 + k] = acc;
+  }
+}
+
 // Fixed-order reduction of the per-CTA table gradients:
 // dtab[h][r][m] = sum_{s < per_head} part[h * per_head + s][r][m].
 __global__ void __launch_bounds__(128) dtable_reduce_kernel(const float* part, float* dtab,

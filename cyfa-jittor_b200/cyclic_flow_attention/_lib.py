@@ -42,6 +42,8 @@ _SIGNATURES = {
     "cyfa_gated_norm_bias_bwd": [_vp, _vp, _vp, _i, _vp, _f, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _i, _i, _vp, ctypes.c_size_t, _vp],
     "cyfa_chunk_bwd": [_vp, _vp, ctypes.c_size_t, _vp, ctypes.c_size_t, _vp],
+    "cyfa_readout_table": [_vp, _vp, _vp, _i, _vp],
+    "cyfa_readout_table_grad": [_vp, _vp, _vp, _i, _vp],
     "cyfa_bucket_gather": [_vp, _i, _vp, _vp],
     "cyfa_bucket_scatter": [_vp, _i, _vp, _f, _vp],
 }

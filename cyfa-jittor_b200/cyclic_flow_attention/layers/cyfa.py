@@ -16,7 +16,6 @@ import torch.nn.functional as F
 from torch import nn
 
 from ..ops import chunk_cyfa, fused_recurrent_cyfa
-from ..ops.chunk import readout_table
 from ..ops.layer_ops import (
     ChunkCyfaPackedFunction,
     GatedNormFunction,
@@ -187,9 +186,8 @@ class CyclicFlowAttention(nn.Module):
             self.a_proj.weight, self.b_proj.weight, self.d_proj.weight, self.q_conv1d.weight,
             self.k_conv1d.weight, self.v_conv1d.weight, self.A_log, self.dt_bias,
             self.b_proj.bias, self.d_proj.bias, H, slot, self.grad_ready)
-        table = readout_table(self.readout)
         o, hk, hv, clock = ChunkCyfaPackedFunction.apply(
-            qkv, H, K, V, g, delta, beta, table, self.q_norm.weight.float(),
+            qkv, H, K, V, g, delta, beta, self.readout, self.q_norm.weight.float(),
             self.k_norm.weight.float(), float(self.q_norm.eps), float(self.k_norm.eps), K ** -0.5)
         g1 = self.g_proj[1]
         y = GatedNormFunction.apply(o, gate_in, g1.weight, g1.bias, self.o_norm.weight,

@@ -56,17 +56,42 @@ def basis(M, device):
     return _BASIS[key]
 
 
+_BASIS_T = {}
+
+
+def basis_t(M, device):
+    """Phi^T [M, M-1] fp32 (contiguous), for the readout gradient kernel."""
+    key = (M, str(device))
+    if key not in _BASIS_T:
+        _BASIS_T[key] = basis(M, device).t().contiguous()
+    return _BASIS_T[key]
+
+
 def readout_table(readout):
     """Table_h = R_h . Phi in fp32, [H, M-1, M] (reference ops/chunk.py:281)."""
     M = readout.shape[-1] + 1
     return readout.float() @ basis(M, readout.device)
 
 
-def _table_bf(table):
-    H, R, M = table.shape
-    out = torch.zeros(H, M, M, device=table.device, dtype=torch.bfloat16)
-    out[:, :R] = table.detach().to(torch.bfloat16)
-    return out
+def table_bf16(readout):
+    """The readout table in the kernels' layout: bf16 [H, 128, 128], Table_h =
+    R_h . Phi rounded once, last row zero (one libcyfa launch)."""
+    H = readout.shape[0]
+    r = readout.detach().to(torch.float32).contiguous()
+    tb = torch.empty(H, 128, 128, device=readout.device, dtype=torch.bfloat16)
+    _lib.call("cyfa_readout_table", _p(r), _p(basis(128, readout.device)), _p(tb), H,
+              _lib.stream())
+    return tb
+
+
+def readout_grad(dtable, readout):
+    """Gradient of the readout from the kernels' table gradient dtable [H,128,128]
+    fp32 (one libcyfa launch); returned in the readout's dtype."""
+    H = dtable.shape[0]
+    dr = torch.empty(H, 127, 127, device=dtable.device, dtype=torch.float32)
+    _lib.call("cyfa_readout_table_grad", _p(dtable), _p(basis_t(128, dtable.device)), _p(dr),
+              H, _lib.stream())
+    return dr if readout.dtype == torch.float32 else dr.to(readout.dtype)
 
 
 def _contig(x, dtype):
@@ -81,12 +106,13 @@ class ChunkCyfaFunction(torch.autograd.Function):
     """Autograd wrapper over cyfa_chunk_fwd / cyfa_chunk_bwd."""
 
     @staticmethod
-    def forward(ctx, q, k, v, g, delta, beta, table, qw, kw, hk0, hv0, clock0,
+    def forward(ctx, q, k, v, g, delta, beta, readout, qw, kw, hk0, hv0, clock0,
                 q_eps, k_eps, scale):
+        ctx.set_materialize_grads(False)  # the final states usually get no gradient
         B, T, H, K = q.shape
         V = v.shape[-1]
         dev = q.device
-        tb = _table_bf(table)
+        tb = table_bf16(readout)
         o = torch.empty(B, T, H, V, device=dev, dtype=torch.bfloat16)
         hk = torch.empty(B, H, K, 128, device=dev, dtype=torch.float32)
         hv = torch.empty(B, H, 128, V, device=dev, dtype=torch.float32)
@@ -102,6 +128,7 @@ class ChunkCyfaFunction(torch.autograd.Function):
                   _lib.stream())
         ctx.save_for_backward(q, k, v, g, delta, beta, qw, kw, tb, hk0, hv0, clock0,
                               hk, hv, clock, saved)
+        ctx.readout_meta = readout.detach()[:0]  # dtype and device of the readout
         ctx.eps = (q_eps, k_eps, scale)
         ctx.has_init = (hk0 is not None, hv0 is not None, clock0 is not None)
         return o, hk, hv, clock
@@ -143,7 +170,8 @@ class ChunkCyfaFunction(torch.autograd.Function):
                   _c.c_size_t(saved.numel()), _lib.ptr(work), _c.c_size_t(nwork),
                   _lib.stream())
         has_hk0, has_hv0, has_c0 = ctx.has_init
-        return (dq, dk, dv, dg, ddelta, dbeta, dtable[:, :127], dqw, dkw,
+        dreadout = readout_grad(dtable, ctx.readout_meta) if ctx.needs_input_grad[6] else None
+        return (dq, dk, dv, dg, ddelta, dbeta, dreadout, dqw, dkw,
                 dhk0 if has_hk0 else None, dhv0 if has_hv0 else None,
                 dclock0 if has_c0 else None, None, None, None)
 
@@ -194,14 +222,13 @@ def chunk_cyfa(
         raise ValueError("chunk_size must be positive")
     out_dtype = q.dtype
     sc = K ** -0.5 if scale is None else float(scale)
-    table = readout_table(readout)
     hk0 = hv0 = clock0 = None
     if initial_state is not None:
         hk0, hv0, clock0 = (_contig(x, torch.float32) for x in initial_state)
     o, hk, hv, clock = ChunkCyfaFunction.apply(
         _contig(q, torch.bfloat16), _contig(k, torch.bfloat16), _contig(v, torch.bfloat16),
         _contig(g, torch.float32), _contig(delta, torch.float32), _contig(beta, torch.float32),
-        table, _contig(q_norm_weight, torch.float32), _contig(k_norm_weight, torch.float32),
+        readout, _contig(q_norm_weight, torch.float32), _contig(k_norm_weight, torch.float32),
         hk0, hv0, clock0, float(q_norm_eps), float(k_norm_eps), sc)
     if out_dtype != torch.bfloat16:
         o = o.to(out_dtype)

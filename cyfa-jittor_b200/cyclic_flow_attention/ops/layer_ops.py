@@ -10,7 +10,7 @@ import ctypes
 import torch
 
 from .. import _lib
-from .chunk import _BwdArgs, _FwdArgs, _p, _table_bf
+from .chunk import _BwdArgs, _FwdArgs, _p, readout_grad, table_bf16
 
 _c = ctypes
 
@@ -221,6 +221,8 @@ class LayerFrontFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w_q, w_k, w_v, w_g0, w_a, w_b, w_d, cw_q, cw_k, cw_v, A_log, dt_bias,
                 b_bias, d_bias, H, slot=None, grad_ready=None):
+        # unused outputs get no gradient tensor (no zero fills, no adds of zeros)
+        ctx.set_materialize_grads(False)
         B, T, hid = x.shape
         rows = B * T
         dev = x.device
@@ -336,12 +338,13 @@ class ChunkCyfaPackedFunction(torch.autograd.Function):
     packed layout."""
 
     @staticmethod
-    def forward(ctx, qkv, H, K, V, g, delta, beta, table, qw, kw, q_eps, k_eps, scale):
+    def forward(ctx, qkv, H, K, V, g, delta, beta, readout, qw, kw, q_eps, k_eps, scale):
+        ctx.set_materialize_grads(False)  # the final states usually get no gradient
         B, T, width = qkv.shape
         dev = qkv.device
         row = qkv.stride(1)
         base = qkv.data_ptr()
-        tb = _table_bf(table)
+        tb = table_bf16(readout)
         o = torch.empty(B, T, H, V, device=dev, dtype=torch.bfloat16)
         hk = torch.empty(B, H, K, 128, device=dev, dtype=torch.float32)
         hv = torch.empty(B, H, 128, V, device=dev, dtype=torch.float32)
@@ -357,6 +360,7 @@ class ChunkCyfaPackedFunction(torch.autograd.Function):
         _lib.call("cyfa_chunk_fwd", _c.byref(args), _lib.ptr(saved), _c.c_size_t(nbytes),
                   _lib.stream())
         ctx.save_for_backward(qkv, g, delta, beta, qw, kw, tb, hk, hv, clock, saved)
+        ctx.readout_meta = readout.detach()[:0]
         ctx.meta = (H, K, V, q_eps, k_eps, scale)
         return o, hk, hv, clock
 
@@ -392,5 +396,5 @@ class ChunkCyfaPackedFunction(torch.autograd.Function):
                         _p(dkw), None, None, None, width, width, width)
         _lib.call("cyfa_chunk_bwd", _c.byref(args), _lib.ptr(saved), _c.c_size_t(saved.numel()),
                   _lib.ptr(work), _c.c_size_t(nwork), _lib.stream())
-        return (dqkv, None, None, None, dg, ddelta, dbeta, dtable[:, :127], dqw, dkw, None,
-                None, None)
+        dreadout = readout_grad(dtable, ctx.readout_meta) if ctx.needs_input_grad[7] else None
+        return (dqkv, None, None, None, dg, ddelta, dbeta, dreadout, dqw, dkw, None, None, None)

@@ -192,6 +192,20 @@ typedef struct {
   long long dv_stride;          /* token stride of dv (0 = H*V) */
 } cyfa_chunk_bwd_args;
 
+/* Readout table in the kernels' layout (replaces the table product of
+ * cyclic_flow_attention/ops/chunk.py:281, jt.matmul(readout, _basis(M))):
+ * table_bf[h][r][m] = bf16(sum_k readout[h][r][k] basis[k][m]) for r < 127, row
+ * 127 zero.  readout [H,127,127] f32, basis (the real Fourier basis Phi)
+ * [127,128] f32, table_bf [H,128,128] bf16. */
+int cyfa_readout_table(const float* readout, const float* basis, void* table_bf, int H,
+                       void* stream);
+
+/* Adjoint of cyfa_readout_table: dreadout[h][r][k] = sum_m dtable[h][r][m]
+ * basis[k][m] for r, k < 127.  dtable [H,128,128] f32 (as cyfa_chunk_bwd writes
+ * it), basis_t = Phi^T [128,127] f32, dreadout [H,127,127] f32. */
+int cyfa_readout_table_grad(const float* dtable, const float* basis_t, float* dreadout, int H,
+                            void* stream);
+
 size_t cyfa_chunk_work_bytes(int B, int T, int H, int K, int V);
 
 int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* args, const void* saved, size_t saved_bytes,
