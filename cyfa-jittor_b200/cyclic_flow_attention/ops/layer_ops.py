@@ -19,6 +19,64 @@ def _work(nbytes, dev):
     return torch.empty(max(int(nbytes), 1), device=dev, dtype=torch.uint8)
 
 
+def _fits_pieces(tensors):
+    """True if every tensor can be a libcyfa bucket piece (CUDA, f32 or bf16,
+    contiguous, 16-byte aligned)."""
+    return all(t.is_cuda and t.dtype in (torch.float32, torch.bfloat16) and t.is_contiguous()
+               and t.data_ptr() % 16 == 0 for t in tensors)
+
+
+def _pieces(tensors, offs):
+    arr = (_lib.BucketPiece * len(tensors))()
+    for k, (t, o) in enumerate(zip(tensors, offs)):
+        arr[k] = _lib.BucketPiece(t.data_ptr(), t.numel(), o,
+                                  0 if t.dtype == torch.float32 else 1)
+    return arr
+
+
+def flat_f32(sizes, device):
+    """One fp32 buffer holding consecutive pieces of the given sizes, each
+    starting at a multiple of 8 elements; returns (buffer, offsets)."""
+    offs, total = [], 0
+    for n in sizes:
+        offs.append(total)
+        total += (n + 7) // 8 * 8
+    return torch.empty(max(total, 8), device=device, dtype=torch.float32), offs
+
+
+def gather_f32(tensors):
+    """The tensors as fp32 views of one buffer, filled by one libcyfa launch
+    (the per-step conversion of the small parameters)."""
+    tensors = [t.detach() for t in tensors]
+    flat, offs = flat_f32([t.numel() for t in tensors], tensors[0].device)
+    if not _fits_pieces(tensors):
+        return [t.float().contiguous() for t in tensors]
+    _lib.call("cyfa_bucket_gather", _pieces(tensors, offs), len(tensors), _p(flat),
+              _lib.stream())
+    return [flat[o:o + t.numel()].view(t.shape) for t, o in zip(tensors, offs)]
+
+
+def scatter_from(flat, offs, like):
+    """Gradients held in fp32 at flat[offs[i]:] converted to the dtype and shape
+    of like[i] by one libcyfa launch; fp32 targets are views of `flat`."""
+    outs, pieces, poffs = [], [], []
+    for o, t in zip(offs, like):
+        if t.dtype == torch.float32:
+            outs.append(flat[o:o + t.numel()].view(t.shape))
+        else:
+            outs.append(torch.empty(t.shape, device=flat.device, dtype=t.dtype))
+            pieces.append(outs[-1])
+            poffs.append(o)
+    if pieces and _fits_pieces(pieces):
+        _lib.call("cyfa_bucket_scatter", _pieces(pieces, poffs), len(pieces), _p(flat),
+                  _c.c_float(1.0), _lib.stream())
+    elif pieces:
+        for i, (o, t) in enumerate(zip(offs, like)):
+            if t.dtype != torch.float32:
+                outs[i] = flat[o:o + t.numel()].view(t.shape).to(t.dtype)
+    return outs
+
+
 class ShortConvFunction(torch.autograd.Function):
     """Causal depthwise conv (no activation) of x [B,T,C] bf16 with weight [C,1,W]."""
 
@@ -233,19 +291,23 @@ class LayerFrontFunction(torch.autograd.Function):
         n_used = c_d + H
         NB = (n_used + 7) // 8 * 8  # 16-byte rows
         parts = [w_q, w_k, w_v, w_g0, w_a, w_b, w_d]
-        if NB > n_used:
-            parts.append(torch.zeros(NB - n_used, hid, device=dev, dtype=w_q.dtype))
-        W_big = torch.cat(parts)
+        # the padding rows stay uninitialised: the columns they produce are never read
+        W_big = torch.empty(NB, hid, device=dev, dtype=w_q.dtype)
+        torch.cat(parts, out=W_big[:n_used])
         big = torch.nn.functional.linear(x, W_big)  # [B, T, NB]
         Wc = cw_q.shape[-1]
-        cw = torch.cat([cw_q, cw_k, cw_v]).detach().float().reshape(n_qkv, Wc).contiguous()
+        # conv weights (one [n_qkv, Wc] block when the q, k, v pieces are adjacent)
+        # and gate parameters as fp32, one launch
+        cwq, cwk, cwv, A, dt, bb, db = gather_f32(
+            [cw_q, cw_k, cw_v, A_log, dt_bias, b_bias, d_bias])
+        if (cwk.data_ptr() == cwq.data_ptr() + 4 * cwq.numel()
+                and cwv.data_ptr() == cwk.data_ptr() + 4 * cwk.numel()):
+            cw = torch.as_strided(cwq, (n_qkv, Wc), (Wc, 1))
+        else:
+            cw = torch.cat([cwq.reshape(-1, Wc), cwk.reshape(-1, Wc), cwv.reshape(-1, Wc)])
         qkv = torch.empty(B, T, n_qkv, device=dev, dtype=torch.bfloat16)
         _lib.call("cyfa_short_conv_fwd", _p(big), _c.c_longlong(NB), None, _p(cw), None, _p(qkv),
                   B, T, n_qkv, Wc, _lib.stream())
-        A = A_log.detach().float().contiguous()
-        dt = dt_bias.detach().float().contiguous()
-        bb = b_bias.detach().float().contiguous()
-        db = d_bias.detach().float().contiguous()
         g = torch.empty(B, T, H, device=dev, dtype=torch.float32)
         delta = torch.empty_like(g)
         beta = torch.empty_like(g)
@@ -266,6 +328,9 @@ class LayerFrontFunction(torch.autograd.Function):
         ctx.meta = (H, NB, n_qkv, c_g, n_g, c_a, c_b, c_d, n_used, Wc,
                     [w.shape[0] for w in parts[:7]], cw_q.dtype,
                     (A_log.dtype, dt_bias.dtype, b_bias.dtype, d_bias.dtype))
+        # shapes and dtypes of the small parameters' gradients (zero-size stand-ins)
+        ctx.small_like = [torch.empty(t.shape, device="meta", dtype=t.dtype)
+                          for t in (cw_q, cw_k, cw_v, A_log, dt_bias, b_bias, d_bias)]
         return qkv, gate_in, g, delta, beta
 
     @staticmethod
@@ -281,8 +346,14 @@ class LayerFrontFunction(torch.autograd.Function):
         if dbig is None:
             dbig = torch.empty(B, T, NB, device=dev, dtype=torch.bfloat16)
         base, dbase, st = big.data_ptr(), dbig.data_ptr(), _c.c_longlong(NB)
-        # short conv adjoint -> columns [0, n_qkv) of the packed gradient
-        dcw = torch.empty(n_qkv, Wc, device=dev, dtype=torch.float32)
+        # fp32 gradients of the small parameters in one buffer: conv weights, A_log,
+        # dt_bias, b_bias, d_bias (converted to the parameters' dtypes in one launch)
+        n_cw = sizes[0] * Wc
+        gflat, goffs = flat_f32([n_cw, sizes[1] * Wc, sizes[2] * Wc, H, H, H, H], dev)
+        dcw = torch.as_strided(gflat, (n_qkv, Wc), (Wc, 1))
+        if goffs[1] != n_cw or goffs[2] != goffs[1] + sizes[1] * Wc:
+            dcw = torch.empty(n_qkv, Wc, device=dev, dtype=torch.float32)
+        dA, ddtb, dbb, ddb = (gflat[o:o + H] for o in goffs[3:])
         if dqkv is None:
             dbig[..., :n_qkv].zero_()
             dcw.zero_()
@@ -297,10 +368,6 @@ class LayerFrontFunction(torch.autograd.Function):
         dg = zeros() if dg is None else dg.float().contiguous()
         ddelta = zeros() if ddelta is None else ddelta.float().contiguous()
         dbeta = zeros() if dbeta is None else dbeta.float().contiguous()
-        dA = torch.empty(H, device=dev, dtype=torch.float32)
-        ddtb = torch.empty(H, device=dev, dtype=torch.float32)
-        dbb = torch.empty(H, device=dev, dtype=torch.float32)
-        ddb = torch.empty(H, device=dev, dtype=torch.float32)
         nbytes = _lib.lib().cyfa_gate_act_work_bytes(rows, H)
         work = _work(nbytes, dev)
         _lib.call("cyfa_gate_act_bwd", _c.c_void_p(base + 2 * c_a), st, _c.c_void_p(base + 2 * c_b),
@@ -321,8 +388,12 @@ class LayerFrontFunction(torch.autograd.Function):
         x2 = x.reshape(rows, hid)
         # weight gradients first, so that their hand-over overlaps the dx GEMM
         dW = torch.matmul(d2[:, :n_used].t(), x2)
-        grads = (*torch.split(dW, sizes), *torch.split(dcw.to(cdt).reshape(n_qkv, 1, Wc), sizes[:3]),
-                 dA.to(gdts[0]), ddtb.to(gdts[1]), dbb.to(gdts[2]), ddb.to(gdts[3]))
+        if dcw.data_ptr() != gflat.data_ptr():  # conv pieces not adjacent in gflat
+            for (o, n), blk in zip(((goffs[0], sizes[0]), (goffs[1], sizes[1]), (goffs[2], sizes[2])),
+                                   torch.split(dcw, sizes[:3])):
+                gflat[o:o + n * Wc].copy_(blk.reshape(-1))
+        small = scatter_from(gflat, goffs, ctx.small_like)
+        grads = (*torch.split(dW, sizes), *small)
         if ctx.grad_ready is not None:
             ctx.grad_ready(ctx.params, grads)
         # dx from every column except d (projected from x.detach()) and the padding
