@@ -284,6 +284,9 @@ __device__ __forceinline__ float softplus_f(float x) {
   return x > 20.f ? x : log1pf(expf(x));  // torch softplus, beta 1, threshold 20
 }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+// Sigmoid from the fast exponential and division intrinsics (a few ulp), for the
+// gated norm whose outputs are rounded to bf16.
+__device__ __forceinline__ float sigmoid_fast(float x) { return __fdividef(1.f, 1.f + __expf(-x)); }
 
 __global__ void __launch_bounds__(256) gate_act_fwd_kernel(GateActParams p) {
   pdl_wait();
@@ -386,25 +389,34 @@ __global__ void __launch_bounds__(256, 3) gated_norm_fwd_kernel(GatedNormParams 
       if (live[u]) {
         load_bf16_vec<E>(p.x + row * D + lane * E, x[u]);
         load_bf16_vec<E>(p.gate + row * D + lane * E, g[u]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) x[u][e] = g[u][e] = 0.f;
       }
+    }
+    // both rows' reductions interleaved (independent shuffle chains)
+    float ss[2] = {0.f, 0.f};
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        x[u][e] *= p.scale;
+        ss[u] += x[u][e] * x[u][e];
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      ss[0] += __shfl_xor_sync(0xffffffffu, ss[0], o);
+      ss[1] += __shfl_xor_sync(0xffffffffu, ss[1], o);
     }
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       if (!live[u]) continue;
       const size_t row = row0 + u * stride;
-      float ss = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) {
-        x[u][e] *= p.scale;
-        ss += x[u][e] * x[u][e];
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float rs = rsqrtf(ss / D + p.eps);
+      const float rs = rsqrtf(ss[u] / D + p.eps);
       if (lane == 0) p.rstd[row] = rs;
       float y[E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) y[e] = x[u][e] * rs * w[e] * sigmoid_f(g[u][e] + bias[e]);
+      for (int e = 0; e < E; ++e) y[e] = x[u][e] * rs * w[e] * sigmoid_fast(g[u][e] + bias[e]);
       store_bf16_vec<E>(p.y + row * D + lane * E, y);
     }
   }
@@ -444,7 +456,7 @@ __global__ void __launch_bounds__(256, 3) gated_norm_bwd_kernel(GatedNormParams 
     float dot = 0.f;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      const float sg = sigmoid_f(g[e] + bias[e]);
+      const float sg = sigmoid_fast(g[e] + bias[e]);
       const float n = x[e] * p.scale * rs;
       const float dz = dy[e] * sg;
       g[e] = dy[e] * n * w[e] * sg * (1.f - sg);  // dgate

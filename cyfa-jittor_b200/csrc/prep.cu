@@ -375,36 +375,22 @@ __global__ void __launch_bounds__(256, 3) token_bwd_kernel(TokenBwdParams p) {
         dwp[part].y += e2.y;
       }
     }
-    // RMSNorm adjoints (ops/qk_norm.py:109-165), q then k
+    // RMSNorm adjoints (ops/qk_norm.py:109-165) of q and k and the write-vector
+    // adjoint (ops/utils.py:598-616): the four row sums are reduced together
+    float xq_[E], gq_[E], xk_[E], gk_[E];
+    xq.unpack(xq_), gq.unpack(gq_), xk.unpack(xk_), gk.unpack(gk_);
+    float dotq = 0.f, dotk = 0.f;
 #pragma unroll
-    for (int side = 0; side < 2; ++side) {
-      float xv[E], gv[E], wv[E];
-      (side ? xk : xq).unpack(xv);
-      (side ? gk : gq).unpack(gv);
-      const float r = side ? rk : rq;
+    for (int j = 0; j < E; j += 4) {
+      const float4 wq4 = *reinterpret_cast<const float4*>(&wts[0][lane * E + j]);
+      const float4 wk4 = *reinterpret_cast<const float4*>(&wts[1][lane * E + j]);
+      const float wq[4] = {wq4.x, wq4.y, wq4.z, wq4.w}, wk[4] = {wk4.x, wk4.y, wk4.z, wk4.w};
 #pragma unroll
-      for (int j = 0; j < E; j += 4) {
-        const float4 w4 = *reinterpret_cast<const float4*>(&wts[side][lane * E + j]);
-        wv[j] = w4.x, wv[j + 1] = w4.y, wv[j + 2] = w4.z, wv[j + 3] = w4.w;
-      }
-      float dot = 0.f;
-#pragma unroll
-      for (int j = 0; j < E; ++j) dot += gv[j] * wv[j] * xv[j];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      dot *= r * r / K;
-      float o_[E];
-#pragma unroll
-      for (int j = 0; j < E; ++j) {
-        o_[j] = (gv[j] * wv[j] - xv[j] * dot) * r;
-        (side ? acc_k : acc_q)[j] += xv[j] * r * gv[j];
-      }
-      if (real) {
-        if (side) store_bf16_vec<E>(p.dk + tok * p.dk_stride + col, o_);
-        else store_bf16_vec<E>(p.dq + tok * p.dq_stride + col, o_);
+      for (int i = 0; i < 4; ++i) {
+        dotq += gq_[j + i] * wq[i] * xq_[j + i];
+        dotk += gk_[j + i] * wk[i] * xk_[j + i];
       }
     }
-    // write-vector adjoint (ops/utils.py:598-616)
     float dl = 0.f, db = 0.f;
 #pragma unroll
     for (int part = 0; part < 2; ++part) {
@@ -418,8 +404,25 @@ __global__ void __launch_bounds__(256, 3) token_bwd_kernel(TokenBwdParams p) {
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
+      dotq += __shfl_xor_sync(0xffffffffu, dotq, o);
+      dotk += __shfl_xor_sync(0xffffffffu, dotk, o);
       dl += __shfl_xor_sync(0xffffffffu, dl, o);
       db += __shfl_xor_sync(0xffffffffu, db, o);
+    }
+    dotq *= rq * rq / K;
+    dotk *= rk * rk / K;
+    float oq[E], ok[E];
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      const float wq = wts[0][lane * E + j], wk = wts[1][lane * E + j];
+      oq[j] = (gq_[j] * wq - xq_[j] * dotq) * rq;
+      ok[j] = (gk_[j] * wk - xk_[j] * dotk) * rk;
+      acc_q[j] += xq_[j] * rq * gq_[j];
+      acc_k[j] += xk_[j] * rk * gk_[j];
+    }
+    if (real) {
+      store_bf16_vec<E>(p.dq + tok * p.dq_stride + col, oq);
+      store_bf16_vec<E>(p.dk + tok * p.dk_stride + col, ok);
     }
     if (lane == 0) {
       p.dlam[row] = dl;

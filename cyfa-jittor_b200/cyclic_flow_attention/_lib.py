@@ -11,7 +11,9 @@ import os
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libcyfa.so")
+# CYFA_LIB selects another build of the library (e.g. to compare two builds in
+# one process environment); the default is the in-tree libcyfa.so.
+LIB_PATH = os.environ.get("CYFA_LIB") or os.path.join(_HERE, "libcyfa.so")
 
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
