@@ -126,11 +126,12 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// bf16 tensor map with a 128-byte swizzle and a box whose inner extent is 64
-// elements (one 128-byte row).  dims innermost first; strides in bytes for
+// bf16 tensor map, by default with a 128-byte swizzle and a box whose inner
+// extent is 64 elements (one 128-byte row).  dims innermost first; strides in bytes for
 // dims 1..rank-1.  Out-of-bounds elements are filled with zeros.
 static int make_tmap_bf16(CUtensorMap* m, const void* base, int rank, const uint64_t* dims,
-                          const uint64_t* strides, const uint32_t* box) {
+                          const uint64_t* strides, const uint32_t* box,
+                          CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (!fn) return kNoDriver;
   if (!aligned(base, 16)) return kMisaligned;
@@ -145,7 +146,7 @@ static int make_tmap_bf16(CUtensorMap* m, const void* base, int rank, const uint
   }
   for (int i = 0; i + 1 < rank; ++i) s[i] = strides[i];
   const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), d, s,
-                        b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? kOk : kTensorMap;
 }

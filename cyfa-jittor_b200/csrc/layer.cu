@@ -251,6 +251,279 @@ inline int conv_bwd_rows(int B, int T) {
   return B * ((T + kConvWarps * kConvRun - 1) / (kConvWarps * kConvRun));
 }
 
+// ------------------------------------------------ TMA-streamed short convolution
+// Without a conv cache and with C % 128 == 0 the convolution streams tiles of
+// kCtRows tokens x 128 channels of one batch row through a shared-memory ring:
+// warp 8 (one lane) issues 3-D TMA loads of the tile and its kCtHalo rows of
+// context (x rows t0-3 .. t0+63, dy rows t0 .. t0+66; rows outside [0, T) read
+// as zeros), warps 0-7 compute 8 tokens each from shared memory (lane = 4
+// channels, sliding register window) and store their rows directly.  The CTAs
+// are persistent, so the loads of the next tiles overlap the current one.
+constexpr int kCtRows = 64;
+constexpr int kCtHalo = 3;                           // context rows (W <= 4)
+constexpr int kCtBoxRows = kCtRows + kCtHalo;        // 67
+constexpr int kCtTileBytes = kCtBoxRows * 128 * 2;   // 17152 (a multiple of 128)
+constexpr int kCtStages = 8;                         // forward: x tiles
+constexpr int kCtStagesB = 4;                        // backward: x and dy tiles
+constexpr int kCtSmem = kCtStages * kCtTileBytes + 1024;
+constexpr int kCtSmemB = kCtStagesB * 2 * kCtTileBytes + 1024;
+static_assert(kCtSmem <= 227 * 1024 && kCtSmemB <= 227 * 1024, "conv ring");
+
+struct ConvTmaParams {
+  int B, T, C, nT;               // nT = tiles per batch row
+  const float* w;                // [C, W]
+  const float* bias;             // [C] or null (forward)
+  __nv_bfloat16* out;            // forward y [B,T,C] dense; backward dx (token stride out_stride)
+  long long out_stride;
+  float* part;                   // backward: [G, C * (W + 1)] partial dw | dbias
+};
+
+__device__ __forceinline__ void ld_row4(const uint8_t* tile, int row, int lane, float* f) {
+  const uint2 r = *reinterpret_cast<const uint2*>(tile + row * 256 + lane * 8);
+  f[0] = __uint_as_float(r.x << 16), f[1] = __uint_as_float(r.x & 0xffff0000u);
+  f[2] = __uint_as_float(r.y << 16), f[3] = __uint_as_float(r.y & 0xffff0000u);
+}
+
+// Forward: CTA (cb, g) = (blockIdx.x % ncb, blockIdx.x / ncb) owns channel block cb
+// (its weights stay in registers) and the token tiles g, g + G, ... (G = gridDim.x
+// / ncb) of all batch rows.  y[t] = bias + sum_i w_i x[t - (W-1) + i].
+template <int W>
+__global__ void __launch_bounds__(288, 1)
+    short_conv_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_x, ConvTmaParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[kCtStages], empty[kCtStages];
+  __shared__ int s_abort;
+  volatile int* abort_flag = &s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ncb = p.C / 128, G = gridDim.x / ncb;
+  const int cb = blockIdx.x % ncb, g = blockIdx.x / ncb;
+  const int ntiles = g < G ? p.B * p.nT : 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kCtStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    s_abort = 0;
+    mbar_fence_init();
+    prefetch_tmap(&map_x);
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  if (warp == 8) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0, k = g; k < ntiles; ++i, k += G) {
+        const int s = i % kCtStages;
+        if (i >= kCtStages && !mbar_wait(&empty[s], ((i / kCtStages) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        const int b = k / p.nT, t0 = (k % p.nT) * kCtRows;
+        mbar_expect_tx(&full[s], kCtTileBytes);
+        tma_load_3d(smem + s * kCtTileBytes, &map_x, &full[s], cb * 128, t0 - kCtHalo, b);
+        issued = i + 1;
+      }
+      for (int i = issued > kCtStages ? issued - kCtStages : 0; i < issued; ++i)
+        mbar_wait(&full[i % kCtStages], (i / kCtStages) & 1);
+    }
+    return;
+  }
+  const int c0 = cb * 128 + lane * 4;
+  float wr[W][4], bias[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+#pragma unroll
+    for (int q = 0; q < W; ++q) wr[q][e] = p.w[size_t(c0 + e) * W + q];
+    bias[e] = p.bias ? p.bias[c0 + e] : 0.f;
+  }
+  for (int i = 0, k = g; k < ntiles; ++i, k += G) {
+    const int s = i % kCtStages;
+    const bool got = __all_sync(0xffffffffu, *abort_flag == 0 &&
+                                                 mbar_wait(&full[s], (i / kCtStages) & 1));
+    if (!got) {
+      *abort_flag = 1;
+      break;
+    }
+    const int b = k / p.nT, t0 = (k % p.nT) * kCtRows;
+    const uint8_t* tile = smem + s * kCtTileBytes;
+    const int r0 = warp * 8;  // first token row of this warp in the tile
+    float win[W > 1 ? W - 1 : 1][4];
+#pragma unroll
+    for (int q = 0; q < W - 1; ++q) ld_row4(tile, r0 + kCtHalo - (W - 1) + q, lane, win[q]);
+    __nv_bfloat16* yb = p.out + (size_t(b) * p.T + t0 + r0) * p.C + c0;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      float xn[4];
+      ld_row4(tile, r0 + kCtHalo + u, lane, xn);
+      float y[4] = {bias[0], bias[1], bias[2], bias[3]};
+#pragma unroll
+      for (int q = 0; q < W; ++q) {
+        const float* r = q < W - 1 ? win[q < W - 1 ? q : 0] : xn;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y[e] += wr[q][e] * r[e];
+      }
+      if (t0 + r0 + u < p.T)
+        *reinterpret_cast<uint2*>(yb + size_t(u) * p.C) =
+            make_uint2(pack_bf16(y[0], y[1]), pack_bf16(y[2], y[3]));
+#pragma unroll
+      for (int q = 0; q + 1 < W - 1; ++q)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) win[q][e] = win[q + 1][e];
+      if (W > 1) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) win[W > 1 ? W - 2 : 0][e] = xn[e];
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+}
+
+// Backward: CTA (cb, g) = (blockIdx.x % ncb, blockIdx.x / ncb) owns channel block
+// cb and the token tiles g, g + G, ... (G = gridDim.x / ncb) of all batch rows, so
+// its dw / dbias sums (registers, then a fixed-order block reduction) form one
+// partial row g.  dx[t] = sum_i w_i dy[t + (W-1) - i], dw_i = sum_t dy[t] x[t + i - (W-1)].
+template <int W>
+__global__ void __launch_bounds__(288, 1)
+    short_conv_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_x,
+                              const __grid_constant__ CUtensorMap map_dy, ConvTmaParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[kCtStagesB], empty[kCtStagesB];
+  __shared__ int s_abort;
+  __shared__ float red[8][128 * (W + 1)];
+  volatile int* abort_flag = &s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ncb = p.C / 128, G = gridDim.x / ncb;
+  const int cb = blockIdx.x % ncb, g = blockIdx.x / ncb;
+  const int ntiles = p.B * p.nT;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kCtStagesB; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    s_abort = 0;
+    mbar_fence_init();
+    prefetch_tmap(&map_x);
+    prefetch_tmap(&map_dy);
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  float acc[W + 1][4];
+#pragma unroll
+  for (int q = 0; q <= W; ++q)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[q][e] = 0.f;
+  if (warp == 8) {
+    if (lane == 0 && g < G) {
+      int issued = 0;
+      for (int i = 0, k = g; k < ntiles; ++i, k += G) {
+        const int s = i % kCtStagesB;
+        if (i >= kCtStagesB && !mbar_wait(&empty[s], ((i / kCtStagesB) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        const int b = k / p.nT, t0 = (k % p.nT) * kCtRows;
+        uint8_t* st = smem + s * 2 * kCtTileBytes;
+        mbar_expect_tx(&full[s], 2 * kCtTileBytes);
+        tma_load_3d(st, &map_x, &full[s], cb * 128, t0 - kCtHalo, b);
+        tma_load_3d(st + kCtTileBytes, &map_dy, &full[s], cb * 128, t0, b);
+        issued = i + 1;
+      }
+      for (int i = issued > kCtStagesB ? issued - kCtStagesB : 0; i < issued; ++i)
+        mbar_wait(&full[i % kCtStagesB], (i / kCtStagesB) & 1);
+    }
+  } else if (g < G) {
+    const int c0 = cb * 128 + lane * 4;
+    float wr[W][4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+#pragma unroll
+      for (int q = 0; q < W; ++q) wr[q][e] = p.w[size_t(c0 + e) * W + q];
+    constexpr int WM = W > 1 ? W - 1 : 1;
+    for (int i = 0, k = g; k < ntiles; ++i, k += G) {
+      const int s = i % kCtStagesB;
+      const bool got = __all_sync(0xffffffffu, *abort_flag == 0 &&
+                                                   mbar_wait(&full[s], (i / kCtStagesB) & 1));
+      if (!got) {
+        *abort_flag = 1;
+        break;
+      }
+      const int b = k / p.nT, t0 = (k % p.nT) * kCtRows;
+      const uint8_t* xt = smem + s * 2 * kCtTileBytes;
+      const uint8_t* dt = xt + kCtTileBytes;
+      const int r0 = warp * 8;
+      // x rows t-(W-1) .. t-1 and dy rows t .. t+W-2 of the warp's first token t
+      float X[WM][4], D[WM][4];
+#pragma unroll
+      for (int q = 0; q < W - 1; ++q) {
+        ld_row4(xt, r0 + kCtHalo - (W - 1) + q, lane, X[q]);
+        ld_row4(dt, r0 + q, lane, D[q]);
+      }
+      __nv_bfloat16* dxb = p.out + (size_t(b) * p.T + t0 + r0) * p.out_stride + c0;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        float xn[4], dn[4];
+        ld_row4(xt, r0 + kCtHalo + u, lane, xn);  // x[t]
+        ld_row4(dt, r0 + u + W - 1, lane, dn);    // dy[t + W - 1]
+        const float* d0 = W > 1 ? D[0] : dn;      // dy[t]
+        float dx[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < W; ++q) {
+          const int j = W - 1 - q;  // dy row t + j
+          const float* dv = j < W - 1 ? D[j < W - 1 ? j : 0] : dn;
+          const float* xv = q < W - 1 ? X[q < W - 1 ? q : 0] : xn;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            dx[e] += wr[q][e] * dv[e];
+            acc[q][e] += d0[e] * xv[e];
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[W][e] += d0[e];
+        if (t0 + r0 + u < p.T)
+          *reinterpret_cast<uint2*>(dxb + size_t(u) * p.out_stride) =
+              make_uint2(pack_bf16(dx[0], dx[1]), pack_bf16(dx[2], dx[3]));
+#pragma unroll
+        for (int q = 0; q + 1 < W - 1; ++q)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            X[q][e] = X[q + 1][e];
+            D[q][e] = D[q + 1][e];
+          }
+        if (W > 1) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            X[W > 1 ? W - 2 : 0][e] = xn[e];
+            D[W > 1 ? W - 2 : 0][e] = dn[e];
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+  if (warp < 8) {
+#pragma unroll
+    for (int q = 0; q <= W; ++q)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) red[warp][(lane * 4 + e) * (W + 1) + q] = acc[q][e];
+  }
+  __syncthreads();
+  if (g >= G) return;
+  for (int idx = threadIdx.x; idx < 128 * (W + 1); idx += blockDim.x) {
+    float sum = 0.f;
+#pragma unroll
+    for (int w8 = 0; w8 < 8; ++w8) sum += red[w8][idx];
+    p.part[size_t(g) * (size_t(p.C) * (W + 1)) + size_t(cb) * 128 * (W + 1) + idx] = sum;
+  }
+}
+
 // ============================================================ gate activations
 struct GateActParams {
   const __nv_bfloat16* a;  // a_proj output, token stride a_stride, H columns

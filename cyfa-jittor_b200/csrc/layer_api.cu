@@ -21,6 +21,30 @@ static int norm_bwd_blocks(int rows) {
 
 using namespace cyfa;
 
+// [B, T, C] bf16 rows `stride` elements apart as a 3-D map {C, T, B} with a
+// {128, kCtBoxRows, 1} unswizzled box (the short-convolution tiles).
+static int conv_tmap(CUtensorMap* m, const void* base, int B, int T, int C, long long stride) {
+  const uint64_t dims[3] = {uint64_t(C), uint64_t(T), uint64_t(B)};
+  const uint64_t strides[2] = {uint64_t(stride) * 2, uint64_t(stride) * 2 * uint64_t(T)};
+  const uint32_t box[3] = {128, uint32_t(kCtBoxRows), 1};
+  return make_tmap_bf16(m, base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+template <int W>
+static void conv_fwd_tma_launch(const CUtensorMap& mx, const ConvTmaParams& p, int grid,
+                                cudaStream_t s) {
+  set_smem(short_conv_fwd_tma_kernel<W>, kCtSmem);
+  CYFA_LAUNCH("short_conv_fwd", s, launch_k(short_conv_fwd_tma_kernel<W>, grid, 288, kCtSmem, s, mx, p));
+}
+
+template <int W>
+static void conv_bwd_tma_launch(const CUtensorMap& mx, const CUtensorMap& md,
+                                const ConvTmaParams& p, int grid, cudaStream_t s) {
+  set_smem(short_conv_bwd_tma_kernel<W>, kCtSmemB);
+  CYFA_LAUNCH("short_conv_bwd", s,
+              launch_k(short_conv_bwd_tma_kernel<W>, grid, 288, kCtSmemB, s, mx, md, p));
+}
+
 extern "C" {
 
 size_t cyfa_short_conv_work_bytes(int B, int T, int C, int W) {
@@ -35,11 +59,28 @@ int cyfa_short_conv_fwd(const void* x, long long x_stride, const void* cache, co
                    x_stride % 8 == 0,
                kBadShape);
   CYFA_REQUIRE(aligned(x, 16) && aligned(y, 16) && (!cache || aligned(cache, 16)), kMisaligned);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap mx;
+  if (!cache && C % 128 == 0 && conv_tmap(&mx, x, B, T, C, x_stride) == kOk) {
+    // persistent CTAs: channel block x token-tile group
+    const int ncb = C / 128, nT = (T + kCtRows - 1) / kCtRows;
+    int G = 148 / ncb;
+    if (G < 1) G = 1;
+    if (G > B * nT) G = B * nT;
+    const int grid = ncb * G;
+    ConvTmaParams q{B, T, C, nT, w, bias, static_cast<__nv_bfloat16*>(y), C, nullptr};
+    switch (W) {
+      case 1: conv_fwd_tma_launch<1>(mx, q, grid, s); break;
+      case 2: conv_fwd_tma_launch<2>(mx, q, grid, s); break;
+      case 3: conv_fwd_tma_launch<3>(mx, q, grid, s); break;
+      default: conv_fwd_tma_launch<4>(mx, q, grid, s); break;
+    }
+    return launch_status();
+  }
   ConvParams p{static_cast<const __nv_bfloat16*>(x), x_stride,
                static_cast<const __nv_bfloat16*>(cache), w, bias, static_cast<__nv_bfloat16*>(y),
                nullptr, nullptr, 0, nullptr, B, T, C};
   const dim3 grid((C + 127) / 128, (T + kConvWarps * kConvRun - 1) / (kConvWarps * kConvRun), B);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (W) {
     case 1: CYFA_LAUNCH("short_conv_fwd", s, launch_k(short_conv_fwd_kernel<1>, grid, 256, 0, s, p)); break;
     case 2: CYFA_LAUNCH("short_conv_fwd", s, launch_k(short_conv_fwd_kernel<2>, grid, 256, 0, s, p)); break;
@@ -59,21 +100,41 @@ int cyfa_short_conv_bwd(const void* x, long long x_stride, const float* w, const
   CYFA_REQUIRE(work_bytes >= cyfa_short_conv_work_bytes(B, T, C, W), kWorkspace);
   CYFA_REQUIRE(aligned(x, 16) && aligned(dy, 16) && aligned(dx, 16), kMisaligned);
   float* part = static_cast<float*>(work);
-  ConvParams p{static_cast<const __nv_bfloat16*>(x), x_stride, nullptr, w, nullptr, nullptr,
-               static_cast<const __nv_bfloat16*>(dy), static_cast<__nv_bfloat16*>(dx), dx_stride,
-               part, B, T, C};
-  const dim3 grid((C + 127) / 128, conv_bwd_rows(B, T));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  switch (W) {
+  int rows = conv_bwd_rows(B, T);
+  CUtensorMap mx, md;
+  if (C % 128 == 0 && conv_tmap(&mx, x, B, T, C, x_stride) == kOk &&
+      conv_tmap(&md, dy, B, T, C, C) == kOk) {
+    // persistent CTAs: channel block x token-tile group; one partial row per group
+    const int ncb = C / 128, nT = (T + kCtRows - 1) / kCtRows;
+    int G = 148 / ncb;
+    if (G < 1) G = 1;
+    if (G > rows) G = rows;
+    if (G > B * nT) G = B * nT;
+    rows = G;
+    ConvTmaParams q{B, T, C, nT, w, nullptr, static_cast<__nv_bfloat16*>(dx), dx_stride, part};
+    switch (W) {
+      case 1: conv_bwd_tma_launch<1>(mx, md, q, ncb * G, s); break;
+      case 2: conv_bwd_tma_launch<2>(mx, md, q, ncb * G, s); break;
+      case 3: conv_bwd_tma_launch<3>(mx, md, q, ncb * G, s); break;
+      default: conv_bwd_tma_launch<4>(mx, md, q, ncb * G, s); break;
+    }
+  } else {
+    ConvParams p{static_cast<const __nv_bfloat16*>(x), x_stride, nullptr, w, nullptr, nullptr,
+                 static_cast<const __nv_bfloat16*>(dy), static_cast<__nv_bfloat16*>(dx), dx_stride,
+                 part, B, T, C};
+    const dim3 grid((C + 127) / 128, rows);
+    switch (W) {
     case 1: CYFA_LAUNCH("short_conv_bwd", s, (launch_k(short_conv_bwd_kernel<1>, grid, 256, 0, s, p))); break;
     case 2: CYFA_LAUNCH("short_conv_bwd", s, (launch_k(short_conv_bwd_kernel<2>, grid, 256, 0, s, p))); break;
     case 3: CYFA_LAUNCH("short_conv_bwd", s, (launch_k(short_conv_bwd_kernel<3>, grid, 256, 0, s, p))); break;
     default: CYFA_LAUNCH("short_conv_bwd", s, (launch_k(short_conv_bwd_kernel<4>, grid, 256, 0, s, p))); break;
+    }
   }
   int rc = launch_status();
   if (rc) return rc;
   // reduce the partial rows: columns are [c][0..W-1] = dw, [c][W] = dbias
-  const int rows = conv_bwd_rows(B, T), cols = C * (W + 1);
+  const int cols = C * (W + 1);
   CYFA_LAUNCH("conv_param_sum", s,
               (launch_k(conv_param_sum_kernel, (cols + 255) / 256, 256, 0, s, part, rows, C, W, dw,
                                                                         dbias)));

@@ -26,21 +26,30 @@ def _conv_ref(x, w, b=None):
     return y.transpose(1, 2)
 
 
-@pytest.mark.parametrize("B,T,C,W", [(2, 300, 256, 4), (1, 128, 3072, 4), (2, 17, 64, 3)])
-def test_short_conv(LO, B, T, C, W):
+# C % 128 == 0 takes the TMA-streamed kernels (T not a multiple of their 64-token
+# tiles, T = 1, every width); other C the register-window kernels.
+@pytest.mark.parametrize("B,T,C,W,bias", [(2, 300, 256, 4, False), (1, 128, 3072, 4, False),
+                                          (2, 17, 64, 3, False), (1, 200, 384, 3, True),
+                                          (3, 64, 128, 2, False), (1, 1, 128, 4, True),
+                                          (2, 70, 256, 1, False)])
+def test_short_conv(LO, B, T, C, W, bias):
     gen = torch.Generator().manual_seed(T + C)
     x = torch.randn(B, T, C, generator=gen).to(torch.bfloat16).cuda().requires_grad_(True)
     w = (0.3 * torch.randn(C, 1, W, generator=gen)).cuda().requires_grad_(True)
+    b = (0.1 * torch.randn(C, generator=gen)).cuda().requires_grad_(True) if bias else None
     dy = torch.randn(B, T, C, generator=gen).cuda()
-    y = LO.ShortConvFunction.apply(x, w, None)
+    y = LO.ShortConvFunction.apply(x, w, b)
     (y.float() * dy).sum().backward()
     xr = x.detach().float().requires_grad_(True)
     wr = w.detach().clone().requires_grad_(True)
-    yr = _conv_ref(xr, wr)
+    br = b.detach().clone().requires_grad_(True) if bias else None
+    yr = _conv_ref(xr, wr, br)
     (yr * dy).sum().backward()
     assert rel_l2(y, yr) < 1e-2
     assert rel_l2(x.grad, xr.grad) < 1e-2
     assert rel_l2(w.grad, wr.grad) < 1e-2  # dy enters in bf16
+    if bias:
+        assert rel_l2(b.grad, br.grad) < 1e-2
 
 
 def test_gate_act(LO):
