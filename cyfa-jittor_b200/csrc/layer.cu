@@ -773,6 +773,271 @@ __global__ void __launch_bounds__(256, 3) gated_norm_bwd_kernel(GatedNormParams 
   }
 }
 
+// TMA-streamed forward of the biased gated norm: the tile scheme of the backward
+// below (CTA = head x token-tile group, warp 8 loads x and gate tiles, warps 0-7
+// four tokens each), y and rstd stored directly.
+constexpr int kNtRows = 32;
+constexpr int kNtStagesF = 6;
+
+template <int E>
+constexpr int norm_fwd_tma_smem() {
+  return kNtStagesF * 2 * kNtRows * 32 * E * 2 + 1024;
+}
+
+template <int E>
+__global__ void __launch_bounds__(288, 1)
+    gated_norm_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_x,
+                              const __grid_constant__ CUtensorMap map_g, GatedNormParams p) {
+  constexpr int D = 32 * E, LB = 2 * E;
+  constexpr int kTile = kNtRows * D * 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[kNtStagesF], empty[kNtStagesF];
+  __shared__ int s_abort;
+  volatile int* abort_flag = &s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = p.H, G = gridDim.x / H, h = blockIdx.x % H, g = blockIdx.x / H;
+  const int BT = p.rows / H, ntiles = g < G ? (BT + kNtRows - 1) / kNtRows : 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kNtStagesF; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    s_abort = 0;
+    mbar_fence_init();
+    prefetch_tmap(&map_x);
+    prefetch_tmap(&map_g);
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  if (warp == 8) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0, tb = g; tb < ntiles; ++i, tb += G) {
+        const int s = i % kNtStagesF;
+        if (i >= kNtStagesF && !mbar_wait(&empty[s], ((i / kNtStagesF) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* st = smem + s * 2 * kTile;
+        mbar_expect_tx(&full[s], 2 * kTile);
+        tma_load_3d(st, &map_x, &full[s], 0, h, tb * kNtRows);
+        tma_load_3d(st + kTile, &map_g, &full[s], 0, h, tb * kNtRows);
+        issued = i + 1;
+      }
+      for (int i = issued > kNtStagesF ? issued - kNtStagesF : 0; i < issued; ++i)
+        mbar_wait(&full[i % kNtStagesF], (i / kNtStagesF) & 1);
+    }
+    return;
+  }
+  float w[E], bias[E];
+  load_f32_vec<E>(p.w + lane * E, w);
+  if (p.gbias) {
+    load_bf16_vec<E>(p.gbias + size_t(h) * D + lane * E, bias);
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; ++e) bias[e] = 0.f;
+  }
+  const int r0 = warp * 4;
+  for (int i = 0, tb = g; tb < ntiles; ++i, tb += G) {
+    const int s = i % kNtStagesF;
+    const bool got = __all_sync(0xffffffffu, *abort_flag == 0 &&
+                                                 mbar_wait(&full[s], (i / kNtStagesF) & 1));
+    if (!got) {
+      *abort_flag = 1;
+      break;
+    }
+    const uint8_t* st = smem + s * 2 * kTile;
+    // the four rows' reductions interleaved
+    float x[4][E], ss[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      load_bf16_vec<E>(reinterpret_cast<const __nv_bfloat16*>(st + (r0 + u) * D * 2 + lane * LB),
+                       x[u]);
+      ss[u] = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        x[u][e] *= p.scale;
+        ss[u] += x[u][e] * x[u][e];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) ss[u] += __shfl_xor_sync(0xffffffffu, ss[u], o);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int tok = tb * kNtRows + r0 + u;
+      float gt[E];
+      load_bf16_vec<E>(
+          reinterpret_cast<const __nv_bfloat16*>(st + kTile + (r0 + u) * D * 2 + lane * LB), gt);
+      const float rs = rsqrtf(ss[u] / D + p.eps);
+      float y[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) y[e] = x[u][e] * rs * w[e] * sigmoid_fast(gt[e] + bias[e]);
+      if (tok < BT) {
+        const size_t row = size_t(tok) * H + h;
+        store_bf16_vec<E>(p.y + row * D + lane * E, y);
+        if (lane == 0) p.rstd[row] = rs;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+}
+
+// TMA-streamed backward of the biased gated norm.  CTA c owns head h = c % H and
+// the 32-token tiles g, g + G, ... (g = c / H, G = gridDim.x / H) of that head:
+// warp 8 (one lane) brings the tile's x, gate and dy rows ([32, D] each, 3-D maps
+// {D, H, tokens}) into a shared ring, warps 0-7 take four tokens each.  The
+// weight and the head's gate bias stay in registers, so the warp sums of the
+// weight and gate-bias gradients need no per-row head bookkeeping.
+constexpr int kNtStagesB = 4;
+
+template <int E>
+constexpr int norm_bwd_tma_smem() {
+  return kNtStagesB * 3 * kNtRows * 32 * E * 2 + 1024;
+}
+
+template <int E>
+__global__ void __launch_bounds__(288, 1)
+    gated_norm_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_x,
+                              const __grid_constant__ CUtensorMap map_g,
+                              const __grid_constant__ CUtensorMap map_dy, GatedNormParams p) {
+  constexpr int D = 32 * E, LB = 2 * E;
+  constexpr int kTile = kNtRows * D * 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[kNtStagesB], empty[kNtStagesB];
+  __shared__ int s_abort;
+  __shared__ float red[8][D];
+  __shared__ float red_b[8][D];
+  volatile int* abort_flag = &s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = p.H, G = gridDim.x / H, h = blockIdx.x % H, g = blockIdx.x / H;
+  const int BT = p.rows / H, ntiles = g < G ? (BT + kNtRows - 1) / kNtRows : 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kNtStagesB; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    s_abort = 0;
+    mbar_fence_init();
+    prefetch_tmap(&map_x);
+    prefetch_tmap(&map_g);
+    prefetch_tmap(&map_dy);
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  float acc[E], acc_b[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = acc_b[e] = 0.f;
+  if (warp == 8) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0, tb = g; tb < ntiles; ++i, tb += G) {
+        const int s = i % kNtStagesB;
+        if (i >= kNtStagesB && !mbar_wait(&empty[s], ((i / kNtStagesB) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        uint8_t* st = smem + s * 3 * kTile;
+        mbar_expect_tx(&full[s], 3 * kTile);
+        tma_load_3d(st, &map_x, &full[s], 0, h, tb * kNtRows);
+        tma_load_3d(st + kTile, &map_g, &full[s], 0, h, tb * kNtRows);
+        tma_load_3d(st + 2 * kTile, &map_dy, &full[s], 0, h, tb * kNtRows);
+        issued = i + 1;
+      }
+      for (int i = issued > kNtStagesB ? issued - kNtStagesB : 0; i < issued; ++i)
+        mbar_wait(&full[i % kNtStagesB], (i / kNtStagesB) & 1);
+    }
+  } else {
+    float w[E], bias[E];
+    load_f32_vec<E>(p.w + lane * E, w);
+    load_bf16_vec<E>(p.gbias + size_t(h) * D + lane * E, bias);
+    const int r0 = warp * 4;
+    // rstd of the warp's four rows, one tile ahead (lanes 0-3)
+    auto rstd_of = [&](int tb) {
+      const int tok = tb * kNtRows + r0 + lane;
+      return (lane < 4 && tb < ntiles && tok < BT) ? p.rstd[size_t(tok) * H + h] : 0.f;
+    };
+    float rs_cur = rstd_of(g);
+    for (int i = 0, tb = g; tb < ntiles; ++i, tb += G) {
+      const float rs_next = rstd_of(tb + G);
+      const int s = i % kNtStagesB;
+      const bool got = __all_sync(0xffffffffu, *abort_flag == 0 &&
+                                                   mbar_wait(&full[s], (i / kNtStagesB) & 1));
+      if (!got) {
+        *abort_flag = 1;
+        break;
+      }
+      const uint8_t* st = smem + s * 3 * kTile;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int tok = tb * kNtRows + r0 + u;
+        const float rs = __shfl_sync(0xffffffffu, rs_cur, u);
+        float x[E], gt[E], dy[E];
+        const int off = (r0 + u) * D * 2 + lane * LB;
+        load_bf16_vec<E>(reinterpret_cast<const __nv_bfloat16*>(st + off), x);
+        load_bf16_vec<E>(reinterpret_cast<const __nv_bfloat16*>(st + kTile + off), gt);
+        load_bf16_vec<E>(reinterpret_cast<const __nv_bfloat16*>(st + 2 * kTile + off), dy);
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const float sg = sigmoid_fast(gt[e] + bias[e]);
+          const float n = x[e] * p.scale * rs;
+          const float dz = dy[e] * sg;
+          gt[e] = dy[e] * n * w[e] * sg * (1.f - sg);  // dgate
+          dy[e] = dz * w[e];                           // dn
+          x[e] = n;
+          if (tok < BT) {
+            acc[e] += dz * n;
+            acc_b[e] += gt[e];
+          }
+          dot += dy[e] * n;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        dot /= D;
+#pragma unroll
+        for (int e = 0; e < E; ++e) dy[e] = p.scale * rs * (dy[e] - x[e] * dot);  // dx
+        if (tok < BT) {
+          const size_t row = size_t(tok) * H + h;
+          store_bf16_vec<E>(p.dx + row * D + lane * E, dy);
+          store_bf16_vec<E>(p.dgate + row * D + lane * E, gt);
+        }
+      }
+      rs_cur = rs_next;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+  if (warp < 8) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      red[warp][lane * E + e] = acc[e];
+      red_b[warp][lane * E + e] = acc_b[e];
+    }
+  }
+  __syncthreads();
+  const int pc = p.part_cols;
+  float* part = p.part + size_t(blockIdx.x) * pc;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float sw = 0.f, sb = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      sw += red[k][c];
+      sb += red_b[k][c];
+    }
+    part[c] = sw;
+    for (int hh = 0; hh < H; ++hh) part[D + hh * D + c] = hh == h ? sb : 0.f;
+  }
+}
+
 // Fixed-order sums of the short-conv partial rows into dw [C, W] and dbias [C].
 __global__ void __launch_bounds__(256) conv_param_sum_kernel(const float* part, int rows, int C,
                                                              int W, float* dw, float* dbias) {

@@ -30,6 +30,15 @@ static int conv_tmap(CUtensorMap* m, const void* base, int B, int T, int C, long
   return make_tmap_bf16(m, base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+// Rows (token, head) x D bf16, dense, as the 3-D map {D, H, tokens} with a
+// {D, 1, kNtRows} unswizzled box: one head's rows of kNtRows consecutive tokens.
+static int norm_tmap(CUtensorMap* m, const void* base, int H, int BT, int D) {
+  const uint64_t dims[3] = {uint64_t(D), uint64_t(H), uint64_t(BT)};
+  const uint64_t strides[2] = {uint64_t(D) * 2, uint64_t(H) * D * 2};
+  const uint32_t box[3] = {uint32_t(D), 1, uint32_t(kNtRows)};
+  return make_tmap_bf16(m, base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 template <int W>
 static void conv_fwd_tma_launch(const CUtensorMap& mx, const ConvTmaParams& p, int grid,
                                 cudaStream_t s) {
@@ -255,10 +264,29 @@ int cyfa_gated_norm_bias_fwd(const void* x, const void* gate, const void* gate_b
   GatedNormParams p{static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(gate),
                     w, eps, scale, static_cast<__nv_bfloat16*>(y), rstd, nullptr, nullptr, nullptr,
                     nullptr, rows, static_cast<const __nv_bfloat16*>(gate_bias), H, 0};
-  const unsigned grid = unsigned(norm_fwd_blocks(rows, H));
+  unsigned grid = unsigned(norm_fwd_blocks(rows, H));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (D == 256) CYFA_LAUNCH("gated_norm_fwd", s, (launch_k(gated_norm_fwd_kernel<8>, grid, 256, 0, s, p)));
-  else CYFA_LAUNCH("gated_norm_fwd", s, (launch_k(gated_norm_fwd_kernel<4>, grid, 256, 0, s, p)));
+  CUtensorMap mx, mg;
+  const int BT = rows / H;
+  if (norm_tmap(&mx, x, H, BT, D) == kOk && norm_tmap(&mg, gate, H, BT, D) == kOk) {
+    int G = 148 / H;  // persistent CTAs: head x token-tile group
+    if (G > (BT + kNtRows - 1) / kNtRows) G = (BT + kNtRows - 1) / kNtRows;
+    if (G < 1) G = 1;
+    grid = unsigned(H * G);
+    if (D == 256) {
+      set_smem(gated_norm_fwd_tma_kernel<8>, norm_fwd_tma_smem<8>());
+      CYFA_LAUNCH("gated_norm_fwd", s, (launch_k(gated_norm_fwd_tma_kernel<8>, grid, 288,
+                                                 norm_fwd_tma_smem<8>(), s, mx, mg, p)));
+    } else {
+      set_smem(gated_norm_fwd_tma_kernel<4>, norm_fwd_tma_smem<4>());
+      CYFA_LAUNCH("gated_norm_fwd", s, (launch_k(gated_norm_fwd_tma_kernel<4>, grid, 288,
+                                                 norm_fwd_tma_smem<4>(), s, mx, mg, p)));
+    }
+  } else if (D == 256) {
+    CYFA_LAUNCH("gated_norm_fwd", s, (launch_k(gated_norm_fwd_kernel<8>, grid, 256, 0, s, p)));
+  } else {
+    CYFA_LAUNCH("gated_norm_fwd", s, (launch_k(gated_norm_fwd_kernel<4>, grid, 256, 0, s, p)));
+  }
   return launch_status();
 }
 
@@ -293,10 +321,32 @@ int cyfa_gated_norm_bias_bwd(const void* x, const void* gate, const void* gate_b
                     static_cast<const __nv_bfloat16*>(dy), static_cast<__nv_bfloat16*>(dx),
                     static_cast<__nv_bfloat16*>(dgate), part, rows,
                     static_cast<const __nv_bfloat16*>(gate_bias), H, cols};
-  const int nblk = norm_bias_bwd_blocks(rows, H);
+  int nblk = norm_bias_bwd_blocks(rows, H);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (D == 256) CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_kernel<8>, nblk, 256, 0, s, p)));
-  else CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_kernel<4>, nblk, 256, 0, s, p)));
+  CUtensorMap mx, mg, md;
+  const int BT = rows / H;
+  if (norm_tmap(&mx, x, H, BT, D) == kOk && norm_tmap(&mg, gate, H, BT, D) == kOk &&
+      norm_tmap(&md, dy, H, BT, D) == kOk) {
+    // persistent CTAs: head x token-tile group (G groups per head)
+    int G = 148 / H;
+    if (G > (BT + kNtRows - 1) / kNtRows) G = (BT + kNtRows - 1) / kNtRows;
+    if (G > nblk / H) G = nblk / H;
+    if (G < 1) G = 1;
+    nblk = H * G;
+    if (D == 256) {
+      set_smem(gated_norm_bwd_tma_kernel<8>, norm_bwd_tma_smem<8>());
+      CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_tma_kernel<8>, nblk, 288,
+                                                 norm_bwd_tma_smem<8>(), s, mx, mg, md, p)));
+    } else {
+      set_smem(gated_norm_bwd_tma_kernel<4>, norm_bwd_tma_smem<4>());
+      CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_tma_kernel<4>, nblk, 288,
+                                                 norm_bwd_tma_smem<4>(), s, mx, mg, md, p)));
+    }
+  } else if (D == 256) {
+    CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_kernel<8>, nblk, 256, 0, s, p)));
+  } else {
+    CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_kernel<4>, nblk, 256, 0, s, p)));
+  }
   int rc = launch_status();
   if (rc) return rc;
   CYFA_LAUNCH("column_sum", s,
