@@ -730,8 +730,11 @@ __global__ void __launch_bounds__(128) readout_table_kernel(const float* R, cons
   if (r < 127 && m < 127) row[m] = R[(size_t(h) * 127 + r) * 127 + m];
   __syncthreads();
   float acc = 0.f;
-  if (r < 127)
-    for (int k = 0; k < 127; ++k) acc = fmaf(row[k], phi[k * 128 + m], acc);
+  if (r < 127) {
+    // loads issued 16 at a time (the basis comes from L2), then a fixed-order sum
+#pragma unroll 16
+    for (int k = 0; k < 127; ++k) acc = fmaf(row[k], __ldg(phi + k * 128 + m), acc);
+  }
   tab[(size_t(h) * 128 + r) * 128 + m] = __float2bfloat16_rn(acc);
 }
 
@@ -748,7 +751,8 @@ __global__ void __launch_bounds__(128) readout_grad_kernel(const float* dtab, co
   __syncthreads();
   if (k < 127) {
     float acc = 0.f;
-    for (int m = 0; m < 128; ++m) acc = fmaf(row[m], phiT[m * 127 + k], acc);
+#pragma unroll 16
+    for (int m = 0; m < 128; ++m) acc = fmaf(row[m], __ldg(phiT + m * 127 + k), acc);
     dR[(size_t(h) * 127 + r) * 127 + k] = acc;
   }
 }

@@ -90,17 +90,29 @@ __device__ __forceinline__ ScanPair scan1024(float x, float* wsum, float* total)
   }
   if (lane == (REVERSE ? 0 : 31)) wsum[w] = x;
   __syncthreads();
-  float tile_carry = 0.f, block_carry = 0.f;
-  const int t0 = w & ~3;  // first warp of this 128-token tile
-  if (!REVERSE) {
-    for (int i = 0; i < w; ++i) block_carry = __fadd_rn(block_carry, wsum[i]);
-    for (int i = t0; i < w; ++i) tile_carry = __fadd_rn(tile_carry, wsum[i]);
-  } else {
-    for (int i = 31; i > w; --i) block_carry = __fadd_rn(block_carry, wsum[i]);
-    for (int i = t0 + 3; i > w; --i) tile_carry = __fadd_rn(tile_carry, wsum[i]);
+  // every warp scans the 32 warp sums with shuffles (a fixed tree order): the
+  // block scan over all warps and the scan within each group of 4 warps (tile)
+  const float ws = wsum[lane];
+  float bs = ws, ts = ws;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float y = REVERSE ? __shfl_down_sync(0xffffffffu, bs, o) : __shfl_up_sync(0xffffffffu, bs, o);
+    if (REVERSE ? (lane + o < 32) : (lane >= o)) bs = __fadd_rn(bs, y);
   }
-  float tot = 0.f;
-  for (int i = 0; i < 32; ++i) tot = __fadd_rn(tot, wsum[REVERSE ? 31 - i : i]);
+#pragma unroll
+  for (int o = 1; o < 4; o <<= 1) {
+    const float y = REVERSE ? __shfl_down_sync(0xffffffffu, ts, o) : __shfl_up_sync(0xffffffffu, ts, o);
+    if (REVERSE ? ((lane & 3) + o < 4) : ((lane & 3) >= o)) ts = __fadd_rn(ts, y);
+  }
+  // carries of warp w: the (tile / block) scans up to warp w - 1 (REVERSE: from w + 1)
+  const int src = REVERSE ? w + 1 : w - 1;
+  const bool first_b = REVERSE ? w == 31 : w == 0;
+  const bool first_t = REVERSE ? (w & 3) == 3 : (w & 3) == 0;
+  const float bsrc = __shfl_sync(0xffffffffu, bs, src & 31);
+  const float tsrc = __shfl_sync(0xffffffffu, ts, src & 31);
+  const float block_carry = first_b ? 0.f : bsrc;
+  const float tile_carry = first_t ? 0.f : tsrc;
+  const float tot = __shfl_sync(0xffffffffu, bs, REVERSE ? 0 : 31);
   __syncthreads();
   *total = tot;
   return {__fadd_rn(x, tile_carry), __fadd_rn(x, block_carry)};
