@@ -24,6 +24,10 @@ static void set_smem(Kern k, int bytes) {
   const auto key = std::make_tuple(reinterpret_cast<const void*>(k), dev, bytes);
   std::lock_guard<std::mutex> lk(mu);
   if (done.count(key)) return;
+  // the largest shared-memory carveout, so that kernels sized for two CTAs per SM
+  // get them (the default carveout may leave room for one)
+  cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout,
+                       cudaSharedmemCarveoutMaxShared);
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess)
     done.insert(key);
 }

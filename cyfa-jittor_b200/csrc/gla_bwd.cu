@@ -78,7 +78,10 @@ __global__ void __launch_bounds__(256, 1)
     mbar_init(&bar_mma, 1);
     mbar_fence_init();
   }
-  if (warp == 0) tmem_alloc(&tmem_base, 256);
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 256);
+    tmem_relinquish();  // one allocation per CTA: let co-resident CTAs allocate
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -254,7 +257,10 @@ __global__ void __launch_bounds__(kDualThreads, 1)
     s_abort = 0;
     mbar_fence_init();
   }
-  if (warp == 0) tmem_alloc(&tmem_base, 512);
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 512);
+    tmem_relinquish();  // one allocation per CTA: let co-resident CTAs allocate
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -508,7 +514,10 @@ __global__ void __launch_bounds__(256, 1)
     mbar_init(&bar_ld, 1);
     mbar_fence_init();
   }
-  if (warp == 0) tmem_alloc(&tmem_base, 512);
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 512);
+    tmem_relinquish();  // one allocation per CTA: let co-resident CTAs allocate
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();

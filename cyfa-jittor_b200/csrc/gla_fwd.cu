@@ -168,7 +168,10 @@ __global__ void __launch_bounds__(kScanThreads, 1)
       prefetch_tmap(&map_ff);
     }
   }
-  if (warp == 0) tmem_alloc(&tmem_base, 64 * kScanBufs);
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 64 * kScanBufs);
+    tmem_relinquish();  // one allocation per CTA: let co-resident CTAs allocate
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -393,11 +396,20 @@ struct TileFwdParams {
   __nv_bfloat16* weights;  // READOUT: [BH, TP, 128]
 };
 
-template <int DK>
+// The output pass without the readout at DK = 128 runs lean, two CTAs per SM:
+// V is loaded into the S region once Q S_j is done, the output staging uses the
+// Q region, and P V accumulates into the Q K^T columns of TMEM (256 columns).
+template <int DK, bool READOUT>
+constexpr bool tile_fwd_lean() {
+  return DK == 128 && !READOUT;
+}
+
+template <int DK, bool READOUT = true>
 constexpr int tile_fwd_smem() {
   // Q | K | S | V, plus (DK = 128) a 16 KiB staging area for the output stores;
   // with DK = 256 the staging uses the S region, free once the MMAs are done
-  return 3 * DK * 256 + 32768 + 1024 + (DK == 256 ? 0 : 16384);
+  return tile_fwd_lean<DK, READOUT>() ? 3 * DK * 256 + 1024
+                                      : 3 * DK * 256 + 32768 + 1024 + (DK == 256 ? 0 : 16384);
 }
 
 // 8 warps: warp w owns TMEM lane quadrant (w & 3) (token rows 32(w&3)..+31) and
@@ -422,6 +434,9 @@ __global__ void __launch_bounds__(256, 1)
   const int r = quad * 32 + lane;
   const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT, dv0 = blockIdx.y * 128;
   const int t = j * 128 + r;
+  constexpr bool kLean = tile_fwd_lean<DK, READOUT>();
+  constexpr uint32_t kTmemCols = kLean ? 256 : 512;
+  constexpr uint32_t kPV = kLean ? 0 : 256;  // TMEM column of the P V accumulator
 
   if (tid == 0) {
     mbar_init(&bar_in, 1);
@@ -430,7 +445,10 @@ __global__ void __launch_bounds__(256, 1)
     for (int i = 0; i < 5; ++i) mbar_init(&bar_m[i], 1);
     mbar_fence_init();
   }
-  if (warp == 0) tmem_alloc(&tmem_base, 512);
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, kTmemCols);
+    tmem_relinquish();  // one allocation per CTA: let co-resident CTAs allocate
+  }
   pdl_wait();
   if (tid < 128) Gs[tid] = p.G[size_t(bh) * p.TP + j * 128 + tid];
   tc_fence_before();
@@ -448,8 +466,10 @@ __global__ void __launch_bounds__(256, 1)
     load_token_tile(smem + kQ, &map_q, kRows2D, bh, p.H, p.TP, j, 0, DK, &bar_in);
     load_token_tile(smem + kK, &map_k, kRows2D, bh, p.H, p.TP, j, 0, DK, &bar_in);
     load_hist_tile(smem + kS, &map_s, (bh * p.NT + j) * DK, dv0, 128, DK, &bar_in);
-    mbar_expect_tx(&bar_v, 32768);
-    load_token_tile(smem + kV, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 128, &bar_v);
+    if (!kLean) {
+      mbar_expect_tx(&bar_v, 32768);
+      load_token_tile(smem + kV, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 128, &bar_v);
+    }
     if (mbar_wait(&bar_in, 0)) {
       tc_fence_after();
       // S_qk = Q K^T -> TMEM[0,128); O_inter = Q S_j -> TMEM[128,256)
@@ -463,9 +483,19 @@ __global__ void __launch_bounds__(256, 1)
         umma_bf16(tmem + 128, kmaj_desc(sQ, 128, ks), mnmaj_desc(sS, DK, ks),
                   make_idesc(128, 128, 0, 1), ks > 0);
       umma_commit(&bar_m[1]);
+      if (kLean) {
+        // V into the S region once Q S_j has read it
+        if (mbar_wait(&bar_m[1], 0)) {
+          mbar_expect_tx(&bar_v, 32768);
+          load_token_tile(smem + kS, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 128, &bar_v);
+        } else {
+          mbar_arrive(&bar_v);
+        }
+      }
     } else {
       mbar_arrive(&bar_m[0]);
       mbar_arrive(&bar_m[1]);
+      if (kLean) mbar_arrive(&bar_v);
     }
   }
   const float gt = Gs[r];
@@ -497,9 +527,10 @@ __global__ void __launch_bounds__(256, 1)
     bool vok = ok && mbar_wait(&bar_v, 0);
     tc_fence_after();
     if (vok) {
+      const uint32_t sVv = kLean ? sS : sV;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks)
-        umma_bf16(tmem + 256, kmaj_desc(sK, 128, ks), mnmaj_desc(sV, 128, ks),
+        umma_bf16(tmem + kPV, kmaj_desc(sK, 128, ks), mnmaj_desc(sVv, 128, ks),
                   make_idesc(128, 128, 0, 1), ks > 0);
       umma_commit(&bar_m[2]);
     } else {
@@ -523,14 +554,14 @@ __global__ void __launch_bounds__(256, 1)
   // per-warp staging for coalesced output stores (8 rows x 64 bytes per
   // instruction): the S region, free once the MMAs above are done, when DK = 256
   // (with DK = 128 the READOUT z tile lives there, so a separate area is used)
-  const uint32_t scratch = (DK == 256 ? sS : sV + 32768) + warp * 2048;
+  const uint32_t scratch = (kLean ? sQ : (DK == 256 ? sS : sV + 32768)) + warp * 2048;
   const int t0 = j * 128 + quad * 32;  // first token row of this warp
   if (__all_sync(0xffffffffu, ok)) {
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
       const int col0 = half * 64 + 32 * c;
       float a[32], b[32];
-      tmem_ld32x2(lane_tmem + 128 + col0, a, lane_tmem + 256 + col0, b);
+      tmem_ld32x2(lane_tmem + 128 + col0, a, lane_tmem + kPV + col0, b);
 #pragma unroll
       for (int i = 0; i < 32; ++i) a[i] = p.scale * (eg * a[i] + b[i]);
       if (p.o_mode == 1) {
@@ -644,7 +675,7 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, kTmemCols);
   }
 }
 

@@ -30,7 +30,10 @@ __global__ void __launch_bounds__(128) umma_selftest_kernel(
     mbar_init(&bar_mma, 1);
     mbar_fence_init();
   }
-  if (warp == 0) tmem_alloc(&tmem_base, 256);
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 256);
+    tmem_relinquish();  // one allocation per CTA: let co-resident CTAs allocate
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
