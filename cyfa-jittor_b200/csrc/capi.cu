@@ -164,6 +164,16 @@ static int tmap_2d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t col
   return make_tmap_bf16(m, base, 2, dims, strides, box);
 }
 
+// Public-layout [B, T, H, K] bf16 rows `stride` elements apart as the 3-D map
+// {H*K, T, B} with an unswizzled {K, 32, 1} box (one head's 32-token tile).
+static int token_tmap(CUtensorMap* m, const void* base, int B, int T, int H, int K,
+                      long long stride) {
+  const uint64_t dims[3] = {uint64_t(H) * K, uint64_t(T), uint64_t(B)};
+  const uint64_t strides[2] = {uint64_t(stride) * 2, uint64_t(stride) * 2 * uint64_t(T)};
+  const uint32_t box[3] = {uint32_t(K), 32, 1};
+  return make_tmap_bf16(m, base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 }  // namespace cyfa
 
 using namespace cyfa;
@@ -189,8 +199,24 @@ static int token_fwd_launch(const void* q, const void* k, const float* q_norm_we
                    static_cast<__nv_bfloat16*>(w), q_rs, k_rs, B, T, H, TP, q_eps, k_eps,
                    q_stride, k_stride};
   const size_t rows = size_t(B) * H * TP;
-  const dim3 grid(unsigned(token_fwd_blocks(rows)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap mq, mk;
+  if (token_tmap(&mq, q, B, T, H, K, q_stride) == kOk &&
+      token_tmap(&mk, k, B, T, H, K, k_stride) == kOk) {
+    const int ntiles = B * H * (TP / kTfRows);
+    const unsigned grid = unsigned(ntiles < 148 ? ntiles : 148);  // persistent
+    if (K == 256) {
+      set_smem(token_fwd_tma_kernel<256>, token_fwd_tma_smem<256>());
+      CYFA_LAUNCH("token_fwd", s, launch_k(token_fwd_tma_kernel<256>, grid, 288,
+                                           token_fwd_tma_smem<256>(), s, mq, mk, p));
+    } else {
+      set_smem(token_fwd_tma_kernel<128>, token_fwd_tma_smem<128>());
+      CYFA_LAUNCH("token_fwd", s, launch_k(token_fwd_tma_kernel<128>, grid, 288,
+                                           token_fwd_tma_smem<128>(), s, mq, mk, p));
+    }
+    return launch_status();
+  }
+  const dim3 grid(unsigned(token_fwd_blocks(rows)));
   if (K == 256) CYFA_LAUNCH("token_fwd", s, launch_k(token_fwd_kernel<256>, grid, 256, 0, s, p));
   else CYFA_LAUNCH("token_fwd", s, launch_k(token_fwd_kernel<128>, grid, 256, 0, s, p));
   return launch_status();

@@ -257,6 +257,153 @@ inline int token_fwd_blocks(size_t rows) {
 template __global__ void token_fwd_kernel<256>(TokenFwdParams);
 template __global__ void token_fwd_kernel<128>(TokenFwdParams);
 
+// TMA-streamed token_fwd: persistent CTAs take 32-token tiles of one (b, h); warp
+// 8 (one lane) loads the tile's q and k rows ([32, K] boxes of 3-D maps {H*K, T, B}
+// over the token-strided inputs, rows past T read as zeros) into a shared ring,
+// warps 0-7 take four tokens each with the norm weights in registers.  Same
+// outputs and arithmetic as token_fwd_kernel.
+constexpr int kTfRows = 32;
+constexpr int kTfStages = 6;
+
+template <int K>
+constexpr int token_fwd_tma_smem() {
+  return kTfStages * 2 * kTfRows * K * 2 + 1024;
+}
+
+template <int K>
+__global__ void __launch_bounds__(288, 1)
+    token_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_q,
+                         const __grid_constant__ CUtensorMap map_k, TokenFwdParams p) {
+  constexpr int E = K / 32;
+  constexpr int kTile = kTfRows * K * 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[kTfStages], empty[kTfStages];
+  __shared__ int s_abort;
+  volatile int* abort_flag = &s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = p.TP / kTfRows, ntiles = p.B * p.H * nb;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTfStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    s_abort = 0;
+    mbar_fence_init();
+    prefetch_tmap(&map_q);
+    prefetch_tmap(&map_k);
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  if (warp == 8) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0, k = blockIdx.x; k < ntiles; ++i, k += gridDim.x) {
+        const int s = i % kTfStages;
+        if (i >= kTfStages && !mbar_wait(&empty[s], ((i / kTfStages) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        const int bh = k / nb, t0 = (k % nb) * kTfRows;
+        uint8_t* st = smem + s * 2 * kTile;
+        mbar_expect_tx(&full[s], 2 * kTile);
+        tma_load_3d(st, &map_q, &full[s], (bh % p.H) * K, t0, bh / p.H);
+        tma_load_3d(st + kTile, &map_k, &full[s], (bh % p.H) * K, t0, bh / p.H);
+        issued = i + 1;
+      }
+      for (int i = issued > kTfStages ? issued - kTfStages : 0; i < issued; ++i)
+        mbar_wait(&full[i % kTfStages], (i / kTfStages) & 1);
+    }
+    return;
+  }
+  float qw[E], kw[E];
+  load_f32_vec<E>(p.qw + lane * E, qw);
+  load_f32_vec<E>(p.kw + lane * E, kw);
+  const int r0 = warp * 4;
+  // lam and beta of the warp's four rows (lanes 0-3), one tile ahead
+  auto scal = [&](int k) {
+    float2 v = make_float2(0.f, 0.f);
+    if (lane < 4 && k < ntiles) {
+      const size_t row = size_t(k / nb) * p.TP + (k % nb) * kTfRows + r0 + lane;
+      v = make_float2(p.lam[row], p.beta_h[row]);
+    }
+    return v;
+  };
+  float2 sc_cur = scal(blockIdx.x);
+  for (int i = 0, k = blockIdx.x; k < ntiles; ++i, k += gridDim.x) {
+    const float2 sc_next = scal(k + gridDim.x);
+    const int s = i % kTfStages;
+    const bool got = __all_sync(0xffffffffu, *abort_flag == 0 &&
+                                                 mbar_wait(&full[s], (i / kTfStages) & 1));
+    if (!got) {
+      *abort_flag = 1;
+      break;
+    }
+    const int bh = k / nb, t0 = (k % nb) * kTfRows;
+    const uint8_t* st = smem + s * 2 * kTile;
+    // the four rows' two norms reduced together
+    float qv[4][E], kv[4][E], q2[4], k2[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int off = (r0 + u) * K * 2 + lane * E * 2;
+      load_bf16_vec<E>(reinterpret_cast<const __nv_bfloat16*>(st + off), qv[u]);
+      load_bf16_vec<E>(reinterpret_cast<const __nv_bfloat16*>(st + kTile + off), kv[u]);
+      q2[u] = k2[u] = 0.f;
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        q2[u] += qv[u][j] * qv[u][j];
+        k2[u] += kv[u][j] * kv[u][j];
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        q2[u] += __shfl_xor_sync(0xffffffffu, q2[u], o);
+        k2[u] += __shfl_xor_sync(0xffffffffu, k2[u], o);
+      }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = t0 + r0 + u;
+      const bool real = t < p.T;
+      const size_t row = size_t(bh) * p.TP + t;
+      const float lam = __shfl_sync(0xffffffffu, sc_cur.x, u);
+      const float bt = __shfl_sync(0xffffffffu, sc_cur.y, u);
+      const float qr = rsqrtf(q2[u] / K + p.q_eps), kr = rsqrtf(k2[u] / K + p.k_eps);
+      float qo[E], ko[E];
+#pragma unroll
+      for (int j = 0; j < E; ++j) {
+        qo[j] = qv[u][j] * qr * qw[j];
+        ko[j] = kv[u][j] * kr * kw[j];
+      }
+      store_bf16_vec<E>(p.qn + row * K + lane * E, qo);
+      store_bf16_vec<E>(p.kn + row * K + lane * E, ko);
+      if (lane == 0) {
+        p.q_rs[row] = real ? qr : 0.f;
+        p.k_rs[row] = real ? kr : 0.f;
+      }
+      // write vector: lane handles pairs lane and lane + 32 (|phase| <= pi)
+      uint32_t wo[2];
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        const int pair = lane + 32 * part;
+        float sn, cs;
+        __sincosf(clock_phase(lam, pair), &sn, &cs);
+        const float a = bt * atom_scale(pair);
+        wo[part] = pack_bf16(a * cs, -a * sn);
+      }
+      uint32_t* wrow = reinterpret_cast<uint32_t*>(p.w + row * 128);
+      wrow[lane] = wo[0];
+      wrow[lane + 32] = wo[1];
+    }
+    sc_cur = sc_next;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+}
+
 struct TokenBwdParams {
   const __nv_bfloat16* q;   // [B,T,H,K]
   const __nv_bfloat16* k;
