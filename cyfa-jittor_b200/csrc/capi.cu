@@ -230,7 +230,7 @@ static int token_bwd_launch(const void* q, const void* k, const float* q_norm_we
                             float* dbeta_h, int B,
                             int T, int H, int K, long long q_stride, long long k_stride,
                             long long dq_stride, long long dk_stride, bool grads_bf16,
-                            void* stream) {
+                            void* stream, int* nblk_out = nullptr) {
   CYFA_REQUIRE(q && k && q_norm_weight && k_norm_weight && q_rs && k_rs && dqn && dkn && lam &&
                    beta_h && dw && dq && dk && dqw_part && dkw_part && dlam && dbeta_h,
                kNullPointer);
@@ -250,6 +250,37 @@ static int token_bwd_launch(const void* q, const void* k, const float* q_norm_we
   const size_t rows = size_t(B) * H * TP;
   const dim3 grid(unsigned(token_bwd_blocks(rows)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // with bf16 gradients, for a caller that takes the partial-row count: the
+  // TMA-streamed kernel (one partial row per persistent CTA)
+  CUtensorMap mq, mk, mdq, mdk, mdw, mdwb;
+  auto map2 = [&](CUtensorMap* m, const void* base, int cols) {
+    const uint64_t dims[2] = {uint64_t(cols), uint64_t(rows)};
+    const uint64_t strides[1] = {uint64_t(cols) * 2};
+    const uint32_t box[2] = {uint32_t(cols), 32};
+    return make_tmap_bf16(m, base, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  };
+  if (grads_bf16 && nblk_out && token_tmap(&mq, q, B, T, H, K, q_stride) == kOk &&
+      token_tmap(&mk, k, B, T, H, K, k_stride) == kOk && map2(&mdq, dqn, K) == kOk &&
+      map2(&mdk, dkn, K) == kOk && map2(&mdw, dw, 128) == kOk &&
+      (!dw_b || map2(&mdwb, dw_b, 128) == kOk)) {
+    if (!dw_b) mdwb = mdw;
+    const int ntiles = B * H * (TP / kTbRows);
+    const unsigned g = unsigned(ntiles < 148 ? ntiles : 148);  // persistent
+    if (K == 256) {
+      set_smem(token_bwd_tma_kernel<256>, token_bwd_tma_smem<256>());
+      CYFA_LAUNCH("token_bwd", s, (launch_k(token_bwd_tma_kernel<256>, g, 288,
+                                            token_bwd_tma_smem<256>(), s, mq, mk, mdq, mdk, mdw,
+                                            mdwb, p)));
+    } else {
+      set_smem(token_bwd_tma_kernel<128>, token_bwd_tma_smem<128>());
+      CYFA_LAUNCH("token_bwd", s, (launch_k(token_bwd_tma_kernel<128>, g, 288,
+                                            token_bwd_tma_smem<128>(), s, mq, mk, mdq, mdk, mdw,
+                                            mdwb, p)));
+    }
+    *nblk_out = int(g);
+    return launch_status();
+  }
+  if (nblk_out) *nblk_out = int(grid.x);
   if (grads_bf16) {
     if (K == 256)
       CYFA_LAUNCH("token_bwd", s, (launch_k(token_bwd_kernel<256, __nv_bfloat16>, grid, 256, 0, s, p)));

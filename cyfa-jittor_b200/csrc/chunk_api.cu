@@ -421,14 +421,14 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     if ((rc = dual(m_A64, m_draw64, m_kn, m_h1_64, v1))) return rc;
   }
   // ================= norms, write vector, gates, clock
+  int nblk = 0;  // partial rows of the norm-weight gradients
   rc = token_bwd_launch(a->q, a->k, a->q_norm_weight, a->k_norm_weight, s.q_rs, s.k_rs, w.dq1,
                         w.dk1, s.lam, s.beta_h, w.dw, w.dw_b, g->dq, g->dk, w.dqw_part, w.dkw_part,
                         w.dlam_w, w.dbeta_h, d.B, d.T, d.H, d.K,
                         stride_or(a->q_stride, d.H * d.K), stride_or(a->k_stride, d.H * d.K),
                         stride_or(g->dq_stride, d.H * d.K), stride_or(g->dk_stride, d.H * d.K),
-                        true, stream);
+                        true, stream, &nblk);
   if (rc) return rc;
-  const int nblk = token_bwd_blocks(rows);
   CYFA_LAUNCH("column_sum", st,
               (launch_k(column_sum_kernel, dim3((d.K + 31) / 32, 2), 1024, 0, st, w.dqw_part,
                         g->dq_norm_weight, nblk, d.K, w.dkw_part, g->dk_norm_weight, 0x7fffffff,

@@ -606,6 +606,208 @@ __global__ void __launch_bounds__(256, 3) token_bwd_kernel(TokenBwdParams p) {
   }
 }
 
+// TMA-streamed token_bwd for bf16 incoming gradients: persistent CTAs take
+// 32-token tiles of one (b, h); warp 8 (one lane) loads the tile's q, k (public
+// layout, 3-D maps), dqn, dkn, dw and dw_b rows (head-major, 2-D maps) into a
+// two-stage shared ring; warps 0-7 take four tokens each.  Same arithmetic as
+// token_bwd_kernel; each CTA writes one row of norm-weight partials (gridDim.x rows).
+constexpr int kTbRows = 32;
+constexpr int kTbStages = 2;
+
+template <int K>
+constexpr int token_bwd_tma_stage() {
+  return kTbRows * (4 * K + 2 * 128) * 2;  // q | k | dqn | dkn | dw | dw_b
+}
+template <int K>
+constexpr int token_bwd_tma_smem() {
+  return kTbStages * token_bwd_tma_stage<K>() + 1024;
+}
+
+template <int K>
+__global__ void __launch_bounds__(288, 1)
+    token_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_q,
+                         const __grid_constant__ CUtensorMap map_k,
+                         const __grid_constant__ CUtensorMap map_dqn,
+                         const __grid_constant__ CUtensorMap map_dkn,
+                         const __grid_constant__ CUtensorMap map_dw,
+                         const __grid_constant__ CUtensorMap map_dwb, TokenBwdParams p) {
+  constexpr int E = K / 32;
+  constexpr int kT = kTbRows * K * 2, kW = kTbRows * 128 * 2;
+  constexpr int oQ = 0, oK = kT, oDQ = 2 * kT, oDK = 3 * kT, oDW = 4 * kT, oDWB = 4 * kT + kW;
+  constexpr int kStage = token_bwd_tma_stage<K>();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full[kTbStages], empty[kTbStages];
+  __shared__ int s_abort;
+  __shared__ float part_s[2][8][K];
+  volatile int* abort_flag = &s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nb = p.TP / kTbRows, ntiles = p.B * p.H * nb;
+  const bool has_b = p.dw_b != nullptr;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTbStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    s_abort = 0;
+    mbar_fence_init();
+    prefetch_tmap(&map_q);
+    prefetch_tmap(&map_k);
+    prefetch_tmap(&map_dqn);
+    prefetch_tmap(&map_dkn);
+    prefetch_tmap(&map_dw);
+    if (has_b) prefetch_tmap(&map_dwb);
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  float acc_q[E], acc_k[E];
+#pragma unroll
+  for (int j = 0; j < E; ++j) acc_q[j] = acc_k[j] = 0.f;
+  if (warp == 8) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0, k = blockIdx.x; k < ntiles; ++i, k += gridDim.x) {
+        const int s = i % kTbStages;
+        if (i >= kTbStages && !mbar_wait(&empty[s], ((i / kTbStages) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        const int bh = k / nb, t0 = (k % nb) * kTbRows, row0 = bh * p.TP + t0;
+        uint8_t* st = smem + s * kStage;
+        mbar_expect_tx(&full[s], 4 * kT + (has_b ? 2 : 1) * kW);
+        tma_load_3d(st + oQ, &map_q, &full[s], (bh % p.H) * K, t0, bh / p.H);
+        tma_load_3d(st + oK, &map_k, &full[s], (bh % p.H) * K, t0, bh / p.H);
+        tma_load_2d(st + oDQ, &map_dqn, &full[s], 0, row0);
+        tma_load_2d(st + oDK, &map_dkn, &full[s], 0, row0);
+        tma_load_2d(st + oDW, &map_dw, &full[s], 0, row0);
+        if (has_b) tma_load_2d(st + oDWB, &map_dwb, &full[s], 0, row0);
+        issued = i + 1;
+      }
+      for (int i = issued > kTbStages ? issued - kTbStages : 0; i < issued; ++i)
+        mbar_wait(&full[i % kTbStages], (i / kTbStages) & 1);
+    }
+  } else {
+    float wq[E], wk[E];
+    load_f32_vec<E>(p.qw + lane * E, wq);
+    load_f32_vec<E>(p.kw + lane * E, wk);
+    const int r0 = warp * 4;
+    // q_rs, k_rs, lam, beta of the warp's four rows (lanes 0-3), one tile ahead
+    auto scal = [&](int k) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (lane < 4 && k < ntiles) {
+        const size_t row = size_t(k / nb) * p.TP + (k % nb) * kTbRows + r0 + lane;
+        v = make_float4(p.q_rs[row], p.k_rs[row], p.lam[row], p.beta_h[row]);
+      }
+      return v;
+    };
+    float4 sc_cur = scal(blockIdx.x);
+    for (int i = 0, k = blockIdx.x; k < ntiles; ++i, k += gridDim.x) {
+      const float4 sc_next = scal(k + gridDim.x);
+      const int s = i % kTbStages;
+      const bool got = __all_sync(0xffffffffu, *abort_flag == 0 &&
+                                                   mbar_wait(&full[s], (i / kTbStages) & 1));
+      if (!got) {
+        *abort_flag = 1;
+        break;
+      }
+      const int bh = k / nb, t0 = (k % nb) * kTbRows;
+      const int b = bh / p.H, h = bh % p.H;
+      const uint8_t* st = smem + s * kStage;
+#pragma unroll 1
+      for (int u = 0; u < 4; ++u) {
+        const int t = t0 + r0 + u;
+        const bool real = t < p.T;
+        const size_t row = size_t(bh) * p.TP + t;
+        const float rq = __shfl_sync(0xffffffffu, sc_cur.x, u);
+        const float rk = __shfl_sync(0xffffffffu, sc_cur.y, u);
+        const float lam = __shfl_sync(0xffffffffu, sc_cur.z, u);
+        const float bt = __shfl_sync(0xffffffffu, sc_cur.w, u);
+        const int off = (r0 + u) * K * 2 + lane * E * 2;
+        float xq_[E], gq_[E], xk_[E], gk_[E];
+        load_bf16_vec<E>(reinterpret_cast<const __nv_bfloat16*>(st + oQ + off), xq_);
+        load_bf16_vec<E>(reinterpret_cast<const __nv_bfloat16*>(st + oK + off), xk_);
+        load_bf16_vec<E>(reinterpret_cast<const __nv_bfloat16*>(st + oDQ + off), gq_);
+        load_bf16_vec<E>(reinterpret_cast<const __nv_bfloat16*>(st + oDK + off), gk_);
+        float dotq = 0.f, dotk = 0.f;
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          dotq += gq_[j] * wq[j] * xq_[j];
+          dotk += gk_[j] * wk[j] * xk_[j];
+        }
+        // write-vector adjoint (ops/utils.py:598-616) of dw + dw_b
+        float dl = 0.f, db = 0.f;
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          const int pair = lane + 32 * part;
+          const int woff = (r0 + u) * 256 + pair * 4;
+          float2 dwp = __bfloat1622float2(
+              *reinterpret_cast<const __nv_bfloat162*>(st + oDW + woff));
+          if (has_b) {
+            const float2 e2 = __bfloat1622float2(
+                *reinterpret_cast<const __nv_bfloat162*>(st + oDWB + woff));
+            dwp.x += e2.x;
+            dwp.y += e2.y;
+          }
+          float sn, cs;
+          __sincosf(clock_phase(lam, pair), &sn, &cs);
+          const float sc = atom_scale(pair);
+          db += dwp.x * sc * cs - dwp.y * sc * sn;
+          dl += (-dwp.x * bt * sc * sn - dwp.y * bt * sc * cs) * (pair * kTwoPiOver127);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          dotq += __shfl_xor_sync(0xffffffffu, dotq, o);
+          dotk += __shfl_xor_sync(0xffffffffu, dotk, o);
+          dl += __shfl_xor_sync(0xffffffffu, dl, o);
+          db += __shfl_xor_sync(0xffffffffu, db, o);
+        }
+        dotq *= rq * rq / K;
+        dotk *= rk * rk / K;
+        float oq[E], ok[E];
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+          oq[j] = (gq_[j] * wq[j] - xq_[j] * dotq) * rq;
+          ok[j] = (gk_[j] * wk[j] - xk_[j] * dotk) * rk;
+          acc_q[j] += xq_[j] * rq * gq_[j];
+          acc_k[j] += xk_[j] * rk * gk_[j];
+        }
+        if (real) {
+          const size_t tok = size_t(b) * p.T + t, col = size_t(h) * K + lane * E;
+          store_bf16_vec<E>(p.dq + tok * p.dq_stride + col, oq);
+          store_bf16_vec<E>(p.dk + tok * p.dk_stride + col, ok);
+        }
+        if (lane == 0) {
+          p.dlam[row] = dl;
+          p.dbeta[row] = db;
+        }
+      }
+      sc_cur = sc_next;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+  if (warp < 8) {
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+      part_s[0][warp][lane * E + j] = acc_q[j];
+      part_s[1][warp][lane * E + j] = acc_k[j];
+    }
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < K; d += blockDim.x) {
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sq += part_s[0][i][d];
+      sk += part_s[1][i][d];
+    }
+    p.dqw_part[size_t(blockIdx.x) * K + d] = sq;
+    p.dkw_part[size_t(blockIdx.x) * K + d] = sk;
+  }
+}
+
 // Number of blocks (= partial rows) token_bwd_kernel uses for a shape: three per SM.
 inline int token_bwd_blocks(size_t rows) {
   const size_t want = (rows + 7) / 8;
