@@ -97,6 +97,21 @@ def _peaks():
         return PEAKS_FALLBACK, "fallback"
 
 
+def _step_traffic_from_profiles():
+    """DRAM bytes of all libcyfa launches of one c3 layer step (committed ncu summary)."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
+    total = 0.0
+    try:
+        with open(path) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 3 and not line.startswith("#"):
+                    total += float(parts[1]) * float(parts[2])
+    except (OSError, ValueError):
+        return None
+    return total or None
+
+
 def _traffic_from_profiles(kernel):
     """Per-launch DRAM bytes of `kernel` from the committed ncu summary, if any."""
     path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
@@ -554,6 +569,26 @@ def run_cyfa(args, rank, world, local_rank):
         roofline.update({"launches_per_step": n, "ms_per_step": ms,
                          "kernel_ms": {k: round(v[0], 4) for k, v in sorted(prof.items())}})
 
+    # the whole step against its two rooflines: the cuBLAS GEMMs (projection, output
+    # gate, o_proj; forward, data and weight gradients) at the bf16 tensor peak, the
+    # libcyfa kernels' DRAM traffic (committed ncu capture of this c3 step) at the
+    # HBM copy bandwidth
+    layer_roofline = None
+    core_bytes = _step_traffic_from_profiles() if args.workload == "c3" else None
+    if core_bytes:
+        hid, H, hd = CFG["hidden"], CFG["heads"], CFG["head_dim"]
+        n_used = 3 * H * hd + hd + 3 * H
+        gemm_flop = 3 * 2 * B * T * (hid * n_used + hd * H * hd + H * hd * hid)
+        tf = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+        gbs = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+        t_gemm = gemm_flop / (tf * 1e12) * 1e3
+        t_core = core_bytes / (gbs * 1e9) * 1e3
+        layer_roofline = {"gemm_tflop": gemm_flop / 1e12, "core_dram_gb": core_bytes / 1e9,
+                          "gemm_ms_at_peak": t_gemm, "core_ms_at_peak": t_core,
+                          "roofline_ms": t_gemm + t_core, "frac": (t_gemm + t_core) / ms_per_step,
+                          "peaks": f"{peak_kind} bf16 {tf} TFLOP/s, HBM {gbs} GB/s",
+                          "traffic_source": "profiles/dram_traffic.txt"}
+
     decode = None if args.no_decode else measure_decode(args, rank, world, dev, peaks, barrier)
     op = None if args.no_op else measure_op(args, rank, world, dev, peaks, barrier)
 
@@ -576,6 +611,7 @@ def run_cyfa(args, rank, world, local_rank):
                        "l2": "flushed between timed steps (2x126 MiB write outside the events)",
                        "launch": "whole step (fwd, bwd, grad all-reduce) replayed as one CUDA graph"},
             "roofline": roofline,
+            "layer_roofline": layer_roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,
