@@ -25,10 +25,12 @@ import subprocess
 import sys
 import time
 
-# Keep stdout to the one JSON line: an image-wide NCCL_DEBUG=VERSION makes NCCL
-# print its version banner there.  Must be set before torch (and NCCL) load.
-if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
-    os.environ["NCCL_DEBUG"] = "WARN"
+# Keep stdout to the one JSON line: NCCL logs to stdout, and any NCCL_DEBUG level
+# from VERSION up (WARN included) prints its version banner there, so an
+# image-wide NCCL_DEBUG=VERSION (or WARN) is dropped; INFO/TRACE, set on purpose
+# for debugging, stay.  Must happen before torch (and NCCL) load.
+if os.environ.get("NCCL_DEBUG", "").upper() in ("VERSION", "WARN"):
+    del os.environ["NCCL_DEBUG"]
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 for _p in (ROOT, os.path.join(ROOT, "cyfa-jittor_b200")):
