@@ -20,6 +20,7 @@ from ..ops.layer_ops import (
     ChunkCyfaPackedFunction,
     GatedNormFunction,
     LayerFrontFunction,
+    LinearFunction,
     PackedGradSlot,
 )
 
@@ -181,6 +182,12 @@ class CyclicFlowAttention(nn.Module):
         H, K, V = self.num_heads, self.head_k_dim, self.head_v_dim
         g0 = self.g_proj[0]
         slot = PackedGradSlot()
+        # LayerFrontFunction's backward runs (and joins deferred side-stream work)
+        # iff one of its differentiable inputs needs a gradient
+        slot.front_backward = torch.is_grad_enabled() and any(
+            t.requires_grad for t in (x, self.q_proj.weight, self.k_proj.weight,
+                                      self.v_proj.weight, g0.weight, self.a_proj.weight,
+                                      self.b_proj.weight, self.d_proj.weight))
         qkv, gate_in, g, delta, beta = LayerFrontFunction.apply(
             x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, g0.weight,
             self.a_proj.weight, self.b_proj.weight, self.d_proj.weight, self.q_conv1d.weight,
@@ -191,8 +198,9 @@ class CyclicFlowAttention(nn.Module):
             self.k_norm.weight.float(), float(self.q_norm.eps), float(self.k_norm.eps), K ** -0.5)
         g1 = self.g_proj[1]
         y = GatedNormFunction.apply(o, gate_in, g1.weight, g1.bias, self.o_norm.weight,
-                                    self.o_norm.eps, float(self.num_slots - 1), slot)
-        y = self.o_proj(y)
+                                    self.o_norm.eps, float(self.num_slots - 1), slot, (g1.weight,))
+        y = LinearFunction.apply(y, self.o_proj.weight, (self.o_proj.weight,), slot) \
+            if self.o_proj.bias is None else self.o_proj(y)
         new_cache = None
         if use_cache:
             W = self.q_conv1d.width

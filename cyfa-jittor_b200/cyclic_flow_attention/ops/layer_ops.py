@@ -174,7 +174,7 @@ class GatedNormFunction(torch.autograd.Function):
     bias; the kernels add b and return its gradient (fixed-order sums)."""
 
     @staticmethod
-    def forward(ctx, x, gate_in, gate_w, gate_b, weight, eps, scale, slot=None):
+    def forward(ctx, x, gate_in, gate_w, gate_b, weight, eps, scale, slot=None, gate_param=None):
         B, T, H, D = x.shape
         rows = B * T * H
         x = x.to(torch.bfloat16).contiguous()
@@ -193,6 +193,8 @@ class GatedNormFunction(torch.autograd.Function):
         ctx.save_for_backward(x, gate, gate_in, gate_w, w, rstd, b)
         ctx.meta = (scale, weight.dtype, None if gate_b is None else gate_b.dtype)
         ctx.slot = slot
+        # (the Parameter behind gate_w,) as a plain object, for a deferred gradient
+        ctx.gate_param = gate_param[0] if gate_param else None
         return y
 
     @staticmethod
@@ -222,8 +224,12 @@ class GatedNormFunction(torch.autograd.Function):
                       _lib.stream())
         dg2 = dgate.reshape(-1, H * D)
         gin2 = gate_in.reshape(-1, gate_in.shape[-1])
-        d_gate_w = dg2.t() @ gin2
         slot = ctx.slot
+        d_gate_w = None
+        if slot is not None and ctx.gate_param is not None:
+            d_gate_w = slot.defer_wgrad(ctx.gate_param, dg2, gin2)
+        if d_gate_w is None:
+            d_gate_w = dg2.t() @ gin2
         if slot is not None:
             # the producer of gate_in collects its gradient in a packed buffer:
             # write this part there directly and pass no separate gradient
@@ -232,7 +238,41 @@ class GatedNormFunction(torch.autograd.Function):
             d_gate_in = None
         else:
             d_gate_in = (dg2 @ gate_w).reshape(gate_in.shape)
-        return dx, d_gate_in, d_gate_w, d_gate_b, dw.to(wdt), None, None, None
+        return dx, d_gate_in, d_gate_w, d_gate_b, dw.to(wdt), None, None, None, None
+
+
+_SIDE = {}
+
+
+def _side_stream(device):
+    key = str(device)
+    if key not in _SIDE:
+        _SIDE[key] = torch.cuda.Stream(device=device)
+    return _SIDE[key]
+
+
+class LinearFunction(torch.autograd.Function):
+    """y = x W^T (no bias) whose weight gradient may be deferred to the layer's
+    side stream through a PackedGradSlot (the layer's o_proj)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, param, slot):
+        # param: (the Parameter behind weight,), passed as a plain object
+        ctx.save_for_backward(x, weight)
+        ctx.param, ctx.slot = param[0], slot
+        return torch.nn.functional.linear(x, weight)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight = ctx.saved_tensors
+        dx = dy @ weight if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            dy2, x2 = dy.reshape(-1, dy.shape[-1]), x.reshape(-1, x.shape[-1])
+            dw = ctx.slot.defer_wgrad(ctx.param, dy2, x2) if ctx.slot is not None else None
+            if dw is None:
+                dw = dy2.t() @ x2
+        return dx, dw, None, None
 
 
 class PackedGradSlot:
@@ -250,6 +290,34 @@ class PackedGradSlot:
         self.shape = None  # (B, T, NB), column range of the gate input
         self.cols = None
         self.buf = None
+        self.pending = []  # operands of deferred weight-gradient GEMMs, until join()
+        self.front_backward = False  # LayerFrontFunction's backward will run (and join)
+
+    def defer_wgrad(self, param, dy2, x2):
+        """Weight gradient dy2^T x2 of `param` on the layer's side stream, so that
+        these long-reduction GEMMs (few output tiles) run beside the attention
+        backward instead of before it; LayerFrontFunction's backward joins them.
+        Only when nothing can read the gradient before the join: the parameter
+        has no gradient yet (autograd then stores the tensor without a kernel) and
+        no hook of its own.  Returns the gradient tensor, or None to compute it now."""
+        if (not self.front_backward or param.grad is not None or param._backward_hooks
+                or not dy2.is_cuda or getattr(param, "_post_accumulate_grad_hooks", None)):
+            return None
+        out = torch.empty(dy2.shape[1], x2.shape[1], device=dy2.device, dtype=param.dtype)
+        side = _side_stream(dy2.device)
+        side.wait_stream(torch.cuda.current_stream(dy2.device))
+        with torch.cuda.stream(side):
+            torch.matmul(dy2.t(), x2, out=out)
+        # the operands stay alive until the join; the result is held only by
+        # autograd, which then stores it as the gradient without a copy
+        self.pending.append((dy2, x2))
+        return out
+
+    def join(self):
+        if self.pending:
+            dev = self.pending[0][0].device
+            torch.cuda.current_stream(dev).wait_stream(_side_stream(dev))
+            self.pending.clear()
 
     def claim(self, device):
         if self.buf is None:
@@ -342,6 +410,8 @@ class LayerFrontFunction(torch.autograd.Function):
         dev = x.device
         # the packed gradient: possibly already holding the gate-input columns
         dbig = ctx.slot.take() if ctx.slot is not None else None
+        if ctx.slot is not None:
+            ctx.slot.join()  # the deferred o_proj / output-gate weight gradients
         gate_done = dbig is not None
         if dbig is None:
             dbig = torch.empty(B, T, NB, device=dev, dtype=torch.bfloat16)

@@ -96,3 +96,29 @@ def test_pdl_launch_matches_stream_order():
     assert torch.equal(off[0], on_[0]) and torch.equal(off[2], on_[2])
     for a, b, c, d in zip(off[1], on_[1], off[3], on_[3]):
         assert torch.equal(a, b) and torch.equal(c, d)
+
+
+def test_deferred_weight_gradients_match_inline():
+    """The o_proj and output-gate weight gradients computed on the layer's side
+    stream (deferred, joined in the front's backward) equal the inline ones: a
+    hook on a parameter turns its deferral off."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+    B, T, hidden, H, hd = 2, 384, 512, 2, 256
+    m, params, step = _setup(B, T, hidden, H, hd)
+    gen = torch.Generator().manual_seed(11)
+    x = torch.randn(B, T, hidden, generator=gen).to(torch.bfloat16).cuda()
+    dy = torch.randn(B, T, hidden, generator=gen).to(torch.bfloat16).cuda()
+    step(x, dy)
+    torch.cuda.synchronize()
+    deferred = [p.grad.clone() for p in params]
+    handles = [p.register_post_accumulate_grad_hook(lambda p: None)
+               for p in (m.o_proj.weight, m.g_proj[1].weight)]
+    try:
+        step(x, dy)
+        torch.cuda.synchronize()
+    finally:
+        for h in handles:
+            h.remove()
+    for (name, p), g in zip(m.named_parameters(), deferred):
+        assert torch.equal(p.grad, g), name
