@@ -74,12 +74,14 @@ def _tile_bytes(K=256, V=256, C=128, M=128):
     b = 2
     out = {}
 
-    def dual(N, KD, dot):
-        # X1 (scores) + Y1 (token rows) + X2 (token rows) + Y2 (state history) + out (+ dot partner)
-        return b * (C * C + C * N + C * KD + KD * N + C * N + (C * N if dot else 0))
+    def dual(dk, dv):
+        # one launch per pass: A and B' + queries and keys (C dk each) + values and
+        # output-gradient rows (C dv each) + state history and its adjoint (dk dv each),
+        # written: dq, dk (C dk each) and dv (C dv); the row-dot partners are the
+        # queries and keys already read
+        return b * (2 * C * C + 2 * C * dk + 2 * C * dv + 2 * dk * dv + 2 * C * dk + C * dv)
 
-    out["dual_gemm"] = (dual(M, V, True) + dual(M, V, True) + dual(V, M, False)
-                        + dual(K, M, True) + dual(K, M, True) + dual(M, K, False))
+    out["dual_gemm"] = dual(K, M) + dual(M, V)
     out["tile_scores"] = sum(b * (2 * C * dk + 2 * C * dv + 2 * C * C) for dk, dv in ((K, M), (M, V)))
     out["state_scan_fwd"] = sum(b * (C * dk + C * dv + dk * dv) for dk, dv in ((K, M), (M, V)))
     out["state_scan_bwd"] = sum(b * (C * dk + C * dv + 2 * dk * dv) for dk, dv in ((K, M), (M, V)))

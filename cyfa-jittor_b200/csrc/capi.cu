@@ -453,7 +453,7 @@ int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h, con
   CYFA_REQUIRE(dG && dlam && dbeta_h && dg && ddelta && dbeta, kNullPointer);
   CYFA_REQUIRE(B > 0 && T > 0 && H > 0, kBadShape);
   const int TP = (T + 127) / 128 * 128;
-  GatesBwdParams p{dG, dlam, nullptr, nullptr, nullptr, 0, 0, dbeta_h, dclock, dg, ddelta,
+  GatesBwdParams p{dG, 1, 0, dlam, nullptr, nullptr, nullptr, 0, 0, dbeta_h, dclock, dg, ddelta,
                    dbeta, dclock0, B, T, H, TP};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   CYFA_LAUNCH("gates_bwd", st, launch_k(gates_bwd_kernel, B * H, 1024, 0, st, p));

@@ -63,6 +63,9 @@ static Saved carve_saved(const Dims& d, void* base, size_t* total) {
   return s;
 }
 
+// Row-dot slots of dG: dweights, dw, and up to two 128-column blocks each of dq^, dk^.
+constexpr int kDgSlots = 6;
+
 // Scratch of the backward pass.
 struct Work {
   __nv_bfloat16 *h1, *h2, *A, *Bp, *draw, *dweights, *dw, *dw_b, *dq1, *dk1;
@@ -84,7 +87,7 @@ static Work carve_work(const Dims& d, void* base, size_t* total) {
   w.dw_b = c.take<__nv_bfloat16>(n * 128);
   w.dq1 = c.take<__nv_bfloat16>(n * d.K);
   w.dk1 = c.take<__nv_bfloat16>(n * d.K);
-  w.dG = c.take<float>(n);
+  w.dG = c.take<float>(n * kDgSlots);
   w.dlam_r = c.take<float>(n);
   w.dlam_w = c.take<float>(n);
   w.dbeta_h = c.take<float>(n);
@@ -295,8 +298,8 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   if ((rc = tmap_public(&m_v, a->v, d.B, d.T, d.H, d.V, stride_or(a->v_stride, d.H * d.V))))
     return rc;
   if ((rc = tmap_public(&m_do, g->d_o, d.B, d.T, d.H, d.V, (long long)d.H * d.V))) return rc;
-  if ((rc = tmap_2d(&m_s1, s.s1, uint64_t(d.BH) * d.NT * d.K, 128, d.K))) return rc;
-  if ((rc = tmap_2d(&m_h1, w.h1, uint64_t(d.BH) * d.NT * d.K, 128, d.K))) return rc;
+  if ((rc = tmap_2d(&m_s1, s.s1, uint64_t(d.BH) * d.NT * d.K, 128, 128))) return rc;
+  if ((rc = tmap_2d(&m_h1, w.h1, uint64_t(d.BH) * d.NT * d.K, 128, 128))) return rc;
   if ((rc = tmap_2d(&m_s2, s.s2, uint64_t(d.BH) * d.NT * 128, d.V, 128))) return rc;
   if ((rc = tmap_2d(&m_h2, w.h2, uint64_t(d.BH) * d.NT * 128, d.V, 128))) return rc;
   if ((rc = tmap_2d(&m_A, w.A, trows, 128, 128))) return rc;
@@ -319,13 +322,24 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   const dim3 persist(d.BH * d.NT < 148 ? d.BH * d.NT : 148);  // one CTA per SM
   set_smem(state_scan_kernel<true>, kScanSmem);
   set_smem(dual_gemm_kernel, kDualSmem);
-  auto dual = [&](const CUtensorMap& x1, const CUtensorMap& y1, const CUtensorMap& x2,
-                  const CUtensorMap& y2, DualParams p) {
-    const unsigned ntile = unsigned(d.BH * d.NT), grid = ntile < 148 ? ntile : 148;  // persistent
+  // The three GEMM pairs of a pass in one persistent launch, their 128-column
+  // units interleaved tile by tile.
+  auto dual = [&](const DualMaps& m, DualParams& p, int njobs) {
+    p.units = 0;
+    for (int jx = 0; jx < njobs; ++jx)
+      for (int nb = 0; nb < p.job[jx].N / 128; ++nb) {
+        p.unit_job[p.units] = jx;
+        p.unit_nb[p.units] = nb;
+        ++p.units;
+      }
+    const unsigned nu = unsigned(d.BH * d.NT * p.units), grid = nu < 148 ? nu : 148;
     CYFA_LAUNCH("dual_gemm", st,
-                (launch_k(dual_gemm_kernel, grid, kDualThreads, kDualSmem, st, x1, y1, x2, y2, p)));
+                (launch_k(dual_gemm_kernel, grid, kDualThreads, kDualSmem, st, m, p)));
     return launch_status();
   };
+  // row-dot slots of dG (summed by gates_bwd): dweights, dw, dq^ blocks, dk^ blocks
+  const size_t slot = size_t(d.BH) * d.TP;
+  const int ndg = 2 + 2 * (d.K / 128);
   // boundary partials per tile: one per (CTA slice, warp)
   const int nsub1 = (d.K / 128) * 2 * 4, nsub2 = (d.V / 64) * 4;
 
@@ -352,18 +366,21 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                       m_weights, m_w, m_do, m_v, sp)));
     }
     if ((rc = launch_status())) return rc;
-    // dweights = B' w + 2^{G_t} dO S^T ;  dG = weights . dweights
-    DualParams q2{d.BH, d.H, d.TP, d.NT, d.T, 0, kRows2D, kPublic4D, 1, 128, d.V, 128, d.V, s.G,
-                  1.f, 0, 3, w.dweights, s.weights, 1.f, 0, w.dG};
-    if ((rc = dual(m_Bp, m_w64, m_do, m_s2, q2))) return rc;
-    // dw = B'^T weights + 2^{G_L-G_s} v H^T ;  dG -= w . dw
-    DualParams k2{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kPublic4D, 1, 128, d.V, 128, d.V, s.G,
-                  1.f, 1, 3, w.dw, s.w, -1.f, 1, w.dG};
-    if ((rc = dual(m_Bp64, m_weights64, m_v, m_h2, k2))) return rc;
+    DualMaps m;
+    DualParams dp{d.BH, d.H, d.TP, d.NT, d.T, s.G};
+    // dweights = B' w + 2^{G_t} dO S^T ;  dG slot 0 = weights . dweights
+    m.x1[0] = m_Bp, m.y1[0] = m_w64, m.x2[0] = m_do, m.y2[0] = m_s2;
+    dp.job[0] = DualJob{0, kRows2D, kPublic4D, 1, 128, d.V, 1.f, 0, 3, w.dweights, 0, s.weights,
+                        1.f, w.dG};
+    // dw = B'^T weights + 2^{G_L-G_s} v H^T ;  dG slot 1 = -(w . dw)
+    m.x1[1] = m_Bp64, m.y1[1] = m_weights64, m.x2[1] = m_v, m.y2[1] = m_h2;
+    dp.job[1] = DualJob{1, kRows2D, kPublic4D, 1, 128, d.V, 1.f, 1, 3, w.dw, 0, s.w, -1.f,
+                        w.dG + slot};
     // dv = A^T dO + 2^{G_L-G_s} w H  (public layout)
-    DualParams v2{d.BH, d.H, d.TP, d.NT, d.T, 1, kPublic4D, kRows2D, 0, d.V, 128, 128, d.V, s.G,
-                  1.f, 1, 2, g->dv, nullptr, 0.f, 0, nullptr, stride_or(g->dv_stride, d.H * d.V)};
-    if ((rc = dual(m_A64, m_do64, m_w, m_h2_64, v2))) return rc;
+    m.x1[2] = m_A64, m.y1[2] = m_do64, m.x2[2] = m_w, m.y2[2] = m_h2_64;
+    dp.job[2] = DualJob{1, kPublic4D, kRows2D, 0, d.V, 128, 1.f, 1, 2, g->dv,
+                        stride_or(g->dv_stride, d.H * d.V), nullptr, 0.f, nullptr};
+    if ((rc = dual(m, dp, 3))) return rc;
   }
   // ================= readout adjoint
   {
@@ -407,18 +424,21 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                       m_qn, m_kn, m_draw, m_w, sp)));
     }
     if ((rc = launch_status())) return rc;
-    // dq^ = B' k^ + scale 2^{G_t} draw S^T ;  dG += q^ . dq^
-    DualParams q1{d.BH, d.H, d.TP, d.NT, d.T, 0, kRows2D, kRows2D, 1, d.K, 128, d.K, 128, s.G,
-                  a->scale, 0, 3, w.dq1, s.qn, 1.f, 1, w.dG};
-    if ((rc = dual(m_Bp, m_kn64, m_draw, m_s1, q1))) return rc;
-    // dk^ = B'^T q^ + 2^{G_L-G_s} w H^T ;  dG -= k^ . dk^
-    DualParams k1{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kRows2D, 1, d.K, 128, d.K, 128, s.G,
-                  1.f, 1, 3, w.dk1, s.kn, -1.f, 1, w.dG};
-    if ((rc = dual(m_Bp64, m_qn64, m_w, m_h1, k1))) return rc;
+    DualMaps m;
+    DualParams dp{d.BH, d.H, d.TP, d.NT, d.T, s.G};
+    // dq^ = B' k^ + scale 2^{G_t} draw S^T ;  dG slots 2.. = q^ . dq^ (per 128 columns)
+    m.x1[0] = m_Bp, m.y1[0] = m_kn64, m.x2[0] = m_draw, m.y2[0] = m_s1;
+    dp.job[0] = DualJob{0, kRows2D, kRows2D, 1, d.K, 128, a->scale, 0, 3, w.dq1, 0, s.qn, 1.f,
+                        w.dG + 2 * slot};
+    // dk^ = B'^T q^ + 2^{G_L-G_s} w H^T ;  next K/128 slots = -(k^ . dk^)
+    m.x1[1] = m_Bp64, m.y1[1] = m_qn64, m.x2[1] = m_w, m.y2[1] = m_h1;
+    dp.job[1] = DualJob{1, kRows2D, kRows2D, 1, d.K, 128, 1.f, 1, 3, w.dk1, 0, s.kn, -1.f,
+                        w.dG + (2 + d.K / 128) * slot};
     // dw_b = A^T draw + 2^{G_L-G_s} k^ H  (the write-vector gradient is dw + dw_b)
-    DualParams v1{d.BH, d.H, d.TP, d.NT, d.T, 1, kRows2D, kRows2D, 0, 128, d.K, d.K, 128, s.G,
-                  1.f, 1, 3, w.dw_b, nullptr, 0.f, 0, nullptr};
-    if ((rc = dual(m_A64, m_draw64, m_kn, m_h1_64, v1))) return rc;
+    m.x1[2] = m_A64, m.y1[2] = m_draw64, m.x2[2] = m_kn, m.y2[2] = m_h1_64;
+    dp.job[2] = DualJob{1, kRows2D, kRows2D, 0, 128, d.K, 1.f, 1, 3, w.dw_b, 0, nullptr, 0.f,
+                        nullptr};
+    if ((rc = dual(m, dp, 3))) return rc;
   }
   // ================= norms, write vector, gates, clock
   int nblk = 0;  // partial rows of the norm-weight gradients
@@ -434,8 +454,9 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                         g->dq_norm_weight, nblk, d.K, w.dkw_part, g->dk_norm_weight, 0x7fffffff,
                         nullptr)));
   if ((rc = launch_status())) return rc;
-  GatesBwdParams gp{w.dG, w.dlam_w, w.dlam_r, w.bpart1, w.bpart2, nsub1, nsub2, w.dbeta_h,
-                    g->dclock, g->dg, g->ddelta, g->dbeta, g->dclock0, d.B, d.T, d.H, d.TP};
+  GatesBwdParams gp{w.dG, ndg, (long long)slot, w.dlam_w, w.dlam_r, w.bpart1, w.bpart2, nsub1,
+                    nsub2, w.dbeta_h, g->dclock, g->dg, g->ddelta, g->dbeta, g->dclock0, d.B, d.T,
+                    d.H, d.TP};
   CYFA_LAUNCH("gates_bwd", st, (launch_k(gates_bwd_kernel, d.BH, 1024, 0, st, gp)));
   return launch_status();
 }

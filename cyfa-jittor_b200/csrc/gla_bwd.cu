@@ -185,68 +185,80 @@ __global__ void __launch_bounds__(256, 1)
 }
 
 // ============================================================ dual GEMM
-struct DualParams {
-  int BH, H, TP, NT, T;
-  int x1_mn;          // 0: X1 as stored ([t][s], K-major); 1: its transpose (MN-major)
-  int y1_mode;        // token-row mode of Y1 [128 tok x N]
-  int x2_mode;        // token-row mode of X2 [128 tok x KD]
-  int y2_kmaj;        // 1: B2 = hist^T (N = hist rows); 0: B2 = hist (N = hist cols)
-  int N, KD;
-  int hrows, hcols;   // history tile [hrows x hcols]
-  const float* G;
+// One GEMM pair of a pass: out = X1 Y1 + r_t (X2 Y2) for every tile.
+struct DualJob {
+  int x1_mn;     // 0: X1 as stored ([t][s], K-major); 1: its transpose (MN-major)
+  int y1_mode;   // token-row mode of Y1 [128 tok x N]
+  int x2_mode;   // token-row mode of X2 [128 tok x KD]
+  int y2_kmaj;   // 1: B2 = hist^T (N = hist rows); 0: B2 = hist (N = hist cols, KD rows)
+  int N, KD;     // output columns (128 or 256), contraction of the second GEMM
   float scale;
-  int fkind;          // row factor: 0 -> scale 2^{G_t}; 1 -> 2^{G_L - G_t}
-  int out_mode;       // 0: fp32 [BH,TP,N]; 2: bf16 public [B,T,H,N]; 3: bf16 [BH,TP,N]
+  int fkind;     // row factor: 0 -> scale 2^{G_t}; 1 -> 2^{G_L - G_t}
+  int out_mode;  // 0: fp32 [BH,TP,N]; 2: bf16 public [B,T,H,N]; 3: bf16 [BH,TP,N]
   void* out;
+  long long out_stride;          // out_mode 2: elements between consecutive tokens
   const __nv_bfloat16* dot_src;  // optional [BH,TP,N] row-dot partner
   float dot_sign;
-  int dot_acc;
-  float* dG;
-  long long out_stride;  // out_mode 2: elements between consecutive tokens
+  float* dG;  // row-dot slots: column block nb writes dot_sign * <partner, out> to dG + nb*BH*TP
 };
 
-constexpr int kDualRing = 192 * 1024;                 // operand ring
+constexpr int kDualMaxJobs = 3;
+constexpr int kDualMaxUnits = 6;  // per tile: sum over the jobs of N / 128
+
+struct DualParams {
+  int BH, H, TP, NT, T;
+  const float* G;
+  int units;  // units per tile
+  int unit_job[kDualMaxUnits], unit_nb[kDualMaxUnits];
+  DualJob job[kDualMaxJobs];
+};
+
+// Tensor maps of the jobs: X1, Y1, X2, Y2 each (box heights as the loads below use).
+struct DualMaps {
+  CUtensorMap x1[kDualMaxJobs], y1[kDualMaxJobs], x2[kDualMaxJobs], y2[kDualMaxJobs];
+};
+
+constexpr int kDualRing = 192 * 1024;                 // operand ring: 6 stages of 32 KiB
+constexpr int kDualStage = 32768;
+constexpr int kDualStages = kDualRing / kDualStage;
 constexpr int kDualSmem = kDualRing + 8 * 2048 + 1024;  // + per-warp staging + alignment
 constexpr int kDualThreads = 320;
-constexpr int kDualMaxStages = 6;
 
 // Persistent, warp-specialised, streaming over the contraction dimension.
-// Every tile's two GEMMs are cut into 64-wide k-blocks (2 for X1 Y1, KD/64 for
-// X2 Y2); a k-block stage holds one 128x64 block of the left operand and the
-// matching 64xN block of the right operand (16 KiB + N*128 B), and a ring of
-// stages keeps the loads streaming across tile boundaries:
+// The work unit is one 128-column block of one job's output tile, and the units
+// of a tile (every job of the pass, both column blocks of a 256-wide output)
+// are consecutive, so the CTAs working side by side share the tile's operands
+// through L2 and each operand is read from DRAM about once per pass.  A unit's
+// two GEMMs are cut into 64-wide k-blocks (2 for X1 Y1, KD/64 for X2 Y2); a
+// k-block stage holds one 128x64 block of the left operand and the matching
+// 64x128 block of the right operand (32 KiB), and a ring of stages keeps the
+// loads streaming across unit boundaries:
 //   warp 8, lane 0 (producer): TMA loads into the ring;
-//   warp 9, lane 0 (MMA issuer): the k-block UMMAs into the tile's TMEM buffer
-//     (acc1 = X1 Y1 | acc2 = X2 Y2, 2N columns; two buffers when N = 128), a
-//     commit per stage frees it, a commit per tile hands the buffer over;
+//   warp 9, lane 0 (MMA issuer): the k-block UMMAs into the unit's TMEM buffer
+//     (acc1 = X1 Y1 | acc2 = X2 Y2, 256 columns; two buffers), a commit per
+//     stage frees it, a commit per unit hands the buffer over;
 //   warps 0-7 (epilogue): warp w reads TMEM lane quadrant (w & 3) and column
-//     half (w >> 2), forms out = acc1 + r_t acc2 (+ the row dot folded into dG).
+//     half (w >> 2), forms out = acc1 + r_t acc2 (and the unit's share of the
+//     row dot, written to its own dG slot).
 // Operand boxes: X1 stored [t][s]; K-major X1 uses the 64-column panel of all
 // 128 rows, MN-major X1 (its transpose) 64 rows x 128 columns.  Y1 (token rows)
 // is read MN-major in 64-row blocks; Y2 (state history) K-major as a 64-column
-// panel of its N rows, or MN-major in 64-row blocks.  Maps given to the kernel
-// have the matching box heights (128, or 64 for the MN-major 64-row blocks).
+// panel of 128 of its N rows, or MN-major in 64-row blocks.  Maps have the
+// matching box heights (128, or 64 for the MN-major 64-row blocks).
 __global__ void __launch_bounds__(kDualThreads, 1)
-    dual_gemm_kernel(const __grid_constant__ CUtensorMap map_x1,
-                     const __grid_constant__ CUtensorMap map_y1,
-                     const __grid_constant__ CUtensorMap map_x2,
-                     const __grid_constant__ CUtensorMap map_y2, DualParams p) {
+    dual_gemm_kernel(const __grid_constant__ DualMaps maps, const __grid_constant__ DualParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  __shared__ __align__(8) uint64_t full[kDualMaxStages], empty[kDualMaxStages];
+  __shared__ __align__(8) uint64_t full[kDualStages], empty[kDualStages];
   __shared__ __align__(8) uint64_t acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ float dot_half[2][2][128];
   __shared__ int s_abort;
   volatile int* abort_flag = &s_abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int ntiles = p.BH * p.NT;
-  const int N = p.N, nkb = 2 + p.KD / 64;
-  const int stage_bytes = 16384 + N * 128;
-  const int nst = (kDualRing / stage_bytes) < kDualMaxStages ? kDualRing / stage_bytes : kDualMaxStages;
-  const int nbuf = 2 * N <= 256 ? 2 : 1;
+  const int nunits = p.BH * p.NT * p.units;
   if (tid == 0) {
-    for (int i = 0; i < nst; ++i) {
+    for (int i = 0; i < kDualStages; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
@@ -272,86 +284,93 @@ __global__ void __launch_bounds__(kDualThreads, 1)
     // ------------------------------------------------ producer
     if (lane == 0) {
       int it = 0;
-      for (int tile = blockIdx.x; tile < ntiles && !*abort_flag; tile += gridDim.x) {
-        const int bh = tile / p.NT, j = tile % p.NT;
+      for (int u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
+        const int tile = u / p.units, ui = u % p.units;
+        const int ji = p.unit_job[ui], n0 = 128 * p.unit_nb[ui];
+        const DualJob& jb = p.job[ji];
+        const int bh = tile / p.NT, j = tile % p.NT, nkb = 2 + jb.KD / 64;
         for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % nst;
-          if (it >= nst && !mbar_wait(&empty[s], ((it / nst) - 1) & 1)) {
+          const int s = it % kDualStages;
+          if (it >= kDualStages && !mbar_wait(&empty[s], ((it / kDualStages) - 1) & 1)) {
             *abort_flag = 1;
             break;
           }
-          uint8_t* xb = smem + s * stage_bytes;
+          uint8_t* xb = smem + s * kDualStage;
           uint8_t* yb = xb + 16384;
-          mbar_expect_tx(&full[s], stage_bytes);
+          mbar_expect_tx(&full[s], kDualStage);
           if (kb < 2) {
-            if (p.x1_mn) {
-              tma_load_2d(xb, &map_x1, &full[s], 0, tile * 128 + 64 * kb);
-              tma_load_2d(xb + 8192, &map_x1, &full[s], 64, tile * 128 + 64 * kb);
+            if (jb.x1_mn) {
+              tma_load_2d(xb, &maps.x1[ji], &full[s], 0, tile * 128 + 64 * kb);
+              tma_load_2d(xb + 8192, &maps.x1[ji], &full[s], 64, tile * 128 + 64 * kb);
             } else {
-              tma_load_2d(xb, &map_x1, &full[s], 64 * kb, tile * 128);
+              tma_load_2d(xb, &maps.x1[ji], &full[s], 64 * kb, tile * 128);
             }
-            for (int c = 0; c < N / 64; ++c) {
-              if (p.y1_mode == kRows2D)
-                tma_load_2d(yb + c * 8192, &map_y1, &full[s], 64 * c, bh * p.TP + j * 128 + 64 * kb);
+            for (int c = 0; c < 2; ++c) {
+              if (jb.y1_mode == kRows2D)
+                tma_load_2d(yb + c * 8192, &maps.y1[ji], &full[s], n0 + 64 * c,
+                            bh * p.TP + j * 128 + 64 * kb);
               else
-                tma_load_4d(yb + c * 8192, &map_y1, &full[s], 64 * c, bh % p.H, j * 128 + 64 * kb,
-                            bh / p.H);
+                tma_load_4d(yb + c * 8192, &maps.y1[ji], &full[s], n0 + 64 * c, bh % p.H,
+                            j * 128 + 64 * kb, bh / p.H);
             }
           } else {
             const int k2 = kb - 2;
-            load_token_tile(xb, &map_x2, p.x2_mode, bh, p.H, p.TP, j, 64 * k2, 64, &full[s]);
-            if (p.y2_kmaj) {
-              tma_load_2d(yb, &map_y2, &full[s], 64 * k2, tile * p.hrows);
+            load_token_tile(xb, &maps.x2[ji], jb.x2_mode, bh, p.H, p.TP, j, 64 * k2, 64, &full[s]);
+            if (jb.y2_kmaj) {
+              tma_load_2d(yb, &maps.y2[ji], &full[s], 64 * k2, tile * jb.N + n0);
             } else {
-              for (int c = 0; c < N / 64; ++c)
-                tma_load_2d(yb + c * 8192, &map_y2, &full[s], 64 * c, tile * p.hrows + 64 * k2);
+              for (int c = 0; c < 2; ++c)
+                tma_load_2d(yb + c * 8192, &maps.y2[ji], &full[s], n0 + 64 * c,
+                            tile * jb.KD + 64 * k2);
             }
           }
         }
       }
       // every issued copy lands before shared memory goes away
-      for (int i = it > nst ? it - nst : 0; i < it; ++i) mbar_wait(&full[i % nst], (i / nst) & 1);
+      for (int i = it > kDualStages ? it - kDualStages : 0; i < it; ++i)
+        mbar_wait(&full[i % kDualStages], (i / kDualStages) & 1);
     }
   } else if (warp == 9) {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t id1 = make_idesc(128, N, p.x1_mn, 1);
-      const uint32_t id2 = make_idesc(128, N, 0, p.y2_kmaj ? 0 : 1);
       int it = 0, tl = 0;
       uint64_t* last_bar = nullptr;
       uint32_t last_par = 0;
-      for (int tile = blockIdx.x; tile < ntiles && !*abort_flag; tile += gridDim.x, ++tl) {
-        const int b = tl % nbuf;
-        if (tl >= nbuf && !mbar_wait(&acc_empty[b], ((tl / nbuf) - 1) & 1)) {
+      for (int u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x, ++tl) {
+        const DualJob& jb = p.job[p.unit_job[u % p.units]];
+        const uint32_t id1 = make_idesc(128, 128, jb.x1_mn, 1);
+        const uint32_t id2 = make_idesc(128, 128, 0, jb.y2_kmaj ? 0 : 1);
+        const int nkb = 2 + jb.KD / 64, b = tl & 1;
+        if (tl >= 2 && !mbar_wait(&acc_empty[b], ((tl >> 1) - 1) & 1)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t acc1 = tmem + b * 2 * N, acc2 = acc1 + N;
+        const uint32_t acc1 = tmem + b * 256, acc2 = acc1 + 128;
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const int s = it % nst;
-          if (!mbar_wait(&full[s], (it / nst) & 1)) {
+          const int s = it % kDualStages;
+          if (!mbar_wait(&full[s], (it / kDualStages) & 1)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t xb = smem_u32(smem + s * stage_bytes), yb = xb + 16384;
+          const uint32_t xb = smem_u32(smem + s * kDualStage), yb = xb + 16384;
           if (kb < 2) {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-              umma_bf16(acc1, p.x1_mn ? mnmaj_desc(xb, 64, ks) : kmaj_desc(xb, 128, ks),
+              umma_bf16(acc1, jb.x1_mn ? mnmaj_desc(xb, 64, ks) : kmaj_desc(xb, 128, ks),
                         mnmaj_desc(yb, 64, ks), id1, kb > 0 || ks > 0);
           } else {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
               umma_bf16(acc2, kmaj_desc(xb, 128, ks),
-                        p.y2_kmaj ? kmaj_desc(yb, N, ks) : mnmaj_desc(yb, 64, ks), id2,
+                        jb.y2_kmaj ? kmaj_desc(yb, 128, ks) : mnmaj_desc(yb, 64, ks), id2,
                         kb > 2 || ks > 0);
           }
           umma_commit(&empty[s]);
           last_bar = &empty[s];
-          last_par = (it / nst) & 1;
+          last_par = (it / kDualStages) & 1;
         }
         if (!ok) {
           *abort_flag = 1;
@@ -359,7 +378,7 @@ __global__ void __launch_bounds__(kDualThreads, 1)
         }
         umma_commit(&acc_full[b]);
         last_bar = &acc_full[b];
-        last_par = (tl / nbuf) & 1;
+        last_par = (tl >> 1) & 1;
       }
       if (last_bar) mbar_wait(last_bar, last_par);  // all issued MMAs are done
     }
@@ -368,38 +387,41 @@ __global__ void __launch_bounds__(kDualThreads, 1)
     const int quad = warp & 3, half = warp >> 2;
     const int r = quad * 32 + lane;  // tile row = TMEM lane
     const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
-    const int ncol = N / 2, c_beg = half * ncol;  // 64 or 128 columns
     const uint32_t scratch = smem_u32(smem) + kDualRing + warp * 2048;
+    const size_t slot = size_t(p.BH) * p.TP;
     int tl = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++tl) {
-      const int bh = tile / p.NT, j = tile % p.NT, b = tl % nbuf;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++tl) {
+      const int tile = u / p.units, ui = u % p.units;
+      const int nb = p.unit_nb[ui];
+      const DualJob& jb = p.job[p.unit_job[ui]];
+      const int bh = tile / p.NT, j = tile % p.NT, b = tl & 1;
+      const int N = jb.N, c_beg = 128 * nb + 64 * half;  // this warp's 64 output columns
       const int t = j * 128 + r;
       const float* Gt = p.G + size_t(bh) * p.TP + j * 128;
-      const float f = p.fkind == 0 ? p.scale * exp2f(Gt[r]) : exp2f(Gt[127] - Gt[r]);
+      const float f = jb.fkind == 0 ? jb.scale * exp2f(Gt[r]) : exp2f(Gt[127] - Gt[r]);
       const size_t row = size_t(bh) * p.TP + t;
+      const __nv_bfloat16* dsrc = jb.dot_src;
       // the row-dot partner, fetched coalesced before the MMAs are waited for
-      uint4 dpre[4][4];
-      if (p.dot_src) {
-        const __nv_bfloat16* src = p.dot_src + (size_t(bh) * p.TP + j * 128 + quad * 32) * N + c_beg;
+      uint4 dpre[2][4];
+      if (dsrc) {
+        const __nv_bfloat16* src = dsrc + (size_t(bh) * p.TP + j * 128 + quad * 32) * N + c_beg;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          if (c < ncol / 32) warp_fetch_block_bf16(src + 32 * c, N, dpre[c]);
+        for (int c = 0; c < 2; ++c) warp_fetch_block_bf16(src + 32 * c, N, dpre[c]);
       }
       const bool got =
-          __all_sync(0xffffffffu, *abort_flag == 0 && mbar_wait(&acc_full[b], (tl / nbuf) & 1));
+          __all_sync(0xffffffffu, *abort_flag == 0 && mbar_wait(&acc_full[b], (tl >> 1) & 1));
       tc_fence_after();
       float dot = 0.f;
       if (got) {
-        const uint32_t acc1 = lane_tmem + b * 2 * N, acc2 = acc1 + N;
+        const uint32_t acc1 = lane_tmem + b * 256 + 64 * half, acc2 = acc1 + 128;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (c >= ncol / 32) break;
+        for (int c = 0; c < 2; ++c) {
           const int col = c_beg + 32 * c;
           float a[32], bb[32];
-          tmem_ld32x2(acc1 + col, a, acc2 + col, bb);
+          tmem_ld32x2(acc1 + 32 * c, a, acc2 + 32 * c, bb);
 #pragma unroll
           for (int i = 0; i < 32; ++i) a[i] += f * bb[i];
-          if (p.dot_src) {
+          if (dsrc) {
             uint4 drow[4];
             warp_transpose_block_bf16(scratch, dpre[c], drow);
 #pragma unroll
@@ -410,22 +432,22 @@ __global__ void __launch_bounds__(kDualThreads, 1)
               for (int e = 0; e < 8; ++e) dot += x[e] * a[8 * q + e];
             }
           }
-          if (p.out_mode == 2) {
+          if (jb.out_mode == 2) {
             const int b_ = bh / p.H, h = bh % p.H, t0 = j * 128 + quad * 32;
             const int nvalid = p.T - t0;
             const uint32_t valid =
                 nvalid >= 32 ? 0xffffffffu : (nvalid <= 0 ? 0u : (1u << nvalid) - 1u);
             warp_store_block_bf16(scratch, a,
-                                  static_cast<__nv_bfloat16*>(p.out) +
-                                      (size_t(b_) * p.T + t0) * p.out_stride + size_t(h) * N + col,
-                                  p.out_stride, valid);
-          } else if (p.out_mode == 3) {
+                                  static_cast<__nv_bfloat16*>(jb.out) +
+                                      (size_t(b_) * p.T + t0) * jb.out_stride + size_t(h) * N + col,
+                                  jb.out_stride, valid);
+          } else if (jb.out_mode == 3) {
             warp_store_block_bf16(scratch, a,
-                                  static_cast<__nv_bfloat16*>(p.out) +
+                                  static_cast<__nv_bfloat16*>(jb.out) +
                                       (size_t(bh) * p.TP + j * 128 + quad * 32) * N + col,
                                   N, 0xffffffffu);
           } else {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + row * N + col);
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(jb.out) + row * N + col);
 #pragma unroll
             for (int q = 0; q < 8; ++q)
               __stcs(dst + q, make_float4(a[4 * q], a[4 * q + 1], a[4 * q + 2], a[4 * q + 3]));
@@ -436,16 +458,14 @@ __global__ void __launch_bounds__(kDualThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
-      if (p.dot_src) dot_half[tl & 1][half][r] = dot;
+      if (dsrc) dot_half[tl & 1][half][r] = dot;
       // join the two column halves of the row dot (and agree on stopping)
       if (named_bar_or(1, 256, !got)) {
         *abort_flag = 1;
         break;
       }
-      if (p.dot_src && half == 0) {
-        const float total = dot_half[tl & 1][0][r] + dot_half[tl & 1][1][r];
-        p.dG[row] = (p.dot_acc ? p.dG[row] : 0.f) + p.dot_sign * total;
-      }
+      if (dsrc && half == 0)
+        jb.dG[nb * slot + row] = jb.dot_sign * (dot_half[tl & 1][0][r] + dot_half[tl & 1][1][r]);
     }
   }
   tc_fence_before();

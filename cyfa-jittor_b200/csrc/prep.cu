@@ -816,7 +816,10 @@ inline int token_bwd_blocks(size_t rows) {
 
 
 struct GatesBwdParams {
-  const float* dG;       // [B,H,TP] gradient of the in-tile gate cumsum (natural log)
+  const float* dG;       // [ndg][B,H,TP] gradient of the in-tile gate cumsum (natural log),
+                         // as ndg partial slots dg_stride elements apart, summed in order
+  int ndg;
+  long long dg_stride;
   const float* dlam;     // [B,H,TP] clock gradient
   const float* dlam2;    // [B,H,TP] second clock gradient term, or null
   const float* bpart1;   // [B*H, NT, nsub1] tile-end gate terms, or null
@@ -842,7 +845,9 @@ __global__ void __launch_bounds__(1024) gates_bwd_kernel(GatesBwdParams p) {
   for (int k = nblk - 1; k >= 0; --k) {
     const int t = k * 1024 + threadIdx.x;
     const bool in = t < p.TP;
-    float dGt = in ? p.dG[base + t] : 0.f;
+    float dGt = 0.f;
+    if (in)
+      for (int s = 0; s < p.ndg; ++s) dGt += p.dG[s * p.dg_stride + base + t];
     if (in && (t & 127) == 127) {
       const size_t tile = size_t(bh) * (p.TP / 128) + t / 128;
       if (p.bpart1)
