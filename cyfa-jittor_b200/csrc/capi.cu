@@ -424,7 +424,8 @@ int cyfa_gates_fwd(const float* g, const float* delta, const float* beta, const 
   const int TP = (T + 127) / 128 * 128;
   GatesParams p{g, delta, beta, clock0, G, lam, beta_h, clock_out, B, T, H, TP};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  CYFA_LAUNCH("gates_fwd", st, launch_k(gates_fwd_kernel, B * H, 1024, 0, st, p));
+  CYFA_LAUNCH("gates_fwd", st,
+              launch_k(gates_fwd_kernel, dim3(B * H, (TP + 1023) / 1024), 1024, 0, st, p));
   return launch_status();
 }
 
@@ -456,7 +457,8 @@ int cyfa_gates_bwd(const float* dG, const float* dlam, const float* dbeta_h, con
   GatesBwdParams p{dG, 1, 0, dlam, nullptr, nullptr, nullptr, 0, 0, dbeta_h, dclock, dg, ddelta,
                    dbeta, dclock0, B, T, H, TP};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  CYFA_LAUNCH("gates_bwd", st, launch_k(gates_bwd_kernel, B * H, 1024, 0, st, p));
+  CYFA_LAUNCH("gates_bwd", st,
+              launch_k(gates_bwd_kernel, dim3(B * H, (TP + 1023) / 1024), 1024, 0, st, p));
   return launch_status();
 }
 

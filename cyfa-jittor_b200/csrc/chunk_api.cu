@@ -457,7 +457,8 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   GatesBwdParams gp{w.dG, ndg, (long long)slot, w.dlam_w, w.dlam_r, w.bpart1, w.bpart2, nsub1,
                     nsub2, w.dbeta_h, g->dclock, g->dg, g->ddelta, g->dbeta, g->dclock0, d.B, d.T,
                     d.H, d.TP};
-  CYFA_LAUNCH("gates_bwd", st, (launch_k(gates_bwd_kernel, d.BH, 1024, 0, st, gp)));
+  CYFA_LAUNCH("gates_bwd", st,
+              (launch_k(gates_bwd_kernel, dim3(d.BH, (d.TP + 1023) / 1024), 1024, 0, st, gp)));
   return launch_status();
 }
 

@@ -118,33 +118,45 @@ __device__ __forceinline__ ScanPair scan1024(float x, float* wsum, float* total)
   return {__fadd_rn(x, tile_carry), __fadd_rn(x, block_carry)};
 }
 
+// Grid (B*H, ceil(TP/1024)): CTA (bh, k) scans token block k.  The clock carry
+// into the block (clock0 plus every earlier block's deltas) is summed by the CTA
+// itself, thread i over column i of the earlier blocks, so the blocks of a
+// sequence run side by side.
 __global__ void __launch_bounds__(1024) gates_fwd_kernel(GatesParams p) {
   pdl_wait();
   pdl_trigger();
-  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
+  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H, k = blockIdx.y;
   __shared__ float wsum[32];
-  float clock = p.clock0 ? p.clock0[bh] : 0.f;
   const size_t obase = size_t(bh) * p.TP;
-  for (int t0 = 0; t0 < p.TP; t0 += 1024) {
-    const int t = t0 + threadIdx.x;
-    float gv = 0.f, dv = 0.f, bv = 0.f;
-    if (t < p.T) {
-      const size_t i = (size_t(b) * p.T + t) * p.H + h;
-      gv = p.g[i];
-      dv = p.delta[i];
-      bv = p.beta[i];
-    }
-    float tot;
-    const ScanPair gs = scan1024<false>(gv, wsum, &tot);
-    const ScanPair ds = scan1024<false>(dv, wsum, &tot);
-    if (t < p.TP) {
-      p.G[obase + t] = gs.tile * kLog2e;
-      p.lam[obase + t] = __fadd_rn(clock, ds.block);
-      p.beta_h[obase + t] = bv;
-    }
-    clock = __fadd_rn(clock, tot);
+  const int t = k * 1024 + threadIdx.x;
+  auto delta_at = [&](int tt) {
+    return tt < p.T ? p.delta[(size_t(b) * p.T + tt) * p.H + h] : 0.f;
+  };
+  float gv = 0.f, dv = 0.f, bv = 0.f;
+  if (t < p.T) {
+    const size_t i = (size_t(b) * p.T + t) * p.H + h;
+    gv = p.g[i];
+    dv = p.delta[i];
+    bv = p.beta[i];
   }
-  if (threadIdx.x == 0 && p.clock_out) p.clock_out[bh] = clock;
+  float e[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  int kk = 0;
+  for (; kk + 8 <= k; kk += 8)
+#pragma unroll
+    for (int u = 0; u < 8; ++u) e[u] += delta_at((kk + u) * 1024 + threadIdx.x);
+  for (; kk < k; ++kk) e[0] += delta_at(kk * 1024 + threadIdx.x);
+  const float earlier = ((e[0] + e[1]) + (e[2] + e[3])) + ((e[4] + e[5]) + (e[6] + e[7]));
+  float tot, etot;
+  const ScanPair gs = scan1024<false>(gv, wsum, &tot);
+  const ScanPair ds = scan1024<false>(dv, wsum, &tot);
+  scan1024<false>(earlier, wsum, &etot);
+  const float clock = __fadd_rn(p.clock0 ? p.clock0[bh] : 0.f, etot);
+  if (t < p.TP) {
+    p.G[obase + t] = gs.tile * kLog2e;
+    p.lam[obase + t] = __fadd_rn(clock, ds.block);
+    p.beta_h[obase + t] = bv;
+  }
+  if (k == gridDim.y - 1 && threadIdx.x == 0 && p.clock_out) p.clock_out[bh] = __fadd_rn(clock, tot);
 }
 
 struct TokenFwdParams {
@@ -815,6 +827,8 @@ inline int token_bwd_blocks(size_t rows) {
 }
 
 
+constexpr int kMaxDgSlots = 6;  // row-dot partial slots of dG a launch may sum
+
 struct GatesBwdParams {
   const float* dG;       // [ndg][B,H,TP] gradient of the in-tile gate cumsum (natural log),
                          // as ndg partial slots dg_stride elements apart, summed in order
@@ -834,42 +848,57 @@ struct GatesBwdParams {
   int B, T, H, TP;
 };
 
+// Grid (B*H, ceil(TP/1024)) as the forward: CTA (bh, k) handles token block k,
+// and sums the clock-gradient carry from the later blocks itself.
 __global__ void __launch_bounds__(1024) gates_bwd_kernel(GatesBwdParams p) {
   pdl_wait();
   pdl_trigger();
-  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H;
+  const int bh = blockIdx.x, b = bh / p.H, h = bh % p.H, k = blockIdx.y;
   __shared__ float wsum[32];
-  float carry = p.dclock ? p.dclock[bh] : 0.f;
   const size_t base = size_t(bh) * p.TP;
-  const int nblk = (p.TP + 1023) / 1024;
-  for (int k = nblk - 1; k >= 0; --k) {
-    const int t = k * 1024 + threadIdx.x;
-    const bool in = t < p.TP;
-    float dGt = 0.f;
-    if (in)
-      for (int s = 0; s < p.ndg; ++s) dGt += p.dG[s * p.dg_stride + base + t];
-    if (in && (t & 127) == 127) {
-      const size_t tile = size_t(bh) * (p.TP / 128) + t / 128;
-      if (p.bpart1)
-        for (int i = 0; i < p.nsub1; ++i) dGt += p.bpart1[tile * p.nsub1 + i];
-      if (p.bpart2)
-        for (int i = 0; i < p.nsub2; ++i) dGt += p.bpart2[tile * p.nsub2 + i];
-    }
-    float dl = in ? p.dlam[base + t] : 0.f;
-    if (in && p.dlam2) dl += p.dlam2[base + t];
-    float tot;
-    const ScanPair gs = scan1024<true>(dGt, wsum, &tot);
-    const ScanPair ls = scan1024<true>(dl, wsum, &tot);
-    const float dd = __fadd_rn(carry, ls.block);
-    carry = __fadd_rn(carry, tot);
-    if (t < p.T) {
-      const size_t i = (size_t(b) * p.T + t) * p.H + h;
-      p.dg[i] = gs.tile;
-      p.ddelta[i] = dd;
-      p.dbeta[i] = p.dbeta_h[base + t];
-    }
+  const int t = k * 1024 + threadIdx.x;
+  const bool in = t < p.TP;
+  auto dlam_at = [&](int tt) {
+    if (tt >= p.TP) return 0.f;
+    float x = p.dlam[base + tt];
+    if (p.dlam2) x += p.dlam2[base + tt];
+    return x;
+  };
+  float v[kMaxDgSlots];
+#pragma unroll
+  for (int s = 0; s < kMaxDgSlots; ++s)
+    v[s] = in && s < p.ndg ? p.dG[s * p.dg_stride + base + t] : 0.f;
+  const float dl = dlam_at(t);
+  float l[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  const int nblk = gridDim.y;
+  int kk = nblk - 1;
+  for (; kk - 8 >= k; kk -= 8)
+#pragma unroll
+    for (int u = 0; u < 8; ++u) l[u] += dlam_at((kk - u) * 1024 + threadIdx.x);
+  for (; kk > k; --kk) l[0] += dlam_at(kk * 1024 + threadIdx.x);
+  const float later = ((l[0] + l[1]) + (l[2] + l[3])) + ((l[4] + l[5]) + (l[6] + l[7]));
+  float dGt = v[0];
+#pragma unroll
+  for (int s = 1; s < kMaxDgSlots; ++s) dGt += v[s];
+  if (in && (t & 127) == 127) {
+    const size_t tile = size_t(bh) * (p.TP / 128) + t / 128;
+    if (p.bpart1)
+      for (int i = 0; i < p.nsub1; ++i) dGt += p.bpart1[tile * p.nsub1 + i];
+    if (p.bpart2)
+      for (int i = 0; i < p.nsub2; ++i) dGt += p.bpart2[tile * p.nsub2 + i];
   }
-  if (threadIdx.x == 0 && p.dclock0) p.dclock0[bh] = carry;
+  float tot, ltot;
+  const ScanPair gs = scan1024<true>(dGt, wsum, &tot);
+  const ScanPair ls = scan1024<true>(dl, wsum, &tot);
+  scan1024<true>(later, wsum, &ltot);
+  const float carry = __fadd_rn(p.dclock ? p.dclock[bh] : 0.f, ltot);
+  if (t < p.T) {
+    const size_t i = (size_t(b) * p.T + t) * p.H + h;
+    p.dg[i] = gs.tile;
+    p.ddelta[i] = __fadd_rn(carry, ls.block);
+    p.dbeta[i] = p.dbeta_h[base + t];
+  }
+  if (k == 0 && threadIdx.x == 0 && p.dclock0) p.dclock0[bh] = __fadd_rn(carry, tot);
 }
 
 }  // namespace cyfa
