@@ -112,6 +112,23 @@ static void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
   cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Auxiliary stream of the calling thread (cyfa_set_aux_stream).  A launch
+// whose result no later kernel of the same entry point reads (a reduction into
+// parameter gradients) goes to it when set, ordered after the work so far on
+// the caller's stream; the caller makes its stream wait for the auxiliary one
+// before the results are read.
+static thread_local cudaStream_t t_aux = nullptr;
+
+static cudaStream_t defer_stream(cudaStream_t st) {
+  if (t_aux == nullptr || t_aux == st) return st;
+  cudaEvent_t ev;
+  if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return st;
+  const bool ok = cudaEventRecord(ev, st) == cudaSuccess &&
+                  cudaStreamWaitEvent(t_aux, ev, 0) == cudaSuccess;
+  cudaEventDestroy(ev);
+  return ok ? t_aux : st;
+}
+
 static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point, so the
@@ -318,6 +335,11 @@ const char* cyfa_strerror(int status) {
 long long cyfa_launch_count(void) { return g_launches.load(); }
 
 int cyfa_set_pdl(int on) { return g_pdl.exchange(on != 0 ? 1 : 0); }
+
+int cyfa_set_aux_stream(void* aux) {
+  t_aux = static_cast<cudaStream_t>(aux);
+  return 0;
+}
 
 int cyfa_profile_enable(int on) {
   std::lock_guard<std::mutex> lk(g_prof_mu);

@@ -269,6 +269,7 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                    a->hk && a->hv && g->d_o && g->dq && g->dk && g->dv && g->dg && g->ddelta &&
                    g->dbeta && g->dtable && g->dq_norm_weight && g->dk_norm_weight,
                kNullPointer);
+  CYFA_REQUIRE(!g->dreadout || g->readout_basis_t, kNullPointer);
   const Dims d = make_dims(a->B, a->T, a->H, a->K, a->V);
   size_t need_s = 0, need_w = 0;
   carve_saved(d, nullptr, &need_s);
@@ -395,9 +396,10 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                 (launch_k(readout_bwd_kernel, d.H * per_head, 256, kReadoutBwdSmem, st, m_tab, m_raw,
                                                                                   m_dwt, rp)));
     if ((rc = launch_status())) return rc;
-    CYFA_LAUNCH("dtable_reduce", st,
-                (launch_k(dtable_reduce_kernel, dim3(d.H, 128), 128, 0, st, w.dtab_part, g->dtable,
-                                                                      per_head)));
+    cudaStream_t sr = defer_stream(st);  // nothing below reads the table gradient
+    CYFA_LAUNCH("dtable_reduce", sr,
+                (launch_k(dtable_reduce_kernel, dim3(d.H, 128), 128, 0, sr, w.dtab_part, g->dtable,
+                          per_head, g->readout_basis_t, g->dreadout)));
     if ((rc = launch_status())) return rc;
   }
   // ================= pass 1 (queries = q^, keys = k^, values = w)
@@ -449,8 +451,9 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                         stride_or(g->dq_stride, d.H * d.K), stride_or(g->dk_stride, d.H * d.K),
                         true, stream, &nblk);
   if (rc) return rc;
-  CYFA_LAUNCH("column_sum", st,
-              (launch_k(column_sum_kernel, dim3((d.K + 31) / 32, 2), 1024, 0, st, w.dqw_part,
+  cudaStream_t sc = defer_stream(st);
+  CYFA_LAUNCH("column_sum", sc,
+              (launch_k(column_sum_kernel, dim3((d.K + 31) / 32, 2), 1024, 0, sc, w.dqw_part,
                         g->dq_norm_weight, nblk, d.K, w.dkw_part, g->dk_norm_weight, 0x7fffffff,
                         nullptr)));
   if ((rc = launch_status())) return rc;

@@ -787,12 +787,16 @@ __global__ void __launch_bounds__(128) readout_grad_kernel(const float* dtab, co
 }
 
 // Fixed-order reduction of the per-CTA table gradients:
-// dtab[h][r][m] = sum_{s < per_head} part[h * per_head + s][r][m].
+// dtab[h][r][m] = sum_{s < per_head} part[h * per_head + s][r][m],
+// and, with dR given, the readout gradient row r < 127 from the reduced row
+// (the sums of readout_grad_kernel).
 __global__ void __launch_bounds__(128) dtable_reduce_kernel(const float* part, float* dtab,
-                                                            int per_head) {
+                                                            int per_head, const float* phiT,
+                                                            float* dR) {
   pdl_wait();
   pdl_trigger();
   const int h = blockIdx.x, r = blockIdx.y, m = threadIdx.x;
+  __shared__ float row[128];
   float s0 = 0.f, s1 = 0.f;
   int k = 0;
   for (; k + 1 < per_head; k += 2) {
@@ -800,7 +804,17 @@ __global__ void __launch_bounds__(128) dtable_reduce_kernel(const float* part, f
     s1 += part[(size_t(h) * per_head + k + 1) * 16384 + r * 128 + m];
   }
   if (k < per_head) s0 += part[(size_t(h) * per_head + k) * 16384 + r * 128 + m];
-  dtab[(size_t(h) * 128 + r) * 128 + m] = s0 + s1;
+  const float s = s0 + s1;
+  dtab[(size_t(h) * 128 + r) * 128 + m] = s;
+  if (dR == nullptr || r >= 127) return;
+  row[m] = s;
+  __syncthreads();
+  if (m < 127) {
+    float acc = 0.f;
+#pragma unroll 16
+    for (int c = 0; c < 128; ++c) acc = fmaf(row[c], __ldg(phiT + c * 127 + m), acc);
+    dR[(size_t(h) * 127 + r) * 127 + m] = acc;
+  }
 }
 
 // Fixed-order column sums of a [rows, cols] partial matrix: out[c] = sum_r part[r][c].

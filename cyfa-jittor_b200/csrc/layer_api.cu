@@ -144,9 +144,10 @@ int cyfa_short_conv_bwd(const void* x, long long x_stride, const float* w, const
   if (rc) return rc;
   // reduce the partial rows: columns are [c][0..W-1] = dw, [c][W] = dbias
   const int cols = C * (W + 1);
-  CYFA_LAUNCH("conv_param_sum", s,
-              (launch_k(conv_param_sum_kernel, (cols + 255) / 256, 256, 0, s, part, rows, C, W, dw,
-                                                                        dbias)));
+  cudaStream_t sr = defer_stream(s);
+  CYFA_LAUNCH("conv_param_sum", sr,
+              (launch_k(conv_param_sum_kernel, (cols + 255) / 256, 256, 0, sr, part, rows, C, W, dw,
+                        dbias)));
   return launch_status();
 }
 
@@ -202,9 +203,10 @@ int cyfa_gate_act_bwd(const void* a, long long a_stride, const void* b, long lon
   int rc = launch_status();
   if (rc) return rc;
   // partial columns: dA_log | ddt_bias | db_bias | dd_bias, each H wide
-  CYFA_LAUNCH("column_sum", s,
-              (launch_k(gate_param_sum_kernel, 1, 1024, 0, s, part, nblk, H, dA_log, ddt_bias, db_bias,
-                                                        dd_bias)));
+  cudaStream_t sr = defer_stream(s);
+  CYFA_LAUNCH("column_sum", sr,
+              (launch_k(gate_param_sum_kernel, 1, 1024, 0, sr, part, nblk, H, dA_log, ddt_bias,
+                        db_bias, dd_bias)));
   return launch_status();
 }
 
@@ -247,8 +249,9 @@ int cyfa_gated_norm_bwd(const void* x, const void* gate, const float* w, float s
   else CYFA_LAUNCH("gated_norm_bwd", s, (launch_k(gated_norm_bwd_kernel<4>, nblk, 256, 0, s, p)));
   int rc = launch_status();
   if (rc) return rc;
-  CYFA_LAUNCH("column_sum", s,
-              (launch_k(column_sum_kernel, (D + 31) / 32, 1024, 0, s, part, dw, nblk, D, nullptr,
+  cudaStream_t sr = defer_stream(s);
+  CYFA_LAUNCH("column_sum", sr,
+              (launch_k(column_sum_kernel, (D + 31) / 32, 1024, 0, sr, part, dw, nblk, D, nullptr,
                         nullptr, 0x7fffffff, nullptr)));
   return launch_status();
 }
@@ -349,8 +352,9 @@ int cyfa_gated_norm_bias_bwd(const void* x, const void* gate, const void* gate_b
   }
   int rc = launch_status();
   if (rc) return rc;
-  CYFA_LAUNCH("column_sum", s,
-              (launch_k(column_sum_kernel, (cols + 31) / 32, 1024, 0, s, part, dw, nblk, cols,
+  cudaStream_t sr = defer_stream(s);
+  CYFA_LAUNCH("column_sum", sr,
+              (launch_k(column_sum_kernel, (cols + 31) / 32, 1024, 0, sr, part, dw, nblk, cols,
                         nullptr, nullptr, D, dgate_bias)));
   return launch_status();
 }

@@ -5,6 +5,7 @@ cyfa-jittor_b200/csrc``).  There is no CPU fallback: if the library or a CUDA
 device is missing, every op raises.
 """
 
+import contextlib
 import ctypes
 import os
 
@@ -103,6 +104,8 @@ def lib():
         handle.cyfa_profile_enable.restype = ctypes.c_int
         handle.cyfa_set_pdl.argtypes = [ctypes.c_int]
         handle.cyfa_set_pdl.restype = ctypes.c_int
+        handle.cyfa_set_aux_stream.argtypes = [ctypes.c_void_p]
+        handle.cyfa_set_aux_stream.restype = ctypes.c_int
         handle.cyfa_profile_report.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
                                                ctypes.POINTER(ctypes.c_float),
                                                ctypes.POINTER(ctypes.c_int)]
@@ -131,6 +134,20 @@ def ptr(t):
 def stream():
     """The current torch CUDA stream as a raw handle."""
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@contextlib.contextmanager
+def deferred(aux):
+    """Inside the block, the library's final parameter-gradient reductions run on
+    the torch stream `aux`, after the work already issued on the current stream
+    (cyfa_set_aux_stream).  The caller makes the current stream wait for `aux`
+    before those gradients are read and keeps the calls' workspaces alive until
+    then."""
+    lib().cyfa_set_aux_stream(ctypes.c_void_p(aux.cuda_stream))
+    try:
+        yield
+    finally:
+        lib().cyfa_set_aux_stream(None)
 
 
 def require_cuda(*tensors):

@@ -16,12 +16,14 @@ import torch.nn.functional as F
 from torch import nn
 
 from ..ops import chunk_cyfa, fused_recurrent_cyfa
+from ..ops.chunk import table_bf16
 from ..ops.layer_ops import (
     ChunkCyfaPackedFunction,
     GatedNormFunction,
     LayerFrontFunction,
     LinearFunction,
     PackedGradSlot,
+    _fork,
 )
 
 
@@ -188,6 +190,11 @@ class CyclicFlowAttention(nn.Module):
             t.requires_grad for t in (x, self.q_proj.weight, self.k_proj.weight,
                                       self.v_proj.weight, g0.weight, self.a_proj.weight,
                                       self.b_proj.weight, self.d_proj.weight))
+        # the readout table on the aux stream, beside the projection (joined with
+        # the parameter conversions before the convolution)
+        tb = torch.empty(H, 128, 128, device=x.device, dtype=torch.bfloat16)
+        with torch.cuda.stream(_fork(x.device)):
+            table_bf16(self.readout, out=tb)
         qkv, gate_in, g, delta, beta = LayerFrontFunction.apply(
             x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, g0.weight,
             self.a_proj.weight, self.b_proj.weight, self.d_proj.weight, self.q_conv1d.weight,
@@ -195,7 +202,8 @@ class CyclicFlowAttention(nn.Module):
             self.b_proj.bias, self.d_proj.bias, H, slot, self.grad_ready)
         o, hk, hv, clock = ChunkCyfaPackedFunction.apply(
             qkv, H, K, V, g, delta, beta, self.readout, self.q_norm.weight.float(),
-            self.k_norm.weight.float(), float(self.q_norm.eps), float(self.k_norm.eps), K ** -0.5)
+            self.k_norm.weight.float(), float(self.q_norm.eps), float(self.k_norm.eps), K ** -0.5,
+            tb)
         g1 = self.g_proj[1]
         y = GatedNormFunction.apply(o, gate_in, g1.weight, g1.bias, self.o_norm.weight,
                                     self.o_norm.eps, float(self.num_slots - 1), slot, (g1.weight,))

@@ -31,7 +31,8 @@ class _BwdArgs(_c.Structure):
         [(n, _c.c_void_p) for n in ("d_o", "dhk", "dhv", "dclock", "dq", "dk", "dv", "dg",
                                      "ddelta", "dbeta", "dtable", "dq_norm_weight",
                                      "dk_norm_weight", "dhk0", "dhv0", "dclock0")] + \
-        [(n, _c.c_longlong) for n in ("dq_stride", "dk_stride", "dv_stride")]
+        [(n, _c.c_longlong) for n in ("dq_stride", "dk_stride", "dv_stride")] + \
+        [(n, _c.c_void_p) for n in ("readout_basis_t", "dreadout")]
 
 
 _BASIS = {}
@@ -73,12 +74,14 @@ def readout_table(readout):
     return readout.float() @ basis(M, readout.device)
 
 
-def table_bf16(readout):
+def table_bf16(readout, out=None):
     """The readout table in the kernels' layout: bf16 [H, 128, 128], Table_h =
-    R_h . Phi rounded once, last row zero (one libcyfa launch)."""
+    R_h . Phi rounded once, last row zero (one libcyfa launch, into `out` if
+    given)."""
     H = readout.shape[0]
     r = readout.detach().to(torch.float32).contiguous()
-    tb = torch.empty(H, 128, 128, device=readout.device, dtype=torch.bfloat16)
+    tb = torch.empty(H, 128, 128, device=readout.device, dtype=torch.bfloat16) if out is None \
+        else out
     _lib.call("cyfa_readout_table", _p(r), _p(basis(128, readout.device)), _p(tb), H,
               _lib.stream())
     return tb

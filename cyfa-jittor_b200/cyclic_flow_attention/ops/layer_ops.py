@@ -10,7 +10,7 @@ import ctypes
 import torch
 
 from .. import _lib
-from .chunk import _BwdArgs, _FwdArgs, _p, readout_grad, table_bf16
+from .chunk import _BwdArgs, _FwdArgs, _p, basis_t, readout_grad, table_bf16
 
 _c = ctypes
 
@@ -44,21 +44,25 @@ def flat_f32(sizes, device):
     return torch.empty(max(total, 8), device=device, dtype=torch.float32), offs
 
 
-def gather_f32(tensors):
+def gather_f32(tensors, stream=None):
     """The tensors as fp32 views of one buffer, filled by one libcyfa launch
-    (the per-step conversion of the small parameters)."""
+    (the per-step conversion of the small parameters).  The buffer belongs to
+    the current stream; the launch goes to `stream` if given (the caller then
+    makes the current stream wait for it before the views are read)."""
     tensors = [t.detach() for t in tensors]
     flat, offs = flat_f32([t.numel() for t in tensors], tensors[0].device)
     if not _fits_pieces(tensors):
         return [t.float().contiguous() for t in tensors]
-    _lib.call("cyfa_bucket_gather", _pieces(tensors, offs), len(tensors), _p(flat),
-              _lib.stream())
+    with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream()):
+        _lib.call("cyfa_bucket_gather", _pieces(tensors, offs), len(tensors), _p(flat),
+                  _lib.stream())
     return [flat[o:o + t.numel()].view(t.shape) for t, o in zip(tensors, offs)]
 
 
-def scatter_from(flat, offs, like):
+def scatter_from(flat, offs, like, stream=None):
     """Gradients held in fp32 at flat[offs[i]:] converted to the dtype and shape
-    of like[i] by one libcyfa launch; fp32 targets are views of `flat`."""
+    of like[i] by one libcyfa launch (on `stream` if given; the outputs belong to
+    the current stream); fp32 targets are views of `flat`."""
     outs, pieces, poffs = [], [], []
     for o, t in zip(offs, like):
         if t.dtype == torch.float32:
@@ -68,9 +72,12 @@ def scatter_from(flat, offs, like):
             pieces.append(outs[-1])
             poffs.append(o)
     if pieces and _fits_pieces(pieces):
-        _lib.call("cyfa_bucket_scatter", _pieces(pieces, poffs), len(pieces), _p(flat),
-                  _c.c_float(1.0), _lib.stream())
+        with torch.cuda.stream(stream if stream is not None else torch.cuda.current_stream()):
+            _lib.call("cyfa_bucket_scatter", _pieces(pieces, poffs), len(pieces), _p(flat),
+                      _c.c_float(1.0), _lib.stream())
     elif pieces:
+        if stream is not None:
+            torch.cuda.current_stream().wait_stream(stream)
         for i, (o, t) in enumerate(zip(offs, like)):
             if t.dtype != torch.float32:
                 outs[i] = flat[o:o + t.numel()].view(t.shape).to(t.dtype)
@@ -212,16 +219,17 @@ class GatedNormFunction(torch.autograd.Function):
             db = torch.empty(H * D, device=x.device, dtype=torch.float32)
             nbytes = _lib.lib().cyfa_gated_norm_bias_work_bytes(rows, D, H)
             work = _work(nbytes, x.device)
-            _lib.call("cyfa_gated_norm_bias_bwd", _p(x), _p(gate), _p(b), H, _p(w), float(scale),
-                      _p(rstd), _p(dy), _p(dx), _p(dgate), _p(dw), _p(db), rows, D, _p(work),
-                      _c.c_size_t(nbytes), _lib.stream())
-            d_gate_b = db.to(bdt)
+            with _lib.deferred(_aux_stream(x.device)):
+                _lib.call("cyfa_gated_norm_bias_bwd", _p(x), _p(gate), _p(b), H, _p(w),
+                          float(scale), _p(rstd), _p(dy), _p(dx), _p(dgate), _p(dw), _p(db), rows,
+                          D, _p(work), _c.c_size_t(nbytes), _lib.stream())
         else:
             nbytes = _lib.lib().cyfa_gated_norm_work_bytes(rows, D)
             work = _work(nbytes, x.device)
-            _lib.call("cyfa_gated_norm_bwd", _p(x), _p(gate), _p(w), float(scale), _p(rstd),
-                      _p(dy), _p(dx), _p(dgate), _p(dw), rows, D, _p(work), _c.c_size_t(nbytes),
-                      _lib.stream())
+            with _lib.deferred(_aux_stream(x.device)):
+                _lib.call("cyfa_gated_norm_bwd", _p(x), _p(gate), _p(w), float(scale), _p(rstd),
+                          _p(dy), _p(dx), _p(dgate), _p(dw), rows, D, _p(work),
+                          _c.c_size_t(nbytes), _lib.stream())
         dg2 = dgate.reshape(-1, H * D)
         gin2 = gate_in.reshape(-1, gate_in.shape[-1])
         slot = ctx.slot
@@ -238,17 +246,43 @@ class GatedNormFunction(torch.autograd.Function):
             d_gate_in = None
         else:
             d_gate_in = (dg2 @ gate_w).reshape(gate_in.shape)
+        _join(x.device)  # the norm-weight (and gate-bias) sums ran on the aux stream
+        if b is not None:
+            d_gate_b = db.to(bdt)
         return dx, d_gate_in, d_gate_w, d_gate_b, dw.to(wdt), None, None, None, None
 
 
 _SIDE = {}
+_AUX = {}
 
 
 def _side_stream(device):
+    """Stream of the deferred weight-gradient GEMMs (joined in the front's backward)."""
     key = str(device)
     if key not in _SIDE:
         _SIDE[key] = torch.cuda.Stream(device=device)
     return _SIDE[key]
+
+
+def _aux_stream(device):
+    """Stream of the small parameter kernels (parameter conversions, the readout
+    table, parameter-gradient reductions), each joined by the Function that
+    forks it."""
+    key = str(device)
+    if key not in _AUX:
+        _AUX[key] = torch.cuda.Stream(device=device)
+    return _AUX[key]
+
+
+def _fork(device):
+    """The aux stream, ordered after the work issued so far on the current stream."""
+    aux = _aux_stream(device)
+    aux.wait_stream(torch.cuda.current_stream(device))
+    return aux
+
+
+def _join(device):
+    torch.cuda.current_stream(device).wait_stream(_aux_stream(device))
 
 
 class LinearFunction(torch.autograd.Function):
@@ -360,14 +394,16 @@ class LayerFrontFunction(torch.autograd.Function):
         NB = (n_used + 7) // 8 * 8  # 16-byte rows
         parts = [w_q, w_k, w_v, w_g0, w_a, w_b, w_d]
         # the padding rows stay uninitialised: the columns they produce are never read
+        # conv weights (one [n_qkv, Wc] block when the q, k, v pieces are adjacent)
+        # and gate parameters as fp32, one launch on the aux stream beside the
+        # projection (joined before the convolution)
+        cwq, cwk, cwv, A, dt, bb, db = gather_f32(
+            [cw_q, cw_k, cw_v, A_log, dt_bias, b_bias, d_bias], _fork(dev))
         W_big = torch.empty(NB, hid, device=dev, dtype=w_q.dtype)
         torch.cat(parts, out=W_big[:n_used])
         big = torch.nn.functional.linear(x, W_big)  # [B, T, NB]
         Wc = cw_q.shape[-1]
-        # conv weights (one [n_qkv, Wc] block when the q, k, v pieces are adjacent)
-        # and gate parameters as fp32, one launch
-        cwq, cwk, cwv, A, dt, bb, db = gather_f32(
-            [cw_q, cw_k, cw_v, A_log, dt_bias, b_bias, d_bias])
+        _join(dev)
         if (cwk.data_ptr() == cwq.data_ptr() + 4 * cwq.numel()
                 and cwv.data_ptr() == cwk.data_ptr() + 4 * cwk.numel()):
             cw = torch.as_strided(cwq, (n_qkv, Wc), (Wc, 1))
@@ -424,28 +460,36 @@ class LayerFrontFunction(torch.autograd.Function):
         if goffs[1] != n_cw or goffs[2] != goffs[1] + sizes[1] * Wc:
             dcw = torch.empty(n_qkv, Wc, device=dev, dtype=torch.float32)
         dA, ddtb, dbb, ddb = (gflat[o:o + H] for o in goffs[3:])
+        # the parameter-gradient reductions of the convolution and gate kernels and
+        # the scatter into the parameters' dtypes run on the aux stream, joined
+        # before the gradients leave this function; their workspaces live until then
+        aux = _aux_stream(dev)
+        keep = []
         if dqkv is None:
             dbig[..., :n_qkv].zero_()
             dcw.zero_()
         else:
             dqkv = dqkv.to(torch.bfloat16).contiguous()
             nbytes = _lib.lib().cyfa_short_conv_work_bytes(B, T, n_qkv, Wc)
-            work = _work(nbytes, dev)
-            _lib.call("cyfa_short_conv_bwd", _p(big), st, _p(cw), _p(dqkv), _p(dbig), st, _p(dcw),
-                      None, B, T, n_qkv, Wc, _p(work), _c.c_size_t(nbytes), _lib.stream())
+            keep.append(_work(nbytes, dev))
+            with _lib.deferred(aux):
+                _lib.call("cyfa_short_conv_bwd", _p(big), st, _p(cw), _p(dqkv), _p(dbig), st,
+                          _p(dcw), None, B, T, n_qkv, Wc, _p(keep[-1]), _c.c_size_t(nbytes),
+                          _lib.stream())
         # gate activation adjoints -> the a, b, d columns
         zeros = lambda: torch.zeros(B, T, H, device=dev, dtype=torch.float32)
         dg = zeros() if dg is None else dg.float().contiguous()
         ddelta = zeros() if ddelta is None else ddelta.float().contiguous()
         dbeta = zeros() if dbeta is None else dbeta.float().contiguous()
         nbytes = _lib.lib().cyfa_gate_act_work_bytes(rows, H)
-        work = _work(nbytes, dev)
-        _lib.call("cyfa_gate_act_bwd", _c.c_void_p(base + 2 * c_a), st, _c.c_void_p(base + 2 * c_b),
-                  st, _c.c_void_p(base + 2 * c_d), st, _p(A), _p(dt), _p(bb), _p(db_), _p(dg),
-                  _p(ddelta), _p(dbeta), _c.c_void_p(dbase + 2 * c_a), st,
-                  _c.c_void_p(dbase + 2 * c_b), st, _c.c_void_p(dbase + 2 * c_d), st, _p(dA),
-                  _p(ddtb), _p(dbb), _p(ddb), rows, H, _p(work), _c.c_size_t(nbytes),
-                  _lib.stream())
+        keep.append(_work(nbytes, dev))
+        with _lib.deferred(aux):
+            _lib.call("cyfa_gate_act_bwd", _c.c_void_p(base + 2 * c_a), st,
+                      _c.c_void_p(base + 2 * c_b), st, _c.c_void_p(base + 2 * c_d), st, _p(A),
+                      _p(dt), _p(bb), _p(db_), _p(dg), _p(ddelta), _p(dbeta),
+                      _c.c_void_p(dbase + 2 * c_a), st, _c.c_void_p(dbase + 2 * c_b), st,
+                      _c.c_void_p(dbase + 2 * c_d), st, _p(dA), _p(ddtb), _p(dbb), _p(ddb), rows,
+                      H, _p(keep[-1]), _c.c_size_t(nbytes), _lib.stream())
         # output-gate input gradient -> its columns (unless its consumer wrote them)
         if dgate_in is not None:
             if gate_done:
@@ -459,17 +503,21 @@ class LayerFrontFunction(torch.autograd.Function):
         # weight gradients first, so that their hand-over overlaps the dx GEMM
         dW = torch.matmul(d2[:, :n_used].t(), x2)
         if dcw.data_ptr() != gflat.data_ptr():  # conv pieces not adjacent in gflat
+            _join(dev)
             for (o, n), blk in zip(((goffs[0], sizes[0]), (goffs[1], sizes[1]), (goffs[2], sizes[2])),
                                    torch.split(dcw, sizes[:3])):
                 gflat[o:o + n * Wc].copy_(blk.reshape(-1))
-        small = scatter_from(gflat, goffs, ctx.small_like)
+        small = scatter_from(gflat, goffs, ctx.small_like, _fork(dev))
         grads = (*torch.split(dW, sizes), *small)
         if ctx.grad_ready is not None:
+            _join(dev)
             ctx.grad_ready(ctx.params, grads)
         # dx from every column except d (projected from x.detach()) and the padding
         dx = None
         if ctx.needs_input_grad[0]:
             dx = torch.matmul(d2[:, :c_d], W_big[:c_d]).view(B, T, hid)
+        _join(dev)
+        del keep
         return (dx, *grads, None, None, None)
 
 
@@ -479,13 +527,18 @@ class ChunkCyfaPackedFunction(torch.autograd.Function):
     packed layout."""
 
     @staticmethod
-    def forward(ctx, qkv, H, K, V, g, delta, beta, readout, qw, kw, q_eps, k_eps, scale):
+    def forward(ctx, qkv, H, K, V, g, delta, beta, readout, qw, kw, q_eps, k_eps, scale,
+                tb=None):
+        # tb: the readout table already computed from `readout` on the aux stream
         ctx.set_materialize_grads(False)  # the final states usually get no gradient
         B, T, width = qkv.shape
         dev = qkv.device
         row = qkv.stride(1)
         base = qkv.data_ptr()
-        tb = table_bf16(readout)
+        if tb is None:
+            tb = table_bf16(readout)
+        else:
+            _join(dev)
         o = torch.empty(B, T, H, V, device=dev, dtype=torch.bfloat16)
         hk = torch.empty(B, H, K, 128, device=dev, dtype=torch.float32)
         hv = torch.empty(B, H, 128, V, device=dev, dtype=torch.float32)
@@ -532,10 +585,23 @@ class ChunkCyfaPackedFunction(torch.autograd.Function):
         dkw = torch.empty(K, device=dev, dtype=torch.float32)
         nwork = _lib.lib().cyfa_chunk_work_bytes(B, T, H, K, V)
         work = _work(nwork, dev)
+        # the readout gradient comes from the table-gradient reduction's launch;
+        # that launch and the norm-weight sums run on the aux stream, beside the
+        # rest of the backward, and are joined before returning
+        dr = torch.empty(H, 127, 127, device=dev, dtype=torch.float32) \
+            if ctx.needs_input_grad[7] else None
         args = _BwdArgs(fwd, _p(do), _p(dhk), _p(dhv), _p(dclock), db_, db_ + 2 * H * K,
                         db_ + 4 * H * K, _p(dg), _p(ddelta), _p(dbeta), _p(dtable), _p(dqw),
-                        _p(dkw), None, None, None, width, width, width)
-        _lib.call("cyfa_chunk_bwd", _c.byref(args), _lib.ptr(saved), _c.c_size_t(saved.numel()),
-                  _lib.ptr(work), _c.c_size_t(nwork), _lib.stream())
-        dreadout = readout_grad(dtable, ctx.readout_meta) if ctx.needs_input_grad[7] else None
-        return (dqkv, None, None, None, dg, ddelta, dbeta, dreadout, dqw, dkw, None, None, None)
+                        _p(dkw), None, None, None, width, width, width,
+                        _p(basis_t(128, dev)) if dr is not None else None, _p(dr))
+        with _lib.deferred(_aux_stream(dev)):
+            _lib.call("cyfa_chunk_bwd", _c.byref(args), _lib.ptr(saved),
+                      _c.c_size_t(saved.numel()), _lib.ptr(work), _c.c_size_t(nwork),
+                      _lib.stream())
+        _join(dev)
+        dreadout = None
+        if dr is not None:
+            rd = ctx.readout_meta.dtype
+            dreadout = dr if rd == torch.float32 else dr.to(rd)
+        return (dqkv, None, None, None, dg, ddelta, dbeta, dreadout, dqw, dkw, None, None, None,
+                None)

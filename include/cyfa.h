@@ -53,6 +53,15 @@ long long cyfa_launch_count(void);
  * order.  Returns the previous setting. */
 int cyfa_set_pdl(int on);
 
+/* Auxiliary stream of the calling thread, or NULL (the default) for none.
+ * While set, the entry points called on this thread launch their final
+ * parameter-gradient reductions (norm-weight, convolution, gate-parameter and
+ * readout-table sums) on it, ordered after the work already issued on the
+ * call's stream, so that they overlap the caller's next kernels.  The caller
+ * makes its stream wait for the auxiliary stream before reading those
+ * gradients or freeing the call's workspace. */
+int cyfa_set_aux_stream(void* aux);
+
 /* Turns per-kernel timing on (1) or off (0) and clears earlier records.  While
  * on, every launch is bracketed by CUDA events on its own stream. */
 int cyfa_profile_enable(int on);
@@ -190,6 +199,10 @@ typedef struct {
   long long dq_stride;          /* token stride of dq (0 = H*K) */
   long long dk_stride;          /* token stride of dk (0 = H*K) */
   long long dv_stride;          /* token stride of dv (0 = H*V) */
+  const float* readout_basis_t; /* Phi^T [128,127] f32, or NULL */
+  float* dreadout;              /* out [H,127,127], or NULL: the readout gradient
+                                   (cyfa_readout_table_grad of dtable) in the same
+                                   launch as dtable */
 } cyfa_chunk_bwd_args;
 
 /* Readout table in the kernels' layout (replaces the table product of
