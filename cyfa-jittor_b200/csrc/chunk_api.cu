@@ -200,16 +200,19 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
     if ((rc = launch_status())) return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, 128, kRows2D, 0, s.G, s.lam, a->scale, s.raw,
                     s.weights};
+    // the state history in 64-row blocks, as the two-CTA kernel streams it
+    CUtensorMap m_s1_64;
+    if ((rc = tmap_2d(&m_s1_64, s.s1, uint64_t(d.BH) * d.NT * d.K, 128, 64))) return rc;
     if (d.K == 256) {
-      set_smem(tile_fwd_kernel<256, true>, tile_fwd_smem<256>());
+      set_smem(tile_fwd_ro_kernel<256>, kRoSmem);
       CYFA_LAUNCH("tile_fwd_readout", st,
-                  (launch_k(tile_fwd_kernel<256, true>, dim3(d.BH * d.NT, 1), 256, tile_fwd_smem<256>(), st, 
-                      m_qn, m_kn, m_w, m_s1, m_tab, t)));
+                  (launch_k(tile_fwd_ro_kernel<256>, dim3(d.BH * d.NT, 1), 256, kRoSmem, st, m_qn,
+                            m_kn, m_w, m_s1_64, m_tab, t)));
     } else {
-      set_smem(tile_fwd_kernel<128, true>, tile_fwd_smem<128>());
+      set_smem(tile_fwd_ro_kernel<128>, kRoSmem);
       CYFA_LAUNCH("tile_fwd_readout", st,
-                  (launch_k(tile_fwd_kernel<128, true>, dim3(d.BH * d.NT, 1), 256, tile_fwd_smem<128>(), st, 
-                      m_qn, m_kn, m_w, m_s1, m_tab, t)));
+                  (launch_k(tile_fwd_ro_kernel<128>, dim3(d.BH * d.NT, 1), 256, kRoSmem, st, m_qn,
+                            m_kn, m_w, m_s1_64, m_tab, t)));
     }
     if ((rc = launch_status())) return rc;
   }

@@ -679,4 +679,292 @@ __global__ void __launch_bounds__(256, 1)
   }
 }
 
+// ============================================================ tile output with readout, 2 CTAs/SM
+// Pass 1's output tile and the slot readout (the READOUT path of tile_fwd_kernel)
+// in half its shared memory, so that two CTAs share an SM and one CTA's loads
+// and MMAs run during the other's epilogues.  Q, K and the state S_j stream
+// through two 48 KiB stages in 64-wide k-blocks (Q | K | S rows of the block);
+// the stages are then reused:
+//   stage 0: V (32 KiB) once k-block NKB-2 is done, then z; table panel 0 at +32 KiB
+//   stage 1: P once all k-blocks are done, then the store staging and p; table
+//            panel 1 at +32 KiB
+// TMEM (256 columns): [0,128) Q K^T -> P V -> logits;  [128,256) Q S_j -> p Tab.
+constexpr int kRoStage = 49152;
+constexpr int kRoSmem = 2 * kRoStage + 1024;
+
+template <int DK>
+__global__ void __launch_bounds__(256, 2)
+    tile_fwd_ro_kernel(const __grid_constant__ CUtensorMap map_q,
+                       const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v,
+                       const __grid_constant__ CUtensorMap map_s64,
+                       const __grid_constant__ CUtensorMap map_tab, TileFwdParams p) {
+  constexpr int NKB = DK / 64;
+  static_assert(NKB % 2 == 0, "k-blocks alternate between the two stages");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  __shared__ __align__(8) uint64_t full[2], empty[2], bar_v, bar_tab[2], bar_m[4];
+  __shared__ uint32_t tmem_base;
+  __shared__ float Gs[128];
+  __shared__ float xch[2][128];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int quad = warp & 3, half = warp >> 2;
+  const int r = quad * 32 + lane;
+  const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT;
+  const int t = j * 128 + r;
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(&bar_v, 1);
+    mbar_init(&bar_tab[0], 1);
+    mbar_init(&bar_tab[1], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&bar_m[i], 1);
+    mbar_fence_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_base, 256);
+    tmem_relinquish();  // one allocation per CTA: let the co-resident CTA allocate
+  }
+  pdl_wait();
+  if (tid < 128) Gs[tid] = p.G[size_t(bh) * p.TP + j * 128 + tid];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_trigger();
+  const uint32_t tmem = tmem_base;
+  const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
+  const uint32_t st0 = smem_u32(smem), st1 = st0 + kRoStage;
+  const uint32_t tab0 = st0 + 32768, tab1 = st1 + 32768;
+  bool ok = true;
+  // copies issued by thread 0 (for the drain after a failed wait)
+  int issued = 0, consumed = 0;
+  bool v_issued = false, tab_issued[2] = {false, false};
+
+  if (tid == 0) {
+    // ---- Q K^T and Q S_j over the k-blocks
+    auto issue = [&](int kb) {
+      const int s = kb & 1;
+      uint8_t* b = smem + s * kRoStage;
+      mbar_expect_tx(&full[s], kRoStage);
+      load_token_tile(b, &map_q, kRows2D, bh, p.H, p.TP, j, 64 * kb, 64, &full[s]);
+      load_token_tile(b + 16384, &map_k, kRows2D, bh, p.H, p.TP, j, 64 * kb, 64, &full[s]);
+      for (int c = 0; c < 2; ++c)
+        tma_load_2d(b + 32768 + c * 8192, &map_s64, &full[s], 64 * c,
+                    (bh * p.NT + j) * DK + 64 * kb);
+      ++issued;
+    };
+    issue(0);
+    issue(1);
+    for (int kb = 0; kb < NKB && ok; ++kb) {
+      const int s = kb & 1;
+      if (!mbar_wait(&full[s], (kb >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      consumed = kb + 1;
+      tc_fence_after();
+      const uint32_t sq = s ? st1 : st0, sk = sq + 16384, ss = sq + 32768;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem, kmaj_desc(sq, 128, ks), kmaj_desc(sk, 128, ks), make_idesc(128, 128, 0, 0),
+                  kb > 0 || ks > 0);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_bf16(tmem + 128, kmaj_desc(sq, 128, ks), mnmaj_desc(ss, 64, ks),
+                  make_idesc(128, 128, 0, 1), kb > 0 || ks > 0);
+      umma_commit(&empty[s]);
+      // the stage's next use once these MMAs are done: k-block kb + 2, or (the
+      // last two k-blocks) V and table panel 0 into stage 0 / panel 1 into stage 1
+      if (!mbar_wait(&empty[s], (kb >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      if (kb + 2 < NKB) {
+        issue(kb + 2);
+      } else if (s == 0) {
+        mbar_expect_tx(&bar_v, 32768);
+        load_token_tile(smem, &map_v, p.v_mode, bh, p.H, p.TP, j, 0, 128, &bar_v);
+        v_issued = true;
+        mbar_expect_tx(&bar_tab[0], 16384);
+        tma_load_2d(smem + 32768, &map_tab, &bar_tab[0], 0, (bh % p.H) * 128);
+        tab_issued[0] = true;
+      } else {
+        mbar_expect_tx(&bar_tab[1], 16384);
+        tma_load_2d(smem + kRoStage + 32768, &map_tab, &bar_tab[1], 64, (bh % p.H) * 128);
+        tab_issued[1] = true;
+      }
+    }
+    umma_commit(&bar_m[0]);  // after the last k-block (or arrives at once on a failed wait)
+  }
+  const float gt = Gs[r];
+  const float lam = p.lam[size_t(bh) * p.TP + t];
+  __syncwarp();
+  // ---- P = mask(S_qk o 2^{G_t - G_s}) -> bf16 K-major into stage 1
+  if (!mbar_wait(&bar_m[0], 0)) ok = false;
+  tc_fence_after();
+  const uint32_t sP = st1;
+  if (ok) {
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      const int col0 = half * 64 + 32 * c;
+      float v[32];
+      tmem_ld32(lane_tmem + col0, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int s_ = col0 + i;
+        v[i] = s_ <= r ? v[i] * exp2f(gt - Gs[s_]) : 0.f;
+      }
+      store_row32_bf16(sP + half * 16384, r, c * 4, v);
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  tc_fence_after();
+  if (tid == 0) {
+    ok = ok && mbar_wait(&bar_v, 0);
+    if (ok) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem, kmaj_desc(sP, 128, ks), mnmaj_desc(st0, 128, ks),
+                  make_idesc(128, 128, 0, 1), ks > 0);
+      umma_commit(&bar_m[1]);
+    } else {
+      mbar_arrive(&bar_m[1]);
+    }
+  }
+  __syncwarp();
+  // ---- raw = scale (2^{G_t} O_inter + O_intra);  z = U(lam) bf16(raw) into stage 0
+  if (!mbar_wait(&bar_m[1], 0)) ok = false;
+  tc_fence_after();
+  const float eg = exp2f(gt);
+  const uint32_t scratch = st1 + warp * 2048;  // P is dead once P V is done
+  const uint32_t sZ = st0;                     // V is dead once P V is done
+  const int t0 = j * 128 + quad * 32;
+  if (__all_sync(0xffffffffu, ok)) {
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      const int col0 = half * 64 + 32 * c;
+      float a[32], b[32];
+      tmem_ld32x2(lane_tmem + 128 + col0, a, lane_tmem + col0, b);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) a[i] = p.scale * (eg * a[i] + b[i]);
+      warp_store_block_bf16(scratch, a, p.out + (size_t(bh) * p.TP + t0) * 128 + col0, 128,
+                            0xffffffffu);
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const float e = bf16_round(a[i]), o = bf16_round(a[i + 1]);
+        float sn, cs;
+        __sincosf(clock_phase(lam, col0 / 2 + i / 2), &sn, &cs);
+        a[i] = cs * e - sn * o;
+        a[i + 1] = sn * e + cs * o;
+      }
+      store_row32_bf16(sZ + half * 16384, r, c * 4, a);
+    }
+  }
+  fence_async_smem();
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  tc_fence_after();
+  if (tid == 0) {
+    ok = ok && mbar_wait(&bar_tab[0], 0) && mbar_wait(&bar_tab[1], 0);
+    if (ok) {
+      tc_fence_after();
+      // logits = z Tab^T: the table's two 64-column panels are a stage apart
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem, kmaj_desc(sZ, 128, ks),
+                  make_sdesc((ks < 4 ? tab0 : tab1) + (ks & 3) * 32, 16, 1024),
+                  make_idesc(128, 128, 0, 0), ks > 0);
+      umma_commit(&bar_m[2]);
+    } else {
+      mbar_arrive(&bar_m[2]);
+    }
+  }
+  __syncwarp();
+  if (!mbar_wait(&bar_m[2], 0)) ok = false;
+  tc_fence_after();
+  // ---- softmax over the 127 active slots; each thread holds half of its token's row
+  float l[64];
+  tmem_ld32(lane_tmem + half * 64, *reinterpret_cast<float(*)[32]>(l));
+  tmem_ld32(lane_tmem + half * 64 + 32, *reinterpret_cast<float(*)[32]>(l + 32));
+  float mx = -1e30f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i)
+    if (half * 64 + i < 127) mx = fmaxf(mx, l[i]);
+  xch[half][r] = mx;
+  __syncthreads();
+  mx = fmaxf(xch[0][r], xch[1][r]);
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    l[i] = (half * 64 + i < 127) ? __expf(l[i] - mx) : 0.f;
+    sum += l[i];
+  }
+  __syncthreads();
+  xch[half][r] = sum;
+  __syncthreads();
+  const float inv = 1.f / (xch[0][r] + xch[1][r]);
+#pragma unroll
+  for (int i = 0; i < 64; ++i) l[i] *= inv;
+  const uint32_t sPr = st1;  // the staging of the raw stores is done
+  if (ok) store_row64_bf16(sPr + half * 16384, r, l);
+  fence_async_smem();
+  tc_fence_before();
+  ok = __syncthreads_and(ok);
+  tc_fence_after();
+  if (tid == 0) {
+    if (ok) {
+      // p Tab: the table as an MN-major operand, 64-column blocks a stage apart
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_bf16(tmem + 128, kmaj_desc(sPr, 128, ks), make_sdesc(tab0 + ks * 2048, kRoStage, 1024),
+                  make_idesc(128, 128, 0, 1), ks > 0);
+      umma_commit(&bar_m[3]);
+    } else {
+      mbar_arrive(&bar_m[3]);
+    }
+  }
+  __syncwarp();
+  if (!mbar_wait(&bar_m[3], 0)) ok = false;
+  tc_fence_after();
+  // ---- weights = U(-lam) (p Tab)
+  if (__all_sync(0xffffffffu, ok)) {
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      const int col0 = half * 64 + 32 * c;
+      float v[32];
+      tmem_ld32(lane_tmem + 128 + col0, v);
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        float sn, cs;
+        __sincosf(clock_phase(lam, col0 / 2 + i / 2), &sn, &cs);
+        const float e = v[i], o = v[i + 1];
+        v[i] = cs * e + sn * o;
+        v[i + 1] = -sn * e + cs * o;
+      }
+      // staging: p (stage 1) is dead once p Tab is done
+      warp_store_block_bf16(scratch, v, p.weights + (size_t(bh) * p.TP + t0) * 128 + col0, 128,
+                            0xffffffffu);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && !ok) {
+    // after a failed wait, copies may be in flight: let them land before exit
+    for (int kb = consumed; kb < issued; ++kb) mbar_wait(&full[kb & 1], (kb >> 1) & 1);
+    if (v_issued) mbar_wait(&bar_v, 0);
+    for (int i = 0; i < 2; ++i)
+      if (tab_issued[i]) mbar_wait(&bar_tab[i], 0);
+  }
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 }  // namespace cyfa
