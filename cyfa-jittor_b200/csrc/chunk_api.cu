@@ -226,10 +226,10 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
     if ((rc = launch_status())) return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, d.V, kPublic4D, 1, s.G, s.lam, 1.f,
                     static_cast<__nv_bfloat16*>(a->o), nullptr};
-    set_smem(tile_fwd_kernel<128, false>, tile_fwd_smem<128, false>());
+    set_smem(tile_fwd_kernel, kTileFwdSmem);
     CYFA_LAUNCH("tile_fwd", st,
-                (launch_k(tile_fwd_kernel<128, false>, dim3(d.BH * d.NT, d.V / 128), 256,
-                          tile_fwd_smem<128, false>(), st, m_weights, m_w, m_v, m_s2, m_tab, t)));
+                (launch_k(tile_fwd_kernel, dim3(d.BH * d.NT, d.V / 128), 256, kTileFwdSmem, st,
+                          m_weights, m_w, m_v, m_s2, t)));
     if ((rc = launch_status())) return rc;
   }
   return kOk;

@@ -16,12 +16,13 @@
 //   REVERSE runs the same recurrence backwards for the state adjoint
 //   H_j = 2^{G_L} H_{j+1} + Q_j^T (dO_j o scale 2^{G_t}) and also emits the
 //   per-tile gate boundary term <S_{j+1}, H_{j+1}>.
-// tile_fwd_kernel: one CTA per (bh, tile, 128-column V slice); all GEMMs of the
-//   tile on tcgen05 (Q K^T, Q S_j, P V), accumulators in TMEM, operands staged by
-//   TMA.  With READOUT (pass 1) the epilogue applies the softmax slot readout
-//   (ops/chunk.py:320-331): z = U(lam) raw, logits = z Table^T, p = softmax over
-//   the 127 active slots, coeff = p Table, weights = U(-lam) coeff, with both
-//   table products on tcgen05 and the rotations in registers.
+// tile_fwd_kernel (pass 2) / tile_fwd_ro_kernel (pass 1): one CTA per (bh, tile,
+//   128-column V slice); all GEMMs of the tile on tcgen05 (Q K^T, Q S_j, P V),
+//   accumulators in TMEM, operands staged by TMA.  Pass 1's epilogue applies the
+//   softmax slot readout (ops/chunk.py:320-331): z = U(lam) raw, logits =
+//   z Table^T, p = softmax over the 127 active slots, coeff = p Table, weights =
+//   U(-lam) coeff, with both table products on tcgen05 and the rotations in
+//   registers.
 #include "cyfa_common.cuh"
 #include "phase.cuh"
 
@@ -396,57 +397,38 @@ struct TileFwdParams {
   __nv_bfloat16* weights;  // READOUT: [BH, TP, 128]
 };
 
-// The output pass without the readout at DK = 128 runs lean, two CTAs per SM:
-// V is loaded into the S region once Q S_j is done, the output staging uses the
-// Q region, and P V accumulates into the Q K^T columns of TMEM (256 columns).
-template <int DK, bool READOUT>
-constexpr bool tile_fwd_lean() {
-  return DK == 128 && !READOUT;
-}
-
-template <int DK, bool READOUT = true>
-constexpr int tile_fwd_smem() {
-  // Q | K | S | V, plus (DK = 128) a 16 KiB staging area for the output stores;
-  // with DK = 256 the staging uses the S region, free once the MMAs are done
-  return tile_fwd_lean<DK, READOUT>() ? 3 * DK * 256 + 1024
-                                      : 3 * DK * 256 + 32768 + 1024 + (DK == 256 ? 0 : 16384);
-}
+// Pass 2's output tile (queries = the readout weights, DK = 128), two CTAs per
+// SM: V is loaded into the S region once Q S_j is done, the output staging uses
+// the Q region, and P V accumulates into the Q K^T columns of TMEM (256 columns).
+constexpr int kTileFwdSmem = 3 * 128 * 256 + 1024;
 
 // 8 warps: warp w owns TMEM lane quadrant (w & 3) (token rows 32(w&3)..+31) and
-// column half (w >> 2) of every 128-column accumulator; row-wide softmax
-// statistics are joined through shared memory.
-template <int DK, bool READOUT>
+// column half (w >> 2) of every 128-column accumulator.
 __global__ void __launch_bounds__(256, 1)
     tile_fwd_kernel(const __grid_constant__ CUtensorMap map_q,
                     const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v,
-                    const __grid_constant__ CUtensorMap map_s,
-                    const __grid_constant__ CUtensorMap map_tab, TileFwdParams p) {
+                    const __grid_constant__ CUtensorMap map_s, TileFwdParams p) {
+  constexpr int DK = 128;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  constexpr int kQ = 0, kK = DK * 256, kS = 2 * DK * 256, kV = 3 * DK * 256;
-  __shared__ __align__(8) uint64_t bar_in, bar_v, bar_tab, bar_m[5];
+  constexpr int kQ = 0, kK = DK * 256, kS = 2 * DK * 256;
+  __shared__ __align__(8) uint64_t bar_in, bar_v, bar_m[3];
   __shared__ uint32_t tmem_base;
   __shared__ float Gs[128];
-  __shared__ float xch[2][128];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int quad = warp & 3, half = warp >> 2;
   const int r = quad * 32 + lane;
   const int bh = blockIdx.x / p.NT, j = blockIdx.x % p.NT, dv0 = blockIdx.y * 128;
-  const int t = j * 128 + r;
-  constexpr bool kLean = tile_fwd_lean<DK, READOUT>();
-  constexpr uint32_t kTmemCols = kLean ? 256 : 512;
-  constexpr uint32_t kPV = kLean ? 0 : 256;  // TMEM column of the P V accumulator
 
   if (tid == 0) {
     mbar_init(&bar_in, 1);
     mbar_init(&bar_v, 1);
-    mbar_init(&bar_tab, 1);
-    for (int i = 0; i < 5; ++i) mbar_init(&bar_m[i], 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&bar_m[i], 1);
     mbar_fence_init();
   }
   if (warp == 0) {
-    tmem_alloc(&tmem_base, kTmemCols);
+    tmem_alloc(&tmem_base, 256);
     tmem_relinquish();  // one allocation per CTA: let co-resident CTAs allocate
   }
   pdl_wait();
@@ -457,8 +439,7 @@ __global__ void __launch_bounds__(256, 1)
   pdl_trigger();
   const uint32_t tmem = tmem_base;
   const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
-  const uint32_t sQ = smem_u32(smem + kQ), sK = smem_u32(smem + kK), sS = smem_u32(smem + kS),
-                 sV = smem_u32(smem + kV);
+  const uint32_t sQ = smem_u32(smem + kQ), sK = smem_u32(smem + kK), sS = smem_u32(smem + kS);
   bool ok = true;
 
   if (tid == 0) {
@@ -466,10 +447,6 @@ __global__ void __launch_bounds__(256, 1)
     load_token_tile(smem + kQ, &map_q, kRows2D, bh, p.H, p.TP, j, 0, DK, &bar_in);
     load_token_tile(smem + kK, &map_k, kRows2D, bh, p.H, p.TP, j, 0, DK, &bar_in);
     load_hist_tile(smem + kS, &map_s, (bh * p.NT + j) * DK, dv0, 128, DK, &bar_in);
-    if (!kLean) {
-      mbar_expect_tx(&bar_v, 32768);
-      load_token_tile(smem + kV, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 128, &bar_v);
-    }
     if (mbar_wait(&bar_in, 0)) {
       tc_fence_after();
       // S_qk = Q K^T -> TMEM[0,128); O_inter = Q S_j -> TMEM[128,256)
@@ -483,24 +460,20 @@ __global__ void __launch_bounds__(256, 1)
         umma_bf16(tmem + 128, kmaj_desc(sQ, 128, ks), mnmaj_desc(sS, DK, ks),
                   make_idesc(128, 128, 0, 1), ks > 0);
       umma_commit(&bar_m[1]);
-      if (kLean) {
-        // V into the S region once Q S_j has read it
-        if (mbar_wait(&bar_m[1], 0)) {
-          mbar_expect_tx(&bar_v, 32768);
-          load_token_tile(smem + kS, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 128, &bar_v);
-        } else {
-          mbar_arrive(&bar_v);
-        }
+      // V into the S region once Q S_j has read it
+      if (mbar_wait(&bar_m[1], 0)) {
+        mbar_expect_tx(&bar_v, 32768);
+        load_token_tile(smem + kS, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 128, &bar_v);
+      } else {
+        mbar_arrive(&bar_v);
       }
     } else {
       mbar_arrive(&bar_m[0]);
       mbar_arrive(&bar_m[1]);
-      if (kLean) mbar_arrive(&bar_v);
+      mbar_arrive(&bar_v);
     }
   }
   const float gt = Gs[r];
-  float lam = 0.f;
-  if (READOUT) lam = p.lam[size_t(bh) * p.TP + t];
   __syncwarp();
   // ---- P = mask(S_qk o 2^{G_t - G_s}) -> bf16, K-major A operand in the K region
   if (!mbar_wait(&bar_m[0], 0)) ok = false;
@@ -524,26 +497,16 @@ __global__ void __launch_bounds__(256, 1)
   ok = __syncthreads_and(ok);
   tc_fence_after();
   if (tid == 0) {
-    bool vok = ok && mbar_wait(&bar_v, 0);
+    const bool vok = ok && mbar_wait(&bar_v, 0);
     tc_fence_after();
     if (vok) {
-      const uint32_t sVv = kLean ? sS : sV;
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks)
-        umma_bf16(tmem + kPV, kmaj_desc(sK, 128, ks), mnmaj_desc(sVv, 128, ks),
+        umma_bf16(tmem, kmaj_desc(sK, 128, ks), mnmaj_desc(sS, 128, ks),
                   make_idesc(128, 128, 0, 1), ks > 0);
       umma_commit(&bar_m[2]);
     } else {
       mbar_arrive(&bar_m[2]);
-    }
-    if (READOUT) {
-      // table rows of head h -> Q region once Q is no longer read
-      if (ok && mbar_wait(&bar_m[1], 0)) {
-        mbar_expect_tx(&bar_tab, 32768);
-        load_hist_tile(smem + kQ, &map_tab, (bh % p.H) * 128, 0, 128, 128, &bar_tab);
-      } else {
-        mbar_arrive(&bar_tab);
-      }
     }
   }
   __syncwarp();
@@ -552,16 +515,15 @@ __global__ void __launch_bounds__(256, 1)
   tc_fence_after();
   const float eg = exp2f(gt);
   // per-warp staging for coalesced output stores (8 rows x 64 bytes per
-  // instruction): the S region, free once the MMAs above are done, when DK = 256
-  // (with DK = 128 the READOUT z tile lives there, so a separate area is used)
-  const uint32_t scratch = (kLean ? sQ : (DK == 256 ? sS : sV + 32768)) + warp * 2048;
+  // instruction): the Q region, free once the MMAs above are done
+  const uint32_t scratch = sQ + warp * 2048;
   const int t0 = j * 128 + quad * 32;  // first token row of this warp
   if (__all_sync(0xffffffffu, ok)) {
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
       const int col0 = half * 64 + 32 * c;
       float a[32], b[32];
-      tmem_ld32x2(lane_tmem + 128 + col0, a, lane_tmem + kPV + col0, b);
+      tmem_ld32x2(lane_tmem + 128 + col0, a, lane_tmem + col0, b);
 #pragma unroll
       for (int i = 0; i < 32; ++i) a[i] = p.scale * (eg * a[i] + b[i]);
       if (p.o_mode == 1) {
@@ -575,114 +537,20 @@ __global__ void __launch_bounds__(256, 1)
         warp_store_block_bf16(scratch, a, p.out + (size_t(bh) * p.TP + t0) * 128 + col0, 128,
                               0xffffffffu);
       }
-      if (READOUT) {
-        // z = U(lam) raw, from the bf16-rounded raw that is saved for the backward pass
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float e = bf16_round(a[i]), o = bf16_round(a[i + 1]);
-          float sn, cs;
-          __sincosf(clock_phase(lam, col0 / 2 + i / 2), &sn, &cs);
-          a[i] = cs * e - sn * o;
-          a[i + 1] = sn * e + cs * o;
-        }
-        store_row32_bf16(sK + 32768 + half * 16384, r, c * 4, a);
-      }
-    }
-  }
-  if (READOUT) {
-    const uint32_t sZ = sK + 32768, sTab = sQ, sP = sV;
-    fence_async_smem();
-    tc_fence_before();
-    ok = __syncthreads_and(ok);
-    tc_fence_after();
-    if (tid == 0) {
-      if (ok && mbar_wait(&bar_tab, 0)) {
-        tc_fence_after();
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma_bf16(tmem, kmaj_desc(sZ, 128, ks), kmaj_desc(sTab, 128, ks),
-                    make_idesc(128, 128, 0, 0), ks > 0);
-        umma_commit(&bar_m[3]);
-      } else {
-        mbar_arrive(&bar_m[3]);
-      }
-    }
-    __syncwarp();
-    if (!mbar_wait(&bar_m[3], 0)) ok = false;
-    tc_fence_after();
-    // softmax over the 127 active slots; each thread holds half of its token's row
-    float l[64];
-    tmem_ld32(lane_tmem + half * 64, *reinterpret_cast<float(*)[32]>(l));
-    tmem_ld32(lane_tmem + half * 64 + 32, *reinterpret_cast<float(*)[32]>(l + 32));
-    float mx = -1e30f;
-#pragma unroll
-    for (int i = 0; i < 64; ++i)
-      if (half * 64 + i < 127) mx = fmaxf(mx, l[i]);
-    xch[half][r] = mx;
-    __syncthreads();
-    mx = fmaxf(xch[0][r], xch[1][r]);
-    float sum = 0.f;
-#pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      l[i] = (half * 64 + i < 127) ? __expf(l[i] - mx) : 0.f;
-      sum += l[i];
-    }
-    __syncthreads();
-    xch[half][r] = sum;
-    __syncthreads();
-    const float inv = 1.f / (xch[0][r] + xch[1][r]);
-#pragma unroll
-    for (int i = 0; i < 64; ++i) l[i] *= inv;
-    if (ok) store_row64_bf16(sP + half * 16384, r, l);
-    fence_async_smem();
-    tc_fence_before();
-    ok = __syncthreads_and(ok);
-    tc_fence_after();
-    if (tid == 0) {
-      if (ok) {
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks)
-          umma_bf16(tmem + 128, kmaj_desc(sP, 128, ks), mnmaj_desc(sTab, 128, ks),
-                    make_idesc(128, 128, 0, 1), ks > 0);
-        umma_commit(&bar_m[4]);
-      } else {
-        mbar_arrive(&bar_m[4]);
-      }
-    }
-    __syncwarp();
-    if (!mbar_wait(&bar_m[4], 0)) ok = false;
-    tc_fence_after();
-    if (__all_sync(0xffffffffu, ok)) {
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        const int col0 = half * 64 + 32 * c;
-        float v[32];
-        tmem_ld32(lane_tmem + 128 + col0, v);
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float sn, cs;
-          __sincosf(clock_phase(lam, col0 / 2 + i / 2), &sn, &cs);
-          const float e = v[i], o = v[i + 1];
-          v[i] = cs * e + sn * o;
-          v[i + 1] = -sn * e + cs * o;
-        }
-        warp_store_block_bf16(scratch, v, p.weights + (size_t(bh) * p.TP + t0) * 128 + col0, 128,
-                              0xffffffffu);
-      }
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, 256);
   }
 }
 
 // ============================================================ tile output with readout, 2 CTAs/SM
-// Pass 1's output tile and the slot readout (the READOUT path of tile_fwd_kernel)
-// in half its shared memory, so that two CTAs share an SM and one CTA's loads
-// and MMAs run during the other's epilogues.  Q, K and the state S_j stream
+// Pass 1's output tile and the slot readout in about 97 KiB of shared memory,
+// so that two CTAs share an SM and one CTA's loads and MMAs run during the
+// other's epilogues.  Q, K and the state S_j stream
 // through two 48 KiB stages in 64-wide k-blocks (Q | K | S rows of the block);
 // the stages are then reused:
 //   stage 0: V (32 KiB) once k-block NKB-2 is done, then z; table panel 0 at +32 KiB
