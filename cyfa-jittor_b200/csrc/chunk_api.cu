@@ -323,9 +323,10 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   if ((rc = tmap_2d(&m_A64, w.A, trows, 128, 64))) return rc;
   if ((rc = tmap_2d(&m_Bp64, w.Bp, trows, 128, 64))) return rc;
   const dim3 tiles(d.BH * d.NT);
-  const dim3 persist(d.BH * d.NT < 148 ? d.BH * d.NT : 148);  // one CTA per SM
   set_smem(state_scan_kernel<true>, kScanSmem);
   set_smem(dual_gemm_kernel, kDualSmem);
+  set_smem(tile_scores_kernel, kScoresSmem);
+  const unsigned scores_grid = 2 * d.BH * d.NT < 148 ? 2 * d.BH * d.NT : 148;  // persistent
   // The three GEMM pairs of a pass in one persistent launch, their 128-column
   // units interleaved tile by tile.
   auto dual = [&](const DualMaps& m, DualParams& p, int njobs) {
@@ -357,18 +358,10 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                 (launch_k(state_scan_kernel<true>, dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st, 
                     m_weights, m_do, m_s2, m_ff2, p)));
     if ((rc = launch_status())) return rc;
-    ScoresParams sp{d.BH, d.H, d.TP, d.NT, kPublic4D, kPublic4D, s.G, 1.f, w.A, w.Bp};
-    if (d.V == 256) {
-      set_smem(tile_scores_kernel<128, 256>, scores_smem<128, 256>());
-      CYFA_LAUNCH("tile_scores", st,
-                  (launch_k(tile_scores_kernel<128, 256>, persist, 256, scores_smem<128, 256>(), st, 
-                      m_weights, m_w, m_do, m_v, sp)));
-    } else {
-      set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
-      CYFA_LAUNCH("tile_scores", st,
-                  (launch_k(tile_scores_kernel<128, 128>, persist, 256, scores_smem<128, 128>(), st, 
-                      m_weights, m_w, m_do, m_v, sp)));
-    }
+    ScoresParams sp{d.BH, d.H, d.TP, d.NT, 128, d.V, kPublic4D, kPublic4D, s.G, 1.f, w.A, w.Bp};
+    CYFA_LAUNCH("tile_scores", st,
+                (launch_k(tile_scores_kernel, scores_grid, kScoresThreads, kScoresSmem, st,
+                          m_weights, m_w, m_do, m_v, sp)));
     if ((rc = launch_status())) return rc;
     DualMaps m;
     DualParams dp{d.BH, d.H, d.TP, d.NT, d.T, s.G};
@@ -416,18 +409,11 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                 (launch_k(state_scan_kernel<true>, dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st, 
                     m_qn, m_draw, m_f1, m_ff1, p)));
     if ((rc = launch_status())) return rc;
-    ScoresParams sp{d.BH, d.H, d.TP, d.NT, kRows2D, kRows2D, s.G, a->scale, w.A, w.Bp};
-    if (d.K == 256) {
-      set_smem(tile_scores_kernel<256, 128>, scores_smem<256, 128>());
-      CYFA_LAUNCH("tile_scores", st,
-                  (launch_k(tile_scores_kernel<256, 128>, persist, 256, scores_smem<256, 128>(), st, 
-                      m_qn, m_kn, m_draw, m_w, sp)));
-    } else {
-      set_smem(tile_scores_kernel<128, 128>, scores_smem<128, 128>());
-      CYFA_LAUNCH("tile_scores", st,
-                  (launch_k(tile_scores_kernel<128, 128>, persist, 256, scores_smem<128, 128>(), st, 
-                      m_qn, m_kn, m_draw, m_w, sp)));
-    }
+    ScoresParams sp{d.BH, d.H, d.TP, d.NT, d.K, 128, kRows2D, kRows2D, s.G, a->scale, w.A,
+                    w.Bp};
+    CYFA_LAUNCH("tile_scores", st,
+                (launch_k(tile_scores_kernel, scores_grid, kScoresThreads, kScoresSmem, st, m_qn,
+                          m_kn, m_draw, m_w, sp)));
     if ((rc = launch_status())) return rc;
     DualMaps m;
     DualParams dp{d.BH, d.H, d.TP, d.NT, d.T, s.G};

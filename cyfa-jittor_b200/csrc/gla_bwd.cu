@@ -30,6 +30,7 @@ namespace cyfa {
 // ============================================================ tile scores
 struct ScoresParams {
   int BH, H, TP, NT;
+  int DK, DV;
   int do_mode, v_mode;
   const float* G;
   float scale;
@@ -37,49 +38,48 @@ struct ScoresParams {
   __nv_bfloat16* Bp;  // [BH*NT*128, 128]
 };
 
-template <int DK, int DV>
-constexpr int scores_smem() {
-  return 2 * DK * 256 + 2 * DV * 256 + 1024 + 8 * 2048;  // operands + per-warp staging
-}
+constexpr int kScoresStage = 32768;  // one 64-wide k-block of both operands
+constexpr int kScoresStages = 6;
+constexpr int kScoresBufs = 4;       // TMEM accumulators of 128 columns
+constexpr int kScoresSmem = kScoresStages * kScoresStage + 8 * 2048 + 1024;
+constexpr int kScoresThreads = 320;
 
-// Persistent: CTA c handles tiles c, c + gridDim.x, ...; the next tile's
-// operands are loaded as soon as the current tile's MMAs have read shared
-// memory, so they stream in during the masked epilogue.
-template <int DK, int DV>
-__device__ __forceinline__ void scores_issue_loads(uint8_t* smem, const CUtensorMap* mq,
-                                                   const CUtensorMap* mk, const CUtensorMap* mdo,
-                                                   const CUtensorMap* mv, const ScoresParams& p,
-                                                   int tile, uint64_t* bar) {
-  constexpr int kK = DK * 256, kD = 2 * DK * 256, kV = 2 * DK * 256 + DV * 256;
-  const int bh = tile / p.NT, j = tile % p.NT;
-  mbar_expect_tx(bar, 2 * DK * 256 + 2 * DV * 256);
-  load_token_tile(smem, mq, kRows2D, bh, p.H, p.TP, j, 0, DK, bar);
-  load_token_tile(smem + kK, mk, kRows2D, bh, p.H, p.TP, j, 0, DK, bar);
-  load_token_tile(smem + kD, mdo, p.do_mode, bh, p.H, p.TP, j, 0, DV, bar);
-  load_token_tile(smem + kV, mv, p.v_mode, bh, p.H, p.TP, j, 0, DV, bar);
-}
-
-template <int DK, int DV>
-__global__ void __launch_bounds__(256, 1)
+// Persistent and warp-specialised like dual_gemm_kernel.  A unit is one score
+// matrix of one tile: units 0..ntiles-1 are A (q.k over DK), the next ntiles B'
+// (dO.v over DV), so every CTA gets a share of both kinds.  The unit's GEMM
+// streams 64-wide k-blocks (the q and k blocks, or the dO and v blocks, 32 KiB)
+// through a ring of stages:
+//   warp 8, lane 0: TMA loads;  warp 9, lane 0: the UMMAs into one of four TMEM
+//   accumulators;  warps 0-7: the masked, decayed epilogue (warp w: TMEM lane
+//   quadrant w & 3 = token rows, column half w >> 2) and the bf16 stores.
+__global__ void __launch_bounds__(kScoresThreads, 1)
     tile_scores_kernel(const __grid_constant__ CUtensorMap map_q,
                        const __grid_constant__ CUtensorMap map_k,
                        const __grid_constant__ CUtensorMap map_do,
                        const __grid_constant__ CUtensorMap map_v, ScoresParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  constexpr int kQ = 0, kK = DK * 256, kD = 2 * DK * 256, kV = 2 * DK * 256 + DV * 256;
-  __shared__ __align__(8) uint64_t bar_in, bar_mma;
+  __shared__ __align__(8) uint64_t full[kScoresStages], empty[kScoresStages];
+  __shared__ __align__(8) uint64_t acc_full[kScoresBufs], acc_empty[kScoresBufs];
   __shared__ uint32_t tmem_base;
-  __shared__ float Gs[128];
+  __shared__ int s_abort;
+  volatile int* abort_flag = &s_abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int ntiles = p.BH * p.NT;
+  const int ntiles = p.BH * p.NT, nunits = 2 * ntiles;
   if (tid == 0) {
-    mbar_init(&bar_in, 1);
-    mbar_init(&bar_mma, 1);
+    for (int i = 0; i < kScoresStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < kScoresBufs; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);
+    }
+    s_abort = 0;
     mbar_fence_init();
   }
   if (warp == 0) {
-    tmem_alloc(&tmem_base, 256);
+    tmem_alloc(&tmem_base, 128 * kScoresBufs);
     tmem_relinquish();  // one allocation per CTA: let co-resident CTAs allocate
   }
   tc_fence_before();
@@ -88,99 +88,132 @@ __global__ void __launch_bounds__(256, 1)
   pdl_wait();
   pdl_trigger();
   const uint32_t tmem = tmem_base;
-  // warp w: TMEM lane quadrant (w & 3) = token rows, column half (w >> 2); it
-  // writes both A (q.k) and B' (dO.v) there, sharing each decay factor
-  const int quad = warp & 3, half = warp >> 2, r = quad * 32 + lane;
-  const uint32_t scratch = smem_u32(smem + 2 * DK * 256 + 2 * DV * 256) + warp * 2048;
-  const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
-  const uint32_t sQ = smem_u32(smem + kQ), sK = smem_u32(smem + kK), sD = smem_u32(smem + kD),
-                 sV = smem_u32(smem + kV);
-  bool ok = true;
-  bool in_pending = false, mma_pending = false;  // elected-thread state, drained before exit
-  uint32_t in_ph = 0;
-  if (tid == 0 && blockIdx.x < ntiles) {
-    scores_issue_loads<DK, DV>(smem, &map_q, &map_k, &map_do, &map_v, p, blockIdx.x, &bar_in);
-    in_pending = true;
-  }
-  uint32_t phase = 0;
-  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, phase ^= 1) {
-    const int bh = tile / p.NT, j = tile % p.NT;
-    if (tid < 128) Gs[tid] = p.G[size_t(bh) * p.TP + j * 128 + tid];
-    if (tid == 0) {
-      bool got = ok && mbar_wait(&bar_in, phase);
-      if (got) in_pending = false;
-      tc_fence_after();
-      if (got) {
-#pragma unroll 4
-        for (int ks = 0; ks < DK / 16; ++ks)
-          umma_bf16(tmem, kmaj_desc(sQ, 128, ks), kmaj_desc(sK, 128, ks),
-                    make_idesc(128, 128, 0, 0), ks > 0);
-#pragma unroll 4
-        for (int ks = 0; ks < DV / 16; ++ks)
-          umma_bf16(tmem + 128, kmaj_desc(sD, 128, ks), kmaj_desc(sV, 128, ks),
-                    make_idesc(128, 128, 0, 0), ks > 0);
-        umma_commit(&bar_mma);
-        mma_pending = true;
-        const int next = tile + gridDim.x;
-        if (next < ntiles) {
-          if (mbar_wait(&bar_mma, phase)) {
-            mma_pending = false;
-            scores_issue_loads<DK, DV>(smem, &map_q, &map_k, &map_do, &map_v, p, next, &bar_in);
-            in_pending = true;
-            in_ph = phase ^ 1;
+
+  if (warp == 8) {
+    // ------------------------------------------------ producer
+    if (lane == 0) {
+      int it = 0;
+      for (int u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x) {
+        const bool bp = u >= ntiles;
+        const int tile = bp ? u - ntiles : u, bh = tile / p.NT, j = tile % p.NT;
+        const int nkb = (bp ? p.DV : p.DK) / 64;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kScoresStages;
+          if (it >= kScoresStages &&
+              !mbar_wait(&empty[s], ((it / kScoresStages) - 1) & 1)) {
+            *abort_flag = 1;
+            break;
+          }
+          uint8_t* xb = smem + s * kScoresStage;
+          mbar_expect_tx(&full[s], kScoresStage);
+          if (bp) {
+            load_token_tile(xb, &map_do, p.do_mode, bh, p.H, p.TP, j, 64 * kb, 64, &full[s]);
+            load_token_tile(xb + 16384, &map_v, p.v_mode, bh, p.H, p.TP, j, 64 * kb, 64, &full[s]);
           } else {
-            got = false;
+            load_token_tile(xb, &map_q, kRows2D, bh, p.H, p.TP, j, 64 * kb, 64, &full[s]);
+            load_token_tile(xb + 16384, &map_k, kRows2D, bh, p.H, p.TP, j, 64 * kb, 64, &full[s]);
           }
         }
-      } else {
-        mbar_arrive(&bar_mma);  // releases the epilogue's wait; its result is discarded
       }
-      if (!got) ok = false;
+      // every issued copy lands before shared memory goes away
+      for (int i = it > kScoresStages ? it - kScoresStages : 0; i < it; ++i)
+        mbar_wait(&full[i % kScoresStages], (i / kScoresStages) & 1);
     }
-    __syncwarp();
-    bool mm = mbar_wait(&bar_mma, phase);
-    if (tid == 0 && mm) mma_pending = false;
-    tc_fence_after();
-    mm = __syncthreads_and(mm && ok) != 0;  // also publishes Gs
-    if (mm) {
-      const float gt = Gs[r];
-      const size_t row0 = (size_t(bh) * p.NT + j) * 128 + quad * 32;  // warp's first row
+  } else if (warp == 9) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc(128, 128, 0, 0);
+      int it = 0, tl = 0;
+      uint64_t* last_bar = nullptr;
+      uint32_t last_par = 0;
+      for (int u = blockIdx.x; u < nunits && !*abort_flag; u += gridDim.x, ++tl) {
+        const int nkb = (u >= ntiles ? p.DV : p.DK) / 64, b = tl % kScoresBufs;
+        if (tl >= kScoresBufs && !mbar_wait(&acc_empty[b], ((tl / kScoresBufs) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % kScoresStages;
+          if (!mbar_wait(&full[s], (it / kScoresStages) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t xb = smem_u32(smem + s * kScoresStage), yb = xb + 16384;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_bf16(tmem + 128 * b, kmaj_desc(xb, 128, ks), kmaj_desc(yb, 128, ks), idesc,
+                      kb > 0 || ks > 0);
+          umma_commit(&empty[s]);
+          last_bar = &empty[s];
+          last_par = (it / kScoresStages) & 1;
+        }
+        if (!ok) {
+          *abort_flag = 1;
+          break;
+        }
+        umma_commit(&acc_full[b]);
+        last_bar = &acc_full[b];
+        last_par = (tl / kScoresBufs) & 1;
+      }
+      if (last_bar) mbar_wait(last_bar, last_par);  // all issued MMAs are done
+    }
+  } else {
+    // ------------------------------------------------ epilogue
+    const int quad = warp & 3, half = warp >> 2;
+    const int r = quad * 32 + lane;  // tile row = TMEM lane
+    const uint32_t lane_tmem = tmem + ((quad * 32) << 16);
+    const uint32_t scratch = smem_u32(smem) + kScoresStages * kScoresStage + warp * 2048;
+    int tl = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++tl) {
+      const bool bp = u >= ntiles;
+      const int tile = bp ? u - ntiles : u, bh = tile / p.NT, j = tile % p.NT;
+      const int b = tl % kScoresBufs;
+      // the gate cumsum of this row and of this warp's 64 columns (one per lane
+      // and chunk, broadcast by shuffles), fetched before the MMAs are waited for
+      const float* Gt = p.G + size_t(bh) * p.TP + j * 128;
+      const float gt = Gt[r];
+      const float gc0 = Gt[64 * half + lane], gc1 = Gt[64 * half + 32 + lane];
+      const bool got = __all_sync(0xffffffffu, *abort_flag == 0 &&
+                                                   mbar_wait(&acc_full[b], (tl / kScoresBufs) & 1));
+      tc_fence_after();
+      if (!got) {
+        *abort_flag = 1;
+        break;
+      }
+      __nv_bfloat16* out = (bp ? p.Bp : p.A) + (size_t(tile) * 128 + quad * 32) * 128;
 #pragma unroll 1
-      for (int c = 2 * half; c < 2 * half + 2; ++c) {
-        float a[32], b[32];
+      for (int cc = 0; cc < 2; ++cc) {
+        const int c = 2 * half + cc;
+        float a[32];
         if (c <= quad) {  // chunks above the diagonal block are all masked
-          tmem_ld32(lane_tmem + 32 * c, a);
-          tmem_ld32(lane_tmem + 128 + 32 * c, b);
+          tmem_ld32(lane_tmem + 128 * b + 32 * c, a);
+          const float gc = cc ? gc1 : gc0;
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int s_ = 32 * c + i;
-            const float f = s_ <= r ? p.scale * fast_exp2(gt - Gs[s_]) : 0.f;
-            a[i] *= f;
-            b[i] *= f;
+            const float gs = __shfl_sync(0xffffffffu, gc, i);
+            a[i] *= s_ <= r ? p.scale * fast_exp2(gt - gs) : 0.f;
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) a[i] = b[i] = 0.f;
+          for (int i = 0; i < 32; ++i) a[i] = 0.f;
         }
-        warp_store_block_bf16(scratch, a, p.A + row0 * 128 + 32 * c, 128, 0xffffffffu);
-        warp_store_block_bf16(scratch, b, p.Bp + row0 * 128 + 32 * c, 128, 0xffffffffu);
+        warp_store_block_bf16(scratch, a, out + 32 * c, 128, 0xffffffffu);
       }
+      // hand the TMEM buffer back to the MMA issuer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
     }
-    // TMEM drained and Gs free before the next tile
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (!mm) break;
-  }
-  if (tid == 0) {
-    if (mma_pending) mbar_wait(&bar_mma, phase);
-    if (in_pending) mbar_wait(&bar_in, in_ph);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 128 * kScoresBufs);
   }
 }
 
