@@ -24,6 +24,7 @@ from ..ops.layer_ops import (
     LinearFunction,
     PackedGradSlot,
     _fork,
+    packed_rows,
 )
 
 
@@ -159,6 +160,31 @@ class CyclicFlowAttention(nn.Module):
             p.data = p.data.float() if keep else p.data.bfloat16()
         return self
 
+    def _front_weights(self):
+        return [self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, self.g_proj[0].weight,
+                self.a_proj.weight, self.b_proj.weight, self.d_proj.weight]
+
+    def _pack_front(self):
+        """Places the seven input-side projection weights as consecutive row blocks
+        of one buffer (padded to a multiple of 8 rows), re-pointing each
+        parameter's data at its block, so that the fused path multiplies by that
+        buffer instead of concatenating the weights every step.  Done once, and
+        again only if something (a device move, a cast, a load) replaced the
+        parameters' storage."""
+        ws = self._front_weights()
+        if packed_rows(ws) is not None or torch.cuda.is_current_stream_capturing():
+            return
+        if any(w.dtype != ws[0].dtype or w.device != ws[0].device for w in ws):
+            return
+        n = sum(w.shape[0] for w in ws)
+        buf = torch.empty((n + 7) // 8 * 8, ws[0].shape[1], device=ws[0].device, dtype=ws[0].dtype)
+        with torch.no_grad():
+            r = 0
+            for w in ws:
+                buf[r:r + w.shape[0]].copy_(w)
+                w.data = buf[r:r + w.shape[0]]
+                r += w.shape[0]
+
     def _fused_ok(self, x, cache, attention_mask):
         return (
             cache is None
@@ -183,6 +209,7 @@ class CyclicFlowAttention(nn.Module):
         B, T, _ = x.shape
         H, K, V = self.num_heads, self.head_k_dim, self.head_v_dim
         g0 = self.g_proj[0]
+        self._pack_front()
         slot = PackedGradSlot()
         # LayerFrontFunction's backward runs (and joins deferred side-stream work)
         # iff one of its differentiable inputs needs a gradient

@@ -364,6 +364,27 @@ class PackedGradSlot:
         return buf
 
 
+def packed_rows(ws):
+    """[rows, cols] view over the 2-D tensors `ws` when they are consecutive row
+    blocks of one buffer that extends to a multiple of 8 rows (the packed
+    projection), else None."""
+    w0 = ws[0]
+    if not all(w.dim() == 2 and w.is_contiguous() and w.dtype == w0.dtype
+               and w.shape[1] == w0.shape[1] for w in ws):
+        return None
+    end = w0.data_ptr()
+    for w in ws:
+        if w.data_ptr() != end:
+            return None
+        end += w.numel() * w.element_size()
+    n = sum(w.shape[0] for w in ws)
+    rows = (n + 7) // 8 * 8
+    avail = w0.untyped_storage().nbytes() - w0.storage_offset() * w0.element_size()
+    if avail < rows * w0.shape[1] * w0.element_size():
+        return None
+    return torch.as_strided(w0, (rows, w0.shape[1]), (w0.shape[1], 1))
+
+
 class LayerFrontFunction(torch.autograd.Function):
     """The layer's input side as one op: a single projection of x onto
     [W_q; W_k; W_v; W_g0; W_a; W_b; W_d] (one GEMM, one read of x), the short
@@ -393,14 +414,18 @@ class LayerFrontFunction(torch.autograd.Function):
         n_used = c_d + H
         NB = (n_used + 7) // 8 * 8  # 16-byte rows
         parts = [w_q, w_k, w_v, w_g0, w_a, w_b, w_d]
-        # the padding rows stay uninitialised: the columns they produce are never read
         # conv weights (one [n_qkv, Wc] block when the q, k, v pieces are adjacent)
         # and gate parameters as fp32, one launch on the aux stream beside the
         # projection (joined before the convolution)
         cwq, cwk, cwv, A, dt, bb, db = gather_f32(
             [cw_q, cw_k, cw_v, A_log, dt_bias, b_bias, d_bias], _fork(dev))
-        W_big = torch.empty(NB, hid, device=dev, dtype=w_q.dtype)
-        torch.cat(parts, out=W_big[:n_used])
+        # the packed projection: a view when the weights already are consecutive
+        # blocks of one buffer (the layer packs them once), else a concatenation;
+        # the padding rows stay uninitialised: the columns they produce are never read
+        W_big = packed_rows(parts)
+        if W_big is None:
+            W_big = torch.empty(NB, hid, device=dev, dtype=w_q.dtype)
+            torch.cat(parts, out=W_big[:n_used])
         big = torch.nn.functional.linear(x, W_big)  # [B, T, NB]
         Wc = cw_q.shape[-1]
         _join(dev)
