@@ -258,13 +258,15 @@ inline int conv_bwd_rows(int B, int T) {
 // context (x rows t0-3 .. t0+63, dy rows t0 .. t0+66; rows outside [0, T) read
 // as zeros), warps 0-7 compute 8 tokens each from shared memory (lane = 4
 // channels, sliding register window) and store their rows directly.  The CTAs
-// are persistent, so the loads of the next tiles overlap the current one.
+// are persistent, so the loads of the next tiles overlap the current one, and
+// two share an SM (rings of 69 KiB), so one's loads also overlap the other's
+// arithmetic.
 constexpr int kCtRows = 64;
 constexpr int kCtHalo = 3;                           // context rows (W <= 4)
 constexpr int kCtBoxRows = kCtRows + kCtHalo;        // 67
 constexpr int kCtTileBytes = kCtBoxRows * 128 * 2;   // 17152 (a multiple of 128)
-constexpr int kCtStages = 8;                         // forward: x tiles
-constexpr int kCtStagesB = 4;                        // backward: x and dy tiles
+constexpr int kCtStages = 4;                         // forward: x tiles
+constexpr int kCtStagesB = 2;                        // backward: x and dy tiles
 constexpr int kCtSmem = kCtStages * kCtTileBytes + 1024;
 constexpr int kCtSmemB = kCtStagesB * 2 * kCtTileBytes + 1024;
 static_assert(kCtSmem <= 227 * 1024 && kCtSmemB <= 227 * 1024, "conv ring");
@@ -387,7 +389,7 @@ __global__ void __launch_bounds__(288, 1)
 // its dw / dbias sums (registers, then a fixed-order block reduction) form one
 // partial row g.  dx[t] = sum_i w_i dy[t + (W-1) - i], dw_i = sum_t dy[t] x[t + i - (W-1)].
 template <int W>
-__global__ void __launch_bounds__(288, 1)
+__global__ void __launch_bounds__(288, 2)
     short_conv_bwd_tma_kernel(const __grid_constant__ CUtensorMap map_x,
                               const __grid_constant__ CUtensorMap map_dy, ConvTmaParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -775,9 +777,10 @@ __global__ void __launch_bounds__(256, 3) gated_norm_bwd_kernel(GatedNormParams 
 
 // TMA-streamed forward of the biased gated norm: the tile scheme of the backward
 // below (CTA = head x token-tile group, warp 8 loads x and gate tiles, warps 0-7
-// four tokens each), y and rstd stored directly.
+// four tokens each), y and rstd stored directly; a 3-stage ring (97 KiB), two
+// CTAs per SM.
 constexpr int kNtRows = 32;
-constexpr int kNtStagesF = 6;
+constexpr int kNtStagesF = 3;
 
 template <int E>
 constexpr int norm_fwd_tma_smem() {

@@ -71,9 +71,9 @@ int cyfa_short_conv_fwd(const void* x, long long x_stride, const void* cache, co
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CUtensorMap mx;
   if (!cache && C % 128 == 0 && conv_tmap(&mx, x, B, T, C, x_stride) == kOk) {
-    // persistent CTAs: channel block x token-tile group
+    // persistent CTAs (two per SM): channel block x token-tile group
     const int ncb = C / 128, nT = (T + kCtRows - 1) / kCtRows;
-    int G = 148 / ncb;
+    int G = 296 / ncb;
     if (G < 1) G = 1;
     if (G > B * nT) G = B * nT;
     const int grid = ncb * G;
@@ -114,9 +114,10 @@ int cyfa_short_conv_bwd(const void* x, long long x_stride, const float* w, const
   CUtensorMap mx, md;
   if (C % 128 == 0 && conv_tmap(&mx, x, B, T, C, x_stride) == kOk &&
       conv_tmap(&md, dy, B, T, C, C) == kOk) {
-    // persistent CTAs: channel block x token-tile group; one partial row per group
+    // persistent CTAs (two per SM): channel block x token-tile group; one partial
+    // row per group
     const int ncb = C / 128, nT = (T + kCtRows - 1) / kCtRows;
-    int G = 148 / ncb;
+    int G = 296 / ncb;
     if (G < 1) G = 1;
     if (G > rows) G = rows;
     if (G > B * nT) G = B * nT;
@@ -272,7 +273,7 @@ int cyfa_gated_norm_bias_fwd(const void* x, const void* gate, const void* gate_b
   CUtensorMap mx, mg;
   const int BT = rows / H;
   if (norm_tmap(&mx, x, H, BT, D) == kOk && norm_tmap(&mg, gate, H, BT, D) == kOk) {
-    int G = 148 / H;  // persistent CTAs: head x token-tile group
+    int G = 296 / H;  // persistent CTAs (two per SM): head x token-tile group
     if (G > (BT + kNtRows - 1) / kNtRows) G = (BT + kNtRows - 1) / kNtRows;
     if (G < 1) G = 1;
     grid = unsigned(H * G);
