@@ -221,7 +221,7 @@ static int token_fwd_launch(const void* q, const void* k, const float* q_norm_we
   if (token_tmap(&mq, q, B, T, H, K, q_stride) == kOk &&
       token_tmap(&mk, k, B, T, H, K, k_stride) == kOk) {
     const int ntiles = B * H * (TP / kTfRows);
-    const unsigned grid = unsigned(ntiles < 148 ? ntiles : 148);  // persistent
+    const unsigned grid = unsigned(ntiles < 296 ? ntiles : 296);  // persistent, two per SM
     if (K == 256) {
       set_smem(token_fwd_tma_kernel<256>, token_fwd_tma_smem<256>());
       CYFA_LAUNCH("token_fwd", s, launch_k(token_fwd_tma_kernel<256>, grid, 288,

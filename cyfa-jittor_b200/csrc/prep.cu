@@ -275,7 +275,7 @@ template __global__ void token_fwd_kernel<128>(TokenFwdParams);
 // warps 0-7 take four tokens each with the norm weights in registers.  Same
 // outputs and arithmetic as token_fwd_kernel.
 constexpr int kTfRows = 32;
-constexpr int kTfStages = 6;
+constexpr int kTfStages = 3;  // 97 KiB ring: two CTAs per SM
 
 template <int K>
 constexpr int token_fwd_tma_smem() {
@@ -283,7 +283,7 @@ constexpr int token_fwd_tma_smem() {
 }
 
 template <int K>
-__global__ void __launch_bounds__(288, 1)
+__global__ void __launch_bounds__(288, 2)
     token_fwd_tma_kernel(const __grid_constant__ CUtensorMap map_q,
                          const __grid_constant__ CUtensorMap map_k, TokenFwdParams p) {
   constexpr int E = K / 32;
