@@ -403,6 +403,75 @@ def measure_decode(args, rank, world, dev, peaks, barrier):
             "hbm_peak_gbs": peak, "frac": gbs / peak}
 
 
+LMCFG = dict(hidden_size=2048, num_heads=8, head_dim=256, num_slots=128, num_hidden_layers=24,
+             vocab_size=32000, batch=256, prompt=512, new_tokens=256)
+
+
+def measure_lm_decode(args, rank, world, dev, peaks, barrier):
+    """BASELINE configs[3] end to end: the random-init 24-layer CyFA LM (hidden
+    2048, 8 x 256 heads, 128 slots, vocab 32000, bf16 weights, fp32 states),
+    batch 256 sharded over the ranks, a 512-token prefill of uniform-random ids,
+    then greedy decode steps, each one replay of the CUDA graph of the whole
+    model step (GraphedDecoder).  Reports decode tokens/s (all ranks, device
+    time, max over ranks), the prefill rate, and the step's HBM traffic (fp32
+    states read + written, bf16 weights read once) against the copy bandwidth."""
+    import torch
+    import torch.distributed as dist
+
+    from cyclic_flow_attention.generation import GraphedDecoder
+    from cyclic_flow_attention.models.cyfa import CyclicFlowAttentionConfig
+    from cyclic_flow_attention.utils import initialize_model
+
+    c = LMCFG
+    cfg = CyclicFlowAttentionConfig(**{k: c[k] for k in ("hidden_size", "num_heads", "head_dim",
+                                                          "num_slots", "num_hidden_layers",
+                                                          "vocab_size")})
+    B = c["batch"] // world
+    model = initialize_model(cfg, generator=torch.Generator(device=dev).manual_seed(11),
+                             device=dev).eval()
+    gen = torch.Generator(device=dev).manual_seed(13 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (B, c["prompt"]), device=dev, generator=gen)
+    dec = GraphedDecoder(model)
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    with torch.no_grad():
+        hidden, _ = model.model(ids, use_cache=False)
+    b.record()
+    del hidden
+    torch.cuda.synchronize()
+    prefill_ms = a.elapsed_time(b)
+    dec.prefill(ids)
+    for _ in range(3):
+        dec.step()
+    barrier()
+    n = c["new_tokens"]
+    a.record()
+    for _ in range(n):
+        dec.step()
+    b.record()
+    barrier()
+    t = torch.tensor([a.elapsed_time(b) / n, prefill_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, prefill_ms = t.tolist()
+    H, K = cfg.num_heads, cfg.head_dim
+    state_bytes = cfg.num_hidden_layers * B * H * 2 * (K * 128 + 128 * K) * 4
+    weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    gbs = (state_bytes + weight_bytes) / (ms / 1000.0) / 1e9
+    peak = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+    dec = model = None
+    torch.cuda.empty_cache()
+    return {"workload": "CyFA LM greedy decode, BASELINE configs[3]: 24 layers, hidden 2048, "
+                        "8x256 heads, vocab 32000, random-init bf16 weights, fp32 states, batch "
+                        "256 over the ranks, 512-token prefill of uniform-random ids",
+            "tokens_per_s": world * B / (ms / 1000.0), "ms_per_token_step": ms,
+            "timed_steps": n, "prefill_tokens_per_s": world * B * c["prompt"] / (prefill_ms / 1000.0),
+            "bytes_per_step_per_gpu": state_bytes + weight_bytes, "achieved_gbs_per_gpu": gbs,
+            "hbm_peak_gbs": peak, "frac": gbs / peak,
+            "launch": "one CUDA graph replay per step (embedding, 24 layers, norm, lm_head, argmax)"}
+
+
 # ---------------------------------------------------------------- GPU arm
 def run_cyfa(args, rank, world, local_rank):
     import torch
@@ -615,6 +684,7 @@ def run_cyfa(args, rank, world, local_rank):
 
     decode = None if args.no_decode else measure_decode(args, rank, world, dev, peaks, barrier)
     op = None if args.no_op else measure_op(args, rank, world, dev, peaks, barrier)
+    decode_lm = None if args.no_lm else measure_lm_decode(args, rank, world, dev, peaks, barrier)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -641,6 +711,7 @@ def run_cyfa(args, rank, world, local_rank):
             "gpu_launches": launches,
             "clocks": clocks,
             "decode": decode,
+            "decode_lm": decode_lm,
             "op": op,
         }
         print(json.dumps(line), flush=True)
@@ -662,6 +733,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-kernel leg")
+    ap.add_argument("--no-lm", action="store_true",
+                    help="skip the 24-layer LM decode leg (configs[3] end to end)")
     ap.add_argument("--no-op", action="store_true", help="skip the chunk_cyfa op leg (configs[1])")
     ap.add_argument("--workload", choices=("c3", "c5"), default="c3",
                     help="layer config: c3 (BASELINE configs[2], default) or c5 (long context, "

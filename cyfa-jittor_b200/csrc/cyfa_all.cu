@@ -12,4 +12,5 @@
 #include "chunk_api.cu"
 #include "layer_api.cu"
 #include "noalloc.cu"
+#include "lm_decode.cu"
 #include "gradbuf.cu"

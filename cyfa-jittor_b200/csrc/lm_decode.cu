@@ -1,0 +1,188 @@
+// Decoder-block glue for one recurrent decode step of the CyFA language model.
+//
+// A decode step of the LM moves little data per kernel (batch x hidden rows), so
+// the cost of the plain-PyTorch glue around the attention core is its number of
+// launches.  These kernels fold each piece of glue into one launch:
+//   add_rmsnorm  : residual add + RMSNorm of the decoder blocks
+//                  (models/cyfa/modeling_cyfa.py:52-55, 64-69; RMSNorm layers/cyfa.py:62-135)
+//   decode_conv  : the q, k and v short convolutions for one token with their
+//                  W-1 cached rows, the caches shifted in place
+//                  (ShortConvolution with a cache, layers/cyfa.py:144-181)
+//   swiglu       : the gated MLP activation g sigmoid(g) u
+//                  (GatedMLP.execute, models/cyfa/modeling_cyfa.py:22-27)
+// All three are HBM/latency bound: each element is read and written once with
+// 16-byte vector accesses, fp32 arithmetic, bf16 rounding where the reference
+// rounds.
+
+struct AddNormParams {
+  __nv_bfloat16* x;        // [rows, D] residual stream (updated in place when y != null)
+  const __nv_bfloat16* y;  // [rows, D] branch output or null
+  const float* w;          // [D]
+  __nv_bfloat16* out;      // [rows, D]
+  float eps;
+  int rows, D;
+};
+
+// One warp per row; lanes own 8 consecutive columns per 256-column sweep.
+__global__ void __launch_bounds__(128) add_rmsnorm_kernel(AddNormParams p) {
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x * 4 + threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (row >= p.rows) return;
+  __nv_bfloat16* xr = p.x + (size_t)row * p.D;
+  float ss = 0.f;
+  for (int d = lane * 8; d < p.D; d += 256) {
+    __align__(16) __nv_bfloat16 v[8];
+    *reinterpret_cast<int4*>(v) = *reinterpret_cast<const int4*>(xr + d);
+    if (p.y) {
+      __align__(16) __nv_bfloat16 u[8];
+      *reinterpret_cast<int4*>(u) = *reinterpret_cast<const int4*>(p.y + (size_t)row * p.D + d);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[j] = __float2bfloat16_rn(__bfloat162float(v[j]) + __bfloat162float(u[j]));
+      *reinterpret_cast<int4*>(xr + d) = *reinterpret_cast<int4*>(v);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float f = __bfloat162float(v[j]);
+      ss += f * f;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rs = rsqrtf(ss / p.D + p.eps);
+  for (int d = lane * 8; d < p.D; d += 256) {
+    __align__(16) __nv_bfloat16 v[8], o8[8];
+    *reinterpret_cast<int4*>(v) = *reinterpret_cast<const int4*>(xr + d);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o8[j] = __float2bfloat16_rn(__bfloat162float(v[j]) * rs * p.w[d + j]);
+    *reinterpret_cast<int4*>(p.out + (size_t)row * p.D + d) = *reinterpret_cast<int4*>(o8);
+  }
+}
+
+struct DecodeConvParams {
+  const __nv_bfloat16* x;  // row b: q|k|v pre-convolution values at x + b * x_stride
+  long long x_stride;
+  __nv_bfloat16* cache[3];  // [B, W-1, C_i], oldest row first; shifted in place
+  const float* w[3];        // [C_i, W]
+  __nv_bfloat16* y[3];      // [B, C_i]
+  int C[3];
+  int B, W;
+};
+
+// One thread per (sequence, 8 channels) over the three convolutions.  Each thread
+// owns its cache column, so the in-place shift needs no synchronisation.
+__global__ void __launch_bounds__(256) decode_conv_kernel(DecodeConvParams p) {
+  pdl_wait();
+  pdl_trigger();
+  const int groups = (p.C[0] + p.C[1] + p.C[2]) / 8;
+  const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+  if (i >= (long long)p.B * groups) return;
+  const int b = int(i / groups);
+  int c = int(i % groups) * 8;
+  const int col = c;  // column in the packed q|k|v row
+  int s = 0;
+  if (c >= p.C[0]) { c -= p.C[0]; s = 1; }
+  if (s == 1 && c >= p.C[1]) { c -= p.C[1]; s = 2; }
+  const int C = p.C[s], W = p.W;
+  __align__(16) __nv_bfloat16 hist[4][8];  // W <= 4: W-1 cached rows + the new token
+  __nv_bfloat16* cache = p.cache[s] + (size_t)b * (W - 1) * C + c;
+  for (int r = 0; r < W - 1; ++r)
+    *reinterpret_cast<int4*>(hist[r]) = *reinterpret_cast<const int4*>(cache + (size_t)r * C);
+  *reinterpret_cast<int4*>(hist[W - 1]) =
+      *reinterpret_cast<const int4*>(p.x + (size_t)b * p.x_stride + col);
+  const float* w = p.w[s] + (size_t)c * W;
+  __align__(16) __nv_bfloat16 out[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float acc = __bfloat162float(hist[0][j]) * w[j * W];
+    for (int r = 1; r < W; ++r) acc += __bfloat162float(hist[r][j]) * w[j * W + r];
+    out[j] = __float2bfloat16_rn(acc);
+  }
+  *reinterpret_cast<int4*>(p.y[s] + (size_t)b * C + c) = *reinterpret_cast<int4*>(out);
+  for (int r = 0; r < W - 1; ++r)
+    *reinterpret_cast<int4*>(cache + (size_t)r * C) = *reinterpret_cast<int4*>(hist[r + 1]);
+}
+
+struct SwigluParams {
+  const __nv_bfloat16* gu;  // [rows, 2 * mid]: gate columns, then up columns
+  __nv_bfloat16* out;       // [rows, mid]
+  int rows, mid;
+};
+
+__global__ void __launch_bounds__(256) swiglu_kernel(SwigluParams p) {
+  pdl_wait();
+  pdl_trigger();
+  const int groups = p.mid / 8;
+  const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+  if (i >= (long long)p.rows * groups) return;
+  const long long r = i / groups;
+  const int m = int(i % groups) * 8;
+  __align__(16) __nv_bfloat16 g[8], u[8], o[8];
+  *reinterpret_cast<int4*>(g) = *reinterpret_cast<const int4*>(p.gu + r * 2 * p.mid + m);
+  *reinterpret_cast<int4*>(u) = *reinterpret_cast<const int4*>(p.gu + r * 2 * p.mid + p.mid + m);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float gf = __bfloat162float(g[j]);
+    o[j] = __float2bfloat16_rn(gf * sigmoid_f(gf) * __bfloat162float(u[j]));
+  }
+  *reinterpret_cast<int4*>(p.out + r * p.mid + m) = *reinterpret_cast<int4*>(o);
+}
+
+extern "C" {
+
+int cyfa_add_rmsnorm(void* x, const void* y, const float* w, float eps, void* out, int rows,
+                     int D, void* stream) {
+  CYFA_REQUIRE(x && w && out, kNullPointer);
+  CYFA_REQUIRE(rows > 0 && D > 0 && D % 8 == 0, kBadShape);
+  CYFA_REQUIRE(aligned(x, 16) && aligned(out, 16) && (!y || aligned(y, 16)), kMisaligned);
+  AddNormParams p{static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y), w,
+                  static_cast<__nv_bfloat16*>(out), eps, rows, D};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CYFA_LAUNCH("add_rmsnorm", s,
+              (launch_k(add_rmsnorm_kernel, unsigned((rows + 3) / 4), 128, 0, s, p)));
+  return launch_status();
+}
+
+int cyfa_decode_conv(const void* x, long long x_stride, void* cache_q, void* cache_k,
+                     void* cache_v, const float* wq, const float* wk, const float* wv, void* yq,
+                     void* yk, void* yv, int B, int Cq, int Ck, int Cv, int W, void* stream) {
+  CYFA_REQUIRE(x && cache_q && cache_k && cache_v && wq && wk && wv && yq && yk && yv,
+               kNullPointer);
+  CYFA_REQUIRE(B > 0 && W >= 2 && W <= 4 && Cq > 0 && Ck > 0 && Cv > 0 && Cq % 8 == 0 &&
+                   Ck % 8 == 0 && Cv % 8 == 0 && x_stride >= (long long)Cq + Ck + Cv &&
+                   x_stride % 8 == 0,
+               kBadShape);
+  CYFA_REQUIRE(aligned(x, 16) && aligned(cache_q, 16) && aligned(cache_k, 16) &&
+                   aligned(cache_v, 16) && aligned(yq, 16) && aligned(yk, 16) && aligned(yv, 16),
+               kMisaligned);
+  DecodeConvParams p{static_cast<const __nv_bfloat16*>(x),
+                     x_stride,
+                     {static_cast<__nv_bfloat16*>(cache_q), static_cast<__nv_bfloat16*>(cache_k),
+                      static_cast<__nv_bfloat16*>(cache_v)},
+                     {wq, wk, wv},
+                     {static_cast<__nv_bfloat16*>(yq), static_cast<__nv_bfloat16*>(yk),
+                      static_cast<__nv_bfloat16*>(yv)},
+                     {Cq, Ck, Cv},
+                     B,
+                     W};
+  const long long n = (long long)B * ((Cq + Ck + Cv) / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CYFA_LAUNCH("decode_conv", s,
+              (launch_k(decode_conv_kernel, unsigned((n + 255) / 256), 256, 0, s, p)));
+  return launch_status();
+}
+
+int cyfa_swiglu(const void* gu, void* out, int rows, int mid, void* stream) {
+  CYFA_REQUIRE(gu && out, kNullPointer);
+  CYFA_REQUIRE(rows > 0 && mid > 0 && mid % 8 == 0, kBadShape);
+  CYFA_REQUIRE(aligned(gu, 16) && aligned(out, 16), kMisaligned);
+  SwigluParams p{static_cast<const __nv_bfloat16*>(gu), static_cast<__nv_bfloat16*>(out), rows,
+                 mid};
+  const long long n = (long long)rows * (mid / 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CYFA_LAUNCH("swiglu", s, (launch_k(swiglu_kernel, unsigned((n + 255) / 256), 256, 0, s, p)));
+  return launch_status();
+}
+
+}  // extern "C"

@@ -49,6 +49,9 @@ _SIGNATURES = {
     "cyfa_readout_table_grad": [_vp, _vp, _vp, _i, _vp],
     "cyfa_bucket_gather": [_vp, _i, _vp, _vp],
     "cyfa_bucket_scatter": [_vp, _i, _vp, _f, _vp],
+    "cyfa_add_rmsnorm": [_vp, _vp, _vp, _f, _vp, _i, _i, _vp],
+    "cyfa_decode_conv": [_vp, ctypes.c_longlong] + [_vp] * 9 + [_i] * 5 + [_vp],
+    "cyfa_swiglu": [_vp, _vp, _i, _i, _vp],
 }
 
 # size queries (restype size_t)

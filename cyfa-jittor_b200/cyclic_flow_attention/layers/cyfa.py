@@ -16,7 +16,8 @@ import torch.nn.functional as F
 from torch import nn
 
 from ..ops import chunk_cyfa, fused_recurrent_cyfa
-from ..ops.chunk import table_bf16
+from .. import _lib
+from ..ops.chunk import readout_table, table_bf16
 from ..ops.layer_ops import (
     ChunkCyfaPackedFunction,
     GatedNormFunction,
@@ -247,9 +248,111 @@ class CyclicFlowAttention(nn.Module):
             new_cache = {"recurrent_state": (hk, hv, clock), "conv_state": (cq, ck, cv)}
         return y, new_cache
 
+    def _decode_ok(self, x, cache, attention_mask):
+        """T = 1 inference step with a full cache (recurrent state and the three
+        convolution histories) on bf16 weights: the libcyfa decode glue path."""
+        if (cache is None or attention_mask is not None or not x.is_cuda
+                or x.dtype != torch.bfloat16 or x.shape[1] != 1 or self.training
+                or torch.is_grad_enabled() or not self.use_short_conv):
+            return False
+        conv, state = cache.get("conv_state"), cache.get("recurrent_state")
+        W = self.q_conv1d.width
+        return (state is not None and conv is not None and all(c is not None for c in conv)
+                and 2 <= W <= 4 and all(c.shape[1] == W - 1 for c in conv)
+                and self.q_conv1d.bias is None and self.o_proj.bias is None
+                and self.q_proj.weight.dtype == torch.bfloat16 and self.num_slots == 128
+                and self.head_k_dim in (128, 256) and self.head_v_dim in (128, 256)
+                and self.key_dim % 8 == 0 and self.value_dim % 8 == 0)
+
+    def _decode_constants(self):
+        """fp32/bf16 copies of the small parameters the decode kernels read (the
+        readout table R.Phi, conv weights, norm weights, gate parameters), made
+        once and remade only when one of those parameters changes."""
+        g1 = self.g_proj[1]
+        ps = (self.readout, self.q_conv1d.weight, self.k_conv1d.weight, self.v_conv1d.weight,
+              self.q_norm.weight, self.k_norm.weight, self.A_log, self.dt_bias,
+              self.b_proj.bias, self.d_proj.bias, self.o_norm.weight, g1.bias)
+        key = tuple((p.data_ptr(), p._version) for p in ps)
+        cached = getattr(self, "_decode_cached", None)
+        if cached is None or cached[0] != key:
+            W = self.q_conv1d.width
+
+            def f32(t):
+                return t.detach().float().contiguous()
+
+            consts = dict(
+                table=readout_table(self.readout.detach()).contiguous(),
+                wq=f32(self.q_conv1d.weight).reshape(-1, W),
+                wk=f32(self.k_conv1d.weight).reshape(-1, W),
+                wv=f32(self.v_conv1d.weight).reshape(-1, W),
+                q_norm=f32(self.q_norm.weight), k_norm=f32(self.k_norm.weight),
+                A_log=f32(self.A_log), dt_bias=f32(self.dt_bias),
+                b_bias=f32(self.b_proj.bias), d_bias=f32(self.d_proj.bias),
+                o_norm=f32(self.o_norm.weight),
+                g_bias=g1.bias.detach().to(torch.bfloat16).contiguous())
+            self._decode_cached = (key, consts)
+        return self._decode_cached[1]
+
+    def _forward_decode(self, x, cache, inplace=False):
+        """One token per sequence (reference layers/cyfa.py:299-357 at T = 1 with
+        a cache): the packed q|k|v|g0|a|b|d projection, the three short
+        convolutions with their histories (cyfa_decode_conv), the gate activations
+        (cyfa_gate_act_fwd), the recurrent step (cyfa_decode_step), the gate's
+        second linear, the gated output norm with its bias (cyfa_gated_norm_bias_fwd)
+        and o_proj.  With ``inplace`` the cache tensors are updated in place (the
+        graphed decoder's static buffers); otherwise a new cache is returned and
+        the caller's is left untouched, as the reference does."""
+        B = x.shape[0]
+        H, K, V = self.num_heads, self.head_k_dim, self.head_v_dim
+        HK, HV = self.key_dim, self.value_dim
+        c = self._decode_constants()
+        self._pack_front()
+        ws = self._front_weights()
+        wf = packed_rows(ws)
+        if wf is None:
+            n = sum(w.shape[0] for w in ws)
+            wf = torch.cat(ws + [ws[0].new_zeros((n + 7) // 8 * 8 - n, ws[0].shape[1])])
+        P = torch.mm(x.reshape(B, -1), wf.t())  # [B, q|k|v|g0|a|b|d (+pad)]
+        hk, hv, clock = cache["recurrent_state"]
+        cq, ck, cv = cache["conv_state"]
+        dev = x.device
+        if inplace:
+            hk_o, hv_o, clock_o = hk, hv, clock
+        else:
+            cq, ck, cv = (t.to(torch.bfloat16).contiguous().clone() for t in (cq, ck, cv))
+            hk_o, hv_o = torch.empty_like(hk), torch.empty_like(hv)
+            clock_o = torch.empty_like(clock)
+        q = torch.empty(B, 1, H, K, device=dev, dtype=torch.bfloat16)
+        k = torch.empty_like(q)
+        v = torch.empty(B, 1, H, V, device=dev, dtype=torch.bfloat16)
+        p, st, ps = _lib.ptr, _lib.stream(), P.stride(0)
+        _lib.call("cyfa_decode_conv", p(P), ps, p(cq), p(ck), p(cv), p(c["wq"]), p(c["wk"]),
+                  p(c["wv"]), p(q), p(k), p(v), B, HK, HK, HV, self.q_conv1d.width, st)
+        g = torch.empty(B, 1, H, device=dev, dtype=torch.float32)
+        delta, beta = torch.empty_like(g), torch.empty_like(g)
+        off = 2 * HK + HV + V  # a | b | d columns after q|k|v|g0
+        _lib.call("cyfa_gate_act_fwd", p(P[:, off:]), ps, p(P[:, off + H:]), ps,
+                  p(P[:, off + 2 * H:]), ps, p(c["A_log"]), p(c["dt_bias"]), p(c["b_bias"]),
+                  p(c["d_bias"]), p(g), p(delta), p(beta), B, H, st)
+        o = torch.empty(B, 1, H, V, device=dev, dtype=torch.bfloat16)
+        _lib.call("cyfa_decode_step", p(q), p(k), p(v), p(g), p(delta), p(beta), p(c["table"]),
+                  p(c["q_norm"]), p(c["k_norm"]), p(hk), p(hv), p(clock), p(hk_o), p(hv_o),
+                  p(clock_o), p(o), B, H, K, V, 0, float(self.q_norm.eps),
+                  float(self.k_norm.eps), K ** -0.5, st)
+        gate = torch.mm(P[:, 2 * HK + HV:2 * HK + HV + V], self.g_proj[1].weight.t())
+        y = torch.empty(B, HV, device=dev, dtype=torch.bfloat16)
+        rstd = torch.empty(B * H, device=dev, dtype=torch.float32)
+        _lib.call("cyfa_gated_norm_bias_fwd", p(o), p(gate), p(c["g_bias"]), H, p(c["o_norm"]),
+                  float(self.o_norm.eps), float(self.num_slots - 1), p(y), p(rstd), B * H, V, st)
+        out = torch.mm(y, self.o_proj.weight.t()).reshape(B, 1, -1)
+        return out, {"recurrent_state": (hk_o, hv_o, clock_o), "conv_state": (cq, ck, cv)}
+
     def forward(self, x, cache=None, use_cache=False, attention_mask=None):
         if self._fused_ok(x, cache, attention_mask):
             return self._forward_fused(x, use_cache)
+        if self._decode_ok(x, cache, attention_mask):
+            y, new_cache = self._forward_decode(x, cache)
+            return y, new_cache if use_cache else None
         B, T, _ = x.shape
         H = self.num_heads
         q, k, v = self.q_proj(x), self.k_proj(x), self.v_proj(x)

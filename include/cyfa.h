@@ -304,6 +304,32 @@ int cyfa_gated_norm_bwd_static(const void* x, const void* gate, const float* w, 
                                const float* rstd, const void* dy, void* dx, void* dgate,
                                float* dw, int rows, int D, void* stream);
 
+/* ---------------------------------------------------------------- LM decode glue
+ * One launch each for the glue of a recurrent decode step of the CyFA language
+ * model (batch x hidden rows per step, so launch count is what they save).
+ *
+ * Residual add + RMSNorm of the decoder blocks.  Replaces: residual = x + y and
+ * RMSNorm (models/cyfa/modeling_cyfa.py:52-55,64-69; RMSNorm layers/cyfa.py:62-135).
+ * If y != NULL, x = bf16(x + y) in place first; then out = bf16(x * rsqrt(mean(x^2)
+ * + eps) * w).  x, y, out [rows, D] bf16, w [D] f32; D % 8 == 0, 16-byte aligned. */
+int cyfa_add_rmsnorm(void* x, const void* y, const float* w, float eps, void* out, int rows,
+                     int D, void* stream);
+
+/* The q, k and v short convolutions of one decode token.  Replaces:
+ * ShortConvolution.execute with a cache at T = 1 (layers/cyfa.py:144-181), three
+ * convolutions in one launch.  Row b of x holds the pre-convolution q|k|v values
+ * (widths Cq, Ck, Cv) at x + b * x_stride; the caches [B, W-1, C] bf16 (oldest row
+ * first) are shifted in place to end with this token; w [C, W] f32; y [B, C] bf16.
+ * 2 <= W <= 4, widths and x_stride multiples of 8, 16-byte aligned, no bias. */
+int cyfa_decode_conv(const void* x, long long x_stride, void* cache_q, void* cache_k,
+                     void* cache_v, const float* wq, const float* wk, const float* wv, void* yq,
+                     void* yk, void* yv, int B, int Cq, int Ck, int Cv, int W, void* stream);
+
+/* Gated MLP activation: out = bf16(g sigmoid(g) u) in fp32, gu [rows, 2 * mid] bf16
+ * (gate columns first, then up columns), out [rows, mid] bf16; mid % 8 == 0.
+ * Replaces: GatedMLP.execute (models/cyfa/modeling_cyfa.py:22-27). */
+int cyfa_swiglu(const void* gu, void* out, int rows, int mid, void* stream);
+
 /* ---------------------------------------------------------------- self test
  * C[128,N] = A * B through TMA + tcgen05 (test hook for the UMMA descriptor and
  * swizzle encodings).  A is [128,K] (a_mn = 0) or [K,128] (a_mn = 1); B is [N,K]

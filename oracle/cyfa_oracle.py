@@ -42,6 +42,7 @@ __all__ = [
     "short_convolution",
     "gated_rmsnorm",
     "cyfa_layer",
+    "cyfa_lm",
 ]
 
 
@@ -372,3 +373,24 @@ def cyfa_layer(params, x, H, head_k_dim, head_v_dim, num_slots=128, eps=1e-6,
     gate = gate.reshape(B, T, H, head_v_dim)
     o = gated_rmsnorm(o * (num_slots - 1), P["o_norm.weight"], eps, gate)
     return o.reshape(B, T, H * head_v_dim) @ P["o_proj.weight"].T
+
+
+def cyfa_lm(params, ids, num_layers, H, head_k_dim, head_v_dim, num_slots=128, eps=1e-6,
+            chunk_size=64, dtype=torch.float32):
+    """CyclicFlowAttentionForCausalLM.execute without cache: embedding, blocks of
+    attn_norm -> attention -> residual, mlp_norm -> SwiGLU MLP -> residual, final
+    norm, lm_head (models/cyfa/modeling_cyfa.py:13-116).  ``params`` maps the
+    reference's state-dict names to tensors; ids [B,T] -> logits [B,T,vocab]."""
+    P = {n: t.to(dtype) for n, t in params.items()}
+    x = P["model.embeddings.weight"][ids]
+    for i in range(num_layers):
+        pre = f"model.layers.{i}."
+        attn = {n[len(pre) + 5:]: t for n, t in P.items() if n.startswith(pre + "attn.")}
+        h = gated_rmsnorm(x, P[pre + "attn_norm.weight"], eps)
+        x = x + cyfa_layer(attn, h, H, head_k_dim, head_v_dim, num_slots, eps, chunk_size)
+        h = gated_rmsnorm(x, P[pre + "mlp_norm.weight"], eps)
+        g = h @ P[pre + "mlp.gate_proj.weight"].T
+        u = h @ P[pre + "mlp.up_proj.weight"].T
+        x = x + (g * torch.sigmoid(g) * u) @ P[pre + "mlp.down_proj.weight"].T
+    x = gated_rmsnorm(x, P["model.norm.weight"], eps)
+    return x @ P["lm_head.weight"].T
