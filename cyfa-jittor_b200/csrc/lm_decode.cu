@@ -23,40 +23,56 @@ struct AddNormParams {
   int rows, D;
 };
 
-// One warp per row; lanes own 8 consecutive columns per 256-column sweep.
-__global__ void __launch_bounds__(128) add_rmsnorm_kernel(AddNormParams p) {
+// One 256-thread CTA per row; thread t owns columns 8t + 2048j (j < 4, so
+// D <= 8192), held in registers between the sum of squares and the output.
+__global__ void __launch_bounds__(256) add_rmsnorm_kernel(AddNormParams p) {
   pdl_wait();
   pdl_trigger();
-  const int row = blockIdx.x * 4 + threadIdx.x / 32, lane = threadIdx.x % 32;
-  if (row >= p.rows) return;
+  __shared__ float red[8];
+  const int row = blockIdx.x, t = threadIdx.x;
   __nv_bfloat16* xr = p.x + (size_t)row * p.D;
+  __align__(16) __nv_bfloat16 v[4][8];
   float ss = 0.f;
-  for (int d = lane * 8; d < p.D; d += 256) {
-    __align__(16) __nv_bfloat16 v[8];
-    *reinterpret_cast<int4*>(v) = *reinterpret_cast<const int4*>(xr + d);
-    if (p.y) {
-      __align__(16) __nv_bfloat16 u[8];
-      *reinterpret_cast<int4*>(u) = *reinterpret_cast<const int4*>(p.y + (size_t)row * p.D + d);
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        v[j] = __float2bfloat16_rn(__bfloat162float(v[j]) + __bfloat162float(u[j]));
-      *reinterpret_cast<int4*>(xr + d) = *reinterpret_cast<int4*>(v);
-    }
+  for (int j = 0; j < 4; ++j) {
+    const int d = t * 8 + j * 2048;
+    if (d < p.D) {
+      *reinterpret_cast<int4*>(v[j]) = *reinterpret_cast<const int4*>(xr + d);
+      if (p.y) {
+        __align__(16) __nv_bfloat16 u[8];
+        *reinterpret_cast<int4*>(u) = *reinterpret_cast<const int4*>(p.y + (size_t)row * p.D + d);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float f = __bfloat162float(v[j]);
-      ss += f * f;
+        for (int i = 0; i < 8; ++i)
+          v[j][i] = __float2bfloat16_rn(__bfloat162float(v[j][i]) + __bfloat162float(u[i]));
+        *reinterpret_cast<int4*>(xr + d) = *reinterpret_cast<int4*>(v[j]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float f = __bfloat162float(v[j][i]);
+        ss += f * f;
+      }
     }
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float rs = rsqrtf(ss / p.D + p.eps);
-  for (int d = lane * 8; d < p.D; d += 256) {
-    __align__(16) __nv_bfloat16 v[8], o8[8];
-    *reinterpret_cast<int4*>(v) = *reinterpret_cast<const int4*>(xr + d);
+  if (t % 32 == 0) red[t / 32] = ss;
+  __syncthreads();
+  float tot = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o8[j] = __float2bfloat16_rn(__bfloat162float(v[j]) * rs * p.w[d + j]);
-    *reinterpret_cast<int4*>(p.out + (size_t)row * p.D + d) = *reinterpret_cast<int4*>(o8);
+  for (int w = 0; w < 8; ++w) tot += red[w];  // same order in every thread
+  const float rs = rsqrtf(tot / p.D + p.eps);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int d = t * 8 + j * 2048;
+    if (d < p.D) {
+      const float4 w0 = *reinterpret_cast<const float4*>(p.w + d);
+      const float4 w1 = *reinterpret_cast<const float4*>(p.w + d + 4);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      __align__(16) __nv_bfloat16 o8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o8[i] = __float2bfloat16_rn(__bfloat162float(v[j][i]) * rs * wv[i]);
+      *reinterpret_cast<int4*>(p.out + (size_t)row * p.D + d) = *reinterpret_cast<int4*>(o8);
+    }
   }
 }
 
@@ -71,7 +87,9 @@ struct DecodeConvParams {
 };
 
 // One thread per (sequence, 8 channels) over the three convolutions.  Each thread
-// owns its cache column, so the in-place shift needs no synchronisation.
+// owns its cache column, so the in-place shift needs no synchronisation.  The
+// eight channels' W taps are 8W consecutive floats, read as float4.
+template <int W>
 __global__ void __launch_bounds__(256) decode_conv_kernel(DecodeConvParams p) {
   pdl_wait();
   pdl_trigger();
@@ -84,22 +102,34 @@ __global__ void __launch_bounds__(256) decode_conv_kernel(DecodeConvParams p) {
   int s = 0;
   if (c >= p.C[0]) { c -= p.C[0]; s = 1; }
   if (s == 1 && c >= p.C[1]) { c -= p.C[1]; s = 2; }
-  const int C = p.C[s], W = p.W;
-  __align__(16) __nv_bfloat16 hist[4][8];  // W <= 4: W-1 cached rows + the new token
+  const int C = p.C[s];
+  __align__(16) __nv_bfloat16 hist[W][8];  // W-1 cached rows, then the new token
   __nv_bfloat16* cache = p.cache[s] + (size_t)b * (W - 1) * C + c;
+#pragma unroll
   for (int r = 0; r < W - 1; ++r)
     *reinterpret_cast<int4*>(hist[r]) = *reinterpret_cast<const int4*>(cache + (size_t)r * C);
   *reinterpret_cast<int4*>(hist[W - 1]) =
       *reinterpret_cast<const int4*>(p.x + (size_t)b * p.x_stride + col);
-  const float* w = p.w[s] + (size_t)c * W;
+  float w[8 * W];
+  const float4* w4 = reinterpret_cast<const float4*>(p.w[s] + (size_t)c * W);
+#pragma unroll
+  for (int q = 0; q < 2 * W; ++q) {
+    const float4 f = w4[q];
+    w[4 * q] = f.x;
+    w[4 * q + 1] = f.y;
+    w[4 * q + 2] = f.z;
+    w[4 * q + 3] = f.w;
+  }
   __align__(16) __nv_bfloat16 out[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     float acc = __bfloat162float(hist[0][j]) * w[j * W];
+#pragma unroll
     for (int r = 1; r < W; ++r) acc += __bfloat162float(hist[r][j]) * w[j * W + r];
     out[j] = __float2bfloat16_rn(acc);
   }
   *reinterpret_cast<int4*>(p.y[s] + (size_t)b * C + c) = *reinterpret_cast<int4*>(out);
+#pragma unroll
   for (int r = 0; r < W - 1; ++r)
     *reinterpret_cast<int4*>(cache + (size_t)r * C) = *reinterpret_cast<int4*>(hist[r + 1]);
 }
@@ -134,13 +164,14 @@ extern "C" {
 int cyfa_add_rmsnorm(void* x, const void* y, const float* w, float eps, void* out, int rows,
                      int D, void* stream) {
   CYFA_REQUIRE(x && w && out, kNullPointer);
-  CYFA_REQUIRE(rows > 0 && D > 0 && D % 8 == 0, kBadShape);
-  CYFA_REQUIRE(aligned(x, 16) && aligned(out, 16) && (!y || aligned(y, 16)), kMisaligned);
+  CYFA_REQUIRE(rows > 0 && D > 0 && D % 8 == 0 && D <= 8192, kBadShape);
+  CYFA_REQUIRE(aligned(x, 16) && aligned(out, 16) && aligned(w, 16) && (!y || aligned(y, 16)),
+               kMisaligned);
   AddNormParams p{static_cast<__nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(y), w,
                   static_cast<__nv_bfloat16*>(out), eps, rows, D};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CYFA_LAUNCH("add_rmsnorm", s,
-              (launch_k(add_rmsnorm_kernel, unsigned((rows + 3) / 4), 128, 0, s, p)));
+              (launch_k(add_rmsnorm_kernel, unsigned(rows), 256, 0, s, p)));
   return launch_status();
 }
 
@@ -154,7 +185,8 @@ int cyfa_decode_conv(const void* x, long long x_stride, void* cache_q, void* cac
                    x_stride % 8 == 0,
                kBadShape);
   CYFA_REQUIRE(aligned(x, 16) && aligned(cache_q, 16) && aligned(cache_k, 16) &&
-                   aligned(cache_v, 16) && aligned(yq, 16) && aligned(yk, 16) && aligned(yv, 16),
+                   aligned(cache_v, 16) && aligned(yq, 16) && aligned(yk, 16) && aligned(yv, 16) &&
+                   aligned(wq, 16) && aligned(wk, 16) && aligned(wv, 16),
                kMisaligned);
   DecodeConvParams p{static_cast<const __nv_bfloat16*>(x),
                      x_stride,
@@ -168,8 +200,10 @@ int cyfa_decode_conv(const void* x, long long x_stride, void* cache_q, void* cac
                      W};
   const long long n = (long long)B * ((Cq + Ck + Cv) / 8);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  CYFA_LAUNCH("decode_conv", s,
-              (launch_k(decode_conv_kernel, unsigned((n + 255) / 256), 256, 0, s, p)));
+  const unsigned grid = unsigned((n + 255) / 256);
+  if (W == 2) CYFA_LAUNCH("decode_conv", s, (launch_k(decode_conv_kernel<2>, grid, 256, 0, s, p)));
+  else if (W == 3) CYFA_LAUNCH("decode_conv", s, (launch_k(decode_conv_kernel<3>, grid, 256, 0, s, p)));
+  else CYFA_LAUNCH("decode_conv", s, (launch_k(decode_conv_kernel<4>, grid, 256, 0, s, p)));
   return launch_status();
 }
 

@@ -311,7 +311,8 @@ int cyfa_gated_norm_bwd_static(const void* x, const void* gate, const float* w, 
  * Residual add + RMSNorm of the decoder blocks.  Replaces: residual = x + y and
  * RMSNorm (models/cyfa/modeling_cyfa.py:52-55,64-69; RMSNorm layers/cyfa.py:62-135).
  * If y != NULL, x = bf16(x + y) in place first; then out = bf16(x * rsqrt(mean(x^2)
- * + eps) * w).  x, y, out [rows, D] bf16, w [D] f32; D % 8 == 0, 16-byte aligned. */
+ * + eps) * w).  x, y, out [rows, D] bf16, w [D] f32; D % 8 == 0, D <= 8192, all
+ * 16-byte aligned. */
 int cyfa_add_rmsnorm(void* x, const void* y, const float* w, float eps, void* out, int rows,
                      int D, void* stream);
 
@@ -320,7 +321,8 @@ int cyfa_add_rmsnorm(void* x, const void* y, const float* w, float eps, void* ou
  * convolutions in one launch.  Row b of x holds the pre-convolution q|k|v values
  * (widths Cq, Ck, Cv) at x + b * x_stride; the caches [B, W-1, C] bf16 (oldest row
  * first) are shifted in place to end with this token; w [C, W] f32; y [B, C] bf16.
- * 2 <= W <= 4, widths and x_stride multiples of 8, 16-byte aligned, no bias. */
+ * 2 <= W <= 4, widths and x_stride multiples of 8, all pointers 16-byte aligned, no
+ * bias. */
 int cyfa_decode_conv(const void* x, long long x_stride, void* cache_q, void* cache_k,
                      void* cache_v, const float* wq, const float* wk, const float* wv, void* yq,
                      void* yk, void* yv, int B, int Cq, int Ck, int Cv, int W, void* stream);
