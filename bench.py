@@ -422,7 +422,11 @@ def measure_lm_decode(args, rank, world, dev, peaks, barrier):
     from cyclic_flow_attention.models.cyfa import CyclicFlowAttentionConfig
     from cyclic_flow_attention.utils import initialize_model
 
-    c = LMCFG
+    c = dict(LMCFG)
+    if args.lm_layers:
+        c["num_hidden_layers"] = args.lm_layers
+    if args.lm_batch:
+        c["batch"] = args.lm_batch
     cfg = CyclicFlowAttentionConfig(**{k: c[k] for k in ("hidden_size", "num_heads", "head_dim",
                                                           "num_slots", "num_hidden_layers",
                                                           "vocab_size")})
@@ -462,9 +466,10 @@ def measure_lm_decode(args, rank, world, dev, peaks, barrier):
     peak = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
     dec = model = None
     torch.cuda.empty_cache()
-    return {"workload": "CyFA LM greedy decode, BASELINE configs[3]: 24 layers, hidden 2048, "
-                        "8x256 heads, vocab 32000, random-init bf16 weights, fp32 states, batch "
-                        "256 over the ranks, 512-token prefill of uniform-random ids",
+    return {"workload": f"CyFA LM greedy decode, BASELINE configs[3]: {cfg.num_hidden_layers} "
+                        "layers, hidden 2048, 8x256 heads, vocab 32000, random-init bf16 weights, "
+                        f"fp32 states, batch {c['batch']} over the ranks, 512-token prefill of "
+                        "uniform-random ids",
             "tokens_per_s": world * B / (ms / 1000.0), "ms_per_token_step": ms,
             "timed_steps": n, "prefill_tokens_per_s": world * B * c["prompt"] / (prefill_ms / 1000.0),
             "bytes_per_step_per_gpu": state_bytes + weight_bytes, "achieved_gbs_per_gpu": gbs,
@@ -483,6 +488,20 @@ def run_cyfa(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
+    if args.lm_only:
+        # the LM decode leg alone (a smaller model for profiling runs)
+        def sync_ranks():
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize()
+
+        res = measure_lm_decode(args, rank, world, dev, _peaks()[0], sync_ranks)
+        if rank == 0:
+            print(json.dumps({"decode_lm": res, "n_gpus": world}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     B, T, hid = CFG["B"], CFG["T"], CFG["hidden"]
     torch.manual_seed(0)
     layer = CyclicFlowAttention(hid, CFG["heads"], CFG["head_dim"], num_slots=CFG["slots"])
@@ -735,6 +754,12 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-kernel leg")
     ap.add_argument("--no-lm", action="store_true",
                     help="skip the 24-layer LM decode leg (configs[3] end to end)")
+    ap.add_argument("--lm-only", action="store_true",
+                    help="run only the LM decode leg and print its result")
+    ap.add_argument("--lm-layers", type=int, default=0,
+                    help="LM decode leg: layers (default 24, configs[3])")
+    ap.add_argument("--lm-batch", type=int, default=0,
+                    help="LM decode leg: batch over all ranks (default 256, configs[3])")
     ap.add_argument("--no-op", action="store_true", help="skip the chunk_cyfa op leg (configs[1])")
     ap.add_argument("--workload", choices=("c3", "c5"), default="c3",
                     help="layer config: c3 (BASELINE configs[2], default) or c5 (long context, "
