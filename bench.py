@@ -25,12 +25,9 @@ import subprocess
 import sys
 import time
 
-# Keep stdout to the one JSON line: NCCL logs to stdout, and any NCCL_DEBUG level
-# from VERSION up (WARN included) prints its version banner there, so an
-# image-wide NCCL_DEBUG=VERSION (or WARN) is dropped; INFO/TRACE, set on purpose
-# for debugging, stay.  Must happen before torch (and NCCL) load.
-if os.environ.get("NCCL_DEBUG", "").upper() in ("VERSION", "WARN"):
-    del os.environ["NCCL_DEBUG"]
+# NCCL_DEBUG is left as the environment sets it: NCCL's own lines (version
+# banner, communicator setup) may share stdout with the result, which is always
+# printed last, as one JSON object on a line of its own.
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 for _p in (ROOT, os.path.join(ROOT, "cyfa-jittor_b200")):
@@ -67,28 +64,43 @@ def _tile_flops(K=256, V=256, C=128, M=128):
     return out
 
 
-def _tile_bytes(K=256, V=256, C=128, M=128):
-    """Algorithmic HBM bytes per 128-token tile of one (batch, head), summed over
-    all launches of each kernel in one layer step (bf16 operands, each tensor
-    read or written once per launch as the kernel's interface requires)."""
+def _compulsory_bytes(K=256, V=256, M=128):
+    """Compulsory HBM bytes per tok-head (one token of one (batch, head)) of the
+    operation each core kernel implements, summed over all its launches of one
+    layer step: the inputs the operation must read and the outputs it must write,
+    once each, bf16 activations and fp32 gates.  Intermediates the kernels choose
+    to keep in HBM (state histories and their adjoints, materialised score
+    matrices) are not counted: they are the kernels' own traffic, reported
+    separately as measured DRAM bytes.
+
+    * ScalarGatedLA forward, per pass: read q, k (Dk each), v (Dv), the gate (4 B);
+      write o (Dv) -> 1,540 B at Dk = Dv = 256 (pass 1 reads the 128-wide write
+      vector as its values and writes raw/weights, the fused readout adding
+      lambda, 4 B).
+    * ScalarGatedLA backward (the dual GEMM forms every dq, dk, dv of both passes):
+      pass 1 reads q, k (256 each), w (128), dY (128), the gate; writes dq, dk,
+      dw, the gate gradient -> 2,824 B; pass 2 reads weights, w (128 each),
+      v, dO (256 each), the gate; writes dweights, dw, dv, the gate gradient
+      -> 2,568 B.
+    * Readout adjoint: read raw, dweights (128 each), lambda; write draw, dlambda
+      -> 776 B; forward readout (fused into the pass-1 tile) 516 B.
+    * The scores and state scans form intermediates only: their compulsory bytes
+      are the inputs they read (q, k, w, dO, v of both passes; k, w, v for the
+      scans)."""
     b = 2
-    out = {}
-
-    def dual(dk, dv):
-        # one launch per pass: A and B' + queries and keys (C dk each) + values and
-        # output-gradient rows (C dv each) + state history and its adjoint (dk dv each),
-        # written: dq, dk (C dk each) and dv (C dv); the row-dot partners are the
-        # queries and keys already read
-        return b * (2 * C * C + 2 * C * dk + 2 * C * dv + 2 * dk * dv + 2 * C * dk + C * dv)
-
-    out["dual_gemm"] = dual(K, M) + dual(M, V)
-    out["tile_scores"] = sum(b * (2 * C * dk + 2 * C * dv + 2 * C * C) for dk, dv in ((K, M), (M, V)))
-    out["state_scan_fwd"] = sum(b * (C * dk + C * dv + dk * dv) for dk, dv in ((K, M), (M, V)))
-    out["state_scan_bwd"] = sum(b * (C * dk + C * dv + 2 * dk * dv) for dk, dv in ((K, M), (M, V)))
-    out["tile_fwd_readout"] = b * (2 * C * K + K * M + C * M + 2 * C * M) + 8 * C
-    out["tile_fwd"] = b * (2 * C * M + M * V + 2 * C * V)
-    out["readout_bwd"] = b * 3 * C * M + 8 * C
-    return out
+    fwd1 = b * (K + K + M + M) + 4 + 4            # q, k, w in; raw/weights out; G, lam
+    fwd2 = b * (M + M + V + V) + 4                # weights, w, v in; o out; G
+    bwd1 = b * (K + K + M + M) + 4 + b * (K + K + M) + 4     # in: q k w dY g; out: dq dk dw dg
+    bwd2 = b * (M + M + V + V) + 4 + b * (M + M + V) + 4     # in: a w v dO g; out: da dw dv dg
+    return {
+        "tile_fwd_readout": fwd1,
+        "tile_fwd": fwd2,
+        "dual_gemm": bwd1 + bwd2,
+        "readout_bwd": b * (M + M + M) + 4 + 4,
+        "tile_scores": b * (K + K + M + M) + b * (M + M + V + V),
+        "state_scan_fwd": b * (K + M) + b * (M + V),
+        "state_scan_bwd": b * (K + M) + b * (M + V),
+    }
 
 
 def _peaks():
@@ -99,21 +111,6 @@ def _peaks():
         return p, "measured"
     except (OSError, ValueError):
         return PEAKS_FALLBACK, "fallback"
-
-
-def _step_traffic_from_profiles():
-    """DRAM bytes of all libcyfa launches of one c3 layer step (committed ncu summary)."""
-    path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
-    total = 0.0
-    try:
-        with open(path) as f:
-            for line in f:
-                parts = line.split()
-                if len(parts) >= 3 and not line.startswith("#"):
-                    total += float(parts[1]) * float(parts[2])
-    except (OSError, ValueError):
-        return None
-    return total or None
 
 
 def _traffic_from_profiles(kernel):
@@ -177,16 +174,26 @@ def _rank_env():
 
 
 # ---------------------------------------------------------------- CPU baseline
-def cpu_layer_tokens_per_s(min_seconds=10.0, max_reps=20, T=None, warm=1):
-    """Times the oracle layer fwd+bwd (fp32, all host threads) on one sequence."""
+def cpu_model_name():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def _cpu_layer_step(T):
+    """One step of the oracle layer forward + backward (fp32, all host threads)
+    on one sequence of T tokens of the workload's layer config: the reference's
+    algorithm restated on the host cores."""
     import torch
 
     from oracle import cyfa_oracle as O
 
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    # long sequences: time 4096 tokens (the chunked cost is linear in T)
-    T = T or min(CFG["T"], 4096)
+    torch.set_num_threads(os.cpu_count() or 1)
     gen = torch.Generator().manual_seed(0)
     H, hd, hid = CFG["heads"], CFG["head_dim"], CFG["hidden"]
     shapes = {
@@ -209,9 +216,22 @@ def cpu_layer_tokens_per_s(min_seconds=10.0, max_reps=20, T=None, warm=1):
     dy = torch.randn(1, T, hid, generator=gen)
 
     def step():
+        for p in params.values():
+            p.grad = None
+        x.grad = None
         y = O.cyfa_layer(params, x, H, hd, hd)
         (y * dy).sum().backward()
 
+    return step
+
+
+def cpu_layer_tokens_per_s(min_seconds=10.0, max_reps=20, T=None, warm=1):
+    """Times the oracle layer fwd+bwd (fp32, all host threads) on one sequence:
+    `warm` untimed steps, then steps until `min_seconds` or `max_reps`."""
+    threads = os.cpu_count() or 1
+    # long sequences: time 4096 tokens (the chunked cost is linear in T)
+    T = T or min(CFG["T"], 4096)
+    step = _cpu_layer_step(T)
     for _ in range(warm):
         step()
     t0 = time.perf_counter()
@@ -224,31 +244,79 @@ def cpu_layer_tokens_per_s(min_seconds=10.0, max_reps=20, T=None, warm=1):
     return reps * T / dt, threads, f"{reps} x (1 seq x {T} tokens) layer fwd+bwd, fp32 oracle{note}"
 
 
-def run_reference(args, rank, world):
-    if rank != 0:
-        return
+def cpu_decode_tokens_per_s(layers, batch, reps=3):
+    """The decode leg's attention cores on the host: the oracle decode step
+    (fp32, all host threads) for one layer at batch 32, timed over `reps` steps
+    and scaled to `layers` layers and `batch` sequences (the step's cost is
+    linear in both)."""
     import torch
 
+    from oracle import cyfa_oracle as O
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    H, K = DECODE["heads"], DECODE["head_dim"]
+    b = min(32, batch)
+    gen = torch.Generator().manual_seed(7)
+    state = (0.01 * torch.randn(b, H, K, 128, generator=gen),
+             0.01 * torch.randn(b, H, 128, K, generator=gen), torch.zeros(b, H))
+    q, k, v = (torch.randn(b, 1, H, K, generator=gen) for _ in range(3))
+    g = torch.full((b, 1, H), -0.05)
+    d = torch.full((b, 1, H), 0.5)
+    r = torch.eye(127).expand(H, -1, -1)
+    w = torch.ones(K)
+    with torch.no_grad():
+        O.fused_recurrent_cyfa(q, k, v, g, d, d, r, w, w, initial_state=state,
+                               output_final_state=True)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            _, state = O.fused_recurrent_cyfa(q, k, v, g, d, d, r, w, w, initial_state=state,
+                                              output_final_state=True)
+        dt = (time.perf_counter() - t0) / reps
+    per_token_step = dt * layers * batch / b
+    return {"value": batch / per_token_step, "unit": "tokens/s", "cores": os.cpu_count() or 1,
+            "kind": "port", "cpu": cpu_model_name(),
+            "sample": f"{reps} decode steps of one layer's attention cores at batch {b}, fp32 "
+                      f"oracle; scaled to {layers} layers x batch {batch} (extrapolated)"}
+
+
+def run_reference(args, rank, world):
+    """The reference arm: the reference algorithm's CPU implementation (its
+    restatement in oracle/; the reference itself has no CPU path and needs
+    Jittor) on the host cores.  Each step is one bounded sample of the workload:
+    one sequence of the layer config, forward + backward.  `warmup` untimed
+    steps, then exactly `steps` timed steps."""
+    if rank != 0:
+        return
     threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    # each step: one sequence of the workload (bounded sample), timed on host cores
-    tps_warm = cpu_layer_tokens_per_s(min_seconds=0.0, max_reps=max(1, args.warmup), warm=0)[0]
+    T = min(CFG["T"], 4096)
+    step = _cpu_layer_step(T)
+    for _ in range(args.warmup):
+        step()
     t0 = time.perf_counter()
-    tps, cores, _ = cpu_layer_tokens_per_s(min_seconds=0.0, max_reps=args.steps, warm=0)
+    for _ in range(args.steps):
+        step()
     dt = time.perf_counter() - t0
-    sample = f"{args.steps} steps x (1 seq x {CFG['T']} tokens) layer fwd+bwd, fp32 CPU oracle"
+    ms = 1000 * dt / args.steps
+    tps = T / (ms / 1000.0)
+    note = "" if T == CFG["T"] else f"; tokens/s extrapolated to T={CFG['T']} (linear cost)"
+    sample = (f"each step: 1 seq x {T} tokens layer fwd+bwd, fp32 CPU oracle, "
+              f"{threads} threads{note}")
     line = {
         "impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": "cyfa_layer_fwd_bwd (BASELINE configs[2]) on host cores",
+        "config": {"workload": ("cyfa_layer_fwd_bwd (BASELINE configs[2]) on host cores"
+                                if args.workload == "c3" else
+                                "cyfa_layer_fwd_bwd long context (BASELINE configs[4]) on host "
+                                "cores"),
                    **CFG, "parallelism": "cpu"},
-        "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": sample},
+        "cpu_baseline": {"value": tps, "unit": UNIT, "cores": threads, "kind": "port",
+                         "cpu": cpu_model_name(), "sample": sample},
         "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "timed_s": dt,
         "note": "the reference (Jittor) has no CPU path and cannot be installed here; "
-                "this is its algorithm restated in oracle/ (warm-up tokens/s %.1f)" % tps_warm,
+                "this is its algorithm restated in oracle/",
     }
     print(json.dumps(line), flush=True)
 
@@ -653,24 +721,28 @@ def run_cyfa(args, rank, world, local_rank):
     prof = _lib.profile_report()
     _lib.profile_enable(False)
     tiles = B * CFG["heads"] * math.ceil(T / 128)
+    tok_heads = B * T * CFG["heads"]
     flops = _tile_flops(CFG["head_dim"], CFG["head_dim"])
-    tbytes = _tile_bytes(CFG["head_dim"], CFG["head_dim"])
+    cbytes = _compulsory_bytes(CFG["head_dim"], CFG["head_dim"])
     roofline = None
     if prof:
         dom = max(prof.items(), key=lambda kv: kv[1][0])
         name, (ms, n) = dom
         traffic = _traffic_from_profiles(name)
-        # the tile kernels move ~64-100 B per FLOP-pair: below the ridge
-        # (peak FLOP/s / peak B/s), so they are bounded by HBM bandwidth
-        if name in tbytes:
+        # every core kernel moves more bytes per FLOP than the ridge (peak FLOP/s
+        # over peak B/s), so it is bounded by HBM bandwidth: achieved = the
+        # compulsory bytes of the operation it implements over its time
+        if name in cbytes:
             peak = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
-            work = tbytes[name] * tiles  # all launches of this kernel in one step
+            work = cbytes[name] * tok_heads  # all launches of this kernel in one step
             achieved = work / (ms / 1000.0) / 1e9 if ms > 0 else 0.0
             roofline = {"bound": "hbm", "kernel": name, "achieved": achieved, "peak": peak,
                         "unit": "GB/s", "frac": achieved / peak,
                         "traffic": traffic, "algorithmic_bytes_per_launch": work / n,
+                        "algorithmic_bytes_per_tok_head": cbytes[name],
                         "tflops": flops.get(name, 0) * tiles / (ms / 1000.0) / 1e12,
-                        "peak_kind": f"{peak_kind} HBM copy"}
+                        "peak_kind": f"{peak_kind} HBM copy (of measured)" if peak_kind ==
+                        "measured" else "fallback HBM copy"}
         else:
             peak = peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"])
             work = flops.get(name, 0) * tiles
@@ -681,25 +753,21 @@ def run_cyfa(args, rank, world, local_rank):
         roofline.update({"launches_per_step": n, "ms_per_step": ms,
                          "kernel_ms": {k: round(v[0], 4) for k, v in sorted(prof.items())}})
 
-    # the whole step against its two rooflines: the cuBLAS GEMMs (projection, output
-    # gate, o_proj; forward, data and weight gradients) at the bf16 tensor peak, the
-    # libcyfa kernels' DRAM traffic (committed ncu capture of this c3 step) at the
-    # HBM copy bandwidth
-    layer_roofline = None
-    core_bytes = _step_traffic_from_profiles() if args.workload == "c3" else None
-    if core_bytes:
-        hid, H, hd = CFG["hidden"], CFG["heads"], CFG["head_dim"]
-        n_used = 3 * H * hd + hd + 3 * H
-        gemm_flop = 3 * 2 * B * T * (hid * n_used + hd * H * hd + H * hd * hid)
-        tf = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
-        gbs = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
-        t_gemm = gemm_flop / (tf * 1e12) * 1e3
-        t_core = core_bytes / (gbs * 1e9) * 1e3
-        layer_roofline = {"gemm_tflop": gemm_flop / 1e12, "core_dram_gb": core_bytes / 1e9,
-                          "gemm_ms_at_peak": t_gemm, "core_ms_at_peak": t_core,
-                          "roofline_ms": t_gemm + t_core, "frac": (t_gemm + t_core) / ms_per_step,
-                          "peaks": f"{peak_kind} bf16 {tf} TFLOP/s, HBM {gbs} GB/s",
-                          "traffic_source": "profiles/dram_traffic.txt"}
+    # the whole step against the tensor-core peak: the layer's FLOPs (projection
+    # GEMMs forward, data and weight gradients, plus the attention core forward and
+    # backward) over the measured step time
+    hid, H, hd = CFG["hidden"], CFG["heads"], CFG["head_dim"]
+    n_used = 3 * H * hd + hd + 3 * H
+    gemm_flop = 3 * 2 * B * T * (hid * n_used + hd * H * hd + H * hd * hid)
+    core_flop = tok_heads * (OP_FLOPS_FWD + OP_FLOPS_BWD)
+    tf_burst = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    tf_sus = peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"])
+    step_tflops = (gemm_flop + core_flop) / (ms_per_step / 1000.0) / 1e12
+    layer_tensor = {"flop_per_step": gemm_flop + core_flop, "gemm_flop": gemm_flop,
+                    "core_flop": core_flop, "achieved_tflops": step_tflops,
+                    "frac_of_burst": step_tflops / tf_burst,
+                    "frac_of_sustained": step_tflops / tf_sus,
+                    "peaks": f"{peak_kind} bf16 {tf_burst} (burst) / {tf_sus} (sustained) TFLOP/s"}
 
     decode = None if args.no_decode else measure_decode(args, rank, world, dev, peaks, barrier)
     op = None if args.no_op else measure_op(args, rank, world, dev, peaks, barrier)
@@ -708,7 +776,10 @@ def run_cyfa(args, rank, world, local_rank):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         tps, cores, sample = cpu_layer_tokens_per_s(min_seconds=args.cpu_seconds)
-        cpu = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        cpu = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+               "cpu": cpu_model_name()}
+        if decode is not None:
+            decode["cpu_baseline"] = cpu_decode_tokens_per_s(DECODE["layers"], DECODE["batch"])
 
     if rank == 0:
         line = {
@@ -724,7 +795,8 @@ def run_cyfa(args, rank, world, local_rank):
                        "l2": "flushed between timed steps (2x126 MiB write outside the events)",
                        "launch": "whole step (fwd, bwd, grad all-reduce) replayed as one CUDA graph"},
             "roofline": roofline,
-            "layer_roofline": layer_roofline,
+            "layer_tensor_frac": layer_tensor["frac_of_burst"],
+            "layer_tensor": layer_tensor,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,

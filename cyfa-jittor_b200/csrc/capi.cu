@@ -438,6 +438,34 @@ int cyfa_decode_step(const void* q, const void* k, const void* v, const float* g
   return launch_status();
 }
 
+int cyfa_chunk_fwd_f32(const float* q, const float* k, const float* v, const float* g,
+                       const float* delta, const float* beta, const float* table,
+                       const float* q_norm_weight, const float* k_norm_weight, const float* hk0,
+                       const float* hv0, const float* clock0, float* o, float* hk, float* hv,
+                       float* clock, int B, int T, int H, int K, int V, float q_eps, float k_eps,
+                       float scale, void* stream) {
+  CYFA_REQUIRE(q && k && v && g && delta && beta && table && q_norm_weight && k_norm_weight &&
+                   o && hk && hv && clock,
+               kNullPointer);
+  CYFA_REQUIRE(B > 0 && T >= 0 && H > 0 && (K == 128 || K == 256) && (V == 128 || V == 256),
+               kBadShape);
+  CYFA_REQUIRE(aligned(hk, 16) && aligned(hv, 16) && aligned(table, 16) &&
+                   (!hk0 || aligned(hk0, 16)) && (!hv0 || aligned(hv0, 16)),
+               kMisaligned);
+  RecurrentParams p{q, k, v, g, delta, beta, table, q_norm_weight, k_norm_weight, hk0, hv0,
+                    clock0, hk, hv, clock, o, B, T, H, q_eps, k_eps, scale};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 grid(B * H);
+#define CYFA_REC(KK, VV) \
+  CYFA_LAUNCH("recurrent_fwd_f32", s, (launch_k(recurrent_fwd_f32_kernel<KK, VV>, grid, 256, 0, s, p)))
+  if (K == 256 && V == 256) CYFA_REC(256, 256);
+  else if (K == 128 && V == 128) CYFA_REC(128, 128);
+  else if (K == 256) CYFA_REC(256, 128);
+  else CYFA_REC(128, 256);
+#undef CYFA_REC
+  return launch_status();
+}
+
 int cyfa_gates_fwd(const float* g, const float* delta, const float* beta, const float* clock0,
                    float* G, float* lam, float* beta_h, float* clock_out, int B, int T, int H,
                    void* stream) {

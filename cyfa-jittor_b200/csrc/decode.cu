@@ -89,22 +89,39 @@ __device__ __forceinline__ float block_max_256(float x, float* red) {
   return s;
 }
 
-template <typename Tin, int K, int V>
-__global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
-  pdl_wait();
-  pdl_trigger();
+// One token of one (batch, head): the whole decode step on this CTA's 256
+// threads.  Each thread reads and writes the same state elements in both sweeps,
+// so the state may be updated in place (src == dst) with no barrier; the shared
+// scratch is reused by the next call only after its trailing barrier.
+struct TokenIO {
+  const void* q;        // this token's q row [K]
+  const void* k;        // [K]
+  const void* v;        // [V]
+  float g, beta, lam;   // log decay, write strength, clock after this token
+  const float* hk_src;  // [K, 128] or null (zero state)
+  const float* hv_src;  // [128, V] or null
+  float* hk_dst;
+  float* hv_dst;
+  float* clock_dst;     // stores lam once every thread has read the clock, or null
+  void* out;            // output row [V]
+};
+
+// kStream: streaming cache hints for states touched once (decode); the chunk
+// loop keeps its per-(b,h) state resident in L2 instead.
+template <typename Tin, int K, int V, bool kStream>
+__device__ __forceinline__ void decode_token(const TokenIO& io, const float* tab,
+                                             const float* qnw, const float* knw, float q_eps,
+                                             float k_eps, float scale) {
   constexpr int M = 128;
-  const int bh = blockIdx.x;
-  const int h = bh % p.H;
   const int tid = threadIdx.x;
   __shared__ float sq[K], sk[K];
   __shared__ float part[8 * M];  // per-group partial sums (sweep 1 uses 8x128, sweep 2 4x256)
   __shared__ float wv[M], raw[M], z[M], wts[M], prob[128];
   __shared__ float red[8];
 
-  const Tin* q = static_cast<const Tin*>(p.q) + size_t(bh) * K;
-  const Tin* kk = static_cast<const Tin*>(p.k) + size_t(bh) * K;
-  const Tin* vv = static_cast<const Tin*>(p.v) + size_t(bh) * V;
+  const Tin* q = static_cast<const Tin*>(io.q);
+  const Tin* kk = static_cast<const Tin*>(io.k);
+  const Tin* vv = static_cast<const Tin*>(io.v);
 
   // ---- q/k RMSNorm (head_dim K), rounded to the input dtype (ref :63-89)
   float q2 = 0.f, k2 = 0.f;
@@ -115,15 +132,14 @@ __global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
   }
   const float qs = block_sum_256(q2, red);
   const float ks = block_sum_256(k2, red);
-  const float qr = rsqrtf(qs / K + p.q_eps), kr = rsqrtf(ks / K + p.k_eps);
+  const float qr = rsqrtf(qs / K + q_eps), kr = rsqrtf(ks / K + k_eps);
   for (int d = tid; d < K; d += 256) {
-    sq[d] = round_in<Tin>(to_f(q[d]) * qr * p.q_norm_weight[d]) * p.scale;
-    sk[d] = round_in<Tin>(to_f(kk[d]) * kr * p.k_norm_weight[d]);
+    sq[d] = round_in<Tin>(to_f(q[d]) * qr * qnw[d]) * scale;
+    sk[d] = round_in<Tin>(to_f(kk[d]) * kr * knw[d]);
   }
-  const float lam = (p.clock_in ? p.clock_in[bh] : 0.f) + p.delta[bh];
-  const float alpha = expf(p.g[bh]);
-  const float bt = p.beta[bh];
-  if (tid == 0) p.clock_out[bh] = lam;
+  const float lam = io.lam;
+  const float alpha = expf(io.g);
+  const float bt = io.beta;
   if (tid < M) {
     const int pair = tid >> 1;
     float s, c;
@@ -131,14 +147,17 @@ __global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
     wv[tid] = round_in<Tin>(bt * atom_scale(pair) * ((tid & 1) ? -s : c));
   }
   __syncthreads();
+  // the clock output may alias the clock input (in-place decode): store only
+  // after the barrier above, by which every thread has read the clock input
+  if (tid == 0 && io.clock_dst) *io.clock_dst = lam;
 
   // ---- sweep 1: hk' = a hk + k^ w^T ; raw = hk'^T q^   (ref :94-112)
   {
     const int mq = tid & 31, dg = tid >> 5;  // 4 m values, 8 d-groups
     const float4 w4 = make_float4(wv[4 * mq], wv[4 * mq + 1], wv[4 * mq + 2], wv[4 * mq + 3]);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4* src = p.hk_in ? reinterpret_cast<const float4*>(p.hk_in + size_t(bh) * K * M) : nullptr;
-    float4* dst = reinterpret_cast<float4*>(p.hk_out + size_t(bh) * K * M);
+    const float4* src = reinterpret_cast<const float4*>(io.hk_src);
+    float4* dst = reinterpret_cast<float4*>(io.hk_dst);
     constexpr int ROWS = K / 8;
     constexpr int U = 8;
 #pragma unroll 1
@@ -147,7 +166,8 @@ __global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int d = dg + 8 * (i0 + u);
-        x[u] = src ? __ldcs(src + d * (M / 4) + mq) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[u] = src ? (kStream ? __ldcs(src + d * (M / 4) + mq) : __ldcg(src + d * (M / 4) + mq))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -158,7 +178,8 @@ __global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
         y.y = x[u].y * alpha + kd * w4.y;
         y.z = x[u].z * alpha + kd * w4.z;
         y.w = x[u].w * alpha + kd * w4.w;
-        __stcs(dst + d * (M / 4) + mq, y);
+        if (kStream) __stcs(dst + d * (M / 4) + mq, y);
+        else __stcg(dst + d * (M / 4) + mq, y);
         acc.x += y.x * qd;
         acc.y += y.y * qd;
         acc.z += y.z * qd;
@@ -185,7 +206,6 @@ __global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
     z[tid] = round_in<Tin>((tid & 1) ? s * e + c * o : c * e - s * o);
   }
   __syncthreads();
-  const float* tab = p.table + size_t(h) * 127 * M;
   {
     const int w = tid >> 5, l = tid & 31;
     for (int r = w; r < 127; r += 8) {
@@ -227,8 +247,8 @@ __global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
     const float4 v4 = make_float4(to_f(vv[4 * vq]), to_f(vv[4 * vq + 1]), to_f(vv[4 * vq + 2]),
                                   to_f(vv[4 * vq + 3]));
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4* src = p.hv_in ? reinterpret_cast<const float4*>(p.hv_in + size_t(bh) * M * V) : nullptr;
-    float4* dst = reinterpret_cast<float4*>(p.hv_out + size_t(bh) * M * V);
+    const float4* src = reinterpret_cast<const float4*>(io.hv_src);
+    float4* dst = reinterpret_cast<float4*>(io.hv_dst);
     constexpr int ROWS = M / MG;
     constexpr int U = 8;
 #pragma unroll 1
@@ -237,7 +257,8 @@ __global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int m = mg + MG * (i0 + u);
-        x[u] = src ? __ldcs(src + m * VQ + vq) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[u] = src ? (kStream ? __ldcs(src + m * VQ + vq) : __ldcg(src + m * VQ + vq))
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -248,7 +269,8 @@ __global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
         y.y = x[u].y * alpha + wm * v4.y;
         y.z = x[u].z * alpha + wm * v4.z;
         y.w = x[u].w * alpha + wm * v4.w;
-        __stcs(dst + m * VQ + vq, y);
+        if (kStream) __stcs(dst + m * VQ + vq, y);
+        else __stcg(dst + m * VQ + vq, y);
         acc.x += am * y.x;
         acc.y += am * y.y;
         acc.z += am * y.z;
@@ -262,10 +284,110 @@ __global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
       float s = 0.f;
 #pragma unroll
       for (int gidx = 0; gidx < MG; ++gidx) s += part[gidx * V + tid];
-      store_out<Tin>(p.out, bh * V + tid, s);
+      store_out<Tin>(io.out, tid, s);
     }
   }
+  __syncthreads();  // the next token may overwrite the shared scratch
 }
+
+template <typename Tin, int K, int V>
+__global__ void __launch_bounds__(256) decode_step_kernel(DecodeParams p) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int M = 128;
+  const int bh = blockIdx.x;
+  const int h = bh % p.H;
+  TokenIO io;
+  io.q = static_cast<const Tin*>(p.q) + size_t(bh) * K;
+  io.k = static_cast<const Tin*>(p.k) + size_t(bh) * K;
+  io.v = static_cast<const Tin*>(p.v) + size_t(bh) * V;
+  io.g = p.g[bh];
+  io.beta = p.beta[bh];
+  io.lam = (p.clock_in ? p.clock_in[bh] : 0.f) + p.delta[bh];
+  io.hk_src = p.hk_in ? p.hk_in + size_t(bh) * K * M : nullptr;
+  io.hv_src = p.hv_in ? p.hv_in + size_t(bh) * M * V : nullptr;
+  io.hk_dst = p.hk_out + size_t(bh) * K * M;
+  io.hv_dst = p.hv_out + size_t(bh) * M * V;
+  io.clock_dst = p.clock_out + bh;
+  io.out = static_cast<Tin*>(p.out) + size_t(bh) * V;
+  decode_token<Tin, K, V, true>(io, p.table + size_t(h) * 127 * M, p.q_norm_weight,
+                                p.k_norm_weight, p.q_eps, p.k_eps, p.scale);
+}
+
+// fp32 chunk forward as the token recurrence: one CTA of 256 threads per
+// (batch, head) runs the decode step over all T tokens of its sequence, keeping
+// its states in the caller's final-state buffers (512 KiB per (b, h) at
+// K = V = 256, resident in L2 between tokens).  Every product and sum is fp32,
+// so the result equals the reference's fp32 chunkwise path
+// (cyclic_flow_attention/ops/chunk.py:136-161,300-331) up to summation order.
+// The clock follows the reference's order: the running sum of delta from zero,
+// plus the initial clock (ops/chunk.py:254-256).
+struct RecurrentParams {
+  const float* q;      // [B, T, H, K]
+  const float* k;      // [B, T, H, K]
+  const float* v;      // [B, T, H, V]
+  const float* g;      // [B, T, H]
+  const float* delta;  // [B, T, H]
+  const float* beta;   // [B, T, H]
+  const float* table;  // [H, 127, 128] fp32
+  const float* q_norm_weight;
+  const float* k_norm_weight;
+  const float* hk0;    // [B*H, K, 128] or null
+  const float* hv0;    // [B*H, 128, V] or null
+  const float* clock0; // [B*H] or null
+  float* hk;           // [B*H, K, 128] running and final state
+  float* hv;           // [B*H, 128, V]
+  float* clock;        // [B*H]
+  float* o;            // [B, T, H, V]
+  int B, T, H;
+  float q_eps, k_eps, scale;
+};
+
+template <int K, int V>
+__global__ void __launch_bounds__(256) recurrent_fwd_f32_kernel(RecurrentParams p) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int M = 128;
+  const int bh = blockIdx.x;
+  const int b = bh / p.H, h = bh % p.H;
+  const float* tab = p.table + size_t(h) * 127 * M;
+  float* hk = p.hk + size_t(bh) * K * M;
+  float* hv = p.hv + size_t(bh) * M * V;
+  const float c0 = p.clock0 ? p.clock0[bh] : 0.f;
+  float csum = 0.f;
+  for (int t = 0; t < p.T; ++t) {
+    const size_t row = (size_t(b) * p.T + t) * p.H + h;
+    TokenIO io;
+    io.q = p.q + row * K;
+    io.k = p.k + row * K;
+    io.v = p.v + row * V;
+    io.g = p.g[row];
+    io.beta = p.beta[row];
+    csum = __fadd_rn(csum, p.delta[row]);
+    io.lam = __fadd_rn(csum, c0);
+    io.hk_src = t ? hk : (p.hk0 ? p.hk0 + size_t(bh) * K * M : nullptr);
+    io.hv_src = t ? hv : (p.hv0 ? p.hv0 + size_t(bh) * M * V : nullptr);
+    io.hk_dst = hk;
+    io.hv_dst = hv;
+    io.clock_dst = nullptr;
+    io.out = p.o + row * V;
+    decode_token<float, K, V, false>(io, tab, p.q_norm_weight, p.k_norm_weight, p.q_eps,
+                                     p.k_eps, p.scale);
+  }
+  if (threadIdx.x == 0) p.clock[bh] = __fadd_rn(csum, c0);
+  if (p.T == 0) {
+    // no tokens: the final state is the initial state
+    const int n = K * M;
+    for (int i = threadIdx.x; i < n; i += 256) hk[i] = p.hk0 ? p.hk0[size_t(bh) * n + i] : 0.f;
+    for (int i = threadIdx.x; i < M * V; i += 256)
+      hv[i] = p.hv0 ? p.hv0[size_t(bh) * M * V + i] : 0.f;
+  }
+}
+
+template __global__ void recurrent_fwd_f32_kernel<256, 256>(RecurrentParams);
+template __global__ void recurrent_fwd_f32_kernel<128, 128>(RecurrentParams);
+template __global__ void recurrent_fwd_f32_kernel<256, 128>(RecurrentParams);
+template __global__ void recurrent_fwd_f32_kernel<128, 256>(RecurrentParams);
 
 template __global__ void decode_step_kernel<__nv_bfloat16, 256, 256>(DecodeParams);
 template __global__ void decode_step_kernel<__nv_bfloat16, 128, 128>(DecodeParams);

@@ -25,7 +25,10 @@ static __device__ __align__(256) float g_norm_scratch[kStaticNormRows * kStaticN
 
 // Device address of g_norm_scratch on the current device.  In host code the
 // array's name is only a host-side stand-in, so the address is looked up once
-// per device (cudaGetSymbolAddress) and cached.
+// per device (cudaGetSymbolAddress) and cached for the life of the process.  A
+// device reset (cudaDeviceReset, or a reset of the primary context) reloads the
+// module at a possibly different address, so the entry point is not for use on
+// a device after such a reset.
 static int static_norm_scratch(float** out) {
   static std::mutex mu;
   static float* cached[64] = {};

@@ -26,6 +26,7 @@ _SIGNATURES = {
     "cyfa_device_error": [_i],
     "cyfa_selftest_umma": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "cyfa_decode_step": [_vp] * 16 + [_i] * 5 + [_f] * 3 + [_vp],
+    "cyfa_chunk_fwd_f32": [_vp] * 16 + [_i] * 5 + [_f] * 3 + [_vp],
     "cyfa_gates_fwd": [_vp] * 8 + [_i] * 3 + [_vp],
     "cyfa_token_fwd": [_vp] * 11 + [_i] * 4 + [_f] * 2 + [_vp],
     "cyfa_token_bwd": [_vp] * 17 + [_i] * 4 + [_vp],

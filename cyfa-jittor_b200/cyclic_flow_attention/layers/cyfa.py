@@ -3,10 +3,15 @@
 Mirror of the reference layer (cyclic_flow_attention/layers/cyfa.py:236-357):
 identical parameter names, shapes and default initialisation, so checkpoints
 saved by the reference (PyTorch-compatible safetensors) load with
-``load_state_dict``.  The projections, short convolutions and the gated output
-norm are library ops (cuBLAS / cuDNN via torch); the attention core is
-``chunk_cyfa`` (training and prefill) or ``fused_recurrent_cyfa`` (T == 1
-decode), both in libcyfa.so.
+``load_state_dict``.
+
+On bf16 weights and CUDA inputs (training and prefill) the fused path runs: one
+packed projection GEMM (cuBLAS), the short convolutions and gate activations on
+its columns, the attention core, and the gated output norm are libcyfa.so
+kernels; only the GEMMs are library calls.  T == 1 decode with a cache runs the
+libcyfa decode glue and ``cyfa_decode_step``.  Other cases (fp32 weights, an
+attention mask, a cache during prefill) run torch glue around ``chunk_cyfa`` /
+``fused_recurrent_cyfa``, whose core is libcyfa.so as well.
 """
 
 import math
@@ -60,10 +65,17 @@ class ShortConvolution(nn.Module):
         B, T, D = x.shape
         history = x if cache is None else torch.cat([cache.to(x.dtype), x], dim=1)
         offset = self.width - 1 if cache is None else 0
-        h = F.pad(history.transpose(1, 2), (offset, 0))
-        y = F.conv1d(h.float(), self.weight.float(), None if self.bias is None else self.bias.float(),
-                     groups=D)
-        y = y[..., y.shape[-1] - T:].transpose(1, 2)
+        # y_t = sum_i w_i h_{t+i} over the left-padded history, as W shifted fp32
+        # multiply-adds (exact fp32 products: no TF32 convolution algorithm)
+        h = F.pad(history.float(), (0, 0, offset, 0))
+        n = h.shape[1] - (self.width - 1)
+        w = self.weight.float()[:, 0]
+        y = h[:, :n] * w[:, 0]
+        for i in range(1, self.width):
+            y = y + h[:, i:i + n] * w[:, i]
+        if self.bias is not None:
+            y = y + self.bias.float()
+        y = y[:, n - T:]
         if self.width == 1:
             new_cache = history[:, :0]
         elif lengths is None and history.shape[1] >= self.width - 1:

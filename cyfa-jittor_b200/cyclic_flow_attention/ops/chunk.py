@@ -179,6 +179,35 @@ class ChunkCyfaFunction(torch.autograd.Function):
                 dclock0 if has_c0 else None, None, None, None)
 
 
+def _chunk_cyfa_f32(q, k, v, g, delta, beta, readout, qw, kw, q_eps, k_eps, scale, hk0, hv0,
+                    clock0, output_final_state):
+    """fp32 inputs: the reference computes these in fp32 throughout (its generic
+    path, ops/chunk.py:136-161,300-331), so they run on cyfa_chunk_fwd_f32, an
+    fp32 token recurrence, instead of the bf16 tensor-core kernels.  Inference
+    only: the fp32 training path is not built, so tracked gradients raise."""
+    tracked = (q, k, v, g, delta, beta, readout, qw, kw, hk0, hv0, clock0)
+    if torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in tracked):
+        raise NotImplementedError(
+            "chunk_cyfa: fp32 inputs run the fp32 inference path, which has no backward; "
+            "pass bfloat16 q/k/v for training, or call under torch.no_grad()")
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    dev = q.device
+    f32 = torch.float32
+    o = torch.empty(B, T, H, V, device=dev, dtype=f32)
+    hk = torch.empty(B, H, K, 128, device=dev, dtype=f32)
+    hv = torch.empty(B, H, 128, V, device=dev, dtype=f32)
+    clock = torch.empty(B, H, device=dev, dtype=f32)
+    with torch.no_grad():
+        table = readout_table(readout.detach()).contiguous()
+        ins = [_contig(t.detach(), f32) for t in (q, k, v, g, delta, beta)]
+        qn, kn = (_contig(t.detach(), f32) for t in (qw, kw))
+        _lib.call("cyfa_chunk_fwd_f32", *[_p(t) for t in ins], _p(table), _p(qn), _p(kn),
+                  _p(hk0), _p(hv0), _p(clock0), _p(o), _p(hk), _p(hv), _p(clock),
+                  B, T, H, K, V, float(q_eps), float(k_eps), float(scale), _lib.stream())
+    return o, ((hk, hv, clock) if output_final_state else None)
+
+
 def chunk_cyfa(
     q,
     k,
@@ -208,6 +237,10 @@ def chunk_cyfa(
     tensors must live on a CUDA device.  ``chunk_size`` keeps its meaning for
     padding semantics; the kernels tile time in blocks of 128 tokens, which
     gives the same result (the chunk size is a scheduling choice).
+
+    bf16 q/k/v run the tcgen05 kernels (bf16 operands, fp32 accumulation) with
+    gradients.  fp32 q/k/v run in fp32 throughout (``cyfa_chunk_fwd_f32``),
+    inference only: with tracked gradients they raise NotImplementedError.
     """
     if cu_seqlens is not None:
         raise NotImplementedError("packed layout requires native segment dispatch")
@@ -223,11 +256,16 @@ def chunk_cyfa(
         raise ValueError(f"head dims must be 128 or 256, got K={K} V={V}")
     if chunk_size <= 0:
         raise ValueError("chunk_size must be positive")
-    out_dtype = q.dtype
     sc = K ** -0.5 if scale is None else float(scale)
     hk0 = hv0 = clock0 = None
     if initial_state is not None:
         hk0, hv0, clock0 = (_contig(x, torch.float32) for x in initial_state)
+    if q.dtype == torch.float32:
+        return _chunk_cyfa_f32(q, k, v, g, delta, beta, readout, q_norm_weight, k_norm_weight,
+                               q_norm_eps, k_norm_eps, sc, hk0, hv0, clock0, output_final_state)
+    if q.dtype != torch.bfloat16:
+        raise ValueError(f"q/k/v must be bfloat16 or float32, got {q.dtype}")
+    out_dtype = q.dtype
     o, hk, hv, clock = ChunkCyfaFunction.apply(
         _contig(q, torch.bfloat16), _contig(k, torch.bfloat16), _contig(v, torch.bfloat16),
         _contig(g, torch.float32), _contig(delta, torch.float32), _contig(beta, torch.float32),

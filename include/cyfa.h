@@ -87,6 +87,23 @@ int cyfa_decode_step(const void* q, const void* k, const void* v, const float* g
                      int K, int V, int dtype, float q_eps, float k_eps, float scale,
                      void* stream);
 
+/* fp32 chunk forward (inference): the whole chunk_cyfa forward for fp32 inputs,
+ * computed in fp32 throughout as the token recurrence (one CTA per (b, h) runs
+ * the decode step over its T tokens), so it equals the reference's generic fp32
+ * chunkwise path up to summation order.
+ * Replaces: chunk_cyfa with fp32 q/k/v, cyclic_flow_attention/ops/chunk.py:136-161
+ * (_scalar_la) and :300-331 (rotation, softmax, table), final state :346-352.
+ * q,k [B,T,H,K], v [B,T,H,V], g/delta/beta [B,T,H] f32 contiguous; table
+ * [H,127,128] f32; hk0/hv0/clock0 may be NULL (zero state); o [B,T,H,V] f32;
+ * hk [B,H,K,128], hv [B,H,128,V], clock [B,H] receive the final state.
+ * K, V in {128, 256}.  No gradients: the fp32 training path is not built. */
+int cyfa_chunk_fwd_f32(const float* q, const float* k, const float* v, const float* g,
+                       const float* delta, const float* beta, const float* table,
+                       const float* q_norm_weight, const float* k_norm_weight, const float* hk0,
+                       const float* hv0, const float* clock0, float* o, float* hk, float* hv,
+                       float* clock, int B, int T, int H, int K, int V, float q_eps, float k_eps,
+                       float scale, void* stream);
+
 /* ---------------------------------------------------------------- forward prep
  * Gate layout + clock scan + in-tile log2 gate cumsum.
  * Replaces: head_gates (ops/utils.py:434-492), ClockScan (:229-302),
@@ -299,7 +316,9 @@ int cyfa_gated_norm_bias_bwd(const void* x, const void* gate, const void* gate_b
  * The first call on each device looks up that array's device address
  * (cudaGetSymbolAddress); make the first call before any stream capture.  All
  * calls share the array: each call overwrites what it reads, but calls whose
- * kernels overlap on the GPU race.  Calls no allocator. */
+ * kernels overlap on the GPU race.  The looked-up address is kept for the life of
+ * the process: do not call it again on a device after cudaDeviceReset (or any
+ * other reset of that device's primary context).  Calls no allocator. */
 int cyfa_gated_norm_bwd_static(const void* x, const void* gate, const float* w, float scale,
                                const float* rstd, const void* dy, void* dx, void* dgate,
                                float* dw, int rows, int D, void* stream);

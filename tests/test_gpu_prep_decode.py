@@ -109,6 +109,33 @@ def test_decode_fp32_inputs(L):
     assert rel_l2(hv, ref_state[1]) < F32_TOL
 
 
+def test_decode_inplace_matches_out_of_place(L):
+    """hk/hv/clock outputs aliased to their inputs (the graphed decoder's static
+    cache) give bitwise the same steps as separate outputs, over many (b, h) and
+    several repeated calls (the clock is read by every warp before it is stored)."""
+    B, H, K, V = 64, 8, 256, 256
+    q, k, v, g, delta, beta, readout, qw, kw, state = _decode_inputs(B, H, K, V, 21)
+    table = O.readout_table(readout).float().cuda()
+    ins = [x.to(torch.bfloat16).contiguous().cuda() for x in (q, k, v)] + \
+        [x.contiguous().cuda() for x in (g, delta, beta)] + [table, qw.cuda(), kw.cuda()]
+    a = [x.contiguous().cuda() for x in state]          # in place
+    b = [x.contiguous().cuda() for x in state]          # out of place, ping-pong
+    b2 = [torch.empty_like(x) for x in b]
+    out_a = torch.empty(B, 1, H, V, device="cuda", dtype=torch.bfloat16)
+    out_b = torch.empty_like(out_a)
+    for _ in range(6):
+        L.call("cyfa_decode_step", *[L.ptr(x) for x in ins + a + a + [out_a]], B, H, K, V, 0,
+               1e-6, 1e-6, K ** -0.5, L.stream())
+        L.call("cyfa_decode_step", *[L.ptr(x) for x in ins + b + b2 + [out_b]], B, H, K, V, 0,
+               1e-6, 1e-6, K ** -0.5, L.stream())
+        b, b2 = b2, b
+        torch.cuda.synchronize()
+        assert torch.equal(out_a, out_b)
+        for x, y in zip(a, b):
+            assert torch.equal(x, y)
+    assert L.device_error() == 0
+
+
 @pytest.mark.parametrize("T", [1, 100, 128, 300])
 def test_gates_fwd(L, T):
     B, H = 2, 3
