@@ -187,6 +187,24 @@ def modal_readout(raw, c, s, table):
     return rotate(coeff, c, s, negative=True)
 
 
+class _RoundBf16(torch.autograd.Function):
+    """Rounds to bf16 in the forward and passes the gradient straight through:
+    the value a bf16 tensor stored by the reference's bf16 path holds, with the
+    gradient its backward formulas use."""
+
+    @staticmethod
+    def forward(ctx, x):
+        return x.to(torch.bfloat16).to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        return g
+
+
+def _rp(x, on):
+    return _RoundBf16.apply(x) if on else x
+
+
 def _pad_time(x, padding):
     if not padding:
         return x
@@ -198,14 +216,23 @@ def _pad_time(x, padding):
 def chunk_cyfa(
     q, k, v, g, delta, beta, readout, q_norm_weight, k_norm_weight,
     q_norm_eps=1e-6, k_norm_eps=1e-6, scale=None, initial_state=None,
-    output_final_state=False, chunk_size=64, dtype=None,
+    output_final_state=False, chunk_size=64, dtype=None, bf16_points=False,
 ):
     """Chunkwise CyFA, generic path (ops/chunk.py:164-353).
 
     q,k [B,T,H,K], v [B,T,H,V], g/delta/beta [B,T,H], readout [H,M-1,M-1].
     Computes in ``dtype`` (default: q's floating dtype).  Returns (o [B,T,H,V],
     (hk [B,H,K,M], hv [B,H,M,V], clock [B,H]) or None).
+
+    ``bf16_points`` rounds to bf16 (straight-through gradient) the tensors the
+    reference's bf16 path stores in bf16: the normalised q/k (qk_norm.py output
+    dtype), the write vector (ops/chunk.py:279, ops/utils.py:575), the pass-1
+    output raw (``round_output``, chunk.py:316-319), the rotated z, the table,
+    the probabilities and the weights (utils.py:804-853, chunk.py:324-331), and
+    the output.  It measures how far those rounding points alone move a result:
+    the conditioning of each gradient under bf16 storage.
     """
+    rp = bf16_points
     dt = dtype or (q.dtype if q.dtype in (torch.float32, torch.float64) else torch.float32)
     q, k, v, g, delta, beta = (x.to(dt) for x in (q, k, v, g, delta, beta))
     B, T, H, K = q.shape
@@ -214,8 +241,8 @@ def chunk_cyfa(
     C = chunk_size
     padding = (-T) % C  # ops/chunk.py:198-207
     q, k, v, g, delta, beta = (_pad_time(x, padding) for x in (q, k, v, g, delta, beta))
-    q = head_rmsnorm(q, q_norm_weight.to(dt), q_norm_eps)  # chunk.py:226
-    k = head_rmsnorm(k, k_norm_weight.to(dt), k_norm_eps)  # chunk.py:227
+    q = _rp(head_rmsnorm(q, q_norm_weight.to(dt), q_norm_eps), rp)  # chunk.py:226
+    k = _rp(head_rmsnorm(k, k_norm_weight.to(dt), k_norm_eps), rp)  # chunk.py:227
     v = v.permute(0, 2, 1, 3)
     g, d, beta = (x.permute(0, 2, 1) for x in (g, delta, beta))  # head_gates, chunk.py:243
     if initial_state is None:
@@ -226,12 +253,19 @@ def chunk_cyfa(
         hk, hv, clock = (x.to(dt) for x in initial_state)
     lam = clock_scan(d, clock)  # chunk.py:254-256
     write, c, s = write_vector(lam, beta, M)  # chunk.py:265-279
+    write = _rp(write, rp)
     sc = K ** -0.5 if scale is None else scale
     raw, hkt = scalar_la_chunk(q, k, write, g, hk, C, sc)  # pass 1, chunk.py:316-319
     table = readout_table(readout, dt)  # chunk.py:320
-    weights = modal_readout(raw, c, s, table)  # chunk.py:324-331
+    if rp:
+        z = _rp(rotate(_rp(raw, rp), c, s), rp)
+        tb = _rp(table, rp)
+        probs = _rp(torch.softmax(torch.einsum("bhtm,hrm->bhtr", z, tb), dim=-1), rp)
+        weights = _rp(rotate(torch.einsum("bhtr,hrm->bhtm", probs, tb), c, s, negative=True), rp)
+    else:
+        weights = modal_readout(raw, c, s, table)  # chunk.py:324-331
     out, hvt = scalar_la_chunk(weights, write, v, g, hv, C, 1.0)  # pass 2, chunk.py:338
-    out = out.permute(0, 2, 1, 3)[:, :T]
+    out = _rp(out.permute(0, 2, 1, 3)[:, :T], rp)
     state = None
     if output_final_state:  # chunk.py:347-352
         final_clock = d.sum(-1)
@@ -344,22 +378,25 @@ def gated_rmsnorm(x, weight, eps, gate=None):
 
 
 def cyfa_layer(params, x, H, head_k_dim, head_v_dim, num_slots=128, eps=1e-6,
-               chunk_size=64, conv=True):
+               chunk_size=64, conv=True, bf16_points=False):
     """CyclicFlowAttention.execute training path (layers/cyfa.py:299-357).
 
     ``params`` maps the reference's parameter names (q_proj.weight, ...) to
-    tensors.  x [B,T,hidden].  Returns y [B,T,hidden].
+    tensors.  x [B,T,hidden].  Returns y [B,T,hidden].  ``bf16_points`` as in
+    ``chunk_cyfa``, plus the bf16 activations between the layer's GEMMs
+    (projection outputs, convolution outputs, gate input).
     """
+    rp = bf16_points
     dt = x.dtype
     P = {n: t.to(dt) for n, t in params.items()}
     B, T, _ = x.shape
-    q = x @ P["q_proj.weight"].T
-    k = x @ P["k_proj.weight"].T
-    v = x @ P["v_proj.weight"].T
+    q = _rp(x @ P["q_proj.weight"].T, rp)
+    k = _rp(x @ P["k_proj.weight"].T, rp)
+    v = _rp(x @ P["v_proj.weight"].T, rp)
     if conv:
-        q = short_convolution(q, P["q_conv1d.weight"])[0]
-        k = short_convolution(k, P["k_conv1d.weight"])[0]
-        v = short_convolution(v, P["v_conv1d.weight"])[0]
+        q = _rp(short_convolution(q, P["q_conv1d.weight"])[0], rp)
+        k = _rp(short_convolution(k, P["k_conv1d.weight"])[0], rp)
+        v = _rp(short_convolution(v, P["v_conv1d.weight"])[0], rp)
     q = q.reshape(B, T, H, head_k_dim)
     k = k.reshape(B, T, H, head_k_dim)
     v = v.reshape(B, T, H, head_v_dim)
@@ -368,8 +405,9 @@ def cyfa_layer(params, x, H, head_k_dim, head_v_dim, num_slots=128, eps=1e-6,
     delta = torch.sigmoid(x.detach() @ P["d_proj.weight"].T + P["d_proj.bias"])
     beta = torch.sigmoid(x @ P["b_proj.weight"].T + P["b_proj.bias"])
     o, _ = chunk_cyfa(q, k, v, g, delta, beta, P["readout"], P["q_norm.weight"],
-                      P["k_norm.weight"], eps, eps, chunk_size=chunk_size, dtype=dt)
-    gate = (x @ P["g_proj.0.weight"].T) @ P["g_proj.1.weight"].T + P["g_proj.1.bias"]
+                      P["k_norm.weight"], eps, eps, chunk_size=chunk_size, dtype=dt,
+                      bf16_points=rp)
+    gate = _rp(x @ P["g_proj.0.weight"].T, rp) @ P["g_proj.1.weight"].T + P["g_proj.1.bias"]
     gate = gate.reshape(B, T, H, head_v_dim)
     o = gated_rmsnorm(o * (num_slots - 1), P["o_norm.weight"], eps, gate)
     return o.reshape(B, T, H * head_v_dim) @ P["o_proj.weight"].T

@@ -13,13 +13,16 @@
   128 slots, T = 2048 (one sequence of the B = 8 batch).
 
 Tolerances: bf16 outputs and gradients rel-L2 <= 1e-2 of the fp32 oracle, fp32
-paths <= 1e-4.  Gate-type gradients keep looser bounds, each justified by
-conditioning: the op's dg / ddelta / dbeta are sums of cancelling bf16 products
-(2e-2, the reference benchmark's own gate for them, benchmarks/core.py:576-580);
-the layer's per-head gate scalars and gate projections are token sums of those
-(test_oracle_gate_param_conditioning: one bf16 rounding of the oracle's own
-inputs moves them by 1-3 %).  Every per-tensor error is printed, and appended
-as one JSON line per case to the file named by CYFA_PARITY_OUT when it is set.
+paths <= 1e-4.  The gate-type gradients that are long sums of cancelling terms
+(the op's ddelta, a reverse cumsum of the clock gradient over all T tokens; the
+layer's per-head gate scalars and gate projections, token sums of the gate
+gradients) are ill-conditioned under bf16 storage: rounding only the tensors
+the reference's own bf16 path stores in bf16 (the oracle's ``bf16_points``)
+already moves them by percents (d_proj.bias by ~20 % at c3).  For those the
+bound is max(1e-2, 3 x that shift), the shift computed in the test on the same
+inputs, so the GPU result must stay within a small multiple of the reference's
+own rounding.  Every per-tensor error and shift is printed, and appended as one
+JSON line per case to the file named by CYFA_PARITY_OUT when it is set.
 """
 
 import json
@@ -35,18 +38,27 @@ pytestmark = pytest.mark.gpu
 
 BF16_TOL = 1e-2
 F32_TOL = 1e-4
-OP_GATE_TOL = 2e-2
+COND_FACTOR = 3.0
+# op gradient that is a reverse cumsum over the whole sequence
+OP_COND = ("ddelta",)
 # layer parameters whose gradients are token sums of gate gradients
-LAYER_GATE_TOL = {"A_log": 1e-1, "dt_bias": 1e-1, "d_proj.bias": 1e-1, "b_proj.bias": 1e-1,
-                  "a_proj.weight": 5e-2, "d_proj.weight": 5e-2, "b_proj.weight": 5e-2}
+LAYER_COND = ("A_log", "dt_bias", "d_proj.bias", "d_proj.weight", "b_proj.bias",
+              "b_proj.weight", "a_proj.weight")
 
 
-def _record(case, errs):
+def _record(case, errs, shift=None):
     print(case, {k: float(f"{v:.3g}") for k, v in errs.items()})
+    if shift:
+        print("  bf16-storage shift", {k: float(f"{v:.3g}") for k, v in shift.items()})
     path = os.environ.get("CYFA_PARITY_OUT")
     if path:
         with open(path, "a") as f:
-            f.write(json.dumps({"case": case, "rel_l2": errs}) + "\n")
+            f.write(json.dumps({"case": case, "rel_l2": errs, "bf16_points_shift": shift})
+                    + "\n")
+
+
+def _cond_tol(shift):
+    return max(BF16_TOL, COND_FACTOR * shift)
 
 
 @pytest.fixture(scope="module")
@@ -175,14 +187,18 @@ def test_c2_op_forward_backward(pkg):
     ref = [x.float().requires_grad_(True) for x in ins]
     ref_o, ref_s = O.chunk_cyfa(*ref, output_final_state=True, dtype=torch.float32)
     (ref_o * do.float()).sum().backward()
+    rnd = [x.float().requires_grad_(True) for x in ins]
+    rnd_o, _ = O.chunk_cyfa(*rnd, dtype=torch.float32, bf16_points=True)
+    (rnd_o * do.float()).sum().backward()
     names = ["q", "k", "v", "g", "delta", "beta", "readout", "q_norm_weight", "k_norm_weight"]
     errs = {"o": rel_l2(o, ref_o), "hk": rel_l2(st[0], ref_s[0]), "hv": rel_l2(st[1], ref_s[1]),
             "clock": rel_l2(st[2], ref_s[2])}
     errs.update({"d" + n: rel_l2(a.grad, b.grad) for n, a, b in zip(names, dev, ref)})
-    _record("c2 op fwd+bwd H4 T4096 K256 V256", errs)
+    shift = {"d" + n: rel_l2(a.grad, b.grad) for n, a, b in zip(names, rnd, ref)}
+    _record("c2 op fwd+bwd H4 T4096 K256 V256", errs, shift)
     for n, e in errs.items():
         tol = F32_TOL if n == "clock" else (
-            OP_GATE_TOL if n in ("dg", "ddelta", "dbeta") else BF16_TOL)
+            _cond_tol(shift[n]) if n in OP_COND else BF16_TOL)
         assert e < tol, (n, e)
     from cyclic_flow_attention import _lib
 
@@ -213,8 +229,12 @@ def test_c3_layer_forward_backward(pkg):
     xr = x.float().requires_grad_(True)
     yr = O.cyfa_layer(params, xr, H, hd, hd)
     (yr * dy.float()).sum().backward()
+    rparams = {n: p.detach().clone().requires_grad_(True) for n, p in params.items()}
+    (O.cyfa_layer(rparams, x.float(), H, hd, hd, bf16_points=True) * dy.float()).sum().backward()
     errs = {"y": rel_l2(y, yr), "x": rel_l2(xg.grad, xr.grad)}
     errs.update({n: rel_l2(p.grad, params[n].grad) for n, p in m.named_parameters()})
-    _record("c3 layer fwd+bwd hidden1024 H4x256 T2048", errs)
+    shift = {n: rel_l2(rparams[n].grad, params[n].grad) for n in LAYER_COND}
+    _record("c3 layer fwd+bwd hidden1024 H4x256 T2048", errs, shift)
     for n, e in errs.items():
-        assert e < LAYER_GATE_TOL.get(n, BF16_TOL), (n, e)
+        tol = _cond_tol(shift[n]) if n in LAYER_COND else BF16_TOL
+        assert e < tol, (n, e)

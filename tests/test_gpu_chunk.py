@@ -1,9 +1,10 @@
 """GPU parity of chunk_cyfa (forward and backward) against the CPU oracle.
 
 Tolerances: bf16 outputs and gradients rel-L2 <= 1e-2 of
-the fp32 oracle; the fp32 clock <= 1e-4.  Gate gradients (dg, ddelta, dbeta)
-are reductions over bf16 products and get 2e-2, as in the reference's own
-benchmark gate (benchmarks/core.py:576-580).
+the fp32 oracle; the fp32 clock <= 1e-4.  The gate gradients (dg, ddelta,
+dbeta, dclock0) are sums of cancelling bf16 products; each gets max(1e-2, 3 x
+the shift that rounding only the reference's own bf16 storage points produces
+in the oracle on the same inputs (``bf16_points``)).
 """
 
 import pytest
@@ -15,8 +16,8 @@ from oracle import cyfa_oracle as O
 pytestmark = pytest.mark.gpu
 
 BF16_TOL = 1e-2
-GATE_TOL = 2e-2
 F32_TOL = 1e-4
+COND_FACTOR = 3.0
 
 
 @pytest.fixture(scope="module")
@@ -135,16 +136,30 @@ def test_chunk_backward(ops, B, T, H, K, V, with_state):
     if dst is not None:
         rl = rl + sum((a * b).sum() for a, b in zip(rs, dst))
     rl.backward()
+    # the same oracle with the reference's bf16 storage points: the conditioning
+    rnd_in = [x.float().clone().requires_grad_(True) for x in ins]
+    rnd_st = None if state is None else tuple(x.clone().requires_grad_(True) for x in state)
+    qo, qs = O.chunk_cyfa(*rnd_in, initial_state=rnd_st, output_final_state=True,
+                          dtype=torch.float32, bf16_points=True)
+    ql = (qo * do).sum()
+    if dst is not None:
+        ql = ql + sum((a * b).sum() for a, b in zip(qs, dst))
+    ql.backward()
+
+    def cond(a, b):
+        return max(BF16_TOL, COND_FACTOR * rel_l2(a.grad, b.grad))
+
     names = ["q", "k", "v", "g", "delta", "beta", "readout", "q_norm_weight", "k_norm_weight"]
-    tols = [BF16_TOL, BF16_TOL, BF16_TOL, GATE_TOL, GATE_TOL, GATE_TOL, BF16_TOL, BF16_TOL,
-            BF16_TOL]
+    tols = [BF16_TOL, BF16_TOL, BF16_TOL] + [cond(rnd_in[i], ref_in[i]) for i in (3, 4, 5)] + \
+        [BF16_TOL, BF16_TOL, BF16_TOL]
     errs = {n: rel_l2(a.grad, b.grad) for n, a, b in zip(names, dev, ref_in)}
     if st is not None:
         for n, a, b in zip(["hk0", "hv0", "clock0"], st, ref_st):
             errs[n] = rel_l2(a.grad, b.grad)
-        tols += [BF16_TOL, BF16_TOL, GATE_TOL]
+        tols += [BF16_TOL, BF16_TOL, cond(rnd_st[2], ref_st[2])]
         names += ["hk0", "hv0", "clock0"]
-    print("chunk grad errors", B, T, H, K, V, with_state, {k: round(v, 5) for k, v in errs.items()})
+    print("chunk grad errors", B, T, H, K, V, with_state, {k: round(v, 5) for k, v in errs.items()},
+          "tolerances", [round(t, 4) for t in tols])
     bad = {n: e for n, t, (n2, e) in zip(names, tols, errs.items()) if e >= t}
     assert not bad, f"gradient errors over tolerance: {bad} (all: {errs})"
     from cyclic_flow_attention import _lib
