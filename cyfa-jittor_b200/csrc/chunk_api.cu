@@ -351,7 +351,7 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   // ================= pass 2 (queries = weights, keys = w, values = v)
   {
     ScanParams p{d.BH, d.H, d.TP, d.NT, 128, d.V, kRows2D, kPublic4D, s.G, g->dhv, w.h2, g->dhv0,
-                 1.f, nullptr, w.bpart2};
+                 1.f, nullptr, w.bpart2, a->hv};
     CUtensorMap m_ff2;
     if ((rc = tmap_2d(&m_ff2, s.s2_fin, uint64_t(d.BH) * 128, d.V, 128))) return rc;
     CYFA_LAUNCH("state_scan_bwd", st,
@@ -401,7 +401,7 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   // ================= pass 1 (queries = q^, keys = k^, values = w)
   {
     ScanParams p{d.BH, d.H, d.TP, d.NT, d.K, 128, kRows2D, kRows2D, s.G, g->dhk, w.h1, g->dhk0,
-                 a->scale, nullptr, w.bpart1};
+                 a->scale, nullptr, w.bpart1, a->hk};
     CUtensorMap m_f1, m_ff1;
     if ((rc = tmap_2d(&m_f1, s.s1, uint64_t(d.BH) * d.NT * d.K, 128, 128))) return rc;
     if ((rc = tmap_2d(&m_ff1, s.s1_fin, uint64_t(d.BH) * d.K, 128, 128))) return rc;

@@ -76,6 +76,7 @@ struct ScanParams {
   float scale;              // reverse: scale of dO
   __nv_bfloat16* last_bf;   // forward: bf16 copy of the final state [BH, DK, DV], or null
   float* bpart;             // reverse: [BH, NT, nsub, 4] partial boundary terms
+  const float* final_f32;   // reverse: the forward final state [BH, DK, DV] fp32, or null
 };
 
 // Ring of the scan: forward stages hold the K tile (32 KiB) and the V tile
@@ -321,7 +322,18 @@ __global__ void __launch_bounds__(kScanThreads, 1)
         const int s = idx % kScanStages;
         got = got && __all_sync(0xffffffffu, mbar_wait(&full[s], (idx / kScanStages) & 1));
         float dot = 0.f;
-        if (got) {
+        if (got && j + 1 == NT && p.final_f32) {
+          // the last tile pairs with the final state, which exists in fp32: its
+          // boundary term cancels against the key rows' dots of the whole tile, so
+          // the bf16 copy's rounding would dominate it when the final state's
+          // adjoint is large
+          const float4* fs = reinterpret_cast<const float4*>(p.final_f32 + row_off);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float4 x = fs[i];
+            dot += x.x * S[4 * i] + x.y * S[4 * i + 1] + x.z * S[4 * i + 2] + x.w * S[4 * i + 3];
+          }
+        } else if (got) {
           const uint32_t fb = smem_u32(smem + s * kScanStageBytes + 49152);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {

@@ -379,6 +379,28 @@ int cyfa_bucket_gather(const cyfa_bucket_piece* pieces, int count, float* flat, 
 int cyfa_bucket_scatter(const cyfa_bucket_piece* pieces, int count, const float* flat,
                         float scale, void* stream);
 
+/* ---------------------------------------------------------------- optimizer
+ * AdamW with fp32 master weights and moments.  Replaces: AdamW.step,
+ * training/optim.py:96-124.  The masters, moments and the (all-reduced,
+ * accumulated) gradient live in flat fp32 buffers; `params` lists each
+ * parameter tensor (bf16 or f32) with its element offset into those buffers
+ * (a multiple of 8; every pointer 16-byte aligned).  One launch per 64
+ * parameters updates m, v and the master in the reference's formula order and
+ * writes the master rounded to the parameter's dtype; `step` >= 1 is the
+ * update count used for the bias corrections. */
+int cyfa_adamw_step(const cyfa_bucket_piece* params, int count, float* master, float* m, float* v,
+                    const float* grad, float lr, float beta1, float beta2, float eps,
+                    float weight_decay, int step, void* stream);
+
+/* Gradient clipping by the global L2 norm.  Replaces: AdamW.clip_grad_norm,
+ * training/optim.py:74-89.  grad [n] f32 is scaled in place by
+ * min(max_norm / (norm + 1e-6), 1); the norm is written to norm_out (device
+ * f32, may be NULL).  Sums run in a fixed order (deterministic).  work:
+ * cyfa_grad_clip_work_bytes() bytes of device memory. */
+size_t cyfa_grad_clip_work_bytes(void);
+int cyfa_grad_clip(float* grad, long long n, float max_norm, float* norm_out, void* work,
+                   size_t work_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -130,11 +130,14 @@ def head_rmsnorm(x, w, eps):
     return (xf * rs * w).permute(0, 2, 1, 3)
 
 
-def scalar_la_chunk(q, k, v, g, initial, C, scale=1.0):
+def scalar_la_chunk(q, k, v, g, initial, C, scale=1.0, bf16_points=False):
     """Chunkwise scalar-gated linear attention (ops/chunk.py:136-161).
 
     q,k [B,H,T,K], v [B,H,T,V], g [B,H,T] (natural-log decay), initial
     [B,H,K,V].  Returns (out [B,H,T,V], final [B,H,K,V]).  T % C == 0.
+    ``bf16_points`` rounds what the reference's bf16 path rounds here: the
+    decayed values of the state update (``v_tail``, :147), the chunk states read
+    by the inter-chunk term (``states.cast``, :150) and the masked scores (:155).
     """
     B, H, T, K = q.shape
     V = v.shape[-1]
@@ -145,7 +148,7 @@ def scalar_la_chunk(q, k, v, g, initial, C, scale=1.0):
     gc = g.reshape(B, H, N, C).cumsum(-1)
     last = gc[..., -1]
     tails = (last.unsqueeze(-1) - gc).exp()
-    updates = kc.transpose(-1, -2) @ (vc * tails.unsqueeze(-1))
+    updates = kc.transpose(-1, -2) @ _rp(vc * tails.unsqueeze(-1), bf16_points)
     decays = last.exp()
     states = []
     h = initial
@@ -153,12 +156,13 @@ def scalar_la_chunk(q, k, v, g, initial, C, scale=1.0):
         states.append(h)
         h = h * decays[:, :, n, None, None] + updates[:, :, n]
     states = torch.stack(states, dim=2)
-    inter = (qc @ states) * gc.exp().unsqueeze(-1)
+    inter = (qc @ _rp(states, bf16_points)) * gc.exp().unsqueeze(-1)
     scores = qc @ kc.transpose(-1, -2)
     i = torch.arange(C)
     mask = i.reshape(C, 1) >= i.reshape(1, C)
     decay = (gc.unsqueeze(-1) - gc.unsqueeze(-2)).masked_fill(~mask, 0.0).exp()
-    scores = torch.where(mask, scores * decay, torch.zeros((), dtype=scores.dtype))
+    scores = _rp(torch.where(mask, scores * decay, torch.zeros((), dtype=scores.dtype)),
+                 bf16_points)
     intra = scores @ vc
     out = (inter + intra) * scale
     return out.reshape(B, H, T, V), h
@@ -228,8 +232,9 @@ def chunk_cyfa(
     reference's bf16 path stores in bf16: the normalised q/k (qk_norm.py output
     dtype), the write vector (ops/chunk.py:279, ops/utils.py:575), the pass-1
     output raw (``round_output``, chunk.py:316-319), the rotated z, the table,
-    the probabilities and the weights (utils.py:804-853, chunk.py:324-331), and
-    the output.  It measures how far those rounding points alone move a result:
+    the probabilities and the weights (utils.py:804-853, chunk.py:324-331), the
+    decayed values, chunk states and scores of both passes (``scalar_la_chunk``),
+    and the output.  It measures how far those rounding points alone move a result:
     the conditioning of each gradient under bf16 storage.
     """
     rp = bf16_points
@@ -255,7 +260,7 @@ def chunk_cyfa(
     write, c, s = write_vector(lam, beta, M)  # chunk.py:265-279
     write = _rp(write, rp)
     sc = K ** -0.5 if scale is None else scale
-    raw, hkt = scalar_la_chunk(q, k, write, g, hk, C, sc)  # pass 1, chunk.py:316-319
+    raw, hkt = scalar_la_chunk(q, k, write, g, hk, C, sc, rp)  # pass 1, chunk.py:316-319
     table = readout_table(readout, dt)  # chunk.py:320
     if rp:
         z = _rp(rotate(_rp(raw, rp), c, s), rp)
@@ -264,7 +269,7 @@ def chunk_cyfa(
         weights = _rp(rotate(torch.einsum("bhtr,hrm->bhtm", probs, tb), c, s, negative=True), rp)
     else:
         weights = modal_readout(raw, c, s, table)  # chunk.py:324-331
-    out, hvt = scalar_la_chunk(weights, write, v, g, hv, C, 1.0)  # pass 2, chunk.py:338
+    out, hvt = scalar_la_chunk(weights, write, v, g, hv, C, 1.0, rp)  # pass 2, chunk.py:338
     out = _rp(out.permute(0, 2, 1, 3)[:, :T], rp)
     state = None
     if output_final_state:  # chunk.py:347-352
@@ -378,13 +383,15 @@ def gated_rmsnorm(x, weight, eps, gate=None):
 
 
 def cyfa_layer(params, x, H, head_k_dim, head_v_dim, num_slots=128, eps=1e-6,
-               chunk_size=64, conv=True, bf16_points=False):
+               chunk_size=64, conv=True, bf16_points=False, taps=None):
     """CyclicFlowAttention.execute training path (layers/cyfa.py:299-357).
 
     ``params`` maps the reference's parameter names (q_proj.weight, ...) to
     tensors.  x [B,T,hidden].  Returns y [B,T,hidden].  ``bf16_points`` as in
     ``chunk_cyfa``, plus the bf16 activations between the layer's GEMMs
-    (projection outputs, convolution outputs, gate input).
+    (projection outputs, convolution outputs, gate input).  ``taps``, a dict,
+    receives the gate tensors g, delta, beta and the gate pre-activations
+    (a + dt_bias, the d and b projections), with their gradients retained.
     """
     rp = bf16_points
     dt = x.dtype
@@ -402,8 +409,16 @@ def cyfa_layer(params, x, H, head_k_dim, head_v_dim, num_slots=128, eps=1e-6,
     v = v.reshape(B, T, H, head_v_dim)
     a = x @ P["a_proj.weight"].T + P["dt_bias"]
     g = -P["A_log"].exp() * torch.nn.functional.softplus(a)
-    delta = torch.sigmoid(x.detach() @ P["d_proj.weight"].T + P["d_proj.bias"])
-    beta = torch.sigmoid(x @ P["b_proj.weight"].T + P["b_proj.bias"])
+    dpre = x.detach() @ P["d_proj.weight"].T + P["d_proj.bias"]
+    bpre = x @ P["b_proj.weight"].T + P["b_proj.bias"]
+    delta = torch.sigmoid(dpre)
+    beta = torch.sigmoid(bpre)
+    if taps is not None:
+        for name, t in (("a", a), ("g", g), ("dpre", dpre), ("bpre", bpre), ("delta", delta),
+                        ("beta", beta)):
+            if t.requires_grad:
+                t.retain_grad()
+            taps[name] = t
     o, _ = chunk_cyfa(q, k, v, g, delta, beta, P["readout"], P["q_norm.weight"],
                       P["k_norm.weight"], eps, eps, chunk_size=chunk_size, dtype=dt,
                       bf16_points=rp)

@@ -7,8 +7,9 @@ bf16 tolerance 1e-2 is used here)."""
 import pytest
 import torch
 
-from gpu_util import rel_l2
+from gpu_util import gate_param_tolerances, rel_l2
 from oracle import cyfa_oracle as O
+
 
 pytestmark = pytest.mark.gpu
 
@@ -45,20 +46,12 @@ def test_layer_forward_backward(Layer, B, T, hidden, H, hd):
     params = {n: p.detach().float().cpu().clone().requires_grad_(True)
               for n, p in m.named_parameters()}
     xr = x.float().requires_grad_(True)
-    yr = O.cyfa_layer(params, xr, H, hd, hd)
+    taps = {}
+    yr = O.cyfa_layer(params, xr, H, hd, hd, taps=taps)
     (yr * dy).sum().backward()
     errs = {"y": rel_l2(y, yr), "x": rel_l2(xg.grad, xr.grad)}
     errs.update({n: rel_l2(p.grad, params[n].grad) for n, p in m.named_parameters()})
-    # Tolerances: 1e-2 for the output and every gradient, except the gate/clock
-    # parameters, token sums of cancelling gate gradients: max(1e-2, 3 x the shift
-    # that rounding only the reference's own bf16 storage points produces in the
-    # oracle on the same inputs (bf16_points); test_oracle_gate_param_conditioning
-    # shows the same ill-conditioning under a bf16-sized input perturbation).
-    gate = ("A_log", "dt_bias", "d_proj.bias", "d_proj.weight", "b_proj.bias", "b_proj.weight",
-            "a_proj.weight")
-    rparams = {n: p.detach().clone().requires_grad_(True) for n, p in params.items()}
-    (O.cyfa_layer(rparams, x.float(), H, hd, hd, bf16_points=True) * dy).sum().backward()
-    tols = {n: max(1e-2, 3.0 * rel_l2(rparams[n].grad, params[n].grad)) for n in gate}
+    tols = gate_param_tolerances(taps, xr.detach(), params)
     print("layer errors", B, T, hidden, H, hd, {k: round(v, 5) for k, v in errs.items()},
           "gate tolerances", {k: round(v, 4) for k, v in tols.items()})
     for n, e in errs.items():
