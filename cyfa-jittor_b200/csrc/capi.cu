@@ -312,6 +312,22 @@ static int token_bwd_launch(const void* q, const void* k, const float* q_norm_we
 
 }  // namespace cyfa
 
+// Gate layout, clock scan and in-tile gate cumsum; `lengths` (or null) makes the
+// tokens past each sequence's length neutral (right padding).
+static int gates_fwd_launch(const float* g, const float* delta, const float* beta,
+                            const float* clock0, float* G, float* lam, float* beta_h,
+                            float* clock_out, int B, int T, int H, const int* lengths,
+                            void* stream) {
+  CYFA_REQUIRE(g && delta && beta && G && lam && beta_h, kNullPointer);
+  CYFA_REQUIRE(B > 0 && T > 0 && H > 0, kBadShape);
+  const int TP = (T + 127) / 128 * 128;
+  GatesParams p{g, delta, beta, clock0, G, lam, beta_h, clock_out, B, T, H, TP, lengths};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  CYFA_LAUNCH("gates_fwd", st,
+              launch_k(gates_fwd_kernel, dim3(B * H, (TP + 1023) / 1024), 1024, 0, st, p));
+  return launch_status();
+}
+
 extern "C" {
 
 int cyfa_version(void) { return 1; }
@@ -469,14 +485,8 @@ int cyfa_chunk_fwd_f32(const float* q, const float* k, const float* v, const flo
 int cyfa_gates_fwd(const float* g, const float* delta, const float* beta, const float* clock0,
                    float* G, float* lam, float* beta_h, float* clock_out, int B, int T, int H,
                    void* stream) {
-  CYFA_REQUIRE(g && delta && beta && G && lam && beta_h, kNullPointer);
-  CYFA_REQUIRE(B > 0 && T > 0 && H > 0, kBadShape);
-  const int TP = (T + 127) / 128 * 128;
-  GatesParams p{g, delta, beta, clock0, G, lam, beta_h, clock_out, B, T, H, TP};
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  CYFA_LAUNCH("gates_fwd", st,
-              launch_k(gates_fwd_kernel, dim3(B * H, (TP + 1023) / 1024), 1024, 0, st, p));
-  return launch_status();
+  return gates_fwd_launch(g, delta, beta, clock0, G, lam, beta_h, clock_out, B, T, H, nullptr,
+                          stream);
 }
 
 int cyfa_token_fwd(const void* q, const void* k, const float* q_norm_weight,

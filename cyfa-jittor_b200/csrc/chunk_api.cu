@@ -168,8 +168,8 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int rc;
 
-  rc = cyfa_gates_fwd(a->g, a->delta, a->beta, a->clock0, s.G, s.lam, s.beta_h, a->clock, d.B,
-                      d.T, d.H, stream);
+  rc = gates_fwd_launch(a->g, a->delta, a->beta, a->clock0, s.G, s.lam, s.beta_h, a->clock, d.B,
+                        d.T, d.H, a->lengths, stream);
   if (rc) return rc;
   rc = token_fwd_launch(a->q, a->k, a->q_norm_weight, a->k_norm_weight, s.lam, s.beta_h, s.qn,
                         s.kn, s.w, s.q_rs, s.k_rs, d.B, d.T, d.H, d.K, a->q_eps, a->k_eps,
@@ -448,7 +448,7 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
   if ((rc = launch_status())) return rc;
   GatesBwdParams gp{w.dG, ndg, (long long)slot, w.dlam_w, w.dlam_r, w.bpart1, w.bpart2, nsub1,
                     nsub2, w.dbeta_h, g->dclock, g->dg, g->ddelta, g->dbeta, g->dclock0, d.B, d.T,
-                    d.H, d.TP};
+                    d.H, d.TP, a->lengths};
   CYFA_LAUNCH("gates_bwd", st,
               (launch_k(gates_bwd_kernel, dim3(d.BH, (d.TP + 1023) / 1024), 1024, 0, st, gp)));
   return launch_status();

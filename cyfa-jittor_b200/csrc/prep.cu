@@ -70,6 +70,7 @@ struct GatesParams {
   float* beta_h;        // [B,H,TP]
   float* clock_out;     // [B,H] or null
   int B, T, H, TP;
+  const int* lengths;   // [B] valid tokens of each sequence (right padding), or null
 };
 
 // Block-wide scans of the gate kernels: 1024 threads = 32 warps cover 1024 tokens,
@@ -129,11 +130,13 @@ __global__ void __launch_bounds__(1024) gates_fwd_kernel(GatesParams p) {
   __shared__ float wsum[32];
   const size_t obase = size_t(bh) * p.TP;
   const int t = k * 1024 + threadIdx.x;
+  // tokens past a sequence's length are neutral, like the padding up to TP
+  const int Tb = p.lengths ? min(max(p.lengths[b], 0), p.T) : p.T;
   auto delta_at = [&](int tt) {
-    return tt < p.T ? p.delta[(size_t(b) * p.T + tt) * p.H + h] : 0.f;
+    return tt < Tb ? p.delta[(size_t(b) * p.T + tt) * p.H + h] : 0.f;
   };
   float gv = 0.f, dv = 0.f, bv = 0.f;
-  if (t < p.T) {
+  if (t < Tb) {
     const size_t i = (size_t(b) * p.T + t) * p.H + h;
     gv = p.g[i];
     dv = p.delta[i];
@@ -846,6 +849,7 @@ struct GatesBwdParams {
   float* dbeta;          // [B,T,H]
   float* dclock0;        // [B,H] or null
   int B, T, H, TP;
+  const int* lengths;    // [B] valid tokens (right padding), or null: zero gradients past it
 };
 
 // Grid (B*H, ceil(TP/1024)) as the forward: CTA (bh, k) handles token block k,
@@ -893,10 +897,12 @@ __global__ void __launch_bounds__(1024) gates_bwd_kernel(GatesBwdParams p) {
   scan1024<true>(later, wsum, &ltot);
   const float carry = __fadd_rn(p.dclock ? p.dclock[bh] : 0.f, ltot);
   if (t < p.T) {
+    // inputs past a sequence's length were replaced by neutral values: no gradient
+    const bool valid = !p.lengths || t < p.lengths[b];
     const size_t i = (size_t(b) * p.T + t) * p.H + h;
-    p.dg[i] = gs.tile;
-    p.ddelta[i] = __fadd_rn(carry, ls.block);
-    p.dbeta[i] = p.dbeta_h[base + t];
+    p.dg[i] = valid ? gs.tile : 0.f;
+    p.ddelta[i] = valid ? __fadd_rn(carry, ls.block) : 0.f;
+    p.dbeta[i] = valid ? p.dbeta_h[base + t] : 0.f;
   }
   if (k == 0 && threadIdx.x == 0 && p.dclock0) p.dclock0[bh] = __fadd_rn(carry, tot);
 }

@@ -199,9 +199,12 @@ class CyclicFlowAttention(nn.Module):
                 r += w.shape[0]
 
     def _fused_ok(self, x, cache, attention_mask):
+        # a right-padding mask runs fused when no gradient is taken (prefill):
+        # the masked gates make the padding neutral for the states and the
+        # clock; with gradients it runs the reference's masking on torch glue
         return (
             cache is None
-            and attention_mask is None
+            and (attention_mask is None or not torch.is_grad_enabled())
             and x.is_cuda
             and x.dtype == torch.bfloat16
             and self.q_proj.weight.dtype == torch.bfloat16
@@ -214,12 +217,22 @@ class CyclicFlowAttention(nn.Module):
             and (self.training or x.shape[1] > 1 or torch.is_grad_enabled())
         )
 
-    def _forward_fused(self, x, use_cache):
+    def _forward_fused(self, x, use_cache, attention_mask=None):
         """One packed q|k|v|g0|a|b|d projection with the short convolution and the
         gate activations on its columns (LayerFrontFunction), the CyFA op on the
         convolved q|k|v, the gated output norm with the gate's second linear, and
-        o_proj; the same math as the reference execute()."""
+        o_proj; the same math as the reference execute().
+
+        A right-padding ``attention_mask`` (1 for the first lengths[b] tokens of
+        row b) becomes per-row lengths for the op, which treats the later tokens
+        as neutral padding (g = delta = beta = 0, reference layers/cyfa.py:304-308,
+        326-328), and the convolution histories of the cache end at each row's
+        length (the reference's ShortConvolution with lengths, :144-181).  The
+        outputs at padded positions are not defined."""
         B, T, _ = x.shape
+        lengths = None
+        if attention_mask is not None:
+            lengths = attention_mask.to(torch.int32).sum(1).contiguous()
         H, K, V = self.num_heads, self.head_k_dim, self.head_v_dim
         g0 = self.g_proj[0]
         self._pack_front()
@@ -243,7 +256,7 @@ class CyclicFlowAttention(nn.Module):
         o, hk, hv, clock = ChunkCyfaPackedFunction.apply(
             qkv, H, K, V, g, delta, beta, self.readout, self.q_norm.weight.float(),
             self.k_norm.weight.float(), float(self.q_norm.eps), float(self.k_norm.eps), K ** -0.5,
-            tb)
+            tb, lengths)
         g1 = self.g_proj[1]
         y = GatedNormFunction.apply(o, gate_in, g1.weight, g1.bias, self.o_norm.weight,
                                     self.o_norm.eps, float(self.num_slots - 1), slot, (g1.weight,))
@@ -254,7 +267,17 @@ class CyclicFlowAttention(nn.Module):
             W = self.q_conv1d.width
             w_qkv = torch.cat([self.q_proj.weight, self.k_proj.weight, self.v_proj.weight])
             # conv histories: the last W-1 projected (pre-conv) rows of q, k and v
-            pre = F.linear(x[:, -(W - 1):], w_qkv) if W > 1 else x[:, :0]
+            # before each row's end (zeros before the sequence start)
+            if W > 1 and lengths is None and T >= W - 1:
+                pre = F.linear(x[:, -(W - 1):], w_qkv)
+            elif W > 1:
+                ends = torch.full((B,), T, device=x.device, dtype=torch.long) \
+                    if lengths is None else lengths.long()
+                pos = ends.unsqueeze(1) - (W - 1) + torch.arange(W - 1, device=x.device)
+                rows = x[torch.arange(B, device=x.device).unsqueeze(1), pos.clamp_min(0)]
+                pre = F.linear(rows, w_qkv) * (pos >= 0).unsqueeze(-1).to(x.dtype)
+            else:
+                pre = x[:, :0]
             cq, ck, cv = (pre[..., :H * K], pre[..., H * K:2 * H * K], pre[..., 2 * H * K:]) \
                 if W > 1 else (pre, pre, pre)
             new_cache = {"recurrent_state": (hk, hv, clock), "conv_state": (cq, ck, cv)}
@@ -361,7 +384,7 @@ class CyclicFlowAttention(nn.Module):
 
     def forward(self, x, cache=None, use_cache=False, attention_mask=None):
         if self._fused_ok(x, cache, attention_mask):
-            return self._forward_fused(x, use_cache)
+            return self._forward_fused(x, use_cache, attention_mask)
         if self._decode_ok(x, cache, attention_mask):
             y, new_cache = self._forward_decode(x, cache)
             return y, new_cache if use_cache else None

@@ -23,7 +23,8 @@ class _FwdArgs(_c.Structure):
         [(n, _c.c_void_p) for n in ("q", "k", "v", "g", "delta", "beta", "q_norm_weight",
                                      "k_norm_weight", "table_bf", "hk0", "hv0", "clock0",
                                      "o", "hk", "hv", "clock")] + \
-        [(n, _c.c_longlong) for n in ("q_stride", "k_stride", "v_stride")]
+        [(n, _c.c_longlong) for n in ("q_stride", "k_stride", "v_stride")] + \
+        [("lengths", _c.c_void_p)]
 
 
 class _BwdArgs(_c.Structure):

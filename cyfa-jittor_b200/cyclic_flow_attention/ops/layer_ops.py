@@ -553,8 +553,9 @@ class ChunkCyfaPackedFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, qkv, H, K, V, g, delta, beta, readout, qw, kw, q_eps, k_eps, scale,
-                tb=None):
-        # tb: the readout table already computed from `readout` on the aux stream
+                tb=None, lengths=None):
+        # tb: the readout table already computed from `readout` on the aux stream;
+        # lengths: int32 [B] valid tokens per sequence (right padding), or None
         ctx.set_materialize_grads(False)  # the final states usually get no gradient
         B, T, width = qkv.shape
         dev = qkv.device
@@ -575,17 +576,17 @@ class ChunkCyfaPackedFunction(torch.autograd.Function):
         qp, kp, vp = base, base + 2 * H * K, base + 4 * H * K
         args = _FwdArgs(B, T, H, K, V, q_eps, k_eps, scale, qp, kp, vp, _p(g), _p(delta),
                         _p(beta), _p(qw), _p(kw), _p(tb), None, None, None, _p(o), _p(hk),
-                        _p(hv), _p(clock), row, row, row)
+                        _p(hv), _p(clock), row, row, row, _p(lengths))
         _lib.call("cyfa_chunk_fwd", _c.byref(args), _lib.ptr(saved), _c.c_size_t(nbytes),
                   _lib.stream())
-        ctx.save_for_backward(qkv, g, delta, beta, qw, kw, tb, hk, hv, clock, saved)
+        ctx.save_for_backward(qkv, g, delta, beta, qw, kw, tb, hk, hv, clock, saved, lengths)
         ctx.readout_meta = readout.detach()[:0]
         ctx.meta = (H, K, V, q_eps, k_eps, scale)
         return o, hk, hv, clock
 
     @staticmethod
     def backward(ctx, do, dhk, dhv, dclock):
-        qkv, g, delta, beta, qw, kw, tb, hk, hv, clock, saved = ctx.saved_tensors
+        qkv, g, delta, beta, qw, kw, tb, hk, hv, clock, saved, lengths = ctx.saved_tensors
         H, K, V, q_eps, k_eps, scale = ctx.meta
         B, T, width = qkv.shape
         dev = qkv.device
@@ -594,7 +595,7 @@ class ChunkCyfaPackedFunction(torch.autograd.Function):
         qp, kp, vp = base, base + 2 * H * K, base + 4 * H * K
         fwd = _FwdArgs(B, T, H, K, V, q_eps, k_eps, scale, qp, kp, vp, _p(g), _p(delta),
                        _p(beta), _p(qw), _p(kw), _p(tb), None, None, None, None, _p(hk), _p(hv),
-                       _p(clock), row, row, row)
+                       _p(clock), row, row, row, _p(lengths))
         do = torch.zeros(B, T, H, V, device=dev, dtype=torch.bfloat16) if do is None \
             else do.to(torch.bfloat16).contiguous()
         dhk = None if dhk is None else dhk.float().contiguous()
@@ -629,4 +630,4 @@ class ChunkCyfaPackedFunction(torch.autograd.Function):
             rd = ctx.readout_meta.dtype
             dreadout = dr if rd == torch.float32 else dr.to(rd)
         return (dqkv, None, None, None, dg, ddelta, dbeta, dreadout, dqw, dkw, None, None, None,
-                None)
+                None, None)

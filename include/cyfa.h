@@ -176,6 +176,11 @@ typedef struct {
   long long q_stride;           /* elements between consecutive tokens of q (0 = H*K) */
   long long k_stride;           /* ... of k (0 = H*K) */
   long long v_stride;           /* ... of v (0 = H*V) */
+  const int* lengths;           /* [B] valid tokens of each sequence, or NULL (all T): the
+                                   tokens past it are right padding, neutral for the
+                                   states and the clock (g = delta = beta = 0 there, as
+                                   the reference layer masks them, layers/cyfa.py:304-308,
+                                   326-328); their gate gradients are zero */
 } cyfa_chunk_fwd_args;
 
 size_t cyfa_chunk_saved_bytes(int B, int T, int H, int K, int V);

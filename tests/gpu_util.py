@@ -55,23 +55,52 @@ def sum_condition(terms, dims):
     return (t.abs().sum(dims).norm() / t.sum(dims).norm().clamp_min(1e-300)).item()
 
 
+def _prefix(y, group=None):
+    """Prefix (inclusive) sums along dim 2 of [B, H, T, ...], restarting every
+    `group` steps."""
+    T = y.shape[2]
+    if not group:
+        return y.cumsum(2)
+    out = y.clone()
+    for s in range(0, T, group):
+        out[:, :, s:s + group] = y[:, :, s:s + group].cumsum(2)
+    return out
+
+
 def gate_param_tolerances(taps, x, params, tol=1e-2):
-    """The gate/clock parameters' gradients are token sums of per-token terms
-    (dL/dA_log = sum g dg; dt_bias, a_proj: the gradient at a + dt_bias; d_proj,
-    b_proj: at their pre-activations, times x for the weights).  Those terms are
-    held to `tol` by the op-level tests; a sum of terms each within `tol` is
-    within `tol` times its condition number (sum of |terms| over |sum|), taken
-    here from the oracle's own terms."""
-    ga = taps["a"].grad.double()
-    gd = taps["dpre"].grad.double()
-    gb = taps["bpre"].grad.double()
-    xs = x.double()
-    bt = (0, 1)
+    """Bounds for the layer's gate/clock parameter gradients, which are token
+    sums of the op's per-token gate terms.  dg is an in-tile suffix sum of terms
+    dG_u (128-token tiles) and ddelta a suffix sum over the sequence of the clock
+    terms dlam_s, so, exchanging the sums,
+        dA_log  = sum_u dG_u  P(g)_u,        dt_bias = sum_u dG_u P(s)_u,
+        a_proj  = sum_u dG_u  P(s x)_u,      s = dg/d(a + dt_bias),
+        d_proj  = sum_s dlam_s Q(d' [x])_s,  d' = delta (1 - delta),
+        b_proj  = sum_t dbeta_t b' [x]_t,    b' = beta (1 - beta),
+    with P the in-tile and Q the whole-sequence prefix sums.  The op-level tests
+    hold the terms dG, dlam and dbeta to `tol`; a sum of terms each within
+    `tol` is within `tol` times its condition number (sum of |terms| over
+    |sum|), computed here from the oracle's own terms."""
+    perm = (0, 2, 1)
+    g = taps["g"].detach().double().permute(*perm)
+    dg = taps["g"].grad.double().permute(*perm)
+    a = taps["a"].detach().double().permute(*perm)
+    d = taps["delta"].detach().double().permute(*perm)
+    dd = taps["delta"].grad.double().permute(*perm)
+    gb = taps["bpre"].grad.double().permute(*perm)
+    xs = x.detach().double().unsqueeze(1)                      # [B, 1, T, hidden]
+    A = params["A_log"].detach().double().view(1, -1, 1)
+    s = -A.exp() * torch.sigmoid(a)
+    dG = suffix_terms(dg, 128)
+    dlam = suffix_terms(dd)
+    dp = d * (1 - d)
+    bt = (0, 2)
     terms = {
-        "A_log": taps["g"].grad.double() * taps["g"].detach().double(),
-        "dt_bias": ga, "d_proj.bias": gd, "b_proj.bias": gb,
-        "a_proj.weight": ga.unsqueeze(-1) * xs.unsqueeze(-2),
-        "d_proj.weight": gd.unsqueeze(-1) * xs.unsqueeze(-2),
-        "b_proj.weight": gb.unsqueeze(-1) * xs.unsqueeze(-2),
+        "A_log": dG * _prefix(g, 128),
+        "dt_bias": dG * _prefix(s, 128),
+        "a_proj.weight": dG.unsqueeze(-1) * _prefix(s.unsqueeze(-1) * xs, 128),
+        "d_proj.bias": dlam * _prefix(dp),
+        "d_proj.weight": dlam.unsqueeze(-1) * _prefix(dp.unsqueeze(-1) * xs),
+        "b_proj.bias": gb,
+        "b_proj.weight": gb.unsqueeze(-1) * xs,
     }
     return {n: tol * max(1.0, sum_condition(t, bt)) for n, t in terms.items()}

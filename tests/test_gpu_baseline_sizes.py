@@ -15,10 +15,13 @@
 Tolerances: bf16 outputs and gradients rel-L2 <= 1e-2 of the fp32 oracle, fp32
 paths <= 1e-4.  Gradients that are sums of many per-token terms -- the op's
 ddelta (a suffix sum of the clock terms over all T tokens) and dg (an in-tile
-suffix sum), the layer's gate/clock parameters (token sums) -- are checked per
-term at 1e-2, and as sums at 1e-2 times the summation's condition number
-(sum of |terms| over |sum|, from the oracle's own terms): the forward error
-bound of a sum whose terms are each within 1e-2.  Every per-tensor error is
+suffix sum), the layer's gate/clock parameters (token sums of those) -- are
+checked per term at 1e-2, and as sums at 1e-2 times the summation's condition
+number (sum of |terms| over |sum|, from the oracle's own terms): the forward
+error bound of a sum whose terms are each within 1e-2.  Where that bound is
+loose (the layer's gate parameters: condition numbers of 1e2-1e4 at c3), they
+must also stay within 4x the shift that rounding only the reference's own bf16
+storage points produces in the oracle (``bf16_points``).  Every per-tensor error is
 printed, and appended as one JSON line per case to the file named by
 CYFA_PARITY_OUT when it is set, together with the condition-number bounds and
 the shift that rounding only the reference's own bf16 storage points produces
@@ -235,7 +238,9 @@ def test_c3_layer_forward_backward(pkg):
     errs = {"y": rel_l2(y, yr), "x": rel_l2(xg.grad, xr.grad)}
     errs.update({n: rel_l2(p.grad, params[n].grad) for n, p in m.named_parameters()})
     shift = {n: rel_l2(rparams[n].grad, params[n].grad) for n in LAYER_COND}
-    bounds = gate_param_tolerances(taps, xr.detach(), params, BF16_TOL)
-    _record("c3 layer fwd+bwd hidden1024 H4x256 T2048", errs, bounds, shift)
+    kappa = gate_param_tolerances(taps, xr.detach(), params, BF16_TOL)
+    bounds = {n: max(BF16_TOL, min(kappa[n], 4.0 * shift[n])) for n in LAYER_COND}
+    _record("c3 layer fwd+bwd hidden1024 H4x256 T2048", errs,
+            {**{"kappa_bound." + n: v for n, v in kappa.items()}, **bounds}, shift)
     for n, e in errs.items():
         assert e < bounds.get(n, BF16_TOL), (n, e)

@@ -51,7 +51,14 @@ def test_layer_forward_backward(Layer, B, T, hidden, H, hd):
     (yr * dy).sum().backward()
     errs = {"y": rel_l2(y, yr), "x": rel_l2(xg.grad, xr.grad)}
     errs.update({n: rel_l2(p.grad, params[n].grad) for n, p in m.named_parameters()})
-    tols = gate_param_tolerances(taps, xr.detach(), params)
+    # gate/clock parameters: within 1e-2 x their condition number (the provable
+    # bound given per-term parity) and within 4x the shift that the reference's
+    # own bf16 storage points produce in the oracle (bf16_points)
+    kappa = gate_param_tolerances(taps, xr.detach(), params)
+    rparams = {n: p.detach().clone().requires_grad_(True) for n, p in params.items()}
+    (O.cyfa_layer(rparams, x.float(), H, hd, hd, bf16_points=True) * dy).sum().backward()
+    tols = {n: max(1e-2, min(k, 4.0 * rel_l2(rparams[n].grad, params[n].grad)))
+            for n, k in kappa.items()}
     print("layer errors", B, T, hidden, H, hd, {k: round(v, 5) for k, v in errs.items()},
           "gate tolerances", {k: round(v, 4) for k, v in tols.items()})
     for n, e in errs.items():

@@ -105,7 +105,9 @@ def test_lm_decode_matches_forward(lm):
             after = [t_ for c in cache for t_ in c["recurrent_state"] + c["conv_state"]]
             assert all(torch.equal(a, b) for a, b in zip(snap, after))  # caller's cache kept
             cache = out["cache"]
-            assert rel_l2(out["logits"][:, 0], full[:, t]) < 2e-2, t
+            err = rel_l2(out["logits"][:, 0], full[:, t])
+            print("decode vs forward logits", t, round(err, 5))
+            assert err < 1e-2, t
 
 
 def test_graphed_decoder_matches_eager(lm):
@@ -119,3 +121,71 @@ def test_graphed_decoder_matches_eager(lm):
     assert torch.equal(graphed, eager)
     # a second prefill re-captures over new state and gives the same tokens
     assert torch.equal(dec.generate(ids, 8), eager)
+
+
+def _right_padded(prompts, width):
+    ids = torch.zeros(len(prompts), width, dtype=torch.long)
+    mask = torch.zeros_like(ids)
+    for r, p in enumerate(prompts):
+        ids[r, :len(p)] = torch.tensor(p)
+        mask[r, :len(p)] = 1
+    return ids.cuda(), mask.cuda()
+
+
+def test_masked_prefill_matches_rows(lm):
+    """A right-padded batch prefilled with its attention mask (the fused layer
+    path with per-row lengths, as generate_batch runs it) gives each row the
+    hidden states, recurrent state and convolution histories of that row run
+    alone, and its last-token logits match the oracle LM on the row
+    (reference layers/cyfa.py:304-328: padding is neutral)."""
+    _, cfg, m = lm
+    gen = seeded(16)
+    lens = [5, 70, 33, 1]
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=gen).tolist() for n in lens]
+    ids, mask = _right_padded(prompts, 128)
+    with torch.no_grad():
+        hidden, cache = m.model(ids, use_cache=True, attention_mask=mask)
+        for r, p in enumerate(prompts):
+            row_ids = torch.tensor([p], device="cuda")
+            h1, c1 = m.model(row_ids, use_cache=True)
+            assert rel_l2(hidden[r, :len(p)], h1[0]) < 1e-2, r
+            for layer, (cb, cr) in enumerate(zip(cache, c1)):
+                for a, b in zip(cb["recurrent_state"], cr["recurrent_state"]):
+                    assert rel_l2(a[r], b[0]) < 1e-2, (r, layer)
+                for a, b in zip(cb["conv_state"], cr["conv_state"]):
+                    assert rel_l2(a[r], b[0]) < 1e-2, (r, layer)
+            logits = m.lm_head(hidden[r, len(p) - 1])
+            ref = _oracle_logits(cfg, m, row_ids)[0, -1]
+            assert rel_l2(logits, ref) < 1e-2, r
+
+
+def test_generate_batch_matches_generate():
+    """generate_batch (one masked prefill, batched decode steps, independent
+    stopping) returns for every prompt the tokens generate() returns for it
+    alone (reference generation.py:23-102)."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+    from cyclic_flow_attention.generation import generate, generate_batch
+    from cyclic_flow_attention.models.cyfa import CyclicFlowAttentionConfig
+    from cyclic_flow_attention.utils import initialize_model
+
+    cfg = CyclicFlowAttentionConfig(hidden_size=256, num_heads=2, head_dim=128,
+                                    num_hidden_layers=2, vocab_size=256)
+    m = initialize_model(cfg, generator=seeded(20))
+    with torch.no_grad():  # peaked logits, so greedy choices are not near ties
+        m.lm_head.weight.mul_(25.0)
+    m = m.cuda().eval()
+    gen = seeded(21)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=gen).tolist()
+               for n in (3, 67, 20)]
+    want = [generate(m, p, max_new_tokens=6) for p in prompts]
+    got = generate_batch(m, prompts, max_new_tokens=6)
+    assert got == want
+    # independent stopping: a row stops at its own end-of-sequence token
+    eos = want[1][2]
+    got = generate_batch(m, prompts, max_new_tokens=6, eos_token_id=eos)
+    for g, w in zip(got, want):
+        stop = w.index(eos) + 1 if eos in w else len(w)
+        assert g == w[:stop]
+    with pytest.raises(ValueError):
+        generate_batch(m, [[]])
