@@ -283,14 +283,19 @@ def chunk_cyfa(
 def fused_recurrent_cyfa(
     q, k, v, g, delta, beta, readout, q_norm_weight, k_norm_weight,
     q_norm_eps=1e-6, k_norm_eps=1e-6, scale=None, initial_state=None,
-    output_final_state=False, dtype=torch.float32,
+    output_final_state=False, dtype=torch.float32, bf16_points=False,
 ):
     """One decode step, T=1 (ops/fused_recurrent.py:10-200, kernel :55-188).
 
     Same math as chunk_cyfa for one token: q/k RMSNorm, lam = clock + delta,
     hk = a hk + k w^T, raw = scale hk^T q, readout, hv = a hv + w v^T,
     o = hv^T weights.  Returns (o [B,1,H,V], (hk, hv, clock) or None).
+    ``bf16_points`` rounds to bf16 where the reference's kernel casts to the
+    bf16 input type: the normalised q and k (:84-85), the write vector (:97,
+    :172), the rotated raw vector (:118), the table in both products (:126,
+    :150), the probabilities (:150), the weights (:170) and the output (:187).
     """
+    rp = bf16_points
     B, T, H, K = q.shape
     if T != 1:
         raise NotImplementedError("decode step needs T=1")
@@ -304,17 +309,24 @@ def fused_recurrent_cyfa(
     else:
         hk, hv, clock = (x.to(dtype) for x in initial_state)
     sc = K ** -0.5 if scale is None else scale
-    qn = head_rmsnorm(q, q_norm_weight.to(dtype), q_norm_eps)[:, :, 0]  # [B,H,K]
-    kn = head_rmsnorm(k, k_norm_weight.to(dtype), k_norm_eps)[:, :, 0]
+    qn = _rp(head_rmsnorm(q, q_norm_weight.to(dtype), q_norm_eps)[:, :, 0], rp)  # [B,H,K]
+    kn = _rp(head_rmsnorm(k, k_norm_weight.to(dtype), k_norm_eps)[:, :, 0], rp)
     lam = clock + delta[:, 0]  # fused_recurrent.py:91
     alpha = g[:, 0].exp()
     w, c, s = write_vector(lam, beta[:, 0], M)
+    w = _rp(w, rp)
     hk = hk * alpha[..., None, None] + kn[..., :, None] * w[..., None, :]  # :105-109
-    raw = torch.einsum("bhkm,bhk->bhm", hk, qn) * sc
+    raw = torch.einsum("bhkm,bhk->bhm", hk, qn * sc)
     table = readout_table(readout, dtype)
-    weights = modal_readout(raw.unsqueeze(2), c.unsqueeze(2), s.unsqueeze(2), table)[:, :, 0]
+    if rp:
+        z = _rp(rotate(raw, c, s), rp)
+        tb = _rp(table, rp)
+        probs = _rp(torch.softmax(torch.einsum("bhm,hrm->bhr", z, tb), dim=-1), rp)
+        weights = _rp(rotate(torch.einsum("bhr,hrm->bhm", probs, tb), c, s, negative=True), rp)
+    else:
+        weights = modal_readout(raw.unsqueeze(2), c.unsqueeze(2), s.unsqueeze(2), table)[:, :, 0]
     hv = hv * alpha[..., None, None] + w[..., :, None] * v[:, 0][..., None, :]  # :177-184
-    o = torch.einsum("bhmv,bhm->bhv", hv, weights).unsqueeze(1)
+    o = _rp(torch.einsum("bhmv,bhm->bhv", hv, weights).unsqueeze(1), rp)
     return o, ((hk, hv, lam) if output_final_state else None)
 
 

@@ -1,0 +1,72 @@
+"""The CUDA kernels against outputs of the reference's OWN kernels (see
+tests/test_golden.py for how tests/golden/ref_decode.npz was made): the decode
+step stepped through each golden sequence, and the chunkwise forward (bf16
+tcgen05 path, fp32 recurrence path) over it.  bf16 to 1e-2, fp32 to 1e-4."""
+
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+from golden_cases import CASES, EPS, case_inputs, summarize_state  # noqa: E402
+
+GOLDEN = os.path.join(HERE, "golden", "ref_decode.npz")
+
+
+@pytest.fixture(scope="module")
+def env():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA GPU")
+    from cyclic_flow_attention import _lib, ops
+
+    return _lib, ops, np.load(GOLDEN)
+
+
+def _check(case, gold, o, hk, hv, clock, tol):
+    name = case[0]
+    errs = {"o": rel_l2(o, torch.from_numpy(gold[f"{name}.o"])),
+            "clock": rel_l2(clock, torch.from_numpy(gold[f"{name}.clock"]))}
+    errs.update({k: rel_l2(v, torch.from_numpy(gold[f"{name}.{k}"]))
+                 for k, v in summarize_state(case, hk, hv).items()})
+    print(name, {k: float(f"{v:.3g}") for k, v in errs.items()})
+    assert errs.pop("clock") < 1e-6
+    for k, e in errs.items():
+        assert e < tol, (name, k, e)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_decode_kernel_matches_reference(env, case):
+    _lib, ops, gold = env
+    x = {n: t.cuda() for n, t in case_inputs(case).items()}
+    state = (x["hk0"], x["hv0"], x["clock0"])
+    outs = []
+    with torch.no_grad():
+        for t in range(case[7]):
+            sl = [x[n][:, t:t + 1] for n in ("q", "k", "v", "g", "delta", "beta")]
+            o, state = ops.fused_recurrent_cyfa(*sl, x["readout"], x["qw"], x["kw"], EPS, EPS,
+                                                initial_state=state, output_final_state=True)
+            outs.append(o)
+    tol = 1e-4 if case[5] == torch.float32 else 1e-2
+    _check(case, gold, torch.cat(outs, 1), *state, tol)
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_chunk_forward_matches_reference(env, case):
+    _lib, ops, gold = env
+    x = {n: t.cuda() for n, t in case_inputs(case).items()}
+    ins = [x[n] for n in ("q", "k", "v", "g", "delta", "beta", "readout", "qw", "kw")]
+    with torch.no_grad():
+        o, state = ops.chunk_cyfa(*ins, EPS, EPS, initial_state=(x["hk0"], x["hv0"], x["clock0"]),
+                                  output_final_state=True)
+    tol = 1e-4 if case[5] == torch.float32 else 1e-2
+    _check(case, gold, o, *state, tol)
+    assert _lib.device_error() == 0
