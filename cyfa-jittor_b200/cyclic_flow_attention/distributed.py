@@ -13,6 +13,7 @@ import contextlib
 
 import torch
 import torch.distributed as dist
+from torch import nn
 
 from . import _lib
 
@@ -283,3 +284,156 @@ def broadcast_parameters(params, src=0, group=None):
     """Copies rank `src`'s parameters to every rank (reference train.py:86-90)."""
     for p in params:
         dist.broadcast(p.data, src=src, group=group)
+
+
+# ---------------------------------------------------------------- head parallelism
+class _ReplicatedInput(torch.autograd.Function):
+    """Identity in the forward; in the backward the input gradient, a partial
+    sum over this rank's heads, is summed over the head group."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, dx):
+        dx = dx.contiguous()
+        dist.all_reduce(dx, op=dist.ReduceOp.SUM, group=ctx.group)
+        return dx, None
+
+
+class _GatherHeads(torch.autograd.Function):
+    """[..., H_l * V] per rank -> [..., world * H_l * V] on every rank, rank r's
+    heads at block r (one all_gather_into_tensor).  The computation after it is
+    replicated, so the adjoint is the rank's own block of the gradient."""
+
+    @staticmethod
+    def forward(ctx, o, group):
+        world = dist.get_world_size(group)
+        ctx.group, ctx.world, ctx.rank = group, world, dist.get_rank(group)
+        lead, width = o.shape[:-1], o.shape[-1]
+        flat = o.reshape(-1, width).contiguous()
+        out = torch.empty(world * flat.shape[0], width, device=o.device, dtype=o.dtype)
+        dist.all_gather_into_tensor(out, flat, group=group)
+        return out.view(world, -1, width).permute(1, 0, 2).reshape(*lead, world * width)
+
+    @staticmethod
+    def backward(ctx, dy):
+        width = dy.shape[-1] // ctx.world
+        return dy[..., ctx.rank * width:(ctx.rank + 1) * width].contiguous(), None
+
+
+# parameters of CyclicFlowAttention split by heads: name -> (rows per head of
+# the head dimension: "k" = head_k_dim, "v" = head_v_dim, 1 = one per head)
+_HEAD_ROWS = {
+    "q_proj.weight": "k", "k_proj.weight": "k", "v_proj.weight": "v",
+    "a_proj.weight": 1, "b_proj.weight": 1, "b_proj.bias": 1, "d_proj.weight": 1,
+    "d_proj.bias": 1, "dt_bias": 1, "A_log": 1, "readout": 1,
+    "q_conv1d.weight": "k", "k_conv1d.weight": "k", "v_conv1d.weight": "v",
+    "q_conv1d.bias": "k", "k_conv1d.bias": "k", "v_conv1d.bias": "v",
+    "g_proj.1.weight": "v", "g_proj.1.bias": "v",
+}
+# shared across heads: every rank holds all of it and contributes a partial gradient
+_SHARED = ("q_norm.weight", "k_norm.weight", "o_norm.weight", "g_proj.0.weight")
+
+
+def _head_rows(layer, name):
+    unit = _HEAD_ROWS[name]
+    return {"k": layer.head_k_dim, "v": layer.head_v_dim, 1: 1}[unit]
+
+
+class HeadParallelAttention(nn.Module):
+    """A CyclicFlowAttention layer split over the ranks of `group` by heads, for
+    batches too small to split over the ranks (B < #GPUs).
+
+    Every rank gets the whole input batch.  Rank r keeps heads [r*H_l, (r+1)*H_l)
+    of every per-head parameter (the q/k/v/a/b/d projection rows, short
+    convolutions, readout, A_log, dt_bias and the output gate's second linear)
+    and a copy of the shared ones (q/k/o norm weights, the output gate's first
+    linear, o_proj), and runs the fused layer on its heads up to the gated
+    output norm.  The head outputs [B, T, H_l*V] are gathered with one
+    all_gather_into_tensor into [B, T, H*V] and projected by o_proj on every
+    rank, so the output is replicated.  Backward: each rank keeps its block of
+    the gathered gradient, its head-sharded weight gradients are final, the
+    input gradient is summed over the group (one all-reduce), and
+    ``sync_grads()`` sums the shared parameters' partial gradients (one flat
+    all-reduce).  The math is the unsplit layer's (layers/cyfa.py:299-357)."""
+
+    def __init__(self, layer, group=None):
+        super().__init__()
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        H = layer.num_heads
+        if H % world:
+            raise ValueError(f"{H} heads do not split over {world} ranks")
+        self.group, self.world, self.rank = group, world, rank
+        self.heads_local = H // world
+        from .layers.cyfa import CyclicFlowAttention
+
+        hidden = layer.q_proj.weight.shape[1]
+        conv = layer.q_conv1d.width if layer.use_short_conv else 4
+        bias = layer.use_short_conv and layer.q_conv1d.bias is not None
+        local = CyclicFlowAttention(hidden, self.heads_local, layer.head_k_dim,
+                                    expand_v=layer.head_v_dim / layer.head_k_dim,
+                                    num_slots=layer.num_slots,
+                                    use_short_conv=layer.use_short_conv, conv_size=conv,
+                                    conv_bias=bias, norm_eps=layer.q_norm.eps,
+                                    chunk_size=layer.chunk_size)
+        full = dict(layer.named_parameters())
+        with torch.no_grad():
+            for name, p in local.named_parameters():
+                src = full[name]
+                if name in _HEAD_ROWS:
+                    n = self.heads_local * _head_rows(layer, name)
+                    src = src[rank * n:(rank + 1) * n]
+                p.data = src.detach().clone()
+        self.local = local
+        self.o_proj = nn.Linear(layer.o_proj.weight.shape[1], hidden, bias=False,
+                                device=layer.o_proj.weight.device,
+                                dtype=layer.o_proj.weight.dtype)
+        with torch.no_grad():
+            self.o_proj.weight.copy_(layer.o_proj.weight)
+        self.local.o_proj = None  # the projection happens after the gather
+
+    def forward(self, x):
+        x = _ReplicatedInput.apply(x, self.group)
+        o, _ = self.local._forward_fused(x, False, project=False)
+        o = _GatherHeads.apply(o, self.group)
+        return torch.nn.functional.linear(o, self.o_proj.weight)
+
+    def shared_parameters(self):
+        named = dict(self.local.named_parameters())
+        return [named[n] for n in _SHARED if n in named]
+
+    def sync_grads(self):
+        """Sums the shared parameters' partial gradients over the group."""
+        ps = [p for p in self.shared_parameters() if p.grad is not None]
+        if not ps:
+            return
+        flat = torch.cat([p.grad.float().reshape(-1) for p in ps])
+        dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group)
+        off = 0
+        for p in ps:
+            n = p.numel()
+            p.grad.copy_(flat[off:off + n].view_as(p.grad))
+            off += n
+
+    def gather_grads(self):
+        """{reference name: full gradient} on every rank: the head-sharded
+        gradients gathered in head order, the others as held (for checking
+        against the unsplit layer)."""
+        out = {}
+        for name, p in self.local.named_parameters():
+            if p.grad is None:
+                continue
+            g = p.grad.contiguous()
+            if name in _HEAD_ROWS:
+                parts = torch.empty((self.world * g.shape[0],) + tuple(g.shape[1:]),
+                                    device=g.device, dtype=g.dtype)
+                dist.all_gather_into_tensor(parts, g, group=self.group)
+                g = parts
+            out[name] = g
+        if self.o_proj.weight.grad is not None:
+            out["o_proj.weight"] = self.o_proj.weight.grad
+        return out

@@ -217,7 +217,7 @@ class CyclicFlowAttention(nn.Module):
             and (self.training or x.shape[1] > 1 or torch.is_grad_enabled())
         )
 
-    def _forward_fused(self, x, use_cache, attention_mask=None):
+    def _forward_fused(self, x, use_cache, attention_mask=None, project=True):
         """One packed q|k|v|g0|a|b|d projection with the short convolution and the
         gate activations on its columns (LayerFrontFunction), the CyFA op on the
         convolved q|k|v, the gated output norm with the gate's second linear, and
@@ -228,7 +228,9 @@ class CyclicFlowAttention(nn.Module):
         as neutral padding (g = delta = beta = 0, reference layers/cyfa.py:304-308,
         326-328), and the convolution histories of the cache end at each row's
         length (the reference's ShortConvolution with lengths, :144-181).  The
-        outputs at padded positions are not defined."""
+        outputs at padded positions are not defined.  With ``project=False`` the
+        result is the gated norm's output [B, T, H*V], before o_proj (the
+        head-parallel layer gathers it across ranks first)."""
         B, T, _ = x.shape
         lengths = None
         if attention_mask is not None:
@@ -260,8 +262,9 @@ class CyclicFlowAttention(nn.Module):
         g1 = self.g_proj[1]
         y = GatedNormFunction.apply(o, gate_in, g1.weight, g1.bias, self.o_norm.weight,
                                     self.o_norm.eps, float(self.num_slots - 1), slot, (g1.weight,))
-        y = LinearFunction.apply(y, self.o_proj.weight, (self.o_proj.weight,), slot) \
-            if self.o_proj.bias is None else self.o_proj(y)
+        if project:
+            y = LinearFunction.apply(y, self.o_proj.weight, (self.o_proj.weight,), slot) \
+                if self.o_proj.bias is None else self.o_proj(y)
         new_cache = None
         if use_cache:
             W = self.q_conv1d.width
