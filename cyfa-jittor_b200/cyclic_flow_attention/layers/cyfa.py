@@ -234,7 +234,7 @@ class CyclicFlowAttention(nn.Module):
         B, T, _ = x.shape
         lengths = None
         if attention_mask is not None:
-            lengths = attention_mask.to(torch.int32).sum(1).contiguous()
+            lengths = attention_mask.sum(1).to(torch.int32).contiguous()  # int32 [B]
         H, K, V = self.num_heads, self.head_k_dim, self.head_v_dim
         g0 = self.g_proj[0]
         self._pack_front()

@@ -558,6 +558,9 @@ class ChunkCyfaPackedFunction(torch.autograd.Function):
         # lengths: int32 [B] valid tokens per sequence (right padding), or None
         ctx.set_materialize_grads(False)  # the final states usually get no gradient
         B, T, width = qkv.shape
+        if lengths is not None and (lengths.dtype != torch.int32 or lengths.shape != (B,)
+                                    or not lengths.is_contiguous()):
+            raise ValueError("lengths must be a contiguous int32 tensor of shape [B]")
         dev = qkv.device
         row = qkv.stride(1)
         base = qkv.data_ptr()
