@@ -14,3 +14,4 @@
 #include "noalloc.cu"
 #include "lm_decode.cu"
 #include "gradbuf.cu"
+#include "skinny_gemm.cu"
