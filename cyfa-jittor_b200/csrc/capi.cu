@@ -95,6 +95,8 @@ static void prof_end(const char* name, cudaEvent_t start, cudaStream_t s) {
 // prologue (barrier setup, TMEM allocation) overlap the previous kernel's tail.
 // cyfa_set_pdl(0) turns it off (plain stream order).
 static std::atomic<int> g_pdl{1};
+// Segmented state scans for scans with fewer CTAs than SMs (cyfa_set_scan_split).
+static std::atomic<int> g_scan_split{1};
 
 template <typename... KArgs, typename... Args>
 static void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
@@ -351,6 +353,8 @@ const char* cyfa_strerror(int status) {
 long long cyfa_launch_count(void) { return g_launches.load(); }
 
 int cyfa_set_pdl(int on) { return g_pdl.exchange(on != 0 ? 1 : 0); }
+
+int cyfa_set_scan_split(int on) { return g_scan_split.exchange(on != 0 ? 1 : 0); }
 
 int cyfa_set_aux_stream(void* aux) {
   t_aux = static_cast<cudaStream_t>(aux);

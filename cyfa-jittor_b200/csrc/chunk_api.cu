@@ -34,11 +34,38 @@ static Dims make_dims(int B, int T, int H, int K, int V) {
   return d;
 }
 
+// Segments of a state scan: when a scan has fewer CTAs than the SMs (few
+// sequences x heads, long sequences), its tiles are split
+// into segments scanned side by side (a summary pass from zero, the carries, and
+// the real pass from the carried states), at least 4 tiles each.
+// Tiles per segment; the segments are ceil(NT / that), none empty.
+static int scan_seg_tiles(const Dims& d, int ctas) {
+  if (!g_scan_split.load(std::memory_order_relaxed)) return d.NT;
+  int n = 148 / (ctas > 0 ? ctas : 1);
+  const int cap = d.NT / 4;
+  if (n > cap) n = cap;
+  return n < 2 ? d.NT : (d.NT + n - 1) / n;
+}
+static int scan_nseg(const Dims& d, int ctas) {
+  const int per = scan_seg_tiles(d, ctas);
+  return (d.NT + per - 1) / per;
+}
+
+// fp32 scratch of the segmented scans: segment end states and carried states,
+// [nseg, BH, DK, DV] each, for the larger of the two passes.
+static size_t scan_scratch_floats(const Dims& d) {
+  const int n1 = scan_nseg(d, d.BH * (d.K / 128) * 2), n2 = scan_nseg(d, d.BH * (d.V / 64));
+  const int n = n1 > n2 ? n1 : n2;
+  const size_t elems = size_t(d.K) * 128 > size_t(128) * d.V ? size_t(d.K) * 128 : size_t(128) * d.V;
+  return n > 1 ? 2 * size_t(n) * d.BH * elems : 0;
+}
+
 // Tensors the forward pass keeps for the backward pass.
 struct Saved {
   float *G, *lam, *beta_h, *q_rs, *k_rs;
   __nv_bfloat16 *qn, *kn, *w, *raw, *weights, *s1, *s2;
   __nv_bfloat16 *s1_fin, *s2_fin;  // bf16 copies of the final states (reverse boundary terms)
+  float* scan_tmp;                 // segmented-scan scratch (scan_scratch_floats)
 };
 
 static Saved carve_saved(const Dims& d, void* base, size_t* total) {
@@ -59,6 +86,7 @@ static Saved carve_saved(const Dims& d, void* base, size_t* total) {
   s.s2 = c.take<__nv_bfloat16>(size_t(d.BH) * d.NT * 128 * d.V);
   s.s1_fin = c.take<__nv_bfloat16>(size_t(d.BH) * d.K * 128);
   s.s2_fin = c.take<__nv_bfloat16>(size_t(d.BH) * 128 * d.V);
+  s.scan_tmp = c.take<float>(scan_scratch_floats(d));
   if (total) *total = c.off + 256;
   return s;
 }
@@ -70,7 +98,7 @@ constexpr int kDgSlots = 6;
 struct Work {
   __nv_bfloat16 *h1, *h2, *A, *Bp, *draw, *dweights, *dw, *dw_b, *dq1, *dk1;
   float *dG, *dlam_r, *dlam_w, *dbeta_h, *bpart1, *bpart2, *dtab_part,
-      *dqw_part, *dkw_part;
+      *dqw_part, *dkw_part, *scan_tmp;
 };
 
 static Work carve_work(const Dims& d, void* base, size_t* total) {
@@ -96,6 +124,7 @@ static Work carve_work(const Dims& d, void* base, size_t* total) {
   w.dtab_part = c.take<float>(tiles * 128 * 128);
   w.dqw_part = c.take<float>(size_t(1184) * d.K);
   w.dkw_part = c.take<float>(size_t(1184) * d.K);
+  w.scan_tmp = c.take<float>(scan_scratch_floats(d));
   if (total) *total = c.off + 256;
   return w;
 }
@@ -130,6 +159,50 @@ static int readout_ctas_per_head(const Dims& d) {
 
 // A token stride of 0 means the dense layout.
 static long long stride_or(long long s, long long dense) { return s > 0 ? s : dense; }
+
+// One state scan over grid (BH, K slices, V slices): a single launch, or, with
+// scan_nseg segments, the summary pass, the carries and the segmented pass
+// (state_scan_kernel, scan_carry_kernel).  `tmp`: scan_scratch_floats floats.
+template <bool REVERSE>
+static int run_scan(const Dims& d, ScanParams p, dim3 grid, const CUtensorMap& mk,
+                    const CUtensorMap& mv, const CUtensorMap& mf, const CUtensorMap& mff,
+                    float* tmp, cudaStream_t st) {
+  const char* name = REVERSE ? "state_scan_bwd" : "state_scan_fwd";
+  const int ctas = int(grid.x * grid.y * grid.z);
+  const int nseg = scan_nseg(d, ctas);
+  p.nseg = nseg;
+  p.seg_tiles = scan_seg_tiles(d, ctas);
+  p.summary = 0;
+  set_smem(state_scan_kernel<REVERSE>, kScanSmem);
+  if (nseg == 1) {
+    CYFA_LAUNCH(name, st, (launch_k(state_scan_kernel<REVERSE>, grid, kScanThreads, kScanSmem,
+                                    st, mk, mv, mf, mff, p)));
+    return launch_status();
+  }
+  CYFA_REQUIRE(tmp, kWorkspace);
+  const size_t elems = size_t(p.DK) * p.DV;
+  float* seg_out = tmp;
+  float* seg_init = tmp + size_t(nseg) * d.BH * elems;
+  const dim3 sgrid(grid.x, grid.y, grid.z * nseg);
+  ScanParams a = p;
+  a.summary = 1;
+  a.seg_out = seg_out;
+  CYFA_LAUNCH("state_scan_summary", st,
+              (launch_k(state_scan_kernel<REVERSE>, sgrid, kScanThreads, kScanSmem, st, mk, mv,
+                        mf, mff, a)));
+  int rc = launch_status();
+  if (rc) return rc;
+  const int e = int(elems);
+  CYFA_LAUNCH("scan_carry", st,
+              (launch_k(scan_carry_kernel<REVERSE>, dim3((e / 4 + 255) / 256, d.BH), 256, 0, st,
+                        static_cast<const float*>(p.G), d.TP, d.NT, d.BH, e, nseg, p.seg_tiles,
+                        static_cast<const float*>(seg_out), seg_init)));
+  if ((rc = launch_status())) return rc;
+  p.seg_init = seg_init;
+  CYFA_LAUNCH(name, st, (launch_k(state_scan_kernel<REVERSE>, sgrid, kScanThreads, kScanSmem, st,
+                                  mk, mv, mf, mff, p)));
+  return launch_status();
+}
 
 
 
@@ -193,11 +266,9 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
   {
     ScanParams p{d.BH, d.H, d.TP, d.NT, d.K, 128, kRows2D, kRows2D, s.G, a->hk0, s.s1, a->hk,
                  0.f, s.s1_fin, nullptr};
-    set_smem(state_scan_kernel<false>, kScanSmem);
-    CYFA_LAUNCH("state_scan_fwd", st,
-                (launch_k(state_scan_kernel<false>, dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st, 
-                    m_kn, m_w, m_kn, m_kn, p)));
-    if ((rc = launch_status())) return rc;
+    if ((rc = run_scan<false>(d, p, dim3(d.BH, d.K / 128, 2), m_kn, m_w, m_kn, m_kn, s.scan_tmp,
+                              st)))
+      return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, 128, kRows2D, 0, s.G, s.lam, a->scale, s.raw,
                     s.weights};
     // the state history in 64-row blocks, as the two-CTA kernel streams it
@@ -220,10 +291,8 @@ int cyfa_chunk_fwd(const cyfa_chunk_fwd_args* a, void* saved, size_t saved_bytes
   {
     ScanParams p{d.BH, d.H, d.TP, d.NT, 128, d.V, kRows2D, kPublic4D, s.G, a->hv0, s.s2, a->hv,
                  0.f, s.s2_fin, nullptr};
-    CYFA_LAUNCH("state_scan_fwd", st,
-                (launch_k(state_scan_kernel<false>, dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st, 
-                    m_w, m_v, m_w, m_w, p)));
-    if ((rc = launch_status())) return rc;
+    if ((rc = run_scan<false>(d, p, dim3(d.BH, 1, d.V / 64), m_w, m_v, m_w, m_w, s.scan_tmp, st)))
+      return rc;
     TileFwdParams t{d.BH, d.H, d.TP, d.NT, d.T, d.V, kPublic4D, 1, s.G, s.lam, 1.f,
                     static_cast<__nv_bfloat16*>(a->o), nullptr};
     set_smem(tile_fwd_kernel, kTileFwdSmem);
@@ -354,10 +423,9 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
                  1.f, nullptr, w.bpart2, a->hv};
     CUtensorMap m_ff2;
     if ((rc = tmap_2d(&m_ff2, s.s2_fin, uint64_t(d.BH) * 128, d.V, 128))) return rc;
-    CYFA_LAUNCH("state_scan_bwd", st,
-                (launch_k(state_scan_kernel<true>, dim3(d.BH, 1, d.V / 64), kScanThreads, kScanSmem, st, 
-                    m_weights, m_do, m_s2, m_ff2, p)));
-    if ((rc = launch_status())) return rc;
+    if ((rc = run_scan<true>(d, p, dim3(d.BH, 1, d.V / 64), m_weights, m_do, m_s2, m_ff2,
+                             w.scan_tmp, st)))
+      return rc;
     ScoresParams sp{d.BH, d.H, d.TP, d.NT, 128, d.V, kPublic4D, kPublic4D, s.G, 1.f, w.A, w.Bp};
     CYFA_LAUNCH("tile_scores", st,
                 (launch_k(tile_scores_kernel, scores_grid, kScoresThreads, kScoresSmem, st,
@@ -405,10 +473,9 @@ int cyfa_chunk_bwd(const cyfa_chunk_bwd_args* g, const void* saved, size_t saved
     CUtensorMap m_f1, m_ff1;
     if ((rc = tmap_2d(&m_f1, s.s1, uint64_t(d.BH) * d.NT * d.K, 128, 128))) return rc;
     if ((rc = tmap_2d(&m_ff1, s.s1_fin, uint64_t(d.BH) * d.K, 128, 128))) return rc;
-    CYFA_LAUNCH("state_scan_bwd", st,
-                (launch_k(state_scan_kernel<true>, dim3(d.BH, d.K / 128, 2), kScanThreads, kScanSmem, st, 
-                    m_qn, m_draw, m_f1, m_ff1, p)));
-    if ((rc = launch_status())) return rc;
+    if ((rc = run_scan<true>(d, p, dim3(d.BH, d.K / 128, 2), m_qn, m_draw, m_f1, m_ff1,
+                             w.scan_tmp, st)))
+      return rc;
     ScoresParams sp{d.BH, d.H, d.TP, d.NT, d.K, 128, kRows2D, kRows2D, s.G, a->scale, w.A,
                     w.Bp};
     CYFA_LAUNCH("tile_scores", st,

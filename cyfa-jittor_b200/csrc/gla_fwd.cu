@@ -77,6 +77,15 @@ struct ScanParams {
   __nv_bfloat16* last_bf;   // forward: bf16 copy of the final state [BH, DK, DV], or null
   float* bpart;             // reverse: [BH, NT, nsub, 4] partial boundary terms
   const float* final_f32;   // reverse: the forward final state [BH, DK, DV] fp32, or null
+  // Segmented scan (tiles split into nseg segments of seg_tiles, grid z = V slices
+  // x segments).  summary != 0: each segment runs from zero (the segment holding
+  // the sequence's first tile in scan order from `init`), writes only its end
+  // state to seg_out [nseg, BH, DK, DV], no history, no boundary terms.
+  // summary == 0 with nseg > 1: segment s starts from seg_init[s] (the carry
+  // formed by scan_carry_kernel) unless it holds the first tile.
+  int nseg, seg_tiles, summary;
+  const float* seg_init;
+  float* seg_out;
 };
 
 // Ring of the scan: forward stages hold the K tile (32 KiB) and the V tile
@@ -147,8 +156,18 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   __shared__ int s_abort;
   volatile int* abort_flag = &s_abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = blockIdx.x, dk0 = blockIdx.y * 128, dv0 = blockIdx.z * 64;
+  const int nvs = p.DV / 64;
+  const int bh = blockIdx.x, dk0 = blockIdx.y * 128, vs = blockIdx.z % nvs, seg = blockIdx.z / nvs;
+  const int dv0 = vs * 64;
   const int NT = p.NT;
+  // this CTA's tiles [t0, t1), walked backwards in REVERSE
+  const int t0 = seg * p.seg_tiles, t1 = min(t0 + p.seg_tiles, NT);
+  const int nloc = t1 > t0 ? t1 - t0 : 0;
+  // the segment holding the first tile in scan order starts from `init`
+  const bool first_seg = REVERSE ? (t1 == NT) : (t0 == 0);
+  // the segment holding the last tile in scan order writes the final outputs
+  const bool last_seg = REVERSE ? (t0 == 0) : (t1 == NT);
+  const bool with_f = REVERSE && !p.summary;  // boundary terms need S_{j+1}
   static_assert(kScanStages <= kScanBufs, "stage reuse relies on mma_done parity");
 
   if (tid == 0) {
@@ -180,30 +199,30 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   pdl_wait();
   pdl_trigger();
   const uint32_t tmem = tmem_base;
-  auto tile_of = [&](int idx) { return REVERSE ? NT - 1 - idx : idx; };
+  auto tile_of = [&](int idx) { return REVERSE ? t1 - 1 - idx : t0 + idx; };
   const float* Gbh = p.G + size_t(bh) * p.TP;
 
   if (warp == 8) {
     // ------------------------------------------------ producer
     if (lane == 0) {
       int issued = 0;
-      for (int idx = 0; idx < NT; ++idx) {
+      for (int idx = 0; idx < nloc; ++idx) {
         if (*abort_flag) break;
         const int s = idx % kScanStages, j = tile_of(idx);
         if (idx >= kScanStages) {
           const int prev = idx - kScanStages;  // previous tile of this stage
           bool ok = mbar_wait(&mma_done[prev % kScanBufs], (prev / kScanBufs) & 1);
-          if (REVERSE && ok) ok = mbar_wait(&f_free[s], (prev / kScanStages) & 1);
+          if (with_f && ok) ok = mbar_wait(&f_free[s], (prev / kScanStages) & 1);
           if (!ok) {
             *abort_flag = 1;
             break;
           }
         }
         uint8_t* st = smem + s * kScanStageBytes;
-        mbar_expect_tx(&full[s], kScanStageBytes);
+        mbar_expect_tx(&full[s], with_f ? 65536 : 49152);
         load_token_tile(st, &map_k, p.k_mode, bh, p.H, p.TP, j, dk0, 128, &full[s]);
         load_token_tile(st + 32768, &map_v, p.v_mode, bh, p.H, p.TP, j, dv0, 64, &full[s]);
-        if (REVERSE) {
+        if (with_f) {
           if (j + 1 < NT)
             tma_load_2d(st + 49152, &map_f, &full[s], dv0, (bh * NT + j + 1) * p.DK + dk0);
           else
@@ -220,7 +239,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = make_idesc(128, 64, 1, 1);
       int last_commit = -1;
-      for (int idx = 0; idx < NT; ++idx) {
+      for (int idx = 0; idx < nloc; ++idx) {
         if (*abort_flag) break;
         const int s = idx % kScanStages, b = idx % kScanBufs;
         bool ok = mbar_wait(&scaled[s], (idx / kScanStages) & 1);
@@ -245,14 +264,14 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     // ------------------------------------------------ scalers
     const int srow = tid - 128;
     float gt_n = 0.f, gl_n = 0.f;
-    if (NT > 0) {
+    if (nloc > 0) {
       gt_n = Gbh[size_t(tile_of(0)) * 128 + srow];
       gl_n = Gbh[size_t(tile_of(0)) * 128 + 127];
     }
-    for (int idx = 0; idx < NT; ++idx) {
+    for (int idx = 0; idx < nloc; ++idx) {
       const int s = idx % kScanStages;
       const float gt = gt_n, gl = gl_n;
-      if (idx + 1 < NT) {
+      if (idx + 1 < nloc) {
         gt_n = Gbh[size_t(tile_of(idx + 1)) * 128 + srow];
         gl_n = Gbh[size_t(tile_of(idx + 1)) * 128 + 127];
       }
@@ -280,8 +299,11 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     // ------------------------------------------------ consumers: the recurrence
     float S[64];
     const size_t row_off = (size_t(bh) * p.DK + dk0 + tid) * p.DV + dv0;
-    if (p.init) {
-      const float4* src = reinterpret_cast<const float4*>(p.init + row_off);
+    const float* init = first_seg ? p.init
+                        : (p.summary ? nullptr
+                                     : p.seg_init + size_t(seg) * p.BH * p.DK * p.DV);
+    if (init) {
+      const float4* src = reinterpret_cast<const float4*>(init + row_off);
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const float4 x = src[i];
@@ -296,16 +318,16 @@ __global__ void __launch_bounds__(kScanThreads, 1)
     }
     const uint32_t lane_tmem = tmem + ((warp * 32) << 16);
     const uint32_t scratch = smem_u32(smem) + kScanStages * kScanStageBytes + warp * 4096;
-    const int nsub = gridDim.y * gridDim.z, sub = blockIdx.y * gridDim.z + blockIdx.z;
+    const int nsub = gridDim.y * nvs, sub = blockIdx.y * nvs + vs;
     bool ok = true;
     // the gate total of the next tile is loaded one iteration ahead
-    float gl_next = NT > 0 ? Gbh[size_t(tile_of(0)) * 128 + 127] : 0.f;
-    for (int idx = 0; idx < NT; ++idx) {
+    float gl_next = nloc > 0 ? Gbh[size_t(tile_of(0)) * 128 + 127] : 0.f;
+    for (int idx = 0; idx < nloc; ++idx) {
       const int j = tile_of(idx), b = idx % kScanBufs;
       const float gl = gl_next;
-      if (idx + 1 < NT) gl_next = Gbh[size_t(tile_of(idx + 1)) * 128 + 127];
+      if (idx + 1 < nloc) gl_next = Gbh[size_t(tile_of(idx + 1)) * 128 + 127];
       // state entering tile j (forward) / adjoint leaving tile j (reverse)
-      {
+      if (!p.summary) {
         uint4 packed[8];
 #pragma unroll
         for (int c = 0; c < 8; ++c)
@@ -317,7 +339,7 @@ __global__ void __launch_bounds__(kScanThreads, 1)
                            p.DV);
       }
       bool got = __all_sync(0xffffffffu, mbar_wait(&mma_done[b], (idx / kScanBufs) & 1));
-      if constexpr (REVERSE) {
+      if (with_f) {
         // <S_{j+1}, H_{j+1}> over this CTA's slice; S holds H_{j+1} until the update
         const int s = idx % kScanStages;
         got = got && __all_sync(0xffffffffu, mbar_wait(&full[s], (idx / kScanStages) & 1));
@@ -370,14 +392,21 @@ __global__ void __launch_bounds__(kScanThreads, 1)
         break;
       }
     }
+    // a summary pass: the segment's end state, for scan_carry_kernel
+    if (ok && p.summary) {
+      float4* dst = reinterpret_cast<float4*>(p.seg_out + size_t(seg) * p.BH * p.DK * p.DV + row_off);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        dst[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
+    }
     // the final state (forward) / initial-state adjoint (reverse)
-    if (ok && p.last) {
+    if (ok && !p.summary && last_seg && p.last) {
       float4* dst = reinterpret_cast<float4*>(p.last + row_off);
 #pragma unroll
       for (int i = 0; i < 16; ++i)
         dst[i] = make_float4(S[4 * i], S[4 * i + 1], S[4 * i + 2], S[4 * i + 3]);
     }
-    if (!REVERSE && ok && p.last_bf) {
+    if (!REVERSE && ok && !p.summary && last_seg && p.last_bf) {
       uint4 packed[8];
 #pragma unroll
       for (int c = 0; c < 8; ++c)
@@ -393,6 +422,47 @@ __global__ void __launch_bounds__(kScanThreads, 1)
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 64 * kScanBufs);
+  }
+}
+
+// Carries of the segmented scan (one thread per 4 state elements of one (b, h)):
+// the state entering each segment from the summaries E_s of the segments before
+// it (forward) or after it (reverse):
+//   forward  C_1 = E_0,      C_{s+1} = Gamma_s C_s + E_s
+//   reverse  D_{n-2} = E_{n-1}, D_{s-1} = Gamma_s D_s + E_s
+// Gamma_s = the product over the segment's tiles of their decay 2^{G_last},
+// formed in the scan's own order.  Writes seg_init[s] for every segment but the
+// one holding the first tile.
+template <bool REVERSE>
+__global__ void __launch_bounds__(256) scan_carry_kernel(const float* G, int TP, int NT, int BH,
+                                                         int elems, int nseg, int seg_tiles,
+                                                         const float* seg_out, float* seg_init) {
+  pdl_wait();
+  pdl_trigger();
+  const int bh = blockIdx.y;
+  const int e = (blockIdx.x * 256 + threadIdx.x) * 4;
+  if (e >= elems) return;
+  const size_t stride = size_t(BH) * elems, base = size_t(bh) * elems + e;
+  const float* Gbh = G + size_t(bh) * TP;
+  auto gamma = [&](int s) {
+    float gm = 1.f;
+    const int a = s * seg_tiles, b = min(a + seg_tiles, NT);
+    if (REVERSE)
+      for (int j = b - 1; j >= a; --j) gm *= exp2f(Gbh[size_t(j) * 128 + 127]);
+    else
+      for (int j = a; j < b; ++j) gm *= exp2f(Gbh[size_t(j) * 128 + 127]);
+    return gm;
+  };
+  const int first = REVERSE ? nseg - 1 : 0;
+  float4 c = *reinterpret_cast<const float4*>(seg_out + first * stride + base);
+  for (int k = 1; k < nseg; ++k) {
+    const int s = REVERSE ? nseg - 1 - k : k;
+    *reinterpret_cast<float4*>(seg_init + s * stride + base) = c;
+    if (k + 1 < nseg) {
+      const float gm = gamma(s);
+      const float4 x = *reinterpret_cast<const float4*>(seg_out + s * stride + base);
+      c = make_float4(c.x * gm + x.x, c.y * gm + x.y, c.z * gm + x.z, c.w * gm + x.w);
+    }
   }
 }
 

@@ -114,6 +114,8 @@ def lib():
         handle.cyfa_profile_enable.restype = ctypes.c_int
         handle.cyfa_set_pdl.argtypes = [ctypes.c_int]
         handle.cyfa_set_pdl.restype = ctypes.c_int
+        handle.cyfa_set_scan_split.argtypes = [ctypes.c_int]
+        handle.cyfa_set_scan_split.restype = ctypes.c_int
         handle.cyfa_set_aux_stream.argtypes = [ctypes.c_void_p]
         handle.cyfa_set_aux_stream.restype = ctypes.c_int
         handle.cyfa_profile_report.argtypes = [ctypes.c_int, ctypes.POINTER(ctypes.c_char_p),
@@ -184,6 +186,12 @@ def set_pdl(on=True):
     """Programmatic dependent launch of the library's kernels on/off; returns
     the previous setting."""
     return bool(lib().cyfa_set_pdl(1 if on else 0))
+
+
+def set_scan_split(on=True):
+    """Segmented state scans (more parallelism for few sequences x heads) on/off;
+    returns the previous setting."""
+    return bool(lib().cyfa_set_scan_split(1 if on else 0))
 
 
 def profile_enable(on=True):

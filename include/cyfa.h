@@ -53,6 +53,13 @@ long long cyfa_launch_count(void);
  * order.  Returns the previous setting. */
 int cyfa_set_pdl(int on);
 
+/* State scans with fewer CTAs than SMs (few sequences x heads, long sequences)
+ * split their tiles into segments scanned side by side: a pass from zero per
+ * segment, the carried states, and the real pass from them.  On (1, the
+ * default) or off (0: one serial pass per state slice, the same summation order
+ * at every batch size).  Returns the previous setting. */
+int cyfa_set_scan_split(int on);
+
 /* Auxiliary stream of the calling thread, or NULL (the default) for none.
  * While set, the entry points called on this thread launch their final
  * parameter-gradient reductions (norm-weight, convolution, gate-parameter and

@@ -188,6 +188,11 @@ def test_chunk_batched_matches_per_sequence(ops, K, V):
     B, T, H = 8, 2048, 4
     ins, state = make_inputs(B, T, H, K, V, seed=K + V, with_state=True)
     do = torch.randn(B, T, H, V, generator=seeded(9)).to(torch.bfloat16).cuda()
+    from cyclic_flow_attention import _lib
+
+    # one serial scan per state slice at every batch size (a single sequence
+    # would otherwise get segmented scans, another summation order)
+    prev_split = _lib.set_scan_split(False)
 
     def run(sl):
         dev = [x[sl].cuda().requires_grad_(True) if i < 6 else x.cuda().requires_grad_(True)
@@ -197,9 +202,12 @@ def test_chunk_batched_matches_per_sequence(ops, K, V):
         (o.float() * do[sl].float()).sum().backward()
         return o.detach(), [x.grad for x in dev] + [x.grad for x in st]
 
-    o_all, g_all = run(slice(0, B))
-    per = [run(slice(b, b + 1)) for b in range(B)]
-    torch.cuda.synchronize()
+    try:
+        o_all, g_all = run(slice(0, B))
+        per = [run(slice(b, b + 1)) for b in range(B)]
+        torch.cuda.synchronize()
+    finally:
+        _lib.set_scan_split(prev_split)
     assert torch.equal(o_all, torch.cat([p[0] for p in per]))
     # per-token tensors: q k v g delta beta and the initial-state grads (batch dim 0)
     for i in list(range(6)) + [9, 10, 11]:
@@ -211,4 +219,47 @@ def test_chunk_batched_matches_per_sequence(ops, K, V):
         assert rel_l2(g_all[i], want) <= 1e-5, i
     from cyclic_flow_attention import _lib
 
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("B,T,H,K,V", [(1, 2048, 1, 256, 256), (1, 4096, 2, 128, 256),
+                                       (2, 1100, 1, 256, 128)])
+def test_segmented_scans_match_serial(ops, B, T, H, K, V):
+    """With few sequences x heads the state scans split their tiles into
+    segments scanned side by side (summary pass, carries, real pass): outputs,
+    final states and every gradient equal the one-serial-pass result up to
+    fp32 summation order, and the oracle to the usual tolerances."""
+    from cyclic_flow_attention import _lib
+
+    ins, state = make_inputs(B, T, H, K, V, seed=T + K, with_state=True)
+    gen = seeded(T)
+    do = torch.randn(B, T, H, V, generator=gen).to(torch.bfloat16).cuda()
+    dst = (torch.randn(B, H, K, 128, generator=gen).cuda(),
+           torch.randn(B, H, 128, V, generator=gen).cuda(), torch.randn(B, H, generator=gen).cuda())
+
+    def run(split):
+        prev = _lib.set_scan_split(split)
+        try:
+            dev = [x.cuda().requires_grad_(True) for x in ins]
+            st = tuple(x.cuda().requires_grad_(True) for x in state)
+            o, fs = ops.chunk_cyfa(*dev, initial_state=st, output_final_state=True)
+            loss = (o.float() * do.float()).sum() + sum((a * b).sum() for a, b in zip(fs, dst))
+            loss.backward()
+            torch.cuda.synchronize()
+        finally:
+            _lib.set_scan_split(prev)
+        return [o.detach()] + [x.detach() for x in fs] + [x.grad for x in dev] + \
+            [x.grad for x in st]
+
+    seg, ser = run(True), run(False)
+    names = ["o", "hk", "hv", "clock", "dq", "dk", "dv", "dg", "ddelta", "dbeta", "dreadout",
+             "dqw", "dkw", "dhk0", "dhv0", "dclock0"]
+    errs = {n: rel_l2(a, b) for n, a, b in zip(names, seg, ser)}
+    print("segmented vs serial", B, T, H, K, V, {k: float(f"{v:.3g}") for k, v in errs.items()})
+    for n, e in errs.items():
+        assert e < 2e-3, (n, e)
+    ref_o, ref_s = O.chunk_cyfa(*[x.float() for x in ins[:6]], *ins[6:], initial_state=state,
+                                output_final_state=True, dtype=torch.float32)
+    assert rel_l2(seg[0], ref_o) < BF16_TOL
+    assert rel_l2(seg[1], ref_s[0]) < BF16_TOL and rel_l2(seg[2], ref_s[1]) < BF16_TOL
     assert _lib.device_error() == 0
