@@ -14,4 +14,3 @@
 #include "noalloc.cu"
 #include "lm_decode.cu"
 #include "gradbuf.cu"
-#include "skinny_gemm.cu"

@@ -52,8 +52,6 @@ _SIGNATURES = {
     "cyfa_bucket_scatter": [_vp, _i, _vp, _f, _vp],
     "cyfa_adamw_step": [_vp, _i, _vp, _vp, _vp, _vp] + [_f] * 5 + [_i, _vp],
     "cyfa_grad_clip": [_vp, ctypes.c_longlong, _f, _vp, _vp, ctypes.c_size_t, _vp],
-    "cyfa_skinny_gemm": [_vp, ctypes.c_longlong, _vp, _vp, ctypes.c_longlong] + [_i] * 3
-    + [_vp, ctypes.c_size_t, _vp],
     "cyfa_add_rmsnorm": [_vp, _vp, _vp, _f, _vp, _i, _i, _vp],
     "cyfa_decode_conv": [_vp, ctypes.c_longlong] + [_vp] * 9 + [_i] * 5 + [_vp],
     "cyfa_swiglu": [_vp, _vp, _i, _i, _vp],
@@ -68,7 +66,6 @@ _SIZE_QUERIES = {
     "cyfa_gated_norm_work_bytes": [_i] * 2,
     "cyfa_gated_norm_bias_work_bytes": [_i] * 3,
     "cyfa_grad_clip_work_bytes": [],
-    "cyfa_skinny_gemm_work_bytes": [_i] * 3,
 }
 
 

@@ -23,7 +23,6 @@ from torch import nn
 from ..ops import chunk_cyfa, fused_recurrent_cyfa
 from .. import _lib
 from ..ops.chunk import readout_table, table_bf16
-from ..ops.gemm import decode_mm
 from ..ops.layer_ops import (
     ChunkCyfaPackedFunction,
     GatedNormFunction,
@@ -351,7 +350,7 @@ class CyclicFlowAttention(nn.Module):
         if wf is None:
             n = sum(w.shape[0] for w in ws)
             wf = torch.cat(ws + [ws[0].new_zeros((n + 7) // 8 * 8 - n, ws[0].shape[1])])
-        P = decode_mm(x.reshape(B, -1), wf)  # [B, q|k|v|g0|a|b|d (+pad)]
+        P = torch.mm(x.reshape(B, -1), wf.t())  # [B, q|k|v|g0|a|b|d (+pad)]
         hk, hv, clock = cache["recurrent_state"]
         cq, ck, cv = cache["conv_state"]
         dev = x.device
@@ -378,12 +377,12 @@ class CyclicFlowAttention(nn.Module):
                   p(c["q_norm"]), p(c["k_norm"]), p(hk), p(hv), p(clock), p(hk_o), p(hv_o),
                   p(clock_o), p(o), B, H, K, V, 0, float(self.q_norm.eps),
                   float(self.k_norm.eps), K ** -0.5, st)
-        gate = decode_mm(P[:, 2 * HK + HV:2 * HK + HV + V], self.g_proj[1].weight)
+        gate = torch.mm(P[:, 2 * HK + HV:2 * HK + HV + V], self.g_proj[1].weight.t())
         y = torch.empty(B, HV, device=dev, dtype=torch.bfloat16)
         rstd = torch.empty(B * H, device=dev, dtype=torch.float32)
         _lib.call("cyfa_gated_norm_bias_fwd", p(o), p(gate), p(c["g_bias"]), H, p(c["o_norm"]),
                   float(self.o_norm.eps), float(self.num_slots - 1), p(y), p(rstd), B * H, V, st)
-        out = decode_mm(y, self.o_proj.weight).reshape(B, 1, -1)
+        out = torch.mm(y, self.o_proj.weight.t()).reshape(B, 1, -1)
         return out, {"recurrent_state": (hk_o, hv_o, clock_o), "conv_state": (cq, ck, cv)}
 
     def forward(self, x, cache=None, use_cache=False, attention_mask=None):

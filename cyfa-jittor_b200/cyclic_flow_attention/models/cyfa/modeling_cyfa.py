@@ -26,7 +26,6 @@ from torch import nn
 
 from ... import _lib
 from ...layers.cyfa import CyclicFlowAttention, RMSNorm
-from ...ops.gemm import decode_mm
 from ...ops.layer_ops import packed_rows
 from .configuration_cyfa import CyclicFlowAttentionConfig
 
@@ -83,10 +82,10 @@ class GatedMLP(nn.Module):
         if wf is None:
             wf = torch.cat(ws)
         mid = self.intermediate_size
-        gu = decode_mm(h, wf)
+        gu = torch.mm(h, wf.t())
         act = torch.empty(h.shape[0], mid, device=h.device, dtype=h.dtype)
         _lib.call("cyfa_swiglu", _lib.ptr(gu), _lib.ptr(act), h.shape[0], mid, _lib.stream())
-        return decode_mm(act, self.down_proj.weight)
+        return torch.mm(act, self.down_proj.weight.t())
 
 
 class CyFABlock(nn.Module):
@@ -203,7 +202,7 @@ class CyclicFlowAttentionForCausalLM(nn.Module):
         norm = self.model.norm
         _lib.call("cyfa_add_rmsnorm", p(x), p(prev), p(_f32(norm.weight)), float(norm.eps), p(h),
                   B, D, st)
-        return decode_mm(h, self.lm_head.weight), new
+        return torch.mm(h, self.lm_head.weight.t()), new
 
     def to_bfloat16(self):
         """bf16 except the parameters the reference keeps in fp32."""

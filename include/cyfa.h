@@ -391,20 +391,6 @@ int cyfa_bucket_gather(const cyfa_bucket_piece* pieces, int count, float* flat, 
 int cyfa_bucket_scatter(const cyfa_bucket_piece* pieces, int count, const float* flat,
                         float scale, void* stream);
 
-/* ---------------------------------------------------------------- decode projections
- * y[M, N] = x[M, K] W[N, K]^T for M <= 256 rows (the projections of a batched
- * decode step: the packed q|k|v|g0|a|b|d projection, the output gate's second
- * linear, o_proj, the MLP and lm_head; reference models/cyfa/modeling_cyfa.py:13-55,
- * layers/cyfa.py:15-37).  x rows ldx elements apart, W contiguous (an
- * nn.Linear weight), y rows ldy apart, all bf16, 16-byte aligned; N % 8 == 0,
- * K % 64 == 0, ldx and ldy multiples of 8.  W is streamed from HBM once by TMA
- * into tcgen05 MMAs (fp32 accumulation in TMEM); narrow N is split along K with
- * fp32 partials in `work` (cyfa_skinny_gemm_work_bytes, 0 when not split)
- * summed in a fixed order. */
-size_t cyfa_skinny_gemm_work_bytes(int M, int N, int K);
-int cyfa_skinny_gemm(const void* x, long long ldx, const void* w, void* y, long long ldy, int M,
-                     int N, int K, void* work, size_t work_bytes, void* stream);
-
 /* ---------------------------------------------------------------- optimizer
  * AdamW with fp32 master weights and moments.  Replaces: AdamW.step,
  * training/optim.py:96-124.  The masters, moments and the (all-reduced,
