@@ -37,12 +37,13 @@ static Dims make_dims(int B, int T, int H, int K, int V) {
 // Segments of a state scan: when a scan has fewer CTAs than the SMs (few
 // sequences x heads, long sequences), its tiles are split
 // into segments scanned side by side (a summary pass from zero, the carries, and
-// the real pass from the carried states), at least 4 tiles each.
+// the real pass from the carried states), at least 16 tiles each, so that the
+// two extra launches pay off against the serial chain they shorten.
 // Tiles per segment; the segments are ceil(NT / that), none empty.
 static int scan_seg_tiles(const Dims& d, int ctas) {
   if (!g_scan_split.load(std::memory_order_relaxed)) return d.NT;
   int n = 148 / (ctas > 0 ? ctas : 1);
-  const int cap = d.NT / 4;
+  const int cap = d.NT / 16;
   if (n > cap) n = cap;
   return n < 2 ? d.NT : (d.NT + n - 1) / n;
 }
