@@ -256,9 +256,19 @@ def test_segmented_scans_match_serial(ops, B, T, H, K, V):
     names = ["o", "hk", "hv", "clock", "dq", "dk", "dv", "dg", "ddelta", "dbeta", "dreadout",
              "dqw", "dkw", "dhk0", "dhv0", "dclock0"]
     errs = {n: rel_l2(a, b) for n, a, b in zip(names, seg, ser)}
-    print("segmented vs serial", B, T, H, K, V, {k: float(f"{v:.3g}") for k, v in errs.items()})
+    # the carries round differently; bf16 histories pass that on as occasional
+    # one-ulp flips.  The clock gradients are suffix sums over the whole sequence:
+    # compared per term, and as sums within their condition number.
+    dd_seg, dd_ser = (x.permute(0, 2, 1) for x in (seg[8], ser[8]))
+    errs["ddelta_terms"] = rel_l2(suffix_terms(dd_seg), suffix_terms(dd_ser))
+    terms = suffix_terms(dd_ser)
+    kappa = {"ddelta": suffix_condition(terms),
+             "dclock0": (terms.abs().sum(-1).norm() / terms.sum(-1).norm()).item()}
+    print("segmented vs serial", B, T, H, K, V, {k: float(f"{v:.3g}") for k, v in errs.items()},
+          "kappa", {k: round(v, 1) for k, v in kappa.items()})
+    assert errs["hk"] < 1e-5 and errs["hv"] < 1e-5 and errs["clock"] < 1e-6
     for n, e in errs.items():
-        assert e < 2e-3, (n, e)
+        assert e < BF16_TOL * max(1.0, kappa.get(n, 1.0)), (n, e)
     ref_o, ref_s = O.chunk_cyfa(*[x.float() for x in ins[:6]], *ins[6:], initial_state=state,
                                 output_final_state=True, dtype=torch.float32)
     assert rel_l2(seg[0], ref_o) < BF16_TOL
