@@ -45,6 +45,7 @@ static int scan_seg_tiles(const Dims& d, int ctas) {
   int n = 148 / (ctas > 0 ? ctas : 1);
   const int cap = d.NT / 16;
   if (n > cap) n = cap;
+  if (n > kScanCarryMaxSegs) n = kScanCarryMaxSegs;
   return n < 2 ? d.NT : (d.NT + n - 1) / n;
 }
 static int scan_nseg(const Dims& d, int ctas) {

@@ -433,26 +433,32 @@ __global__ void __launch_bounds__(kScanThreads, 1)
 // Gamma_s = the product over the segment's tiles of their decay 2^{G_last},
 // formed in the scan's own order.  Writes seg_init[s] for every segment but the
 // one holding the first tile.
+constexpr int kScanCarryMaxSegs = 160;
+
 template <bool REVERSE>
 __global__ void __launch_bounds__(256) scan_carry_kernel(const float* G, int TP, int NT, int BH,
                                                          int elems, int nseg, int seg_tiles,
                                                          const float* seg_out, float* seg_init) {
+  __shared__ float s_gamma[kScanCarryMaxSegs];
   pdl_wait();
   pdl_trigger();
   const int bh = blockIdx.y;
-  const int e = (blockIdx.x * 256 + threadIdx.x) * 4;
-  if (e >= elems) return;
-  const size_t stride = size_t(BH) * elems, base = size_t(bh) * elems + e;
   const float* Gbh = G + size_t(bh) * TP;
-  auto gamma = [&](int s) {
+  // Gamma_s of every segment, one thread each (the tile decays read in parallel)
+  for (int s = threadIdx.x; s < nseg; s += blockDim.x) {
     float gm = 1.f;
     const int a = s * seg_tiles, b = min(a + seg_tiles, NT);
     if (REVERSE)
-      for (int j = b - 1; j >= a; --j) gm *= exp2f(Gbh[size_t(j) * 128 + 127]);
+      for (int j = b - 1; j >= a; --j) gm *= exp2f(__ldg(Gbh + size_t(j) * 128 + 127));
     else
-      for (int j = a; j < b; ++j) gm *= exp2f(Gbh[size_t(j) * 128 + 127]);
-    return gm;
-  };
+      for (int j = a; j < b; ++j) gm *= exp2f(__ldg(Gbh + size_t(j) * 128 + 127));
+    s_gamma[s] = gm;
+  }
+  __syncthreads();
+  const int e = (blockIdx.x * 256 + threadIdx.x) * 4;
+  if (e >= elems) return;
+  const size_t stride = size_t(BH) * elems, base = size_t(bh) * elems + e;
+  auto gamma = [&](int s) { return s_gamma[s]; };
   const int first = REVERSE ? nseg - 1 : 0;
   float4 c = *reinterpret_cast<const float4*>(seg_out + first * stride + base);
   for (int k = 1; k < nseg; ++k) {
