@@ -185,17 +185,18 @@ def cpu_model_name():
     return None
 
 
-def _cpu_layer_step(T):
+def _cpu_layer_step(T, cfg=None):
     """One step of the oracle layer forward + backward (fp32, all host threads)
-    on one sequence of T tokens of the workload's layer config: the reference's
-    algorithm restated on the host cores."""
+    on one sequence of T tokens of the workload's layer config (or `cfg`): the
+    reference's algorithm restated on the host cores."""
     import torch
 
     from oracle import cyfa_oracle as O
 
+    cfg = cfg or CFG
     torch.set_num_threads(os.cpu_count() or 1)
     gen = torch.Generator().manual_seed(0)
-    H, hd, hid = CFG["heads"], CFG["head_dim"], CFG["hidden"]
+    H, hd, hid = cfg["heads"], cfg["head_dim"], cfg["hidden"]
     shapes = {
         "q_proj.weight": (H * hd, hid), "k_proj.weight": (H * hd, hid),
         "v_proj.weight": (H * hd, hid), "a_proj.weight": (H, hid), "b_proj.weight": (H, hid),
@@ -545,6 +546,88 @@ def measure_lm_decode(args, rank, world, dev, peaks, barrier):
             "launch": "one CUDA graph replay per step (embedding, 24 layers, norm, lm_head, argmax)"}
 
 
+def measure_c5(args, rank, world, dev, peaks, barrier):
+    """BASELINE configs[4], long context: the layer forward + backward at hidden
+    2048, 8 x 256 heads, 128 slots, one 32768-token sequence per GPU (weak
+    scaling: the 8-sequence batch over 8 GPUs), bf16, the step captured as one
+    CUDA graph with the weight-gradient all-reduce when N > 1.  CUDA events per
+    step, L2 flushed between steps; the CPU baseline times the oracle on 4096
+    tokens and scales linearly (the chunked cost is linear in T)."""
+    import torch
+    import torch.distributed as dist
+
+    from cyclic_flow_attention import CyclicFlowAttention
+    from cyclic_flow_attention.distributed import GradientBuckets
+    from cyclic_flow_attention.graphs import GraphedStep
+
+    B, T, hid = C5["B"], C5["T"], C5["hidden"]
+    torch.manual_seed(0)
+    layer = CyclicFlowAttention(hid, C5["heads"], C5["head_dim"], num_slots=C5["slots"])
+    with torch.no_grad():
+        for name, p in layer.named_parameters():
+            if p.dim() >= 2 and name != "readout":
+                p.normal_(0, 0.02)
+    layer = layer.keep_fp32().to(dev)
+    params = list(layer.parameters())
+    gen = torch.Generator(device=dev).manual_seed(2000 + rank)
+    x = torch.randn(B, T, hid, device=dev, generator=gen).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(B, T, hid, device=dev, generator=gen).to(torch.bfloat16)
+    buckets = None
+    if world > 1:
+        buckets = GradientBuckets(params, groups=[sum(layer.grad_groups(), [])])
+        layer.grad_ready = buckets.early
+
+    def step(xin, dyin):
+        for p in params:
+            p.grad = None
+        xin.grad = None
+        y, _ = layer(xin)
+        y.backward(dyin)
+        if buckets is not None:
+            buckets.finish()
+        return y[:, -1].sum(dtype=torch.float32)
+
+    graphed = GraphedStep(step, [x, dy], params, warmup=3)
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev)
+    n = max(3, min(args.steps, 8))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n)]
+    barrier()
+    for a, b in evs:
+        flush.fill_(1)
+        a.record()
+        graphed.replay()
+        b.record()
+    barrier()
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs) / n], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    flop = T * B * (3 * 35_749_888 + C5["heads"] * (OP_FLOPS_FWD + OP_FLOPS_BWD))
+    tf = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    out = {"workload": "cyfa_layer_fwd_bwd long context, BASELINE configs[4]: hidden 2048, "
+                       "8x256 heads, 128 slots, one 32768-token sequence per GPU, bf16",
+           "tokens_per_s": world * B * T / (ms / 1000.0), "ms_per_step": ms,
+           "tensor_frac_of_burst": flop / (ms / 1000.0) / 1e12 / tf,
+           "l2": "flushed between timed steps"}
+    del graphed
+    if buckets is not None:
+        buckets.remove()
+    torch.cuda.empty_cache()
+    if rank == 0 and world == 1 and not args.no_cpu:
+        step_cpu = _cpu_layer_step(4096, C5)
+        step_cpu()
+        t0 = time.perf_counter()
+        step_cpu()
+        dt = time.perf_counter() - t0
+        out["cpu_baseline"] = {
+            "value": 4096 / dt, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "port",
+            "cpu": cpu_model_name(),
+            "sample": "1 x (1 seq x 4096 tokens) layer fwd+bwd at the configs[4] layer, fp32 "
+                      "oracle; tokens/s extrapolated to T=32768 (linear cost)"}
+    return out
+
+
 # ---------------------------------------------------------------- GPU arm
 def run_cyfa(args, rank, world, local_rank):
     import torch
@@ -772,6 +855,8 @@ def run_cyfa(args, rank, world, local_rank):
     decode = None if args.no_decode else measure_decode(args, rank, world, dev, peaks, barrier)
     op = None if args.no_op else measure_op(args, rank, world, dev, peaks, barrier)
     decode_lm = None if args.no_lm else measure_lm_decode(args, rank, world, dev, peaks, barrier)
+    long_ctx = None if (args.no_c5 or args.workload == "c5") else \
+        measure_c5(args, rank, world, dev, peaks, barrier)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -804,6 +889,7 @@ def run_cyfa(args, rank, world, local_rank):
             "decode": decode,
             "decode_lm": decode_lm,
             "op": op,
+            "c5": long_ctx,
         }
         print(json.dumps(line), flush=True)
     # a graph that holds NCCL calls must be gone before the process group is
@@ -833,6 +919,8 @@ def main():
     ap.add_argument("--lm-batch", type=int, default=0,
                     help="LM decode leg: batch over all ranks (default 256, configs[3])")
     ap.add_argument("--no-op", action="store_true", help="skip the chunk_cyfa op leg (configs[1])")
+    ap.add_argument("--no-c5", action="store_true",
+                    help="skip the long-context leg (configs[4], one 32768-token sequence per GPU)")
     ap.add_argument("--workload", choices=("c3", "c5"), default="c3",
                     help="layer config: c3 (BASELINE configs[2], default) or c5 (long context, "
                          "configs[4], one 32768-token sequence per GPU)")
