@@ -11,6 +11,7 @@
 #include "capi.cu"
 #include "chunk_api.cu"
 #include "layer_api.cu"
+#include "gate_norm.cu"
 #include "noalloc.cu"
 #include "lm_decode.cu"
 #include "gradbuf.cu"

@@ -119,6 +119,27 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, uint64_
       "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
 }
+// Tiled tensor store from shared memory (bulk async group of the issuing
+// thread).  Rows or columns outside the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const void* tmap, const void* src, int x, int y,
+                                             int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          tmap),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Waits until the committed bulk stores of this thread have read their shared
+// memory sources (the buffers may be reused), or until they are complete.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
 // Coalesced warp load of a 32-row x 32-column bf16 block (the inverse of
 // warp_store_block_bf16, in two steps so that the global loads can be issued
 // early): warp_fetch_block_bf16 reads 8 rows x 64 contiguous bytes per

@@ -102,16 +102,21 @@ __global__ void __launch_bounds__(256) decode_conv_kernel(DecodeConvParams p) {
   int s = 0;
   if (c >= p.C[0]) { c -= p.C[0]; s = 1; }
   if (s == 1 && c >= p.C[1]) { c -= p.C[1]; s = 2; }
-  const int C = p.C[s];
+  // select the convolution's pointers without indexing the parameter arrays by
+  // a runtime value (which would copy them to local memory in every thread)
+  const int C = s == 0 ? p.C[0] : (s == 1 ? p.C[1] : p.C[2]);
+  __nv_bfloat16* const cache_s = s == 0 ? p.cache[0] : (s == 1 ? p.cache[1] : p.cache[2]);
+  const float* const w_s = s == 0 ? p.w[0] : (s == 1 ? p.w[1] : p.w[2]);
+  __nv_bfloat16* const y_s = s == 0 ? p.y[0] : (s == 1 ? p.y[1] : p.y[2]);
   __align__(16) __nv_bfloat16 hist[W][8];  // W-1 cached rows, then the new token
-  __nv_bfloat16* cache = p.cache[s] + (size_t)b * (W - 1) * C + c;
+  __nv_bfloat16* cache = cache_s + (size_t)b * (W - 1) * C + c;
 #pragma unroll
   for (int r = 0; r < W - 1; ++r)
     *reinterpret_cast<int4*>(hist[r]) = *reinterpret_cast<const int4*>(cache + (size_t)r * C);
   *reinterpret_cast<int4*>(hist[W - 1]) =
       *reinterpret_cast<const int4*>(p.x + (size_t)b * p.x_stride + col);
   float w[8 * W];
-  const float4* w4 = reinterpret_cast<const float4*>(p.w[s] + (size_t)c * W);
+  const float4* w4 = reinterpret_cast<const float4*>(w_s + (size_t)c * W);
 #pragma unroll
   for (int q = 0; q < 2 * W; ++q) {
     const float4 f = w4[q];
@@ -128,7 +133,7 @@ __global__ void __launch_bounds__(256) decode_conv_kernel(DecodeConvParams p) {
     for (int r = 1; r < W; ++r) acc += __bfloat162float(hist[r][j]) * w[j * W + r];
     out[j] = __float2bfloat16_rn(acc);
   }
-  *reinterpret_cast<int4*>(p.y[s] + (size_t)b * C + c) = *reinterpret_cast<int4*>(out);
+  *reinterpret_cast<int4*>(y_s + (size_t)b * C + c) = *reinterpret_cast<int4*>(out);
 #pragma unroll
   for (int r = 0; r < W - 1; ++r)
     *reinterpret_cast<int4*>(cache + (size_t)r * C) = *reinterpret_cast<int4*>(hist[r + 1]);

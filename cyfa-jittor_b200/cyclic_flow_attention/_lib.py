@@ -43,6 +43,8 @@ _SIGNATURES = {
                             ctypes.c_size_t, _vp],
     "cyfa_gated_norm_bwd_static": [_vp, _vp, _vp, _f, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp],
     "cyfa_gated_norm_bias_fwd": [_vp, _vp, _vp, _i, _vp, _f, _f, _vp, _vp, _i, _i, _vp],
+    "cyfa_gated_norm_gate_fwd": [_vp, _vp, ctypes.c_longlong, _vp, _vp, _i, _i, _vp, _f, _f,
+                                 _vp, _vp, _vp, _i, _i, _vp],
     "cyfa_gated_norm_bias_bwd": [_vp, _vp, _vp, _i, _vp, _f, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _i, _i, _vp, ctypes.c_size_t, _vp],
     "cyfa_chunk_bwd": [_vp, _vp, ctypes.c_size_t, _vp, ctypes.c_size_t, _vp],

@@ -7,9 +7,10 @@ module tree and parameter names (``model.embeddings``, ``model.layers.N.attn``,
 (``cyclic_flow_attention.utils.load_model``).
 
 Two execution paths:
-* ``forward`` over a sequence (training, prefill): the attention layer's fused
-  path, with the block norms and the gated MLP in PyTorch as the reference
-  computes them (fp32 math, bf16 results).
+* ``forward`` over a sequence: with gradients (training) the attention layer's
+  fused path with the block norms and the gated MLP in PyTorch as the reference
+  computes them (fp32 math, bf16 results); without (prefill) the same glue
+  launches as the decode step below.
 * ``decode_step`` for one token per sequence with a cache: every piece of glue
   is one libcyfa launch (``cyfa_add_rmsnorm`` for residual + norm,
   ``cyfa_swiglu`` for the MLP activation) around cuBLAS GEMMs on packed
@@ -117,13 +118,49 @@ class CyclicFlowAttentionModel(nn.Module):
         self.layers = nn.ModuleList([CyFABlock(config) for _ in range(config.num_hidden_layers)])
         self.norm = RMSNorm(config.hidden_size, config.norm_eps)
 
+    def _glue_ok(self, input_ids):
+        w = self.embeddings.weight
+        D = w.shape[1]
+        return (not torch.is_grad_enabled() and w.is_cuda and w.dtype == torch.bfloat16
+                and input_ids.is_cuda and D % 8 == 0 and D <= 8192
+                and all(l.mlp.intermediate_size % 8 == 0 for l in self.layers))
+
     def forward(self, input_ids, cache=None, use_cache=False, attention_mask=None):
+        if self._glue_ok(input_ids):
+            return self._forward_glue(input_ids, cache, use_cache, attention_mask)
         x = self.embeddings(input_ids)
         new = []
         for i, layer in enumerate(self.layers):
             x, s = layer(x, None if cache is None else cache[i], use_cache, attention_mask)
             new.append(s)
         return self.norm(x), new if use_cache else None
+
+    def _forward_glue(self, input_ids, cache, use_cache, attention_mask):
+        """Inference over a sequence (prefill): the blocks of ``forward`` with
+        their glue as libcyfa launches, as ``decode_step`` runs it.  The residual
+        stream stays in one bf16 buffer: each cyfa_add_rmsnorm adds the previous
+        branch output into it (rounded to bf16 as the reference's ``x + y``) and
+        normalises it for the next branch; the MLP is one GEMM on the packed
+        gate|up weights, cyfa_swiglu and down_proj."""
+        x = self.embeddings(input_ids).contiguous()
+        B, T, D = x.shape
+        rows = B * T
+        h = torch.empty_like(x)
+        p, st = _lib.ptr, _lib.stream()
+        prev = None
+        new = []
+        for i, layer in enumerate(self.layers):
+            _lib.call("cyfa_add_rmsnorm", p(x), p(prev), p(_f32(layer.attn_norm.weight)),
+                      float(layer.attn_norm.eps), p(h), rows, D, st)
+            y, s = layer.attn(h, None if cache is None else cache[i], use_cache, attention_mask)
+            new.append(s)
+            _lib.call("cyfa_add_rmsnorm", p(x), p(y.contiguous()),
+                      p(_f32(layer.mlp_norm.weight)), float(layer.mlp_norm.eps), p(h), rows, D,
+                      st)
+            prev = layer.mlp.decode(h.view(rows, D))
+        _lib.call("cyfa_add_rmsnorm", p(x), p(prev), p(_f32(self.norm.weight)),
+                  float(self.norm.eps), p(h), rows, D, st)
+        return h, new if use_cache else None
 
 
 class CyclicFlowAttentionForCausalLM(nn.Module):

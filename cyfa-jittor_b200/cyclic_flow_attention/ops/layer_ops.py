@@ -174,24 +174,61 @@ class GateActFunction(torch.autograd.Function):
         return (daux, dd, dA.to(adt), ddtb.to(ddt), dbb.to(bdt), ddb.to(dbt), None, None, None)
 
 
+def _gate_rows_stride(gate_in, gate_w, D):
+    """Row stride (elements) of gate_in [B,T,Kg] when the fused gate + norm
+    kernel can read it (bf16, unit column stride, tokens uniformly strided,
+    16-byte aligned rows, Kg a multiple of 64), else None."""
+    if (gate_in.dtype != torch.bfloat16 or gate_w.dtype != torch.bfloat16 or gate_in.dim() != 3
+            or D not in (128, 256) or gate_in.shape[-1] % 64 or not gate_w.is_contiguous()):
+        return None
+    B, T, Kg = gate_in.shape
+    s0, s1, s2 = gate_in.stride()
+    if s2 != 1 or (B > 1 and s0 != T * s1) or s1 < Kg or s1 % 8 or gate_in.data_ptr() % 16:
+        return None
+    return s1
+
+
+def gated_norm_infer(x, gate_in, gate_w, gate_b, weight, eps, scale):
+    """GatedNormFunction's forward without autograd (inference): the gate's
+    second linear runs inside the norm kernel (cyfa_gated_norm_gate_fwd: tcgen05
+    per 128-token tile and head, the gate rounded to bf16 as a bf16 linear's
+    output is), so the gate never goes to memory.  Returns None for inputs the
+    kernel does not take (the caller then uses GatedNormFunction)."""
+    B, T, H, D = x.shape
+    stride = _gate_rows_stride(gate_in, gate_w, D)
+    if stride is None or x.dtype != torch.bfloat16 or not x.is_contiguous():
+        return None
+    w = weight.detach().float().contiguous()
+    b = None if gate_b is None else gate_b.detach().to(torch.bfloat16).contiguous()
+    y = torch.empty(B, T, H * D, device=x.device, dtype=torch.bfloat16)
+    rstd = torch.empty(B * T * H, device=x.device, dtype=torch.float32)
+    _lib.call("cyfa_gated_norm_gate_fwd", _p(x), _p(gate_in), _c.c_longlong(stride),
+              _p(gate_w.detach()), _p(b), H, gate_in.shape[-1], _p(w), float(eps), float(scale),
+              _p(y), _p(rstd), None, B * T, D, _lib.stream())
+    return y
+
+
 class GatedNormFunction(torch.autograd.Function):
     """y = RMSNorm(scale * x) * w * sigmoid(gate) over the last dim D of
     x [B,T,H,D], with gate = gate_in @ W^T + b (the output gate's second linear,
     [B,T,H*D]); returns [B,T,H*D] bf16.  The linear runs on cuBLAS without its
-    bias; the kernels add b and return its gradient (fixed-order sums)."""
+    bias and the gate is kept for the backward (writing it from the fused
+    kernel of gated_norm_infer measured slower than the separate linear); the
+    kernels add b and return its gradient (fixed-order sums)."""
 
     @staticmethod
     def forward(ctx, x, gate_in, gate_w, gate_b, weight, eps, scale, slot=None, gate_param=None):
         B, T, H, D = x.shape
         rows = B * T * H
         x = x.to(torch.bfloat16).contiguous()
-        gate = torch.nn.functional.linear(gate_in, gate_w).contiguous()
         w = weight.detach().float().contiguous()
         y = torch.empty(B, T, H * D, device=x.device, dtype=torch.bfloat16)
         rstd = torch.empty(rows, device=x.device, dtype=torch.float32)
         b = None
         if gate_b is not None:
             b = gate_b.detach().to(torch.bfloat16).contiguous()
+        gate = torch.nn.functional.linear(gate_in, gate_w).contiguous()
+        if b is not None:
             _lib.call("cyfa_gated_norm_bias_fwd", _p(x), _p(gate), _p(b), H, _p(w), float(eps),
                       float(scale), _p(y), _p(rstd), rows, D, _lib.stream())
         else:

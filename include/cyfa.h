@@ -319,6 +319,21 @@ int cyfa_gated_norm_bias_bwd(const void* x, const void* gate, const void* gate_b
                              void* dx, void* dgate, float* dw, float* dgate_bias, int rows, int D,
                              void* work, size_t work_bytes, void* stream);
 
+/* The output gate's second linear fused into the biased gated norm (replaces the
+ * g_proj second linear plus o_norm of reference layers/cyfa.py:292-295,349-350):
+ *   gate = bf16(gin Wg^T),  y = RMSNorm(scale * x) * w * sigmoid(gate + gate_bias)
+ * x, y: [tokens, H, D] bf16 (D = 128 or 256); gin: [tokens, Kg] bf16 rows
+ * gin_stride elements apart (Kg a multiple of 64; a column view of a packed
+ * projection is fine); gate_w: [H*D, Kg] bf16 row-major; gate_bias: [H*D] bf16 or
+ * NULL; rstd: [tokens*H] f32.  gate_out ([tokens, H*D] bf16, the gate before its
+ * bias, as cyfa_gated_norm_bias_bwd reads it) is written when not NULL.  The
+ * linear accumulates in fp32 on the tensor cores and is rounded to bf16 before
+ * the bias, as a bf16 linear's output is. */
+int cyfa_gated_norm_gate_fwd(const void* x, const void* gin, long long gin_stride,
+                             const void* gate_w, const void* gate_bias, int H, int Kg,
+                             const float* w, float eps, float scale, void* y, float* rstd,
+                             void* gate_out, int tokens, int D, void* stream);
+
 /* Allocation-free variant of cyfa_gated_norm_bwd, for callers that cannot hand the
  * library a workspace: bindings whose signature carries only the op's tensors, or
  * processes whose device memory belongs entirely to a framework allocator.  No

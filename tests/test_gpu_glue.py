@@ -112,3 +112,65 @@ def test_gated_norm(LO, D, B, T, H):
     for a, b in ((gin, ginr), (gw, gwr), (gb, gbr)):
         assert rel_l2(a.grad, b.grad) < 1e-2
     assert rel_l2(w.grad, wr.grad) < 1e-2  # dy enters in bf16
+
+
+@pytest.mark.parametrize("D,Kg,H,tokens,bias", [(256, 256, 4, 16384, True), (256, 192, 3, 333, True),
+                                                (128, 128, 2, 1, False), (128, 320, 5, 700, True)])
+def test_gated_norm_gate_fused(D, Kg, H, tokens, bias):
+    """cyfa_gated_norm_gate_fwd (the gate linear on tcgen05 inside the norm
+    kernel) against the gate linear in fp32 rounded to bf16 followed by the
+    norm in fp32, with gin a strided column view of a wider packed tensor, a
+    partial last 128-token tile, and the optional gate output."""
+    from cyclic_flow_attention import _lib
+
+    gen = torch.Generator().manual_seed(D + Kg + H)
+    width = Kg + 72  # gin sits at column 40 of a [tokens, Kg + 72] projection
+    P = torch.randn(tokens, width, generator=gen).to(torch.bfloat16).cuda()
+    gin = P[:, 40:40 + Kg]
+    x = (0.01 * torch.randn(tokens, H, D, generator=gen)).to(torch.bfloat16).cuda()
+    gw = (0.05 * torch.randn(H * D, Kg, generator=gen)).to(torch.bfloat16).cuda()
+    gb = (0.1 * torch.randn(H * D, generator=gen)).to(torch.bfloat16).cuda() if bias else None
+    w = (1 + 0.1 * torch.randn(D, generator=gen)).cuda()
+    y = torch.empty(tokens, H * D, device="cuda", dtype=torch.bfloat16)
+    rstd = torch.empty(tokens * H, device="cuda")
+    gate = torch.empty(tokens, H * D, device="cuda", dtype=torch.bfloat16)
+    p = _lib.ptr
+    _lib.call("cyfa_gated_norm_gate_fwd", p(x), p(gin), width, p(gw), p(gb), H, Kg, p(w), 1e-6,
+              127.0, p(y), p(rstd), p(gate), tokens, D, _lib.stream())
+    torch.cuda.synchronize()
+    g_ref = (gin.float() @ gw.float().t())
+    # the gate: fp32 accumulation in another order, then bf16 rounding
+    assert (gate.float() - g_ref).abs().max() <= 2 ** -7 * g_ref.abs().max() + 1e-3
+    assert rel_l2(gate, g_ref) < 4e-3
+    u = x.float() * 127.0
+    rs = torch.rsqrt(u.pow(2).mean(-1) + 1e-6)
+    gt = g_ref.to(torch.bfloat16).float() + (gb.float() if bias else 0.0)
+    yr = (u * rs[..., None] * w) * torch.sigmoid(gt.reshape(tokens, H, D))
+    assert rel_l2(rstd, rs.reshape(-1)) < 1e-5
+    assert rel_l2(y, yr.reshape(tokens, H * D)) < 1e-2
+    # no gate output requested: same y
+    y2 = torch.empty_like(y)
+    _lib.call("cyfa_gated_norm_gate_fwd", p(x), p(gin), width, p(gw), p(gb), H, Kg, p(w), 1e-6,
+              127.0, p(y2), p(rstd), None, tokens, D, _lib.stream())
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2)
+    assert _lib.device_error() == 0
+
+
+def test_gated_norm_inference_path(LO):
+    """gated_norm_infer (the inference path: the gate linear inside the norm
+    kernel) matches GatedNormFunction (cuBLAS linear, then the norm) up to the
+    bf16 rounding of a gate accumulated in another order."""
+    gen = torch.Generator().manual_seed(7)
+    B, T, H, D = 2, 300, 4, 256
+    P = torch.randn(B, T, 3 * D, generator=gen).to(torch.bfloat16).cuda()
+    gin = P[..., D:2 * D]  # a column view, as the layer passes it
+    x = (0.01 * torch.randn(B, T, H, D, generator=gen)).to(torch.bfloat16).cuda()
+    gw = (0.05 * torch.randn(H * D, D, generator=gen)).to(torch.bfloat16).cuda()
+    gb = (0.1 * torch.randn(H * D, generator=gen)).to(torch.bfloat16).cuda()
+    w = (1 + 0.1 * torch.randn(D, generator=gen)).cuda()
+    with torch.no_grad():
+        y_inf = LO.gated_norm_infer(x, gin, gw, gb, w, 1e-6, 127.0)
+    y_train = LO.GatedNormFunction.apply(x, gin, gw, gb, w.clone().requires_grad_(True), 1e-6,
+                                         127.0)
+    assert rel_l2(y_inf, y_train) < 2e-3
