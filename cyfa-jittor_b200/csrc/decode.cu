@@ -115,7 +115,9 @@ __device__ __forceinline__ void decode_token(const TokenIO& io, const float* tab
   constexpr int M = 128;
   const int tid = threadIdx.x;
   __shared__ float sq[K], sk[K];
-  __shared__ float part[8 * M];  // per-group partial sums (sweep 1 uses 8x128, sweep 2 4x256)
+  // per-group partial sums (sweep 1 uses 8x128, sweep 2 4x256), written as float4:
+  // 16-byte alignment is required whatever other shared arrays the kernel declares
+  __shared__ __align__(16) float part[8 * M];
   __shared__ float wv[M], raw[M], z[M], wts[M], prob[128];
   __shared__ float red[8];
 

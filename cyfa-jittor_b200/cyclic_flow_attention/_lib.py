@@ -27,6 +27,7 @@ _SIGNATURES = {
     "cyfa_selftest_umma": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "cyfa_decode_step": [_vp] * 16 + [_i] * 5 + [_f] * 3 + [_vp],
     "cyfa_chunk_fwd_f32": [_vp] * 16 + [_i] * 5 + [_f] * 3 + [_vp],
+    "cyfa_decode_layer": [_vp, _vp],
     "cyfa_gates_fwd": [_vp] * 8 + [_i] * 3 + [_vp],
     "cyfa_token_fwd": [_vp] * 11 + [_i] * 4 + [_f] * 2 + [_vp],
     "cyfa_token_bwd": [_vp] * 17 + [_i] * 4 + [_vp],
@@ -69,6 +70,19 @@ _SIZE_QUERIES = {
     "cyfa_gated_norm_bias_work_bytes": [_i] * 3,
     "cyfa_grad_clip_work_bytes": [],
 }
+
+
+class DecodeLayerArgs(ctypes.Structure):
+    """cyfa_decode_layer_args."""
+
+    _fields_ = [(n, _i) for n in ("B", "H", "K", "V", "W", "a_col")] + \
+        [("P_stride", ctypes.c_longlong)] + \
+        [(n, _vp) for n in ("P", "cache_q", "cache_k", "cache_v", "wconv_q", "wconv_k",
+                            "wconv_v", "A_log", "dt_bias", "b_bias", "d_bias", "table",
+                            "q_norm_weight", "k_norm_weight", "hk_in", "hv_in", "clock_in",
+                            "hk_out", "hv_out", "clock_out", "gate", "gate_bias",
+                            "o_norm_weight", "y")] + \
+        [(n, _f) for n in ("q_eps", "k_eps", "scale", "o_eps", "o_scale")]
 
 
 class BucketPiece(ctypes.Structure):

@@ -340,12 +340,11 @@ class CyclicFlowAttention(nn.Module):
 
     def _forward_decode(self, x, cache, inplace=False):
         """One token per sequence (reference layers/cyfa.py:299-357 at T = 1 with
-        a cache): the packed q|k|v|g0|a|b|d projection, the three short
-        convolutions with their histories (cyfa_decode_conv), the gate activations
-        (cyfa_gate_act_fwd), the recurrent step (cyfa_decode_step), the gate's
-        second linear, the gated output norm with its bias (cyfa_gated_norm_bias_fwd)
-        and o_proj.  (At T = 1 the fused gate + norm kernel of the prefill path
-        measured slower than the two launches: 17 against 11 us at batch 256.)  With ``inplace`` the cache tensors are updated in place (the
+        a cache): the packed q|k|v|g0|a|b|d projection and the gate's second
+        linear (cuBLAS), then one cyfa_decode_layer launch for everything between
+        them and o_proj: the three short convolutions with their histories, the
+        gate activations, the recurrent step and the gated output norm with its
+        bias.  With ``inplace`` the cache tensors are updated in place (the
         graphed decoder's static buffers); otherwise a new cache is returned and
         the caller's is left untouched, as the reference does."""
         B = x.shape[0]
@@ -359,6 +358,7 @@ class CyclicFlowAttention(nn.Module):
             n = sum(w.shape[0] for w in ws)
             wf = torch.cat(ws + [ws[0].new_zeros((n + 7) // 8 * 8 - n, ws[0].shape[1])])
         P = torch.mm(x.reshape(B, -1), wf.t())  # [B, q|k|v|g0|a|b|d (+pad)]
+        gate = torch.mm(P[:, 2 * HK + HV:2 * HK + HV + V], self.g_proj[1].weight.t())
         hk, hv, clock = cache["recurrent_state"]
         cq, ck, cv = cache["conv_state"]
         dev = x.device
@@ -368,28 +368,20 @@ class CyclicFlowAttention(nn.Module):
             cq, ck, cv = (t.to(torch.bfloat16).contiguous().clone() for t in (cq, ck, cv))
             hk_o, hv_o = torch.empty_like(hk), torch.empty_like(hv)
             clock_o = torch.empty_like(clock)
-        q = torch.empty(B, 1, H, K, device=dev, dtype=torch.bfloat16)
-        k = torch.empty_like(q)
-        v = torch.empty(B, 1, H, V, device=dev, dtype=torch.bfloat16)
-        p, st, ps = _lib.ptr, _lib.stream(), P.stride(0)
-        _lib.call("cyfa_decode_conv", p(P), ps, p(cq), p(ck), p(cv), p(c["wq"]), p(c["wk"]),
-                  p(c["wv"]), p(q), p(k), p(v), B, HK, HK, HV, self.q_conv1d.width, st)
-        g = torch.empty(B, 1, H, device=dev, dtype=torch.float32)
-        delta, beta = torch.empty_like(g), torch.empty_like(g)
-        off = 2 * HK + HV + V  # a | b | d columns after q|k|v|g0
-        _lib.call("cyfa_gate_act_fwd", p(P[:, off:]), ps, p(P[:, off + H:]), ps,
-                  p(P[:, off + 2 * H:]), ps, p(c["A_log"]), p(c["dt_bias"]), p(c["b_bias"]),
-                  p(c["d_bias"]), p(g), p(delta), p(beta), B, H, st)
-        o = torch.empty(B, 1, H, V, device=dev, dtype=torch.bfloat16)
-        _lib.call("cyfa_decode_step", p(q), p(k), p(v), p(g), p(delta), p(beta), p(c["table"]),
-                  p(c["q_norm"]), p(c["k_norm"]), p(hk), p(hv), p(clock), p(hk_o), p(hv_o),
-                  p(clock_o), p(o), B, H, K, V, 0, float(self.q_norm.eps),
-                  float(self.k_norm.eps), K ** -0.5, st)
-        gate = torch.mm(P[:, 2 * HK + HV:2 * HK + HV + V], self.g_proj[1].weight.t())
         y = torch.empty(B, HV, device=dev, dtype=torch.bfloat16)
-        rstd = torch.empty(B * H, device=dev, dtype=torch.float32)
-        _lib.call("cyfa_gated_norm_bias_fwd", p(o), p(gate), p(c["g_bias"]), H, p(c["o_norm"]),
-                  float(self.o_norm.eps), float(self.num_slots - 1), p(y), p(rstd), B * H, V, st)
+        p = _lib.ptr
+        a = _lib.DecodeLayerArgs(
+            B=B, H=H, K=K, V=V, W=self.q_conv1d.width, a_col=2 * HK + HV + V,
+            P_stride=P.stride(0), P=p(P), cache_q=p(cq), cache_k=p(ck), cache_v=p(cv),
+            wconv_q=p(c["wq"]), wconv_k=p(c["wk"]), wconv_v=p(c["wv"]), A_log=p(c["A_log"]),
+            dt_bias=p(c["dt_bias"]), b_bias=p(c["b_bias"]), d_bias=p(c["d_bias"]),
+            table=p(c["table"]), q_norm_weight=p(c["q_norm"]), k_norm_weight=p(c["k_norm"]),
+            hk_in=p(hk), hv_in=p(hv), clock_in=p(clock), hk_out=p(hk_o), hv_out=p(hv_o),
+            clock_out=p(clock_o), gate=p(gate), gate_bias=p(c["g_bias"]),
+            o_norm_weight=p(c["o_norm"]), y=p(y), q_eps=float(self.q_norm.eps),
+            k_eps=float(self.k_norm.eps), scale=K ** -0.5, o_eps=float(self.o_norm.eps),
+            o_scale=float(self.num_slots - 1))
+        _lib.call("cyfa_decode_layer", _lib.ctypes.byref(a), _lib.stream())
         out = torch.mm(y, self.o_proj.weight.t()).reshape(B, 1, -1)
         return out, {"recurrent_state": (hk_o, hv_o, clock_o), "conv_state": (cq, ck, cv)}
 

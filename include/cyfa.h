@@ -94,6 +94,50 @@ int cyfa_decode_step(const void* q, const void* k, const void* v, const float* g
                      int K, int V, int dtype, float q_eps, float k_eps, float scale,
                      void* stream);
 
+/* One decode step of the CyclicFlowAttention layer between its input and output
+ * projections, for all (sequence, head) pairs in one launch (replaces, at T = 1
+ * with a cache, reference layers/cyfa.py:299-357 after the q/k/v/g/a/b/d
+ * projections and before o_proj: ShortConvolution with a cache :144-181, the gate
+ * activations :323-326, fused_recurrent_cyfa, o_norm(o * scale, gate) :350).
+ * P: the packed projection rows [B, P_stride] bf16 holding q | k | v (H*K, H*K,
+ * H*V columns from column 0) and a | b | d (H columns each from a_col); the conv
+ * histories cache_q/k/v [B, W-1, C] bf16 (oldest row first) are shifted in place;
+ * wconv_* [C, W] f32; A_log, dt_bias [H] f32, b_bias, d_bias [H] f32 or NULL;
+ * gate [B, H*V] bf16 is the output gate's linear without its bias, gate_bias
+ * [H*V] bf16, o_norm_weight [V] f32; y [B, H*V] bf16.  State arguments as in
+ * cyfa_decode_step (outputs may alias inputs).  K, V in {128, 256}; 2 <= W <= 4. */
+typedef struct {
+  int B, H, K, V, W;
+  int a_col;
+  long long P_stride;
+  const void* P;
+  void* cache_q;
+  void* cache_k;
+  void* cache_v;
+  const float* wconv_q;
+  const float* wconv_k;
+  const float* wconv_v;
+  const float* A_log;
+  const float* dt_bias;
+  const float* b_bias;
+  const float* d_bias;
+  const float* table;
+  const float* q_norm_weight;
+  const float* k_norm_weight;
+  const float* hk_in;
+  const float* hv_in;
+  const float* clock_in;
+  float* hk_out;
+  float* hv_out;
+  float* clock_out;
+  const void* gate;
+  const void* gate_bias;
+  const float* o_norm_weight;
+  void* y;
+  float q_eps, k_eps, scale, o_eps, o_scale;
+} cyfa_decode_layer_args;
+int cyfa_decode_layer(const cyfa_decode_layer_args* args, void* stream);
+
 /* fp32 chunk forward (inference): the whole chunk_cyfa forward for fp32 inputs,
  * computed in fp32 throughout as the token recurrence (one CTA per (b, h) runs
  * the decode step over its T tokens), so it equals the reference's generic fp32

@@ -281,3 +281,78 @@ def test_readout_table_kernels(L):
     assert dr.shape == (H, 127, 127)
     assert rel_l2(dr.cpu(), ref_dr) < F32_TOL
     assert L.device_error() == 0
+
+
+@pytest.mark.parametrize("K,V,W", [(256, 256, 4), (128, 256, 3), (256, 128, 2)])
+def test_decode_layer_matches_separate_kernels(L, K, V, W):
+    """cyfa_decode_layer (convolutions, gate activations, decode step and gated
+    output norm of a layer's T = 1 step in one launch) against the chain of
+    separate launches it replaces (cyfa_decode_conv, cyfa_gate_act_fwd,
+    cyfa_decode_step, cyfa_gated_norm_bias_fwd): bitwise equal convolution
+    histories, states and clock; the output equal up to the order of the norm's
+    row sum (rare one-ulp bf16 differences)."""
+    import ctypes
+
+    gen = seeded(K + V + W)
+    B, H = 6, 4
+    HK, HV = H * K, H * V
+    a_col = 2 * HK + HV + V
+    NB = (a_col + 3 * H + 7) // 8 * 8
+    bf = torch.bfloat16
+    P = torch.randn(B, NB, generator=gen).to(bf).cuda()
+    caches = [(0.5 * torch.randn(B, W - 1, C, generator=gen)).to(bf).cuda() for C in (HK, HK, HV)]
+    wconv = [(0.3 * torch.randn(C, W, generator=gen)).cuda() for C in (HK, HK, HV)]
+    A_log = torch.randn(H, generator=gen).cuda()
+    dt_bias = torch.randn(H, generator=gen).cuda()
+    b_bias = torch.randn(H, generator=gen).cuda()
+    d_bias = torch.randn(H, generator=gen).cuda()
+    table = (0.1 * torch.randn(H, 127, 128, generator=gen)).cuda()
+    qn = (1 + 0.1 * torch.randn(K, generator=gen)).cuda()
+    kn = (1 + 0.1 * torch.randn(K, generator=gen)).cuda()
+    hk = (0.1 * torch.randn(B * H, K, 128, generator=gen)).cuda()
+    hv = (0.1 * torch.randn(B * H, 128, V, generator=gen)).cuda()
+    clock = (100 * torch.rand(B * H, generator=gen)).cuda()
+    gate = torch.randn(B, HV, generator=gen).to(bf).cuda()
+    gbias = (0.1 * torch.randn(HV, generator=gen)).to(bf).cuda()
+    onorm = (1 + 0.1 * torch.randn(V, generator=gen)).cuda()
+    p, st, ps = L.ptr, L.stream(), NB
+    # ---- the separate launches
+    c1 = [t.clone() for t in caches]
+    q = torch.empty(B, 1, H, K, device="cuda", dtype=bf)
+    k = torch.empty_like(q)
+    v = torch.empty(B, 1, H, V, device="cuda", dtype=bf)
+    L.call("cyfa_decode_conv", p(P), ps, p(c1[0]), p(c1[1]), p(c1[2]), p(wconv[0]), p(wconv[1]),
+           p(wconv[2]), p(q), p(k), p(v), B, HK, HK, HV, W, st)
+    g = torch.empty(B, 1, H, device="cuda")
+    delta, beta = torch.empty_like(g), torch.empty_like(g)
+    L.call("cyfa_gate_act_fwd", p(P[:, a_col:]), ps, p(P[:, a_col + H:]), ps,
+           p(P[:, a_col + 2 * H:]), ps, p(A_log), p(dt_bias), p(b_bias), p(d_bias), p(g),
+           p(delta), p(beta), B, H, st)
+    hk1, hv1, clock1 = torch.empty_like(hk), torch.empty_like(hv), torch.empty_like(clock)
+    o = torch.empty(B, 1, H, V, device="cuda", dtype=bf)
+    L.call("cyfa_decode_step", p(q), p(k), p(v), p(g), p(delta), p(beta), p(table), p(qn), p(kn),
+           p(hk), p(hv), p(clock), p(hk1), p(hv1), p(clock1), p(o), B, H, K, V, 0, 1e-6, 1e-6,
+           K ** -0.5, st)
+    y1 = torch.empty(B, HV, device="cuda", dtype=bf)
+    rstd = torch.empty(B * H, device="cuda")
+    L.call("cyfa_gated_norm_bias_fwd", p(o), p(gate), p(gbias), H, p(onorm), 1e-5, 127.0, p(y1),
+           p(rstd), B * H, V, st)
+    # ---- one launch
+    c2 = [t.clone() for t in caches]
+    hk2, hv2, clock2 = torch.empty_like(hk), torch.empty_like(hv), torch.empty_like(clock)
+    y2 = torch.empty_like(y1)
+    a = L.DecodeLayerArgs(
+        B=B, H=H, K=K, V=V, W=W, a_col=a_col, P_stride=NB, P=p(P), cache_q=p(c2[0]),
+        cache_k=p(c2[1]), cache_v=p(c2[2]), wconv_q=p(wconv[0]), wconv_k=p(wconv[1]),
+        wconv_v=p(wconv[2]), A_log=p(A_log), dt_bias=p(dt_bias), b_bias=p(b_bias),
+        d_bias=p(d_bias), table=p(table), q_norm_weight=p(qn), k_norm_weight=p(kn), hk_in=p(hk),
+        hv_in=p(hv), clock_in=p(clock), hk_out=p(hk2), hv_out=p(hv2), clock_out=p(clock2),
+        gate=p(gate), gate_bias=p(gbias), o_norm_weight=p(onorm), y=p(y2), q_eps=1e-6,
+        k_eps=1e-6, scale=K ** -0.5, o_eps=1e-5, o_scale=127.0)
+    L.call("cyfa_decode_layer", ctypes.byref(a), st)
+    torch.cuda.synchronize()
+    for x1, x2 in zip(c1, c2):
+        assert torch.equal(x1, x2)
+    assert torch.equal(hk1, hk2) and torch.equal(hv1, hv2) and torch.equal(clock1, clock2)
+    assert rel_l2(y2, y1) < 2e-3
+    assert L.device_error() == 0
