@@ -454,8 +454,10 @@ class LayerFrontFunction(torch.autograd.Function):
         # conv weights (one [n_qkv, Wc] block when the q, k, v pieces are adjacent)
         # and gate parameters as fp32, one launch on the aux stream beside the
         # projection (joined before the convolution)
+        aux = _fork(dev)
         cwq, cwk, cwv, A, dt, bb, db = gather_f32(
-            [cw_q, cw_k, cw_v, A_log, dt_bias, b_bias, d_bias], _fork(dev))
+            [cw_q, cw_k, cw_v, A_log, dt_bias, b_bias, d_bias], aux)
+        params_ready = aux.record_event()
         # the packed projection: a view when the weights already are consecutive
         # blocks of one buffer (the layer packs them once), else a concatenation;
         # the padding rows stay uninitialised: the columns they produce are never read
@@ -465,7 +467,19 @@ class LayerFrontFunction(torch.autograd.Function):
             torch.cat(parts, out=W_big[:n_used])
         big = torch.nn.functional.linear(x, W_big)  # [B, T, NB]
         Wc = cw_q.shape[-1]
-        _join(dev)
+        # the gate activations (a | b | d columns) run on the aux stream beside the
+        # convolution (q | k | v columns); the convolution waits only for its weights
+        g = torch.empty(B, T, H, device=dev, dtype=torch.float32)
+        delta = torch.empty_like(g)
+        beta = torch.empty_like(g)
+        torch.cuda.current_stream(dev).wait_event(params_ready)
+        aux.wait_stream(torch.cuda.current_stream(dev))
+        base, st = big.data_ptr(), _c.c_longlong(NB)
+        with torch.cuda.stream(aux):
+            _lib.call("cyfa_gate_act_fwd", _c.c_void_p(base + 2 * c_a), st,
+                      _c.c_void_p(base + 2 * c_b), st, _c.c_void_p(base + 2 * c_d), st, _p(A),
+                      _p(dt), _p(bb), _p(db), _p(g), _p(delta), _p(beta), rows, H,
+                      _lib.stream())
         if (cwk.data_ptr() == cwq.data_ptr() + 4 * cwq.numel()
                 and cwv.data_ptr() == cwk.data_ptr() + 4 * cwk.numel()):
             cw = torch.as_strided(cwq, (n_qkv, Wc), (Wc, 1))
@@ -474,13 +488,7 @@ class LayerFrontFunction(torch.autograd.Function):
         qkv = torch.empty(B, T, n_qkv, device=dev, dtype=torch.bfloat16)
         _lib.call("cyfa_short_conv_fwd", _p(big), _c.c_longlong(NB), None, _p(cw), None, _p(qkv),
                   B, T, n_qkv, Wc, _lib.stream())
-        g = torch.empty(B, T, H, device=dev, dtype=torch.float32)
-        delta = torch.empty_like(g)
-        beta = torch.empty_like(g)
-        base, st = big.data_ptr(), _c.c_longlong(NB)
-        _lib.call("cyfa_gate_act_fwd", _c.c_void_p(base + 2 * c_a), st, _c.c_void_p(base + 2 * c_b),
-                  st, _c.c_void_p(base + 2 * c_d), st, _p(A), _p(dt), _p(bb), _p(db), _p(g),
-                  _p(delta), _p(beta), rows, H, _lib.stream())
+        _join(dev)
         gate_in = big[..., c_g:c_g + n_g]
         if slot is not None:
             slot.shape, slot.cols, slot.buf = (B, T, NB), (c_g, c_g + n_g), None
