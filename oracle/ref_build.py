@@ -23,7 +23,8 @@ jt.code input / output order).
 
 Nothing in the product imports this file; ``tests/golden/make_golden.py`` runs
 the built kernels on the GPU box to produce the golden vectors committed under
-``tests/golden/``.  Run: ``python oracle/ref_build.py [reference_root]``.
+``tests/golden/``, and ``tests/test_gpu_ref_decode_c4.py`` runs the
+configs[3]-shape build beside the library's decode step.  Run: ``python oracle/ref_build.py [reference_root]``.
 """
 
 import importlib.util
@@ -38,11 +39,14 @@ REF_ROOT = "/root/reference"
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17",
               "-Xcompiler", "-fPIC", "-shared", "-cudart", "static"]
 
-# configurations of the golden vectors: (name, B, H, K, V, dtype)
+# configurations: (name, B, H, K, V, dtype) -- those of the golden vectors, and
+# BASELINE configs[3]'s decode shape (batch 256, 8 heads of 256) for the
+# full-size parity and timing comparison of tests/test_gpu_ref_decode_c4.py
 CONFIGS = [
     ("bf16_k128", 1, 2, 128, 128, "bfloat16"),
     ("f32_k128", 1, 2, 128, 128, "float32"),
     ("bf16_k256", 1, 2, 256, 256, "bfloat16"),
+    ("bf16_c4", 256, 8, 256, 256, "bfloat16"),
 ]
 EPS = 1e-6
 
