@@ -740,11 +740,16 @@ def run_cyfa(args, rank, world, local_rank):
     # and reads its result (the output checksum) back.  The cotangent dy is the
     # objective's fixed weight and stays on the device, as the reference
     # benchmark's `do` does (benchmarks/core.py:295-296: one tensor for every
-    # step).  The next step's host-to-device copy runs on a side stream into a
-    # staging buffer while the current step computes, as a data loader would;
-    # the step then moves it into the graph's input buffer.
+    # step).  The next step's host-to-device copy runs on a side stream into the
+    # other of two input buffers while the current step computes, as a data loader
+    # would, and the step reads it there: a second capture of the step (sharing
+    # the first one's memory pool; the two never run at the same time) takes the
+    # other buffer, so steps alternate between the two graphs and no device-side
+    # copy is needed.
+    x2 = torch.empty_like(x).requires_grad_(True)
+    graphed2 = GraphedStep(step, [x2, dy], params, warmup=1, pool=graphed.pool())
+    graphs, bufs = [graphed, graphed2], [x, x2]
     copy_stream = torch.cuda.Stream(device=dev)
-    bufs = [torch.empty_like(x, requires_grad=False) for _ in range(2)]
     copied = [torch.cuda.Event() for _ in range(2)]
     done = [torch.cuda.Event() for _ in range(2)]
     main = torch.cuda.current_stream(dev)
@@ -752,7 +757,7 @@ def run_cyfa(args, rank, world, local_rank):
     def start_copy(i):
         b = i % 2
         copy_stream.wait_event(done[b])
-        with torch.cuda.stream(copy_stream):
+        with torch.cuda.stream(copy_stream), torch.no_grad():
             bufs[b].copy_(x_host, non_blocking=True)
             copied[b].record(copy_stream)
 
@@ -773,7 +778,7 @@ def run_cyfa(args, rank, world, local_rank):
         main.wait_event(copied[b])
         if i + 1 < args.steps:
             start_copy(i + 1)
-        check = graphed(bufs[b], dy)
+        check = graphs[b].replay()
         done[b].record(main)
         checks_host[b].copy_(check, non_blocking=True)
         read[b].record(main)
@@ -896,7 +901,7 @@ def run_cyfa(args, rank, world, local_rank):
         }
         print(json.dumps(line), flush=True)
     # a graph that holds NCCL calls must be gone before the process group is
-    graphed = None
+    graphed = graphed2 = graphs = None
     gc.collect()
     torch.cuda.synchronize()
     if world > 1:
