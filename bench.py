@@ -128,8 +128,17 @@ def _traffic_from_profiles(kernel):
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle sampling during the timed region."""
+    """SM clock and clock-event reasons of this process's GPU, sampled while the
+    timed work runs: NVML is read from the host thread that waits for the timed
+    region (`poll_until`), so every sample falls inside it.  Only reads: no clock
+    or other setting is changed.  nvidia-smi at 200 ms is the fallback when NVML
+    is unavailable."""
 
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -137,17 +146,74 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.nvml = None
+        self.handle = None
+        self.samples = []
+
+    def _nvml_handle(self, nv):
+        import torch
+
+        props = torch.cuda.get_device_properties(self.index)
+        uid = str(props.uuid)
+        for u in (uid, "GPU-" + uid):
+            try:
+                return nv.nvmlDeviceGetHandleByUUID(u)
+            except Exception:
+                pass
+        bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        return nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
 
     def start(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.handle = self._nvml_handle(nv)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM)
+            self.nvml = nv
+            return
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)
         except OSError:
             self.proc = None
 
+    def sample(self):
+        if self.nvml is None:
+            return
+        nv = self.nvml
+        try:
+            mhz = nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)
+            mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        except Exception:
+            return
+        self.samples.append((mhz, mask))
+
+    def poll_until(self, event):
+        """Samples every ~2 ms until `event` (recorded after the timed work) has
+        completed on the device."""
+        while not event.query():
+            self.sample()
+            time.sleep(0.002)
+
     def stop(self):
+        if self.nvml is not None:
+            nv = self.nvml
+            try:
+                nv.nvmlShutdown()
+            except Exception:
+                pass
+            if not self.samples:
+                return None
+            reasons = sorted({name for name, attr in self.REASONS for _, m in self.samples
+                              if hasattr(nv, attr) and m & getattr(nv, attr)})
+            return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                    "sm_max_mhz": float(self.max_mhz), "reasons": reasons,
+                    "samples": len(self.samples), "source": "NVML, inside the timed region"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -165,7 +231,7 @@ class ClockSampler:
                           if r[5 + i].strip().lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": float(rows[0][2]) if rows[0][2].strip().replace(".", "").isdigit() else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi, 200 ms"}
 
 
 def _rank_env():
@@ -717,7 +783,6 @@ def run_cyfa(args, rank, world, local_rank):
     # ---- device-resident timing (value): per-step events, L2 flushed between steps
     sampler = ClockSampler(torch.cuda.current_device() if world == 1 else local_rank)
     sampler.start()
-    time.sleep(0.3)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
     barrier()
@@ -726,6 +791,7 @@ def run_cyfa(args, rank, world, local_rank):
         a.record()
         graphed.replay()
         b.record()
+    sampler.poll_until(evs[-1][1])
     barrier()
     launches = graphed.library_launches * args.steps
     clocks = sampler.stop()
