@@ -80,9 +80,13 @@ class GradientBuckets:
     (training/optim.py:52-63); the arithmetic is the same, the transfer overlaps.
     """
 
-    def __init__(self, params, group=None, bucket_bytes=8 << 20, groups=None):
+    def __init__(self, params, group=None, bucket_bytes=8 << 20, groups=None,
+                 comm_sms=0):
         self.params = [p for p in params if p.requires_grad]
         self.group = group
+        # SMs that a GEMM issued right after an early hand-over leaves to the
+        # all-reduce it launched (`early` returns it; 0: the GEMM takes them all)
+        self.comm_sms = comm_sms
         self.bucket_bytes = bucket_bytes
         self.world = dist.get_world_size(group)
         self.avg_op = dist.get_backend(group) == "nccl"
@@ -180,24 +184,27 @@ class GradientBuckets:
         have already arrived) and every earlier bucket has been launched, the
         bucket is gathered (these from `grads`, the others from `.grad`) and
         all-reduced now, overlapping the rest of the op; the parameters' hooks
-        then do nothing.  Otherwise nothing happens and the hooks work as usual."""
+        then do nothing, and the return value is `comm_sms` (the SMs the op's next
+        GEMM should leave to the collective).  Otherwise nothing happens, the hooks
+        work as usual and the return value is 0."""
         if self.world == 1 or not self.sync or not params:
-            return
+            return 0
         first = self.slot.get(params[0])
         if first is None:
-            return
+            return 0
         i = first[0]
         given = dict(zip(params, grads))
         if any(self.slot.get(p, (None,))[0] != i for p in params):
-            return
+            return 0
         if any(p not in given and p not in self.filled[i] for p in self.buckets[i]):
-            return
+            return 0
         self._launch_ready()
         if self.next != i:
-            return
+            return 0
         self.filled[i] = set(self.buckets[i])
         self.pending[i] = 0
         self._launch(i, given)
+        return self.comm_sms
 
     def _pieces(self, i, given=None):
         """Bucket i's gradients as library pieces, or None if one of them does

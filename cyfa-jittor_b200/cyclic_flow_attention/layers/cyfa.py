@@ -147,9 +147,10 @@ class CyclicFlowAttention(nn.Module):
         self.o_norm = RMSNorm(self.head_v_dim, norm_eps)
         self.o_proj = nn.Linear(self.value_dim, hidden_size, bias=False)
 
-    # Optional callable(params, grads): receives the input-side weight gradients
-    # as soon as the fused backward has formed them (before the input gradient),
-    # e.g. GradientBuckets.early to start their all-reduce early.
+    # Optional callable(params, grads) -> int: receives the input-side weight
+    # gradients as soon as the fused backward has formed them (before the input
+    # gradient), e.g. GradientBuckets.early to start their all-reduce early; it
+    # returns how many SMs the input-gradient GEMM should leave free (0: none).
     grad_ready = None
 
     def grad_groups(self):

@@ -5,12 +5,33 @@ All compute runs in libcyfa.so; these wrappers allocate outputs and work
 buffers and pass raw pointers.
 """
 
+import contextlib
 import ctypes
 
 import torch
 
 from .. import _lib
 from .chunk import _BwdArgs, _FwdArgs, _p, basis_t, readout_grad, table_bf16
+
+
+@contextlib.contextmanager
+def _sm_carveout(n):
+    """GEMMs issued inside run through cuBLASLt targeting n fewer SMs than the
+    device has (CUBLASLT_MATMUL_DESC_SM_COUNT_TARGET), so that a collective
+    already running beside them keeps its SMs instead of waiting for the GEMM
+    to finish (n = 0: no change)."""
+    if not n:
+        yield
+        return
+    prev = torch._C._get_sm_carveout_experimental()
+    prev_lib = torch.backends.cuda.preferred_blas_library()
+    torch._C._set_sm_carveout_experimental(int(n))
+    torch.backends.cuda.preferred_blas_library("cublaslt")
+    try:
+        yield
+    finally:
+        torch.backends.cuda.preferred_blas_library(prev_lib)
+        torch._C._set_sm_carveout_experimental(prev)
 
 _c = ctypes
 
@@ -579,13 +600,15 @@ class LayerFrontFunction(torch.autograd.Function):
                 gflat[o:o + n * Wc].copy_(blk.reshape(-1))
         small = scatter_from(gflat, goffs, ctx.small_like, _fork(dev))
         grads = (*torch.split(dW, sizes), *small)
+        leave = 0  # SMs the dx GEMM leaves to a collective launched just now
         if ctx.grad_ready is not None:
             _join(dev)
-            ctx.grad_ready(ctx.params, grads)
+            leave = ctx.grad_ready(ctx.params, grads) or 0
         # dx from every column except d (projected from x.detach()) and the padding
         dx = None
         if ctx.needs_input_grad[0]:
-            dx = torch.matmul(d2[:, :c_d], W_big[:c_d]).view(B, T, hid)
+            with _sm_carveout(leave):
+                dx = torch.matmul(d2[:, :c_d], W_big[:c_d]).view(B, T, hid)
         _join(dev)
         del keep
         return (dx, *grads, None, None, None)

@@ -178,6 +178,8 @@ def test_gradient_buckets_match_flat_allreduce():
 class _EarlyLinear(torch.autograd.Function):
     """y = x w^T + b whose backward hands (w, b)'s gradients over before dx."""
 
+    leave = []  # what each hand-over returned (SMs to leave to the collective)
+
     @staticmethod
     def forward(ctx, x, w, b, ready):
         ctx.save_for_backward(x, w)
@@ -188,7 +190,7 @@ class _EarlyLinear(torch.autograd.Function):
     def backward(ctx, dy):
         x, w = ctx.saved_tensors
         dw, db = dy.t() @ x, dy.sum(0)
-        ctx.ready(ctx.params, (dw, db))
+        _EarlyLinear.leave.append(ctx.ready(ctx.params, (dw, db)))
         return dy @ w, dw, db, None
 
 
@@ -213,7 +215,8 @@ def _early_worker(rank, world, port, q):
         r1, r2 = make()
         params = list(l1.parameters()) + list(l2.parameters())
         # explicit groups in backward order: l2 first, then l1 (handed over early)
-        buckets = GradientBuckets(params, groups=[list(l2.parameters()), list(l1.parameters())])
+        buckets = GradientBuckets(params, groups=[list(l2.parameters()), list(l1.parameters())],
+                                  comm_sms=24)
         torch.manual_seed(10 + rank)
         x = torch.randn(4, 5)
         out = {"n": len(buckets.buckets)}
@@ -228,6 +231,9 @@ def _early_worker(rank, world, port, q):
             allreduce_gradients(list(r1.parameters()) + list(r2.parameters()))
             out[f"net{step}"] = [p.grad.tolist() for p in params]
             out[f"ref{step}"] = [p.grad.tolist() for p in list(r1.parameters()) + list(r2.parameters())]
+        out["leave"] = list(_EarlyLinear.leave)
+        # a hand-over that cannot complete its bucket launches nothing: 0
+        out["leave_incomplete"] = buckets.early([l2.weight], [torch.zeros_like(l2.weight)])
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
@@ -250,6 +256,9 @@ def test_gradient_buckets_groups_and_early_handover():
         assert p.exitcode == 0
     for r in range(world):
         assert res[r]["n"] == 2
+        # each early launch asks the next GEMM to leave comm_sms SMs to it
+        assert res[r]["leave"] == [24, 24]
+        assert res[r]["leave_incomplete"] == 0
         for step in range(2):
             assert res[r][f"early_used{step}"] == 2  # both buckets launched during backward
             for a, b in zip(res[r][f"net{step}"], res[r][f"ref{step}"]):
