@@ -85,3 +85,40 @@ def test_layer_state_dict_roundtrip(Layer, tmp_path):
     m2.load_state_dict(torch.load(path))
     for (n, a), (_, b) in zip(m.state_dict().items(), m2.state_dict().items()):
         assert torch.equal(a, b), n
+
+
+def test_dx_gemm_sm_target_after_early_handover(Layer):
+    """When the early gradient hand-over launches a collective it returns a number
+    of SMs; the layer's input-gradient GEMM then runs through cuBLASLt targeting
+    that many fewer SMs.  The input gradient equals the default path's up to the
+    GEMM's summation order, the weight gradients are unchanged (formed before),
+    and the BLAS backend and SM target are restored afterwards."""
+    m = _layer(Layer, 512, 2, 256, seed=7)
+    gen = torch.Generator().manual_seed(2)
+    x = torch.randn(2, 256, 512, generator=gen).to(torch.bfloat16).cuda()
+    dy = torch.randn(2, 256, 512, generator=gen).cuda()
+    lib0 = torch.backends.cuda.preferred_blas_library()
+    carve0 = torch._C._get_sm_carveout_experimental()
+    seen = []
+
+    def run(ready):
+        m.grad_ready = ready
+        for p in m.parameters():
+            p.grad = None
+        xg = x.clone().requires_grad_(True)
+        y, _ = m(xg)
+        (y.float() * dy).sum().backward()
+        torch.cuda.synchronize()
+        return xg.grad.clone(), {n: p.grad.clone() for n, p in m.named_parameters()}
+
+    try:
+        dx0, g0 = run(None)
+        dx1, g1 = run(lambda params, grads: seen.append(len(params)) or 32)
+    finally:
+        m.grad_ready = None
+    assert seen, "the fused backward did not hand its weight gradients over"
+    assert rel_l2(dx1, dx0) < 1e-3
+    for n in g0:
+        assert torch.equal(g0[n], g1[n]), n
+    assert torch.backends.cuda.preferred_blas_library() == lib0
+    assert torch._C._get_sm_carveout_experimental() == carve0
