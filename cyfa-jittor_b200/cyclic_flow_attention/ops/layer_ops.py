@@ -19,17 +19,22 @@ def _sm_carveout(n):
     """GEMMs issued inside run through cuBLASLt targeting n fewer SMs than the
     device has (CUBLASLT_MATMUL_DESC_SM_COUNT_TARGET), so that a collective
     already running beside them keeps its SMs instead of waiting for the GEMM
-    to finish (n = 0: no change)."""
+    to finish (n = 0: no change).  Split-K partial sums stay in fp32 (no bf16
+    reduction), so the result is as precise as the default path's."""
     if not n:
         yield
         return
+    mm = torch.backends.cuda.matmul
     prev = torch._C._get_sm_carveout_experimental()
     prev_lib = torch.backends.cuda.preferred_blas_library()
+    prev_red = mm.allow_bf16_reduced_precision_reduction
     torch._C._set_sm_carveout_experimental(int(n))
     torch.backends.cuda.preferred_blas_library("cublaslt")
+    mm.allow_bf16_reduced_precision_reduction = False
     try:
         yield
     finally:
+        mm.allow_bf16_reduced_precision_reduction = prev_red
         torch.backends.cuda.preferred_blas_library(prev_lib)
         torch._C._set_sm_carveout_experimental(prev)
 
