@@ -8,10 +8,12 @@ saved by the reference (PyTorch-compatible safetensors) load with
 On bf16 weights and CUDA inputs (training and prefill) the fused path runs: one
 packed projection GEMM (cuBLAS), the short convolutions and gate activations on
 its columns, the attention core, and the gated output norm are libcyfa.so
-kernels; only the GEMMs are library calls.  T == 1 decode with a cache runs the
-libcyfa decode glue and ``cyfa_decode_step``.  Other cases (fp32 weights, an
-attention mask, a cache during prefill) run torch glue around ``chunk_cyfa`` /
-``fused_recurrent_cyfa``, whose core is libcyfa.so as well.
+kernels; only the GEMMs are library calls.  A right-padding attention mask runs
+the fused path when no gradient is taken (per-row lengths).  T == 1 decode with a
+cache runs ``cyfa_decode_layer`` (convolutions, gate activations, decode step
+and gated norm in one launch) between the cuBLAS projections.  Other cases (fp32
+weights, a mask with gradients, a cache during prefill) run torch glue around
+``chunk_cyfa`` / ``fused_recurrent_cyfa``, whose core is libcyfa.so as well.
 """
 
 import math
