@@ -747,9 +747,11 @@ def run_cyfa(args, rank, world, local_rank):
         # one fp32 bucket for the whole layer, completed by the input-side weight
         # gradients, which the fused backward hands over before its dx GEMM: the
         # all-reduce overlaps that GEMM instead of the persistent core kernels;
-        # the GEMM leaves 32 SMs to it (cuBLASLt SM-count target), so the
-        # collective runs beside the GEMM instead of after it
-        buckets = GradientBuckets(params, groups=[sum(layer.grad_groups(), [])], comm_sms=32)
+        # at configs[2] the GEMM leaves 32 SMs to it (cuBLASLt SM-count target),
+        # so the collective runs beside the GEMM instead of after it (at
+        # configs[4] that measured no faster: the larger GEMM hides it already)
+        buckets = GradientBuckets(params, groups=[sum(layer.grad_groups(), [])],
+                                  comm_sms=32 if args.workload == "c3" else 0)
         layer.grad_ready = buckets.early
 
     def allreduce_grads():
